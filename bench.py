@@ -1,0 +1,347 @@
+"""Benchmark: batched frame forward (pack -> encode -> select), frames/sec.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+A step is one pass of the hot path over one packed ragged batch of the
+workload (default: 4096 frames, records/frame uniform 16-256 with 1-16
+questions, V=4096 token rows): GPU packing, embedding, the two encoder
+blocks, pooling, the two mixer blocks, and the pointer selector, producing
+p [sum Q_f R_f] and one index per question. Inputs are synthetic and seeded.
+
+Frames are independent, so ranks shard by frame with no collective on the
+data path: each rank runs its own batch (weak scaling); the barrier and the
+max-over-ranks of the device time are the only NCCL traffic.
+
+value: frames/s over all ranks, inputs resident in HBM, CUDA events on the
+stream the kernels run on. e2e: the same through the C-ABI host entry point
+(kc_forward_batch) with pinned host buffers, copies included. The line also
+carries the dominant kernel's roofline, the oracle timed on host cores, the
+clocks seen during the timed region, and p50/p99 single-frame latency.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from krystal_b200 import synth  # noqa: E402
+from krystal_b200.frame import QUERY_BAND  # noqa: E402
+
+METRIC = "frames/sec"
+UNIT = "frames/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="ragged_4096", choices=sorted(synth.WORKLOADS))
+    ap.add_argument("--frames", type=int, default=None, help="frames per batch (default: the workload's)")
+    ap.add_argument("--device-only", action="store_true",
+                    help="time only the device-resident leg (for profiler captures of the same kernels)")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [[c.strip() for c in line.split(",")] for line in out.strip().splitlines() if line.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(cfg, w, wl, frames_total: int, seed: int, budget_s: float) -> dict:
+    """The oracle (C++ restatement of the reference CPU path) on host cores, on a
+    bounded sample of the same workload."""
+    from oracle import oracle as O
+    cores = O.max_threads()
+    chunk = 4 * max(cores, 8)
+    done, t_all, i = 0, 0.0, 0
+    while t_all < budget_s and done < frames_total:
+        n = min(chunk, frames_total - done)
+        b = synth.make_batch(wl, seed=seed + 1000 + i, frames=n)
+        t0 = time.perf_counter()
+        O.forward_batch(cfg, w.page, b, threads=cores)
+        t_all += time.perf_counter() - t0
+        done += n
+        i += 1
+    return {"value": done / t_all, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{done} frames of {wl.name} in {t_all:.1f} s on {cores} threads ({O.cpu_model()})"}
+
+
+def reference_arm(args) -> None:
+    """The reference's CPU path (its oracle, restated in C++; no JS runtime
+    exists on these machines) with all host threads, each step a bounded sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    wl = synth.WORKLOADS[args.workload]
+    cfg = synth.workload_config(wl)
+    w = synth.workload_weights(cfg, wl.vocab)
+    cores = O.max_threads()
+    per_step = 4 * max(cores, 8)  # several frames per thread: frames vary 16-256 records
+    batches = [synth.make_batch(wl, seed=900 + s, frames=per_step) for s in range(args.steps + args.warmup)]
+    for s in range(args.warmup):
+        O.forward_batch(cfg, w.page, batches[s], threads=cores)
+    t0 = time.perf_counter()
+    nq = 0
+    for s in range(args.steps):
+        b = batches[args.warmup + s]
+        O.forward_batch(cfg, w.page, b, threads=cores)
+        nq += int((b.band_ids == QUERY_BAND).sum())
+    dt = time.perf_counter() - t0
+    value = args.steps * per_step / dt
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "questions_per_sec": nq / dt,
+            "config": {"workload": wl.name, "frames_per_step": per_step,
+                       "note": "reference CPU path = the C++ restatement of packages/krystal/src/forward/oracle.ts"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{per_step} frames of {wl.name} per step, {O.cpu_model()}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from krystal_b200.backend import CudaBrainBackend
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    wl = synth.WORKLOADS[args.workload]
+    frames = args.frames or wl.frames
+    cfg = synth.workload_config(wl)
+    w = synth.workload_weights(cfg, wl.vocab)
+    be = CudaBrainBackend(cfg, w, local)
+    stream = torch.cuda.Stream(device=dev)
+    be.set_stream(stream.cuda_stream)
+
+    # this rank's shard: its own batch of `frames` frames (weak scaling by frame)
+    batch = synth.make_batch(wl, seed=1 + rank, frames=frames)
+    offs = batch.offsets()
+    n_q = int(offs["q_off"][-1])
+    d_in = {k: torch.from_numpy(np.ascontiguousarray(getattr(batch, k)).view(np.int32)).to(dev)
+            for k in ("token_ids", "field_roles", "schema_ids", "band_ids")}
+    d_off = torch.from_numpy(batch.rec_off.astype(np.int64)).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    torch.cuda.synchronize(dev)
+
+    def step():
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+        return be.forward_batch_device(batch.frames, batch.records, d_off.data_ptr(), d_in["token_ids"].data_ptr(),
+                                       d_in["field_roles"].data_ptr(), d_in["schema_ids"].data_ptr(),
+                                       d_in["band_ids"].data_ptr())
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+
+    clocks = Clocks(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    be.profile(True)
+    be.profile_read(reset=True)
+    launches0 = be.launch_count()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        res = step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    launches = be.launch_count() - launches0
+    prof = be.profile_read(reset=True)
+    be.profile(False)
+    clk = clocks.stop() if clocks else None
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    assert res.total_q == n_q
+
+    line = None
+    if rank == 0:
+        peaks, peaks_kind = load_peaks()
+        sec = ms_max / 1e3
+        value = world * frames * args.steps / sec
+        gemm_ms = prof["enc_gemm_ms"] / max(prof["enc_gemm_launches"], 1)
+        gemm_flops = prof["enc_gemm_flops"] / max(prof["enc_gemm_launches"], 1)
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "questions_per_sec": world * n_q * args.steps / sec,
+            "config": {"workload": wl.name, "frames": frames, "records": batch.records, "questions": n_q,
+                       "tokens": int(offs["t_off"][-1]), "bank_rows": int(offs["r_off"][-1]),
+                       "p_entries": int(offs["p_off"][-1]), "parallelism": f"frame-shard x{world}",
+                       "l2": "256 MiB buffer written between steps (inside the timed region); "
+                             "a step's working set is several GB",
+                       "precision": "exact: f64 accumulation in the oracle's order, f32 stores"},
+            "gpu_launches": launches,
+            "stage_ms_per_step": {k[:-3]: round(prof[k] / args.steps, 3) for k in prof if k.endswith("_ms")},
+            "roofline": {"kernel": "k_dgemm_exact (encoder QKV/W1/W2)", "bound": "tensor",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); the kernel runs on the FP64 pipe "
+                                      "(~37 TFLOP/s nominal B200 FP64)",
+                         "launch_ms": gemm_ms, "flops_per_launch": gemm_flops},
+        }
+        if clk:
+            line["clocks"] = clk
+    if not args.device_only:
+        e2e = e2e_leg(be, batch, stream, args, dev, world)
+        if rank == 0:
+            line["e2e"] = e2e
+            line["latency"] = latency_leg(be, stream, dev)
+            from oracle import oracle as O  # noqa: F401  (cpu baseline below)
+            line["cpu_baseline"] = cpu_baseline(cfg, w, wl, frames, seed=7, budget_s=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    be.destroy()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def e2e_leg(be, batch, stream, args, dev, world) -> dict:
+    """kc_forward_batch with pinned host buffers: H2D, compute, D2H per step."""
+    import torch
+    import torch.distributed as dist
+
+    def pinned(a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        return t.numpy()
+
+    from krystal_b200.frame import FrameBatch
+    hb = FrameBatch(pinned(batch.rec_off.astype(np.uint64)), pinned(batch.token_ids), pinned(batch.field_roles),
+                    pinned(batch.schema_ids), pinned(batch.band_ids))
+    offs = batch.offsets()
+    p_cap = int(offs["p_off"][-1])
+    for _ in range(max(1, args.warmup)):
+        res = be.forward_batch(hb, p_capacity=p_cap)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        res = be.forward_batch(hb, p_capacity=p_cap)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sec = float(t.item()) / 1e3
+    h2d = sum(a.nbytes for a in (hb.rec_off, hb.token_ids, hb.field_roles, hb.schema_ids, hb.band_ids))
+    d2h = res["p"].nbytes + res["index"].nbytes + 2 * (batch.frames + 1) * 8
+    return {"value": world * batch.frames * args.steps / sec, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "entry": "kc_forward_batch (host buffers, pinned)"}
+
+
+def latency_leg(be, stream, dev, repeats: int = 200) -> dict:
+    """Single-frame think latency: one 64-record frame (56 bank + 8 questions)
+    through kc_forward_batch, host buffers in and out, per call."""
+    import torch
+    wl = synth.WORKLOADS["single_frame_64"]
+    b = synth.make_batch(wl, seed=3, frames=1)
+    for _ in range(10):
+        be.forward_batch(b)
+    torch.cuda.synchronize(dev)
+    dev_ms, wall_ms = [], []
+    for _ in range(repeats):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(stream)
+        be.forward_batch(b)
+        e1.record(stream)
+        e1.synchronize()
+        wall_ms.append((time.perf_counter() - t0) * 1e3)
+        dev_ms.append(e0.elapsed_time(e1))
+    q = lambda v, x: float(np.percentile(v, x))  # noqa: E731
+    return {"workload": "single_frame_64 (note: the weights of the batch workload)", "p50_ms": q(dev_ms, 50),
+            "p99_ms": q(dev_ms, 99), "p50_wall_ms": q(wall_ms, 50), "p99_wall_ms": q(wall_ms, 99),
+            "repeats": repeats}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,230 @@
+/*
+ * krystal_cuda.h — C ABI of the B200 backend for Krystal's frame forward.
+ *
+ * This is the drop-in boundary. The reference session talks to a device
+ * through the `BrainBackend` seam (packages/krystal/src/host/backend.ts:
+ * 261-295); `@krystal/webgpu` implements it in packages/webgpu/src/
+ * backend.ts:91-181. A `@krystal/cuda` adapter binds the functions below
+ * through bun:ffi and implements the same seam:
+ *
+ *   BrainBackendFactory (backend.ts:292-295)  -> kc_create
+ *   BrainBackend.encode (backend.ts:264)      -> kc_encode
+ *   BrainBackend.sync   (backend.ts:282)      -> kc_sync
+ *   BrainBackend.destroy(backend.ts:283)      -> kc_destroy
+ *   selectorOracle in choose() (session.ts:149-176, forward/oracle.ts:332-382)
+ *                                             -> kc_select (optional seam
+ *                                                extension `select?`)
+ *   packed ragged batches of think()          -> kc_forward_batch /
+ *                                                kc_forward_batch_device
+ *
+ * Conventions. All arrays are row-major fp32 / u32, exactly the typed arrays
+ * the TypeScript side holds. Host pointers unless a function says "device".
+ * The library owns its device buffers; the caller owns every pointer it
+ * passes. Every call returns a kc_status; kc_last_error() gives the message.
+ * Calls on one handle are serialised by an internal mutex (the reference
+ * serialises device work per engine, webgpu/src/backend.ts:84-89). One CUDA
+ * stream per handle. Nothing here allocates host memory the caller must free.
+ *
+ * Numerics. The forward reproduces the reference CPU oracle's arithmetic:
+ * f64 accumulation in the reference's loop order, rounding to f32 wherever
+ * the oracle stores into a Float32Array. Selected indices match the oracle
+ * bit for bit; distributions agree to far inside 1e-4.
+ */
+#ifndef KRYSTAL_CUDA_H
+#define KRYSTAL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KC_ABI_VERSION 1u
+#define KC_RECORD_WIDTH 8u        /* BRAIN_LIMITS.recordWidth (schema/src/krystal-engine-schema.ts:97) */
+#define KC_QUERY_BAND 5u          /* index of "query" in BRAIN_FRAME_BANDS (:150-172) */
+#define KC_NO_SELECTION 0xffffffffu /* index of an all-blocked row (forward/oracle.ts:364-365) */
+#define KC_MAX_BANK 4096u         /* largest bank one frame may hold */
+
+typedef enum kc_status {
+  KC_OK = 0,
+  KC_ERR_INVALID_ARG = 1, /* malformed frame, weights or arguments */
+  KC_ERR_CAPACITY = 2,    /* a size beyond what the library supports, or device memory exhausted */
+  KC_ERR_CUDA = 3,        /* a CUDA runtime error */
+  KC_ERR_TIMEOUT = 4,     /* a bounded device-side wait expired */
+  KC_ERR_NONFINITE = 5,   /* non-finite values where finite ones are required */
+  KC_ERR_NO_DEVICE = 6    /* no usable CUDA device */
+} kc_status;
+
+typedef struct kc_handle kc_handle;
+
+/* BrainForwardConfig (forward/model.ts:27-53). The six embedding table row
+ * counts are parameters; the reference's defaults are 4352, 4352, 256, 8, 2, 8.
+ * token_rows maps a token (or field-role) id to its embedding row (model.ts:52). */
+typedef struct kc_config {
+  uint32_t hidden_size, head_count, head_dim, ffn_size, encoder_blocks, mixer_blocks;
+  uint32_t token_space, field_space, schema_space, band_space, stream_space, pos_space;
+  uint32_t route_kind_count;
+  const uint32_t* token_rows;
+  uint32_t token_rows_len;
+} kc_config;
+
+/* BlockWeights (model.ts:131-137): wq, wk, wv [H,H], w1 [FFN,H], w2 [H,FFN]. */
+typedef struct kc_block_view {
+  const float *wq, *wk, *wv, *w1, *w2;
+} kc_block_view;
+
+/* BrainForwardWeights (model.ts:145-183). */
+typedef struct kc_weights_view {
+  const float* embeddings;      /* concatenated tables, embeddingTableBases order */
+  const kc_block_view* enc;     /* encoder_blocks entries */
+  const float* pool;            /* [2,H] */
+  const kc_block_view* mixer;   /* mixer_blocks entries */
+  const float* selector_wq;     /* [H,H] */
+  const float* selector_wk;     /* [H,H] */
+  const float* decision_head_wh;/* [route_kind_count, 3H] */
+  const float* value_head_wv;   /* [3H] */
+} kc_weights_view;
+
+/* WeightChanges (host/backend.ts:249-259). embedding_rows are element
+ * offsets into the embeddings page, each hidden_size long. */
+typedef struct kc_changes {
+  int32_t selector, pool, value_head, decision_head, blocks;
+  const uint32_t* embedding_rows;
+  uint32_t embedding_rows_count;
+} kc_changes;
+
+/* One packed frame: BrainFrameGpu (schema/src/krystal-engine-schema.ts:
+ * 203-209) as built by packHostFrame (host/frame.ts:72-115). */
+typedef struct kc_frame_view {
+  uint32_t slots;
+  const uint32_t* token_ids;             /* [slots*8], PAD = 0 */
+  const uint32_t* field_roles;           /* [slots*8] */
+  const uint32_t* schema_ids;            /* [slots] */
+  const uint32_t* band_ids;              /* [slots]; band 5 marks a question */
+  const uint32_t* active_record_indices; /* [slots], ascending, 0xffffffff ends the list */
+} kc_frame_view;
+
+/* EncodedFrame (host/backend.ts:148-154). */
+typedef struct kc_encoded_view {
+  uint32_t q, r;
+  const float* query_output; /* [Q,H] */
+  const float* bank_keys;    /* [R,H] */
+  const float* bank_values;  /* [R,H] */
+} kc_encoded_view;
+
+/* Device form of the host grammar `allows(query, record)` that selectionMask
+ * (host/learn.ts:215-232) turns into a [Q,R] mask: question i admits bank
+ * record s iff bit schema_ids[s] of schema_allow[i*8..i*8+8) (256 bits) and
+ * bit band_ids[s] of band_allow[i] are set. A question that admits nothing is
+ * reopened to the whole bank (learn.ts:229). */
+typedef struct kc_mask_rule {
+  const uint32_t* schema_allow;    /* [Q*8] */
+  const uint32_t* band_allow;      /* [Q] */
+  const uint32_t* bank_schema_ids; /* [R] schema of each bank row (kc_select only) */
+  const uint32_t* bank_band_ids;   /* [R] band of each bank row (kc_select only) */
+} kc_mask_rule;
+
+/* A packed ragged batch: frame f owns records rec_off[f] .. rec_off[f+1]-1,
+ * every record active and in order (packHostFrame's layout). Questions are
+ * numbered across the batch in frame order, then slot order. */
+typedef struct kc_batch_view {
+  uint32_t frames;
+  uint64_t records;              /* rec_off[frames] */
+  const uint64_t* rec_off;       /* [frames+1] */
+  const uint32_t* token_ids;     /* [records*8] */
+  const uint32_t* field_roles;   /* [records*8] */
+  const uint32_t* schema_ids;    /* [records] */
+  const uint32_t* band_ids;      /* [records] */
+  const uint32_t* schema_allow;  /* optional rule, [batch questions * 8] */
+  const uint32_t* band_allow;    /* optional rule, [batch questions] */
+  const double* uniforms;        /* optional: sample instead of argmax, [batch questions] */
+} kc_batch_view;
+
+/* Outputs of a batch. p of frame f is a [Q_f, R_f] block at p_off[f]; the
+ * indices of its questions start at q_off[f]. Questions of a frame whose bank
+ * is empty get KC_NO_SELECTION (the session returns no selection for them,
+ * session.ts:133). */
+typedef struct kc_batch_out {
+  float* p;                /* [total_p] */
+  uint64_t p_capacity;
+  uint32_t* index;         /* [total_q] */
+  uint64_t q_capacity;
+  uint64_t* p_off;         /* optional [frames+1] */
+  uint64_t* q_off;         /* optional [frames+1] */
+  float* query_output;     /* optional [total_q, H] */
+  uint64_t total_p, total_q, total_r, total_t; /* written by the call */
+} kc_batch_out;
+
+/* Library-owned device results of kc_forward_batch_device, valid until the
+ * next call on the handle. */
+typedef struct kc_device_result {
+  const float* p;
+  const uint32_t* index;
+  const uint64_t* p_off;
+  const uint64_t* q_off;
+  uint64_t total_p, total_q, total_r, total_t;
+} kc_device_result;
+
+/* Per-stage device time, accumulated while profiling is on. */
+typedef struct kc_stage_times {
+  double pack_ms, embed_ms, enc_gemm_ms, enc_attn_ms, pool_ms, mixer_ms, selector_ms, total_ms;
+  uint64_t enc_gemm_launches, launches, batches;
+  double enc_gemm_flops; /* algorithmic FLOPs of the encoder GEMMs timed */
+} kc_stage_times;
+
+uint32_t kc_abi_version(void);
+
+/* BrainBackendFactory (host/backend.ts:292-295): copy the weights to `device`
+ * and return a handle. */
+kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int device, kc_handle** out);
+
+/* BrainBackend.sync (host/backend.ts:282). changes == NULL means everything. */
+kc_status kc_sync(kc_handle* h, const kc_weights_view* weights, const kc_changes* changes);
+
+/* BrainBackend.encode (host/backend.ts:264) for one frame. Outputs are
+ * [Q,H], [R,H], [R,H]; *q_out / *r_out receive Q and R. q_cap / r_cap are the
+ * rows the output buffers hold. A frame without a question is refused, as
+ * the WebGPU runner refuses it (webgpu/src/krystal-forward.ts:216). */
+kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_output, float* bank_keys,
+                    float* bank_values, uint32_t q_cap, uint32_t r_cap, uint32_t* q_out, uint32_t* r_out);
+
+/* selectorOracle (forward/oracle.ts:332-382) on the device: score, mask,
+ * softmax, first-max argmax (or an inverse-CDF draw when uniforms != NULL,
+ * forward/sampling.ts:41-57), soft gather. mask: [Q,R] (NEG_INF -1e30 =
+ * blocked) or NULL; rule: the device form of the grammar or NULL; both NULL
+ * = open. p: [Q,R]; index: [Q]; gather: [Q,H] or NULL. */
+kc_status kc_select(kc_handle* h, const kc_encoded_view* encoded, const float* mask, const kc_mask_rule* rule,
+                    const double* uniforms, float* p, uint32_t* index, float* gather);
+
+/* Whole-batch think: pack on the GPU, encode, select. Host buffers; the
+ * host<->device copies are part of the call. */
+kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* batch, kc_batch_out* out);
+
+/* As kc_forward_batch, but every array in `batch` is a DEVICE pointer on the
+ * handle's device. Work is queued on the handle's stream; the call returns
+ * once the result is queued (one short host wait inside, for the batch's
+ * sizes). Results are library-owned device arrays. */
+kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* batch, kc_device_result* out);
+
+/* Stream control: run on `stream` (a cudaStream_t; NULL = the handle's own). */
+kc_status kc_set_stream(kc_handle* h, void* stream);
+void* kc_get_stream(kc_handle* h);
+kc_status kc_synchronize(kc_handle* h);
+
+/* Profiling: per-stage CUDA-event timing (adds events between stages). */
+kc_status kc_profile(kc_handle* h, int enable);
+kc_status kc_profile_read(kc_handle* h, kc_stage_times* out, int reset);
+/* Kernel launches the handle has issued since creation. */
+uint64_t kc_launch_count(kc_handle* h);
+
+/* BrainBackend.destroy (host/backend.ts:283). */
+void kc_destroy(kc_handle* h);
+
+/* Last error message for the handle (or the last failed kc_create if NULL). */
+const char* kc_last_error(kc_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,159 @@
+"""ctypes binding of the C ABI in include/krystal_cuda.h.
+
+The shared library is the product; this module only declares its structs and
+signatures and turns a non-OK status into ``KrystalCudaError`` carrying the
+library's message. Loading fails loudly when the library is missing or does
+not export a declared symbol: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libkrystal_cuda.so"
+
+KC_OK = 0
+KC_ERR_INVALID_ARG = 1
+KC_ERR_CAPACITY = 2
+KC_ERR_CUDA = 3
+KC_ERR_TIMEOUT = 4
+KC_ERR_NONFINITE = 5
+KC_ERR_NO_DEVICE = 6
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "CAPACITY", 3: "CUDA", 4: "TIMEOUT", 5: "NONFINITE", 6: "NO_DEVICE"}
+KC_NO_SELECTION = 0xFFFFFFFF
+KC_MAX_BANK = 4096
+
+# Every function include/krystal_cuda.h declares.
+EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
+           "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
+           "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error")
+
+
+class KrystalCudaError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+P = C.c_void_p
+u32p = C.POINTER(C.c_uint32)
+f32p = C.POINTER(C.c_float)
+
+
+class KcConfig(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "hidden_size", "head_count", "head_dim", "ffn_size", "encoder_blocks", "mixer_blocks", "token_space",
+        "field_space", "schema_space", "band_space", "stream_space", "pos_space", "route_kind_count")] + [
+        ("token_rows", P), ("token_rows_len", C.c_uint32)]
+
+
+class KcBlockView(C.Structure):
+    _fields_ = [("wq", P), ("wk", P), ("wv", P), ("w1", P), ("w2", P)]
+
+
+class KcWeightsView(C.Structure):
+    _fields_ = [("embeddings", P), ("enc", C.POINTER(KcBlockView)), ("pool", P), ("mixer", C.POINTER(KcBlockView)),
+                ("selector_wq", P), ("selector_wk", P), ("decision_head_wh", P), ("value_head_wv", P)]
+
+
+class KcChanges(C.Structure):
+    _fields_ = [("selector", C.c_int32), ("pool", C.c_int32), ("value_head", C.c_int32),
+                ("decision_head", C.c_int32), ("blocks", C.c_int32), ("embedding_rows", P),
+                ("embedding_rows_count", C.c_uint32)]
+
+
+class KcFrameView(C.Structure):
+    _fields_ = [("slots", C.c_uint32), ("token_ids", P), ("field_roles", P), ("schema_ids", P), ("band_ids", P),
+                ("active_record_indices", P)]
+
+
+class KcEncodedView(C.Structure):
+    _fields_ = [("q", C.c_uint32), ("r", C.c_uint32), ("query_output", P), ("bank_keys", P), ("bank_values", P)]
+
+
+class KcMaskRule(C.Structure):
+    _fields_ = [("schema_allow", P), ("band_allow", P), ("bank_schema_ids", P), ("bank_band_ids", P)]
+
+
+class KcBatchView(C.Structure):
+    _fields_ = [("frames", C.c_uint32), ("records", C.c_uint64), ("rec_off", P), ("token_ids", P),
+                ("field_roles", P), ("schema_ids", P), ("band_ids", P), ("schema_allow", P), ("band_allow", P),
+                ("uniforms", P)]
+
+
+class KcBatchOut(C.Structure):
+    _fields_ = [("p", P), ("p_capacity", C.c_uint64), ("index", P), ("q_capacity", C.c_uint64), ("p_off", P),
+                ("q_off", P), ("query_output", P), ("total_p", C.c_uint64), ("total_q", C.c_uint64),
+                ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
+
+
+class KcDeviceResult(C.Structure):
+    _fields_ = [("p", P), ("index", P), ("p_off", P), ("q_off", P), ("total_p", C.c_uint64),
+                ("total_q", C.c_uint64), ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
+
+
+class KcStageTimes(C.Structure):
+    _fields_ = [(n, C.c_double) for n in ("pack_ms", "embed_ms", "enc_gemm_ms", "enc_attn_ms", "pool_ms",
+                                          "mixer_ms", "selector_ms", "total_ms")] + [
+        ("enc_gemm_launches", C.c_uint64), ("launches", C.c_uint64), ("batches", C.c_uint64),
+        ("enc_gemm_flops", C.c_double)]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Load the library (once). Raises if it is missing or incomplete."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(f"krystal_b200: CUDA library {p} is not built (run krystal_b200.build)")
+    lib = C.CDLL(str(p))
+    missing = [s for s in EXPORTS if not hasattr(lib, s)]
+    if missing:
+        raise ImportError(f"krystal_b200: {p} lacks exports {missing}")
+    i = C.c_int
+    lib.kc_abi_version.restype = C.c_uint32
+    lib.kc_create.argtypes = [C.POINTER(KcConfig), C.POINTER(KcWeightsView), i, C.POINTER(P)]
+    lib.kc_sync.argtypes = [P, C.POINTER(KcWeightsView), C.POINTER(KcChanges)]
+    lib.kc_encode.argtypes = [P, C.POINTER(KcFrameView), P, P, P, C.c_uint32, C.c_uint32, u32p, u32p]
+    lib.kc_select.argtypes = [P, C.POINTER(KcEncodedView), P, C.POINTER(KcMaskRule), P, P, P, P]
+    lib.kc_forward_batch.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcBatchOut)]
+    lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
+    lib.kc_set_stream.argtypes = [P, P]
+    lib.kc_get_stream.argtypes = [P]
+    lib.kc_get_stream.restype = P
+    lib.kc_synchronize.argtypes = [P]
+    lib.kc_profile.argtypes = [P, i]
+    lib.kc_profile_read.argtypes = [P, C.POINTER(KcStageTimes), i]
+    lib.kc_launch_count.argtypes = [P]
+    lib.kc_launch_count.restype = C.c_uint64
+    lib.kc_destroy.argtypes = [P]
+    lib.kc_destroy.restype = None
+    lib.kc_last_error.argtypes = [P]
+    lib.kc_last_error.restype = C.c_char_p
+    for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
+                 "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read"):
+        getattr(lib, name).restype = C.c_int
+    _lib = lib
+    return lib
+
+
+def check(status: int, handle=None) -> None:
+    if status != KC_OK:
+        msg = load().kc_last_error(handle)
+        raise KrystalCudaError(status, msg.decode() if msg else "")
+
+
+def ptr(a) -> int | None:
+    """Data pointer of a numpy array (or None)."""
+    if a is None:
+        return None
+    return a.ctypes.data

@@ -1,0 +1,256 @@
+"""The CUDA device backend: ``BrainBackend`` over the C ABI.
+
+Mirrors the seam of packages/krystal/src/host/backend.ts (``EncodedFrame``
+:148-154, ``WeightChanges`` :249-259, ``BrainBackend`` :261-284,
+``BrainBackendFactory`` :292-295) and the WebGPU adapter that implements it
+(packages/webgpu/src/backend.ts:91-181): ``cuda_backend(device)`` returns a
+factory that the session calls with its config and the weights it owns; the
+backend keeps a device copy and is told of changes through ``sync``.
+
+Beyond the reference seam it offers ``select`` (the selector on the device,
+the optional ``select?`` extension ``choose()`` uses when present) and
+``forward_batch`` (a packed ragged batch of frames, pack → encode → select in
+one call).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Callable, Sequence
+
+import numpy as np
+
+from . import abi
+from .frame import FrameBatch, HostFrame
+from .model import BrainForwardConfig, BrainForwardWeights
+
+
+@dataclass
+class EncodedFrame:
+    """[Q,H] mixed query output and the [R,H] pooled bank (backend.ts:148-154)."""
+
+    query_output: np.ndarray
+    bank_keys: np.ndarray
+    bank_values: np.ndarray
+
+    @property
+    def q(self) -> int:
+        return self.query_output.size // 128
+
+    @property
+    def r(self) -> int:
+        return self.bank_keys.size // 128
+
+
+@dataclass
+class WeightChanges:
+    """Which arrays an update wrote (backend.ts:249-259); all None/False = nothing."""
+
+    selector: bool = False
+    pool: bool = False
+    value_head: bool = False
+    decision_head: bool = False
+    blocks: bool = False
+    embedding_rows: Sequence[int] = field(default_factory=list)
+
+
+@dataclass
+class Selection:
+    """selectorOracle's result (forward/oracle.ts:305-319)."""
+
+    p: np.ndarray  # [Q*R]
+    index: np.ndarray  # [Q] u32, KC_NO_SELECTION when a row is all blocked
+    gather: np.ndarray | None  # [Q*H]
+
+
+@dataclass
+class MaskRule:
+    """Device form of `allows`: 256-bit schema and 8-bit band masks per question."""
+
+    schema_allow: np.ndarray  # u32 [Q*8]
+    band_allow: np.ndarray  # u32 [Q]
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+class _Views:
+    """Keeps the arrays a kc_weights_view points at alive for one call."""
+
+    def __init__(self, weights: BrainForwardWeights):
+        self.keep = []
+
+        def p(a):
+            a = _f32(a)
+            self.keep.append(a)
+            return a.ctypes.data
+
+        def blocks(bs):
+            arr = (abi.KcBlockView * max(1, len(bs)))()
+            for i, b in enumerate(bs):
+                arr[i] = abi.KcBlockView(p(b.wq), p(b.wk), p(b.wv), p(b.w1), p(b.w2))
+            self.keep.append(arr)
+            return arr
+
+        self.view = abi.KcWeightsView(
+            p(weights.embeddings), blocks(weights.enc), p(weights.pool), blocks(weights.mixer),
+            p(weights.selector.wq), p(weights.selector.wk), p(weights.decision_head_wh), p(weights.value_head_wv))
+
+
+def _config_struct(config: BrainForwardConfig) -> tuple[abi.KcConfig, np.ndarray]:
+    rows = _u32(config.token_rows)
+    c = abi.KcConfig(config.hidden_size, config.head_count, config.head_dim, config.ffn_size, config.encoder_blocks,
+                     config.mixer_blocks, config.token_space, config.field_space, config.schema_space,
+                     config.band_space, config.stream_space, config.pos_space, config.route_kind_count,
+                     rows.ctypes.data if rows.size else None, rows.size)
+    return c, rows
+
+
+class CudaBrainBackend:
+    """One device, one handle (GpuBrainBackend's role, webgpu/src/backend.ts:91-168)."""
+
+    def __init__(self, config: BrainForwardConfig, weights: BrainForwardWeights, device: int = 0):
+        self._lib = abi.load()
+        self.config = config
+        self.device = device
+        cfg, self._rows = _config_struct(config)
+        views = _Views(weights)
+        h = C.c_void_p()
+        abi.check(self._lib.kc_create(C.byref(cfg), C.byref(views.view), device, C.byref(h)))
+        self._h = h
+
+    # --- BrainBackend -----------------------------------------------------
+    def encode(self, frame: HostFrame) -> EncodedFrame:
+        g = frame.gpu
+        tok, role, sch, band, act = (_u32(g.token_ids), _u32(g.field_roles), _u32(g.schema_ids), _u32(g.band_ids),
+                                     _u32(g.active_record_indices))
+        fv = abi.KcFrameView(sch.size, tok.ctypes.data, role.ctypes.data, sch.ctypes.data, band.ctypes.data,
+                             act.ctypes.data)
+        q_cap = max(1, frame.active.query_records.size)
+        r_cap = max(1, frame.active.bank_records.size)
+        h = self.config.hidden_size
+        qo = np.empty(q_cap * h, dtype=np.float32)
+        bk = np.empty(r_cap * h, dtype=np.float32)
+        bvv = np.empty(r_cap * h, dtype=np.float32)
+        q, r = C.c_uint32(), C.c_uint32()
+        abi.check(self._lib.kc_encode(self._h, C.byref(fv), qo.ctypes.data, bk.ctypes.data, bvv.ctypes.data, q_cap,
+                                      r_cap, C.byref(q), C.byref(r)), self._h)
+        return EncodedFrame(qo[:q.value * h], bk[:r.value * h], bvv[:r.value * h])
+
+    def sync(self, weights: BrainForwardWeights, changes: WeightChanges | None = None) -> None:
+        views = _Views(weights)
+        if changes is None:
+            abi.check(self._lib.kc_sync(self._h, C.byref(views.view), None), self._h)
+            return
+        rows = _u32(list(changes.embedding_rows))
+        ch = abi.KcChanges(int(changes.selector), int(changes.pool), int(changes.value_head),
+                           int(changes.decision_head), int(changes.blocks), rows.ctypes.data if rows.size else None,
+                           rows.size)
+        abi.check(self._lib.kc_sync(self._h, C.byref(views.view), C.byref(ch)), self._h)
+
+    def destroy(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.kc_destroy(self._h)
+            self._h = None
+
+    # --- seam extension: the selector on the device -------------------------
+    def select(self, encoded: EncodedFrame, mask: np.ndarray | None = None, rule: MaskRule | None = None,
+               bank_schema_ids=None, bank_band_ids=None, uniforms=None, gather: bool = True) -> Selection:
+        h = self.config.hidden_size
+        qo, bk, bvv = _f32(encoded.query_output), _f32(encoded.bank_keys), _f32(encoded.bank_values)
+        q, r = qo.size // h, bk.size // h
+        ev = abi.KcEncodedView(q, r, qo.ctypes.data, bk.ctypes.data if r else None, bvv.ctypes.data if r else None)
+        p = np.empty(max(1, q * r), dtype=np.float32)
+        idx = np.empty(max(1, q), dtype=np.uint32)
+        g = np.empty(max(1, q * h), dtype=np.float32) if gather else None
+        m = _f32(mask) if mask is not None else None
+        if m is not None and m.size != q * r:
+            raise ValueError(f"the selection mask must be [{q}, {r}]")
+        rule_s = None
+        keep = []
+        if rule is not None:
+            sa, ba, bs, bb = _u32(rule.schema_allow), _u32(rule.band_allow), _u32(bank_schema_ids), \
+                _u32(bank_band_ids)
+            keep += [sa, ba, bs, bb]
+            rule_s = abi.KcMaskRule(sa.ctypes.data, ba.ctypes.data, bs.ctypes.data, bb.ctypes.data)
+        u = np.ascontiguousarray(uniforms, dtype=np.float64) if uniforms is not None else None
+        abi.check(self._lib.kc_select(self._h, C.byref(ev), abi.ptr(m), C.byref(rule_s) if rule_s else None,
+                                      abi.ptr(u), p.ctypes.data, idx.ctypes.data, abi.ptr(g)), self._h)
+        return Selection(p[:q * r], idx[:q], g[:q * h] if g is not None else None)
+
+    # --- packed ragged batches ------------------------------------------------
+    def forward_batch(self, batch: FrameBatch, rule: MaskRule | None = None, uniforms=None,
+                      want_query_output: bool = False, p_capacity: int | None = None) -> dict:
+        """Pack, encode and select a whole batch; host arrays in and out."""
+        keep = [_u32(batch.token_ids), _u32(batch.field_roles), _u32(batch.schema_ids), _u32(batch.band_ids),
+                np.ascontiguousarray(batch.rec_off, dtype=np.uint64)]
+        tok, role, sch, band, off = keep
+        sa = ba = u = None
+        if rule is not None:
+            sa, ba = _u32(rule.schema_allow), _u32(rule.band_allow)
+        if uniforms is not None:
+            u = np.ascontiguousarray(uniforms, dtype=np.float64)
+        bv = abi.KcBatchView(batch.frames, batch.records, off.ctypes.data, tok.ctypes.data, role.ctypes.data,
+                             sch.ctypes.data, band.ctypes.data, abi.ptr(sa), abi.ptr(ba), abi.ptr(u))
+        nq = int((band == 5).sum())
+        if p_capacity is None:
+            rec = np.diff(off.astype(np.int64))
+            isq = np.add.reduceat((band == 5).astype(np.int64), off[:-1].astype(np.int64)) if batch.frames else 0
+            p_capacity = int((isq * (rec - isq)).sum())
+        p = np.empty(max(1, p_capacity), dtype=np.float32)
+        idx = np.empty(max(1, nq), dtype=np.uint32)
+        p_off = np.empty(batch.frames + 1, dtype=np.uint64)
+        q_off = np.empty(batch.frames + 1, dtype=np.uint64)
+        qo = np.empty(max(1, nq) * self.config.hidden_size, dtype=np.float32) if want_query_output else None
+        out = abi.KcBatchOut(p.ctypes.data, p.size, idx.ctypes.data, idx.size, p_off.ctypes.data, q_off.ctypes.data,
+                             abi.ptr(qo), 0, 0, 0, 0)
+        abi.check(self._lib.kc_forward_batch(self._h, C.byref(bv), C.byref(out)), self._h)
+        res = {"p": p[:out.total_p], "index": idx[:out.total_q], "p_off": p_off, "q_off": q_off,
+               "total_t": out.total_t, "total_r": out.total_r}
+        if qo is not None:
+            res["query_output"] = qo[:out.total_q * self.config.hidden_size]
+        return res
+
+    def forward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,
+                             schema_ids: int, band_ids: int, schema_allow: int | None = None,
+                             band_allow: int | None = None, uniforms: int | None = None) -> abi.KcDeviceResult:
+        """Device-resident batch (raw device pointers); results stay on the device."""
+        bv = abi.KcBatchView(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow,
+                             band_allow, uniforms)
+        res = abi.KcDeviceResult()
+        abi.check(self._lib.kc_forward_batch_device(self._h, C.byref(bv), C.byref(res)), self._h)
+        return res
+
+    # --- plumbing -------------------------------------------------------------
+    def set_stream(self, stream_ptr: int | None) -> None:
+        abi.check(self._lib.kc_set_stream(self._h, stream_ptr), self._h)
+
+    def synchronize(self) -> None:
+        abi.check(self._lib.kc_synchronize(self._h), self._h)
+
+    def profile(self, enable: bool) -> None:
+        abi.check(self._lib.kc_profile(self._h, int(enable)), self._h)
+
+    def profile_read(self, reset: bool = False) -> dict:
+        st = abi.KcStageTimes()
+        abi.check(self._lib.kc_profile_read(self._h, C.byref(st), int(reset)), self._h)
+        return st.as_dict()
+
+    def launch_count(self) -> int:
+        return int(self._lib.kc_launch_count(self._h))
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+def cuda_backend(device: int = 0) -> Callable[[BrainForwardConfig, BrainForwardWeights], CudaBrainBackend]:
+    """BrainBackendFactory for the CUDA backend (cf. gpuBackend, webgpu/src/backend.ts:174-181)."""
+    return lambda config, weights: CudaBrainBackend(config, weights, device)

@@ -1,0 +1,592 @@
+// exact.cuh — the forward in the reference oracle's exact arithmetic.
+//
+// Every kernel here reproduces packages/krystal/src/forward/oracle.ts the way
+// JavaScript evaluates it: each dot product / weighted sum is ONE f64
+// accumulator walked in the oracle's index order (products of two f32 are
+// exact in f64, so an f64 FMA equals the oracle's multiply-then-add), and
+// results are rounded to f32 exactly where the oracle stores into a
+// Float32Array. Reductions whose order matters (softmax sums) are walked
+// sequentially; order-free ones (max, any/all, first-argmax) run in parallel.
+// The file is compiled with --fmad=false so that no a*b+c outside an
+// explicit fma() is contracted.
+#pragma once
+#include "common.cuh"
+
+namespace kc {
+
+// ---------------------------------------------------------------------------
+// fieldEmbed (oracle.ts:151-184): x[t] = token + field + schema + band +
+// stream + pos rows, summed in that order in f64, stored f32.
+// One warp per compact token, float4 per lane (H = 128).
+// ---------------------------------------------------------------------------
+struct EmbedArgs {
+  const uint32_t* tok_recpos;
+  const uint32_t* token_ids;
+  const uint32_t* field_roles;
+  const uint32_t* schema_ids;
+  const uint32_t* band_ids;
+  const uint32_t* token_rows;
+  const float* table;  // embeddings page
+  uint64_t tb_token, tb_field, tb_schema, tb_band, tb_stream, tb_pos;
+  float* x;  // [T,128]
+  uint64_t t;
+};
+
+__global__ void __launch_bounds__(256) k_embed_exact(EmbedArgs a) {
+  const uint64_t t = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= a.t) return;
+  const int d = (threadIdx.x & 31) * 4;
+  const uint32_t rp = a.tok_recpos[t];
+  const uint32_t g = rp >> 3, l = rp & 7u;
+  const uint32_t tok = a.token_rows[a.token_ids[uint64_t(g) * KC_RW + l]];
+  const uint32_t role = a.token_rows[a.field_roles[uint64_t(g) * KC_RW + l]];
+  const uint32_t band = a.band_ids[g];
+  const uint32_t stream = band == KC_QUERY_BAND_ID ? 1u : 0u;
+  const float4 r0 = *reinterpret_cast<const float4*>(a.table + a.tb_token + uint64_t(tok) * KC_H + d);
+  const float4 r1 = *reinterpret_cast<const float4*>(a.table + a.tb_field + uint64_t(role) * KC_H + d);
+  const float4 r2 = *reinterpret_cast<const float4*>(a.table + a.tb_schema + uint64_t(a.schema_ids[g]) * KC_H + d);
+  const float4 r3 = *reinterpret_cast<const float4*>(a.table + a.tb_band + uint64_t(band) * KC_H + d);
+  const float4 r4 = *reinterpret_cast<const float4*>(a.table + a.tb_stream + uint64_t(stream) * KC_H + d);
+  const float4 r5 = *reinterpret_cast<const float4*>(a.table + a.tb_pos + uint64_t(l) * KC_H + d);
+  auto sum6 = [](float v0, float v1, float v2, float v3, float v4, float v5) {
+    double v = 0.0;
+    v += double(v0); v += double(v1); v += double(v2); v += double(v3); v += double(v4); v += double(v5);
+    return f32(v);
+  };
+  float4 o;
+  o.x = sum6(r0.x, r1.x, r2.x, r3.x, r4.x, r5.x);
+  o.y = sum6(r0.y, r1.y, r2.y, r3.y, r4.y, r5.y);
+  o.z = sum6(r0.z, r1.z, r2.z, r3.z, r4.z, r5.z);
+  o.w = sum6(r0.w, r1.w, r2.w, r3.w, r4.w, r5.w);
+  *reinterpret_cast<float4*>(a.x + t * KC_H + d) = o;
+}
+
+// ---------------------------------------------------------------------------
+// matmulOracle (oracle.ts:114-125) and its fused consumers:
+//   C = f32(A·Bᵀ)                          kEpiStore
+//   C = relu(f32(A·Bᵀ))                    kEpiRelu   (reluOracle of the W1 output)
+//   C = f32(C + f32(A·Bᵀ))                 kEpiResid  (addInPlace of the W2 output)
+// A [M,K] f32, B [N,K] f32 (weights, [out,in]); every output is one f64
+// accumulator over k = 0..K-1 in order. 128x128 CTA tile, 8x8 per thread,
+// operands converted to f64 once when staged in shared memory.
+// Requires N % 128 == 0, K % 8 == 0, 16-byte aligned rows.
+// ---------------------------------------------------------------------------
+enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2 };
+
+template <int EPI>
+__global__ void __launch_bounds__(256, 1) k_dgemm_exact(const float* __restrict__ A, const float* __restrict__ B,
+                                                       float* C, int M, int N, int K, int lda, int ldb, int ldc) {
+  constexpr int BM = 128, BN = 128, BK = 8;
+  __shared__ double As[2][BK][BM];
+  __shared__ double Bs[2][BK][BN];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = int64_t(blockIdx.x) * BM;  // row tiles on x: M may exceed 65535 tiles
+  const int n0 = blockIdx.y * BN;
+  const int lr = tid >> 1, lc = (tid & 1) * 4;
+  const bool a_ok = m0 + lr < M;
+  const float* Ap = A + (m0 + lr) * int64_t(lda) + lc;
+  const float* Bp = B + int64_t(n0 + lr) * ldb + lc;
+
+  double acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+
+  float4 ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 rb = __ldg(reinterpret_cast<const float4*>(Bp));
+  As[0][lc + 0][lr] = ra.x; As[0][lc + 1][lr] = ra.y; As[0][lc + 2][lr] = ra.z; As[0][lc + 3][lr] = ra.w;
+  Bs[0][lc + 0][lr] = rb.x; Bs[0][lc + 1][lr] = rb.y; Bs[0][lc + 2][lr] = rb.z; Bs[0][lc + 3][lr] = rb.w;
+  __syncthreads();
+
+  const int steps = K / BK;
+  for (int s = 0; s < steps; s++) {
+    const int cur = s & 1;
+    const bool more = s + 1 < steps;
+    if (more) {
+      ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap + (s + 1) * BK)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      rb = __ldg(reinterpret_cast<const float4*>(Bp + (s + 1) * BK));
+    }
+#pragma unroll
+    for (int kk = 0; kk < BK; kk++) {
+      double av[8], bv[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) av[i] = As[cur][kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 8; j++) bv[j] = Bs[cur][kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+    }
+    if (more) {
+      const int nx = cur ^ 1;
+      As[nx][lc + 0][lr] = ra.x; As[nx][lc + 1][lr] = ra.y; As[nx][lc + 2][lr] = ra.z; As[nx][lc + 3][lr] = ra.w;
+      Bs[nx][lc + 0][lr] = rb.x; Bs[nx][lc + 1][lr] = rb.y; Bs[nx][lc + 2][lr] = rb.z; Bs[nx][lc + 3][lr] = rb.w;
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int64_t row = m0 + ty + 16 * i;
+    if (row >= M) continue;
+    float* cp = C + row * int64_t(ldc) + n0 + tx;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float v = f32(acc[i][j]);
+      if (EPI == kEpiStore) cp[16 * j] = v;
+      else if (EPI == kEpiRelu) cp[16 * j] = js_relu(v);
+      else cp[16 * j] = f32(double(cp[16 * j]) + double(v));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// softmaxRow (oracle.ts:38-49) over a warp-held row of <= 8 f32 scores,
+// evaluated by a single lane (the rows are at most 8 long).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void softmax_small(float* v, int count) {
+  double mx = -INFINITY;
+  for (int i = 0; i < count; i++) mx = js_max(mx, double(v[i]));
+  double sum = 0.0;
+  for (int i = 0; i < count; i++) {
+    const double e = exp(double(v[i]) - mx);
+    v[i] = f32(e);
+    sum += e;
+  }
+  const double inv = 1.0 / js_max(sum, 1e-20);
+  for (int i = 0; i < count; i++) v[i] = f32(double(v[i]) * inv);
+}
+
+// ---------------------------------------------------------------------------
+// Record-local attention (attentionOracle local mode, oracle.ts:64-105, as
+// called at :255) fused with the residual add (addInPlace, :256).
+// One warp per record; lane = token*4 + head. q/k/v of the record are
+// staged in shared memory; the head's output overwrites its q slice, then
+// the warp adds the record's rows into x with coalesced stores.
+// ---------------------------------------------------------------------------
+struct LocalAttnArgs {
+  const float* qkv;          // [T,384]: q | k | v
+  float* x;                  // [T,128], updated in place
+  const uint32_t* rec_start; // [N]
+  const uint2* rec_meta;     // [N] (.y & 15 = token count)
+  uint64_t records;
+  double scale;              // 1/sqrt(headDim)
+};
+
+__global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
+  __shared__ float sm[4][KC_RW][3 * KC_H];  // 48 KB
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = uint64_t(blockIdx.x) * 4 + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  if (cnt == 0) return;
+  float(*rec)[3 * KC_H] = sm[warp];
+  // stage q|k|v rows: cnt * 384 floats = cnt * 96 float4
+  const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
+  float4* dst = reinterpret_cast<float4*>(&rec[0][0]);
+  for (int i = lane; i < cnt * 96; i += 32) dst[i] = src[i];
+  __syncwarp();
+  const int ti = lane >> 2, head = lane & 3, hb = head * KC_HEAD_DIM;
+  float p[KC_RW];
+  if (ti < cnt) {
+    for (int j = 0; j < cnt; j++) {
+      double s = 0.0;
+#pragma unroll 8
+      for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(rec[ti][hb + d]), double(rec[j][KC_H + hb + d]), s);
+      p[j] = f32(s * a.scale + 0.0);
+    }
+    bool blocked = true;
+    for (int j = 0; j < cnt; j++)
+      if (double(p[j]) >= -1e29) { blocked = false; break; }
+    if (blocked) {
+      for (int j = 0; j < cnt; j++) p[j] = 0.0f;
+    } else {
+      softmax_small(p, cnt);
+    }
+  }
+  __syncwarp();
+  if (ti < cnt) {
+    float out[KC_HEAD_DIM];
+#pragma unroll 4
+    for (int d = 0; d < KC_HEAD_DIM; d++) {
+      double v = 0.0;
+      for (int j = 0; j < cnt; j++) v = fma(double(p[j]), double(rec[j][2 * KC_H + hb + d]), v);
+      out[d] = f32(v);
+    }
+    // every lane is done reading q (only lane ti*4+head reads this slice)
+#pragma unroll
+    for (int d = 0; d < KC_HEAD_DIM; d++) rec[ti][hb + d] = out[d];
+  }
+  __syncwarp();
+  float* xr = a.x + uint64_t(start) * KC_H;
+  for (int i = lane; i < cnt * KC_H; i += 32) {
+    const int r = i >> 7, d = i & 127;
+    xr[i] = f32(double(xr[i]) + double(rec[r][d]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// poolRecord (oracle.ts:186-224) for every record of the batch: two learned-
+// query softmax poolings over the record's tokens. Bank records write their
+// key and value rows; questions write their value row (the mixer's input
+// state; the pooled query key is never read downstream).
+// One warp per record.
+// ---------------------------------------------------------------------------
+struct PoolArgs {
+  const float* x;            // [T,128]
+  const float* pool;         // [2,128]
+  const uint32_t* rec_start;
+  const uint2* rec_meta;
+  const uint32_t* rec_row;   // bank row, or question row | 0x80000000
+  uint64_t records;
+  double scale;              // 1/sqrt(H)
+  float* bank_keys;          // [R,128]
+  float* bank_values;        // [R,128]
+  float* query_values;       // [Q,128]
+};
+
+__global__ void __launch_bounds__(256) k_pool_exact(PoolArgs a) {
+  __shared__ float xs[8][KC_RW][KC_H];  // 32 KB
+  __shared__ float ps[2][KC_H];
+  __shared__ float sc[8][2][KC_RW];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 2 * KC_H; i += 256) (&ps[0][0])[i] = a.pool[i];
+  __syncthreads();
+  const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  const uint32_t row = a.rec_row[g];
+  const bool isq = row & 0x80000000u;
+  const uint32_t r = row & 0x7fffffffu;
+  float* key_out = isq ? nullptr : a.bank_keys + uint64_t(r) * KC_H;
+  float* val_out = isq ? a.query_values + uint64_t(r) * KC_H : a.bank_values + uint64_t(r) * KC_H;
+  if (cnt == 0) {  // a record without tokens pools to zeros (oracle.ts:195)
+    for (int d = lane; d < KC_H; d += 32) {
+      if (key_out) key_out[d] = 0.0f;
+      val_out[d] = 0.0f;
+    }
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H);
+  float4* dst = reinterpret_cast<float4*>(&xs[warp][0][0]);
+  for (int i = lane; i < cnt * 32; i += 32) dst[i] = src[i];
+  __syncwarp();
+  // lanes 0..7: key scores, lanes 8..15: value scores
+  if (lane < 16) {
+    const int j = lane & 7, which = lane >> 3;
+    if (j < cnt) {
+      double s = 0.0;
+      for (int d = 0; d < KC_H; d++) s = fma(double(ps[which][d]), double(xs[warp][j][d]), s);
+      sc[warp][which][j] = f32(s * a.scale);
+    }
+  }
+  __syncwarp();
+  if (lane == 0 || lane == 8) softmax_small(sc[warp][lane >> 3], cnt);
+  __syncwarp();
+  for (int d = lane; d < KC_H; d += 32) {
+    double ka = 0.0, va = 0.0;
+    for (int j = 0; j < cnt; j++) {
+      const double s = xs[warp][j][d];
+      ka = fma(double(sc[warp][0][j]), s, ka);
+      va = fma(double(sc[warp][1][j]), s, va);
+    }
+    if (key_out) key_out[d] = f32(ka);
+    val_out[d] = f32(va);
+  }
+}
+
+// Block-wide helpers for the per-question kernels (NT threads).
+template <int NT>
+__device__ __forceinline__ double block_js_max(double v, double* red) {
+  for (int o = 16; o; o >>= 1) v = js_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double r = red[0];
+  for (int w = 1; w < NT / 32; w++) r = js_max(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ int block_or(int v, int* red) {
+  v = __any_sync(0xffffffffu, v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = 0;
+  for (int w = 0; w < NT / 32; w++) r |= red[w];
+  __syncthreads();
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t r = 0;
+  for (int w = 0; w < NT / 32; w++) r += red[w];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Mixer cross-attention (attentionOracle dense mode with the session's open
+// mixer mask, oracle.ts:292, session.ts:146) fused with the residual add
+// (:293). One CTA of 128 threads per question; the frame's bank rows are
+// R = r_off[f+1]-r_off[f] (<= max_r). Dynamic shared memory: 4 heads x R
+// f32 scores + 4 x R f64 exponentials.
+// ---------------------------------------------------------------------------
+struct CrossAttnArgs {
+  const float* mq;          // [Q,128]
+  const float* mk;          // [R,128]
+  const float* mv;          // [R,128]
+  float* query;             // [Q,128], updated in place
+  const uint32_t* query_frame;
+  const uint64_t* r_off;
+  uint32_t max_r;
+  double scale;             // 1/sqrt(headDim)
+};
+
+__global__ void __launch_bounds__(128) k_cross_attn_exact(CrossAttnArgs a) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ float qs[KC_H];
+  __shared__ double sums[KC_HEADS];
+  const uint32_t qi = blockIdx.x;
+  const uint32_t f = a.query_frame[qi];
+  const uint64_t rb = a.r_off[f];
+  const int R = int(a.r_off[f + 1] - rb);
+  double* e64 = reinterpret_cast<double*>(dyn);                  // [4][max_r]
+  float* sc = reinterpret_cast<float*>(e64 + 4 * size_t(a.max_r)); // [4][max_r]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  qs[tid] = a.mq[uint64_t(qi) * KC_H + tid];
+  __syncthreads();
+  // scores: thread handles (j, head) pairs; one f64 accumulator over d
+  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
+    const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
+    const float* kr = a.mk + (rb + j) * KC_H + hb;
+    double s = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(qs[hb + d]), double(kr[d]), s);
+    sc[head * a.max_r + j] = f32(s * a.scale + 0.0);
+  }
+  __syncthreads();
+  // per head (warp w = head w): all-blocked test, max, exponentials
+  {
+    const int head = warp;
+    float* row = sc + head * a.max_r;
+    bool any_open = false;
+    double mx = -INFINITY;
+    for (int j = lane; j < R; j += 32) {
+      any_open |= double(row[j]) >= -1e29;
+      mx = js_max(mx, double(row[j]));
+    }
+    any_open = __any_sync(0xffffffffu, any_open);
+    for (int o = 16; o; o >>= 1) mx = js_max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (any_open) {
+      double* er = e64 + head * size_t(a.max_r);
+      for (int j = lane; j < R; j += 32) {
+        const double e = exp(double(row[j]) - mx);
+        er[j] = e;
+        row[j] = f32(e);
+      }
+      __syncwarp();
+      if (lane == 0) {  // softmaxRow's running sum, in index order
+        double sum = 0.0;
+        for (int j = 0; j < R; j++) sum += er[j];
+        sums[head] = 1.0 / js_max(sum, 1e-20);
+      }
+      __syncwarp();
+      const double inv = sums[head];
+      for (int j = lane; j < R; j += 32) row[j] = f32(double(row[j]) * inv);
+    } else {
+      for (int j = lane; j < R; j += 32) row[j] = 0.0f;
+    }
+  }
+  __syncthreads();
+  // P·V: thread (head, d), one f64 accumulator over j in order
+  {
+    const int head = tid >> 5, d = tid & 31, col = head * KC_HEAD_DIM + d;
+    const float* row = sc + head * a.max_r;
+    double v = 0.0;
+    for (int j = 0; j < R; j++) v = fma(double(row[j]), double(a.mv[(rb + j) * KC_H + col]), v);
+    float* qp = a.query + uint64_t(qi) * KC_H + col;
+    *qp = f32(double(*qp) + double(f32(v)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// selectorOracle (oracle.ts:332-382) for one question per CTA:
+// score = f32(qProj·kProj · (1/sqrt(H)) + mask), all-blocked rows -> p = 0 and
+// KC_NO_SELECTION, softmaxRow, first-max argmax over the stored p (or
+// sampleRow, sampling.ts:41-57), optional soft gather.
+// The mask is the open mask, an explicit [Q,R] mask, or the rule form of
+// selectionMask (host/learn.ts:215-232) with reopen-if-none-admitted (:229).
+// ---------------------------------------------------------------------------
+struct SelectArgs {
+  const float* sq;          // [Q,128] query projections
+  const float* sk;          // [R,128] bank key projections
+  const float* bank_values; // [R,128], for the gather (may be null)
+  const uint32_t* query_frame;
+  const uint64_t* r_off;
+  const uint64_t* q_off;
+  const uint64_t* p_off;
+  const float* mask;        // explicit mask laid out like p, or null
+  const uint32_t* schema_allow; // rule, or null
+  const uint32_t* band_allow;
+  const uint32_t* bank_rec;  // bank row -> record (for the rule)
+  const uint32_t* schema_ids;
+  const uint32_t* band_ids;
+  const double* uniforms;   // [Q] or null
+  uint32_t max_r;
+  double scale;             // 1/sqrt(H)
+  float* p;                 // [sum Q_f R_f]
+  uint32_t* index;          // [Q]
+  float* gather;            // [Q,128] or null
+};
+
+__global__ void __launch_bounds__(256) k_select_exact(SelectArgs a) {
+  constexpr int NT = 256;
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ double qs[KC_H];
+  __shared__ double red[NT / 32];
+  __shared__ int redi[NT / 32];
+  __shared__ uint32_t redu[NT / 32];
+  __shared__ double inv_s;
+  __shared__ float bestv[NT / 32];
+  __shared__ uint32_t besti[NT / 32];
+  const uint32_t qi = blockIdx.x;
+  const uint32_t f = a.query_frame[qi];
+  const uint64_t rb = a.r_off[f];
+  const int R = int(a.r_off[f + 1] - rb);
+  const uint64_t il = qi - a.q_off[f];  // question index within the frame
+  float* prow = a.p + a.p_off[f] + il * uint64_t(R);
+  if (R == 0) {
+    if (threadIdx.x == 0) a.index[qi] = KC_INVALID;
+    return;
+  }
+  double* e64 = reinterpret_cast<double*>(dyn);               // [max_r]
+  float* sc = reinterpret_cast<float*>(e64 + size_t(a.max_r)); // [max_r]
+  const int tid = threadIdx.x;
+  if (tid < KC_H) qs[tid] = a.sq[uint64_t(qi) * KC_H + tid];
+
+  // mask rule: admitted count first (a row nothing admits is reopened)
+  bool reopen = false;
+  const uint32_t* sa = nullptr;
+  uint32_t ba = 0;
+  if (a.schema_allow) {
+    sa = a.schema_allow + uint64_t(qi) * 8;
+    ba = a.band_allow[qi];
+    uint32_t admitted = 0;
+    for (int j = tid; j < R; j += NT) {
+      const uint32_t g = a.bank_rec[rb + j];
+      const uint32_t s = a.schema_ids[g], b = a.band_ids[g];
+      admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
+    }
+    reopen = block_sum_u32<NT>(admitted, redu) == 0;
+  }
+  __syncthreads();
+
+  for (int j = tid; j < R; j += NT) {
+    const float* kr = a.sk + (rb + j) * KC_H;
+    double s = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < KC_H; d++) s = fma(qs[d], double(kr[d]), s);
+    float m = 0.0f;
+    if (a.mask) {
+      m = a.mask[a.p_off[f] + il * uint64_t(R) + j];
+    } else if (sa && !reopen) {
+      const uint32_t g = a.bank_rec[rb + j];
+      const uint32_t sid = a.schema_ids[g], b = a.band_ids[g];
+      const bool ok = sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u);
+      m = ok ? 0.0f : -1e30f;
+    }
+    sc[j] = f32(s * a.scale + double(m));
+  }
+  __syncthreads();
+
+  // scores.every(score => score < -1e29): NaN is NOT blocked here
+  int open = 0;
+  double mx = -INFINITY;
+  for (int j = tid; j < R; j += NT) {
+    open |= !(double(sc[j]) < -1e29);
+    mx = js_max(mx, double(sc[j]));
+  }
+  const bool all_blocked = !block_or<NT>(open, redi);
+  if (all_blocked) {
+    for (int j = tid; j < R; j += NT) sc[j] = 0.0f;
+  } else {
+    mx = block_js_max<NT>(mx, red);
+    for (int j = tid; j < R; j += NT) {
+      const double e = exp(double(sc[j]) - mx);
+      e64[j] = e;
+      sc[j] = f32(e);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      double sum = 0.0;
+      for (int j = 0; j < R; j++) sum += e64[j];
+      inv_s = 1.0 / js_max(sum, 1e-20);
+    }
+    __syncthreads();
+    const double inv = inv_s;
+    for (int j = tid; j < R; j += NT) sc[j] = f32(double(sc[j]) * inv);
+  }
+  __syncthreads();
+  for (int j = tid; j < R; j += NT) prow[j] = sc[j];
+
+  // first j with the largest p (strict > scan from best = 0, oracle.ts:359-363):
+  // the first index of the maximum over non-NaN p, unless p[0] is NaN.
+  float bv = -INFINITY;
+  uint32_t bi = KC_INVALID;
+  for (int j = tid; j < R; j += NT) {
+    const float v = sc[j];
+    if (v == v && (bi == KC_INVALID || v > bv)) { bv = v; bi = uint32_t(j); }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi != KC_INVALID && (bi == KC_INVALID || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+  }
+  if ((tid & 31) == 0) { bestv[tid >> 5] = bv; besti[tid >> 5] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    float v = bestv[0];
+    uint32_t b = besti[0];
+    for (int w = 1; w < NT / 32; w++) {
+      const float ov = bestv[w];
+      const uint32_t oi = besti[w];
+      if (oi != KC_INVALID && (b == KC_INVALID || ov > v || (ov == v && oi < b))) { v = ov; b = oi; }
+    }
+    uint32_t best = (sc[0] != sc[0] || b == KC_INVALID) ? 0u : b;
+    if (all_blocked) {
+      best = KC_INVALID;
+    } else if (a.uniforms) {  // sampleRow (sampling.ts:41-57)
+      const double u = a.uniforms[qi];
+      double cum = 0.0;
+      int last = -1, drawn = -2;
+      for (int j = 0; j < R; j++) {
+        const double w = sc[j];
+        if (!(w > 0)) continue;
+        last = j;
+        cum += w;
+        if (u < cum) { drawn = j; break; }
+      }
+      if (drawn == -2) drawn = last;
+      best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
+    }
+    a.index[qi] = best;
+  }
+  if (a.gather) {
+    for (int d = tid; d < KC_H; d += NT) {
+      double g = 0.0;
+      for (int j = 0; j < R; j++) g = fma(double(sc[j]), double(a.bank_values[(rb + j) * KC_H + d]), g);
+      a.gather[uint64_t(qi) * KC_H + d] = f32(g);
+    }
+  }
+}
+
+}  // namespace kc

@@ -1,0 +1,829 @@
+// krystal_cuda.cu — the C ABI (include/krystal_cuda.h) and the batch driver.
+//
+// One handle = one device, one stream, one device copy of the weight page,
+// and a grow-only workspace sized to the largest batch seen. A batch runs as:
+//
+//   pack      k_frame_scan -> k_frame_offsets -> (one 64-byte readback of the
+//             batch totals, the only host wait) -> k_record_rows
+//   embed     k_embed_exact                                 fieldEmbed
+//   encoder   per block: QKV GEMM, local attention + residual,
+//             W1 GEMM + ReLU, W2 GEMM + residual            oracle.ts:250-259
+//   pool      k_pool_exact                                  oracle.ts:261-283
+//   mixer     per block: Q/K/V GEMMs, cross-attention + residual,
+//             W1 GEMM + ReLU, W2 GEMM + residual            oracle.ts:285-296
+//   selector  Wq/Wk GEMMs, k_select_exact                   oracle.ts:332-382
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/krystal_cuda.h"
+#include "common.cuh"
+#include "exact.cuh"
+#include "pack.cuh"
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+cudaError_t ensure(DevBuf& b, size_t bytes) {
+  if (bytes <= b.cap && b.p) return cudaSuccess;
+  if (b.p) cudaFree(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  size_t want = bytes < 256 ? 256 : bytes;
+  want = (want + 255) & ~size_t(255);
+  cudaError_t e = cudaMalloc(&b.p, want);
+  if (e == cudaSuccess) b.cap = want;
+  return e;
+}
+
+template <typename T>
+T* P(DevBuf& b) { return static_cast<T*>(b.p); }
+
+struct Dims {
+  uint32_t h, heads, hd, ffn, enc, mix, route;
+  uint32_t token_space, field_space, schema_space, band_space, stream_space, pos_space;
+  uint64_t tb_token, tb_field, tb_schema, tb_band, tb_stream, tb_pos;
+  uint64_t emb_elems, off_enc, off_pool, off_mixer, off_swq, off_swk, off_dec, off_val, total, block;
+};
+
+Dims dims_of(const kc_config* c) {
+  Dims d{};
+  d.h = c->hidden_size; d.heads = c->head_count; d.hd = c->head_dim; d.ffn = c->ffn_size;
+  d.enc = c->encoder_blocks; d.mix = c->mixer_blocks; d.route = c->route_kind_count;
+  d.token_space = c->token_space; d.field_space = c->field_space; d.schema_space = c->schema_space;
+  d.band_space = c->band_space; d.stream_space = c->stream_space; d.pos_space = c->pos_space;
+  const uint64_t h = d.h, f = d.ffn;
+  uint64_t cur = 0;
+  d.tb_token = cur; cur += uint64_t(d.token_space) * h;
+  d.tb_field = cur; cur += uint64_t(d.field_space) * h;
+  d.tb_schema = cur; cur += uint64_t(d.schema_space) * h;
+  d.tb_band = cur; cur += uint64_t(d.band_space) * h;
+  d.tb_stream = cur; cur += uint64_t(d.stream_space) * h;
+  d.tb_pos = cur; cur += uint64_t(d.pos_space) * h;
+  d.emb_elems = cur;
+  d.block = 3 * h * h + 2 * f * h;
+  d.off_enc = cur; cur += d.block * d.enc;
+  d.off_pool = cur; cur += 2 * h;
+  d.off_mixer = cur; cur += d.block * d.mix;
+  d.off_swq = cur; cur += h * h;
+  d.off_swk = cur; cur += h * h;
+  d.off_dec = cur; cur += uint64_t(d.route) * 3 * h;
+  d.off_val = cur; cur += 3 * h;
+  d.total = cur;
+  return d;
+}
+
+struct Workspace {
+  // staged inputs (host entry points)
+  DevBuf rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow, band_allow, uniforms, mask;
+  DevBuf bank_schema, bank_band;
+  // pack
+  DevBuf rec_meta, frame_t, frame_q, frame_r, t_off, q_off, r_off, p_off, totals;
+  DevBuf tok_recpos, rec_start, rec_row, bank_rec, bank_frame, query_rec, query_frame;
+  // activations
+  DevBuf x, qkv, bk, bv, mk, mv, qstate, mq, mh, sq, sk, p, index, gather;
+  // weight-row scatter staging
+  DevBuf rows_val, rows_off;
+};
+
+enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStCount };
+
+}  // namespace
+
+struct kc_handle {
+  std::mutex mu;
+  int device = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  Dims d{};
+  float* w = nullptr;
+  uint32_t* token_rows = nullptr;
+  uint32_t token_rows_len = 0;
+  Workspace ws;
+  kc::FrameTotals* h_tot = nullptr;  // pinned
+  std::string err;
+  uint64_t launches = 0;
+  // profiling
+  bool profiling = false;
+  kc_stage_times prof{};
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
+  std::vector<std::pair<int, size_t>> ev_used;  // (stage, index into ev_pool)
+  std::vector<double> ev_flops;
+};
+
+namespace {
+
+kc_status fail(kc_handle* h, kc_status s, const std::string& msg) {
+  if (h) h->err = msg;
+  else g_create_error = msg;
+  return s;
+}
+
+kc_status cuda_fail(kc_handle* h, cudaError_t e, const char* what) {
+  return fail(h, e == cudaErrorMemoryAllocation ? KC_ERR_CAPACITY : KC_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define KC_TRY(expr, what)                                     \
+  do {                                                         \
+    cudaError_t _e = (expr);                                   \
+    if (_e != cudaSuccess) return cuda_fail(h, _e, what);      \
+  } while (0)
+
+// Profiling: a pair of events around each launch group.
+struct ProfScope {
+  kc_handle* h;
+  int stage;
+  size_t idx = 0;
+  bool on;
+  ProfScope(kc_handle* hh, int st, double flops = 0) : h(hh), stage(st), on(hh->profiling) {
+    if (!on) return;
+    idx = h->ev_used.size();
+    if (idx >= h->ev_pool.size()) {
+      cudaEvent_t a, b;
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      h->ev_pool.emplace_back(a, b);
+    }
+    h->ev_used.emplace_back(stage, idx);
+    h->ev_flops.push_back(flops);
+    cudaEventRecord(h->ev_pool[idx].first, h->stream);
+  }
+  ~ProfScope() {
+    if (on) cudaEventRecord(h->ev_pool[idx].second, h->stream);
+  }
+};
+
+void prof_collect(kc_handle* h) {
+  if (!h->profiling || h->ev_used.empty()) return;
+  cudaStreamSynchronize(h->stream);
+  double* dst[kStCount] = {&h->prof.pack_ms, &h->prof.embed_ms, &h->prof.enc_gemm_ms, &h->prof.enc_attn_ms,
+                           &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms};
+  for (size_t i = 0; i < h->ev_used.size(); i++) {
+    float ms = 0;
+    auto& pr = h->ev_pool[h->ev_used[i].second];
+    cudaEventElapsedTime(&ms, pr.first, pr.second);
+    *dst[h->ev_used[i].first] += ms;
+    h->prof.total_ms += ms;
+    if (h->ev_used[i].first == kStEncGemm) {
+      h->prof.enc_gemm_launches++;
+      h->prof.enc_gemm_flops += h->ev_flops[i];
+    }
+  }
+  h->ev_used.clear();
+  h->ev_flops.clear();
+}
+
+template <int EPI>
+kc_status dgemm(kc_handle* h, const float* A, const float* B, float* C, uint64_t M, uint32_t N, uint32_t K) {
+  if (M == 0) return KC_OK;
+  dim3 grid(unsigned((M + 127) / 128), N / 128);
+  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(K), int(K), int(N));
+  h->launches++;
+  return KC_OK;
+}
+
+// Device-side view of one batch (all pointers on the handle's device).
+struct DevBatch {
+  uint32_t frames = 0;
+  uint64_t records = 0;
+  const uint64_t* rec_off = nullptr;
+  const uint32_t *token_ids = nullptr, *field_roles = nullptr, *schema_ids = nullptr, *band_ids = nullptr;
+  const uint32_t *schema_allow = nullptr, *band_allow = nullptr;
+  const double* uniforms = nullptr;
+};
+
+const char* bad_message(uint32_t code) {
+  switch (code) {
+    case kc::kBadTokenId: return "token id has no entry in tokenRows";
+    case kc::kBadTokenRow: return "token row outside the token table";
+    case kc::kBadRoleId: return "field role id has no entry in tokenRows";
+    case kc::kBadRoleRow: return "field role row outside the field table";
+    case kc::kBadSchema: return "schema id outside the schema table";
+    case kc::kBadBand: return "band id outside the band table";
+    case kc::kBadEmptyFrame: return "a frame with no records has nothing to think about";
+    case kc::kBadBank: return "bank exceeds capacity";
+    default: return "malformed frame";
+  }
+}
+
+// Encoder + pool + mixer (+ selector unless encode_only). Results stay in
+// the workspace: qstate [Q,H], bk/bv [R,H], p, index.
+kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
+  Workspace& ws = h->ws;
+  const Dims& d = h->d;
+  const uint32_t F = b.frames;
+  const uint64_t N = b.records;
+  if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "a batch with no frames");
+  KC_TRY(ensure(ws.rec_meta, N * sizeof(uint2)), "workspace");
+  KC_TRY(ensure(ws.frame_t, F * 4ull), "workspace");
+  KC_TRY(ensure(ws.frame_q, F * 4ull), "workspace");
+  KC_TRY(ensure(ws.frame_r, F * 4ull), "workspace");
+  KC_TRY(ensure(ws.t_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(ws.q_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(ws.r_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(ws.p_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(ws.totals, sizeof(kc::FrameTotals)), "workspace");
+  KC_TRY(ensure(ws.rec_start, N * 4), "workspace");
+  KC_TRY(ensure(ws.rec_row, N * 4), "workspace");
+  kc::FrameTotals* dtot = P<kc::FrameTotals>(ws.totals);
+  {
+    ProfScope ps(h, kStPack);
+    KC_TRY(cudaMemsetAsync(dtot, 0, sizeof(kc::FrameTotals), h->stream), "memset");
+    kc::k_frame_scan<256><<<F, 256, 0, h->stream>>>(
+        b.rec_off, F, b.token_ids, b.field_roles, b.schema_ids, b.band_ids, h->token_rows, h->token_rows_len,
+        d.token_space, d.field_space, d.schema_space, d.band_space, KC_MAX_BANK, P<uint2>(ws.rec_meta),
+        P<uint32_t>(ws.frame_t), P<uint32_t>(ws.frame_q), P<uint32_t>(ws.frame_r), dtot);
+    kc::k_frame_offsets<1024><<<1, 1024, 0, h->stream>>>(F, P<uint32_t>(ws.frame_t), P<uint32_t>(ws.frame_q),
+                                                          P<uint32_t>(ws.frame_r), P<uint64_t>(ws.t_off),
+                                                          P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+                                                          P<uint64_t>(ws.p_off), dtot);
+    h->launches += 2;
+    KC_TRY(cudaMemcpyAsync(h->h_tot, dtot, sizeof(kc::FrameTotals), cudaMemcpyDeviceToHost, h->stream), "readback");
+  }
+  KC_TRY(cudaStreamSynchronize(h->stream), "pack");
+  const kc::FrameTotals tot = *h->h_tot;
+  if (tot.bad) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "%s (%s %u)", bad_message(tot.bad),
+             tot.bad == kc::kBadEmptyFrame || tot.bad == kc::kBadBank ? "frame" : "record", tot.bad_where);
+    if (tot.bad == kc::kBadBank)
+      snprintf(buf, sizeof buf, "bank records of frame %u exceed capacity %u", tot.bad_where, KC_MAX_BANK);
+    return fail(h, tot.bad == kc::kBadBank ? KC_ERR_CAPACITY : KC_ERR_INVALID_ARG, buf);
+  }
+  const uint64_t T = tot.t, Q = tot.q, R = tot.r, PP = tot.p;
+  const uint32_t H = d.h, FF = d.ffn;
+  KC_TRY(ensure(ws.tok_recpos, T * 4), "workspace");
+  KC_TRY(ensure(ws.bank_rec, R * 4), "workspace");
+  KC_TRY(ensure(ws.bank_frame, R * 4), "workspace");
+  KC_TRY(ensure(ws.query_rec, Q * 4), "workspace");
+  KC_TRY(ensure(ws.query_frame, Q * 4), "workspace");
+  KC_TRY(ensure(ws.x, T * H * 4), "workspace");
+  KC_TRY(ensure(ws.qkv, T * (3 * H > FF ? 3 * H : FF) * 4ull), "workspace");
+  KC_TRY(ensure(ws.bk, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.bv, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.mk, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.mv, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.sk, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.qstate, Q * H * 4), "workspace");
+  KC_TRY(ensure(ws.mq, Q * H * 4), "workspace");
+  KC_TRY(ensure(ws.sq, Q * H * 4), "workspace");
+  KC_TRY(ensure(ws.mh, Q * FF * 4ull), "workspace");
+  KC_TRY(ensure(ws.p, PP * 4), "workspace");
+  KC_TRY(ensure(ws.index, Q * 4), "workspace");
+  {
+    ProfScope ps(h, kStPack);
+    kc::k_record_rows<256><<<F, 256, 0, h->stream>>>(
+        b.rec_off, F, b.token_ids, P<uint2>(ws.rec_meta), P<uint64_t>(ws.t_off), P<uint64_t>(ws.q_off),
+        P<uint64_t>(ws.r_off), P<uint32_t>(ws.tok_recpos), P<uint32_t>(ws.rec_start), P<uint32_t>(ws.rec_row),
+        P<uint32_t>(ws.bank_rec), P<uint32_t>(ws.query_rec), P<uint32_t>(ws.query_frame),
+        P<uint32_t>(ws.bank_frame));
+    h->launches++;
+  }
+  float* x = P<float>(ws.x);
+  float* qkv = P<float>(ws.qkv);
+  if (T > 0) {
+    ProfScope ps(h, kStEmbed);
+    kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
+                     h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
+                     x, T};
+    kc::k_embed_exact<<<unsigned((T + 7) / 8), 256, 0, h->stream>>>(ea);
+    h->launches++;
+  }
+  const double attn_scale = 1.0 / std::sqrt(double(d.hd));
+  const double h_scale = 1.0 / std::sqrt(double(H));
+  for (uint32_t blk = 0; blk < d.enc && T > 0; blk++) {
+    const float* W = h->w + d.off_enc + d.block * blk;
+    const float* w1 = W + 3ull * H * H;
+    const float* w2 = w1 + uint64_t(FF) * H;
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H);
+      dgemm<kc::kEpiStore>(h, x, W, qkv, T, 3 * H, H);
+    }
+    {
+      ProfScope ps(h, kStEncAttn);
+      kc::LocalAttnArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale};
+      kc::k_local_attn_exact<<<unsigned((N + 3) / 4), 128, 0, h->stream>>>(la);
+      h->launches++;
+    }
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF);
+      dgemm<kc::kEpiRelu>(h, x, w1, qkv, T, FF, H);
+    }
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF);
+      dgemm<kc::kEpiResid>(h, qkv, w2, x, T, H, FF);
+    }
+  }
+  {
+    ProfScope ps(h, kStPool);
+    kc::PoolArgs pa{x, h->w + d.off_pool, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), P<uint32_t>(ws.rec_row),
+                    N, h_scale, P<float>(ws.bk), P<float>(ws.bv), P<float>(ws.qstate)};
+    kc::k_pool_exact<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pa);
+    h->launches++;
+  }
+  if (Q > 0) {
+    ProfScope ps(h, kStMixer);
+    for (uint32_t blk = 0; blk < d.mix; blk++) {
+      const float* W = h->w + d.off_mixer + d.block * blk;
+      const float* w1 = W + 3ull * H * H;
+      const float* w2 = w1 + uint64_t(FF) * H;
+      dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), W, P<float>(ws.mq), Q, H, H);
+      dgemm<kc::kEpiStore>(h, P<float>(ws.bk), W + uint64_t(H) * H, P<float>(ws.mk), R, H, H);
+      dgemm<kc::kEpiStore>(h, P<float>(ws.bv), W + 2ull * H * H, P<float>(ws.mv), R, H, H);
+      kc::CrossAttnArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
+                           P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off), tot.max_r, attn_scale};
+      const size_t smem = size_t(tot.max_r) * 4 * (8 + 4);
+      kc::k_cross_attn_exact<<<unsigned(Q), 128, smem, h->stream>>>(ca);
+      h->launches++;
+      dgemm<kc::kEpiRelu>(h, P<float>(ws.qstate), w1, P<float>(ws.mh), Q, FF, H);
+      dgemm<kc::kEpiResid>(h, P<float>(ws.mh), w2, P<float>(ws.qstate), Q, H, FF);
+    }
+  }
+  if (!encode_only && Q > 0) {
+    ProfScope ps(h, kStSelector);
+    dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), h->w + d.off_swq, P<float>(ws.sq), Q, H, H);
+    dgemm<kc::kEpiStore>(h, P<float>(ws.bk), h->w + d.off_swk, P<float>(ws.sk), R, H, H);
+    kc::SelectArgs sa{};
+    sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk); sa.bank_values = nullptr;
+    sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
+    sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
+    sa.mask = nullptr; sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
+    sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
+    sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = h_scale;
+    sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = nullptr;
+    const size_t smem = size_t(tot.max_r) * (8 + 4);
+    kc::k_select_exact<<<unsigned(Q), 256, smem, h->stream>>>(sa);
+    h->launches++;
+  }
+  KC_TRY(cudaGetLastError(), "launch");
+  return KC_OK;
+}
+
+kc_status check_config(const kc_config* c) {
+  if (!c) return fail(nullptr, KC_ERR_INVALID_ARG, "config is null");
+  if (c->hidden_size != KC_H || c->head_count != KC_HEADS || c->head_dim != KC_HEAD_DIM)
+    return fail(nullptr, KC_ERR_CAPACITY, "hiddenSize/headCount/headDim must be 128/4/32 (the kernels' geometry)");
+  if (c->ffn_size == 0 || c->ffn_size % 128 != 0 || c->ffn_size > 1024)
+    return fail(nullptr, KC_ERR_CAPACITY, "ffnSize must be a multiple of 128 up to 1024");
+  if (c->pos_space < KC_RW || c->stream_space < 2 || c->band_space == 0 || c->schema_space == 0 ||
+      c->token_space == 0 || c->field_space == 0)
+    return fail(nullptr, KC_ERR_INVALID_ARG, "embedding table sizes are too small for the frame ABI");
+  if (!c->token_rows || c->token_rows_len == 0)
+    return fail(nullptr, KC_ERR_INVALID_ARG, "tokenRows is empty: a session supplies its own vocabulary");
+  return KC_OK;
+}
+
+bool weights_ok(const Dims& d, const kc_weights_view* w) {
+  if (!w || !w->embeddings || !w->pool || !w->selector_wq || !w->selector_wk || !w->value_head_wv) return false;
+  if (d.route && !w->decision_head_wh) return false;
+  if ((d.enc && !w->enc) || (d.mix && !w->mixer)) return false;
+  for (uint32_t b = 0; b < d.enc; b++)
+    if (!w->enc[b].wq || !w->enc[b].wk || !w->enc[b].wv || !w->enc[b].w1 || !w->enc[b].w2) return false;
+  for (uint32_t b = 0; b < d.mix; b++)
+    if (!w->mixer[b].wq || !w->mixer[b].wk || !w->mixer[b].wv || !w->mixer[b].w1 || !w->mixer[b].w2) return false;
+  return true;
+}
+
+kc_status upload_blocks(kc_handle* h, const kc_block_view* blocks, uint32_t n, uint64_t base) {
+  const Dims& d = h->d;
+  const uint64_t hh = uint64_t(d.h) * d.h, fh = uint64_t(d.ffn) * d.h;
+  for (uint32_t b = 0; b < n; b++) {
+    float* dst = h->w + base + d.block * b;
+    KC_TRY(cudaMemcpyAsync(dst, blocks[b].wq, hh * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    KC_TRY(cudaMemcpyAsync(dst + hh, blocks[b].wk, hh * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    KC_TRY(cudaMemcpyAsync(dst + 2 * hh, blocks[b].wv, hh * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    KC_TRY(cudaMemcpyAsync(dst + 3 * hh, blocks[b].w1, fh * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    KC_TRY(cudaMemcpyAsync(dst + 3 * hh + fh, blocks[b].w2, fh * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+  }
+  return KC_OK;
+}
+
+__global__ void k_scatter_rows(float* page, const float* vals, const uint32_t* offs, uint32_t n, uint32_t h) {
+  const uint32_t r = blockIdx.x;
+  if (r >= n) return;
+  for (uint32_t i = threadIdx.x; i < h; i += blockDim.x) page[uint64_t(offs[r]) + i] = vals[uint64_t(r) * h + i];
+}
+
+kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) {
+  const Dims& d = h->d;
+  if (!weights_ok(d, w)) return fail(h, KC_ERR_INVALID_ARG, "weights view is incomplete");
+  auto put = [&](uint64_t off, const float* src, uint64_t n) -> kc_status {
+    KC_TRY(cudaMemcpyAsync(h->w + off, src, n * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    return KC_OK;
+  };
+  kc_status s = KC_OK;
+  const uint64_t hh = uint64_t(d.h) * d.h;
+  const bool all = ch == nullptr;
+  if (all) {
+    if ((s = put(0, w->embeddings, d.emb_elems))) return s;
+  } else if (ch->embedding_rows_count) {
+    const uint32_t n = ch->embedding_rows_count;
+    std::vector<float> vals(uint64_t(n) * d.h);
+    for (uint32_t i = 0; i < n; i++) {
+      const uint32_t off = ch->embedding_rows[i];
+      if (uint64_t(off) + d.h > d.emb_elems) return fail(h, KC_ERR_INVALID_ARG, "embedding row outside the page");
+      memcpy(&vals[uint64_t(i) * d.h], w->embeddings + off, d.h * 4);
+    }
+    KC_TRY(ensure(h->ws.rows_val, vals.size() * 4), "workspace");
+    KC_TRY(ensure(h->ws.rows_off, n * 4ull), "workspace");
+    KC_TRY(cudaMemcpyAsync(h->ws.rows_val.p, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice, h->stream), "sync");
+    KC_TRY(cudaMemcpyAsync(h->ws.rows_off.p, ch->embedding_rows, n * 4ull, cudaMemcpyHostToDevice, h->stream), "sync");
+    k_scatter_rows<<<n, 128, 0, h->stream>>>(h->w, P<float>(h->ws.rows_val), P<uint32_t>(h->ws.rows_off), n, d.h);
+    h->launches++;
+  }
+  if (all || ch->blocks) {
+    if ((s = upload_blocks(h, w->enc, d.enc, d.off_enc))) return s;
+    if ((s = upload_blocks(h, w->mixer, d.mix, d.off_mixer))) return s;
+  }
+  if (all || ch->pool)
+    if ((s = put(d.off_pool, w->pool, 2ull * d.h))) return s;
+  if (all || ch->selector) {
+    if ((s = put(d.off_swq, w->selector_wq, hh))) return s;
+    if ((s = put(d.off_swk, w->selector_wk, hh))) return s;
+  }
+  if ((all || ch->decision_head) && d.route)
+    if ((s = put(d.off_dec, w->decision_head_wh, uint64_t(d.route) * 3 * d.h))) return s;
+  if (all || ch->value_head)
+    if ((s = put(d.off_val, w->value_head_wv, 3ull * d.h))) return s;
+  KC_TRY(cudaStreamSynchronize(h->stream), "sync");
+  return KC_OK;
+}
+
+template <typename T>
+kc_status stage(kc_handle* h, DevBuf& buf, const T* src, uint64_t n) {
+  KC_TRY(ensure(buf, n * sizeof(T)), "workspace");
+  if (n) KC_TRY(cudaMemcpyAsync(buf.p, src, n * sizeof(T), cudaMemcpyHostToDevice, h->stream), "upload");
+  return KC_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+uint32_t kc_abi_version(void) { return KC_ABI_VERSION; }
+
+kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int device, kc_handle** out) {
+  if (!out) return fail(nullptr, KC_ERR_INVALID_ARG, "out is null");
+  *out = nullptr;
+  kc_status s = check_config(config);
+  if (s) return s;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    return fail(nullptr, KC_ERR_NO_DEVICE, "no CUDA device");
+  }
+  if (device < 0 || device >= ndev) return fail(nullptr, KC_ERR_INVALID_ARG, "device index out of range");
+  DeviceGuard dg(device);
+  auto* h = new kc_handle();
+  h->device = device;
+  h->d = dims_of(config);
+  if (!weights_ok(h->d, weights)) {
+    delete h;
+    return fail(nullptr, KC_ERR_INVALID_ARG, "weights view is incomplete");
+  }
+  auto bail = [&](cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    kc_destroy(h);
+    return fail(nullptr, e == cudaErrorMemoryAllocation ? KC_ERR_CAPACITY : KC_ERR_CUDA, m);
+  };
+  cudaError_t e;
+  if ((e = cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking))) return bail(e, "stream");
+  h->stream = h->own;
+  if ((e = cudaMalloc(&h->w, h->d.total * 4))) return bail(e, "weights");
+  h->token_rows_len = config->token_rows_len;
+  if ((e = cudaMalloc(&h->token_rows, uint64_t(h->token_rows_len) * 4))) return bail(e, "tokenRows");
+  if ((e = cudaMemcpy(h->token_rows, config->token_rows, uint64_t(h->token_rows_len) * 4, cudaMemcpyHostToDevice)))
+    return bail(e, "tokenRows");
+  if ((e = cudaMallocHost(&h->h_tot, sizeof(kc::FrameTotals)))) return bail(e, "pinned");
+  if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(KC_MAX_BANK) * (8 + 4)))) return bail(e, "smem");
+  s = do_sync(h, weights, nullptr);
+  if (s) {
+    std::string m = h->err;
+    kc_destroy(h);
+    return fail(nullptr, s, m);
+  }
+  *out = h;
+  return KC_OK;
+}
+
+kc_status kc_sync(kc_handle* h, const kc_weights_view* weights, const kc_changes* changes) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  return do_sync(h, weights, changes);
+}
+
+kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_output, float* bank_keys,
+                    float* bank_values, uint32_t q_cap, uint32_t r_cap, uint32_t* q_out, uint32_t* r_out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!frame || !frame->token_ids || !frame->field_roles || !frame->schema_ids || !frame->band_ids)
+    return fail(h, KC_ERR_INVALID_ARG, "frame view is incomplete");
+  if (frame->slots == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
+  // compileActiveFrame's record walk (masks.ts:73-74): the active list in
+  // order, ending at the first unoccupied entry. Active records are compacted
+  // into a one-frame batch; slot numbers only name positions, so the
+  // forward is unchanged.
+  const uint32_t slots = frame->slots;
+  std::vector<uint32_t> act;
+  act.reserve(slots);
+  for (uint32_t i = 0; i < slots; i++) {
+    const uint32_t s = frame->active_record_indices ? frame->active_record_indices[i] : i;
+    if (s == KC_INVALID || s >= slots) break;
+    act.push_back(s);
+  }
+  const uint32_t n = uint32_t(act.size());
+  if (n == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
+  std::vector<uint32_t> tok(n * 8ull), role(n * 8ull), sch(n), bnd(n);
+  uint32_t q = 0;
+  for (uint32_t i = 0; i < n; i++) {
+    const uint32_t s = act[i];
+    memcpy(&tok[i * 8ull], frame->token_ids + s * 8ull, 32);
+    memcpy(&role[i * 8ull], frame->field_roles + s * 8ull, 32);
+    sch[i] = frame->schema_ids[s];
+    bnd[i] = frame->band_ids[s];
+    q += bnd[i] == KC_QUERY_BAND;
+  }
+  if (q == 0) return fail(h, KC_ERR_INVALID_ARG, "the frame must contain at least one query record for the mixer");
+  const uint32_t r = n - q;
+  if (q > q_cap || r > r_cap) return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the frame's Q/R");
+  const uint64_t off[2] = {0, n};
+  kc_status s;
+  Workspace& ws = h->ws;
+  if ((s = stage(h, ws.rec_off, off, 2)) || (s = stage(h, ws.token_ids, tok.data(), tok.size())) ||
+      (s = stage(h, ws.field_roles, role.data(), role.size())) || (s = stage(h, ws.schema_ids, sch.data(), n)) ||
+      (s = stage(h, ws.band_ids, bnd.data(), n)))
+    return s;
+  DevBatch b;
+  b.frames = 1; b.records = n; b.rec_off = P<uint64_t>(ws.rec_off);
+  b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
+  b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  if ((s = run_batch(h, b, true))) return s;
+  const uint64_t H = h->d.h;
+  KC_TRY(cudaMemcpyAsync(query_output, ws.qstate.p, q * H * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (r) {
+    KC_TRY(cudaMemcpyAsync(bank_keys, ws.bk.p, r * H * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+    KC_TRY(cudaMemcpyAsync(bank_values, ws.bv.p, r * H * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  }
+  KC_TRY(cudaStreamSynchronize(h->stream), "encode");
+  prof_collect(h);
+  if (q_out) *q_out = q;
+  if (r_out) *r_out = r;
+  return KC_OK;
+}
+
+kc_status kc_select(kc_handle* h, const kc_encoded_view* enc, const float* mask, const kc_mask_rule* rule,
+                    const double* uniforms, float* p, uint32_t* index, float* gather) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!enc || !enc->query_output || (enc->r && (!enc->bank_keys || !enc->bank_values)) || !p || !index)
+    return fail(h, KC_ERR_INVALID_ARG, "select arguments are incomplete");
+  if (rule && (!rule->schema_allow || !rule->band_allow || !rule->bank_schema_ids || !rule->bank_band_ids))
+    return fail(h, KC_ERR_INVALID_ARG, "mask rule is incomplete");
+  const uint32_t Q = enc->q, R = enc->r;
+  if (Q == 0) return KC_OK;
+  if (R > KC_MAX_BANK) return fail(h, KC_ERR_CAPACITY, "bank records exceed capacity");
+  const uint64_t H = h->d.h;
+  Workspace& ws = h->ws;
+  // a one-frame view: every question belongs to frame 0
+  const uint64_t r_off[2] = {0, R}, q_off[2] = {0, Q}, p_off[2] = {0, uint64_t(Q) * R};
+  std::vector<uint32_t> qframe(Q, 0u), bank_rec(R);
+  for (uint32_t j = 0; j < R; j++) bank_rec[j] = j;
+  kc_status s;
+  if ((s = stage(h, ws.r_off, r_off, 2)) || (s = stage(h, ws.q_off, q_off, 2)) || (s = stage(h, ws.p_off, p_off, 2)) ||
+      (s = stage(h, ws.query_frame, qframe.data(), Q)) || (s = stage(h, ws.bank_rec, bank_rec.data(), R)) ||
+      (s = stage(h, ws.qstate, enc->query_output, Q * H)) || (s = stage(h, ws.bk, enc->bank_keys, R * H)) ||
+      (s = stage(h, ws.bv, enc->bank_values, R * H)))
+    return s;
+  if (mask && (s = stage(h, ws.mask, mask, uint64_t(Q) * R))) return s;
+  if (rule) {
+    if ((s = stage(h, ws.schema_allow, rule->schema_allow, Q * 8ull)) ||
+        (s = stage(h, ws.band_allow, rule->band_allow, Q)) ||
+        (s = stage(h, ws.bank_schema, rule->bank_schema_ids, R)) || (s = stage(h, ws.bank_band, rule->bank_band_ids, R)))
+      return s;
+  }
+  if (uniforms && (s = stage(h, ws.uniforms, uniforms, Q))) return s;
+  KC_TRY(ensure(ws.sq, Q * H * 4), "workspace");
+  KC_TRY(ensure(ws.sk, R * H * 4), "workspace");
+  KC_TRY(ensure(ws.p, uint64_t(Q) * R * 4), "workspace");
+  KC_TRY(ensure(ws.index, Q * 4ull), "workspace");
+  KC_TRY(ensure(ws.gather, Q * H * 4), "workspace");
+  {
+    ProfScope ps(h, kStSelector);
+    dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), h->w + h->d.off_swq, P<float>(ws.sq), Q, uint32_t(H), uint32_t(H));
+    dgemm<kc::kEpiStore>(h, P<float>(ws.bk), h->w + h->d.off_swk, P<float>(ws.sk), R, uint32_t(H), uint32_t(H));
+    kc::SelectArgs sa{};
+    sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk); sa.bank_values = P<float>(ws.bv);
+    sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
+    sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
+    sa.mask = mask ? P<float>(ws.mask) : nullptr;
+    sa.schema_allow = rule ? P<uint32_t>(ws.schema_allow) : nullptr;
+    sa.band_allow = rule ? P<uint32_t>(ws.band_allow) : nullptr;
+    sa.bank_rec = P<uint32_t>(ws.bank_rec);
+    sa.schema_ids = rule ? P<uint32_t>(ws.bank_schema) : nullptr;
+    sa.band_ids = rule ? P<uint32_t>(ws.bank_band) : nullptr;
+    sa.uniforms = uniforms ? P<double>(ws.uniforms) : nullptr;
+    sa.max_r = R; sa.scale = 1.0 / std::sqrt(double(H));
+    sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = P<float>(ws.gather);
+    kc::k_select_exact<<<Q, 256, size_t(R) * 12, h->stream>>>(sa);
+    h->launches++;
+  }
+  KC_TRY(cudaGetLastError(), "launch");
+  if (R) KC_TRY(cudaMemcpyAsync(p, ws.p.p, uint64_t(Q) * R * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(index, ws.index.p, Q * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (gather) KC_TRY(cudaMemcpyAsync(gather, ws.gather.p, Q * H * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "select");
+  prof_collect(h);
+  return KC_OK;
+}
+
+static kc_status batch_host_common(kc_handle* h, const kc_batch_view* bv, DevBatch& b) {
+  Workspace& ws = h->ws;
+  const uint32_t F = bv->frames;
+  if (!bv->rec_off || !bv->token_ids || !bv->field_roles || !bv->schema_ids || !bv->band_ids)
+    return fail(h, KC_ERR_INVALID_ARG, "batch view is incomplete");
+  if (bv->rec_off[0] != 0 || bv->rec_off[F] != bv->records)
+    return fail(h, KC_ERR_INVALID_ARG, "rec_off must start at 0 and end at the record count");
+  for (uint32_t f = 0; f < F; f++)
+    if (bv->rec_off[f + 1] < bv->rec_off[f]) return fail(h, KC_ERR_INVALID_ARG, "rec_off must not decrease");
+  const uint64_t N = bv->records;
+  kc_status s;
+  if ((s = stage(h, ws.rec_off, bv->rec_off, F + 1ull)) || (s = stage(h, ws.token_ids, bv->token_ids, N * 8)) ||
+      (s = stage(h, ws.field_roles, bv->field_roles, N * 8)) || (s = stage(h, ws.schema_ids, bv->schema_ids, N)) ||
+      (s = stage(h, ws.band_ids, bv->band_ids, N)))
+    return s;
+  b.frames = F; b.records = N; b.rec_off = P<uint64_t>(ws.rec_off);
+  b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
+  b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  return KC_OK;
+}
+
+kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
+  if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
+    return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  DevBatch b;
+  kc_status s = batch_host_common(h, bv, b);
+  if (s) return s;
+  // The rule and uniforms are per batch question; their count is known only
+  // after packing, so they are staged at the largest possible size.
+  Workspace& ws = h->ws;
+  const uint64_t N = bv->records;
+  // count questions on the host to size the optional per-question arrays
+  if (bv->schema_allow || bv->uniforms) {
+    uint64_t nq = 0;
+    for (uint64_t i = 0; i < N; i++) nq += bv->band_ids[i] == KC_QUERY_BAND;
+    if (bv->schema_allow) {
+      if ((s = stage(h, ws.schema_allow, bv->schema_allow, nq * 8)) || (s = stage(h, ws.band_allow, bv->band_allow, nq)))
+        return s;
+      b.schema_allow = P<uint32_t>(ws.schema_allow);
+      b.band_allow = P<uint32_t>(ws.band_allow);
+    }
+    if (bv->uniforms) {
+      if ((s = stage(h, ws.uniforms, bv->uniforms, nq))) return s;
+      b.uniforms = P<double>(ws.uniforms);
+    }
+  }
+  if ((s = run_batch(h, b, false))) return s;
+  const kc::FrameTotals& tot = *h->h_tot;
+  out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
+  if (tot.p > out->p_capacity || tot.q > out->q_capacity || (tot.p && !out->p) || (tot.q && !out->index))
+    return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the batch's p / index");
+  if (tot.p) KC_TRY(cudaMemcpyAsync(out->p, ws.p.p, tot.p * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (tot.q) KC_TRY(cudaMemcpyAsync(out->index, ws.index.p, tot.q * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (out->p_off) KC_TRY(cudaMemcpyAsync(out->p_off, ws.p_off.p, (bv->frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (out->q_off) KC_TRY(cudaMemcpyAsync(out->q_off, ws.q_off.p, (bv->frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (out->query_output && tot.q)
+    KC_TRY(cudaMemcpyAsync(out->query_output, ws.qstate.p, tot.q * h->d.h * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "batch");
+  prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_device_result* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
+  if (!bv->rec_off || !bv->token_ids || !bv->field_roles || !bv->schema_ids || !bv->band_ids)
+    return fail(h, KC_ERR_INVALID_ARG, "batch view is incomplete");
+  if ((reinterpret_cast<uintptr_t>(bv->token_ids) & 15) || (reinterpret_cast<uintptr_t>(bv->rec_off) & 7))
+    return fail(h, KC_ERR_INVALID_ARG, "token_ids must be 16-byte aligned and rec_off 8-byte aligned");
+  if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
+    return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  DevBatch b;
+  b.frames = bv->frames; b.records = bv->records; b.rec_off = bv->rec_off;
+  b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
+  b.band_ids = bv->band_ids; b.schema_allow = bv->schema_allow; b.band_allow = bv->band_allow;
+  b.uniforms = bv->uniforms;
+  kc_status s = run_batch(h, b, false);
+  if (s) return s;
+  const kc::FrameTotals& tot = *h->h_tot;
+  out->p = P<float>(h->ws.p); out->index = P<uint32_t>(h->ws.index);
+  out->p_off = P<uint64_t>(h->ws.p_off); out->q_off = P<uint64_t>(h->ws.q_off);
+  out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
+  if (h->profiling) prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_set_stream(kc_handle* h, void* stream) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own;
+  return KC_OK;
+}
+
+void* kc_get_stream(kc_handle* h) { return h ? static_cast<void*>(h->stream) : nullptr; }
+
+kc_status kc_synchronize(kc_handle* h) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  DeviceGuard dg(h->device);
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return cuda_fail(h, e, "synchronize");
+  return KC_OK;
+}
+
+kc_status kc_profile(kc_handle* h, int enable) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  h->profiling = enable != 0;
+  return KC_OK;
+}
+
+kc_status kc_profile_read(kc_handle* h, kc_stage_times* out, int reset) {
+  if (!h || !out) return fail(h, KC_ERR_INVALID_ARG, "arguments are null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  prof_collect(h);
+  *out = h->prof;
+  out->launches = h->launches;
+  if (reset) h->prof = kc_stage_times{};
+  return KC_OK;
+}
+
+uint64_t kc_launch_count(kc_handle* h) { return h ? h->launches : 0; }
+
+void kc_destroy(kc_handle* h) {
+  if (!h) return;
+  {
+    std::lock_guard<std::mutex> lk(h->mu);
+    DeviceGuard dg(h->device);
+    if (h->own) cudaStreamSynchronize(h->own);
+    DevBuf* bufs[] = {&h->ws.rec_off, &h->ws.token_ids, &h->ws.field_roles, &h->ws.schema_ids, &h->ws.band_ids,
+                      &h->ws.schema_allow, &h->ws.band_allow, &h->ws.uniforms, &h->ws.mask, &h->ws.bank_schema,
+                      &h->ws.bank_band, &h->ws.rec_meta, &h->ws.frame_t, &h->ws.frame_q, &h->ws.frame_r,
+                      &h->ws.t_off, &h->ws.q_off, &h->ws.r_off, &h->ws.p_off, &h->ws.totals, &h->ws.tok_recpos,
+                      &h->ws.rec_start, &h->ws.rec_row, &h->ws.bank_rec, &h->ws.bank_frame, &h->ws.query_rec,
+                      &h->ws.query_frame, &h->ws.x, &h->ws.qkv, &h->ws.bk, &h->ws.bv, &h->ws.mk, &h->ws.mv,
+                      &h->ws.qstate, &h->ws.mq, &h->ws.mh, &h->ws.sq, &h->ws.sk, &h->ws.p, &h->ws.index,
+                      &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off};
+    for (DevBuf* b : bufs)
+      if (b->p) cudaFree(b->p);
+    for (auto& pr : h->ev_pool) {
+      cudaEventDestroy(pr.first);
+      cudaEventDestroy(pr.second);
+    }
+    if (h->w) cudaFree(h->w);
+    if (h->token_rows) cudaFree(h->token_rows);
+    if (h->h_tot) cudaFreeHost(h->h_tot);
+    if (h->own) cudaStreamDestroy(h->own);
+  }
+  delete h;
+}
+
+const char* kc_last_error(kc_handle* h) { return h ? h->err.c_str() : g_create_error.c_str(); }
+
+}  // extern "C"
