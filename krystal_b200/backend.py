@@ -200,7 +200,8 @@ class CudaBrainBackend:
         nq = int((band == 5).sum())
         if p_capacity is None:
             rec = np.diff(off.astype(np.int64))
-            isq = np.add.reduceat((band == 5).astype(np.int64), off[:-1].astype(np.int64)) if batch.frames else 0
+            fid = np.repeat(np.arange(batch.frames), rec)
+            isq = np.bincount(fid, weights=(band == 5), minlength=batch.frames).astype(np.int64)
             p_capacity = int((isq * (rec - isq)).sum())
         p = np.empty(max(1, p_capacity), dtype=np.float32)
         idx = np.empty(max(1, nq), dtype=np.uint32)

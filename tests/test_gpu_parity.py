@@ -276,7 +276,7 @@ class _DevArray:
     """A library-owned device array, exposed to torch through __cuda_array_interface__."""
 
     def __init__(self, ptr: int, n: int, typestr: str):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, True), "version": 2}
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 2}
 
 
 def test_device_resident_batch_equals_host_batch():
