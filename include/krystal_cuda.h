@@ -197,6 +197,23 @@ kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_outpu
 kc_status kc_select(kc_handle* h, const kc_encoded_view* encoded, const float* mask, const kc_mask_rule* rule,
                     const double* uniforms, float* p, uint32_t* index, float* gather);
 
+/* The selector of kc_select over DEVICE pointers, allocating no device memory.
+ * No counterpart in the reference: it exists for callers that cannot call
+ * cudaMalloc at the point they select — code running inside CUDA stream
+ * capture, real-time loops that forbid allocation, or hosts whose memory is
+ * handed out by their own pool. Its scratch is one static device array of
+ * about 2.2 MB that every GPU loading this library holds until exit; it caps
+ * a call at 256 questions and KC_MAX_BANK bank rows (KC_ERR_CAPACITY above).
+ * Inputs [Q,H], [R,H], [R,H] (bank_values only needed for the gather), mask
+ * [Q,R] or NULL; outputs p [Q,R], index [Q], gather [Q,H] or NULL. Work is
+ * queued on the handle's stream and the call returns without waiting. The
+ * first call on a device looks up the scratch's device address; make that
+ * first call before any stream capture. All calls share the one scratch
+ * array, so calls whose GPU work overlaps (two streams, two handles on one
+ * device) race: serialise them. */
+kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, const float* query_output, const float* bank_keys,
+                            const float* bank_values, const float* mask, float* p, uint32_t* index, float* gather);
+
 /* Whole-batch think: pack on the GPU, encode, select. Host buffers; the
  * host<->device copies are part of the call. */
 kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* batch, kc_batch_out* out);

@@ -27,7 +27,7 @@ KC_MAX_BANK = 4096
 # Every function include/krystal_cuda.h declares.
 EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
            "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
-           "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error")
+           "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc")
 
 
 class KrystalCudaError(RuntimeError):
@@ -127,6 +127,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_select.argtypes = [P, C.POINTER(KcEncodedView), P, C.POINTER(KcMaskRule), P, P, P, P]
     lib.kc_forward_batch.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcBatchOut)]
     lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
+    lib.kc_select_noalloc.argtypes = [P, C.c_uint32, C.c_uint32, P, P, P, P, P, P, P]
     lib.kc_set_stream.argtypes = [P, P]
     lib.kc_get_stream.argtypes = [P]
     lib.kc_get_stream.restype = P
@@ -140,7 +141,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_last_error.argtypes = [P]
     lib.kc_last_error.restype = C.c_char_p
     for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
-                 "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read"):
+                 "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

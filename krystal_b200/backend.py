@@ -183,6 +183,13 @@ class CudaBrainBackend:
                                       abi.ptr(u), p.ctypes.data, idx.ctypes.data, abi.ptr(g)), self._h)
         return Selection(p[:q * r], idx[:q], g[:q * h] if g is not None else None)
 
+    def select_noalloc(self, q: int, r: int, query_output: int, bank_keys: int, bank_values: int | None,
+                       mask: int | None, p: int, index: int, gather: int | None = None) -> None:
+        """kc_select_noalloc: the selector on caller-owned DEVICE buffers (raw
+        pointers), with no device allocation; queued on the handle's stream."""
+        abi.check(self._lib.kc_select_noalloc(self._h, q, r, query_output, bank_keys, bank_values, mask, p, index,
+                                              gather), self._h)
+
     # --- packed ragged batches ------------------------------------------------
     def forward_batch(self, batch: FrameBatch, rule: MaskRule | None = None, uniforms=None,
                       want_query_output: bool = False, p_capacity: int | None = None) -> dict:

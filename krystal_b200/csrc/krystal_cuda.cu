@@ -667,6 +667,94 @@ kc_status kc_select(kc_handle* h, const kc_encoded_view* enc, const float* mask,
   return KC_OK;
 }
 
+// ---------------------------------------------------------------------------
+// kc_select_noalloc: the selector over device-resident inputs with no device
+// allocation. Its scratch — the two projections and the one-frame offset
+// tables — is one file-scope device array, present on every GPU that loads
+// this library until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr uint32_t kNoAllocMaxQ = 256;
+constexpr uint32_t kNoAllocMaxR = KC_MAX_BANK;
+// layout: sq [maxQ,H] f32 | sk [maxR,H] f32 | r_off, q_off, p_off [2] u64 | query_frame [maxQ] u32
+constexpr size_t kNoAllocSq = 0;
+constexpr size_t kNoAllocSk = kNoAllocSq + size_t(kNoAllocMaxQ) * KC_H * 4;
+constexpr size_t kNoAllocOff = kNoAllocSk + size_t(kNoAllocMaxR) * KC_H * 4;
+constexpr size_t kNoAllocQf = kNoAllocOff + 6 * 8;
+constexpr size_t kNoAllocBytes = kNoAllocQf + size_t(kNoAllocMaxQ) * 4;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Per-device address of g_noalloc_scratch (the host-side symbol is only a
+// stand-in), looked up once per device.
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Writes the one-frame tables every call: every question belongs to frame 0.
+__global__ void k_noalloc_tables(unsigned char* scratch, uint32_t q, uint32_t r) {
+  uint64_t* off = reinterpret_cast<uint64_t*>(scratch + kNoAllocOff);
+  uint32_t* qf = reinterpret_cast<uint32_t*>(scratch + kNoAllocQf);
+  if (threadIdx.x == 0) {
+    off[0] = 0; off[1] = r;               // r_off
+    off[2] = 0; off[3] = q;               // q_off
+    off[4] = 0; off[5] = uint64_t(q) * r; // p_off
+  }
+  for (uint32_t i = threadIdx.x; i < q; i += blockDim.x) qf[i] = 0u;
+}
+
+}  // namespace
+
+extern "C" kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, const float* query_output,
+                                       const float* bank_keys, const float* bank_values, const float* mask,
+                                       float* p, uint32_t* index, float* gather) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (q > kNoAllocMaxQ || r > kNoAllocMaxR) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "kc_select_noalloc holds at most %u questions and %u bank rows (got %u, %u)",
+             kNoAllocMaxQ, kNoAllocMaxR, q, r);
+    return fail(h, KC_ERR_CAPACITY, buf);
+  }
+  if (q == 0) return KC_OK;
+  if (!query_output || (r && !bank_keys) || !p || !index || (gather && r && !bank_values))
+    return fail(h, KC_ERR_INVALID_ARG, "kc_select_noalloc arguments are incomplete");
+  if ((reinterpret_cast<uintptr_t>(query_output) | reinterpret_cast<uintptr_t>(bank_keys)) & 15)
+    return fail(h, KC_ERR_INVALID_ARG, "kc_select_noalloc: query_output and bank_keys must be 16-byte aligned");
+  if (h->device < 0 || h->device >= kMaxDevices) return fail(h, KC_ERR_INVALID_ARG, "device index out of range");
+  unsigned char* scratch;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[h->device]) {
+      void* ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(h, e, "kc_select_noalloc scratch address");
+      g_noalloc_ptr[h->device] = ptr;
+    }
+    scratch = static_cast<unsigned char*>(g_noalloc_ptr[h->device]);
+  }
+  float* sq = reinterpret_cast<float*>(scratch + kNoAllocSq);
+  float* sk = reinterpret_cast<float*>(scratch + kNoAllocSk);
+  const uint64_t* off = reinterpret_cast<const uint64_t*>(scratch + kNoAllocOff);
+  const uint32_t H = h->d.h;
+  k_noalloc_tables<<<1, 256, 0, h->stream>>>(scratch, q, r);
+  dgemm<kc::kEpiStore>(h, query_output, h->w + h->d.off_swq, sq, q, H, H);
+  dgemm<kc::kEpiStore>(h, bank_keys, h->w + h->d.off_swk, sk, r, H, H);
+  kc::SelectArgs sa{};
+  sa.sq = sq; sa.sk = sk; sa.bank_values = bank_values;
+  sa.query_frame = reinterpret_cast<const uint32_t*>(scratch + kNoAllocQf);
+  sa.r_off = off; sa.q_off = off + 2; sa.p_off = off + 4;
+  sa.mask = mask;
+  sa.max_r = r; sa.scale = 1.0 / std::sqrt(double(H));
+  sa.p = p; sa.index = index; sa.gather = gather;
+  kc::k_select_exact<<<q, 256, size_t(r) * 12, h->stream>>>(sa);
+  h->launches += 2;
+  KC_TRY(cudaGetLastError(), "kc_select_noalloc launch");
+  return KC_OK;
+}
+
 static kc_status batch_host_common(kc_handle* h, const kc_batch_view* bv, DevBatch& b) {
   Workspace& ws = h->ws;
   const uint32_t F = bv->frames;
