@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--device-only", action="store_true",
                     help="time only the device-resident leg (for profiler captures of the same kernels)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--precision", choices=["certified", "exact", "fast"], default="certified",
+                    help="certified: tensor cores + exact recomputation of uncertain frames (the product default)")
     return ap.parse_args()
 
 
@@ -186,6 +188,7 @@ def main():
     cfg = synth.workload_config(wl)
     w = synth.workload_weights(cfg, wl.vocab)
     be = CudaBrainBackend(cfg, w, local)
+    be.set_precision(args.precision)
     stream = torch.cuda.Stream(device=dev)
     be.set_stream(stream.cuda_stream)
 
@@ -243,29 +246,47 @@ def main():
         peaks, peaks_kind = load_peaks()
         sec = ms_max / 1e3
         value = world * frames * args.steps / sec
-        gemm_ms = prof["enc_gemm_ms"] / max(prof["enc_gemm_launches"], 1)
-        gemm_flops = prof["enc_gemm_flops"] / max(prof["enc_gemm_launches"], 1)
-        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
-        peak = peaks.get("bf16_tflops")
+        launches_g = max(prof["enc_gemm_launches"], 1)
+        gemm_ms = prof["enc_gemm_ms"] / launches_g
+        gemm_flops = prof["enc_gemm_flops"] / launches_g
+        gemm_bytes = prof["enc_gemm_bytes"] / launches_g
+        tflops = gemm_flops / (gemm_ms / 1e3) / 1e12
+        gbs = gemm_bytes / (gemm_ms / 1e3) / 1e9
+        if args.precision == "exact":
+            peak = peaks.get("bf16_tflops")
+            roof = {"kernel": "k_dgemm_exact (encoder QKV / W1 / W2, FP64 pipe)", "bound": "tensor",
+                    "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak if peak else None,
+                    "traffic": None,
+                    "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); this kernel runs on the FP64 pipe "
+                                 "(~37 TFLOP/s nominal on B200)"}
+        else:
+            peak = peaks.get("hbm_gbs")
+            roof = {"kernel": "k_tc_gemm (encoder QKV / W1 / W2; tcgen05 split-fp16, 3 MMAs per product)",
+                    "bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak if peak else None,
+                    "traffic": None, "peak_kind": f"{peaks_kind} HBM copy bandwidth",
+                    "tensor_tflops_algorithmic": tflops,
+                    "tensor_frac_of_bf16_peak": tflops / peaks["bf16_tflops"] if peaks.get("bf16_tflops") else None}
+        roof.update({"launch_ms": gemm_ms, "flops_per_launch": gemm_flops, "bytes_per_launch": gemm_bytes})
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f64" if args.precision == "exact" else "f32", "data": "synthetic",
             "questions_per_sec": world * n_q * args.steps / sec,
             "config": {"workload": wl.name, "frames": frames, "records": batch.records, "questions": n_q,
                        "tokens": int(offs["t_off"][-1]), "bank_rows": int(offs["r_off"][-1]),
                        "p_entries": int(offs["p_off"][-1]), "parallelism": f"frame-shard x{world}",
                        "l2": "256 MiB buffer written between steps (inside the timed region); "
                              "a step's working set is several GB",
-                       "precision": "exact: f64 accumulation in the oracle's order, f32 stores"},
+                       "precision": {
+                           "exact": "exact: f64 accumulation in the oracle's order, f32 stores",
+                           "certified": "certified: tcgen05 split-fp16 GEMMs + f32; frames whose selection is "
+                                        "within the certification margin are recomputed on the exact path",
+                           "fast": "fast: tcgen05 split-fp16 GEMMs + f32, no recomputation (diagnostic)"}[
+                           args.precision]},
             "gpu_launches": launches,
+            "fallback_frames_per_step": prof["fallback_frames"] / args.steps,
             "stage_ms_per_step": {k[:-3]: round(prof[k] / args.steps, 3) for k in prof if k.endswith("_ms")},
-            "roofline": {"kernel": "k_dgemm_exact (encoder QKV/W1/W2)", "bound": "tensor",
-                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak if peak else None, "traffic": None,
-                         "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); the kernel runs on the FP64 pipe "
-                                      "(~37 TFLOP/s nominal B200 FP64)",
-                         "launch_ms": gemm_ms, "flops_per_launch": gemm_flops},
+            "roofline": roof,
         }
         if clk:
             line["clocks"] = clk

@@ -46,6 +46,19 @@ extern "C" {
 #define KC_NO_SELECTION 0xffffffffu /* index of an all-blocked row (forward/oracle.ts:364-365) */
 #define KC_MAX_BANK 4096u         /* largest bank one frame may hold */
 
+/* Precision of the batch entry points (kc_forward_batch[_device]).
+ * EXACT: the oracle's arithmetic (f64 accumulation in its order, f32 stores).
+ * CERTIFIED (default): tensor cores at fp32-class accuracy; every question
+ *   whose selection could differ from the exact computation's (top-two score
+ *   gap <= tau, a sampled draw within tau of a cumulative edge, non-finite
+ *   values) has its frame recomputed on the exact path, so selections match
+ *   the exact path and distributions agree to ~1e-6.
+ * FAST: the tensor-core path without the recomputation (diagnostics).
+ * kc_encode and kc_select always compute exactly. */
+#define KC_PRECISION_EXACT 0
+#define KC_PRECISION_CERTIFIED 1
+#define KC_PRECISION_FAST 2
+
 typedef enum kc_status {
   KC_OK = 0,
   KC_ERR_INVALID_ARG = 1, /* malformed frame, weights or arguments */
@@ -170,7 +183,10 @@ typedef struct kc_device_result {
 typedef struct kc_stage_times {
   double pack_ms, embed_ms, enc_gemm_ms, enc_attn_ms, pool_ms, mixer_ms, selector_ms, total_ms;
   uint64_t enc_gemm_launches, launches, batches;
-  double enc_gemm_flops; /* algorithmic FLOPs of the encoder GEMMs timed */
+  double enc_gemm_flops;    /* algorithmic FLOPs of the encoder GEMMs timed */
+  double fallback_ms;       /* exact recomputation of uncertified frames */
+  uint64_t fallback_frames; /* frames recomputed (counted whether or not profiling is on) */
+  double enc_gemm_bytes;    /* algorithmic bytes of the encoder GEMMs timed (A read, C written) */
 } kc_stage_times;
 
 uint32_t kc_abi_version(void);
@@ -223,6 +239,10 @@ kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* batch, kc_batch_ou
  * once the result is queued (one short host wait inside, for the batch's
  * sizes). Results are library-owned device arrays. */
 kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* batch, kc_device_result* out);
+
+/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
+ * certification margin (default 2e-5, in score units; 0 keeps it). */
+kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 
 /* Stream control: run on `stream` (a cudaStream_t; NULL = the handle's own). */
 kc_status kc_set_stream(kc_handle* h, void* stream);

@@ -22,12 +22,16 @@ KC_ERR_NONFINITE = 5
 KC_ERR_NO_DEVICE = 6
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "CAPACITY", 3: "CUDA", 4: "TIMEOUT", 5: "NONFINITE", 6: "NO_DEVICE"}
 KC_NO_SELECTION = 0xFFFFFFFF
+KC_PRECISION_EXACT = 0
+KC_PRECISION_CERTIFIED = 1
+KC_PRECISION_FAST = 2
 KC_MAX_BANK = 4096
 
 # Every function include/krystal_cuda.h declares.
 EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
            "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
-           "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc")
+           "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc",
+           "kc_set_precision")
 
 
 class KrystalCudaError(RuntimeError):
@@ -98,7 +102,8 @@ class KcStageTimes(C.Structure):
     _fields_ = [(n, C.c_double) for n in ("pack_ms", "embed_ms", "enc_gemm_ms", "enc_attn_ms", "pool_ms",
                                           "mixer_ms", "selector_ms", "total_ms")] + [
         ("enc_gemm_launches", C.c_uint64), ("launches", C.c_uint64), ("batches", C.c_uint64),
-        ("enc_gemm_flops", C.c_double)]
+        ("enc_gemm_flops", C.c_double), ("fallback_ms", C.c_double), ("fallback_frames", C.c_uint64),
+        ("enc_gemm_bytes", C.c_double)]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -128,6 +133,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_forward_batch.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcBatchOut)]
     lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
     lib.kc_select_noalloc.argtypes = [P, C.c_uint32, C.c_uint32, P, P, P, P, P, P, P]
+    lib.kc_set_precision.argtypes = [P, C.c_int, C.c_float]
     lib.kc_set_stream.argtypes = [P, P]
     lib.kc_get_stream.argtypes = [P]
     lib.kc_get_stream.restype = P
@@ -141,7 +147,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_last_error.argtypes = [P]
     lib.kc_last_error.restype = C.c_char_p
     for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
-                 "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc"):
+                 "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
+                 "kc_set_precision"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

@@ -241,6 +241,13 @@ class CudaBrainBackend:
     def synchronize(self) -> None:
         abi.check(self._lib.kc_synchronize(self._h), self._h)
 
+    def set_precision(self, mode: int | str, tau: float = 0.0) -> None:
+        """KC_PRECISION_EXACT / CERTIFIED (default) / FAST for the batch entry points."""
+        modes = {"exact": abi.KC_PRECISION_EXACT, "certified": abi.KC_PRECISION_CERTIFIED,
+                 "fast": abi.KC_PRECISION_FAST}
+        m = modes[mode] if isinstance(mode, str) else int(mode)
+        abi.check(self._lib.kc_set_precision(self._h, m, float(tau)), self._h)
+
     def profile(self, enable: bool) -> None:
         abi.check(self._lib.kc_profile(self._h, int(enable)), self._h)
 

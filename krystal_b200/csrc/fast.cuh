@@ -1,0 +1,414 @@
+// fast.cuh — f32 SIMT kernels of the tensor-core path.
+//
+// The tensor-core path computes the forward to fp32-class accuracy (split
+// fp16 GEMMs, f32 everywhere else) instead of the oracle's exact f64 order.
+// Its distributions agree with the oracle to ~1e-6; its selections are
+// CERTIFIED: k_select_fast marks a question whose decision could differ from
+// the exact computation's (top-two score gap within tau, a sampled draw within
+// tau_c of a cumulative boundary, anything non-finite), and the frames holding
+// such questions are recomputed on the exact path.
+#pragma once
+#include "common.cuh"
+
+namespace kc {
+
+// ---------------------------------------------------------------------------
+// Record-local attention + residual, f32 (attentionOracle local mode,
+// forward/oracle.ts:64-105, :255-256). One warp per record, lane =
+// head*8 + token. The record's q|k|v rows are staged with a row stride of
+// 420 floats (= 4 mod 32) and 33-float head segments, so the 32 lanes of a
+// q read hit 32 different banks and the k / v reads broadcast per head.
+// ---------------------------------------------------------------------------
+constexpr int kLaRow = 420;   // floats per staged token row
+constexpr int kLaSeg = 33;    // floats per head segment
+constexpr int kLaPart = 132;  // q / k / v part: 4 heads x 33
+constexpr int kLaWarps = 4;
+constexpr int kLaSmem = kLaWarps * KC_RW * kLaRow * 4;  // 53 760 bytes
+
+struct LocalAttnFastArgs {
+  const float* qkv;           // [T,384]
+  float* x;                   // [T,128], updated in place
+  const uint32_t* rec_start;  // [N]
+  const uint2* rec_meta;      // [N]
+  uint64_t records;
+  float scale;                // 1/sqrt(headDim)
+};
+
+__global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFastArgs a) {
+  extern __shared__ __align__(16) float la_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = uint64_t(blockIdx.x) * kLaWarps + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  if (cnt == 0) return;
+  float* rec = la_smem + warp * KC_RW * kLaRow;
+  const float* src = a.qkv + uint64_t(start) * 3 * KC_H;
+  for (int i = lane; i < cnt * 3 * KC_H; i += 32) {
+    const int r = i / (3 * KC_H), c = i % (3 * KC_H);
+    const int part = c >> 7, head = (c >> 5) & 3, d = c & 31;
+    rec[r * kLaRow + part * kLaPart + head * kLaSeg + d] = src[i];
+  }
+  __syncwarp();
+  const int head = lane >> 3, ti = lane & 7;
+  float out[KC_HEAD_DIM];
+  if (ti < cnt) {
+    const float* q = rec + ti * kLaRow + head * kLaSeg;
+    float p[KC_RW];
+    float mx = -INFINITY;
+    for (int j = 0; j < cnt; j++) {
+      const float* k = rec + j * kLaRow + kLaPart + head * kLaSeg;
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < KC_HEAD_DIM; d++) s = fmaf(q[d], k[d], s);
+      p[j] = s * a.scale;
+      mx = fmaxf(mx, p[j]);
+    }
+    float sum = 0.f;
+    for (int j = 0; j < cnt; j++) {
+      p[j] = expf(p[j] - mx);
+      sum += p[j];
+    }
+    const float inv = 1.f / fmaxf(sum, 1e-20f);
+#pragma unroll
+    for (int d = 0; d < KC_HEAD_DIM; d++) out[d] = 0.f;
+    for (int j = 0; j < cnt; j++) {
+      const float pj = p[j] * inv;
+      const float* v = rec + j * kLaRow + 2 * kLaPart + head * kLaSeg;
+#pragma unroll
+      for (int d = 0; d < KC_HEAD_DIM; d++) out[d] = fmaf(pj, v[d], out[d]);
+    }
+  }
+  __syncwarp();
+  if (ti < cnt) {  // only this lane reads its q slice: overwrite it with the output
+    float* q = rec + ti * kLaRow + head * kLaSeg;
+#pragma unroll
+    for (int d = 0; d < KC_HEAD_DIM; d++) q[d] = out[d];
+  }
+  __syncwarp();
+  float* xr = a.x + uint64_t(start) * KC_H;
+  for (int i = lane; i < cnt * KC_H; i += 32) {
+    const int r = i >> 7, c = i & 127;
+    xr[i] += rec[r * kLaRow + (c >> 5) * kLaSeg + (c & 31)];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Mixer cross-attention + residual, f32 (oracle.ts:292-293 with the open
+// mixer mask). One CTA of 128 threads per question; warp w = head w.
+// ---------------------------------------------------------------------------
+struct CrossAttnFastArgs {
+  const float* mq;
+  const float* mk;
+  const float* mv;
+  float* query;
+  const uint32_t* query_frame;
+  const uint64_t* r_off;
+  uint32_t max_r;
+  float scale;
+};
+
+__global__ void __launch_bounds__(128) k_cross_attn_fast(CrossAttnFastArgs a) {
+  extern __shared__ __align__(16) float ca_smem[];  // [4][max_r]
+  __shared__ float qs[KC_H];
+  __shared__ float inv_s[KC_HEADS];
+  const uint32_t qi = blockIdx.x;
+  const uint32_t f = a.query_frame[qi];
+  const uint64_t rb = a.r_off[f];
+  const int R = int(a.r_off[f + 1] - rb);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  qs[tid] = a.mq[uint64_t(qi) * KC_H + tid];
+  __syncthreads();
+  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
+    const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
+    const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
+    float s = 0.f;
+#pragma unroll
+    for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+      const float4 k = kr[d4];
+      s = fmaf(qs[hb + 4 * d4], k.x, s);
+      s = fmaf(qs[hb + 4 * d4 + 1], k.y, s);
+      s = fmaf(qs[hb + 4 * d4 + 2], k.z, s);
+      s = fmaf(qs[hb + 4 * d4 + 3], k.w, s);
+    }
+    ca_smem[head * a.max_r + j] = s * a.scale;
+  }
+  __syncthreads();
+  {
+    float* row = ca_smem + warp * a.max_r;
+    float mx = -INFINITY;
+    for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < R; j += 32) {
+      const float e = expf(row[j] - mx);
+      row[j] = e;
+      sum += e;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) inv_s[warp] = 1.f / fmaxf(sum, 1e-20f);
+  }
+  __syncthreads();
+  {
+    const int head = tid >> 5, d = tid & 31, col = head * KC_HEAD_DIM + d;
+    const float* row = ca_smem + head * a.max_r;
+    float v0 = 0.f, v1 = 0.f;
+    int j = 0;
+    for (; j + 1 < R; j += 2) {
+      v0 = fmaf(row[j], a.mv[(rb + j) * KC_H + col], v0);
+      v1 = fmaf(row[j + 1], a.mv[(rb + j + 1) * KC_H + col], v1);
+    }
+    if (j < R) v0 = fmaf(row[j], a.mv[(rb + j) * KC_H + col], v0);
+    a.query[uint64_t(qi) * KC_H + col] += (v0 + v1) * inv_s[head];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pointer selector, f32, with certification (selectorOracle,
+// forward/oracle.ts:332-382). One CTA of 256 threads per question. Writes p
+// and the index, and raises flags[frame] when the decision is not certain.
+// ---------------------------------------------------------------------------
+struct SelectFastArgs {
+  const float* sq;
+  const float* sk;
+  const uint32_t* query_frame;
+  const uint64_t* r_off;
+  const uint64_t* q_off;
+  const uint64_t* p_off;
+  const uint32_t* schema_allow;
+  const uint32_t* band_allow;
+  const uint32_t* bank_rec;
+  const uint32_t* schema_ids;
+  const uint32_t* band_ids;
+  const double* uniforms;
+  uint32_t max_r;
+  float scale;
+  float tau;        // certified argmax: top-two score gap above tau
+  float tau_c;      // certified draw: the uniform farther than tau_c from a cumulative boundary
+  float* p;
+  uint32_t* index;
+  uint32_t* flags;  // [frames]
+};
+
+__global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
+  constexpr int NT = 256;
+  extern __shared__ __align__(16) float sel_smem[];  // [max_r]
+  __shared__ float qs[KC_H];
+  __shared__ float red_f[NT / 32];
+  __shared__ float red_g[NT / 32];
+  __shared__ uint32_t red_u[NT / 32];
+  __shared__ uint32_t red_i[NT / 32];
+  __shared__ int red_b[NT / 32];
+  const uint32_t qi = blockIdx.x;
+  const uint32_t f = a.query_frame[qi];
+  const uint64_t rb = a.r_off[f];
+  const int R = int(a.r_off[f + 1] - rb);
+  const uint64_t il = qi - a.q_off[f];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (R == 0) {
+    if (tid == 0) a.index[qi] = KC_INVALID;
+    return;
+  }
+  float* prow = a.p + a.p_off[f] + il * uint64_t(R);
+  if (tid < KC_H) qs[tid] = a.sq[uint64_t(qi) * KC_H + tid];
+
+  bool reopen = false;
+  const uint32_t* sa = nullptr;
+  uint32_t ba = 0;
+  if (a.schema_allow) {
+    sa = a.schema_allow + uint64_t(qi) * 8;
+    ba = a.band_allow[qi];
+    uint32_t admitted = 0;
+    for (int j = tid; j < R; j += NT) {
+      const uint32_t gr = a.bank_rec[rb + j];
+      const uint32_t s = a.schema_ids[gr], b = a.band_ids[gr];
+      admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
+    }
+    for (int o = 16; o; o >>= 1) admitted += __shfl_xor_sync(0xffffffffu, admitted, o);
+    if (lane == 0) red_u[warp] = admitted;
+    __syncthreads();
+    uint32_t tot = 0;
+    for (int w = 0; w < NT / 32; w++) tot += red_u[w];
+    reopen = tot == 0;
+  }
+  __syncthreads();
+
+  // scores; per-thread best / second-best (value, first index) and finiteness
+  float b1 = -INFINITY, b2 = -INFINITY;
+  uint32_t i1 = KC_INVALID;
+  int nonfinite = 0, open = 0;
+  for (int j = tid; j < R; j += NT) {
+    const float4* kr = reinterpret_cast<const float4*>(a.sk + (rb + j) * KC_H);
+    float s = 0.f;
+#pragma unroll 8
+    for (int d4 = 0; d4 < KC_H / 4; d4++) {
+      const float4 k = kr[d4];
+      s = fmaf(qs[4 * d4], k.x, s);
+      s = fmaf(qs[4 * d4 + 1], k.y, s);
+      s = fmaf(qs[4 * d4 + 2], k.z, s);
+      s = fmaf(qs[4 * d4 + 3], k.w, s);
+    }
+    float m = 0.f;
+    if (sa && !reopen) {
+      const uint32_t gr = a.bank_rec[rb + j];
+      const uint32_t sid = a.schema_ids[gr], b = a.band_ids[gr];
+      m = (sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u)) ? 0.f : -1e30f;
+    }
+    const float sc = s * a.scale + m;
+    sel_smem[j] = sc;
+    nonfinite |= !isfinite(s);
+    open |= sc >= -1e29f;
+    if (sc > b1) { b2 = b1; b1 = sc; i1 = uint32_t(j); }
+    else if (sc > b2) b2 = sc;
+  }
+  // block reduce: top two values, index of the first top, any-open, any-nonfinite
+  for (int o = 16; o; o >>= 1) {
+    const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o), ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
+    const uint32_t oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
+    if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b2 = fmaxf(b1, ob2); b1 = ob1; i1 = oi1; }
+    else b2 = fmaxf(b2, ob1);
+    nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
+    open |= __shfl_xor_sync(0xffffffffu, open, o);
+  }
+  if (lane == 0) { red_f[warp] = b1; red_g[warp] = b2; red_i[warp] = i1; red_b[warp] = (nonfinite << 1) | open; }
+  __syncthreads();
+  float B1 = red_f[0], B2 = red_g[0];
+  uint32_t I1 = red_i[0];
+  int flagsum = red_b[0];
+  for (int w = 1; w < NT / 32; w++) {
+    const float ob1 = red_f[w], ob2 = red_g[w];
+    const uint32_t oi1 = red_i[w];
+    if (ob1 > B1 || (ob1 == B1 && oi1 < I1)) { B2 = fmaxf(B1, ob2); B1 = ob1; I1 = oi1; }
+    else B2 = fmaxf(B2, ob1);
+    flagsum |= red_b[w];
+  }
+  const bool any_nonfinite = flagsum & 2, any_open = flagsum & 1;
+  __syncthreads();
+  // softmax (the all-blocked row keeps p = 0)
+  float inv = 0.f;
+  if (any_open) {
+    float sum = 0.f;
+    for (int j = tid; j < R; j += NT) {
+      const float e = expf(sel_smem[j] - B1);
+      sel_smem[j] = e;
+      sum += e;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red_f[warp] = sum;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < NT / 32; w++) tot += red_f[w];
+    inv = 1.f / fmaxf(tot, 1e-20f);
+  }
+  for (int j = tid; j < R; j += NT) {
+    const float pv = any_open ? sel_smem[j] * inv : 0.f;
+    sel_smem[j] = pv;
+    prow[j] = pv;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    bool certain = !any_nonfinite;
+    uint32_t best;
+    if (!any_open) {
+      best = KC_INVALID;  // every score below -1e29 on any accurate computation
+    } else if (a.uniforms) {
+      // sampleRow's inverse CDF; certain when the draw is clear of both edges
+      const double u = a.uniforms[qi];
+      double cum = 0.0, prev = 0.0;
+      int last = -1, drawn = -2;
+      for (int j = 0; j < R; j++) {
+        const double w = sel_smem[j];
+        if (!(w > 0)) continue;
+        last = j;
+        prev = cum;
+        cum += w;
+        if (u < cum) { drawn = j; break; }
+      }
+      if (drawn == -2) {
+        drawn = last;
+        certain = certain && (u - cum > a.tau_c);
+      } else {
+        certain = certain && (cum - u > a.tau_c) && (u - prev > a.tau_c || drawn == 0);
+      }
+      // tiny weights near zero may flip between zero and positive
+      best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
+    } else {
+      best = I1;
+      certain = certain && (R == 1 || B1 - B2 > a.tau);
+    }
+    a.index[qi] = best;
+    if (!certain) atomicOr(&a.flags[f], 1u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fallback plumbing: gather the records of the frames to recompute into a
+// compact batch, and scatter their exact results back.
+// ---------------------------------------------------------------------------
+// One CTA: sub_rec_off / sub_q_off over the listed frames.
+__global__ void k_fallback_offsets(const uint32_t* __restrict__ list, uint32_t n, const uint64_t* __restrict__ rec_off,
+                                   const uint64_t* __restrict__ q_off, uint64_t* __restrict__ sub_rec_off,
+                                   uint64_t* __restrict__ sub_q_off) {
+  __shared__ unsigned long long tmp[32];
+  unsigned long long br = 0, bq = 0;
+  for (uint32_t c = 0; c < n; c += 1024) {
+    const uint32_t i = c + threadIdx.x;
+    unsigned long long r = 0, q = 0;
+    if (i < n) {
+      const uint32_t f = list[i];
+      r = rec_off[f + 1] - rec_off[f];
+      q = q_off[f + 1] - q_off[f];
+    }
+    unsigned long long tr, tq;
+    const unsigned long long er = block_excl_scan<1024, unsigned long long>(r, &tr, tmp);
+    const unsigned long long eq = block_excl_scan<1024, unsigned long long>(q, &tq, tmp);
+    if (i < n) { sub_rec_off[i] = br + er; sub_q_off[i] = bq + eq; }
+    br += tr; bq += tq;
+  }
+  if (threadIdx.x == 0) { sub_rec_off[n] = br; sub_q_off[n] = bq; }
+}
+
+// One CTA per listed frame: copy its records (and its questions' rule rows
+// and uniforms) into the compact batch.
+__global__ void k_fallback_gather(const uint32_t* __restrict__ list, const uint64_t* __restrict__ rec_off,
+                                  const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ sub_rec_off,
+                                  const uint64_t* __restrict__ sub_q_off, const uint32_t* __restrict__ token_ids,
+                                  const uint32_t* __restrict__ field_roles, const uint32_t* __restrict__ schema_ids,
+                                  const uint32_t* __restrict__ band_ids, const uint32_t* __restrict__ schema_allow,
+                                  const uint32_t* __restrict__ band_allow, const double* __restrict__ uniforms,
+                                  uint32_t* __restrict__ s_tok, uint32_t* __restrict__ s_role,
+                                  uint32_t* __restrict__ s_schema, uint32_t* __restrict__ s_band,
+                                  uint32_t* __restrict__ s_sallow, uint32_t* __restrict__ s_ballow,
+                                  double* __restrict__ s_uni) {
+  const uint32_t i = blockIdx.x, f = list[i];
+  const uint64_t r0 = rec_off[f], n = rec_off[f + 1] - r0, d0 = sub_rec_off[i];
+  for (uint64_t k = threadIdx.x; k < n * KC_RW; k += blockDim.x) {
+    s_tok[d0 * KC_RW + k] = token_ids[r0 * KC_RW + k];
+    s_role[d0 * KC_RW + k] = field_roles[r0 * KC_RW + k];
+  }
+  for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) {
+    s_schema[d0 + k] = schema_ids[r0 + k];
+    s_band[d0 + k] = band_ids[r0 + k];
+  }
+  const uint64_t q0 = q_off[f], nq = q_off[f + 1] - q0, e0 = sub_q_off[i];
+  if (schema_allow) {
+    for (uint64_t k = threadIdx.x; k < nq * 8; k += blockDim.x) s_sallow[e0 * 8 + k] = schema_allow[q0 * 8 + k];
+    for (uint64_t k = threadIdx.x; k < nq; k += blockDim.x) s_ballow[e0 + k] = band_allow[q0 + k];
+  }
+  if (uniforms)
+    for (uint64_t k = threadIdx.x; k < nq; k += blockDim.x) s_uni[e0 + k] = uniforms[q0 + k];
+}
+
+// One CTA per listed frame: exact p block and indices back to the batch.
+__global__ void k_fallback_scatter(const uint32_t* __restrict__ list, const uint64_t* __restrict__ p_off,
+                                   const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ sub_p_off,
+                                   const uint64_t* __restrict__ sub_q_off, const float* __restrict__ sub_p,
+                                   const uint32_t* __restrict__ sub_index, float* __restrict__ p,
+                                   uint32_t* __restrict__ index) {
+  const uint32_t i = blockIdx.x, f = list[i];
+  const uint64_t np = p_off[f + 1] - p_off[f], nq = q_off[f + 1] - q_off[f];
+  for (uint64_t k = threadIdx.x; k < np; k += blockDim.x) p[p_off[f] + k] = sub_p[sub_p_off[i] + k];
+  for (uint64_t k = threadIdx.x; k < nq; k += blockDim.x) index[q_off[f] + k] = sub_index[sub_q_off[i] + k];
+}
+
+}  // namespace kc

@@ -14,6 +14,7 @@
 //   selector  Wq/Wk GEMMs, k_select_exact                   oracle.ts:332-382
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -24,7 +25,9 @@
 #include "../../include/krystal_cuda.h"
 #include "common.cuh"
 #include "exact.cuh"
+#include "fast.cuh"
 #include "pack.cuh"
+#include "tc_gemm.cuh"
 
 namespace {
 
@@ -95,31 +98,80 @@ struct Workspace {
   DevBuf x, qkv, bk, bv, mk, mv, qstate, mq, mh, sq, sk, p, index, gather;
   // weight-row scatter staging
   DevBuf rows_val, rows_off;
+  // certification flags per frame, and the list of frames to recompute
+  DevBuf flags, list;
 };
 
-enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStCount };
+enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStCount };
+
+// The matrices the tensor-core path multiplies by, in a fixed order:
+// per encoder block QKV [3H,H], W1 [F,H], W2 [H,F]; per mixer block Wq, Wk,
+// Wv [H,H], W1, W2; the selector's Wq, Wk.
+struct Mat {
+  uint64_t page_off;
+  uint32_t n, k;
+};
+
+std::vector<Mat> mat_list(const Dims& d) {
+  std::vector<Mat> v;
+  const uint64_t hh = uint64_t(d.h) * d.h, fh = uint64_t(d.ffn) * d.h;
+  for (uint32_t b = 0; b < d.enc; b++) {
+    const uint64_t o = d.off_enc + d.block * b;
+    v.push_back({o, 3 * d.h, d.h});
+    v.push_back({o + 3 * hh, d.ffn, d.h});
+    v.push_back({o + 3 * hh + fh, d.h, d.ffn});
+  }
+  for (uint32_t b = 0; b < d.mix; b++) {
+    const uint64_t o = d.off_mixer + d.block * b;
+    v.push_back({o, d.h, d.h});
+    v.push_back({o + hh, d.h, d.h});
+    v.push_back({o + 2 * hh, d.h, d.h});
+    v.push_back({o + 3 * hh, d.ffn, d.h});
+    v.push_back({o + 3 * hh + fh, d.h, d.ffn});
+  }
+  v.push_back({d.off_swq, d.h, d.h});
+  v.push_back({d.off_swk, d.h, d.h});
+  return v;
+}
 
 }  // namespace
 
 struct kc_handle {
   std::mutex mu;
   int device = 0;
+  int sms = 148;
   cudaStream_t own = nullptr;
   cudaStream_t stream = nullptr;
   Dims d{};
   float* w = nullptr;
   uint32_t* token_rows = nullptr;
   uint32_t token_rows_len = 0;
-  Workspace ws;
+  Workspace ws;      // the batch
+  Workspace ws_fb;   // frames recomputed on the exact path
   kc::FrameTotals* h_tot = nullptr;  // pinned
   std::string err;
   uint64_t launches = 0;
+  // precision
+  int precision = KC_PRECISION_CERTIFIED;
+  float tau = 2e-5f, tau_c = 2e-5f;
+  int sa = 10;                      // activations are split at x * 2^sa
+  std::vector<Mat> mats;
+  std::vector<float> mat_max;       // max |W| per matrix (host side, from the last sync)
+  std::vector<uint64_t> img_off;    // byte offset of each matrix's image
+  DevBuf images;
+  bool images_dirty = true;
+  int* d_err = nullptr;             // tensor-core pipeline error word
+  int* h_err = nullptr;             // pinned
+  std::vector<uint32_t> h_flags;
+  uint32_t* h_flags_pinned = nullptr;
+  size_t h_flags_cap = 0;
   // profiling
   bool profiling = false;
   kc_stage_times prof{};
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
   std::vector<std::pair<int, size_t>> ev_used;  // (stage, index into ev_pool)
   std::vector<double> ev_flops;
+  std::vector<double> ev_bytes;
 };
 
 namespace {
@@ -141,13 +193,19 @@ kc_status cuda_fail(kc_handle* h, cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail(h, _e, what);      \
   } while (0)
 
+#define KC_CHECK(expr)             \
+  do {                             \
+    kc_status _s = (expr);         \
+    if (_s != KC_OK) return _s;    \
+  } while (0)
+
 // Profiling: a pair of events around each launch group.
 struct ProfScope {
   kc_handle* h;
   int stage;
   size_t idx = 0;
   bool on;
-  ProfScope(kc_handle* hh, int st, double flops = 0) : h(hh), stage(st), on(hh->profiling) {
+  ProfScope(kc_handle* hh, int st, double flops = 0, double bytes = 0) : h(hh), stage(st), on(hh->profiling) {
     if (!on) return;
     idx = h->ev_used.size();
     if (idx >= h->ev_pool.size()) {
@@ -158,6 +216,7 @@ struct ProfScope {
     }
     h->ev_used.emplace_back(stage, idx);
     h->ev_flops.push_back(flops);
+    h->ev_bytes.push_back(bytes);
     cudaEventRecord(h->ev_pool[idx].first, h->stream);
   }
   ~ProfScope() {
@@ -169,7 +228,7 @@ void prof_collect(kc_handle* h) {
   if (!h->profiling || h->ev_used.empty()) return;
   cudaStreamSynchronize(h->stream);
   double* dst[kStCount] = {&h->prof.pack_ms, &h->prof.embed_ms, &h->prof.enc_gemm_ms, &h->prof.enc_attn_ms,
-                           &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms};
+                           &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms, &h->prof.fallback_ms};
   for (size_t i = 0; i < h->ev_used.size(); i++) {
     float ms = 0;
     auto& pr = h->ev_pool[h->ev_used[i].second];
@@ -179,10 +238,12 @@ void prof_collect(kc_handle* h) {
     if (h->ev_used[i].first == kStEncGemm) {
       h->prof.enc_gemm_launches++;
       h->prof.enc_gemm_flops += h->ev_flops[i];
+      h->prof.enc_gemm_bytes += h->ev_bytes[i];
     }
   }
   h->ev_used.clear();
   h->ev_flops.clear();
+  h->ev_bytes.clear();
 }
 
 template <int EPI>
@@ -190,6 +251,54 @@ kc_status dgemm(kc_handle* h, const float* A, const float* B, float* C, uint64_t
   if (M == 0) return KC_OK;
   dim3 grid(unsigned((M + 127) / 128), N / 128);
   kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(K), int(K), int(N));
+  h->launches++;
+  return KC_OK;
+}
+
+// Rebuild the split fp16 images of every matrix (after a sync changed them).
+kc_status build_images(kc_handle* h) {
+  if (!h->images_dirty) return KC_OK;
+  const auto& m = h->mats;
+  if (h->img_off.size() != m.size()) {
+    h->img_off.resize(m.size());
+    uint64_t off = 0;
+    for (size_t i = 0; i < m.size(); i++) {
+      h->img_off[i] = off;
+      off += uint64_t(m[i].n) * m[i].k * 4;  // hi + lo fp16
+    }
+    KC_TRY(ensure(h->images, off), "weight images");
+  }
+  for (size_t i = 0; i < m.size(); i++) {
+    const int sw = int(std::floor(std::log2(2048.0 / std::max(double(h->mat_max[i]), 1e-30))));
+    const int swc = std::min(std::max(sw, -40), 40);
+    kc::tc::k_weight_image<<<(m[i].n / 128) * (m[i].k / 64), 256, 0, h->stream>>>(
+        h->w + m[i].page_off, int(m[i].n), int(m[i].k), std::ldexp(1.0f, swc),
+        P<uint8_t>(h->images) + h->img_off[i]);
+    h->launches++;
+  }
+  KC_TRY(cudaGetLastError(), "weight images");
+  h->images_dirty = false;
+  return KC_OK;
+}
+
+int mat_sw(kc_handle* h, int i) {
+  const int sw = int(std::floor(std::log2(2048.0 / std::max(double(h->mat_max[i]), 1e-30))));
+  return std::min(std::max(sw, -40), 40);
+}
+
+// y = A·Wᵀ on the tensor cores for matrix `mat` of mat_list.
+template <int EPI>
+kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C) {
+  if (M == 0) return KC_OK;
+  const Mat& mt = h->mats[mat];
+  CUtensorMap map;
+  if (!kc::tc::make_a_map(&map, A, M, mt.k, mt.k))
+    return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a GEMM operand");
+  kc::tc::GemmArgs g{int(M), int(mt.k), int(mt.n / 128), P<uint8_t>(h->images) + h->img_off[mat], C,
+                     int(mt.n), std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat))), h->d_err};
+  const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
+  const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
+  kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, g);
   h->launches++;
   return KC_OK;
 }
@@ -218,10 +327,9 @@ const char* bad_message(uint32_t code) {
   }
 }
 
-// Encoder + pool + mixer (+ selector unless encode_only). Results stay in
-// the workspace: qstate [Q,H], bk/bv [R,H], p, index.
-kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
-  Workspace& ws = h->ws;
+// Pack on the GPU: offset tables, compact token list, row lists. One host
+// wait for the batch totals (sizes the rest of the workspace).
+kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTotals* out_tot) {
   const Dims& d = h->d;
   const uint32_t F = b.frames;
   const uint64_t N = b.records;
@@ -282,6 +390,7 @@ kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
   KC_TRY(ensure(ws.mh, Q * FF * 4ull), "workspace");
   KC_TRY(ensure(ws.p, PP * 4), "workspace");
   KC_TRY(ensure(ws.index, Q * 4), "workspace");
+  KC_TRY(ensure(ws.flags, F * 4ull), "workspace");
   {
     ProfScope ps(h, kStPack);
     kc::k_record_rows<256><<<F, 256, 0, h->stream>>>(
@@ -291,6 +400,17 @@ kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
         P<uint32_t>(ws.bank_frame));
     h->launches++;
   }
+  *out_tot = tot;
+  return KC_OK;
+}
+
+// The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
+// the workspace: qstate [Q,H], bk/bv [R,H], p, index.
+kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
+                        bool encode_only) {
+  const Dims& d = h->d;
+  const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r;
+  const uint32_t H = d.h, FF = d.ffn;
   float* x = P<float>(ws.x);
   float* qkv = P<float>(ws.qkv);
   if (T > 0) {
@@ -308,7 +428,7 @@ kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
     const float* w1 = W + 3ull * H * H;
     const float* w2 = w1 + uint64_t(FF) * H;
     {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H);
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
       dgemm<kc::kEpiStore>(h, x, W, qkv, T, 3 * H, H);
     }
     {
@@ -318,11 +438,11 @@ kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
       h->launches++;
     }
     {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF);
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
       dgemm<kc::kEpiRelu>(h, x, w1, qkv, T, FF, H);
     }
     {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF);
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
       dgemm<kc::kEpiResid>(h, qkv, w2, x, T, H, FF);
     }
   }
@@ -368,6 +488,181 @@ kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only) {
     h->launches++;
   }
   KC_TRY(cudaGetLastError(), "launch");
+  return KC_OK;
+}
+
+// The forward on the tensor cores (tc_gemm.cuh, fast.cuh): the selector
+// raises ws.flags[f] for frames whose decisions it cannot certify.
+kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
+  const Dims& d = h->d;
+  const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r;
+  const uint32_t H = d.h, FF = d.ffn;
+  KC_CHECK(build_images(h));
+  KC_TRY(cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream), "memset");
+  KC_TRY(cudaMemsetAsync(ws.flags.p, 0, b.frames * 4ull, h->stream), "memset");
+  float* x = P<float>(ws.x);
+  float* qkv = P<float>(ws.qkv);
+  if (T > 0) {
+    ProfScope ps(h, kStEmbed);
+    kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
+                     h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
+                     x, T};
+    kc::k_embed_exact<<<unsigned((T + 7) / 8), 256, 0, h->stream>>>(ea);
+    h->launches++;
+  }
+  const float attn_scale = float(1.0 / std::sqrt(double(d.hd)));
+  const int enc_m = 0, mix_m = 3 * int(d.enc), sel_m = mix_m + 5 * int(d.mix);
+  for (uint32_t blk = 0; blk < d.enc && T > 0; blk++) {
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
+      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, x, T, enc_m + 3 * blk, qkv));
+    }
+    {
+      ProfScope ps(h, kStEncAttn);
+      kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale};
+      kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, kc::kLaSmem,
+                              h->stream>>>(la);
+      h->launches++;
+    }
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
+      KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, x, T, enc_m + 3 * blk + 1, qkv));
+    }
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
+      KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, qkv, T, enc_m + 3 * blk + 2, x));
+    }
+  }
+  {
+    ProfScope ps(h, kStPool);
+    kc::PoolArgs pa{x, h->w + d.off_pool, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), P<uint32_t>(ws.rec_row),
+                    N, 1.0 / std::sqrt(double(H)), P<float>(ws.bk), P<float>(ws.bv), P<float>(ws.qstate)};
+    kc::k_pool_exact<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pa);
+    h->launches++;
+  }
+  if (Q > 0) {
+    ProfScope ps(h, kStMixer);
+    for (uint32_t blk = 0; blk < d.mix; blk++) {
+      const int m0 = mix_m + 5 * int(blk);
+      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
+      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
+      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
+      kc::CrossAttnFastArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
+                               P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off), tot.max_r, attn_scale};
+      kc::k_cross_attn_fast<<<unsigned(Q), 128, size_t(tot.max_r) * 4 * 4, h->stream>>>(ca);
+      h->launches++;
+      KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, P<float>(ws.qstate), Q, m0 + 3, P<float>(ws.mh)));
+      KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, P<float>(ws.mh), Q, m0 + 4, P<float>(ws.qstate)));
+    }
+  }
+  if (Q > 0) {
+    ProfScope ps(h, kStSelector);
+    KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, sel_m, P<float>(ws.sq)));
+    KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, sel_m + 1, P<float>(ws.sk)));
+    kc::SelectFastArgs sa{};
+    sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk);
+    sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
+    sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
+    sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
+    sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
+    sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = float(1.0 / std::sqrt(double(H)));
+    sa.tau = h->tau; sa.tau_c = h->tau_c;
+    sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
+    kc::k_select_fast<<<unsigned(Q), 256, size_t(tot.max_r) * 4, h->stream>>>(sa);
+    h->launches++;
+  }
+  KC_TRY(cudaGetLastError(), "launch");
+  return KC_OK;
+}
+
+// Recompute on the exact path every frame the fast selector could not
+// certify (or all of them after a split overflow), then scatter the exact
+// p blocks and indices into the batch's outputs.
+kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
+  const uint32_t F = b.frames;
+  if (h->h_flags_cap < F) {
+    if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
+    h->h_flags_pinned = nullptr;
+    h->h_flags_cap = 0;
+    KC_TRY(cudaMallocHost(&h->h_flags_pinned, F * 4ull), "pinned");
+    h->h_flags_cap = F;
+  }
+  KC_TRY(cudaMemcpyAsync(h->h_flags_pinned, ws.flags.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "certify");
+  const int e = *h->h_err;
+  if (e & kc::tc::kErrTimeout)
+    return fail(h, KC_ERR_TIMEOUT, "a tensor-core pipeline wait expired; the batch was not completed");
+  const bool all = e & kc::tc::kErrOverflow;
+  if (all && h->sa > -24) h->sa -= 6;  // later batches split at a smaller scale
+  std::vector<uint32_t>& list = h->h_flags;
+  list.clear();
+  for (uint32_t f = 0; f < F; f++)
+    if (all || h->h_flags_pinned[f]) list.push_back(f);
+  if (list.empty() || tot.q == 0) return KC_OK;
+  ProfScope ps(h, kStFallback);
+  h->prof.fallback_frames += list.size();
+  const uint32_t n = uint32_t(list.size());
+  Workspace& fb = h->ws_fb;
+  KC_TRY(ensure(fb.list, n * 4ull), "workspace");
+  KC_TRY(ensure(fb.rec_off, (n + 1) * 8ull), "workspace");
+  KC_TRY(ensure(fb.uniforms, (n + 1) * 8ull), "workspace");  // sub question offsets
+  KC_TRY(cudaMemcpyAsync(fb.list.p, list.data(), n * 4ull, cudaMemcpyHostToDevice, h->stream), "upload");
+  kc::k_fallback_offsets<<<1, 1024, 0, h->stream>>>(P<uint32_t>(fb.list), n, b.rec_off, P<uint64_t>(ws.q_off),
+                                                    P<uint64_t>(fb.rec_off), P<uint64_t>(fb.uniforms));
+  h->launches++;
+  uint64_t sizes[2];
+  KC_TRY(cudaMemcpyAsync(&sizes[0], P<uint64_t>(fb.rec_off) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(&sizes[1], P<uint64_t>(fb.uniforms) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "certify");
+  const uint64_t nrec = sizes[0], nq = sizes[1];
+  // the sub question offsets live in fb.uniforms until the gather; move them
+  KC_TRY(ensure(fb.rows_off, (n + 1) * 8ull), "workspace");
+  KC_TRY(cudaMemcpyAsync(fb.rows_off.p, fb.uniforms.p, (n + 1) * 8ull, cudaMemcpyDeviceToDevice, h->stream), "copy");
+  KC_TRY(ensure(fb.token_ids, nrec * 32), "workspace");
+  KC_TRY(ensure(fb.field_roles, nrec * 32), "workspace");
+  KC_TRY(ensure(fb.schema_ids, nrec * 4), "workspace");
+  KC_TRY(ensure(fb.band_ids, nrec * 4), "workspace");
+  KC_TRY(ensure(fb.schema_allow, nq * 32 + 32), "workspace");
+  KC_TRY(ensure(fb.band_allow, nq * 4 + 4), "workspace");
+  KC_TRY(ensure(fb.uniforms, nq * 8 + 8), "workspace");
+  kc::k_fallback_gather<<<n, 256, 0, h->stream>>>(
+      P<uint32_t>(fb.list), b.rec_off, P<uint64_t>(ws.q_off), P<uint64_t>(fb.rec_off), P<uint64_t>(fb.rows_off),
+      b.token_ids, b.field_roles, b.schema_ids, b.band_ids, b.schema_allow, b.band_allow, b.uniforms,
+      P<uint32_t>(fb.token_ids), P<uint32_t>(fb.field_roles), P<uint32_t>(fb.schema_ids), P<uint32_t>(fb.band_ids),
+      P<uint32_t>(fb.schema_allow), P<uint32_t>(fb.band_allow), P<double>(fb.uniforms));
+  h->launches++;
+  DevBatch sub;
+  sub.frames = n; sub.records = nrec; sub.rec_off = P<uint64_t>(fb.rec_off);
+  sub.token_ids = P<uint32_t>(fb.token_ids); sub.field_roles = P<uint32_t>(fb.field_roles);
+  sub.schema_ids = P<uint32_t>(fb.schema_ids); sub.band_ids = P<uint32_t>(fb.band_ids);
+  sub.schema_allow = b.schema_allow ? P<uint32_t>(fb.schema_allow) : nullptr;
+  sub.band_allow = b.band_allow ? P<uint32_t>(fb.band_allow) : nullptr;
+  sub.uniforms = b.uniforms ? P<double>(fb.uniforms) : nullptr;
+  kc::FrameTotals sub_tot;
+  KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
+  KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
+  kc::k_fallback_scatter<<<n, 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.p_off),
+                                                   P<uint64_t>(ws.q_off), P<uint64_t>(fb.p_off),
+                                                   P<uint64_t>(fb.q_off), P<float>(fb.p), P<uint32_t>(fb.index),
+                                                   P<float>(ws.p), P<uint32_t>(ws.index));
+  h->launches++;
+  KC_TRY(cudaGetLastError(), "launch");
+  return KC_OK;
+}
+
+// Pack, then encode (+ select) at the handle's precision. *tot receives the
+// batch totals.
+kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only, kc::FrameTotals* tot_out) {
+  kc::FrameTotals tot;
+  KC_CHECK(pack_batch(h, h->ws, b, &tot));
+  if (encode_only || h->precision == KC_PRECISION_EXACT) {
+    KC_CHECK(forward_exact(h, h->ws, b, tot, encode_only));
+  } else {
+    KC_CHECK(forward_fast(h, h->ws, b, tot));
+    if (h->precision == KC_PRECISION_CERTIFIED) KC_CHECK(certify(h, h->ws, b, tot));
+  }
+  *tot_out = tot;
   return KC_OK;
 }
 
@@ -457,6 +752,37 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
     if ((s = put(d.off_dec, w->decision_head_wh, uint64_t(d.route) * 3 * d.h))) return s;
   if (all || ch->value_head)
     if ((s = put(d.off_val, w->value_head_wv, 3ull * d.h))) return s;
+  // max |W| of every tensor-core matrix whose values moved (sets its split scale)
+  const bool blocks = all || ch->blocks, sel = all || ch->selector;
+  if (blocks || sel) {
+    auto amax = [](const float* a, uint64_t n, float m) {
+      for (uint64_t i = 0; i < n; i++) m = std::max(m, std::fabs(a[i]));
+      return m;
+    };
+    const uint64_t fh = uint64_t(d.ffn) * d.h;
+    size_t i = 0;
+    for (uint32_t b = 0; b < d.enc; b++, i += 3) {
+      if (!blocks) continue;
+      const kc_block_view& bv = w->enc[b];
+      h->mat_max[i] = amax(bv.wk, hh, amax(bv.wv, hh, amax(bv.wq, hh, 0.f)));
+      h->mat_max[i + 1] = amax(bv.w1, fh, 0.f);
+      h->mat_max[i + 2] = amax(bv.w2, fh, 0.f);
+    }
+    for (uint32_t b = 0; b < d.mix; b++, i += 5) {
+      if (!blocks) continue;
+      const kc_block_view& bv = w->mixer[b];
+      h->mat_max[i] = amax(bv.wq, hh, 0.f);
+      h->mat_max[i + 1] = amax(bv.wk, hh, 0.f);
+      h->mat_max[i + 2] = amax(bv.wv, hh, 0.f);
+      h->mat_max[i + 3] = amax(bv.w1, fh, 0.f);
+      h->mat_max[i + 4] = amax(bv.w2, fh, 0.f);
+    }
+    if (sel) {
+      h->mat_max[i] = amax(w->selector_wq, hh, 0.f);
+      h->mat_max[i + 1] = amax(w->selector_wk, hh, 0.f);
+    }
+    h->images_dirty = true;
+  }
   KC_TRY(cudaStreamSynchronize(h->stream), "sync");
   return KC_OK;
 }
@@ -520,6 +846,26 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   if ((e = cudaMemcpy(h->token_rows, config->token_rows, uint64_t(h->token_rows_len) * 4, cudaMemcpyHostToDevice)))
     return bail(e, "tokenRows");
   if ((e = cudaMallocHost(&h->h_tot, sizeof(kc::FrameTotals)))) return bail(e, "pinned");
+  if ((e = cudaMallocHost(&h->h_err, sizeof(int)))) return bail(e, "pinned");
+  if ((e = cudaMalloc(&h->d_err, sizeof(int)))) return bail(e, "error word");
+  if ((e = cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device))) return bail(e, "attributes");
+  h->mats = mat_list(h->d);
+  h->mat_max.assign(h->mats.size(), 0.f);
+  for (const Mat& m : h->mats)
+    if (m.n % 128 || m.k % 64) {
+      kc_destroy(h);
+      return fail(nullptr, KC_ERR_CAPACITY, "tensor-core path needs matrix sizes in multiples of 128 x 64");
+    }
+  if ((e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kSmemBytesT)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kSmemBytesT)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kSmemBytesT)) ||
+      (e = cudaFuncSetAttribute(kc::k_local_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::kLaSmem)) ||
+      (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(KC_MAX_BANK) * 4 * 4)))
+    return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -587,7 +933,8 @@ kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_outpu
   b.frames = 1; b.records = n; b.rec_off = P<uint64_t>(ws.rec_off);
   b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
   b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
-  if ((s = run_batch(h, b, true))) return s;
+  kc::FrameTotals tot;
+  if ((s = run_batch(h, b, true, &tot))) return s;
   const uint64_t H = h->d.h;
   KC_TRY(cudaMemcpyAsync(query_output, ws.qstate.p, q * H * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
   if (r) {
@@ -805,8 +1152,8 @@ kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* 
       b.uniforms = P<double>(ws.uniforms);
     }
   }
-  if ((s = run_batch(h, b, false))) return s;
-  const kc::FrameTotals& tot = *h->h_tot;
+  kc::FrameTotals tot;
+  if ((s = run_batch(h, b, false, &tot))) return s;
   out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
   if (tot.p > out->p_capacity || tot.q > out->q_capacity || (tot.p && !out->p) || (tot.q && !out->index))
     return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the batch's p / index");
@@ -837,13 +1184,24 @@ kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_devi
   b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
   b.band_ids = bv->band_ids; b.schema_allow = bv->schema_allow; b.band_allow = bv->band_allow;
   b.uniforms = bv->uniforms;
-  kc_status s = run_batch(h, b, false);
+  kc::FrameTotals tot;
+  kc_status s = run_batch(h, b, false, &tot);
   if (s) return s;
-  const kc::FrameTotals& tot = *h->h_tot;
   out->p = P<float>(h->ws.p); out->index = P<uint32_t>(h->ws.index);
   out->p_off = P<uint64_t>(h->ws.p_off); out->q_off = P<uint64_t>(h->ws.q_off);
   out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
   if (h->profiling) prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_set_precision(kc_handle* h, int mode, float tau) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (mode != KC_PRECISION_EXACT && mode != KC_PRECISION_CERTIFIED && mode != KC_PRECISION_FAST)
+    return fail(h, KC_ERR_INVALID_ARG, "unknown precision mode");
+  if (tau < 0.f || !(tau == tau)) return fail(h, KC_ERR_INVALID_ARG, "tau must be a non-negative number");
+  h->precision = mode;
+  if (tau > 0.f) h->tau = h->tau_c = tau;
   return KC_OK;
 }
 
@@ -900,6 +1258,19 @@ void kc_destroy(kc_handle* h) {
                       &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off};
     for (DevBuf* b : bufs)
       if (b->p) cudaFree(b->p);
+    Workspace& f = h->ws_fb;
+    DevBuf* fbufs[] = {&f.rec_off, &f.token_ids, &f.field_roles, &f.schema_ids, &f.band_ids, &f.schema_allow,
+                       &f.band_allow, &f.uniforms, &f.mask, &f.bank_schema, &f.bank_band, &f.rec_meta, &f.frame_t,
+                       &f.frame_q, &f.frame_r, &f.t_off, &f.q_off, &f.r_off, &f.p_off, &f.totals, &f.tok_recpos,
+                       &f.rec_start, &f.rec_row, &f.bank_rec, &f.bank_frame, &f.query_rec, &f.query_frame, &f.x,
+                       &f.qkv, &f.bk, &f.bv, &f.mk, &f.mv, &f.qstate, &f.mq, &f.mh, &f.sq, &f.sk, &f.p, &f.index,
+                       &f.gather, &f.rows_val, &f.rows_off, &f.flags, &f.list, &h->ws.flags, &h->ws.list,
+                       &h->images};
+    for (DevBuf* b : fbufs)
+      if (b->p) cudaFree(b->p);
+    if (h->d_err) cudaFree(h->d_err);
+    if (h->h_err) cudaFreeHost(h->h_err);
+    if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
     for (auto& pr : h->ev_pool) {
       cudaEventDestroy(pr.first);
       cudaEventDestroy(pr.second);
