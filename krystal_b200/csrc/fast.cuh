@@ -14,16 +14,12 @@ namespace kc {
 
 // ---------------------------------------------------------------------------
 // Record-local attention + residual, f32 (attentionOracle local mode,
-// forward/oracle.ts:64-105, :255-256). One warp per record, lane =
-// head*8 + token. The record's q|k|v rows are staged with a row stride of
-// 420 floats (= 4 mod 32) and 33-float head segments, so the 32 lanes of a
-// q read hit 32 different banks and the k / v reads broadcast per head.
+// forward/oracle.ts:64-105, :255-256). One warp per record, lane = head*8 +
+// token; no shared memory. A lane holds its token's q slice and the output
+// in registers; the 8 lanes of a head read each key / value row slice with
+// the same address, so every load request of the warp touches 4 segments.
 // ---------------------------------------------------------------------------
-constexpr int kLaRow = 420;   // floats per staged token row
-constexpr int kLaSeg = 33;    // floats per head segment
-constexpr int kLaPart = 132;  // q / k / v part: 4 heads x 33
-constexpr int kLaWarps = 4;
-constexpr int kLaSmem = kLaWarps * KC_RW * kLaRow * 4;  // 53 760 bytes
+constexpr int kLaWarps = 8;
 
 struct LocalAttnFastArgs {
   const float* qkv;           // [T,384]
@@ -35,62 +31,135 @@ struct LocalAttnFastArgs {
 };
 
 __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFastArgs a) {
-  extern __shared__ __align__(16) float la_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * kLaWarps + warp;
   if (g >= a.records) return;
   const uint32_t start = a.rec_start[g];
   const int cnt = int(a.rec_meta[g].y & 15u);
-  if (cnt == 0) return;
-  float* rec = la_smem + warp * KC_RW * kLaRow;
-  const float* src = a.qkv + uint64_t(start) * 3 * KC_H;
-  for (int i = lane; i < cnt * 3 * KC_H; i += 32) {
-    const int r = i / (3 * KC_H), c = i % (3 * KC_H);
-    const int part = c >> 7, head = (c >> 5) & 3, d = c & 31;
-    rec[r * kLaRow + part * kLaPart + head * kLaSeg + d] = src[i];
-  }
-  __syncwarp();
   const int head = lane >> 3, ti = lane & 7;
-  float out[KC_HEAD_DIM];
-  if (ti < cnt) {
-    const float* q = rec + ti * kLaRow + head * kLaSeg;
-    float p[KC_RW];
-    float mx = -INFINITY;
-    for (int j = 0; j < cnt; j++) {
-      const float* k = rec + j * kLaRow + kLaPart + head * kLaSeg;
+  if (ti >= cnt) return;
+  const float4* base = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
+  // row r, part (0 q, 1 k, 2 v), head slice: float4 index r*96 + part*32 + head*8
+  float4 q[8];
+#pragma unroll
+  for (int m = 0; m < 8; m++) q[m] = __ldg(base + ti * 96 + head * 8 + m);
+  float p[KC_RW];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++) {
+    if (j < cnt) {
+      const float4* k = base + j * 96 + 32 + head * 8;
       float s = 0.f;
 #pragma unroll
-      for (int d = 0; d < KC_HEAD_DIM; d++) s = fmaf(q[d], k[d], s);
+      for (int m = 0; m < 8; m++) {
+        const float4 kv = __ldg(k + m);
+        s = fmaf(q[m].x, kv.x, s); s = fmaf(q[m].y, kv.y, s); s = fmaf(q[m].z, kv.z, s); s = fmaf(q[m].w, kv.w, s);
+      }
       p[j] = s * a.scale;
       mx = fmaxf(mx, p[j]);
     }
-    float sum = 0.f;
-    for (int j = 0; j < cnt; j++) {
-      p[j] = expf(p[j] - mx);
-      sum += p[j];
-    }
-    const float inv = 1.f / fmaxf(sum, 1e-20f);
+  }
+  float sum = 0.f;
 #pragma unroll
-    for (int d = 0; d < KC_HEAD_DIM; d++) out[d] = 0.f;
-    for (int j = 0; j < cnt; j++) {
+  for (int j = 0; j < KC_RW; j++)
+    if (j < cnt) { p[j] = expf(p[j] - mx); sum += p[j]; }
+  const float inv = 1.f / fmaxf(sum, 1e-20f);
+  float4 o[8];
+#pragma unroll
+  for (int m = 0; m < 8; m++) o[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++) {
+    if (j < cnt) {
       const float pj = p[j] * inv;
-      const float* v = rec + j * kLaRow + 2 * kLaPart + head * kLaSeg;
+      const float4* v = base + j * 96 + 64 + head * 8;
 #pragma unroll
-      for (int d = 0; d < KC_HEAD_DIM; d++) out[d] = fmaf(pj, v[d], out[d]);
+      for (int m = 0; m < 8; m++) {
+        const float4 vv = __ldg(v + m);
+        o[m].x = fmaf(pj, vv.x, o[m].x); o[m].y = fmaf(pj, vv.y, o[m].y);
+        o[m].z = fmaf(pj, vv.z, o[m].z); o[m].w = fmaf(pj, vv.w, o[m].w);
+      }
     }
   }
-  __syncwarp();
-  if (ti < cnt) {  // only this lane reads its q slice: overwrite it with the output
-    float* q = rec + ti * kLaRow + head * kLaSeg;
+  float4* xr = reinterpret_cast<float4*>(a.x + (uint64_t(start) + ti) * KC_H) + head * 8;
 #pragma unroll
-    for (int d = 0; d < KC_HEAD_DIM; d++) q[d] = out[d];
+  for (int m = 0; m < 8; m++) {
+    float4 xv = xr[m];
+    xv.x += o[m].x; xv.y += o[m].y; xv.z += o[m].z; xv.w += o[m].w;
+    xr[m] = xv;
   }
-  __syncwarp();
-  float* xr = a.x + uint64_t(start) * KC_H;
-  for (int i = lane; i < cnt * KC_H; i += 32) {
-    const int r = i >> 7, c = i & 127;
-    xr[i] += rec[r * kLaRow + (c >> 5) * kLaSeg + (c & 31)];
+}
+
+// ---------------------------------------------------------------------------
+// Learned-query pooling, f32 (poolRecord, oracle.ts:186-224). One warp per
+// record; lane l holds dims 4l..4l+3 of each token row; the two score dot
+// products are reduced across the warp.
+// ---------------------------------------------------------------------------
+struct PoolFastArgs {
+  const float* x;
+  const float* pool;          // [2,128]
+  const uint32_t* rec_start;
+  const uint2* rec_meta;
+  const uint32_t* rec_row;    // bank row, or question row | 0x80000000
+  uint64_t records;
+  float scale;                // 1/sqrt(H)
+  float* bank_keys;
+  float* bank_values;
+  float* query_values;
+};
+
+__global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  const uint32_t row = a.rec_row[g];
+  const bool isq = row & 0x80000000u;
+  const uint32_t r = row & 0x7fffffffu;
+  float4* key_out = isq ? nullptr : reinterpret_cast<float4*>(a.bank_keys + uint64_t(r) * KC_H) + lane;
+  float4* val_out = reinterpret_cast<float4*>(isq ? a.query_values + uint64_t(r) * KC_H
+                                                  : a.bank_values + uint64_t(r) * KC_H) + lane;
+  const float4 pk = __ldg(reinterpret_cast<const float4*>(a.pool) + lane);
+  const float4 pv = __ldg(reinterpret_cast<const float4*>(a.pool + KC_H) + lane);
+  float4 xs[KC_RW];
+  float ks[KC_RW], vs[KC_RW];
+  float kmx = -INFINITY, vmx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++) {
+    if (j < cnt) {
+      xs[j] = __ldg(reinterpret_cast<const float4*>(a.x + (uint64_t(start) + j) * KC_H) + lane);
+      float k = pk.x * xs[j].x + pk.y * xs[j].y + pk.z * xs[j].z + pk.w * xs[j].w;
+      float v = pv.x * xs[j].x + pv.y * xs[j].y + pv.z * xs[j].z + pv.w * xs[j].w;
+      for (int o = 16; o; o >>= 1) {
+        k += __shfl_xor_sync(0xffffffffu, k, o);
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+      }
+      ks[j] = k * a.scale;
+      vs[j] = v * a.scale;
+      kmx = fmaxf(kmx, ks[j]);
+      vmx = fmaxf(vmx, vs[j]);
+    }
   }
+  float ksum = 0.f, vsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++)
+    if (j < cnt) {
+      ks[j] = expf(ks[j] - kmx); ksum += ks[j];
+      vs[j] = expf(vs[j] - vmx); vsum += vs[j];
+    }
+  const float kinv = cnt ? 1.f / fmaxf(ksum, 1e-20f) : 0.f, vinv = cnt ? 1.f / fmaxf(vsum, 1e-20f) : 0.f;
+  float4 ko = make_float4(0.f, 0.f, 0.f, 0.f), vo = ko;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++)
+    if (j < cnt) {
+      const float kw = ks[j] * kinv, vw = vs[j] * vinv;
+      ko.x = fmaf(kw, xs[j].x, ko.x); ko.y = fmaf(kw, xs[j].y, ko.y);
+      ko.z = fmaf(kw, xs[j].z, ko.z); ko.w = fmaf(kw, xs[j].w, ko.w);
+      vo.x = fmaf(vw, xs[j].x, vo.x); vo.y = fmaf(vw, xs[j].y, vo.y);
+      vo.z = fmaf(vw, xs[j].z, vo.z); vo.w = fmaf(vw, xs[j].w, vo.w);
+    }
+  if (key_out) *key_out = ko;
+  *val_out = vo;
 }
 
 // ---------------------------------------------------------------------------

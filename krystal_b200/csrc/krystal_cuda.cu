@@ -291,14 +291,14 @@ template <int EPI>
 kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C) {
   if (M == 0) return KC_OK;
   const Mat& mt = h->mats[mat];
-  CUtensorMap map;
-  if (!kc::tc::make_a_map(&map, A, M, mt.k, mt.k))
+  CUtensorMap map, cmap;
+  if (!kc::tc::make_a_map(&map, A, M, mt.k, mt.k) || !kc::tc::make_c_map(&cmap, C, M, mt.n, mt.n))
     return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a GEMM operand");
   kc::tc::GemmArgs g{int(M), int(mt.k), int(mt.n / 128), P<uint8_t>(h->images) + h->img_off[mat], C,
                      int(mt.n), std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat))), h->d_err};
   const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
-  kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, g);
+  kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, g);
   h->launches++;
   return KC_OK;
 }
@@ -520,8 +520,8 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     {
       ProfScope ps(h, kStEncAttn);
       kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale};
-      kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, kc::kLaSmem,
-                              h->stream>>>(la);
+      kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, 0, h->stream>>>(
+          la);
       h->launches++;
     }
     {
@@ -535,9 +535,10 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   }
   {
     ProfScope ps(h, kStPool);
-    kc::PoolArgs pa{x, h->w + d.off_pool, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), P<uint32_t>(ws.rec_row),
-                    N, 1.0 / std::sqrt(double(H)), P<float>(ws.bk), P<float>(ws.bv), P<float>(ws.qstate)};
-    kc::k_pool_exact<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pa);
+    kc::PoolFastArgs pa{x, h->w + d.off_pool, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta),
+                        P<uint32_t>(ws.rec_row), N, float(1.0 / std::sqrt(double(H))), P<float>(ws.bk),
+                        P<float>(ws.bv), P<float>(ws.qstate)};
+    kc::k_pool_fast<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pa);
     h->launches++;
   }
   if (Q > 0) {
@@ -862,7 +863,6 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
-      (e = cudaFuncSetAttribute(kc::k_local_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::kLaSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * 4)))
     return bail(e, "smem");

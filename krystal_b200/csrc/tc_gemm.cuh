@@ -16,8 +16,9 @@
 //              into a 128x128 fp32 accumulator in TMEM; tcgen05.commit frees
 //              the stage; two accumulators double-buffer the epilogue.
 //   warps 6-9  epilogue: tcgen05.ld the accumulator rows, unscale, apply
-//              store / ReLU / residual, write f32 to global.
-// Every wait is bounded (about a second); on expiry the kernel raises the
+//              store / ReLU / residual in 128-byte swizzled shared tiles,
+//              TMA-store them (the residual input arrives by TMA load).
+// Every wait is bounded (about two seconds); on expiry the kernel raises the
 // error word and drains, so a fault in the pipeline can never hang the GPU.
 #pragma once
 #include <cuda.h>
@@ -33,19 +34,13 @@ constexpr int kBN = 128;         // columns per tile (TMEM columns per accumulat
 constexpr int kBK = 64;          // K per chunk: one 128-byte swizzle row of fp16
 constexpr int kTileBytes = kBM * kBK * 2;           // 16 KB: one fp16 [128 x 64] tile
 constexpr uint32_t kTmemCols = 2 * kBN;              // two accumulators
-constexpr unsigned long long kWaitNs = 1000000000ull; // 1 s per wait
+constexpr long long kWaitCycles = 4000000000ll;      // ~2 s per wait at the B200's clocks
 
 // Error word bits.
 enum : int { kErrTimeout = 1, kErrOverflow = 2 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -75,16 +70,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on a phase parity. Returns false (and raises the error word)
-// when the budget expires or another thread has already raised it.
+// when the budget expires or another thread has already raised it. The loop
+// stays tight: the error word (a global load) and the SM clock are looked at
+// once every 64 failed tries, so a completed phase is seen at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  while (true) {
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; i++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) return false;
-    if (globaltimer() - t0 > kWaitNs) {
-      atomicOr(err, kErrTimeout);
-      return false;
+    if ((i & 63u) == 0) {
+      if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        atomicOr(err, kErrTimeout);
+        return false;
+      }
     }
   }
 }
@@ -204,13 +203,15 @@ constexpr int kStagesT = 3;
 // A region (32 KB: the TMA lands f32 there, the split rewrites it in place as
 // fp16 hi | lo) then B hi | B lo (32 KB)
 constexpr int kStageBytesT = 4 * kTileBytes;
-constexpr int kEpiBytes = 4 * 32 * 33 * 4;     // one padded 32x32 f32 block per epilogue warp
+constexpr int kEpiBuf = 32 * 32 * 4;           // one 32x32 f32 block, 128-byte swizzled rows
+constexpr int kEpiBytes = 4 * 2 * kEpiBuf;      // two per epilogue warp
 constexpr int kSmemBytesT = kStagesT * kStageBytesT + kEpiBytes + 1024 + 256;
 constexpr int kThreadsT = 320;                // TMA warp, 4 split warps, MMA warp, 4 epilogue warps
 
 // Warp roles: 0 TMA issuer, 1-4 split A f32 -> fp16 hi/lo, 5 MMA issuer, 6-9 epilogue.
 template <int EPI>
-__global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant__ CUtensorMap amap, GemmArgs a) {
+__global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant__ CUtensorMap amap,
+                                                           const __grid_constant__ CUtensorMap cmap, GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,7 +222,8 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
   uint64_t* tfull = empty + kStagesT;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* cload = drain + 1;  // [4 warps][2 buffers]: residual tiles landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cload + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (a.M + kBM - 1) / kBM;
@@ -239,6 +241,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       mbar_init(&tempty[i], 128);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; i++) mbar_init(&cload[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
@@ -359,49 +362,80 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
     __syncwarp();
   } else {
     // ---------------- epilogue ----------------
-    // Each 32x32 accumulator block goes through a padded shared buffer so a
-    // warp store writes one contiguous 128-byte row segment.
+    // Each 32x32 accumulator block is written as 128-byte swizzled rows into
+    // one of this warp's two shared buffers and leaves with one TMA store;
+    // the residual block arrives the same way, by a TMA load.
     const int g = warp & 3;  // TMEM lane quarter this warp may read
-    float* buf = epi_buf + (warp - 6) * 32 * 33;
+    const int ew = warp - 6;
+    unsigned char* bufs = reinterpret_cast<unsigned char*>(epi_buf) + ew * 2 * kEpiBuf;
+    uint32_t cphase = 0;      // parity bits of this warp's two residual barriers
     uint32_t tl = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
       const int m = t / a.n_sub, n = t % a.n_sub;
       const uint32_t acc = tl & 1, aph = (tl >> 1) & 1;
       // one lane waits, the warp follows: tcgen05.ld below is warp-collective
       int okw = 0;
       if (lane == 0) okw = mbar_wait(&tfull[acc], aph, a.err) ? 1 : 0;
       okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw) break;
+      if (!okw) { ok = false; break; }
       tc_fence_after();
-      const int64_t row0 = int64_t(m) * kBM + g * 32;
+      const int row0 = m * kBM + g * 32;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_base + (uint32_t(g * 32) << 16) + acc * kBN + c0, v);
-#pragma unroll
-        for (int j = 0; j < 32; j++) buf[lane * 33 + j] = v[j] * a.unscale;  // row = lane
-        __syncwarp();
-        float* cbase = a.C + n * kBN + c0 + lane;
-        const int rows = a.M - row0 < 32 ? int(a.M - row0) : 32;
-        float cin[32];
-        if (EPI == kEpiResid) {  // all residual loads in flight before any use
-#pragma unroll
-          for (int r = 0; r < 32; r++) cin[r] = r < rows ? cbase[(row0 + r) * a.ldc] : 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < 32; r++) {
-          if (r < rows) {
-            float o = buf[r * 33 + lane];
-            if (EPI == kEpiRelu) o = fmaxf(o, 0.f);
-            else if (EPI == kEpiResid) o += cin[r];
-            cbase[(row0 + r) * a.ldc] = o;
+      for (int cc = 0; cc < kBN / 32; cc++) {
+        const int b = cc & 1;
+        unsigned char* buf = bufs + b * kEpiBuf;
+        const int x = n * kBN + cc * 32;
+        if (lane == 0) {
+          // the TMA store that last read this buffer must be done with it
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          if (EPI == kEpiResid) {
+            mbar_arrive_expect_tx(&cload[ew * 2 + b], kEpiBuf);
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                ::"r"(smem_u32(buf)), "l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0),
+                "r"(smem_u32(&cload[ew * 2 + b]))
+                : "memory");
           }
         }
+        float v[32];
+        tmem_ld32(tmem_base + (uint32_t(g * 32) << 16) + acc * kBN + cc * 32, v);
+        if (EPI == kEpiResid) {  // every lane observes the landing of the tile it reads
+          const bool mine = mbar_wait(&cload[ew * 2 + b], (cphase >> b) & 1, a.err);
+          cphase ^= 1u << b;
+          if (!__all_sync(0xffffffffu, mine)) { ok = false; break; }
+        }
+        // row = lane; 16-byte chunk j of the row sits at chunk j ^ (row & 7)
+        unsigned char* rowp = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float4 o = make_float4(v[4 * j] * a.unscale, v[4 * j + 1] * a.unscale, v[4 * j + 2] * a.unscale,
+                                 v[4 * j + 3] * a.unscale);
+          float4* cp = reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4));
+          if (EPI == kEpiRelu) {
+            o.x = fmaxf(o.x, 0.f); o.y = fmaxf(o.y, 0.f); o.z = fmaxf(o.z, 0.f); o.w = fmaxf(o.w, 0.f);
+          } else if (EPI == kEpiResid) {
+            const float4 c = *cp;
+            o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+          }
+          *cp = o;
+        }
+        fence_proxy_async_smem();
         __syncwarp();
+        if (lane == 0) {
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                       ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0), "r"(smem_u32(buf))
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    // every store has left shared memory and landed before the CTA exits
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -456,6 +490,19 @@ inline EncodeTiledFn encode_tiled_fn() {
 
 // Returns false if the encoder is unavailable or refuses the map (A must be
 // 16-byte aligned and lda a multiple of 4).
+// The C operand [rows, cols] f32: boxes of [32 rows x 32 cols], 128-byte swizzle.
+inline bool make_c_map(CUtensorMap* map, const float* C, uint64_t rows, uint64_t cols, uint64_t ldc) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(C) & 15) || (ldc & 3) || cols % 32 || rows == 0) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ldc * 4};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(C), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool make_a_map(CUtensorMap* map, const float* A, uint64_t rows, uint64_t cols, uint64_t lda) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (!fn || (reinterpret_cast<uintptr_t>(A) & 15) || (lda & 3) || cols % kBK || rows == 0) return false;
