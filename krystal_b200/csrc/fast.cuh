@@ -14,12 +14,16 @@ namespace kc {
 
 // ---------------------------------------------------------------------------
 // Record-local attention + residual, f32 (attentionOracle local mode,
-// forward/oracle.ts:64-105, :255-256). One warp per record, lane = head*8 +
-// token; no shared memory. A lane holds its token's q slice and the output
-// in registers; the 8 lanes of a head read each key / value row slice with
-// the same address, so every load request of the warp touches 4 segments.
+// forward/oracle.ts:64-105, :255-256). One warp per record. The record's
+// q|k|v rows (contiguous, cnt x 1.5 KB) are staged in shared memory with
+// coalesced 16-byte loads; float4 f of token row i is stored at f ^ i (an
+// XOR swizzle within each aligned group of 8 float4), so the 8 lanes of a
+// quarter-warp — one head, tokens 0..7 — read 8 different bank groups.
+// lane = head*8 + token computes its scores, softmax and output in
+// registers; the residual add then streams x with coalesced loads/stores.
 // ---------------------------------------------------------------------------
-constexpr int kLaWarps = 8;
+constexpr int kLaWarps = 4;
+constexpr int kLaRowF4 = 96;  // float4 per staged q|k|v row
 
 struct LocalAttnFastArgs {
   const float* qkv;           // [T,384]
@@ -30,62 +34,78 @@ struct LocalAttnFastArgs {
   float scale;                // 1/sqrt(headDim)
 };
 
+__device__ __forceinline__ int la_swz(int row, int f4) { return row * kLaRowF4 + (f4 ^ row); }
+
 __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFastArgs a) {
+  __shared__ float4 stage[kLaWarps][KC_RW * kLaRowF4];  // 48 KB
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * kLaWarps + warp;
   if (g >= a.records) return;
   const uint32_t start = a.rec_start[g];
   const int cnt = int(a.rec_meta[g].y & 15u);
+  if (cnt == 0) return;
+  float4* st = stage[warp];
+  const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
+  const int n4 = cnt * kLaRowF4;
+  for (int i = lane; i < n4; i += 32) {
+    const int r = i / kLaRowF4, f = i - r * kLaRowF4;
+    st[la_swz(r, f)] = __ldg(src + i);
+  }
+  __syncwarp();
   const int head = lane >> 3, ti = lane & 7;
-  if (ti >= cnt) return;
-  const float4* base = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
-  // row r, part (0 q, 1 k, 2 v), head slice: float4 index r*96 + part*32 + head*8
-  float4 q[8];
-#pragma unroll
-  for (int m = 0; m < 8; m++) q[m] = __ldg(base + ti * 96 + head * 8 + m);
-  float p[KC_RW];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < KC_RW; j++) {
-    if (j < cnt) {
-      const float4* k = base + j * 96 + 32 + head * 8;
-      float s = 0.f;
-#pragma unroll
-      for (int m = 0; m < 8; m++) {
-        const float4 kv = __ldg(k + m);
-        s = fmaf(q[m].x, kv.x, s); s = fmaf(q[m].y, kv.y, s); s = fmaf(q[m].z, kv.z, s); s = fmaf(q[m].w, kv.w, s);
-      }
-      p[j] = s * a.scale;
-      mx = fmaxf(mx, p[j]);
-    }
-  }
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < KC_RW; j++)
-    if (j < cnt) { p[j] = expf(p[j] - mx); sum += p[j]; }
-  const float inv = 1.f / fmaxf(sum, 1e-20f);
   float4 o[8];
+  if (ti < cnt) {
+    float4 q[8];
 #pragma unroll
-  for (int m = 0; m < 8; m++) o[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int m = 0; m < 8; m++) q[m] = st[la_swz(ti, head * 8 + m)];
+    float p[KC_RW];
+    float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < KC_RW; j++) {
-    if (j < cnt) {
-      const float pj = p[j] * inv;
-      const float4* v = base + j * 96 + 64 + head * 8;
+    for (int j = 0; j < KC_RW; j++) {
+      if (j < cnt) {
+        float s = 0.f;
 #pragma unroll
-      for (int m = 0; m < 8; m++) {
-        const float4 vv = __ldg(v + m);
-        o[m].x = fmaf(pj, vv.x, o[m].x); o[m].y = fmaf(pj, vv.y, o[m].y);
-        o[m].z = fmaf(pj, vv.z, o[m].z); o[m].w = fmaf(pj, vv.w, o[m].w);
+        for (int m = 0; m < 8; m++) {
+          const float4 kv = st[la_swz(j, 32 + head * 8 + m)];
+          s = fmaf(q[m].x, kv.x, s); s = fmaf(q[m].y, kv.y, s); s = fmaf(q[m].z, kv.z, s); s = fmaf(q[m].w, kv.w, s);
+        }
+        p[j] = s * a.scale;
+        mx = fmaxf(mx, p[j]);
+      }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++)
+      if (j < cnt) { p[j] = expf(p[j] - mx); sum += p[j]; }
+    const float inv = 1.f / fmaxf(sum, 1e-20f);
+#pragma unroll
+    for (int m = 0; m < 8; m++) o[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) {
+      if (j < cnt) {
+        const float pj = p[j] * inv;
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+          const float4 vv = st[la_swz(j, 64 + head * 8 + m)];
+          o[m].x = fmaf(pj, vv.x, o[m].x); o[m].y = fmaf(pj, vv.y, o[m].y);
+          o[m].z = fmaf(pj, vv.z, o[m].z); o[m].w = fmaf(pj, vv.w, o[m].w);
+        }
       }
     }
   }
-  float4* xr = reinterpret_cast<float4*>(a.x + (uint64_t(start) + ti) * KC_H) + head * 8;
+  __syncwarp();
+  if (ti < cnt) {  // only this lane read its q slice: it now holds the head's output
 #pragma unroll
-  for (int m = 0; m < 8; m++) {
-    float4 xv = xr[m];
-    xv.x += o[m].x; xv.y += o[m].y; xv.z += o[m].z; xv.w += o[m].w;
-    xr[m] = xv;
+    for (int m = 0; m < 8; m++) st[la_swz(ti, head * 8 + m)] = o[m];
+  }
+  __syncwarp();
+  float4* xr = reinterpret_cast<float4*>(a.x + uint64_t(start) * KC_H);
+  for (int i = lane; i < cnt * 32; i += 32) {
+    const int r = i >> 5, f = i & 31;
+    float4 xv = xr[i];
+    const float4 ov = st[la_swz(r, f)];
+    xv.x += ov.x; xv.y += ov.y; xv.z += ov.z; xv.w += ov.w;
+    xr[i] = xv;
   }
 }
 
