@@ -47,9 +47,21 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
   float4* st = stage[warp];
   const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
   const int n4 = cnt * kLaRowF4;
-  for (int i = lane; i < n4; i += 32) {
-    const int r = i / kLaRowF4, f = i - r * kLaRowF4;
-    st[la_swz(r, f)] = __ldg(src + i);
+  for (int b0 = 0; b0 < n4; b0 += 4 * 32) {  // four 16-byte loads in flight per lane
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = b0 + u * 32 + lane;
+      if (i < n4) v[u] = __ldg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = b0 + u * 32 + lane;
+      if (i < n4) {
+        const int r = i / kLaRowF4, f = i - r * kLaRowF4;
+        st[la_swz(r, f)] = v[u];
+      }
+    }
   }
   __syncwarp();
   const int head = lane >> 3, ti = lane & 7;
@@ -100,13 +112,17 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
   }
   __syncwarp();
   float4* xr = reinterpret_cast<float4*>(a.x + uint64_t(start) * KC_H);
-  for (int i = lane; i < cnt * 32; i += 32) {
-    const int r = i >> 5, f = i & 31;
-    float4 xv = xr[i];
-    const float4 ov = st[la_swz(r, f)];
-    xv.x += ov.x; xv.y += ov.y; xv.z += ov.z; xv.w += ov.w;
-    xr[i] = xv;
-  }
+  float4 xv[KC_RW];
+#pragma unroll
+  for (int r = 0; r < KC_RW; r++)
+    if (r < cnt) xv[r] = xr[r * 32 + lane];
+#pragma unroll
+  for (int r = 0; r < KC_RW; r++)
+    if (r < cnt) {
+      const float4 ov = st[la_swz(r, lane)];
+      xv[r].x += ov.x; xv[r].y += ov.y; xv[r].z += ov.z; xv[r].w += ov.w;
+      xr[r * 32 + lane] = xv[r];
+    }
 }
 
 // ---------------------------------------------------------------------------
