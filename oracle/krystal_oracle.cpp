@@ -397,6 +397,451 @@ int forward(const ko_dims* d, const float* W, const uint32_t* token_rows, uint32
   return 0;
 }
 
+// ---------------------------------------------------------------------------
+// Backward (packages/krystal/src/forward/backward.ts), as host/gradients.ts:
+// 30-66 runs it for a session: context "available", the argument slot given
+// nothing to aim at (it contributes exactly zero), no route-kind labels.
+// ---------------------------------------------------------------------------
+
+// attentionWithP (backward.ts:580-618) with p kept per query row over its key
+// window: p_row[(head*q_rows + i) * kw + (j - from)], kw = window width.
+void attention_with_p(const float* q, const float* k, const float* v, const float* mask, uint64_t q_rows,
+                      uint64_t k_rows, uint32_t h, uint32_t heads, uint32_t head_dim, const uint32_t* local_start,
+                      const uint32_t* local_count, uint32_t kw, float* out, float* p) {
+  std::vector<float> scores(k_rows ? k_rows : 1);
+  const double scale = 1 / std::sqrt(double(head_dim));
+  for (uint64_t i = 0; i < q_rows * h; i++) out[i] = 0;
+  for (uint32_t head = 0; head < heads; head++) {
+    const uint32_t hb = head * head_dim;
+    for (uint64_t i = 0; i < q_rows; i++) {
+      const uint64_t from = local_start ? local_start[i] : 0;
+      const uint64_t to = local_start ? from + local_count[i] : k_rows;
+      for (uint64_t j = from; j < to; j++) {
+        double s = 0;
+        for (uint32_t dd = 0; dd < head_dim; dd++) s += double(q[i * h + hb + dd]) * double(k[j * h + hb + dd]);
+        scores[j] = f32(s * scale + (mask ? double(mask[i * k_rows + j]) : 0.0));
+      }
+      bool all_blocked = true;
+      for (uint64_t j = from; j < to; j++)
+        if (scores[j] >= -1e29) { all_blocked = false; break; }
+      if (all_blocked) {
+        for (uint64_t j = from; j < to; j++) scores[j] = 0;
+      } else {
+        softmax_row(scores.data() + from, uint32_t(to - from));
+      }
+      for (uint64_t j = from; j < to; j++) p[(uint64_t(head) * q_rows + i) * kw + (j - from)] = scores[j];
+      for (uint32_t dd = 0; dd < head_dim; dd++) {
+        double value = 0;
+        for (uint64_t j = from; j < to; j++) value += double(scores[j]) * double(v[j * h + hb + dd]);
+        out[i * h + hb + dd] = f32(value);
+      }
+    }
+  }
+}
+
+// attentionBackwardScores (backward.ts:79-115) then attentionBackwardQkv
+// (:117-166) for one attention, p in the windowed layout above. For the
+// dense (mixer) case the window is the whole key range (kw = k_rows).
+void attention_backward(const float* d_out, const float* q, const float* k, const float* v, const float* p,
+                        uint64_t q_rows, uint64_t k_rows, uint32_t h, uint32_t heads, uint32_t head_dim,
+                        const uint32_t* local_start, const uint32_t* local_count, uint32_t kw, float* dq, float* dk,
+                        float* dv) {
+  std::vector<float> d_scores(uint64_t(heads) * q_rows * kw + 1, 0.0f), dp(k_rows ? k_rows : 1);
+  for (uint32_t head = 0; head < heads; head++) {
+    for (uint64_t i = 0; i < q_rows; i++) {
+      const uint64_t from = local_start ? local_start[i] : 0;
+      const uint64_t to = local_start ? from + local_count[i] : k_rows;
+      const float* prow = p + (uint64_t(head) * q_rows + i) * kw;
+      double row_sum = 0;
+      for (uint64_t j = from; j < to; j++) {
+        double s = 0;
+        for (uint32_t d = 0; d < head_dim; d++)
+          s += double(d_out[i * h + head * head_dim + d]) * double(v[j * h + head * head_dim + d]);
+        dp[j] = f32(s);
+        row_sum += double(prow[j - from]) * s;
+      }
+      for (uint64_t j = from; j < to; j++)
+        d_scores[(uint64_t(head) * q_rows + i) * kw + (j - from)] = f32(double(prow[j - from]) * (double(dp[j]) - row_sum));
+    }
+  }
+  const double scale = 1 / std::sqrt(double(head_dim));
+  for (uint64_t i = 0; i < q_rows; i++) {
+    const uint64_t from = local_start ? local_start[i] : 0;
+    const uint64_t to = local_start ? from + local_count[i] : k_rows;
+    for (uint32_t col = 0; col < h; col++) {
+      const uint32_t head = col / head_dim;
+      double acc = 0;
+      for (uint64_t j = from; j < to; j++)
+        acc += double(d_scores[(uint64_t(head) * q_rows + i) * kw + (j - from)]) * double(k[j * h + col]);
+      dq[i * h + col] = f32(acc * scale);
+    }
+  }
+  // keys read the same windows the other way round: for the local case a key
+  // j is scored by its own record's rows; kw-relative index of j in row i's
+  // window is j - start[i]
+  for (uint64_t j = 0; j < k_rows; j++) {
+    const uint64_t from = local_start ? local_start[j] : 0;
+    const uint64_t to = local_start ? from + local_count[j] : q_rows;
+    for (uint32_t col = 0; col < h; col++) {
+      const uint32_t head = col / head_dim;
+      double acc_k = 0, acc_v = 0;
+      for (uint64_t i = from; i < to; i++) {
+        const uint64_t wi = local_start ? j - local_start[i] : j;
+        acc_k += double(d_scores[(uint64_t(head) * q_rows + i) * kw + wi]) * double(q[i * h + col]);
+        acc_v += double(p[(uint64_t(head) * q_rows + i) * kw + wi]) * double(d_out[i * h + col]);
+      }
+      dk[j * h + col] = f32(acc_k * scale);
+      dv[j * h + col] = f32(acc_v);
+    }
+  }
+}
+
+// matmulBackInput (backward.ts:548-557): dX[m,k] = sum_n dY[m,n] W[n,k]
+void matmul_back_input(const float* dy, const float* w, uint64_t m, uint32_t n, uint32_t k, float* dx) {
+  for (uint64_t i = 0; i < m; i++)
+    for (uint32_t j = 0; j < k; j++) {
+      double s = 0;
+      for (uint32_t l = 0; l < n; l++) s += double(dy[i * n + l]) * double(w[uint64_t(l) * k + j]);
+      dx[i * k + j] = f32(s);
+    }
+}
+
+// matmulBackWeight (backward.ts:560-569): dW[n,k] = sum_m dY[m,n] X[m,k]
+void matmul_back_weight(const float* dy, const float* x, uint64_t m, uint32_t n, uint32_t k, float* dw) {
+  for (uint32_t i = 0; i < n; i++)
+    for (uint32_t j = 0; j < k; j++) {
+      double s = 0;
+      for (uint64_t l = 0; l < m; l++) s += double(dy[l * n + i]) * double(x[l * k + j]);
+      dw[uint64_t(i) * k + j] = f32(s);
+    }
+}
+
+// poolBackward (backward.ts:184-262) over the records listed, accumulating
+// into d_states (f32 store per add) and d_pool (f32 store per add).
+void pool_backward(const float* states, const std::vector<uint32_t>& recs, const Active& a, const float* pool,
+                   const float* d_keys, const float* d_values, uint32_t h, float* d_states, float* d_pool) {
+  const double scale = 1 / std::sqrt(double(h));
+  for (size_t rec = 0; rec < recs.size(); rec++) {
+    const uint32_t slot = recs[rec];
+    const uint32_t start = a.offset[slot], count = a.count[slot];
+    if (count == 0) continue;
+    std::vector<float> pk(count), pv(count), dpk(count), dpv(count), ks(count), vs(count);
+    for (uint32_t j = 0; j < count; j++) {
+      double kk = 0, vv = 0;
+      for (uint32_t d = 0; d < h; d++) {
+        const double s = states[uint64_t(start + j) * h + d];
+        kk += double(pool[d]) * s;
+        vv += double(pool[h + d]) * s;
+      }
+      ks[j] = f32(kk * scale);
+      vs[j] = f32(vv * scale);
+    }
+    softmax_row(ks.data(), count);
+    softmax_row(vs.data(), count);
+    for (uint32_t j = 0; j < count; j++) {
+      pk[j] = ks[j];
+      pv[j] = vs[j];
+      double dk = 0, dv = 0;
+      for (uint32_t d = 0; d < h; d++) {
+        const double s = states[uint64_t(start + j) * h + d];
+        dk += double(d_keys[rec * h + d]) * s;
+        dv += double(d_values[rec * h + d]) * s;
+      }
+      dpk[j] = f32(dk);
+      dpv[j] = f32(dv);
+    }
+    double krs = 0, vrs = 0;
+    for (uint32_t j = 0; j < count; j++) {
+      krs += double(pk[j]) * double(dpk[j]);
+      vrs += double(pv[j]) * double(dpv[j]);
+    }
+    for (uint32_t j = 0; j < count; j++) {
+      const double dsk = double(pk[j]) * (double(dpk[j]) - krs);
+      const double dsv = double(pv[j]) * (double(dpv[j]) - vrs);
+      for (uint32_t d = 0; d < h; d++) {
+        const double s = states[uint64_t(start + j) * h + d];
+        const double ds = double(pk[j]) * double(d_keys[rec * h + d]) + double(pv[j]) * double(d_values[rec * h + d]) +
+                          scale * (dsk * double(pool[d]) + dsv * double(pool[h + d]));
+        float& dst = d_states[uint64_t(start + j) * h + d];
+        dst = f32(double(dst) + ds);
+        d_pool[d] = f32(double(d_pool[d]) + scale * dsk * s);
+        d_pool[h + d] = f32(double(d_pool[h + d]) + scale * dsv * s);
+      }
+    }
+  }
+}
+
+struct BackwardOut {
+  std::vector<float> policy, value_prediction, d_sel_wq, d_sel_wk, d_pool, d_field_states, d_value_wv;
+  double value_loss = 0;
+};
+
+// brainBackwardOracle (backward.ts:751-982) for a session's request.
+// selection: [Q,R] mask; targets: [Q] or null; has_target/valence.
+int backward(const ko_dims* d, const float* W, const uint32_t* token_rows, uint32_t token_rows_len, uint32_t slots,
+             const uint32_t* token_ids, const uint32_t* field_roles, const uint32_t* schema_ids,
+             const uint32_t* band_ids, const Active& a, const float* selection, const uint32_t* targets,
+             int has_valence, double valence, BackwardOut& out) {
+  const Layout L = layout_of(d);
+  const uint32_t h = d->hidden, f = d->ffn, heads = d->heads, hd = d->head_dim;
+  const uint64_t t = a.tokens.size();
+  const uint32_t r = uint32_t(a.bank.size()), q = uint32_t(a.query.size());
+  (void)slots;
+  std::vector<uint32_t> rs(t), rc(t);
+  for (uint32_t slot : a.records)
+    for (uint32_t i = a.offset[slot]; i < a.offset[slot] + a.count[slot]; i++) { rs[i] = a.offset[slot]; rc[i] = a.count[slot]; }
+
+  // forward with per-block saves (fieldEmbed as the forward)
+  std::vector<float> x(t * h);
+  const float* table = W + L.emb;
+  for (uint64_t ti = 0; ti < t; ti++) {
+    const uint32_t ft = a.tokens[ti];
+    const uint32_t slot = ft >> 3, local = ft & 7;
+    const uint32_t tid = token_ids[ft], rid = field_roles[ft];
+    if (tid >= token_rows_len || rid >= token_rows_len) return -1;
+    const uint32_t tok = token_rows[tid], role = token_rows[rid];
+    const uint32_t schema = schema_ids[slot], band = band_ids[slot], stream = a.stream[slot];
+    if (tok >= d->token_space || role >= d->field_space || schema >= d->schema_space || band >= d->band_space)
+      return -1;
+    for (uint32_t dd = 0; dd < h; dd++) {
+      double value = 0;
+      value += table[L.tb_token + uint64_t(tok) * h + dd];
+      value += table[L.tb_field + uint64_t(role) * h + dd];
+      value += table[L.tb_schema + uint64_t(schema) * h + dd];
+      value += table[L.tb_band + uint64_t(band) * h + dd];
+      value += table[L.tb_stream + uint64_t(stream) * h + dd];
+      value += table[L.tb_pos + uint64_t(local) * h + dd];
+      x[ti * h + dd] = f32(value);
+    }
+  }
+  struct Saved { std::vector<float> q, k, v, p, h1; };
+  const uint32_t kw_enc = 8;  // local windows are at most one record wide
+  std::vector<Saved> enc(d->enc_blocks);
+  std::vector<float> attn(t * h), ff(t * h);
+  for (uint32_t b = 0; b < d->enc_blocks; b++) {
+    const float* blk = W + L.enc + L.block * b;
+    Saved& sv = enc[b];
+    sv.q.resize(t * h); sv.k.resize(t * h); sv.v.resize(t * h); sv.p.assign(uint64_t(heads) * t * kw_enc, 0.f);
+    sv.h1.resize(t * f);
+    matmul(x.data(), blk, t, h, h, sv.q.data());
+    matmul(x.data(), blk + h * h, t, h, h, sv.k.data());
+    matmul(x.data(), blk + 2 * h * h, t, h, h, sv.v.data());
+    attention_with_p(sv.q.data(), sv.k.data(), sv.v.data(), nullptr, t, t, h, heads, hd, rs.data(), rc.data(), kw_enc,
+                     attn.data(), sv.p.data());
+    add_inplace(x.data(), attn.data(), t * h);
+    matmul(x.data(), blk + 3 * h * h, t, f, h, sv.h1.data());
+    relu_inplace(sv.h1.data(), t * f);
+    matmul(sv.h1.data(), blk + 3 * h * h + uint64_t(f) * h, t, h, f, ff.data());
+    add_inplace(x.data(), ff.data(), t * h);
+  }
+  std::vector<float> bk(uint64_t(r) * h), bv(uint64_t(r) * h), qk(uint64_t(q) * h), qv(uint64_t(q) * h);
+  const float* pool = W + L.pool;
+  for (uint32_t i = 0; i < r; i++)
+    pool_record(x.data(), a.offset[a.bank[i]], a.count[a.bank[i]], pool, h, bk.data() + uint64_t(i) * h,
+                bv.data() + uint64_t(i) * h);
+  for (uint32_t i = 0; i < q; i++)
+    pool_record(x.data(), a.offset[a.query[i]], a.count[a.query[i]], pool, h, qk.data() + uint64_t(i) * h,
+                qv.data() + uint64_t(i) * h);
+  std::vector<Saved> mix(d->mixer_blocks);
+  std::vector<float>& query = qv;
+  std::vector<float> mattn(uint64_t(q) * h), mff(uint64_t(q) * h), zeros_qr(uint64_t(q) * r + 1, 0.f);
+  for (uint32_t b = 0; b < d->mixer_blocks; b++) {
+    const float* blk = W + L.mixer + L.block * b;
+    Saved& sv = mix[b];
+    sv.q.resize(uint64_t(q) * h); sv.k.resize(uint64_t(r) * h); sv.v.resize(uint64_t(r) * h);
+    sv.p.assign(uint64_t(heads) * q * r + 1, 0.f); sv.h1.resize(uint64_t(q) * f);
+    matmul(query.data(), blk, q, h, h, sv.q.data());
+    matmul(bk.data(), blk + h * h, r, h, h, sv.k.data());
+    matmul(bv.data(), blk + 2 * h * h, r, h, h, sv.v.data());
+    attention_with_p(sv.q.data(), sv.k.data(), sv.v.data(), zeros_qr.data(), q, r, h, heads, hd, nullptr, nullptr, r,
+                     mattn.data(), sv.p.data());
+    add_inplace(query.data(), mattn.data(), uint64_t(q) * h);
+    matmul(query.data(), blk + 3 * h * h, q, f, h, sv.h1.data());
+    relu_inplace(sv.h1.data(), uint64_t(q) * f);
+    matmul(sv.h1.data(), blk + 3 * h * h + uint64_t(f) * h, q, h, f, mff.data());
+    add_inplace(query.data(), mff.data(), uint64_t(q) * h);
+  }
+  const std::vector<float>& qout = query;
+
+  // the intent slot: selectorOracle under the selection mask
+  std::vector<float> policy(uint64_t(q) * r + 1), gather(uint64_t(q) * h);
+  std::vector<uint32_t> index(q + 1);
+  selector(qout.data(), bk.data(), bv.data(), selection, W + L.sel_wq, W + L.sel_wk, q, r, h, nullptr, policy.data(),
+           gather.data(), index.data());
+  // offered: the mean bank value over what the grammar allows (backward.ts:834-843)
+  std::vector<float> offered(uint64_t(q) * h, 0.f);
+  std::vector<std::vector<uint32_t>> allowed(q);
+  for (uint32_t i = 0; i < q; i++) {
+    for (uint32_t j = 0; j < r; j++)
+      if (double(selection[uint64_t(i) * r + j]) > -1e29) allowed[i].push_back(j);
+    if (allowed[i].empty()) continue;
+    for (uint32_t row : allowed[i])
+      for (uint32_t dd = 0; dd < h; dd++)
+        offered[uint64_t(i) * h + dd] = f32(double(offered[uint64_t(i) * h + dd]) + double(bv[uint64_t(row) * h + dd]));
+    for (uint32_t dd = 0; dd < h; dd++)
+      offered[uint64_t(i) * h + dd] = f32(double(offered[uint64_t(i) * h + dd]) / double(allowed[i].size()));
+  }
+  // value head: decisionHeadOracle with one class over [qout | gather | offered]
+  const float* wv = W + L.value;
+  const uint32_t hin = 3 * h;
+  auto ctx = [&](uint32_t i, uint32_t dd) -> double {
+    return dd < h ? qout[uint64_t(i) * h + dd]
+                  : dd < 2 * h ? gather[uint64_t(i) * h + (dd - h)] : offered[uint64_t(i) * h + (dd - 2 * h)];
+  };
+  std::vector<float> pred(q + 1), dpred(q + 1, 0.f);
+  for (uint32_t i = 0; i < q; i++) {
+    double s = 0;
+    for (uint32_t dd = 0; dd < hin; dd++) s += ctx(i, dd) * double(wv[dd]);
+    pred[i] = f32(s);
+  }
+  double loss = 0;  // valueHeadLoss (backward.ts:49-62)
+  if (has_valence && q) {
+    for (uint32_t i = 0; i < q; i++) {
+      const double e = double(pred[i]) - valence;
+      loss += 0.5 * e * e;
+      dpred[i] = f32(e / q);
+    }
+    loss /= q;
+  }
+  // decisionHeadBackward (backward.ts:459-506) for the value head, C = 1
+  std::vector<float> dqo(uint64_t(q) * h), dig(uint64_t(q) * h), dag(uint64_t(q) * h), dwv(hin);
+  for (uint32_t i = 0; i < q; i++)
+    for (uint32_t dd = 0; dd < h; dd++) {
+      const double dl = dpred[i];
+      dqo[uint64_t(i) * h + dd] = f32(dl * double(wv[dd]));
+      dig[uint64_t(i) * h + dd] = f32(dl * double(wv[h + dd]));
+      dag[uint64_t(i) * h + dd] = f32(dl * double(wv[2 * h + dd]));
+    }
+  for (uint32_t dd = 0; dd < hin; dd++) {
+    double s = 0;
+    for (uint32_t i = 0; i < q; i++) s += double(dpred[i]) * ctx(i, dd);
+    dwv[dd] = f32(s);
+  }
+  // dValue: the offered mean's gradient shared over its rows
+  std::vector<float> dvalue(uint64_t(r) * h + 1, 0.f);
+  for (uint32_t i = 0; i < q; i++) {
+    if (allowed[i].empty()) continue;
+    for (uint32_t row : allowed[i])
+      for (uint32_t dd = 0; dd < h; dd++)
+        dvalue[uint64_t(row) * h + dd] =
+            f32(double(dvalue[uint64_t(row) * h + dd]) + double(dag[uint64_t(i) * h + dd]) / double(allowed[i].size()));
+  }
+  // selectorBackwardScores (backward.ts:293-336) for the intent slot
+  std::vector<float> sq(uint64_t(q) * h), sk(uint64_t(r) * h);
+  matmul(qout.data(), W + L.sel_wq, q, h, h, sq.data());
+  matmul(bk.data(), W + L.sel_wk, r, h, h, sk.data());
+  std::vector<float> dscore(uint64_t(q) * r + 1, 0.f), dpj(r + 1);
+  for (uint32_t i = 0; i < q; i++) {
+    const uint32_t raw = targets ? targets[i] : kInvalidU32;
+    const bool valid = raw != kInvalidU32;
+    const bool away = valid && raw >= 0x80000000u;
+    const uint32_t target = away ? raw - 0x80000000u : raw;
+    const double p_away = away && target < r ? double(policy[uint64_t(i) * r + target]) : 0.0;
+    const double sc = away ? p_away / js_max(1 - p_away, 1e-6) : 0.0;
+    double row_sum = 0;
+    for (uint32_t j = 0; j < r; j++) {
+      double s = 0;
+      for (uint32_t dd = 0; dd < h; dd++) s += double(dig[uint64_t(i) * h + dd]) * double(bv[uint64_t(j) * h + dd]);
+      dpj[j] = f32(s);
+      row_sum += double(policy[uint64_t(i) * r + j]) * s;
+    }
+    for (uint32_t j = 0; j < r; j++) {
+      const double pij = policy[uint64_t(i) * r + j];
+      const double one = j == target ? 1.0 : 0.0;
+      const double pg = !valid ? 0.0 : away ? sc * (one - pij) : pij - one;
+      dscore[uint64_t(i) * r + j] = f32(pij * (double(dpj[j]) - row_sum) + pg);
+    }
+  }
+  // selectorBackwardQkv (backward.ts:354-392), no gold filter for the intent slot
+  const double hscale = 1 / std::sqrt(double(h));
+  std::vector<float> dqp(uint64_t(q) * h), dkp(uint64_t(r) * h), dval2(uint64_t(r) * h);
+  for (uint32_t i = 0; i < q; i++)
+    for (uint32_t c = 0; c < h; c++) {
+      double acc = 0;
+      for (uint32_t j = 0; j < r; j++) acc += double(dscore[uint64_t(i) * r + j]) * double(sk[uint64_t(j) * h + c]);
+      dqp[uint64_t(i) * h + c] = f32(acc * hscale);
+    }
+  for (uint32_t j = 0; j < r; j++)
+    for (uint32_t c = 0; c < h; c++) {
+      double ak = 0, av = 0;
+      for (uint32_t i = 0; i < q; i++) {
+        ak += double(dscore[uint64_t(i) * r + j]) * double(sq[uint64_t(i) * h + c]);
+        av += double(policy[uint64_t(i) * r + j]) * double(dig[uint64_t(i) * h + c]);
+      }
+      dkp[uint64_t(j) * h + c] = f32(ak * hscale);
+      dval2[uint64_t(j) * h + c] = f32(av);
+    }
+  // the accumulators start at zero (backward.ts:890-892): f32(0 + x) = x
+  add_inplace(dvalue.data(), dval2.data(), uint64_t(r) * h);
+  std::vector<float> dquery(uint64_t(q) * h), tmp_q(uint64_t(q) * h), dbk(uint64_t(r) * h);
+  matmul_back_input(dqp.data(), W + L.sel_wq, q, h, h, tmp_q.data());
+  dquery = dqo;
+  add_inplace(dquery.data(), tmp_q.data(), uint64_t(q) * h);
+  matmul_back_input(dkp.data(), W + L.sel_wk, r, h, h, dbk.data());
+  std::vector<float> dbv = dvalue;
+  out.d_sel_wq.assign(uint64_t(h) * h, 0.f);
+  out.d_sel_wk.assign(uint64_t(h) * h, 0.f);
+  matmul_back_weight(dqp.data(), qout.data(), q, h, h, out.d_sel_wq.data());
+  matmul_back_weight(dkp.data(), bk.data(), r, h, h, out.d_sel_wk.data());
+
+  // mixer blocks in reverse (backward.ts:925-941)
+  std::vector<float> dh1r(uint64_t(q) * f), dffn(uint64_t(q) * h), dattn(uint64_t(q) * h), mdq(uint64_t(q) * h),
+      mdk(uint64_t(r) * h), mdv(uint64_t(r) * h), t1(uint64_t(q) * h), t2(uint64_t(r) * h);
+  for (int b = int(d->mixer_blocks) - 1; b >= 0; b--) {
+    const float* blk = W + L.mixer + L.block * b;
+    const Saved& sv = mix[b];
+    matmul_back_input(dquery.data(), blk + 3 * h * h + uint64_t(f) * h, q, h, f, dh1r.data());
+    for (uint64_t i = 0; i < uint64_t(q) * f; i++) dh1r[i] = sv.h1[i] > 0 ? dh1r[i] : 0.0f;
+    matmul_back_input(dh1r.data(), blk + 3 * h * h, q, f, h, dffn.data());
+    for (uint64_t i = 0; i < uint64_t(q) * h; i++) dattn[i] = f32(double(dquery[i]) + double(dffn[i]));
+    attention_backward(dattn.data(), sv.q.data(), sv.k.data(), sv.v.data(), sv.p.data(), q, r, h, heads, hd, nullptr,
+                       nullptr, r, mdq.data(), mdk.data(), mdv.data());
+    dquery = dattn;
+    matmul_back_input(mdq.data(), blk, q, h, h, t1.data());
+    add_inplace(dquery.data(), t1.data(), uint64_t(q) * h);
+    matmul_back_input(mdk.data(), blk + h * h, r, h, h, t2.data());
+    add_inplace(dbk.data(), t2.data(), uint64_t(r) * h);
+    matmul_back_input(mdv.data(), blk + 2 * h * h, r, h, h, t2.data());
+    add_inplace(dbv.data(), t2.data(), uint64_t(r) * h);
+  }
+  // pool backward: bank records, then question records (zero key gradient)
+  std::vector<float> dfs_bank(t * h, 0.f), dfs_query(t * h, 0.f), dpool_b(2 * h, 0.f), dpool_q(2 * h, 0.f);
+  std::vector<float> zero_qk(uint64_t(q) * h + 1, 0.f);
+  pool_backward(x.data(), a.bank, a, pool, dbk.data(), dbv.data(), h, dfs_bank.data(), dpool_b.data());
+  pool_backward(x.data(), a.query, a, pool, zero_qk.data(), dquery.data(), h, dfs_query.data(), dpool_q.data());
+  std::vector<float> dfs(t * h, 0.f), dpool(2 * h, 0.f);
+  add_inplace(dfs.data(), dfs_bank.data(), t * h);
+  add_inplace(dfs.data(), dfs_query.data(), t * h);
+  add_inplace(dpool.data(), dpool_b.data(), 2 * h);
+  add_inplace(dpool.data(), dpool_q.data(), 2 * h);
+  // encoder blocks in reverse (backward.ts:956-968)
+  std::vector<float> edh1(t * f), effn(t * h), eattn(t * h), edq(t * h), edk(t * h), edv(t * h), et(t * h);
+  for (int b = int(d->enc_blocks) - 1; b >= 0; b--) {
+    const float* blk = W + L.enc + L.block * b;
+    const Saved& sv = enc[b];
+    matmul_back_input(dfs.data(), blk + 3 * h * h + uint64_t(f) * h, t, h, f, edh1.data());
+    for (uint64_t i = 0; i < t * f; i++) edh1[i] = sv.h1[i] > 0 ? edh1[i] : 0.0f;
+    matmul_back_input(edh1.data(), blk + 3 * h * h, t, f, h, effn.data());
+    for (uint64_t i = 0; i < t * h; i++) eattn[i] = f32(double(dfs[i]) + double(effn[i]));
+    attention_backward(eattn.data(), sv.q.data(), sv.k.data(), sv.v.data(), sv.p.data(), t, t, h, heads, hd, rs.data(),
+                       rc.data(), kw_enc, edq.data(), edk.data(), edv.data());
+    dfs = eattn;
+    matmul_back_input(edq.data(), blk, t, h, h, et.data());
+    add_inplace(dfs.data(), et.data(), t * h);
+    matmul_back_input(edk.data(), blk + h * h, t, h, h, et.data());
+    add_inplace(dfs.data(), et.data(), t * h);
+    matmul_back_input(edv.data(), blk + 2 * h * h, t, h, h, et.data());
+    add_inplace(dfs.data(), et.data(), t * h);
+  }
+  out.policy.assign(policy.begin(), policy.begin() + uint64_t(q) * r);
+  out.value_prediction.assign(pred.begin(), pred.begin() + q);
+  out.value_loss = loss;
+  out.d_pool = dpool;
+  out.d_field_states = dfs;
+  out.d_value_wv = dwv;
+  return 0;
+}
+
 void mask_rule(uint32_t q, uint32_t r, const uint32_t* bank, const uint32_t* schema_ids, const uint32_t* band_ids,
                const uint32_t* schema_allow, const uint32_t* band_allow, float* mask) {
   for (uint32_t i = 0; i < q; i++) {
@@ -582,6 +1027,29 @@ int ko_forward_batch(const ko_dims* d, const float* weights, const uint32_t* tok
   worker();
   for (auto& th : pool) th.join();
   return failed ? -1 : 0;
+}
+
+int ko_backward(const ko_dims* d, const float* weights, const uint32_t* token_rows, uint32_t token_rows_len,
+                uint32_t slots, const uint32_t* token_ids, const uint32_t* field_roles, const uint32_t* schema_ids,
+                const uint32_t* band_ids, const uint32_t* active_record_indices, const float* selection,
+                const uint32_t* targets, int has_valence, double valence, float* policy, float* value_prediction,
+                double* value_loss, float* d_selector_wq, float* d_selector_wk, float* d_pool,
+                float* d_field_states, float* d_value_wv) {
+  Active a;
+  compile_active(slots, token_ids, band_ids, active_record_indices, a);
+  BackwardOut out;
+  const int rc = backward(d, weights, token_rows, token_rows_len, slots, token_ids, field_roles, schema_ids, band_ids,
+                          a, selection, targets, has_valence, valence, out);
+  if (rc) return rc;
+  std::memcpy(policy, out.policy.data(), out.policy.size() * 4);
+  std::memcpy(value_prediction, out.value_prediction.data(), out.value_prediction.size() * 4);
+  *value_loss = out.value_loss;
+  std::memcpy(d_selector_wq, out.d_sel_wq.data(), out.d_sel_wq.size() * 4);
+  std::memcpy(d_selector_wk, out.d_sel_wk.data(), out.d_sel_wk.size() * 4);
+  std::memcpy(d_pool, out.d_pool.data(), out.d_pool.size() * 4);
+  std::memcpy(d_field_states, out.d_field_states.data(), out.d_field_states.size() * 4);
+  std::memcpy(d_value_wv, out.d_value_wv.data(), out.d_value_wv.size() * 4);
+  return 0;
 }
 
 int ko_max_threads(void) {

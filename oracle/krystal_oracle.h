@@ -113,6 +113,20 @@ int ko_forward_batch(const ko_dims* d, const float* weights, const uint32_t* tok
 void ko_batch_offsets(uint32_t frames, const uint64_t* rec_off, const uint32_t* token_ids,
                       const uint32_t* band_ids, uint64_t* p_off, uint64_t* q_off, uint64_t* r_off, uint64_t* t_off);
 
+/* brainBackwardOracle (forward/backward.ts:751-982) as host/gradients.ts:
+ * 30-66 runs it for a session: context "available", the argument slot given
+ * nothing to aim at, no route-kind labels. selection: [Q,R] mask; targets:
+ * [Q] (0xffffffff = none, top bit = push away) or NULL; has_valence selects
+ * whether the value head has a target. Outputs are BackwardResult
+ * (host/backend.ts:220-238): policy [Q,R], value_prediction [Q], value_loss,
+ * d_selector_wq/wk [H,H], d_pool [2,H], d_field_states [T,H], d_value_wv [3H]. */
+int ko_backward(const ko_dims* d, const float* weights, const uint32_t* token_rows, uint32_t token_rows_len,
+                uint32_t slots, const uint32_t* token_ids, const uint32_t* field_roles, const uint32_t* schema_ids,
+                const uint32_t* band_ids, const uint32_t* active_record_indices, const float* selection,
+                const uint32_t* targets, int has_valence, double valence, float* policy, float* value_prediction,
+                double* value_loss, float* d_selector_wq, float* d_selector_wk, float* d_pool,
+                float* d_field_states, float* d_value_wv);
+
 int ko_max_threads(void);
 
 #ifdef __cplusplus

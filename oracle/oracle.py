@@ -59,6 +59,9 @@ def lib():
         _lib.ko_forward_batch.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, P, C.c_int, P, P, P, P, P]
         _lib.ko_batch_offsets.argtypes = [u32, P, P, P, P, P, P, P]
         _lib.ko_max_threads.restype = C.c_int
+        _lib.ko_backward.restype = C.c_int
+        _lib.ko_backward.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, C.c_int, C.c_double, P, P, P, P, P, P,
+                                     P, P]
     return _lib
 
 
@@ -208,6 +211,35 @@ def forward_batch(config, weights_page: np.ndarray, batch, rule=None, uniforms=N
     out = {"p": p, "index": index, **offs}
     if qout is not None:
         out["query_output"] = qout
+    return out
+
+
+def backward(config, weights_page: np.ndarray, frame, selection, targets=None, valence=None) -> dict:
+    """brainBackwardOracle as a session runs it (BackwardResult fields)."""
+    d = dims_of(config)
+    h = config.hidden_size
+    act = compile_active(frame.token_ids, frame.band_ids, frame.active_record_indices)
+    t, r, q = act["active_tokens"].size, act["bank_records"].size, act["query_records"].size
+    out = {"policy": np.zeros(max(1, q * r), np.float32), "value_prediction": np.zeros(max(1, q), np.float32),
+           "d_selector_wq": np.zeros(h * h, np.float32), "d_selector_wk": np.zeros(h * h, np.float32),
+           "d_pool": np.zeros(2 * h, np.float32), "d_field_states": np.zeros(max(1, t * h), np.float32),
+           "d_value_wv": np.zeros(3 * h, np.float32)}
+    loss = C.c_double()
+    rows = np.ascontiguousarray(config.token_rows, dtype=np.uint32)
+    sel = np.ascontiguousarray(selection, dtype=np.float32)
+    tg = None if targets is None else np.ascontiguousarray(targets, dtype=np.uint32)
+    rc = lib().ko_backward(C.byref(d), _p(weights_page), _p(rows), rows.size, frame.schema_ids.size,
+                           _p(frame.token_ids), _p(frame.field_roles), _p(frame.schema_ids), _p(frame.band_ids),
+                           _p(frame.active_record_indices), _p(sel), _p(tg), int(valence is not None),
+                           float(valence or 0.0), _p(out["policy"]), _p(out["value_prediction"]), C.byref(loss),
+                           _p(out["d_selector_wq"]), _p(out["d_selector_wk"]), _p(out["d_pool"]),
+                           _p(out["d_field_states"]), _p(out["d_value_wv"]))
+    if rc != 0:
+        raise ValueError("oracle: frame references a row outside its table")
+    out["policy"] = out["policy"][:q * r]
+    out["value_prediction"] = out["value_prediction"][:q]
+    out["d_field_states"] = out["d_field_states"][:t * h]
+    out.update(value_loss=loss.value, t=t, r=r, q=q, active=act)
     return out
 
 
