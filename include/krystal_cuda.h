@@ -7,10 +7,13 @@
  * backend.ts:91-181. A `@krystal/cuda` adapter binds the functions below
  * through bun:ffi and implements the same seam:
  *
- *   BrainBackendFactory (backend.ts:292-295)  -> kc_create
- *   BrainBackend.encode (backend.ts:264)      -> kc_encode
- *   BrainBackend.sync   (backend.ts:282)      -> kc_sync
- *   BrainBackend.destroy(backend.ts:283)      -> kc_destroy
+ *   BrainBackendFactory (backend.ts:177-180)  -> kc_create
+ *   BrainBackend.encode (backend.ts:149)      -> kc_encode
+ *   BrainBackend.sync   (backend.ts:167)      -> kc_sync
+ *   BrainBackend.backward (backend.ts:158)    -> kc_backward
+ *   GradientSource.backward over many frames (gradients.ts:15-24, learn.ts:
+ *     318-400)                                -> kc_backward_batch_device
+ *   BrainBackend.destroy(backend.ts:168)      -> kc_destroy
  *   selectorOracle in choose() (session.ts:149-176, forward/oracle.ts:332-382)
  *                                             -> kc_select (optional seam
  *                                                extension `select?`)
@@ -99,7 +102,7 @@ typedef struct kc_weights_view {
   const float* value_head_wv;   /* [3H] */
 } kc_weights_view;
 
-/* WeightChanges (host/backend.ts:249-259). embedding_rows are element
+/* WeightChanges (host/backend.ts:134-145). embedding_rows are element
  * offsets into the embeddings page, each hidden_size long. */
 typedef struct kc_changes {
   int32_t selector, pool, value_head, decision_head, blocks;
@@ -118,7 +121,7 @@ typedef struct kc_frame_view {
   const uint32_t* active_record_indices; /* [slots], ascending, 0xffffffff ends the list */
 } kc_frame_view;
 
-/* EncodedFrame (host/backend.ts:148-154). */
+/* EncodedFrame (host/backend.ts:33-39). */
 typedef struct kc_encoded_view {
   uint32_t q, r;
   const float* query_output; /* [Q,H] */
@@ -191,14 +194,14 @@ typedef struct kc_stage_times {
 
 uint32_t kc_abi_version(void);
 
-/* BrainBackendFactory (host/backend.ts:292-295): copy the weights to `device`
+/* BrainBackendFactory (host/backend.ts:177-180): copy the weights to `device`
  * and return a handle. */
 kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int device, kc_handle** out);
 
-/* BrainBackend.sync (host/backend.ts:282). changes == NULL means everything. */
+/* BrainBackend.sync (host/backend.ts:167). changes == NULL means everything. */
 kc_status kc_sync(kc_handle* h, const kc_weights_view* weights, const kc_changes* changes);
 
-/* BrainBackend.encode (host/backend.ts:264) for one frame. Outputs are
+/* BrainBackend.encode (host/backend.ts:149) for one frame. Outputs are
  * [Q,H], [R,H], [R,H]; *q_out / *r_out receive Q and R. q_cap / r_cap are the
  * rows the output buffers hold. A frame without a question is refused, as
  * the WebGPU runner refuses it (webgpu/src/krystal-forward.ts:216). */
@@ -240,6 +243,62 @@ kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* batch, kc_batch_ou
  * sizes). Results are library-owned device arrays. */
 kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* batch, kc_device_result* out);
 
+/* BackwardRequest (host/backend.ts:74-94) targets: a bank row, KC_NO_TARGET
+ * (NO_TARGET, :42), or a bank row | KC_AWAY_TARGET (AWAY, :58: push
+ * probability away from that row). */
+#define KC_NO_TARGET 0xffffffffu
+#define KC_AWAY_TARGET 0x80000000u
+
+/* BackwardResult (host/backend.ts:105-123) of one frame, host buffers the
+ * caller sizes from the frame: Q questions, R bank records, T non-PAD tokens
+ * of the active records (active-token order, compileActiveFrame). */
+typedef struct kc_backward_out {
+  float* policy;            /* [Q*R] */
+  float* value_prediction;  /* [Q] */
+  double value_loss;        /* written by the call */
+  float* d_selector_wq;     /* [H*H] */
+  float* d_selector_wk;     /* [H*H] */
+  float* d_pool;            /* [2*H] */
+  float* d_field_states;    /* [T*H], may be NULL */
+  float* d_value_wv;        /* [3*H] */
+  uint64_t p_capacity, q_capacity, t_capacity; /* elements of policy, value_prediction, d_field_states/H */
+  uint32_t q, r, t;         /* written by the call */
+} kc_backward_out;
+
+/* BrainBackend.backward (host/backend.ts:158) for one frame:
+ * brainBackwardOracle (forward/backward.ts:751-982) as host/gradients.ts:
+ * 30-66 requests it (context "available", open mixer mask, the argument slot
+ * aimed at nothing). selection: [Q,R] mask (-1e30 blocked, 0 open), NULL =
+ * open. targets: [Q] or NULL. has_valence = 0: no value target. Computed in
+ * the reference's exact arithmetic. */
+kc_status kc_backward(kc_handle* h, const kc_frame_view* frame, const float* selection, const uint32_t* targets,
+                      int has_valence, double valence, kc_backward_out* out);
+
+/* Library-owned device results of kc_backward_batch_device, valid until the
+ * next call on the handle. Per-frame arrays are indexed by frame. */
+typedef struct kc_backward_result {
+  const float* policy;            /* [total_p], frame f at p_off[f] */
+  const float* value_prediction;  /* [total_q] */
+  const double* value_loss;       /* [frames] */
+  const float* d_selector_wq;     /* [frames, H, H] */
+  const float* d_selector_wk;     /* [frames, H, H] */
+  const float* d_pool;            /* [frames, 2H] */
+  const float* d_field_states;    /* [total_t, H], frame f at t_off[f] */
+  const float* d_value_wv;        /* [frames, 3H] */
+  const uint64_t *p_off, *q_off, *r_off, *t_off; /* [frames+1] */
+  uint64_t total_p, total_q, total_r, total_t;
+} kc_backward_result;
+
+/* The backward of every frame of a packed batch at once (learn and teach
+ * differentiate many frames against one set of weights, host/learn.ts:
+ * 318-400). DEVICE pointers: `batch` as for kc_forward_batch_device;
+ * selection [total_p] laid out like p, or NULL (then the batch's mask rule,
+ * or open when it has none); targets [total_q] or NULL; valence [frames] with
+ * NaN = no value target, or NULL = none. Work is queued on the handle's
+ * stream (one short host wait inside, for the batch's sizes). */
+kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* batch, const float* selection,
+                                   const uint32_t* targets, const double* valence, kc_backward_result* out);
+
 /* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
  * certification margin (default 2e-5, in score units; 0 keeps it). */
 kc_status kc_set_precision(kc_handle* h, int mode, float tau);
@@ -255,7 +314,7 @@ kc_status kc_profile_read(kc_handle* h, kc_stage_times* out, int reset);
 /* Kernel launches the handle has issued since creation. */
 uint64_t kc_launch_count(kc_handle* h);
 
-/* BrainBackend.destroy (host/backend.ts:283). */
+/* BrainBackend.destroy (host/backend.ts:168). */
 void kc_destroy(kc_handle* h);
 
 /* Last error message for the handle (or the last failed kc_create if NULL). */

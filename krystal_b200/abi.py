@@ -26,12 +26,14 @@ KC_PRECISION_EXACT = 0
 KC_PRECISION_CERTIFIED = 1
 KC_PRECISION_FAST = 2
 KC_MAX_BANK = 4096
+KC_NO_TARGET = 0xFFFFFFFF
+KC_AWAY_TARGET = 0x80000000
 
 # Every function include/krystal_cuda.h declares.
 EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
            "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
            "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc",
-           "kc_set_precision")
+           "kc_set_precision", "kc_backward", "kc_backward_batch_device")
 
 
 class KrystalCudaError(RuntimeError):
@@ -98,6 +100,20 @@ class KcDeviceResult(C.Structure):
                 ("total_q", C.c_uint64), ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
 
 
+class KcBackwardOut(C.Structure):
+    _fields_ = [("policy", P), ("value_prediction", P), ("value_loss", C.c_double), ("d_selector_wq", P),
+                ("d_selector_wk", P), ("d_pool", P), ("d_field_states", P), ("d_value_wv", P),
+                ("p_capacity", C.c_uint64), ("q_capacity", C.c_uint64), ("t_capacity", C.c_uint64),
+                ("q", C.c_uint32), ("r", C.c_uint32), ("t", C.c_uint32)]
+
+
+class KcBackwardResult(C.Structure):
+    _fields_ = [("policy", P), ("value_prediction", P), ("value_loss", P), ("d_selector_wq", P),
+                ("d_selector_wk", P), ("d_pool", P), ("d_field_states", P), ("d_value_wv", P), ("p_off", P),
+                ("q_off", P), ("r_off", P), ("t_off", P), ("total_p", C.c_uint64), ("total_q", C.c_uint64),
+                ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
+
+
 class KcStageTimes(C.Structure):
     _fields_ = [(n, C.c_double) for n in ("pack_ms", "embed_ms", "enc_gemm_ms", "enc_attn_ms", "pool_ms",
                                           "mixer_ms", "selector_ms", "total_ms")] + [
@@ -134,6 +150,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
     lib.kc_select_noalloc.argtypes = [P, C.c_uint32, C.c_uint32, P, P, P, P, P, P, P]
     lib.kc_set_precision.argtypes = [P, C.c_int, C.c_float]
+    lib.kc_backward.argtypes = [P, C.POINTER(KcFrameView), P, P, i, C.c_double, C.POINTER(KcBackwardOut)]
+    lib.kc_backward_batch_device.argtypes = [P, C.POINTER(KcBatchView), P, P, P, C.POINTER(KcBackwardResult)]
     lib.kc_set_stream.argtypes = [P, P]
     lib.kc_get_stream.argtypes = [P]
     lib.kc_get_stream.restype = P
@@ -148,7 +166,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_last_error.restype = C.c_char_p
     for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
-                 "kc_set_precision"):
+                 "kc_set_precision", "kc_backward", "kc_backward_batch_device"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

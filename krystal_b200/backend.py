@@ -1,16 +1,20 @@
 """The CUDA device backend: ``BrainBackend`` over the C ABI.
 
 Mirrors the seam of packages/krystal/src/host/backend.ts (``EncodedFrame``
-:148-154, ``WeightChanges`` :249-259, ``BrainBackend`` :261-284,
-``BrainBackendFactory`` :292-295) and the WebGPU adapter that implements it
+:33-39, ``BackwardRequest`` :74-94, ``BackwardResult`` :105-123,
+``WeightChanges`` :134-145, ``BrainBackend`` :146-169, ``BrainBackendFactory``
+:177-180) and the WebGPU adapter that implements it
 (packages/webgpu/src/backend.ts:91-181): ``cuda_backend(device)`` returns a
 factory that the session calls with its config and the weights it owns; the
 backend keeps a device copy and is told of changes through ``sync``.
 
+``backward`` is the seam's optional ``backward?`` (:158): the gradients of one
+frame, computed on the device in the reference's arithmetic.
+
 Beyond the reference seam it offers ``select`` (the selector on the device,
-the optional ``select?`` extension ``choose()`` uses when present) and
+the optional ``select?`` extension ``choose()`` uses when present),
 ``forward_batch`` (a packed ragged batch of frames, pack → encode → select in
-one call).
+one call) and ``backward_batch_device`` (the backward of a whole batch).
 """
 from __future__ import annotations
 
@@ -27,7 +31,7 @@ from .model import BrainForwardConfig, BrainForwardWeights
 
 @dataclass
 class EncodedFrame:
-    """[Q,H] mixed query output and the [R,H] pooled bank (backend.ts:148-154)."""
+    """[Q,H] mixed query output and the [R,H] pooled bank (backend.ts:33-39)."""
 
     query_output: np.ndarray
     bank_keys: np.ndarray
@@ -44,7 +48,7 @@ class EncodedFrame:
 
 @dataclass
 class WeightChanges:
-    """Which arrays an update wrote (backend.ts:249-259); all None/False = nothing."""
+    """Which arrays an update wrote (backend.ts:134-145); all None/False = nothing."""
 
     selector: bool = False
     pool: bool = False
@@ -61,6 +65,20 @@ class Selection:
     p: np.ndarray  # [Q*R]
     index: np.ndarray  # [Q] u32, KC_NO_SELECTION when a row is all blocked
     gather: np.ndarray | None  # [Q*H]
+
+
+@dataclass
+class BackwardResult:
+    """BackwardResult (backend.ts:105-123): the policy the update differentiates,
+    the critic's predictions and loss, and the gradients the host may apply."""
+    policy: np.ndarray            # [Q*R]
+    value_prediction: np.ndarray  # [Q]
+    value_loss: float
+    d_selector_wq: np.ndarray     # [H*H]
+    d_selector_wk: np.ndarray     # [H*H]
+    d_pool: np.ndarray            # [2H]
+    d_field_states: np.ndarray    # [T*H], active-token order
+    d_value_wv: np.ndarray        # [3H]
 
 
 @dataclass
@@ -157,6 +175,56 @@ class CudaBrainBackend:
         if getattr(self, "_h", None):
             self._lib.kc_destroy(self._h)
             self._h = None
+
+    def backward(self, frame: HostFrame, selection=None, targets=None,
+                 valence_target: float | None = None) -> BackwardResult:
+        """BrainBackend.backward (backend.ts:158): one frame differentiated on the
+        device. selection: [Q,R] mask (None = open); targets: [Q] bank rows,
+        KC_NO_TARGET, or row | KC_AWAY_TARGET (None = none); valence_target:
+        the value head's target (None = none)."""
+        g = frame.gpu
+        tok, role, sch, band, act = (_u32(g.token_ids), _u32(g.field_roles), _u32(g.schema_ids), _u32(g.band_ids),
+                                     _u32(g.active_record_indices))
+        fv = abi.KcFrameView(sch.size, tok.ctypes.data, role.ctypes.data, sch.ctypes.data, band.ctypes.data,
+                             act.ctypes.data)
+        q, r = frame.active.query_records.size, frame.active.bank_records.size
+        t = frame.active.active_tokens.size
+        h = self.config.hidden_size
+        sel = _f32(selection) if selection is not None else None
+        if sel is not None and sel.size != q * r:
+            raise ValueError(f"the selection mask must be [{q}, {r}]")
+        tg = _u32(targets) if targets is not None else None
+        if tg is not None and tg.size != q:
+            raise ValueError(f"targets must have one entry per question ({q})")
+        res = BackwardResult(np.empty(max(1, q * r), np.float32), np.empty(max(1, q), np.float32), 0.0,
+                             np.empty(h * h, np.float32), np.empty(h * h, np.float32), np.empty(2 * h, np.float32),
+                             np.empty(max(1, t) * h, np.float32), np.empty(3 * h, np.float32))
+        out = abi.KcBackwardOut(res.policy.ctypes.data, res.value_prediction.ctypes.data, 0.0,
+                                res.d_selector_wq.ctypes.data, res.d_selector_wk.ctypes.data, res.d_pool.ctypes.data,
+                                res.d_field_states.ctypes.data, res.d_value_wv.ctypes.data, res.policy.size,
+                                res.value_prediction.size, max(1, t), 0, 0, 0)
+        abi.check(self._lib.kc_backward(self._h, C.byref(fv), abi.ptr(sel), abi.ptr(tg),
+                                        int(valence_target is not None), float(valence_target or 0.0),
+                                        C.byref(out)), self._h)
+        res.policy = res.policy[:out.q * out.r]
+        res.value_prediction = res.value_prediction[:out.q]
+        res.d_field_states = res.d_field_states[:out.t * h]
+        res.value_loss = out.value_loss
+        return res
+
+    def backward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,
+                              schema_ids: int, band_ids: int, selection: int | None = None,
+                              targets: int | None = None, valence: int | None = None,
+                              schema_allow: int | None = None,
+                              band_allow: int | None = None) -> abi.KcBackwardResult:
+        """The backward of a device-resident batch (raw device pointers);
+        results stay on the device (library-owned, valid until the next call)."""
+        bv = abi.KcBatchView(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow,
+                             band_allow, None)
+        res = abi.KcBackwardResult()
+        abi.check(self._lib.kc_backward_batch_device(self._h, C.byref(bv), selection, targets, valence,
+                                                     C.byref(res)), self._h)
+        return res
 
     # --- seam extension: the selector on the device -------------------------
     def select(self, encoded: EncodedFrame, mask: np.ndarray | None = None, rule: MaskRule | None = None,

@@ -1,0 +1,598 @@
+// backward.cuh — brainBackwardOracle (packages/krystal/src/forward/backward.ts:
+// 751-982) as a session runs it (host/gradients.ts:30-66): context
+// "available", the argument slot aimed at nothing (it contributes exactly
+// zero), no route-kind labels, an open mixer mask.
+//
+// Same arithmetic contract as exact.cuh: one f64 accumulator per dot product
+// walked in the reference's index order, f32 rounding wherever the reference
+// stores into a Float32Array, and no contraction of a*b+c (the file is
+// compiled with --fmad=false). fma() appears only where the product is of
+// two f32 values, which is exact in f64, so fma equals multiply-then-add.
+// Every kernel works on the packed batch layout of pack.cuh: compact tokens
+// (t_off), questions (q_off), bank rows (r_off), and per-frame [Q_f, R_f]
+// blocks at p_off.
+//
+// The backward's own dense products (gradients through Wq/Wk/Wv/W1/W2 and the
+// selector projections) run on k_dgemm_exact with transposed weight copies;
+// this file holds everything else.
+#pragma once
+#include "common.cuh"
+#include "exact.cuh"
+
+namespace kc {
+
+// dst[k, n] = src[n, k]: the transposed copy a back-input product multiplies by
+// (matmulBackInput, backward.ts:548-557, is dY · W = dY · (Wᵀ)ᵀ).
+__global__ void __launch_bounds__(256) k_transpose(const float* __restrict__ src, float* __restrict__ dst, int n,
+                                                  int k) {
+  __shared__ float tile[32][33];
+  const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = n0 + i, c = k0 + threadIdx.x;
+    if (r < n && c < k) tile[i][threadIdx.x] = src[int64_t(r) * k + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = k0 + i, c = n0 + threadIdx.x;
+    if (r < k && c < n) dst[int64_t(r) * n + c] = tile[threadIdx.x][i];
+  }
+}
+
+// Shared batch geometry of the per-question / per-bank-row kernels.
+struct BatchGeo {
+  const uint32_t* query_frame;  // [Q]
+  const uint32_t* bank_frame;   // [R]
+  const uint64_t* q_off;        // [F+1]
+  const uint64_t* r_off;        // [F+1]
+  const uint64_t* p_off;        // [F+1]
+};
+
+// selectionMask (host/learn.ts:215-232) from the device rule: -1e30 where the
+// rule forbids, 0 where it admits, and a row that admits nothing reopened to
+// zeros (:229). One CTA per question.
+struct RuleMaskArgs {
+  BatchGeo g;
+  const uint32_t* schema_allow;  // [Q*8]
+  const uint32_t* band_allow;    // [Q]
+  const uint32_t* bank_rec;      // bank row -> record
+  const uint32_t* schema_ids;    // [records]
+  const uint32_t* band_ids;      // [records]
+  float* mask;                   // [P]
+};
+
+__global__ void __launch_bounds__(256) k_rule_mask(RuleMaskArgs a) {
+  __shared__ uint32_t red[8];
+  const uint32_t qi = blockIdx.x, f = a.g.query_frame[qi];
+  const uint64_t rb = a.g.r_off[f];
+  const int R = int(a.g.r_off[f + 1] - rb);
+  float* row = a.mask + a.g.p_off[f] + (qi - a.g.q_off[f]) * uint64_t(R);
+  const uint32_t* sa = a.schema_allow + uint64_t(qi) * 8;
+  const uint32_t ba = a.band_allow[qi];
+  auto admits = [&](int j) {
+    const uint32_t rec = a.bank_rec[rb + j];
+    const uint32_t s = a.schema_ids[rec], b = a.band_ids[rec];
+    return s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u);
+  };
+  uint32_t n = 0;
+  for (int j = threadIdx.x; j < R; j += 256) n += admits(j) ? 1u : 0u;
+  const bool reopen = block_sum_u32<256>(n, red) == 0;
+  for (int j = threadIdx.x; j < R; j += 256) row[j] = reopen || admits(j) ? 0.0f : -1e30f;
+}
+
+// The critic's third input block, the mean bank value over what the selection
+// allows (backward.ts:834-843, context "available"): a running f32 sum over
+// the allowed rows in order, then one f64 division. Then the value head's
+// prediction (decisionHeadOracle with one class, :845-852) over
+// [queryOutput | gather | offered]. One CTA of 128 threads per question.
+struct OfferedArgs {
+  BatchGeo g;
+  const float* mask;         // [P] the selection
+  const float* bank_values;  // [R,128]
+  const float* qout;         // [Q,128]
+  const float* gather;       // [Q,128]
+  const float* wv;           // value head [384]
+  float* offered;            // [Q,128]
+  uint32_t* n_allowed;       // [Q]
+  float* pred;               // [Q]
+};
+
+__global__ void __launch_bounds__(128) k_offered_pred(OfferedArgs a) {
+  __shared__ float ctx[3 * KC_H];
+  const uint32_t qi = blockIdx.x, f = a.g.query_frame[qi];
+  const uint64_t rb = a.g.r_off[f];
+  const int R = int(a.g.r_off[f + 1] - rb);
+  const float* mrow = a.mask + a.g.p_off[f] + (qi - a.g.q_off[f]) * uint64_t(R);
+  const int d = threadIdx.x;
+  float o = 0.0f;
+  uint32_t n = 0;
+  for (int j = 0; j < R; j++) {
+    if (double(mrow[j]) > -1e29) {
+      o = f32(double(o) + double(a.bank_values[(rb + j) * KC_H + d]));
+      n++;
+    }
+  }
+  if (n) o = f32(double(o) / double(n));
+  a.offered[uint64_t(qi) * KC_H + d] = o;
+  if (d == 0) a.n_allowed[qi] = n;
+  ctx[d] = a.qout[uint64_t(qi) * KC_H + d];
+  ctx[KC_H + d] = a.gather[uint64_t(qi) * KC_H + d];
+  ctx[2 * KC_H + d] = o;
+  __syncthreads();
+  if (d == 0) {
+    double s = 0.0;
+    for (int k = 0; k < 3 * KC_H; k++) s = fma(double(ctx[k]), double(a.wv[k]), s);
+    a.pred[qi] = f32(s);
+  }
+}
+
+// valueHeadLoss (backward.ts:49-62) per frame: the mean of 0.5·e² over the
+// frame's questions and dPred = e / Q stored f32; no target (NaN valence) =
+// no loss and no gradient.
+__global__ void k_value_loss(const float* pred, const double* valence, const uint64_t* q_off, uint32_t frames,
+                             float* dpred, double* loss) {
+  const uint32_t f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= frames) return;
+  const uint64_t q0 = q_off[f];
+  const uint32_t Q = uint32_t(q_off[f + 1] - q0);
+  const double v = valence ? valence[f] : __longlong_as_double(0x7ff8000000000000ll);
+  double l = 0.0;
+  if (v == v && Q) {
+    for (uint32_t i = 0; i < Q; i++) {
+      const double e = double(pred[q0 + i]) - v;
+      l += 0.5 * e * e;
+      dpred[q0 + i] = f32(e / Q);
+    }
+    l /= Q;
+  } else {
+    for (uint32_t i = 0; i < Q; i++) dpred[q0 + i] = 0.0f;
+  }
+  loss[f] = l;
+}
+
+// dValueWv of decisionHeadBackward (backward.ts:459-506, C = 1): per frame,
+// one f64 accumulator per input column over the frame's questions in order.
+__global__ void __launch_bounds__(384) k_value_wv(const float* qout, const float* gather, const float* offered,
+                                                 const float* dpred, const uint64_t* q_off, float* dwv) {
+  const uint32_t f = blockIdx.x;
+  const int dd = threadIdx.x;
+  const uint64_t q0 = q_off[f], Q = q_off[f + 1] - q0;
+  const float* src = dd < KC_H ? qout + dd : dd < 2 * KC_H ? gather + (dd - KC_H) : offered + (dd - 2 * KC_H);
+  double s = 0.0;
+  for (uint64_t i = 0; i < Q; i++) s = fma(double(dpred[q0 + i]), double(src[(q0 + i) * KC_H]), s);
+  dwv[uint64_t(f) * 3 * KC_H + dd] = f32(s);
+}
+
+// decisionHeadBackward's input gradients (dQueryOut, dIntentGather,
+// dAvailable = dPred·Wv blocks) and selectorBackwardScores (backward.ts:
+// 293-336) for the intent slot: dP[j] = f32(dGather·V[j]); the row sum
+// Σ p·(unrounded dot); dScore = f32(p·(dP − rowSum) + policy term), where the
+// policy term is p − onehot for a target, sc·(onehot − p) with
+// sc = pAway / max(1 − pAway, 1e-6) for an AWAY target (bit 31), 0 without.
+// One CTA per question; dynamic shared memory 8 B × max_r.
+struct SelBackArgs {
+  BatchGeo g;
+  const float* p;            // [P] policy
+  const float* bank_values;  // [R,128]
+  const float* wv;           // [384]
+  const float* dpred;        // [Q]
+  const uint32_t* targets;   // [Q] or null
+  float* dquery;             // [Q,128] <- dQueryOut
+  float* dig;                // [Q,128]
+  float* dag;                // [Q,128]
+  float* dscore;             // [P]
+};
+
+__global__ void __launch_bounds__(256) k_sel_back_scores(SelBackArgs a) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  double* s64 = reinterpret_cast<double*>(dyn);
+  __shared__ double digs[KC_H];
+  __shared__ double row_sum_s;
+  const uint32_t qi = blockIdx.x, f = a.g.query_frame[qi];
+  const uint64_t rb = a.g.r_off[f];
+  const int R = int(a.g.r_off[f + 1] - rb);
+  const uint64_t po = a.g.p_off[f] + (qi - a.g.q_off[f]) * uint64_t(R);
+  const float* prow = a.p + po;
+  const int tid = threadIdx.x;
+  if (tid < KC_H) {
+    const double dl = a.dpred[qi];
+    const uint64_t o = uint64_t(qi) * KC_H + tid;
+    const float vig = f32(dl * double(a.wv[KC_H + tid]));
+    a.dquery[o] = f32(dl * double(a.wv[tid]));
+    a.dig[o] = vig;
+    a.dag[o] = f32(dl * double(a.wv[2 * KC_H + tid]));
+    digs[tid] = vig;
+  }
+  __syncthreads();
+  for (int j = tid; j < R; j += 256) {
+    const float* vr = a.bank_values + (rb + j) * KC_H;
+    double s = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < KC_H; d++) s = fma(digs[d], double(vr[d]), s);
+    s64[j] = s;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double rs = 0.0;
+    for (int j = 0; j < R; j++) rs = rs + double(prow[j]) * s64[j];
+    row_sum_s = rs;
+  }
+  __syncthreads();
+  const double row_sum = row_sum_s;
+  const uint32_t raw = a.targets ? a.targets[qi] : KC_INVALID;
+  const bool valid = raw != KC_INVALID;
+  const bool away = valid && raw >= 0x80000000u;
+  const uint32_t target = away ? raw - 0x80000000u : raw;
+  const double p_away = away && target < uint32_t(R) ? double(prow[target]) : 0.0;
+  const double sc = away ? p_away / js_max(1.0 - p_away, 1e-6) : 0.0;
+  for (int j = tid; j < R; j += 256) {
+    const double pij = prow[j];
+    const double one = uint32_t(j) == target ? 1.0 : 0.0;
+    const double pg = !valid ? 0.0 : away ? sc * (one - pij) : pij - one;
+    a.dscore[po + j] = f32(pij * (double(f32(s64[j])) - row_sum) + pg);
+  }
+}
+
+// selectorBackwardQkv (backward.ts:354-392), question side:
+// dQProj[i,c] = f32(Σ_j dScore[i,j]·kProj[j,c] · 1/√H). One CTA per question.
+__global__ void __launch_bounds__(128) k_sel_back_dq(BatchGeo g, const float* dscore, const float* sk, double hscale,
+                                                    float* dqp) {
+  const uint32_t qi = blockIdx.x, f = g.query_frame[qi];
+  const uint64_t rb = g.r_off[f];
+  const int R = int(g.r_off[f + 1] - rb);
+  const float* drow = dscore + g.p_off[f] + (qi - g.q_off[f]) * uint64_t(R);
+  const int c = threadIdx.x;
+  double acc = 0.0;
+  for (int j = 0; j < R; j++) acc = fma(double(drow[j]), double(sk[(rb + j) * KC_H + c]), acc);
+  dqp[uint64_t(qi) * KC_H + c] = f32(acc * hscale);
+}
+
+// selectorBackwardQkv, bank side, with the bank-value gradient assembled:
+// dKProj[j,c] = f32(Σ_i dScore[i,j]·qProj[i,c] · 1/√H); the gather's
+// dV2[j,c] = f32(Σ_i p[i,j]·dGather[i,c]); the offered mean's share
+// dV1[j,c] = running f32 sum over questions allowing j of dAvailable/count;
+// dBankValues = f32(dV1 + dV2) (backward.ts:890-898). One CTA per bank row.
+struct SelBackKArgs {
+  BatchGeo g;
+  const float* dscore;      // [P]
+  const float* p;           // [P]
+  const float* mask;        // [P]
+  const float* sq;          // [Q,128]
+  const float* dig;         // [Q,128]
+  const float* dag;         // [Q,128]
+  const uint32_t* n_allowed;// [Q]
+  double hscale;
+  float* dkp;               // [R,128]
+  float* dbv;               // [R,128]
+};
+
+__global__ void __launch_bounds__(128) k_sel_back_dk(SelBackKArgs a) {
+  const uint32_t jg = blockIdx.x, f = a.g.bank_frame[jg];
+  const uint64_t rb = a.g.r_off[f];
+  const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
+  const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0, pb = a.g.p_off[f];
+  const int c = threadIdx.x;
+  float dv1 = 0.0f;
+  double ak = 0.0, av = 0.0;
+  for (uint64_t i = 0; i < Q; i++) {
+    const uint64_t pi = pb + i * R + j;
+    const uint64_t qr = (q0 + i) * KC_H + c;
+    if (double(a.mask[pi]) > -1e29) dv1 = f32(double(dv1) + double(a.dag[qr]) / double(a.n_allowed[q0 + i]));
+    ak = fma(double(a.dscore[pi]), double(a.sq[qr]), ak);
+    av = fma(double(a.p[pi]), double(a.dig[qr]), av);
+  }
+  a.dkp[uint64_t(jg) * KC_H + c] = f32(ak * a.hscale);
+  a.dbv[uint64_t(jg) * KC_H + c] = f32(double(dv1) + double(f32(av)));
+}
+
+// matmulBackWeight (backward.ts:560-569) per frame: dW_f[n,k] =
+// f32(Σ_l dY[l,n]·X[l,k]) over the frame's rows l in order (row_off gives
+// each frame's rows). Grid (frames, H/8); thread (k, 4 consecutive n).
+__global__ void __launch_bounds__(256) k_weight_grad(const float* __restrict__ dY, const float* __restrict__ X,
+                                                    const uint64_t* row_off, float* dW) {
+  const uint32_t f = blockIdx.x;
+  const int k = threadIdx.x & 127, n0 = blockIdx.y * 8 + (threadIdx.x >> 7) * 4;
+  const uint64_t l0 = row_off[f], L = row_off[f + 1] - l0;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (uint64_t l = 0; l < L; l++) {
+    const double x = X[(l0 + l) * KC_H + k];
+    const float* dy = dY + (l0 + l) * KC_H + n0;
+#pragma unroll
+    for (int m = 0; m < 4; m++) acc[m] = fma(double(dy[m]), x, acc[m]);
+  }
+  float* out = dW + uint64_t(f) * KC_H * KC_H;
+#pragma unroll
+  for (int m = 0; m < 4; m++) out[uint64_t(n0 + m) * KC_H + k] = f32(acc[m]);
+}
+
+// attentionBackwardScores + attentionBackwardQkv (backward.ts:79-166) for the
+// mixer's dense cross-attention, question side. Per head: dP[j] =
+// f32(dOut·V[j]), rowSum = Σ_j p·(unrounded dot), dS = f32(p·(dP − rowSum)),
+// kept in ds [4][P]; dQ[i,c] = f32(Σ_j dS·K[j,c] · 1/√headDim).
+// One CTA per question; dynamic shared memory 12 B × 4 × max_r.
+struct CrossBackArgs {
+  BatchGeo g;
+  const float* dout;  // [Q,128]
+  const float* mq;    // [Q,128]
+  const float* mk;    // [R,128]
+  const float* mv;    // [R,128]
+  const float* p;     // [4][P]
+  uint64_t total_p;
+  uint32_t max_r;
+  double scale;
+  float* ds;          // [4][P]
+  float* dq;          // [Q,128]
+  float* dk;          // [R,128]
+  float* dv;          // [R,128]
+};
+
+__global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  double* s64 = reinterpret_cast<double*>(dyn);                     // [4][max_r]
+  float* dss = reinterpret_cast<float*>(s64 + 4 * size_t(a.max_r));  // [4][max_r]
+  __shared__ float dos[KC_H];
+  __shared__ double rsum[KC_HEADS];
+  const uint32_t qi = blockIdx.x, f = a.g.query_frame[qi];
+  const uint64_t rb = a.g.r_off[f];
+  const int R = int(a.g.r_off[f + 1] - rb);
+  const uint64_t po = a.g.p_off[f] + (qi - a.g.q_off[f]) * uint64_t(R);
+  const int tid = threadIdx.x;
+  dos[tid] = a.dout[uint64_t(qi) * KC_H + tid];
+  __syncthreads();
+  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
+    const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
+    const float* vr = a.mv + (rb + j) * KC_H + hb;
+    double s = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(dos[hb + d]), double(vr[d]), s);
+    s64[head * size_t(a.max_r) + j] = s;
+  }
+  __syncthreads();
+  if (tid < KC_HEADS) {
+    const float* prow = a.p + uint64_t(tid) * a.total_p + po;
+    const double* sr = s64 + tid * size_t(a.max_r);
+    double rs = 0.0;
+    for (int j = 0; j < R; j++) rs = rs + double(prow[j]) * sr[j];
+    rsum[tid] = rs;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
+    const int head = idx / R, j = idx - head * R;
+    const uint64_t pi = uint64_t(head) * a.total_p + po + j;
+    const double pij = a.p[pi];
+    const float v = f32(pij * (double(f32(s64[head * size_t(a.max_r) + j])) - rsum[head]));
+    dss[head * size_t(a.max_r) + j] = v;
+    a.ds[pi] = v;
+  }
+  __syncthreads();
+  const int head = tid >> 5;
+  const float* dr = dss + head * size_t(a.max_r);
+  double acc = 0.0;
+  for (int j = 0; j < R; j++) acc = fma(double(dr[j]), double(a.mk[(rb + j) * KC_H + tid]), acc);
+  a.dq[uint64_t(qi) * KC_H + tid] = f32(acc * a.scale);
+}
+
+// The key/value side: dK[j,c] = f32(Σ_i dS·Q[i,c] · 1/√headDim),
+// dV[j,c] = f32(Σ_i p·dOut[i,c]), i over the frame's questions in order.
+// One CTA per bank row; warp w is head w.
+__global__ void __launch_bounds__(128) k_cross_attn_back_kv(CrossBackArgs a) {
+  const uint32_t jg = blockIdx.x, f = a.g.bank_frame[jg];
+  const uint64_t rb = a.g.r_off[f];
+  const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
+  const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0;
+  const int col = threadIdx.x, head = col >> 5;
+  const uint64_t base = uint64_t(head) * a.total_p + a.g.p_off[f] + j;
+  double ak = 0.0, av = 0.0;
+  for (uint64_t i = 0; i < Q; i++) {
+    const uint64_t pi = base + i * R;
+    const uint64_t qr = (q0 + i) * KC_H + col;
+    ak = fma(double(a.ds[pi]), double(a.mq[qr]), ak);
+    av = fma(double(a.p[pi]), double(a.dout[qr]), av);
+  }
+  a.dk[uint64_t(jg) * KC_H + col] = f32(ak * a.scale);
+  a.dv[uint64_t(jg) * KC_H + col] = f32(av);
+}
+
+// poolBackward (backward.ts:184-262) for every record: the two pooling
+// softmaxes are recomputed as the forward computed them; dP = f32(dOut·s_j),
+// dS = p·(dP − Σ p·dP), the token-state gradient
+// f32(pk·dKey + pv·dValue + 1/√H·(dSk·pool_k + dSv·pool_v)), and dSk/dSv kept
+// per token for the pool-weight gradient. Bank records take the bank-key and
+// bank-value gradients; questions take a zero key gradient and the query
+// gradient (backward.ts:944-950). One warp per record.
+struct PoolBackArgs {
+  const float* x;            // [T,128] the encoder's output
+  const float* pool;         // [2,128]
+  const uint32_t* rec_start;
+  const uint2* rec_meta;
+  const uint32_t* rec_row;   // bank row, or question row | 0x80000000
+  uint64_t records;
+  double scale;              // 1/sqrt(H)
+  const float* dbk;          // [R,128]
+  const float* dbv;          // [R,128]
+  const float* dquery;       // [Q,128]
+  float* dfs;                // [T,128]
+  double* tok_ds;            // [T][2]
+};
+
+__global__ void __launch_bounds__(256) k_pool_back(PoolBackArgs a) {
+  __shared__ float xs[8][KC_RW][KC_H];  // 32 KB
+  __shared__ float ps[2][KC_H];
+  __shared__ float pr[8][2][KC_RW];     // pooling softmax rows (pk, pv)
+  __shared__ float dp[8][2][KC_RW];     // dPk, dPv
+  __shared__ double dsm[8][2][KC_RW];   // dSk, dSv
+  __shared__ double rsm[8][2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 2 * KC_H; i += 256) (&ps[0][0])[i] = a.pool[i];
+  __syncthreads();
+  const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  if (cnt == 0) return;
+  const uint32_t row = a.rec_row[g];
+  const bool isq = row & 0x80000000u;
+  const uint32_t r = row & 0x7fffffffu;
+  const float* dkey = isq ? nullptr : a.dbk + uint64_t(r) * KC_H;
+  const float* dval = isq ? a.dquery + uint64_t(r) * KC_H : a.dbv + uint64_t(r) * KC_H;
+  const float4* src = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H);
+  float4* dst = reinterpret_cast<float4*>(&xs[warp][0][0]);
+  for (int i = lane; i < cnt * 32; i += 32) dst[i] = src[i];
+  __syncwarp();
+  const int j = lane & 7, which = lane >> 3;  // lanes 0..15 work
+  if (lane < 16 && j < cnt) {
+    double s = 0.0;
+    for (int d = 0; d < KC_H; d++) s = fma(double(ps[which][d]), double(xs[warp][j][d]), s);
+    pr[warp][which][j] = f32(s * a.scale);
+  }
+  __syncwarp();
+  if (lane == 0 || lane == 8) softmax_small(pr[warp][lane >> 3], cnt);
+  __syncwarp();
+  if (lane < 16 && j < cnt) {
+    const float* gr = which ? dval : dkey;
+    double s = 0.0;
+    for (int d = 0; d < KC_H; d++) s = fma(gr ? double(gr[d]) : 0.0, double(xs[warp][j][d]), s);
+    dp[warp][which][j] = f32(s);
+  }
+  __syncwarp();
+  if (lane == 0 || lane == 8) {
+    const int w = lane >> 3;
+    double rs = 0.0;
+    for (int i = 0; i < cnt; i++) rs = fma(double(pr[warp][w][i]), double(dp[warp][w][i]), rs);
+    rsm[warp][w] = rs;
+  }
+  __syncwarp();
+  if (lane < 16 && j < cnt) {
+    const double v = double(pr[warp][which][j]) * (double(dp[warp][which][j]) - rsm[warp][which]);
+    dsm[warp][which][j] = v;
+    a.tok_ds[(uint64_t(start) + j) * 2 + which] = v;
+  }
+  __syncwarp();
+  for (int d = lane; d < KC_H; d += 32) {
+    const double gk = dkey ? double(dkey[d]) : 0.0, gv = double(dval[d]);
+    const double pk_d = ps[0][d], pv_d = ps[1][d];
+    for (int t = 0; t < cnt; t++) {
+      const double ds = double(pr[warp][0][t]) * gk + double(pr[warp][1][t]) * gv +
+                        a.scale * (dsm[warp][0][t] * pk_d + dsm[warp][1][t] * pv_d);
+      a.dfs[(uint64_t(start) + t) * KC_H + d] = f32(0.0 + ds);
+    }
+  }
+}
+
+// The pool-weight gradient per frame: for column c of [2,H], a running f32
+// sum of 1/√H·dS·s over the frame's bank records, then (separately) its
+// questions, each in order, token by token; dPool = f32(f32(0 + bank) +
+// questions) (backward.ts:944-953). One CTA of 256 threads per frame.
+struct PoolGradArgs {
+  const float* x;
+  const double* tok_ds;
+  const uint32_t* rec_start;
+  const uint2* rec_meta;
+  const uint32_t* bank_rec;
+  const uint32_t* query_rec;
+  const uint64_t* r_off;
+  const uint64_t* q_off;
+  double scale;
+  float* dpool;  // [F, 2H]
+};
+
+__global__ void __launch_bounds__(256) k_pool_grad(PoolGradArgs a) {
+  const uint32_t f = blockIdx.x;
+  const int c = threadIdx.x, which = c >> 7, d = c & 127;
+  auto walk = [&](const uint32_t* list, uint64_t b, uint64_t e) {
+    float acc = 0.0f;
+    for (uint64_t r = b; r < e; r++) {
+      const uint32_t g = list[r];
+      const uint32_t start = a.rec_start[g];
+      const int cnt = int(a.rec_meta[g].y & 15u);
+      for (int t = 0; t < cnt; t++) {
+        const uint64_t tok = uint64_t(start) + t;
+        acc = f32(double(acc) + a.scale * a.tok_ds[tok * 2 + which] * double(a.x[tok * KC_H + d]));
+      }
+    }
+    return acc;
+  };
+  const float b = walk(a.bank_rec, a.r_off[f], a.r_off[f + 1]);
+  const float q = walk(a.query_rec, a.q_off[f], a.q_off[f + 1]);
+  a.dpool[uint64_t(f) * 2 * KC_H + c] = f32(double(f32(0.0 + double(b))) + double(q));
+}
+
+// attentionBackwardScores + attentionBackwardQkv for the encoder's record-
+// local attention (backward.ts:79-166, local windows): per record, head and
+// token, dS over the record's keys from the saved p; then dQ, dK, dV of every
+// token of the record, each one accumulator over the record in order.
+// One warp per record; outputs dq | dk | dv as [T,384].
+struct LocalBackArgs {
+  const float* qkv;          // saved [T,384]
+  const float* p;            // saved [T][4][8]
+  const float* dout;         // [T,128]
+  const uint32_t* rec_start;
+  const uint2* rec_meta;
+  uint64_t records;
+  double scale;              // 1/sqrt(headDim)
+  float* dqkv;               // [T,384]
+};
+
+constexpr int kLocalBackWarps = 4;
+constexpr int kLocalBackWarpFloats = KC_RW * 3 * KC_H + KC_RW * KC_H + 2 * KC_HEADS * KC_RW * KC_RW;
+constexpr size_t kLocalBackSmem = size_t(kLocalBackWarps) * kLocalBackWarpFloats * 4;
+
+__global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
+  extern __shared__ __align__(16) float lsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = uint64_t(blockIdx.x) * kLocalBackWarps + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  if (cnt == 0) return;
+  float* base = lsm + size_t(warp) * kLocalBackWarpFloats;
+  float(*rec)[3 * KC_H] = reinterpret_cast<float(*)[3 * KC_H]>(base);                         // q|k|v
+  float(*dos)[KC_H] = reinterpret_cast<float(*)[KC_H]>(base + KC_RW * 3 * KC_H);              // dOut
+  float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(base + KC_RW * 4 * KC_H);  // [head][i][j]
+  float(*dsh)[KC_RW][KC_RW] = pp + KC_HEADS;                                                   // [head][i][j]
+  {
+    const float4* s1 = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
+    float4* d1 = reinterpret_cast<float4*>(&rec[0][0]);
+    for (int i = lane; i < cnt * 96; i += 32) d1[i] = s1[i];
+    const float4* s2 = reinterpret_cast<const float4*>(a.dout + uint64_t(start) * KC_H);
+    float4* d2 = reinterpret_cast<float4*>(&dos[0][0]);
+    for (int i = lane; i < cnt * 32; i += 32) d2[i] = s2[i];
+    for (int i = lane; i < cnt * KC_HEADS * KC_RW; i += 32) {
+      const int ti = i >> 5, head = (i >> 3) & 3, jj = i & 7;
+      pp[head][ti][jj] = a.p[(uint64_t(start) + ti) * KC_HEADS * KC_RW + head * KC_RW + jj];
+    }
+  }
+  __syncwarp();
+  {
+    const int ti = lane >> 2, head = lane & 3, hb = head * KC_HEAD_DIM;
+    if (ti < cnt) {
+      double s[KC_RW];
+      double rs = 0.0;
+      for (int j = 0; j < cnt; j++) {
+        double acc = 0.0;
+#pragma unroll 8
+        for (int d = 0; d < KC_HEAD_DIM; d++) acc = fma(double(dos[ti][hb + d]), double(rec[j][2 * KC_H + hb + d]), acc);
+        s[j] = acc;
+        rs = rs + double(pp[head][ti][j]) * acc;
+      }
+      for (int j = 0; j < cnt; j++) dsh[head][ti][j] = f32(double(pp[head][ti][j]) * (double(f32(s[j])) - rs));
+    }
+  }
+  __syncwarp();
+  float* out = a.dqkv + uint64_t(start) * 3 * KC_H;
+  for (int m = 0; m < KC_HEADS; m++) {
+    const int col = m * KC_HEAD_DIM + lane;
+    for (int i = 0; i < cnt; i++) {
+      double aq = 0.0, ak = 0.0, av = 0.0;
+      for (int j = 0; j < cnt; j++) {
+        aq = fma(double(dsh[m][i][j]), double(rec[j][KC_H + col]), aq);
+        ak = fma(double(dsh[m][j][i]), double(rec[j][col]), ak);
+        av = fma(double(pp[m][j][i]), double(dos[j][col]), av);
+      }
+      out[uint64_t(i) * 3 * KC_H + col] = f32(aq * a.scale);
+      out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak * a.scale);
+      out[uint64_t(i) * 3 * KC_H + 2 * KC_H + col] = f32(av);
+    }
+  }
+}
+
+}  // namespace kc

@@ -71,11 +71,14 @@ __global__ void __launch_bounds__(256) k_embed_exact(EmbedArgs a) {
 // operands converted to f64 once when staged in shared memory.
 // Requires N % 128 == 0, K % 8 == 0, 16-byte aligned rows.
 // ---------------------------------------------------------------------------
-enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2 };
+//   C = gate > 0 ? f32(A·Bᵀ) : 0            kEpiGate   (reluBackward of a saved ReLU output,
+//                                                        backward.ts:65-70)
+enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2, kEpiGate = 3 };
 
 template <int EPI>
 __global__ void __launch_bounds__(256, 1) k_dgemm_exact(const float* __restrict__ A, const float* __restrict__ B,
-                                                       float* C, int M, int N, int K, int lda, int ldb, int ldc) {
+                                                       float* C, int M, int N, int K, int lda, int ldb, int ldc,
+                                                       const float* __restrict__ gate = nullptr) {
   constexpr int BM = 128, BN = 128, BK = 8;
   __shared__ double As[2][BK][BM];
   __shared__ double Bs[2][BK][BN];
@@ -137,6 +140,7 @@ __global__ void __launch_bounds__(256, 1) k_dgemm_exact(const float* __restrict_
       const float v = f32(acc[i][j]);
       if (EPI == kEpiStore) cp[16 * j] = v;
       else if (EPI == kEpiRelu) cp[16 * j] = js_relu(v);
+      else if (EPI == kEpiGate) cp[16 * j] = gate[row * int64_t(ldc) + n0 + tx + 16 * j] > 0.0f ? v : 0.0f;
       else cp[16 * j] = f32(double(cp[16 * j]) + double(v));
     }
   }
@@ -173,6 +177,7 @@ struct LocalAttnArgs {
   const uint2* rec_meta;     // [N] (.y & 15 = token count)
   uint64_t records;
   double scale;              // 1/sqrt(headDim)
+  float* p_out;              // optional [T][4][8]: the softmax row over the record's window
 };
 
 __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
@@ -206,6 +211,8 @@ __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
     } else {
       softmax_small(p, cnt);
     }
+    if (a.p_out)
+      for (int j = 0; j < cnt; j++) a.p_out[((uint64_t(start) + ti) * KC_HEADS + head) * KC_RW + j] = p[j];
   }
   __syncwarp();
   if (ti < cnt) {
@@ -349,6 +356,10 @@ struct CrossAttnArgs {
   const uint64_t* r_off;
   uint32_t max_r;
   double scale;             // 1/sqrt(headDim)
+  float* p_out;             // optional [4][sum Q_f R_f]: head h of question i at h*P + p_off[f] + il*R + j
+  const uint64_t* q_off;
+  const uint64_t* p_off;
+  uint64_t total_p;
 };
 
 __global__ void __launch_bounds__(128) k_cross_attn_exact(CrossAttnArgs a) {
@@ -404,6 +415,10 @@ __global__ void __launch_bounds__(128) k_cross_attn_exact(CrossAttnArgs a) {
       for (int j = lane; j < R; j += 32) row[j] = f32(double(row[j]) * inv);
     } else {
       for (int j = lane; j < R; j += 32) row[j] = 0.0f;
+    }
+    if (a.p_out) {
+      float* po = a.p_out + uint64_t(head) * a.total_p + a.p_off[f] + (qi - a.q_off[f]) * uint64_t(R);
+      for (int j = lane; j < R; j += 32) po[j] = row[j];
     }
   }
   __syncthreads();

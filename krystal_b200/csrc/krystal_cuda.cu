@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "../../include/krystal_cuda.h"
+#include "backward.cuh"
 #include "common.cuh"
 #include "exact.cuh"
 #include "fast.cuh"
@@ -102,6 +103,16 @@ struct Workspace {
   DevBuf flags, list;
 };
 
+// The backward's buffers: what the forward saves for it (per block), the
+// request, the intermediate gradients, and the per-frame results.
+struct BackWs {
+  DevBuf mask, targets, valence;
+  DevBuf enc_qkv, enc_p, enc_h1, mix_q, mix_k, mix_v, mix_p, mix_h1;
+  DevBuf gather, offered, n_allowed, pred, dpred, loss, dwv;
+  DevBuf dquery, dig, dag, dscore, dqp, dkp, dbk, dbv, dswq, dswk;
+  DevBuf dh1, ads, mdq, mdk, mdv, tok_ds, dfs, dpool, edqkv;
+};
+
 enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStCount };
 
 // The matrices the tensor-core path multiplies by, in a fixed order:
@@ -148,6 +159,9 @@ struct kc_handle {
   uint32_t token_rows_len = 0;
   Workspace ws;      // the batch
   Workspace ws_fb;   // frames recomputed on the exact path
+  BackWs bw;         // the backward
+  DevBuf wt;         // transposed copies of the block and selector matrices (page layout)
+  bool wt_dirty = true;
   kc::FrameTotals* h_tot = nullptr;  // pinned
   std::string err;
   uint64_t launches = 0;
@@ -252,6 +266,49 @@ kc_status dgemm(kc_handle* h, const float* A, const float* B, float* C, uint64_t
   dim3 grid(unsigned((M + 127) / 128), N / 128);
   kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(K), int(K), int(N));
   h->launches++;
+  return KC_OK;
+}
+
+// As dgemm, with A's row stride and the gate of kEpiGate.
+template <int EPI>
+kc_status dgemm_ld(kc_handle* h, const float* A, uint32_t lda, const float* B, float* C, uint64_t M, uint32_t N,
+                   uint32_t K, const float* gate = nullptr) {
+  if (M == 0) return KC_OK;
+  dim3 grid(unsigned((M + 127) / 128), N / 128);
+  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(lda), int(K), int(N),
+                                                      gate);
+  h->launches++;
+  return KC_OK;
+}
+
+// Transposed copies of every block and selector matrix, at their page offsets
+// in h->wt (the backward's input products multiply by them).
+kc_status build_transposes(kc_handle* h) {
+  if (!h->wt_dirty) return KC_OK;
+  const Dims& d = h->d;
+  KC_TRY(ensure(h->wt, d.total * 4), "transposed weights");
+  float* wt = P<float>(h->wt);
+  auto tr = [&](uint64_t off, uint32_t n, uint32_t k) {
+    dim3 grid((k + 31) / 32, (n + 31) / 32);
+    kc::k_transpose<<<grid, dim3(32, 8), 0, h->stream>>>(h->w + off, wt + off, int(n), int(k));
+    h->launches++;
+  };
+  const uint64_t hh = uint64_t(d.h) * d.h, fh = uint64_t(d.ffn) * d.h;
+  for (int pass = 0; pass < 2; pass++) {
+    const uint64_t base = pass ? d.off_mixer : d.off_enc;
+    for (uint32_t b = 0; b < (pass ? d.mix : d.enc); b++) {
+      const uint64_t o = base + d.block * b;
+      tr(o, d.h, d.h);
+      tr(o + hh, d.h, d.h);
+      tr(o + 2 * hh, d.h, d.h);
+      tr(o + 3 * hh, d.ffn, d.h);
+      tr(o + 3 * hh + fh, d.h, d.ffn);
+    }
+  }
+  tr(d.off_swq, d.h, d.h);
+  tr(d.off_swk, d.h, d.h);
+  KC_TRY(cudaGetLastError(), "transposed weights");
+  h->wt_dirty = false;
   return KC_OK;
 }
 
@@ -404,10 +461,20 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
   return KC_OK;
 }
 
+// What the backward needs from the forward, per block: the encoder's q|k|v,
+// local-attention p and ReLU output; the mixer's projections, p and ReLU
+// output. The selector then runs under `mask` and writes the soft gather.
+struct Saves {
+  float *enc_qkv, *enc_p, *enc_h1;                  // strides T*3H, T*32, T*F
+  float *mix_q, *mix_k, *mix_v, *mix_p, *mix_h1;    // strides Q*H, R*H, R*H, 4*P, Q*F
+  const float* mask;                                // [P]
+  float* gather;                                    // [Q,H]
+};
+
 // The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
 // the workspace: qstate [Q,H], bk/bv [R,H], p, index.
 kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
-                        bool encode_only) {
+                        bool encode_only, const Saves* sv = nullptr) {
   const Dims& d = h->d;
   const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r;
   const uint32_t H = d.h, FF = d.ffn;
@@ -427,23 +494,26 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     const float* W = h->w + d.off_enc + d.block * blk;
     const float* w1 = W + 3ull * H * H;
     const float* w2 = w1 + uint64_t(FF) * H;
+    float* bqkv = sv ? sv->enc_qkv + blk * T * 3 * H : qkv;
+    float* bh1 = sv ? sv->enc_h1 + blk * T * FF : qkv;
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
-      dgemm<kc::kEpiStore>(h, x, W, qkv, T, 3 * H, H);
+      dgemm<kc::kEpiStore>(h, x, W, bqkv, T, 3 * H, H);
     }
     {
       ProfScope ps(h, kStEncAttn);
-      kc::LocalAttnArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale};
+      kc::LocalAttnArgs la{bqkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
+                           sv ? sv->enc_p + blk * T * 32 : nullptr};
       kc::k_local_attn_exact<<<unsigned((N + 3) / 4), 128, 0, h->stream>>>(la);
       h->launches++;
     }
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
-      dgemm<kc::kEpiRelu>(h, x, w1, qkv, T, FF, H);
+      dgemm<kc::kEpiRelu>(h, x, w1, bh1, T, FF, H);
     }
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
-      dgemm<kc::kEpiResid>(h, qkv, w2, x, T, H, FF);
+      dgemm<kc::kEpiResid>(h, bh1, w2, x, T, H, FF);
     }
   }
   {
@@ -459,16 +529,21 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
       const float* W = h->w + d.off_mixer + d.block * blk;
       const float* w1 = W + 3ull * H * H;
       const float* w2 = w1 + uint64_t(FF) * H;
-      dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), W, P<float>(ws.mq), Q, H, H);
-      dgemm<kc::kEpiStore>(h, P<float>(ws.bk), W + uint64_t(H) * H, P<float>(ws.mk), R, H, H);
-      dgemm<kc::kEpiStore>(h, P<float>(ws.bv), W + 2ull * H * H, P<float>(ws.mv), R, H, H);
-      kc::CrossAttnArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
-                           P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off), tot.max_r, attn_scale};
+      float* mq = sv ? sv->mix_q + blk * Q * H : P<float>(ws.mq);
+      float* mk = sv ? sv->mix_k + blk * R * H : P<float>(ws.mk);
+      float* mv = sv ? sv->mix_v + blk * R * H : P<float>(ws.mv);
+      float* mh = sv ? sv->mix_h1 + blk * Q * FF : P<float>(ws.mh);
+      dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), W, mq, Q, H, H);
+      dgemm<kc::kEpiStore>(h, P<float>(ws.bk), W + uint64_t(H) * H, mk, R, H, H);
+      dgemm<kc::kEpiStore>(h, P<float>(ws.bv), W + 2ull * H * H, mv, R, H, H);
+      kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off),
+                           tot.max_r, attn_scale, sv ? sv->mix_p + blk * 4 * tot.p : nullptr,
+                           P<uint64_t>(ws.q_off), P<uint64_t>(ws.p_off), tot.p};
       const size_t smem = size_t(tot.max_r) * 4 * (8 + 4);
       kc::k_cross_attn_exact<<<unsigned(Q), 128, smem, h->stream>>>(ca);
       h->launches++;
-      dgemm<kc::kEpiRelu>(h, P<float>(ws.qstate), w1, P<float>(ws.mh), Q, FF, H);
-      dgemm<kc::kEpiResid>(h, P<float>(ws.mh), w2, P<float>(ws.qstate), Q, H, FF);
+      dgemm<kc::kEpiRelu>(h, P<float>(ws.qstate), w1, mh, Q, FF, H);
+      dgemm<kc::kEpiResid>(h, mh, w2, P<float>(ws.qstate), Q, H, FF);
     }
   }
   if (!encode_only && Q > 0) {
@@ -483,6 +558,10 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
     sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = h_scale;
     sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = nullptr;
+    if (sv) {  // the backward's selection: its mask, no sampling, the soft gather
+      sa.mask = sv->mask; sa.schema_allow = nullptr; sa.band_allow = nullptr; sa.uniforms = nullptr;
+      sa.bank_values = P<float>(ws.bv); sa.gather = sv->gather;
+    }
     const size_t smem = size_t(tot.max_r) * (8 + 4);
     kc::k_select_exact<<<unsigned(Q), 256, smem, h->stream>>>(sa);
     h->launches++;
@@ -783,6 +862,7 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
       h->mat_max[i + 1] = amax(w->selector_wk, hh, 0.f);
     }
     h->images_dirty = true;
+    h->wt_dirty = true;
   }
   KC_TRY(cudaStreamSynchronize(h->stream), "sync");
   return KC_OK;
@@ -792,6 +872,50 @@ template <typename T>
 kc_status stage(kc_handle* h, DevBuf& buf, const T* src, uint64_t n) {
   KC_TRY(ensure(buf, n * sizeof(T)), "workspace");
   if (n) KC_TRY(cudaMemcpyAsync(buf.p, src, n * sizeof(T), cudaMemcpyHostToDevice, h->stream), "upload");
+  return KC_OK;
+}
+
+// compileActiveFrame's record walk (masks.ts:73-74): the active list in
+// order, ending at the first unoccupied entry. Active records are compacted
+// into a one-frame batch staged on the device; slot numbers only name
+// positions, so the forward is unchanged. *q and *r count the frame's
+// questions and bank records.
+kc_status stage_frame(kc_handle* h, const kc_frame_view* frame, DevBatch& b, uint32_t* q_out, uint32_t* r_out) {
+  if (!frame || !frame->token_ids || !frame->field_roles || !frame->schema_ids || !frame->band_ids)
+    return fail(h, KC_ERR_INVALID_ARG, "frame view is incomplete");
+  if (frame->slots == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
+  const uint32_t slots = frame->slots;
+  std::vector<uint32_t> act;
+  act.reserve(slots);
+  for (uint32_t i = 0; i < slots; i++) {
+    const uint32_t s = frame->active_record_indices ? frame->active_record_indices[i] : i;
+    if (s == KC_INVALID || s >= slots) break;
+    act.push_back(s);
+  }
+  const uint32_t n = uint32_t(act.size());
+  if (n == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
+  std::vector<uint32_t> tok(n * 8ull), role(n * 8ull), sch(n), bnd(n);
+  uint32_t q = 0;
+  for (uint32_t i = 0; i < n; i++) {
+    const uint32_t s = act[i];
+    memcpy(&tok[i * 8ull], frame->token_ids + s * 8ull, 32);
+    memcpy(&role[i * 8ull], frame->field_roles + s * 8ull, 32);
+    sch[i] = frame->schema_ids[s];
+    bnd[i] = frame->band_ids[s];
+    q += bnd[i] == KC_QUERY_BAND;
+  }
+  const uint64_t off[2] = {0, n};
+  kc_status s;
+  Workspace& ws = h->ws;
+  if ((s = stage(h, ws.rec_off, off, 2)) || (s = stage(h, ws.token_ids, tok.data(), tok.size())) ||
+      (s = stage(h, ws.field_roles, role.data(), role.size())) || (s = stage(h, ws.schema_ids, sch.data(), n)) ||
+      (s = stage(h, ws.band_ids, bnd.data(), n)))
+    return s;
+  b.frames = 1; b.records = n; b.rec_off = P<uint64_t>(ws.rec_off);
+  b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
+  b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  *q_out = q;
+  *r_out = n - q;
   return KC_OK;
 }
 
@@ -807,6 +931,193 @@ struct DeviceGuard {
     if (prev >= 0 && cur != prev) cudaSetDevice(prev);
   }
 };
+
+// The backward of every frame of a packed batch (backward.cuh), after an
+// exact forward that saves what the backward reads. `sel`, `targets`,
+// `valence` are device arrays or null. Results stay in h->bw and ws.p.
+kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, const uint32_t* targets,
+                         const double* valence, kc::FrameTotals* tot_out) {
+  const Dims& d = h->d;
+  Workspace& ws = h->ws;
+  BackWs& bw = h->bw;
+  kc::FrameTotals tot;
+  KC_CHECK(pack_batch(h, ws, b, &tot));
+  const uint32_t F = b.frames;
+  const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r, PP = tot.p;
+  const uint64_t H = d.h, FF = d.ffn;
+  auto need = [&](DevBuf& buf, uint64_t bytes) { return ensure(buf, bytes); };
+  KC_TRY(need(bw.mask, PP * 4), "workspace");
+  KC_TRY(need(bw.enc_qkv, uint64_t(d.enc) * T * 3 * H * 4), "workspace");
+  KC_TRY(need(bw.enc_p, uint64_t(d.enc) * T * 32 * 4), "workspace");
+  KC_TRY(need(bw.enc_h1, uint64_t(d.enc) * T * FF * 4), "workspace");
+  KC_TRY(need(bw.mix_q, uint64_t(d.mix) * Q * H * 4), "workspace");
+  KC_TRY(need(bw.mix_k, uint64_t(d.mix) * R * H * 4), "workspace");
+  KC_TRY(need(bw.mix_v, uint64_t(d.mix) * R * H * 4), "workspace");
+  KC_TRY(need(bw.mix_p, uint64_t(d.mix) * 4 * PP * 4), "workspace");
+  KC_TRY(need(bw.mix_h1, uint64_t(d.mix) * Q * FF * 4), "workspace");
+  KC_TRY(need(bw.gather, Q * H * 4), "workspace");
+  KC_TRY(need(bw.offered, Q * H * 4), "workspace");
+  KC_TRY(need(bw.n_allowed, Q * 4), "workspace");
+  KC_TRY(need(bw.pred, Q * 4), "workspace");
+  KC_TRY(need(bw.dpred, Q * 4), "workspace");
+  KC_TRY(need(bw.loss, F * 8ull), "workspace");
+  KC_TRY(need(bw.dwv, F * 3 * H * 4), "workspace");
+  KC_TRY(need(bw.dquery, Q * H * 4), "workspace");
+  KC_TRY(need(bw.dig, Q * H * 4), "workspace");
+  KC_TRY(need(bw.dag, Q * H * 4), "workspace");
+  KC_TRY(need(bw.dscore, PP * 4), "workspace");
+  KC_TRY(need(bw.dqp, Q * H * 4), "workspace");
+  KC_TRY(need(bw.dkp, R * H * 4), "workspace");
+  KC_TRY(need(bw.dbk, R * H * 4), "workspace");
+  KC_TRY(need(bw.dbv, R * H * 4), "workspace");
+  KC_TRY(need(bw.dswq, F * H * H * 4), "workspace");
+  KC_TRY(need(bw.dswk, F * H * H * 4), "workspace");
+  KC_TRY(need(bw.dh1, (Q > T ? Q : T) * FF * 4), "workspace");
+  KC_TRY(need(bw.ads, 4 * PP * 4), "workspace");
+  KC_TRY(need(bw.mdq, Q * H * 4), "workspace");
+  KC_TRY(need(bw.mdk, R * H * 4), "workspace");
+  KC_TRY(need(bw.mdv, R * H * 4), "workspace");
+  KC_TRY(need(bw.tok_ds, T * 16), "workspace");
+  KC_TRY(need(bw.dfs, T * H * 4), "workspace");
+  KC_TRY(need(bw.dpool, F * 2 * H * 4), "workspace");
+  KC_TRY(need(bw.edqkv, T * 3 * H * 4), "workspace");
+  KC_TRY(ensure(ws.gather, Q * H * 4), "workspace");
+  KC_CHECK(build_transposes(h));
+  const float* wt = P<float>(h->wt);
+  kc::BatchGeo geo{P<uint32_t>(ws.query_frame), P<uint32_t>(ws.bank_frame), P<uint64_t>(ws.q_off),
+                   P<uint64_t>(ws.r_off), P<uint64_t>(ws.p_off)};
+  // the selection: given, from the batch's rule, or open
+  const float* mask = P<float>(bw.mask);
+  if (sel) {
+    mask = sel;
+  } else if (b.schema_allow && Q) {
+    kc::RuleMaskArgs ra{geo, b.schema_allow, b.band_allow, P<uint32_t>(ws.bank_rec), b.schema_ids, b.band_ids,
+                        P<float>(bw.mask)};
+    kc::k_rule_mask<<<unsigned(Q), 256, 0, h->stream>>>(ra);
+    h->launches++;
+  } else if (PP) {
+    KC_TRY(cudaMemsetAsync(bw.mask.p, 0, PP * 4, h->stream), "memset");
+  }
+  if (Q) KC_TRY(cudaMemsetAsync(bw.gather.p, 0, Q * H * 4, h->stream), "memset");
+  if (T) KC_TRY(cudaMemsetAsync(bw.dfs.p, 0, T * H * 4, h->stream), "memset");
+  Saves sv{P<float>(bw.enc_qkv), P<float>(bw.enc_p), P<float>(bw.enc_h1), P<float>(bw.mix_q), P<float>(bw.mix_k),
+           P<float>(bw.mix_v), P<float>(bw.mix_p), P<float>(bw.mix_h1), mask, P<float>(bw.gather)};
+  KC_CHECK(forward_exact(h, ws, b, tot, false, &sv));
+
+  const double h_scale = 1.0 / std::sqrt(double(H));
+  const double attn_scale = 1.0 / std::sqrt(double(d.hd));
+  const float* qout = P<float>(ws.qstate);
+  const float* bk = P<float>(ws.bk);
+  const float* bv = P<float>(ws.bv);
+  const float* p = P<float>(ws.p);
+  float* dquery = P<float>(bw.dquery);
+  float* dbk = P<float>(bw.dbk);
+  float* dbv = P<float>(bw.dbv);
+  {
+    ProfScope ps(h, kStSelector);
+    if (Q) {
+      kc::OfferedArgs oa{geo, mask, bv, qout, P<float>(bw.gather), h->w + d.off_val, P<float>(bw.offered),
+                         P<uint32_t>(bw.n_allowed), P<float>(bw.pred)};
+      kc::k_offered_pred<<<unsigned(Q), 128, 0, h->stream>>>(oa);
+      h->launches++;
+    }
+    kc::k_value_loss<<<(F + 127) / 128, 128, 0, h->stream>>>(P<float>(bw.pred), valence, P<uint64_t>(ws.q_off), F,
+                                                              P<float>(bw.dpred), P<double>(bw.loss));
+    kc::k_value_wv<<<F, 384, 0, h->stream>>>(qout, P<float>(bw.gather), P<float>(bw.offered), P<float>(bw.dpred),
+                                             P<uint64_t>(ws.q_off), P<float>(bw.dwv));
+    h->launches += 2;
+    if (Q) {
+      kc::SelBackArgs sb{geo, p, bv, h->w + d.off_val, P<float>(bw.dpred), targets, dquery, P<float>(bw.dig),
+                         P<float>(bw.dag), P<float>(bw.dscore)};
+      kc::k_sel_back_scores<<<unsigned(Q), 256, size_t(tot.max_r) * 8, h->stream>>>(sb);
+      kc::k_sel_back_dq<<<unsigned(Q), 128, 0, h->stream>>>(geo, P<float>(bw.dscore), P<float>(ws.sk), h_scale,
+                                                           P<float>(bw.dqp));
+      h->launches += 2;
+    }
+    if (R) {
+      kc::SelBackKArgs sk{geo, P<float>(bw.dscore), p, mask, P<float>(ws.sq), P<float>(bw.dig), P<float>(bw.dag),
+                          P<uint32_t>(bw.n_allowed), h_scale, P<float>(bw.dkp), dbv};
+      kc::k_sel_back_dk<<<unsigned(R), 128, 0, h->stream>>>(sk);
+      h->launches++;
+    }
+    // dQuery = dQueryOut + dQProj·Wq; dBankKeys = dKProj·Wk (backward.ts:900-912)
+    KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.dqp), H, wt + d.off_swq, dquery, Q, H, H));
+    KC_CHECK(dgemm_ld<kc::kEpiStore>(h, P<float>(bw.dkp), H, wt + d.off_swk, dbk, R, H, H));
+    kc::k_weight_grad<<<dim3(F, H / 8), 256, 0, h->stream>>>(P<float>(bw.dqp), qout, P<uint64_t>(ws.q_off),
+                                                             P<float>(bw.dswq));
+    kc::k_weight_grad<<<dim3(F, H / 8), 256, 0, h->stream>>>(P<float>(bw.dkp), bk, P<uint64_t>(ws.r_off),
+                                                             P<float>(bw.dswk));
+    h->launches += 2;
+  }
+  // mixer blocks in reverse (backward.ts:925-941)
+  if (Q) {
+    ProfScope ps(h, kStMixer);
+    for (int blk = int(d.mix) - 1; blk >= 0; blk--) {
+      const uint64_t o = d.off_mixer + d.block * blk;
+      const float* wT = wt + o;  // Wqᵀ, Wkᵀ, Wvᵀ [H,H], W1ᵀ [H,F], W2ᵀ [F,H]
+      float* dh1 = P<float>(bw.dh1);
+      KC_CHECK(dgemm_ld<kc::kEpiGate>(h, dquery, H, wT + 3 * H * H + FF * H, dh1, Q, FF, H,
+                                      P<float>(bw.mix_h1) + blk * Q * FF));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, dh1, FF, wT + 3 * H * H, dquery, Q, H, FF));
+      kc::CrossBackArgs cb{geo, dquery, P<float>(bw.mix_q) + blk * Q * H, P<float>(bw.mix_k) + blk * R * H,
+                           P<float>(bw.mix_v) + blk * R * H, P<float>(bw.mix_p) + blk * 4 * PP, PP, tot.max_r,
+                           attn_scale, P<float>(bw.ads), P<float>(bw.mdq), P<float>(bw.mdk), P<float>(bw.mdv)};
+      kc::k_cross_attn_back_q<<<unsigned(Q), 128, size_t(tot.max_r) * 48, h->stream>>>(cb);
+      h->launches++;
+      if (R) {
+        kc::k_cross_attn_back_kv<<<unsigned(R), 128, 0, h->stream>>>(cb);
+        h->launches++;
+      }
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdq), H, wT, dquery, Q, H, H));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdk), H, wT + H * H, dbk, R, H, H));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdv), H, wT + 2 * H * H, dbv, R, H, H));
+    }
+  }
+  // pool backward (backward.ts:944-953)
+  {
+    ProfScope ps(h, kStPool);
+    kc::PoolBackArgs pb{P<float>(ws.x), h->w + d.off_pool, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta),
+                        P<uint32_t>(ws.rec_row), N, h_scale, dbk, dbv, dquery, P<float>(bw.dfs),
+                        P<double>(bw.tok_ds)};
+    kc::k_pool_back<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pb);
+    kc::PoolGradArgs pg{P<float>(ws.x), P<double>(bw.tok_ds), P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta),
+                        P<uint32_t>(ws.bank_rec), P<uint32_t>(ws.query_rec), P<uint64_t>(ws.r_off),
+                        P<uint64_t>(ws.q_off), h_scale, P<float>(bw.dpool)};
+    kc::k_pool_grad<<<F, 256, 0, h->stream>>>(pg);
+    h->launches += 2;
+  }
+  // encoder blocks in reverse (backward.ts:956-968)
+  float* dfs = P<float>(bw.dfs);
+  for (int blk = int(d.enc) - 1; blk >= 0 && T > 0; blk--) {
+    const uint64_t o = d.off_enc + d.block * blk;
+    const float* wT = wt + o;
+    float* dh1 = P<float>(bw.dh1);
+    {
+      ProfScope ps(h, kStEncGemm);
+      KC_CHECK(dgemm_ld<kc::kEpiGate>(h, dfs, H, wT + 3 * H * H + FF * H, dh1, T, FF, H,
+                                      P<float>(bw.enc_h1) + blk * T * FF));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, dh1, FF, wT + 3 * H * H, dfs, T, H, FF));
+    }
+    {
+      ProfScope ps(h, kStEncAttn);
+      kc::LocalBackArgs lb{P<float>(bw.enc_qkv) + blk * T * 3 * H, P<float>(bw.enc_p) + blk * T * 32, dfs,
+                           P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale, P<float>(bw.edqkv)};
+      kc::k_local_attn_back<<<unsigned((N + kc::kLocalBackWarps - 1) / kc::kLocalBackWarps), 128,
+                              kc::kLocalBackSmem, h->stream>>>(lb);
+      h->launches++;
+    }
+    {
+      ProfScope ps(h, kStEncGemm);
+      const float* e = P<float>(bw.edqkv);
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e, 3 * H, wT, dfs, T, H, H));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + H, 3 * H, wT + H * H, dfs, T, H, H));
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + 2 * H, 3 * H, wT + 2 * H * H, dfs, T, H, H));
+    }
+  }
+  KC_TRY(cudaGetLastError(), "backward launch");
+  *tot_out = tot;
+  return KC_OK;
+}
 
 }  // namespace
 
@@ -870,6 +1181,11 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * (8 + 4)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_cross_attn_back_q, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(KC_MAX_BANK) * 48)) ||
+      (e = cudaFuncSetAttribute(kc::k_local_attn_back, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kLocalBackSmem))))
+    return bail(e, "smem");
   s = do_sync(h, weights, nullptr);
   if (s) {
     std::string m = h->err;
@@ -892,47 +1208,13 @@ kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_outpu
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard dg(h->device);
-  if (!frame || !frame->token_ids || !frame->field_roles || !frame->schema_ids || !frame->band_ids)
-    return fail(h, KC_ERR_INVALID_ARG, "frame view is incomplete");
-  if (frame->slots == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
-  // compileActiveFrame's record walk (masks.ts:73-74): the active list in
-  // order, ending at the first unoccupied entry. Active records are compacted
-  // into a one-frame batch; slot numbers only name positions, so the
-  // forward is unchanged.
-  const uint32_t slots = frame->slots;
-  std::vector<uint32_t> act;
-  act.reserve(slots);
-  for (uint32_t i = 0; i < slots; i++) {
-    const uint32_t s = frame->active_record_indices ? frame->active_record_indices[i] : i;
-    if (s == KC_INVALID || s >= slots) break;
-    act.push_back(s);
-  }
-  const uint32_t n = uint32_t(act.size());
-  if (n == 0) return fail(h, KC_ERR_INVALID_ARG, "a frame with no records has nothing to think about");
-  std::vector<uint32_t> tok(n * 8ull), role(n * 8ull), sch(n), bnd(n);
-  uint32_t q = 0;
-  for (uint32_t i = 0; i < n; i++) {
-    const uint32_t s = act[i];
-    memcpy(&tok[i * 8ull], frame->token_ids + s * 8ull, 32);
-    memcpy(&role[i * 8ull], frame->field_roles + s * 8ull, 32);
-    sch[i] = frame->schema_ids[s];
-    bnd[i] = frame->band_ids[s];
-    q += bnd[i] == KC_QUERY_BAND;
-  }
-  if (q == 0) return fail(h, KC_ERR_INVALID_ARG, "the frame must contain at least one query record for the mixer");
-  const uint32_t r = n - q;
-  if (q > q_cap || r > r_cap) return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the frame's Q/R");
-  const uint64_t off[2] = {0, n};
-  kc_status s;
-  Workspace& ws = h->ws;
-  if ((s = stage(h, ws.rec_off, off, 2)) || (s = stage(h, ws.token_ids, tok.data(), tok.size())) ||
-      (s = stage(h, ws.field_roles, role.data(), role.size())) || (s = stage(h, ws.schema_ids, sch.data(), n)) ||
-      (s = stage(h, ws.band_ids, bnd.data(), n)))
-    return s;
+  uint32_t q = 0, r = 0;
   DevBatch b;
-  b.frames = 1; b.records = n; b.rec_off = P<uint64_t>(ws.rec_off);
-  b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
-  b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  kc_status s = stage_frame(h, frame, b, &q, &r);
+  if (s) return s;
+  if (q == 0) return fail(h, KC_ERR_INVALID_ARG, "the frame must contain at least one query record for the mixer");
+  if (q > q_cap || r > r_cap) return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the frame's Q/R");
+  Workspace& ws = h->ws;
   kc::FrameTotals tot;
   if ((s = run_batch(h, b, true, &tot))) return s;
   const uint64_t H = h->d.h;
@@ -1189,6 +1471,83 @@ kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_devi
   if (s) return s;
   out->p = P<float>(h->ws.p); out->index = P<uint32_t>(h->ws.index);
   out->p_off = P<uint64_t>(h->ws.p_off); out->q_off = P<uint64_t>(h->ws.q_off);
+  out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
+  if (h->profiling) prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_backward(kc_handle* h, const kc_frame_view* frame, const float* selection, const uint32_t* targets,
+                      int has_valence, double valence, kc_backward_out* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!out || !out->policy || !out->value_prediction || !out->d_selector_wq || !out->d_selector_wk ||
+      !out->d_pool || !out->d_value_wv)
+    return fail(h, KC_ERR_INVALID_ARG, "backward outputs are incomplete");
+  DevBatch b;
+  uint32_t q = 0, r = 0;
+  kc_status s = stage_frame(h, frame, b, &q, &r);
+  if (s) return s;
+  if (q == 0) return fail(h, KC_ERR_INVALID_ARG, "the frame must contain at least one query record for the mixer");
+  if (uint64_t(q) * r > out->p_capacity || q > out->q_capacity)
+    return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the frame's Q/R");
+  Workspace& ws = h->ws;
+  BackWs& bw = h->bw;
+  const double v = has_valence ? valence : std::nan("");
+  if ((selection && (s = stage(h, ws.mask, selection, uint64_t(q) * r))) ||
+      (targets && (s = stage(h, bw.targets, targets, q))) || (s = stage(h, bw.valence, &v, 1)))
+    return s;
+  kc::FrameTotals tot;
+  if ((s = backward_batch(h, b, selection ? P<float>(ws.mask) : nullptr, targets ? P<uint32_t>(bw.targets) : nullptr,
+                          P<double>(bw.valence), &tot)))
+    return s;
+  out->q = q;
+  out->r = r;
+  out->t = uint32_t(tot.t);
+  if (out->d_field_states && tot.t > out->t_capacity)
+    return fail(h, KC_ERR_CAPACITY, "d_field_states is smaller than the frame's active tokens");
+  const uint64_t H = h->d.h;
+  auto get = [&](void* dst, const DevBuf& src, uint64_t bytes) -> kc_status {
+    if (bytes) KC_TRY(cudaMemcpyAsync(dst, src.p, bytes, cudaMemcpyDeviceToHost, h->stream), "readback");
+    return KC_OK;
+  };
+  if ((s = get(out->policy, ws.p, uint64_t(q) * r * 4)) || (s = get(out->value_prediction, bw.pred, q * 4ull)) ||
+      (s = get(&out->value_loss, bw.loss, 8)) || (s = get(out->d_selector_wq, bw.dswq, H * H * 4)) ||
+      (s = get(out->d_selector_wk, bw.dswk, H * H * 4)) || (s = get(out->d_pool, bw.dpool, 2 * H * 4)) ||
+      (s = get(out->d_value_wv, bw.dwv, 3 * H * 4)) ||
+      (out->d_field_states && (s = get(out->d_field_states, bw.dfs, tot.t * H * 4))))
+    return s;
+  KC_TRY(cudaStreamSynchronize(h->stream), "backward");
+  prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* bv, const float* selection,
+                                   const uint32_t* targets, const double* valence, kc_backward_result* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
+  if (!bv->rec_off || !bv->token_ids || !bv->field_roles || !bv->schema_ids || !bv->band_ids)
+    return fail(h, KC_ERR_INVALID_ARG, "batch view is incomplete");
+  if ((reinterpret_cast<uintptr_t>(bv->token_ids) & 15) || (reinterpret_cast<uintptr_t>(bv->rec_off) & 7))
+    return fail(h, KC_ERR_INVALID_ARG, "token_ids must be 16-byte aligned and rec_off 8-byte aligned");
+  if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
+    return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  DevBatch b;
+  b.frames = bv->frames; b.records = bv->records; b.rec_off = bv->rec_off;
+  b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
+  b.band_ids = bv->band_ids; b.schema_allow = bv->schema_allow; b.band_allow = bv->band_allow;
+  kc::FrameTotals tot;
+  kc_status s = backward_batch(h, b, selection, targets, valence, &tot);
+  if (s) return s;
+  BackWs& bw = h->bw;
+  Workspace& ws = h->ws;
+  out->policy = P<float>(ws.p); out->value_prediction = P<float>(bw.pred); out->value_loss = P<double>(bw.loss);
+  out->d_selector_wq = P<float>(bw.dswq); out->d_selector_wk = P<float>(bw.dswk); out->d_pool = P<float>(bw.dpool);
+  out->d_field_states = P<float>(bw.dfs); out->d_value_wv = P<float>(bw.dwv);
+  out->p_off = P<uint64_t>(ws.p_off); out->q_off = P<uint64_t>(ws.q_off); out->r_off = P<uint64_t>(ws.r_off);
+  out->t_off = P<uint64_t>(ws.t_off);
   out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
   if (h->profiling) prof_collect(h);
   return KC_OK;
