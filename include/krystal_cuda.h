@@ -299,7 +299,25 @@ typedef struct kc_backward_result {
 kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* batch, const float* selection,
                                    const uint32_t* targets, const double* valence, kc_backward_result* out);
 
-/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
+/* learnFromExperience's per-frame readings (host/learn.ts:318-400) of the
+ * last batch kc_backward_batch_device differentiated on this handle. stats:
+ * DEVICE [frames * KC_LEARN_STATS] f64, per frame: questions, bank rows,
+ * baseline (mean valuePrediction), valueLoss, entropy total and rows,
+ * confidence total and rows (the report's terms, learn.ts:372-389; targets:
+ * DEVICE [total_q] bank rows or KC_NO_TARGET, NULL = none). Queued on the
+ * handle's stream. */
+#define KC_LEARN_STATS 8
+kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* stats);
+
+/* The batch gradients the update applies (host/learn.ts:440-470), over the
+ * last batch differentiated: sums = [sum_f step[f]*dSelectorWq_f (H*H) |
+ * sum_f step[f]*dSelectorWk_f (H*H) | sum_f step[f]*dPool_f (2H) |
+ * sum_f value_weight[f]*dValueWv_f (3H)], f64. step / value_weight: DEVICE
+ * [frames] f64 (0 leaves a frame out); sums: DEVICE [2H*H + 5H] f64. With
+ * several GPUs, these per-rank sums are what an all-reduce adds. */
+kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums);
+
+/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
  * certification margin (default 2e-5, in score units; 0 keeps it). */
 kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 

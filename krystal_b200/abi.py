@@ -28,12 +28,14 @@ KC_PRECISION_FAST = 2
 KC_MAX_BANK = 4096
 KC_NO_TARGET = 0xFFFFFFFF
 KC_AWAY_TARGET = 0x80000000
+KC_LEARN_STATS = 8
 
 # Every function include/krystal_cuda.h declares.
 EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
            "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
            "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc",
-           "kc_set_precision", "kc_backward", "kc_backward_batch_device")
+           "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
+           "kc_learn_accumulate")
 
 
 class KrystalCudaError(RuntimeError):
@@ -152,6 +154,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_set_precision.argtypes = [P, C.c_int, C.c_float]
     lib.kc_backward.argtypes = [P, C.POINTER(KcFrameView), P, P, i, C.c_double, C.POINTER(KcBackwardOut)]
     lib.kc_backward_batch_device.argtypes = [P, C.POINTER(KcBatchView), P, P, P, C.POINTER(KcBackwardResult)]
+    lib.kc_learn_frame_stats.argtypes = [P, P, P]
+    lib.kc_learn_accumulate.argtypes = [P, P, P, P]
     lib.kc_set_stream.argtypes = [P, P]
     lib.kc_get_stream.argtypes = [P]
     lib.kc_get_stream.restype = P
@@ -166,7 +170,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_last_error.restype = C.c_char_p
     for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
-                 "kc_set_precision", "kc_backward", "kc_backward_batch_device"):
+                 "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
+           "kc_learn_accumulate"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

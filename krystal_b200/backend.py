@@ -226,6 +226,14 @@ class CudaBrainBackend:
                                                      C.byref(res)), self._h)
         return res
 
+    def learn_frame_stats(self, targets: int | None, stats: int) -> None:
+        """kc_learn_frame_stats over the last batch differentiated (device pointers)."""
+        abi.check(self._lib.kc_learn_frame_stats(self._h, targets, stats), self._h)
+
+    def learn_accumulate(self, step: int, value_weight: int, sums: int) -> None:
+        """kc_learn_accumulate over the last batch differentiated (device pointers)."""
+        abi.check(self._lib.kc_learn_accumulate(self._h, step, value_weight, sums), self._h)
+
     # --- seam extension: the selector on the device -------------------------
     def select(self, encoded: EncodedFrame, mask: np.ndarray | None = None, rule: MaskRule | None = None,
                bank_schema_ids=None, bank_band_ids=None, uniforms=None, gather: bool = True) -> Selection:

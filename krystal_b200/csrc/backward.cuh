@@ -595,4 +595,108 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   }
 }
 
+// learnFromExperience's per-frame readings (host/learn.ts:318-400), from a
+// batch's backward: questions, bank rows, the critic's baseline (the mean of
+// valuePrediction, summed in order), the value loss, and the report's
+// entropy (Σ over rows with more than one allowed record of
+// −Σ p·log p / log allowed, blocked = mask <= NEG_INF/2) and confidence
+// (Σ p[target] over questions with a target row). One warp per frame; lane i
+// walks question i (and i+32, ...), lane 0 adds the lanes' terms in question
+// order.
+constexpr int kLearnStats = 8;
+
+__global__ void __launch_bounds__(256) k_learn_frame_stats(BatchGeo g, const float* p, const float* mask,
+                                                          const float* pred, const double* loss,
+                                                          const uint32_t* targets, uint32_t frames,
+                                                          double* stats) {
+  __shared__ double ent[8][32], conf[8][32];
+  __shared__ int ent_ok[8][32], conf_ok[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t f = blockIdx.x * 8 + warp;
+  if (f >= frames) return;
+  const uint64_t q0 = g.q_off[f], Q = g.q_off[f + 1] - q0;
+  const uint64_t R = g.r_off[f + 1] - g.r_off[f], pb = g.p_off[f];
+  double et = 0.0, er = 0.0, ct = 0.0, cr = 0.0;
+  for (uint64_t base = 0; base < Q; base += 32) {
+    const uint64_t i = base + lane;
+    ent_ok[warp][lane] = 0;
+    conf_ok[warp][lane] = 0;
+    if (i < Q) {
+      const float* prow = p + pb + i * R;
+      const float* mrow = mask + pb + i * R;
+      uint32_t allowed = 0;
+      double e = 0.0;
+      for (uint64_t j = 0; j < R; j++) {
+        if (double(mrow[j]) <= -1e30 / 2) continue;
+        allowed++;
+        const double pj = prow[j];
+        if (pj > 0) e -= pj * log(pj);
+      }
+      if (allowed > 1) {
+        ent[warp][lane] = e / log(double(allowed));
+        ent_ok[warp][lane] = 1;
+      }
+      const uint32_t t = targets ? targets[q0 + i] : KC_INVALID;
+      if (t != KC_INVALID && t < R) {
+        conf[warp][lane] = prow[t];
+        conf_ok[warp][lane] = 1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0)
+      for (int k = 0; k < 32; k++) {
+        if (ent_ok[warp][k]) { et += ent[warp][k]; er += 1; }
+        if (conf_ok[warp][k]) { ct += conf[warp][k]; cr += 1; }
+      }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    double baseline = 0.0;
+    for (uint64_t i = 0; i < Q; i++) baseline += double(pred[q0 + i]);
+    baseline = Q ? baseline / double(Q) : 0.0;
+    double* o = stats + uint64_t(f) * kLearnStats;
+    o[0] = double(Q); o[1] = double(R); o[2] = baseline; o[3] = loss[f];
+    o[4] = et; o[5] = er; o[6] = ct; o[7] = cr;
+  }
+}
+
+// The actor's and critic's batch gradients as the update applies them
+// (host/learn.ts:440-470): out = [Σ_f step_f·dSelectorWq_f | Σ step_f·dSelectorWk_f
+// | Σ step_f·dPool_f | Σ_f value_weight_f·dValueWv_f], in f64. Frames are
+// summed in fixed chunks of kLearnChunk (partials [chunks][E]), then the
+// chunks in order: deterministic for a given batch.
+constexpr int kLearnChunk = 32;
+
+__global__ void __launch_bounds__(256) k_learn_partial(const double* step, const double* value_weight,
+                                                      const float* dwq, const float* dwk, const float* dpool,
+                                                      const float* dwv, uint32_t frames, double* partial) {
+  const uint32_t HH = KC_H * KC_H, E = 2 * HH + 2 * KC_H + 3 * KC_H;
+  const uint32_t e = blockIdx.x * 256 + threadIdx.x;
+  if (e >= E) return;
+  const uint32_t f0 = blockIdx.y * kLearnChunk;
+  const uint32_t f1 = f0 + kLearnChunk < frames ? f0 + kLearnChunk : frames;
+  const float* src;
+  uint32_t stride, off;
+  const double* wgt = step;
+  if (e < HH) { src = dwq; stride = HH; off = e; }
+  else if (e < 2 * HH) { src = dwk; stride = HH; off = e - HH; }
+  else if (e < 2 * HH + 2 * KC_H) { src = dpool; stride = 2 * KC_H; off = e - 2 * HH; }
+  else { src = dwv; stride = 3 * KC_H; off = e - 2 * HH - 2 * KC_H; wgt = value_weight; }
+  double acc = 0.0;
+  for (uint32_t f = f0; f < f1; f++) {
+    const double w = wgt[f];
+    if (w != 0.0) acc += w * double(src[uint64_t(f) * stride + off]);
+  }
+  partial[uint64_t(blockIdx.y) * E + e] = acc;
+}
+
+__global__ void __launch_bounds__(256) k_learn_sum(const double* partial, uint32_t chunks, double* out) {
+  const uint32_t E = 2 * KC_H * KC_H + 2 * KC_H + 3 * KC_H;
+  const uint32_t e = blockIdx.x * 256 + threadIdx.x;
+  if (e >= E) return;
+  double acc = 0.0;
+  for (uint32_t c = 0; c < chunks; c++) acc += partial[uint64_t(c) * E + e];
+  out[e] = acc;
+}
+
 }  // namespace kc

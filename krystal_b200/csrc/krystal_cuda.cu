@@ -111,6 +111,10 @@ struct BackWs {
   DevBuf gather, offered, n_allowed, pred, dpred, loss, dwv;
   DevBuf dquery, dig, dag, dscore, dqp, dkp, dbk, dbv, dswq, dswk;
   DevBuf dh1, ads, mdq, mdk, mdv, tok_ds, dfs, dpool, edqkv;
+  DevBuf learn_partial;
+  // the last batch differentiated: its frame count and the selection it ran under
+  uint32_t frames = 0;
+  const float* mask_used = nullptr;
 };
 
 enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStCount };
@@ -1000,6 +1004,8 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
   }
   if (Q) KC_TRY(cudaMemsetAsync(bw.gather.p, 0, Q * H * 4, h->stream), "memset");
   if (T) KC_TRY(cudaMemsetAsync(bw.dfs.p, 0, T * H * 4, h->stream), "memset");
+  bw.frames = 0;
+  bw.mask_used = mask;
   Saves sv{P<float>(bw.enc_qkv), P<float>(bw.enc_p), P<float>(bw.enc_h1), P<float>(bw.mix_q), P<float>(bw.mix_k),
            P<float>(bw.mix_v), P<float>(bw.mix_p), P<float>(bw.mix_h1), mask, P<float>(bw.gather)};
   KC_CHECK(forward_exact(h, ws, b, tot, false, &sv));
@@ -1115,6 +1121,7 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
     }
   }
   KC_TRY(cudaGetLastError(), "backward launch");
+  bw.frames = F;
   *tot_out = tot;
   return KC_OK;
 }
@@ -1550,6 +1557,44 @@ kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* bv, const 
   out->t_off = P<uint64_t>(ws.t_off);
   out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
   if (h->profiling) prof_collect(h);
+  return KC_OK;
+}
+
+kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* stats) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  const uint32_t F = h->bw.frames;
+  if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "no batch has been differentiated on this handle");
+  if (!stats) return fail(h, KC_ERR_INVALID_ARG, "stats is null");
+  Workspace& ws = h->ws;
+  kc::BatchGeo geo{P<uint32_t>(ws.query_frame), P<uint32_t>(ws.bank_frame), P<uint64_t>(ws.q_off),
+                   P<uint64_t>(ws.r_off), P<uint64_t>(ws.p_off)};
+  kc::k_learn_frame_stats<<<(F + 7) / 8, 256, 0, h->stream>>>(geo, P<float>(ws.p), h->bw.mask_used,
+                                                              P<float>(h->bw.pred), P<double>(h->bw.loss), targets,
+                                                              F, stats);
+  h->launches++;
+  KC_TRY(cudaGetLastError(), "learn stats");
+  return KC_OK;
+}
+
+kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  const uint32_t F = h->bw.frames;
+  if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "no batch has been differentiated on this handle");
+  if (!step || !value_weight || !sums) return fail(h, KC_ERR_INVALID_ARG, "learn arguments are incomplete");
+  const uint64_t H = h->d.h, E = 2 * H * H + 2 * H + 3 * H;
+  const uint32_t chunks = (F + kc::kLearnChunk - 1) / kc::kLearnChunk;
+  KC_TRY(ensure(h->bw.learn_partial, uint64_t(chunks) * E * 8), "workspace");
+  BackWs& bw = h->bw;
+  kc::k_learn_partial<<<dim3(unsigned((E + 255) / 256), chunks), 256, 0, h->stream>>>(
+      step, value_weight, P<float>(bw.dswq), P<float>(bw.dswk), P<float>(bw.dpool), P<float>(bw.dwv), F,
+      P<double>(bw.learn_partial));
+  kc::k_learn_sum<<<unsigned((E + 255) / 256), 256, 0, h->stream>>>(P<double>(bw.learn_partial), chunks, sums);
+  h->launches += 2;
+  KC_TRY(cudaGetLastError(), "learn accumulate");
   return KC_OK;
 }
 

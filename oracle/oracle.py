@@ -80,6 +80,15 @@ def weight_count(config) -> int:
     return int(lib().ko_weight_count(C.byref(d)))
 
 
+WEIGHT_PARTS = ("embeddings", "encoder", "pool", "mixer", "selector_wq", "selector_wk", "decision_head", "value_head")
+
+
+def weight_offset(config, part: str) -> int:
+    """Element offset of a part of the weight page (model.ts:233-265 order)."""
+    d = dims_of(config)
+    return int(lib().ko_weight_offset(C.byref(d), WEIGHT_PARTS.index(part)))
+
+
 def create_weights(config, seed: int) -> np.ndarray:
     d = dims_of(config)
     out = np.empty(weight_count(config), dtype=np.float32)
