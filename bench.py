@@ -160,8 +160,193 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def learn_reference_arm(args) -> None:
+    """The reference's learn step on the CPU: its backward oracle (restated in
+    C++) frame by frame on all host threads, then its host update, on a bounded
+    sample of the learn workload per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import learn_oracle as LO
+    from oracle import oracle as O
+    wl = synth.WORKLOADS[args.workload]
+    cfg = synth.workload_config(wl)
+    w = synth.workload_weights(cfg, wl.vocab)
+    cores = O.max_threads()
+    per_step = 2 * max(cores, 8)
+
+    def one_step(seed):
+        b = synth.make_batch(wl, seed=seed, frames=per_step)
+        targets, rewards = synth.make_learn_inputs(b, seed=seed + 1)
+        offs = b.offsets()
+        exps = []
+        for f in range(b.frames):
+            g = b.frame(f)
+            q0, q1 = int(offs["q_off"][f]), int(offs["q_off"][f + 1])
+            bank = np.flatnonzero(g.band_ids != QUERY_BAND)
+            exps.append(dict(frame=g, chosen=[int(bank[t]) for t in targets[q0:q1]], reward=float(rewards[f]),
+                             mask=np.zeros((q1 - q0) * bank.size, np.float32)))
+        LO.learn_from_experience(cfg, w.page, exps, threads=cores)
+
+    for s_ in range(args.warmup):
+        one_step(900 + 10 * s_)
+    t0 = time.perf_counter()
+    for s_ in range(args.steps):
+        one_step(2000 + 10 * s_)
+    dt = time.perf_counter() - t0
+    value = args.steps * per_step / dt
+    line = {"metric": "learn frames/sec", "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "frames_per_step": per_step,
+                       "note": "reference CPU path = the C++ restatement of packages/krystal/src/forward/backward.ts "
+                               "and learnFromExperience (host/learn.ts:280-512)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{per_step} frames of {wl.name} per step, {O.cpu_model()}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def learn_main(args) -> None:
+    """The learn step (forward + backward + update) over one global batch split
+    into contiguous frame shards, one per rank; the gradient sums cross NVLink
+    in one NCCL all-reduce per step (strong scaling: the batch is fixed)."""
+    import torch
+    import torch.distributed as dist
+
+    from krystal_b200.backend import CudaBrainBackend
+    from krystal_b200.learn import BatchLearner, LearnOptions, shard_bounds
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+    wl = synth.WORKLOADS[args.workload]
+    F = args.frames or wl.frames
+    cfg = synth.workload_config(wl)
+    w = synth.workload_weights(cfg, wl.vocab)
+    be = CudaBrainBackend(cfg, w, local)
+    stream = torch.cuda.current_stream(dev)
+    be.set_stream(stream.cuda_stream)
+    full = synth.make_batch(wl, seed=1, frames=F)
+    targets_all, rewards_all = synth.make_learn_inputs(full, seed=3)
+    lo, hi = shard_bounds(F, world, rank)
+    batch = full.subset(slice(lo, hi))
+    offs_full = full.offsets()
+    tq0, tq1 = int(offs_full["q_off"][lo]), int(offs_full["q_off"][hi])
+    targets = targets_all[tq0:tq1]
+    rewards = rewards_all[lo:hi]
+    answered = np.ones(hi - lo, bool)
+    offs = batch.offsets()
+    learner = BatchLearner(be, w, group)
+    opts = LearnOptions()
+
+    def pinned(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+
+    h_in = {k: pinned(np.ascontiguousarray(getattr(batch, k)).view(np.int32))
+            for k in ("token_ids", "field_roles", "schema_ids", "band_ids")}
+    h_in["rec_off"] = pinned(batch.rec_off.astype(np.int64))
+    h_in["targets"] = pinned(targets.view(np.int32))
+    d_in = {k: v.to(dev) for k, v in h_in.items()}
+    torch.cuda.synchronize(dev)
+
+    def step(src):
+        return learner.step(batch.frames, batch.records, src["rec_off"].data_ptr(), src["token_ids"].data_ptr(),
+                            src["field_roles"].data_ptr(), src["schema_ids"].data_ptr(), src["band_ids"].data_ptr(),
+                            rewards, answered, src["targets"].data_ptr(), None, options=opts, global_frames=F)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn) -> float:
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 0)):
+        rep = step(d_in)
+    clocks = Clocks(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    be.profile(True)
+    be.profile_read(reset=True)
+    launches0 = be.launch_count()
+    ms = timed(lambda: step(d_in))
+    launches = be.launch_count() - launches0
+    prof = be.profile_read(reset=True)
+    be.profile(False)
+    clk = clocks.stop() if clocks else None
+
+    def e2e_step():
+        fresh = {k: v.to(dev, non_blocking=True) for k, v in h_in.items()}
+        return step(fresh)
+
+    ms_e2e = None if args.device_only else timed(e2e_step)
+    rep = step(d_in)
+    if rank == 0:
+        peaks, peaks_kind = load_peaks()
+        value = F * args.steps / (ms / 1e3)
+        lg = max(prof["enc_gemm_launches"], 1)
+        gemm_ms = prof["enc_gemm_ms"] / lg
+        tflops = (prof["enc_gemm_flops"] / lg) / (gemm_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops")
+        line = {
+            "metric": "learn frames/sec", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": wl.name, "frames": F, "frames_per_rank": hi - lo, "questions": int(offs["q_off"][-1]),
+                       "tokens": int(offs["t_off"][-1]), "parallelism": f"frame-shard x{world}, gradient all-reduce",
+                       "l2": "a step's working set is several GB (saved activations and gradients)",
+                       "precision": "exact: f64 accumulation in the reference's order, f32 stores",
+                       "step": "pack + forward with saves + backward + per-frame readings + gradient sums + "
+                               "all-reduce + host update + sync of what moved"},
+            "gpu_launches": launches,
+            "stage_ms_per_step": {k[:-3]: round(prof[k] / args.steps, 3) for k in prof if k.endswith("_ms")},
+            "roofline": {"kernel": "k_dgemm_exact (encoder GEMMs, forward and backward; FP64 pipe)", "bound": "tensor",
+                         "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak if peak else None,
+                         "traffic": None, "launch_ms": gemm_ms,
+                         "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); this kernel runs on the FP64 pipe"},
+            "report": {"frames_seen": rep.frames_seen, "mean_value_loss": rep.mean_value_loss,
+                       "mean_entropy": rep.mean_entropy, "update_applied": rep.update_applied},
+        }
+        if ms_e2e is not None:
+            h2d = sum(int(v.numel() * v.element_size()) for v in h_in.values())
+            line["e2e"] = {"value": F * args.steps / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                           "d2h_bytes_per_step": int((hi - lo) * 8 * 8 + (2 * 128 * 128 + 5 * 128) * 8),
+                           "entry": "learn step from pinned host inputs"}
+        if clk:
+            line["clocks"] = clk
+        print(json.dumps(line), flush=True)
+    be.destroy()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
+    if args.workload.startswith("learn"):
+        (learn_reference_arm if args.impl == "reference" else learn_main)(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

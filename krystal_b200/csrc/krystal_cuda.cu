@@ -1099,9 +1099,12 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
     const float* wT = wt + o;
     float* dh1 = P<float>(bw.dh1);
     {
-      ProfScope ps(h, kStEncGemm);
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + 2 * FF));
       KC_CHECK(dgemm_ld<kc::kEpiGate>(h, dfs, H, wT + 3 * H * H + FF * H, dh1, T, FF, H,
                                       P<float>(bw.enc_h1) + blk * T * FF));
+    }
+    {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
       KC_CHECK(dgemm_ld<kc::kEpiResid>(h, dh1, FF, wT + 3 * H * H, dfs, T, H, FF));
     }
     {
@@ -1112,12 +1115,10 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
                               kc::kLocalBackSmem, h->stream>>>(lb);
       h->launches++;
     }
-    {
-      ProfScope ps(h, kStEncGemm);
-      const float* e = P<float>(bw.edqkv);
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e, 3 * H, wT, dfs, T, H, H));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + H, 3 * H, wT + H * H, dfs, T, H, H));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + 2 * H, 3 * H, wT + 2 * H * H, dfs, T, H, H));
+    const float* e = P<float>(bw.edqkv);
+    for (int part = 0; part < 3; part++) {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * H, 4.0 * T * 3 * H);
+      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + part * H, 3 * H, wT + part * H * H, dfs, T, H, H));
     }
   }
   KC_TRY(cudaGetLastError(), "backward launch");

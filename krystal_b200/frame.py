@@ -187,7 +187,8 @@ class FrameBatch:
         counts = (self.rec_off[idx + 1] - self.rec_off[idx]).astype(np.uint64)
         rec_off = np.zeros(idx.size + 1, dtype=np.uint64)
         np.cumsum(counts, out=rec_off[1:])
-        recs = np.concatenate([np.arange(self.rec_off[i], self.rec_off[i + 1]) for i in idx]) if idx.size else \
+        off = self.rec_off.astype(np.int64)
+        recs = np.concatenate([np.arange(off[i], off[i + 1]) for i in idx]) if idx.size else \
             np.zeros(0, dtype=np.int64)
         tok = (recs[:, None] * RECORD_WIDTH + np.arange(RECORD_WIDTH)).reshape(-1)
         return FrameBatch(rec_off, self.token_ids[tok], self.field_roles[tok], self.schema_ids[recs],

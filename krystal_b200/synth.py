@@ -46,6 +46,8 @@ WORKLOADS = {
     "ragged_4096": Workload("ragged_4096", 4096, (16, 256), (1, 16), 4096, 64),
     # 1024 frames, 4096-record bank + 64 questions, V=16384
     "long_bank_1024": Workload("long_bank_1024", 1024, (4160, 4160), (64, 64), 16384, 64, bank=4096),
+    # learn step: 1024 frames, records 16-256 with 4 questions each, V=4096, schema 0-63
+    "learn_1024": Workload("learn_1024", 1024, (16, 256), (4, 4), 4096, 64),
 }
 
 
@@ -94,6 +96,17 @@ def make_batch(w: Workload, seed: int = 1, frames: int | None = None) -> FrameBa
     ids = rng.integers(1, w.vocab, (N, RECORD_WIDTH)).astype(np.uint32)
     ids[np.arange(RECORD_WIDTH)[None, :] >= ntok[:, None]] = 0
     return FrameBatch(rec_off, ids.reshape(-1), np.zeros(N * RECORD_WIDTH, dtype=np.uint32), schema, band)
+
+
+def make_learn_inputs(batch: FrameBatch, seed: int = 3) -> tuple[np.ndarray, np.ndarray]:
+    """A learn batch's outcome: per question a target bank row drawn uniformly
+    from its frame's bank (u32 [Q]), and per frame a reward ~ N(0, 1) (f64 [F])."""
+    rng = np.random.default_rng(seed)
+    offs = batch.offsets()
+    q, r = offs["q"].astype(np.int64), offs["r"].astype(np.int64)
+    bank_of_q = np.repeat(r, q)
+    targets = np.floor(rng.random(bank_of_q.size) * bank_of_q).astype(np.uint32)
+    return targets, rng.normal(size=batch.frames)
 
 
 def make_rule(batch: FrameBatch, seed: int = 2, density: float = 0.5) -> tuple[np.ndarray, np.ndarray]:

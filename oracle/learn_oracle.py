@@ -47,7 +47,8 @@ def _max_abs(a: np.ndarray) -> float:
 def learn_from_experience(config, page: np.ndarray, experiences, options: Options = Options(),
                           threads: int = 0) -> tuple[np.ndarray, dict]:
     """Returns the updated weight page (a copy) and the LearnReport fields.
-    Token-table unfreezing (learn.ts:298-299) is not restated here."""
+    threads > 1 runs the per-frame backwards on that many threads. Token-table
+    unfreezing (learn.ts:298-299) is not restated here."""
     h = config.hidden_size
     page = page.copy()
     off = {k: O.weight_offset(config, k) for k in O.WEIGHT_PARTS}
@@ -61,6 +62,11 @@ def learn_from_experience(config, page: np.ndarray, experiences, options: Option
     seen = 0
     adv_total = loss_total = ent_total = conf_total = 0.0
     ent_rows = conf_rows = 0
+    # Every frame is differentiated against the weights as they stand before
+    # the update (the gradients are collected first, learn.ts:349-357), so the
+    # per-frame backwards may run in parallel; the host logic then walks the
+    # frames in order.
+    work = []
     for ex in experiences:
         if ex["reward"] is None:
             continue
@@ -80,7 +86,19 @@ def learn_from_experience(config, page: np.ndarray, experiences, options: Option
             targets[i] = bank.index(slot)
             answered = True
         mask = np.ascontiguousarray(ex["mask"], np.float32)
-        res = O.backward(config, page, frame, mask, targets if answered else None, float(ex["reward"]))
+        work.append((ex, q, r, targets, answered, mask))
+
+    def diff(item):
+        ex, _, _, targets, answered, mask = item
+        return O.backward(config, page, ex["frame"], mask, targets if answered else None, float(ex["reward"]))
+
+    if threads > 1 and len(work) > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(threads) as workers:
+            results = list(workers.map(diff, work))
+    else:
+        results = [diff(item) for item in work]
+    for (ex, q, r, targets, answered, mask), res in zip(work, results):
         pred = res["value_prediction"]
         baseline = 0.0
         for v in pred:
