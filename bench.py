@@ -233,6 +233,7 @@ def learn_main(args) -> None:
     cfg = synth.workload_config(wl)
     w = synth.workload_weights(cfg, wl.vocab)
     be = CudaBrainBackend(cfg, w, local)
+    be.set_precision(args.precision)
     stream = torch.cuda.current_stream(dev)
     be.set_stream(stream.cuda_stream)
     full = synth.make_batch(wl, seed=1, frames=F)
@@ -309,23 +310,33 @@ def learn_main(args) -> None:
         lg = max(prof["enc_gemm_launches"], 1)
         gemm_ms = prof["enc_gemm_ms"] / lg
         tflops = (prof["enc_gemm_flops"] / lg) / (gemm_ms / 1e3) / 1e12
-        peak = peaks.get("bf16_tflops")
+        gbs = (prof["enc_gemm_bytes"] / lg) / (gemm_ms / 1e3) / 1e9
+        if args.precision == "exact":
+            peak = peaks.get("bf16_tflops")
+            roof = {"kernel": "k_dgemm_exact (encoder GEMMs, forward and backward; FP64 pipe)", "bound": "tensor",
+                    "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak if peak else None,
+                    "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); this kernel runs on the FP64 pipe"}
+        else:
+            peak = peaks.get("hbm_gbs")
+            roof = {"kernel": "k_tc_gemm (encoder GEMMs, forward and backward; tcgen05 split-fp16)", "bound": "hbm",
+                    "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak if peak else None,
+                    "peak_kind": f"{peaks_kind} HBM copy bandwidth", "tensor_tflops_algorithmic": tflops}
+        roof.update({"traffic": None, "launch_ms": gemm_ms})
         line = {
             "metric": "learn frames/sec", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f64" if args.precision == "exact" else "f32", "data": "synthetic",
             "config": {"workload": wl.name, "frames": F, "frames_per_rank": hi - lo, "questions": int(offs["q_off"][-1]),
                        "tokens": int(offs["t_off"][-1]), "parallelism": f"frame-shard x{world}, gradient all-reduce",
                        "l2": "a step's working set is several GB (saved activations and gradients)",
-                       "precision": "exact: f64 accumulation in the reference's order, f32 stores",
+                       "precision": "exact: f64 accumulation in the reference's order, f32 stores"
+                       if args.precision == "exact" else
+                       "tensor cores: tcgen05 split-fp16 GEMMs (fp32-class), f64 attention/pool/selector",
                        "step": "pack + forward with saves + backward + per-frame readings + gradient sums + "
                                "all-reduce + host update + sync of what moved"},
             "gpu_launches": launches,
             "stage_ms_per_step": {k[:-3]: round(prof[k] / args.steps, 3) for k in prof if k.endswith("_ms")},
-            "roofline": {"kernel": "k_dgemm_exact (encoder GEMMs, forward and backward; FP64 pipe)", "bound": "tensor",
-                         "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak if peak else None,
-                         "traffic": None, "launch_ms": gemm_ms,
-                         "peak_kind": f"{peaks_kind} bf16 dense (cuBLAS); this kernel runs on the FP64 pipe"},
+            "roofline": roof,
             "report": {"frames_seen": rep.frames_seen, "mean_value_loss": rep.mean_value_loss,
                        "mean_entropy": rep.mean_entropy, "update_applied": rep.update_applied},
         }

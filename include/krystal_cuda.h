@@ -57,7 +57,10 @@ extern "C" {
  *   values) has its frame recomputed on the exact path, so selections match
  *   the exact path and distributions agree to ~1e-6.
  * FAST: the tensor-core path without the recomputation (diagnostics).
- * kc_encode and kc_select always compute exactly. */
+ * kc_backward_batch_device runs its products on the tensor cores at CERTIFIED
+ * and FAST (gradients to fp32-class accuracy; the backward makes no discrete
+ * choice to certify) and in the oracle's arithmetic at EXACT.
+ * kc_encode, kc_select and kc_backward always compute exactly. */
 #define KC_PRECISION_EXACT 0
 #define KC_PRECISION_CERTIFIED 1
 #define KC_PRECISION_FAST 2
@@ -295,7 +298,8 @@ typedef struct kc_backward_result {
  * selection [total_p] laid out like p, or NULL (then the batch's mask rule,
  * or open when it has none); targets [total_q] or NULL; valence [frames] with
  * NaN = no value target, or NULL = none. Work is queued on the handle's
- * stream (one short host wait inside, for the batch's sizes). */
+ * stream; the call waits for the batch's sizes and, on the tensor-core path,
+ * for the pipeline's error word (a split overflow reruns the batch exactly). */
 kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* batch, const float* selection,
                                    const uint32_t* targets, const double* valence, kc_backward_result* out);
 

@@ -121,31 +121,39 @@ enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSe
 
 // The matrices the tensor-core path multiplies by, in a fixed order:
 // per encoder block QKV [3H,H], W1 [F,H], W2 [H,F]; per mixer block Wq, Wk,
-// Wv [H,H], W1, W2; the selector's Wq, Wk.
+// Wv [H,H], W1, W2; the selector's Wq, Wk. Then the same list again,
+// transposed (the backward's input products): entry nF + i is the transpose
+// of entry i, read from the transposed page, where an encoder block's QKV
+// becomes one [H, 3H] matrix [Wqᵀ | Wkᵀ | Wvᵀ].
 struct Mat {
   uint64_t page_off;
   uint32_t n, k;
+  bool transposed;
 };
 
 std::vector<Mat> mat_list(const Dims& d) {
   std::vector<Mat> v;
   const uint64_t hh = uint64_t(d.h) * d.h, fh = uint64_t(d.ffn) * d.h;
-  for (uint32_t b = 0; b < d.enc; b++) {
-    const uint64_t o = d.off_enc + d.block * b;
-    v.push_back({o, 3 * d.h, d.h});
-    v.push_back({o + 3 * hh, d.ffn, d.h});
-    v.push_back({o + 3 * hh + fh, d.h, d.ffn});
+  for (int t = 0; t < 2; t++) {
+    const bool tr = t == 1;
+    auto add = [&](uint64_t off, uint32_t n, uint32_t k) { v.push_back(tr ? Mat{off, k, n, true} : Mat{off, n, k, false}); };
+    for (uint32_t b = 0; b < d.enc; b++) {
+      const uint64_t o = d.off_enc + d.block * b;
+      add(o, 3 * d.h, d.h);
+      add(o + 3 * hh, d.ffn, d.h);
+      add(o + 3 * hh + fh, d.h, d.ffn);
+    }
+    for (uint32_t b = 0; b < d.mix; b++) {
+      const uint64_t o = d.off_mixer + d.block * b;
+      add(o, d.h, d.h);
+      add(o + hh, d.h, d.h);
+      add(o + 2 * hh, d.h, d.h);
+      add(o + 3 * hh, d.ffn, d.h);
+      add(o + 3 * hh + fh, d.h, d.ffn);
+    }
+    add(d.off_swq, d.h, d.h);
+    add(d.off_swk, d.h, d.h);
   }
-  for (uint32_t b = 0; b < d.mix; b++) {
-    const uint64_t o = d.off_mixer + d.block * b;
-    v.push_back({o, d.h, d.h});
-    v.push_back({o + hh, d.h, d.h});
-    v.push_back({o + 2 * hh, d.h, d.h});
-    v.push_back({o + 3 * hh, d.ffn, d.h});
-    v.push_back({o + 3 * hh + fh, d.h, d.ffn});
-  }
-  v.push_back({d.off_swq, d.h, d.h});
-  v.push_back({d.off_swk, d.h, d.h});
   return v;
 }
 
@@ -276,11 +284,11 @@ kc_status dgemm(kc_handle* h, const float* A, const float* B, float* C, uint64_t
 // As dgemm, with A's row stride and the gate of kEpiGate.
 template <int EPI>
 kc_status dgemm_ld(kc_handle* h, const float* A, uint32_t lda, const float* B, float* C, uint64_t M, uint32_t N,
-                   uint32_t K, const float* gate = nullptr) {
+                   uint32_t K, const float* gate = nullptr, uint32_t ldb = 0) {
   if (M == 0) return KC_OK;
   dim3 grid(unsigned((M + 127) / 128), N / 128);
-  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(lda), int(K), int(N),
-                                                      gate);
+  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(lda),
+                                                      int(ldb ? ldb : K), int(N), gate);
   h->launches++;
   return KC_OK;
 }
@@ -302,9 +310,13 @@ kc_status build_transposes(kc_handle* h) {
     const uint64_t base = pass ? d.off_mixer : d.off_enc;
     for (uint32_t b = 0; b < (pass ? d.mix : d.enc); b++) {
       const uint64_t o = base + d.block * b;
-      tr(o, d.h, d.h);
-      tr(o + hh, d.h, d.h);
-      tr(o + 2 * hh, d.h, d.h);
+      if (pass == 0) {
+        tr(o, 3 * d.h, d.h);  // [Wq; Wk; Wv] -> [Wqᵀ | Wkᵀ | Wvᵀ]
+      } else {
+        tr(o, d.h, d.h);
+        tr(o + hh, d.h, d.h);
+        tr(o + 2 * hh, d.h, d.h);
+      }
       tr(o + 3 * hh, d.ffn, d.h);
       tr(o + 3 * hh + fh, d.h, d.ffn);
     }
@@ -319,6 +331,7 @@ kc_status build_transposes(kc_handle* h) {
 // Rebuild the split fp16 images of every matrix (after a sync changed them).
 kc_status build_images(kc_handle* h) {
   if (!h->images_dirty) return KC_OK;
+  KC_CHECK(build_transposes(h));
   const auto& m = h->mats;
   if (h->img_off.size() != m.size()) {
     h->img_off.resize(m.size());
@@ -332,9 +345,9 @@ kc_status build_images(kc_handle* h) {
   for (size_t i = 0; i < m.size(); i++) {
     const int sw = int(std::floor(std::log2(2048.0 / std::max(double(h->mat_max[i]), 1e-30))));
     const int swc = std::min(std::max(sw, -40), 40);
+    const float* src = (m[i].transposed ? P<float>(h->wt) : h->w) + m[i].page_off;
     kc::tc::k_weight_image<<<(m[i].n / 128) * (m[i].k / 64), 256, 0, h->stream>>>(
-        h->w + m[i].page_off, int(m[i].n), int(m[i].k), std::ldexp(1.0f, swc),
-        P<uint8_t>(h->images) + h->img_off[i]);
+        src, int(m[i].n), int(m[i].k), std::ldexp(1.0f, swc), P<uint8_t>(h->images) + h->img_off[i]);
     h->launches++;
   }
   KC_TRY(cudaGetLastError(), "weight images");
@@ -349,19 +362,31 @@ int mat_sw(kc_handle* h, int i) {
 
 // y = A·Wᵀ on the tensor cores for matrix `mat` of mat_list.
 template <int EPI>
-kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C) {
+kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, const float* gate = nullptr) {
   if (M == 0) return KC_OK;
   const Mat& mt = h->mats[mat];
-  CUtensorMap map, cmap;
-  if (!kc::tc::make_a_map(&map, A, M, mt.k, mt.k) || !kc::tc::make_c_map(&cmap, C, M, mt.n, mt.n))
+  CUtensorMap map, cmap, gmap;
+  if (!kc::tc::make_a_map(&map, A, M, mt.k, mt.k) || !kc::tc::make_c_map(&cmap, C, M, mt.n, mt.n) ||
+      !kc::tc::make_c_map(&gmap, gate ? gate : C, M, mt.n, mt.n))
     return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a GEMM operand");
   kc::tc::GemmArgs g{int(M), int(mt.k), int(mt.n / 128), P<uint8_t>(h->images) + h->img_off[mat], C,
                      int(mt.n), std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat))), h->d_err};
   const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
-  kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, g);
+  kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, gmap, g);
   h->launches++;
   return KC_OK;
+}
+
+// One GEMM of the exact sequence: on the FP64 pipe in the oracle's order, or
+// (tc) on the tensor cores, where `mat` names the matrix in the tensor-core
+// list and B / ldb the same matrix for the FP64 kernel. The tensor-core path
+// reads A with row stride K.
+template <int EPI>
+kc_status gemm(kc_handle* h, bool tc, const float* A, uint32_t lda, uint64_t M, int mat, const float* B,
+               uint32_t ldb, float* C, uint32_t N, uint32_t K, const float* gate = nullptr) {
+  if (tc) return tc_gemm<EPI>(h, A, M, mat, C, gate);
+  return dgemm_ld<EPI>(h, A, lda, B, C, M, N, K, gate, ldb);
 }
 
 // Device-side view of one batch (all pointers on the handle's device).
@@ -478,7 +503,7 @@ struct Saves {
 // The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
 // the workspace: qstate [Q,H], bk/bv [R,H], p, index.
 kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
-                        bool encode_only, const Saves* sv = nullptr) {
+                        bool encode_only, const Saves* sv = nullptr, bool tc = false) {
   const Dims& d = h->d;
   const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r;
   const uint32_t H = d.h, FF = d.ffn;
@@ -500,9 +525,10 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     const float* w2 = w1 + uint64_t(FF) * H;
     float* bqkv = sv ? sv->enc_qkv + blk * T * 3 * H : qkv;
     float* bh1 = sv ? sv->enc_h1 + blk * T * FF : qkv;
+    const int em = 3 * int(blk);  // this block's matrices in the tensor-core list
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
-      dgemm<kc::kEpiStore>(h, x, W, bqkv, T, 3 * H, H);
+      KC_CHECK(gemm<kc::kEpiStore>(h, tc, x, H, T, em, W, H, bqkv, 3 * H, H));
     }
     {
       ProfScope ps(h, kStEncAttn);
@@ -513,11 +539,11 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     }
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
-      dgemm<kc::kEpiRelu>(h, x, w1, bh1, T, FF, H);
+      KC_CHECK(gemm<kc::kEpiRelu>(h, tc, x, H, T, em + 1, w1, H, bh1, FF, H));
     }
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
-      dgemm<kc::kEpiResid>(h, bh1, w2, x, T, H, FF);
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, bh1, FF, T, em + 2, w2, FF, x, H, FF));
     }
   }
   {
@@ -537,23 +563,25 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
       float* mk = sv ? sv->mix_k + blk * R * H : P<float>(ws.mk);
       float* mv = sv ? sv->mix_v + blk * R * H : P<float>(ws.mv);
       float* mh = sv ? sv->mix_h1 + blk * Q * FF : P<float>(ws.mh);
-      dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), W, mq, Q, H, H);
-      dgemm<kc::kEpiStore>(h, P<float>(ws.bk), W + uint64_t(H) * H, mk, R, H, H);
-      dgemm<kc::kEpiStore>(h, P<float>(ws.bv), W + 2ull * H * H, mv, R, H, H);
+      const int m0 = 3 * int(d.enc) + 5 * int(blk);
+      KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, m0, W, H, mq, H, H));
+      KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, m0 + 1, W + uint64_t(H) * H, H, mk, H, H));
+      KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bv), H, R, m0 + 2, W + 2ull * H * H, H, mv, H, H));
       kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off),
                            tot.max_r, attn_scale, sv ? sv->mix_p + blk * 4 * tot.p : nullptr,
                            P<uint64_t>(ws.q_off), P<uint64_t>(ws.p_off), tot.p};
       const size_t smem = size_t(tot.max_r) * 4 * (8 + 4);
       kc::k_cross_attn_exact<<<unsigned(Q), 128, smem, h->stream>>>(ca);
       h->launches++;
-      dgemm<kc::kEpiRelu>(h, P<float>(ws.qstate), w1, mh, Q, FF, H);
-      dgemm<kc::kEpiResid>(h, mh, w2, P<float>(ws.qstate), Q, H, FF);
+      KC_CHECK(gemm<kc::kEpiRelu>(h, tc, P<float>(ws.qstate), H, Q, m0 + 3, w1, H, mh, FF, H));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, mh, FF, Q, m0 + 4, w2, FF, P<float>(ws.qstate), H, FF));
     }
   }
   if (!encode_only && Q > 0) {
     ProfScope ps(h, kStSelector);
-    dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), h->w + d.off_swq, P<float>(ws.sq), Q, H, H);
-    dgemm<kc::kEpiStore>(h, P<float>(ws.bk), h->w + d.off_swk, P<float>(ws.sk), R, H, H);
+    const int sm = 3 * int(d.enc) + 5 * int(d.mix);
+    KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, sm, h->w + d.off_swq, H, P<float>(ws.sq), H, H));
+    KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, sm + 1, h->w + d.off_swk, H, P<float>(ws.sk), H, H));
     kc::SelectArgs sa{};
     sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk); sa.bank_values = nullptr;
     sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
@@ -865,6 +893,8 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
       h->mat_max[i] = amax(w->selector_wq, hh, 0.f);
       h->mat_max[i + 1] = amax(w->selector_wk, hh, 0.f);
     }
+    const size_t nf = h->mats.size() / 2;  // a transposed matrix has its original's largest entry
+    for (size_t j = 0; j < nf; j++) h->mat_max[nf + j] = h->mat_max[j];
     h->images_dirty = true;
     h->wt_dirty = true;
   }
@@ -940,7 +970,10 @@ struct DeviceGuard {
 // exact forward that saves what the backward reads. `sel`, `targets`,
 // `valence` are device arrays or null. Results stay in h->bw and ws.p.
 kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, const uint32_t* targets,
-                         const double* valence, kc::FrameTotals* tot_out) {
+                         const double* valence, kc::FrameTotals* tot_out, bool exact) {
+  // The GEMMs run on the tensor cores unless the handle or the caller asks
+  // for the oracle's arithmetic; a split overflow reruns the batch exactly.
+  const bool tc = !exact && h->precision != KC_PRECISION_EXACT;
   const Dims& d = h->d;
   Workspace& ws = h->ws;
   BackWs& bw = h->bw;
@@ -1008,7 +1041,13 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
   bw.mask_used = mask;
   Saves sv{P<float>(bw.enc_qkv), P<float>(bw.enc_p), P<float>(bw.enc_h1), P<float>(bw.mix_q), P<float>(bw.mix_k),
            P<float>(bw.mix_v), P<float>(bw.mix_p), P<float>(bw.mix_h1), mask, P<float>(bw.gather)};
-  KC_CHECK(forward_exact(h, ws, b, tot, false, &sv));
+  if (tc) {
+    KC_CHECK(build_images(h));
+    KC_TRY(cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream), "memset");
+  }
+  KC_CHECK(forward_exact(h, ws, b, tot, false, &sv, tc));
+  const int nf = int(h->mats.size() / 2);  // transposed matrices follow the forward ones
+  const int sel_m = 3 * int(d.enc) + 5 * int(d.mix);
 
   const double h_scale = 1.0 / std::sqrt(double(H));
   const double attn_scale = 1.0 / std::sqrt(double(d.hd));
@@ -1047,8 +1086,8 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
       h->launches++;
     }
     // dQuery = dQueryOut + dQProj·Wq; dBankKeys = dKProj·Wk (backward.ts:900-912)
-    KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.dqp), H, wt + d.off_swq, dquery, Q, H, H));
-    KC_CHECK(dgemm_ld<kc::kEpiStore>(h, P<float>(bw.dkp), H, wt + d.off_swk, dbk, R, H, H));
+    KC_CHECK(gemm<kc::kEpiResid>(h, tc, P<float>(bw.dqp), H, Q, nf + sel_m, wt + d.off_swq, H, dquery, H, H));
+    KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(bw.dkp), H, R, nf + sel_m + 1, wt + d.off_swk, H, dbk, H, H));
     kc::k_weight_grad<<<dim3(F, H / 8), 256, 0, h->stream>>>(P<float>(bw.dqp), qout, P<uint64_t>(ws.q_off),
                                                              P<float>(bw.dswq));
     kc::k_weight_grad<<<dim3(F, H / 8), 256, 0, h->stream>>>(P<float>(bw.dkp), bk, P<uint64_t>(ws.r_off),
@@ -1062,9 +1101,10 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
       const uint64_t o = d.off_mixer + d.block * blk;
       const float* wT = wt + o;  // Wqᵀ, Wkᵀ, Wvᵀ [H,H], W1ᵀ [H,F], W2ᵀ [F,H]
       float* dh1 = P<float>(bw.dh1);
-      KC_CHECK(dgemm_ld<kc::kEpiGate>(h, dquery, H, wT + 3 * H * H + FF * H, dh1, Q, FF, H,
-                                      P<float>(bw.mix_h1) + blk * Q * FF));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, dh1, FF, wT + 3 * H * H, dquery, Q, H, FF));
+      const int m0 = nf + 3 * int(d.enc) + 5 * blk;
+      KC_CHECK(gemm<kc::kEpiGate>(h, tc, dquery, H, Q, m0 + 4, wT + 3 * H * H + FF * H, H, dh1, FF, H,
+                                  P<float>(bw.mix_h1) + blk * Q * FF));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, dh1, FF, Q, m0 + 3, wT + 3 * H * H, FF, dquery, H, FF));
       kc::CrossBackArgs cb{geo, dquery, P<float>(bw.mix_q) + blk * Q * H, P<float>(bw.mix_k) + blk * R * H,
                            P<float>(bw.mix_v) + blk * R * H, P<float>(bw.mix_p) + blk * 4 * PP, PP, tot.max_r,
                            attn_scale, P<float>(bw.ads), P<float>(bw.mdq), P<float>(bw.mdk), P<float>(bw.mdv)};
@@ -1074,9 +1114,9 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
         kc::k_cross_attn_back_kv<<<unsigned(R), 128, 0, h->stream>>>(cb);
         h->launches++;
       }
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdq), H, wT, dquery, Q, H, H));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdk), H, wT + H * H, dbk, R, H, H));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, P<float>(bw.mdv), H, wT + 2 * H * H, dbv, R, H, H));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, P<float>(bw.mdq), H, Q, m0, wT, H, dquery, H, H));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, P<float>(bw.mdk), H, R, m0 + 1, wT + H * H, H, dbk, H, H));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, P<float>(bw.mdv), H, R, m0 + 2, wT + 2 * H * H, H, dbv, H, H));
     }
   }
   // pool backward (backward.ts:944-953)
@@ -1098,14 +1138,15 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
     const uint64_t o = d.off_enc + d.block * blk;
     const float* wT = wt + o;
     float* dh1 = P<float>(bw.dh1);
+    const int em = nf + 3 * blk;
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + 2 * FF));
-      KC_CHECK(dgemm_ld<kc::kEpiGate>(h, dfs, H, wT + 3 * H * H + FF * H, dh1, T, FF, H,
-                                      P<float>(bw.enc_h1) + blk * T * FF));
+      KC_CHECK(gemm<kc::kEpiGate>(h, tc, dfs, H, T, em + 2, wT + 3 * H * H + FF * H, H, dh1, FF, H,
+                                  P<float>(bw.enc_h1) + blk * T * FF));
     }
     {
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, dh1, FF, wT + 3 * H * H, dfs, T, H, FF));
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, dh1, FF, T, em + 1, wT + 3 * H * H, FF, dfs, H, FF));
     }
     {
       ProfScope ps(h, kStEncAttn);
@@ -1115,13 +1156,27 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
                               kc::kLocalBackSmem, h->stream>>>(lb);
       h->launches++;
     }
+    // dStates += dQ·Wq + dK·Wk + dV·Wv: three f32-rounded adds in the oracle's
+    // order, or one product over [dQ | dK | dV] · [Wqᵀ | Wkᵀ | Wvᵀ]ᵀ on the tensor cores
     const float* e = P<float>(bw.edqkv);
-    for (int part = 0; part < 3; part++) {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * H, 4.0 * T * 3 * H);
-      KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + part * H, 3 * H, wT + part * H * H, dfs, T, H, H));
+    if (tc) {
+      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * 5 * H);
+      KC_CHECK(gemm<kc::kEpiResid>(h, tc, e, 3 * H, T, em, wT, 3 * H, dfs, H, 3 * H));
+    } else {
+      for (int part = 0; part < 3; part++) {
+        ProfScope ps(h, kStEncGemm, 2.0 * T * H * H, 4.0 * T * 3 * H);
+        KC_CHECK(dgemm_ld<kc::kEpiResid>(h, e + part * H, 3 * H, wT + part * H, dfs, T, H, H, nullptr, 3 * H));
+      }
     }
   }
   KC_TRY(cudaGetLastError(), "backward launch");
+  if (tc) {
+    KC_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream), "readback");
+    KC_TRY(cudaStreamSynchronize(h->stream), "backward");
+    const int e = *h->h_err;
+    if (e & kc::tc::kErrTimeout) return fail(h, KC_ERR_TIMEOUT, "a tensor-core pipeline wait expired");
+    if (e & kc::tc::kErrOverflow) return backward_batch(h, b, sel, targets, valence, tot_out, true);
+  }
   bw.frames = F;
   *tot_out = tot;
   return KC_OK;
@@ -1181,6 +1236,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kSmemBytesT)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiGate>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * 4)))
@@ -1507,7 +1564,7 @@ kc_status kc_backward(kc_handle* h, const kc_frame_view* frame, const float* sel
     return s;
   kc::FrameTotals tot;
   if ((s = backward_batch(h, b, selection ? P<float>(ws.mask) : nullptr, targets ? P<uint32_t>(bw.targets) : nullptr,
-                          P<double>(bw.valence), &tot)))
+                          P<double>(bw.valence), &tot, true)))
     return s;
   out->q = q;
   out->r = r;
@@ -1547,7 +1604,7 @@ kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* bv, const 
   b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
   b.band_ids = bv->band_ids; b.schema_allow = bv->schema_allow; b.band_allow = bv->band_allow;
   kc::FrameTotals tot;
-  kc_status s = backward_batch(h, b, selection, targets, valence, &tot);
+  kc_status s = backward_batch(h, b, selection, targets, valence, &tot, false);
   if (s) return s;
   BackWs& bw = h->bw;
   Workspace& ws = h->ws;

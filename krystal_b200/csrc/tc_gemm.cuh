@@ -178,7 +178,9 @@ __device__ __forceinline__ uint32_t swz_offset(uint32_t row, uint32_t k) {
   return (row >> 3) * 1024 + (row & 7) * 128 + ((((byte >> 4) ^ (row & 7)) & 7) << 4) + (byte & 15);
 }
 
-enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2 };
+// Epilogues: store, ReLU, residual add (C += acc, C loaded by TMA), and the
+// ReLU backward gate (C = gate > 0 ? acc : 0, the gate [M, N] loaded by TMA).
+enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2, kEpiGate = 3 };
 
 struct GemmArgs {
   int M, K;
@@ -211,7 +213,9 @@ constexpr int kThreadsT = 320;                // TMA warp, 4 split warps, MMA wa
 // Warp roles: 0 TMA issuer, 1-4 split A f32 -> fp16 hi/lo, 5 MMA issuer, 6-9 epilogue.
 template <int EPI>
 __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant__ CUtensorMap amap,
-                                                           const __grid_constant__ CUtensorMap cmap, GemmArgs a) {
+                                                           const __grid_constant__ CUtensorMap cmap,
+                                                           const __grid_constant__ CUtensorMap gmap, GemmArgs a) {
+  constexpr bool kLoadTile = EPI == kEpiResid || EPI == kEpiGate;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -389,18 +393,19 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
         if (lane == 0) {
           // the TMA store that last read this buffer must be done with it
           asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          if (EPI == kEpiResid) {
+          if (kLoadTile) {
+            const CUtensorMap* lmap = EPI == kEpiGate ? &gmap : &cmap;
             mbar_arrive_expect_tx(&cload[ew * 2 + b], kEpiBuf);
             asm volatile(
                 "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                ::"r"(smem_u32(buf)), "l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0),
+                ::"r"(smem_u32(buf)), "l"(reinterpret_cast<uint64_t>(lmap)), "r"(x), "r"(row0),
                 "r"(smem_u32(&cload[ew * 2 + b]))
                 : "memory");
           }
         }
         float v[32];
         tmem_ld32(tmem_base + (uint32_t(g * 32) << 16) + acc * kBN + cc * 32, v);
-        if (EPI == kEpiResid) {  // every lane observes the landing of the tile it reads
+        if (kLoadTile) {  // every lane observes the landing of the tile it reads
           const bool mine = mbar_wait(&cload[ew * 2 + b], (cphase >> b) & 1, a.err);
           cphase ^= 1u << b;
           if (!__all_sync(0xffffffffu, mine)) { ok = false; break; }
@@ -417,6 +422,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
           } else if (EPI == kEpiResid) {
             const float4 c = *cp;
             o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+          } else if (EPI == kEpiGate) {
+            const float4 c = *cp;
+            o.x = c.x > 0.f ? o.x : 0.f; o.y = c.y > 0.f ? o.y : 0.f;
+            o.z = c.z > 0.f ? o.z : 0.f; o.w = c.w > 0.f ? o.w : 0.f;
           }
           *cp = o;
         }

@@ -26,11 +26,13 @@ def check_report(got, want):
         assert abs(getattr(got, k) - want[k]) <= 1e-6, k
 
 
+@pytest.mark.parametrize("precision", ["exact", "certified"])
 @pytest.mark.parametrize("unfreeze_pool", [False, True])
-def test_learn_matches_oracle_learn(oracle, unfreeze_pool):
+def test_learn_matches_oracle_learn(oracle, unfreeze_pool, precision):
     cfg, w0 = world()
     w = BrainForwardWeights(cfg, w0.page.copy())
     be = CudaBrainBackend(cfg, w, 0)
+    be.set_precision(precision)
     try:
         learner = BatchLearner(be, w)
         page = w0.page.copy()
