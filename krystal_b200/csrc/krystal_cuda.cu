@@ -173,7 +173,8 @@ struct kc_handle {
   Workspace ws_fb;   // frames recomputed on the exact path
   BackWs bw;         // the backward
   DevBuf wt;         // transposed copies of the block and selector matrices (page layout)
-  bool wt_dirty = true;
+  bool wt_blocks_dirty = true;  // the blocks' transposed copies are stale
+  bool wt_sel_dirty = true;     // the selector's transposed copies are stale
   kc::FrameTotals* h_tot = nullptr;  // pinned
   std::string err;
   uint64_t launches = 0;
@@ -185,7 +186,7 @@ struct kc_handle {
   std::vector<float> mat_max;       // max |W| per matrix (host side, from the last sync)
   std::vector<uint64_t> img_off;    // byte offset of each matrix's image
   DevBuf images;
-  bool images_dirty = true;
+  std::vector<char> mat_dirty;      // per matrix: its image is stale
   int* d_err = nullptr;             // tensor-core pipeline error word
   int* h_err = nullptr;             // pinned
   std::vector<uint32_t> h_flags;
@@ -296,7 +297,7 @@ kc_status dgemm_ld(kc_handle* h, const float* A, uint32_t lda, const float* B, f
 // Transposed copies of every block and selector matrix, at their page offsets
 // in h->wt (the backward's input products multiply by them).
 kc_status build_transposes(kc_handle* h) {
-  if (!h->wt_dirty) return KC_OK;
+  if (!h->wt_blocks_dirty && !h->wt_sel_dirty) return KC_OK;
   const Dims& d = h->d;
   KC_TRY(ensure(h->wt, d.total * 4), "transposed weights");
   float* wt = P<float>(h->wt);
@@ -306,7 +307,7 @@ kc_status build_transposes(kc_handle* h) {
     h->launches++;
   };
   const uint64_t hh = uint64_t(d.h) * d.h, fh = uint64_t(d.ffn) * d.h;
-  for (int pass = 0; pass < 2; pass++) {
+  for (int pass = 0; pass < 2 && h->wt_blocks_dirty; pass++) {
     const uint64_t base = pass ? d.off_mixer : d.off_enc;
     for (uint32_t b = 0; b < (pass ? d.mix : d.enc); b++) {
       const uint64_t o = base + d.block * b;
@@ -321,16 +322,20 @@ kc_status build_transposes(kc_handle* h) {
       tr(o + 3 * hh + fh, d.h, d.ffn);
     }
   }
-  tr(d.off_swq, d.h, d.h);
-  tr(d.off_swk, d.h, d.h);
+  if (h->wt_sel_dirty) {
+    tr(d.off_swq, d.h, d.h);
+    tr(d.off_swk, d.h, d.h);
+  }
   KC_TRY(cudaGetLastError(), "transposed weights");
-  h->wt_dirty = false;
+  h->wt_blocks_dirty = h->wt_sel_dirty = false;
   return KC_OK;
 }
 
-// Rebuild the split fp16 images of every matrix (after a sync changed them).
+// Rebuild the split fp16 images of the matrices a sync changed.
 kc_status build_images(kc_handle* h) {
-  if (!h->images_dirty) return KC_OK;
+  bool any = false;
+  for (char c : h->mat_dirty) any |= c != 0;
+  if (!any) return KC_OK;
   KC_CHECK(build_transposes(h));
   const auto& m = h->mats;
   if (h->img_off.size() != m.size()) {
@@ -343,6 +348,8 @@ kc_status build_images(kc_handle* h) {
     KC_TRY(ensure(h->images, off), "weight images");
   }
   for (size_t i = 0; i < m.size(); i++) {
+    if (!h->mat_dirty[i]) continue;
+    h->mat_dirty[i] = 0;
     const int sw = int(std::floor(std::log2(2048.0 / std::max(double(h->mat_max[i]), 1e-30))));
     const int swc = std::min(std::max(sw, -40), 40);
     const float* src = (m[i].transposed ? P<float>(h->wt) : h->w) + m[i].page_off;
@@ -351,7 +358,6 @@ kc_status build_images(kc_handle* h) {
     h->launches++;
   }
   KC_TRY(cudaGetLastError(), "weight images");
-  h->images_dirty = false;
   return KC_OK;
 }
 
@@ -894,9 +900,13 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
       h->mat_max[i + 1] = amax(w->selector_wk, hh, 0.f);
     }
     const size_t nf = h->mats.size() / 2;  // a transposed matrix has its original's largest entry
-    for (size_t j = 0; j < nf; j++) h->mat_max[nf + j] = h->mat_max[j];
-    h->images_dirty = true;
-    h->wt_dirty = true;
+    const size_t nsel = nf - 2;            // the selector's two matrices end each half
+    for (size_t j = 0; j < nf; j++) {
+      h->mat_max[nf + j] = h->mat_max[j];
+      if (j < nsel ? blocks : sel) h->mat_dirty[j] = h->mat_dirty[nf + j] = 1;
+    }
+    h->wt_blocks_dirty |= blocks;
+    h->wt_sel_dirty |= sel;
   }
   KC_TRY(cudaStreamSynchronize(h->stream), "sync");
   return KC_OK;
@@ -1226,6 +1236,7 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   if ((e = cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device))) return bail(e, "attributes");
   h->mats = mat_list(h->d);
   h->mat_max.assign(h->mats.size(), 0.f);
+  h->mat_dirty.assign(h->mats.size(), 1);
   for (const Mat& m : h->mats)
     if (m.n % 128 || m.k % 64) {
       kc_destroy(h);
