@@ -3,7 +3,7 @@
  *
  * This is the drop-in boundary. The reference session talks to a device
  * through the `BrainBackend` seam (packages/krystal/src/host/backend.ts:
- * 261-295); `@krystal/webgpu` implements it in packages/webgpu/src/
+ * 146-180); `@krystal/webgpu` implements it in packages/webgpu/src/
  * backend.ts:91-181. A `@krystal/cuda` adapter binds the functions below
  * through bun:ffi and implements the same seam:
  *
@@ -19,6 +19,7 @@
  *                                                extension `select?`)
  *   packed ragged batches of think()          -> kc_forward_batch /
  *                                                kc_forward_batch_device
+ *   think() turns arriving one at a time      -> kc_stream_* (rolling batches)
  *
  * Conventions. All arrays are row-major fp32 / u32, exactly the typed arrays
  * the TypeScript side holds. Host pointers unless a function says "device".
@@ -321,7 +322,60 @@ kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* st
  * several GPUs, these per-rank sums are what an all-reduce adds. */
 kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums);
 
-/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
+/* Streaming packer: frames that arrive one at a time (one think() per turn
+ * of many sessions, host/session.ts:128-181) leave in rolling packed batches.
+ * kc_stream_push copies a frame's active records into the open pinned staging
+ * buffer and validates them there (a malformed frame is refused alone);
+ * kc_stream_flush seals that buffer and queues it; a worker thread runs sealed
+ * buffers back to back through the batch path (the handle's precision) while
+ * the caller keeps pushing into the next buffer; kc_stream_poll hands back the
+ * oldest finished batch. No counterpart in the reference, which thinks about
+ * one frame per call. Destroy a stream before its handle. */
+typedef struct kc_stream kc_stream;
+
+typedef struct kc_stream_result {
+  uint64_t first_ticket;   /* the batch holds tickets first_ticket .. first_ticket + frames - 1 */
+  uint32_t frames;         /* 0: nothing finished */
+  uint64_t questions, total_p;
+  const uint64_t* p_off;   /* [frames+1] */
+  const uint64_t* q_off;   /* [frames+1] */
+  const float* p;          /* [total_p] */
+  const uint32_t* index;   /* [questions] */
+  kc_status status;        /* the batch's own status; error: its message or NULL */
+  const char* error;
+  double sealed_ms, done_ms; /* kc_stream_clock_ms() at flush and when the results landed */
+} kc_stream_result;
+
+/* depth >= 2 staging buffers, each for up to max_frames frames, max_records
+ * records and max_p p entries (0: 64 per record). Pinned host memory only. */
+kc_status kc_stream_create(kc_handle* h, uint32_t max_frames, uint64_t max_records, uint64_t max_p, uint32_t depth,
+                           kc_stream** out);
+/* Queue one packed frame (kc_frame_view as for kc_encode). schema_allow /
+ * band_allow: the frame's questions' rule ([Q*8], [Q]) or both NULL (open).
+ * *ticket numbers the frame (consecutive from 0). KC_ERR_CAPACITY when the
+ * open buffer is full (flush) or every buffer is in flight (poll). */
+kc_status kc_stream_push(kc_stream* s, const kc_frame_view* frame, const uint32_t* schema_allow,
+                         const uint32_t* band_allow, uint64_t* ticket);
+/* Queue a run of packed frames in one call, as kc_stream_push would one by
+ * one: frame f is records rec_off[f] .. rec_off[f+1]-1 of the arrays
+ * (rec_off[0] need not be 0), every record active; the rule, if given, is per
+ * question of these frames in order. *pushed counts the frames queued before
+ * a refusal; their tickets start at *first_ticket. */
+kc_status kc_stream_push_many(kc_stream* s, const kc_batch_view* frames, uint64_t* first_ticket, uint32_t* pushed);
+/* Seal the open buffer and queue it for the device; returns at once. */
+kc_status kc_stream_flush(kc_stream* s);
+/* Batches sealed but not finished. */
+uint32_t kc_stream_pending(kc_stream* s);
+/* The oldest finished batch (wait != 0: block until one finishes, unless none
+ * is queued). Its arrays stay valid until the next poll. */
+kc_status kc_stream_poll(kc_stream* s, int wait, kc_stream_result* out);
+/* The steady clock the stream's timestamps use, in milliseconds. */
+double kc_stream_clock_ms(void);
+const char* kc_stream_last_error(kc_stream* s);
+/* Finishes the batch running, discards the rest. */
+void kc_stream_destroy(kc_stream* s);
+
+/* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
  * certification margin (default 2e-5, in score units; 0 keeps it). */
 kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 

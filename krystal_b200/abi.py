@@ -35,7 +35,9 @@ EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "
            "kc_forward_batch_device", "kc_set_stream", "kc_get_stream", "kc_synchronize", "kc_profile",
            "kc_profile_read", "kc_launch_count", "kc_destroy", "kc_last_error", "kc_select_noalloc",
            "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
-           "kc_learn_accumulate")
+           "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_pending",
+           "kc_stream_poll", "kc_stream_clock_ms", "kc_stream_last_error", "kc_stream_destroy",
+           "kc_stream_push_many")
 
 
 class KrystalCudaError(RuntimeError):
@@ -116,6 +118,12 @@ class KcBackwardResult(C.Structure):
                 ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
 
 
+class KcStreamResult(C.Structure):
+    _fields_ = [("first_ticket", C.c_uint64), ("frames", C.c_uint32), ("questions", C.c_uint64),
+                ("total_p", C.c_uint64), ("p_off", P), ("q_off", P), ("p", P), ("index", P), ("status", C.c_int),
+                ("error", C.c_char_p), ("sealed_ms", C.c_double), ("done_ms", C.c_double)]
+
+
 class KcStageTimes(C.Structure):
     _fields_ = [(n, C.c_double) for n in ("pack_ms", "embed_ms", "enc_gemm_ms", "enc_attn_ms", "pool_ms",
                                           "mixer_ms", "selector_ms", "total_ms")] + [
@@ -156,6 +164,19 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_backward_batch_device.argtypes = [P, C.POINTER(KcBatchView), P, P, P, C.POINTER(KcBackwardResult)]
     lib.kc_learn_frame_stats.argtypes = [P, P, P]
     lib.kc_learn_accumulate.argtypes = [P, P, P, P]
+    lib.kc_stream_create.argtypes = [P, C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint32, C.POINTER(P)]
+    lib.kc_stream_push.argtypes = [P, C.POINTER(KcFrameView), P, P, C.POINTER(C.c_uint64)]
+    lib.kc_stream_push_many.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]
+    lib.kc_stream_flush.argtypes = [P]
+    lib.kc_stream_pending.argtypes = [P]
+    lib.kc_stream_pending.restype = C.c_uint32
+    lib.kc_stream_poll.argtypes = [P, i, C.POINTER(KcStreamResult)]
+    lib.kc_stream_clock_ms.argtypes = []
+    lib.kc_stream_clock_ms.restype = C.c_double
+    lib.kc_stream_last_error.argtypes = [P]
+    lib.kc_stream_last_error.restype = C.c_char_p
+    lib.kc_stream_destroy.argtypes = [P]
+    lib.kc_stream_destroy.restype = None
     lib.kc_set_stream.argtypes = [P, P]
     lib.kc_get_stream.argtypes = [P]
     lib.kc_get_stream.restype = P
@@ -171,7 +192,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     for name in ("kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch", "kc_forward_batch_device",
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
                  "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
-           "kc_learn_accumulate"):
+                 "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_poll",
+                 "kc_stream_push_many"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

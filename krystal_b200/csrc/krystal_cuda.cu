@@ -169,6 +169,8 @@ struct kc_handle {
   float* w = nullptr;
   uint32_t* token_rows = nullptr;
   uint32_t token_rows_len = 0;
+  std::vector<uint32_t> token_rows_host;  // for validating frames on the host (streams)
+  std::vector<uint8_t> id_ok;             // per id: bit 0 a valid token, bit 1 a valid field role
   Workspace ws;      // the batch
   Workspace ws_fb;   // frames recomputed on the exact path
   BackWs bw;         // the backward
@@ -1227,6 +1229,11 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   h->stream = h->own;
   if ((e = cudaMalloc(&h->w, h->d.total * 4))) return bail(e, "weights");
   h->token_rows_len = config->token_rows_len;
+  h->token_rows_host.assign(config->token_rows, config->token_rows + config->token_rows_len);
+  h->id_ok.resize(h->token_rows_len);
+  for (uint32_t i = 0; i < h->token_rows_len; i++)
+    h->id_ok[i] = uint8_t((h->token_rows_host[i] < h->d.token_space ? 1u : 0u) |
+                          (h->token_rows_host[i] < h->d.field_space ? 2u : 0u));
   if ((e = cudaMalloc(&h->token_rows, uint64_t(h->token_rows_len) * 4))) return bail(e, "tokenRows");
   if ((e = cudaMemcpy(h->token_rows, config->token_rows, uint64_t(h->token_rows_len) * 4, cudaMemcpyHostToDevice)))
     return bail(e, "tokenRows");
@@ -1481,10 +1488,11 @@ static kc_status batch_host_common(kc_handle* h, const kc_batch_view* bv, DevBat
   return KC_OK;
 }
 
-kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* out) {
-  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
-  std::lock_guard<std::mutex> lk(h->mu);
-  DeviceGuard dg(h->device);
+}  // extern "C"
+
+namespace {
+// kc_forward_batch with the handle's lock held and its device current.
+kc_status forward_batch_host(kc_handle* h, const kc_batch_view* bv, kc_batch_out* out) {
   if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
   if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
     return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
@@ -1524,6 +1532,16 @@ kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* 
   KC_TRY(cudaStreamSynchronize(h->stream), "batch");
   prof_collect(h);
   return KC_OK;
+}
+}  // namespace
+
+extern "C" {
+
+kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  return forward_batch_host(h, bv, out);
 }
 
 kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_device_result* out) {
@@ -1741,6 +1759,14 @@ void kc_destroy(kc_handle* h) {
                        &h->images};
     for (DevBuf* b : fbufs)
       if (b->p) cudaFree(b->p);
+    BackWs& k = h->bw;
+    DevBuf* bbufs[] = {&k.mask, &k.targets, &k.valence, &k.enc_qkv, &k.enc_p, &k.enc_h1, &k.mix_q, &k.mix_k,
+                       &k.mix_v, &k.mix_p, &k.mix_h1, &k.gather, &k.offered, &k.n_allowed, &k.pred, &k.dpred,
+                       &k.loss, &k.dwv, &k.dquery, &k.dig, &k.dag, &k.dscore, &k.dqp, &k.dkp, &k.dbk, &k.dbv,
+                       &k.dswq, &k.dswk, &k.dh1, &k.ads, &k.mdq, &k.mdk, &k.mdv, &k.tok_ds, &k.dfs, &k.dpool,
+                       &k.edqkv, &k.learn_partial, &h->wt};
+    for (DevBuf* b : bbufs)
+      if (b->p) cudaFree(b->p);
     if (h->d_err) cudaFree(h->d_err);
     if (h->h_err) cudaFreeHost(h->h_err);
     if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
@@ -1759,3 +1785,5 @@ void kc_destroy(kc_handle* h) {
 const char* kc_last_error(kc_handle* h) { return h ? h->err.c_str() : g_create_error.c_str(); }
 
 }  // extern "C"
+
+#include "stream.cuh"

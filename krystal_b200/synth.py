@@ -48,7 +48,15 @@ WORKLOADS = {
     "long_bank_1024": Workload("long_bank_1024", 1024, (4160, 4160), (64, 64), 16384, 64, bank=4096),
     # learn step: 1024 frames, records 16-256 with 4 questions each, V=4096, schema 0-63
     "learn_1024": Workload("learn_1024", 1024, (16, 256), (4, 4), 4096, 64),
+    # interactive stream: 100k frames, records 8-512 with 1-32 questions, V=4096, schema 0-63
+    "stream_100k": Workload("stream_100k", 100000, (8, 512), (1, 32), 4096, 64),
 }
+
+
+def poisson_arrivals(frames: int, rate_per_s: float, seed: int = 4) -> np.ndarray:
+    """Arrival times (ms from 0) of a Poisson process at rate_per_s."""
+    rng = np.random.default_rng(seed)
+    return np.cumsum(rng.exponential(1e3 / rate_per_s, frames))
 
 
 def workload_config(w: Workload, base: BrainForwardConfig = BRAIN_FORWARD_CONFIG) -> BrainForwardConfig:
