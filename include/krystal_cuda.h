@@ -322,6 +322,33 @@ kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* st
  * several GPUs, these per-rank sums are what an all-reduce adds. */
 kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums);
 
+/* KRY1 checkpoints (host/checkpoint.ts:17-116): 11 little-endian u32 header
+ * words (magic "KRY1" = 0x4b525931, version 1, hiddenSize, ffnSize,
+ * encoderBlocks, mixerBlocks, headCount, headDim, routeKindCount, tokenRows
+ * length, weight element count), the tokenRows, then every weight array in
+ * createBrainForwardWeights order, which is the device page's order. */
+#define KC_CHECKPOINT_MAGIC 0x4b525931u
+#define KC_CHECKPOINT_VERSION 1u
+typedef enum kc_checkpoint_refusal {  /* CheckpointRefusal (checkpoint.ts:44-49) */
+  KC_CHECKPOINT_FITS = 0,
+  KC_CHECKPOINT_NOT_KRYSTAL = 1,      /* "not a krystal checkpoint" */
+  KC_CHECKPOINT_LATER_FORMAT = 2,     /* "a later checkpoint format" */
+  KC_CHECKPOINT_GEOMETRY = 3,         /* "a different geometry" */
+  KC_CHECKPOINT_VOCABULARY = 4,       /* "a different vocabulary" */
+  KC_CHECKPOINT_TRUNCATED = 5         /* "truncated" */
+} kc_checkpoint_refusal;
+
+/* decodeCheckpoint (checkpoint.ts:78-116) straight into the device weight
+ * page: the same checks against the handle's geometry and tokenRows, then one
+ * host-to-device copy; `bytes` may start anywhere. A refusal leaves the
+ * device weights untouched and returns KC_OK with *refusal set; the host's own
+ * arrays are the caller's to decode. */
+kc_status kc_load_checkpoint(kc_handle* h, const void* bytes, uint64_t len, int* refusal);
+/* encodeCheckpoint (checkpoint.ts:51-69) from the device weight page:
+ * *written = the checkpoint's size; nothing is written when cap is smaller
+ * (KC_ERR_CAPACITY), so a NULL out with cap 0 asks for the size. */
+kc_status kc_save_checkpoint(kc_handle* h, void* out, uint64_t cap, uint64_t* written);
+
 /* Streaming packer: frames that arrive one at a time (one think() per turn
  * of many sessions, host/session.ts:128-181) leave in rolling packed batches.
  * kc_stream_push copies a frame's active records into the open pinned staging

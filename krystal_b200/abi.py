@@ -29,6 +29,8 @@ KC_MAX_BANK = 4096
 KC_NO_TARGET = 0xFFFFFFFF
 KC_AWAY_TARGET = 0x80000000
 KC_LEARN_STATS = 8
+CHECKPOINT_REFUSALS = {1: "not a krystal checkpoint", 2: "a later checkpoint format", 3: "a different geometry",
+                       4: "a different vocabulary", 5: "truncated"}
 
 # Every function include/krystal_cuda.h declares.
 EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "kc_forward_batch",
@@ -37,7 +39,7 @@ EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "
            "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
            "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_pending",
            "kc_stream_poll", "kc_stream_clock_ms", "kc_stream_last_error", "kc_stream_destroy",
-           "kc_stream_push_many")
+           "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint")
 
 
 class KrystalCudaError(RuntimeError):
@@ -168,6 +170,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_stream_push.argtypes = [P, C.POINTER(KcFrameView), P, P, C.POINTER(C.c_uint64)]
     lib.kc_stream_push_many.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]
     lib.kc_stream_flush.argtypes = [P]
+    lib.kc_load_checkpoint.argtypes = [P, P, C.c_uint64, C.POINTER(C.c_int)]
+    lib.kc_save_checkpoint.argtypes = [P, P, C.c_uint64, C.POINTER(C.c_uint64)]
     lib.kc_stream_pending.argtypes = [P]
     lib.kc_stream_pending.restype = C.c_uint32
     lib.kc_stream_poll.argtypes = [P, i, C.POINTER(KcStreamResult)]
@@ -193,7 +197,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
                  "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
                  "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_poll",
-                 "kc_stream_push_many"):
+                 "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

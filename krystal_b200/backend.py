@@ -234,6 +234,23 @@ class CudaBrainBackend:
         """kc_learn_accumulate over the last batch differentiated (device pointers)."""
         abi.check(self._lib.kc_learn_accumulate(self._h, step, value_weight, sums), self._h)
 
+    def load_checkpoint(self, data) -> str | None:
+        """A KRY1 checkpoint straight into the device weight page
+        (kc_load_checkpoint); None when taken up, else the refusal."""
+        buf = np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8)
+        refusal = C.c_int()
+        abi.check(self._lib.kc_load_checkpoint(self._h, buf.ctypes.data if buf.size else None, buf.size,
+                                               C.byref(refusal)), self._h)
+        return abi.CHECKPOINT_REFUSALS.get(refusal.value)
+
+    def save_checkpoint(self) -> bytes:
+        """KRY1 bytes of the device weight page (kc_save_checkpoint)."""
+        n = C.c_uint64()
+        self._lib.kc_save_checkpoint(self._h, None, 0, C.byref(n))
+        out = np.empty(n.value, dtype=np.uint8)
+        abi.check(self._lib.kc_save_checkpoint(self._h, out.ctypes.data, out.size, C.byref(n)), self._h)
+        return out.tobytes()
+
     # --- seam extension: the selector on the device -------------------------
     def select(self, encoded: EncodedFrame, mask: np.ndarray | None = None, rule: MaskRule | None = None,
                bank_schema_ids=None, bank_band_ids=None, uniforms=None, gather: bool = True) -> Selection:

@@ -1685,6 +1685,74 @@ kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* va
   return KC_OK;
 }
 
+kc_status kc_load_checkpoint(kc_handle* h, const void* bytes, uint64_t len, int* refusal) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!refusal || (!bytes && len)) return fail(h, KC_ERR_INVALID_ARG, "checkpoint arguments are incomplete");
+  const Dims& d = h->d;
+  const unsigned char* b = static_cast<const unsigned char*>(bytes);
+  auto word = [&](uint64_t i) {  // the reader copes with any alignment
+    uint32_t v;
+    memcpy(&v, b + 4 * i, 4);
+    return v;
+  };
+  constexpr uint64_t kHeader = 11;
+  *refusal = KC_CHECKPOINT_FITS;
+  if (len < kHeader * 4) return *refusal = KC_CHECKPOINT_TRUNCATED, KC_OK;
+  if (word(0) != KC_CHECKPOINT_MAGIC) return *refusal = KC_CHECKPOINT_NOT_KRYSTAL, KC_OK;
+  if (word(1) > KC_CHECKPOINT_VERSION) return *refusal = KC_CHECKPOINT_LATER_FORMAT, KC_OK;
+  const uint32_t geometry[7] = {d.h, d.ffn, d.enc, d.mix, d.heads, d.hd, d.route};
+  for (int i = 0; i < 7; i++)
+    if (word(2 + i) != geometry[i]) return *refusal = KC_CHECKPOINT_GEOMETRY, KC_OK;
+  const uint64_t rows = word(9), elements = word(10);
+  if (rows != h->token_rows_len) return *refusal = KC_CHECKPOINT_VOCABULARY, KC_OK;
+  if (len < (kHeader + rows + elements) * 4) return *refusal = KC_CHECKPOINT_TRUNCATED, KC_OK;
+  for (uint64_t i = 0; i < rows; i++)
+    if (word(kHeader + i) != h->token_rows_host[i]) return *refusal = KC_CHECKPOINT_VOCABULARY, KC_OK;
+  if (elements != d.total) return *refusal = KC_CHECKPOINT_GEOMETRY, KC_OK;
+  const unsigned char* fl = b + (kHeader + rows) * 4;
+  KC_TRY(cudaMemcpyAsync(h->w, fl, elements * 4, cudaMemcpyHostToDevice, h->stream), "checkpoint");
+  // every matrix moved: largest entries for the split scales, all images stale
+  auto amax = [&](uint64_t off, uint64_t n) {
+    float m = 0.f;
+    for (uint64_t i = 0; i < n; i++) {
+      float v;
+      memcpy(&v, fl + 4 * (off + i), 4);
+      m = std::max(m, std::fabs(v));
+    }
+    return m;
+  };
+  const size_t nf = h->mats.size() / 2;
+  for (size_t i = 0; i < nf; i++) {
+    const Mat& m = h->mats[i];
+    h->mat_max[i] = h->mat_max[nf + i] = amax(m.page_off, uint64_t(m.n) * m.k);
+  }
+  std::fill(h->mat_dirty.begin(), h->mat_dirty.end(), 1);
+  h->wt_blocks_dirty = h->wt_sel_dirty = true;
+  KC_TRY(cudaStreamSynchronize(h->stream), "checkpoint");
+  return KC_OK;
+}
+
+kc_status kc_save_checkpoint(kc_handle* h, void* out, uint64_t cap, uint64_t* written) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!written) return fail(h, KC_ERR_INVALID_ARG, "written is null");
+  const Dims& d = h->d;
+  const uint64_t rows = h->token_rows_len, bytes = (11 + rows + d.total) * 4;
+  *written = bytes;
+  if (cap < bytes || !out) return fail(h, KC_ERR_CAPACITY, "the checkpoint buffer is smaller than the checkpoint");
+  const uint32_t header[11] = {KC_CHECKPOINT_MAGIC, KC_CHECKPOINT_VERSION, d.h, d.ffn, d.enc, d.mix, d.heads,
+                               d.hd, d.route, uint32_t(rows), uint32_t(d.total)};
+  unsigned char* o = static_cast<unsigned char*>(out);
+  memcpy(o, header, sizeof header);
+  memcpy(o + 44, h->token_rows_host.data(), rows * 4);
+  KC_TRY(cudaMemcpyAsync(o + 44 + rows * 4, h->w, d.total * 4, cudaMemcpyDeviceToHost, h->stream), "checkpoint");
+  KC_TRY(cudaStreamSynchronize(h->stream), "checkpoint");
+  return KC_OK;
+}
+
 kc_status kc_set_precision(kc_handle* h, int mode, float tau) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);

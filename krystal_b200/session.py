@@ -5,8 +5,8 @@ Mirrors packages/krystal/src/host/session.ts (``BrainSession`` :106-255,
 selector moved onto the device through the backend's ``select`` — the
 optional seam extension; the mask is built by ``selection_mask`` exactly as
 the reference builds it (host/learn.ts:215-232), so choosing and learning see
-the same grammar. ``learn``/``teach``/checkpointing are outside this
-backend's scope; their device half is the backward pass.
+the same grammar. ``snapshot``/``restore`` write and read KRY1 checkpoints
+(session.ts:226-249); learning lives in ``krystal_b200.learn``.
 """
 from __future__ import annotations
 
@@ -16,6 +16,7 @@ from typing import Callable, Sequence
 import numpy as np
 
 from .backend import CudaBrainBackend, EncodedFrame, cuda_backend
+from .checkpoint import decode_checkpoint, encode_checkpoint
 from .frame import HostFrame, pack_host_frame
 from .model import BRAIN_FORWARD_CONFIG, BrainForwardConfig, BrainForwardWeights, create_brain_forward_weights, \
     validate_brain_forward_weights
@@ -106,6 +107,20 @@ class BrainSession:
 
     def sync(self, changes=None) -> None:
         self.backend.sync(self.weights, changes)
+
+    def snapshot(self) -> bytes:
+        """session.ts:235-237: the weights, their geometry and vocabulary as KRY1."""
+        return encode_checkpoint(self.weights, self.config, self.config.token_rows)
+
+    def restore(self, data) -> str | None:
+        """session.ts:245-249: take up a checkpoint in place, or say why it does
+        not fit. The device page takes the same bytes directly."""
+        refusal = decode_checkpoint(data, self.weights, self.config, self.config.token_rows)
+        if refusal is None:
+            device_refusal = self.backend.load_checkpoint(data)
+            if device_refusal is not None:  # the host took it: the device must hold the same weights
+                self.backend.sync(self.weights)
+        return refusal
 
     def destroy(self) -> None:
         self.backend.destroy()
