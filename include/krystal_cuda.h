@@ -49,6 +49,7 @@ extern "C" {
 #define KC_QUERY_BAND 5u          /* index of "query" in BRAIN_FRAME_BANDS (:150-172) */
 #define KC_NO_SELECTION 0xffffffffu /* index of an all-blocked row (forward/oracle.ts:364-365) */
 #define KC_MAX_BANK 4096u         /* largest bank one frame may hold */
+#define KC_NO_WORD 0xffffffffu    /* INVALID_WORD_ID (forward/masks.ts:145) */
 
 /* Precision of the batch entry points (kc_forward_batch[_device]).
  * EXACT: the oracle's arithmetic (f64 accumulation in its order, f32 stores).
@@ -159,6 +160,15 @@ typedef struct kc_batch_view {
   const uint32_t* schema_allow;  /* optional rule, [batch questions * 8] */
   const uint32_t* band_allow;    /* optional rule, [batch questions] */
   const double* uniforms;        /* optional: sample instead of argmax, [batch questions] */
+  /* Optional same-word bias on the encoder's record-local attention (WordBias,
+   * forward/masks.ts:145-198): word_ids [records*8] parallel to token_ids,
+   * 0xffffffff = no word; two tokens of one record with the same word id get
+   * word_alpha (stored f32) added to their attention logit. word_alpha = 0 or
+   * word_ids NULL: no bias. The backward entry points ignore it, as the
+   * session's gradient source passes no record mask (host/gradients.ts:30-66),
+   * and so does the streaming packer. */
+  const uint32_t* word_ids;
+  float word_alpha;
 } kc_batch_view;
 
 /* Outputs of a batch. p of frame f is a [Q_f, R_f] block at p_off[f]; the

@@ -29,6 +29,7 @@ KC_MAX_BANK = 4096
 KC_NO_TARGET = 0xFFFFFFFF
 KC_AWAY_TARGET = 0x80000000
 KC_LEARN_STATS = 8
+KC_NO_WORD = 0xFFFFFFFF
 CHECKPOINT_REFUSALS = {1: "not a krystal checkpoint", 2: "a later checkpoint format", 3: "a different geometry",
                        4: "a different vocabulary", 5: "truncated"}
 
@@ -92,7 +93,7 @@ class KcMaskRule(C.Structure):
 class KcBatchView(C.Structure):
     _fields_ = [("frames", C.c_uint32), ("records", C.c_uint64), ("rec_off", P), ("token_ids", P),
                 ("field_roles", P), ("schema_ids", P), ("band_ids", P), ("schema_allow", P), ("band_allow", P),
-                ("uniforms", P)]
+                ("uniforms", P), ("word_ids", P), ("word_alpha", C.c_float)]
 
 
 class KcBatchOut(C.Structure):

@@ -285,8 +285,10 @@ class CudaBrainBackend:
 
     # --- packed ragged batches ------------------------------------------------
     def forward_batch(self, batch: FrameBatch, rule: MaskRule | None = None, uniforms=None,
-                      want_query_output: bool = False, p_capacity: int | None = None) -> dict:
-        """Pack, encode and select a whole batch; host arrays in and out."""
+                      want_query_output: bool = False, p_capacity: int | None = None, word_ids=None,
+                      word_alpha: float = 0.0) -> dict:
+        """Pack, encode and select a whole batch; host arrays in and out.
+        word_ids [records*8] / word_alpha: the same-word bias (WordBias)."""
         keep = [_u32(batch.token_ids), _u32(batch.field_roles), _u32(batch.schema_ids), _u32(batch.band_ids),
                 np.ascontiguousarray(batch.rec_off, dtype=np.uint64)]
         tok, role, sch, band, off = keep
@@ -295,8 +297,12 @@ class CudaBrainBackend:
             sa, ba = _u32(rule.schema_allow), _u32(rule.band_allow)
         if uniforms is not None:
             u = np.ascontiguousarray(uniforms, dtype=np.float64)
+        wid = _u32(word_ids) if word_ids is not None else None
+        if wid is not None and wid.size != batch.records * 8:
+            raise ValueError("word_ids must hold one label per token slot (records * 8)")
         bv = abi.KcBatchView(batch.frames, batch.records, off.ctypes.data, tok.ctypes.data, role.ctypes.data,
-                             sch.ctypes.data, band.ctypes.data, abi.ptr(sa), abi.ptr(ba), abi.ptr(u))
+                             sch.ctypes.data, band.ctypes.data, abi.ptr(sa), abi.ptr(ba), abi.ptr(u), abi.ptr(wid),
+                             float(word_alpha))
         nq = int((band == 5).sum())
         if p_capacity is None:
             rec = np.diff(off.astype(np.int64))
@@ -319,10 +325,11 @@ class CudaBrainBackend:
 
     def forward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,
                              schema_ids: int, band_ids: int, schema_allow: int | None = None,
-                             band_allow: int | None = None, uniforms: int | None = None) -> abi.KcDeviceResult:
+                             band_allow: int | None = None, uniforms: int | None = None,
+                             word_ids: int | None = None, word_alpha: float = 0.0) -> abi.KcDeviceResult:
         """Device-resident batch (raw device pointers); results stay on the device."""
         bv = abi.KcBatchView(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow,
-                             band_allow, uniforms)
+                             band_allow, uniforms, word_ids, float(word_alpha))
         res = abi.KcDeviceResult()
         abi.check(self._lib.kc_forward_batch_device(self._h, C.byref(bv), C.byref(res)), self._h)
         return res

@@ -27,6 +27,12 @@ __device__ __forceinline__ float js_relu(float v) {
 
 __device__ __forceinline__ float f32(double v) { return __double2float_rn(v); }
 
+// The record mask's entry for two tokens of one record (compileRecordMask,
+// masks.ts:167-198): alpha when both carry the same valid word id, else 0.
+__device__ __forceinline__ float word_bias(uint32_t wi, uint32_t wj, float alpha) {
+  return (alpha != 0.0f && wi != KC_INVALID && wi == wj) ? alpha : 0.0f;
+}
+
 // Exclusive block scan of one value per thread (NT threads, NT % 32 == 0).
 // `tmp` holds NT/32 entries. Returns the exclusive prefix; *total gets the sum.
 template <int NT, typename T>

@@ -178,7 +178,11 @@ struct LocalAttnArgs {
   uint64_t records;
   double scale;              // 1/sqrt(headDim)
   float* p_out;              // optional [T][4][8]: the softmax row over the record's window
+  const uint32_t* tok_recpos; // [T] record*8 | position, for the word ids
+  const uint32_t* word_ids;   // optional [records*8]: the same-word bias's labels
+  float word_alpha;           // the bias, f32 as the record mask stores it
 };
+
 
 __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
   __shared__ float sm[4][KC_RW][3 * KC_H];  // 48 KB
@@ -196,12 +200,22 @@ __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
   __syncwarp();
   const int ti = lane >> 2, head = lane & 3, hb = head * KC_HEAD_DIM;
   float p[KC_RW];
+  // word ids of the record's tokens: lane 4j holds token j's (all lanes shuffle)
+  uint32_t wmine = KC_INVALID, wj[KC_RW];
+  if (a.word_ids) {
+    if (ti < cnt) wmine = a.word_ids[a.tok_recpos[start + ti]];
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) wj[j] = __shfl_sync(0xffffffffu, wmine, 4 * j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) wj[j] = KC_INVALID;
+  }
   if (ti < cnt) {
     for (int j = 0; j < cnt; j++) {
       double s = 0.0;
 #pragma unroll 8
       for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(rec[ti][hb + d]), double(rec[j][KC_H + hb + d]), s);
-      p[j] = f32(s * a.scale + 0.0);
+      p[j] = f32(s * a.scale + double(word_bias(wmine, wj[j], a.word_alpha)));
     }
     bool blocked = true;
     for (int j = 0; j < cnt; j++)

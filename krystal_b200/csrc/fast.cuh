@@ -32,6 +32,9 @@ struct LocalAttnFastArgs {
   const uint2* rec_meta;      // [N]
   uint64_t records;
   float scale;                // 1/sqrt(headDim)
+  const uint32_t* tok_recpos; // [T] record*8 | position, for the word ids
+  const uint32_t* word_ids;   // optional [records*8]: the same-word bias's labels
+  float word_alpha;
 };
 
 __device__ __forceinline__ int la_swz(int row, int f4) { return row * kLaRowF4 + (f4 ^ row); }
@@ -65,6 +68,14 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
   }
   __syncwarp();
   const int head = lane >> 3, ti = lane & 7;
+  // word ids of the record's tokens: lane j (head 0) holds token j's
+  uint32_t wmine = KC_INVALID, wj[KC_RW];
+  const bool words = a.word_ids != nullptr;
+  if (words) {
+    if (ti < cnt) wmine = a.word_ids[a.tok_recpos[start + ti]];
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) wj[j] = __shfl_sync(0xffffffffu, wmine, j);
+  }
   float4 o[8];
   if (ti < cnt) {
     float4 q[8];
@@ -82,6 +93,7 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
           s = fmaf(q[m].x, kv.x, s); s = fmaf(q[m].y, kv.y, s); s = fmaf(q[m].z, kv.z, s); s = fmaf(q[m].w, kv.w, s);
         }
         p[j] = s * a.scale;
+        if (words) p[j] += word_bias(wmine, wj[j], a.word_alpha);
         mx = fmaxf(mx, p[j]);
       }
     }
@@ -89,7 +101,8 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
 #pragma unroll
     for (int j = 0; j < KC_RW; j++)
       if (j < cnt) { p[j] = expf(p[j] - mx); sum += p[j]; }
-    const float inv = 1.f / fmaxf(sum, 1e-20f);
+    // attentionOracle's all-blocked row (only a bias can block one): p = 0
+    const float inv = words && !(mx >= -1e29f) ? 0.f : 1.f / fmaxf(sum, 1e-20f);
 #pragma unroll
     for (int m = 0; m < 8; m++) o[m] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -481,15 +494,17 @@ __global__ void k_fallback_gather(const uint32_t* __restrict__ list, const uint6
                                   const uint32_t* __restrict__ field_roles, const uint32_t* __restrict__ schema_ids,
                                   const uint32_t* __restrict__ band_ids, const uint32_t* __restrict__ schema_allow,
                                   const uint32_t* __restrict__ band_allow, const double* __restrict__ uniforms,
+                                  const uint32_t* __restrict__ word_ids,
                                   uint32_t* __restrict__ s_tok, uint32_t* __restrict__ s_role,
                                   uint32_t* __restrict__ s_schema, uint32_t* __restrict__ s_band,
                                   uint32_t* __restrict__ s_sallow, uint32_t* __restrict__ s_ballow,
-                                  double* __restrict__ s_uni) {
+                                  double* __restrict__ s_uni, uint32_t* __restrict__ s_words) {
   const uint32_t i = blockIdx.x, f = list[i];
   const uint64_t r0 = rec_off[f], n = rec_off[f + 1] - r0, d0 = sub_rec_off[i];
   for (uint64_t k = threadIdx.x; k < n * KC_RW; k += blockDim.x) {
     s_tok[d0 * KC_RW + k] = token_ids[r0 * KC_RW + k];
     s_role[d0 * KC_RW + k] = field_roles[r0 * KC_RW + k];
+    if (word_ids) s_words[d0 * KC_RW + k] = word_ids[r0 * KC_RW + k];
   }
   for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) {
     s_schema[d0 + k] = schema_ids[r0 + k];

@@ -91,6 +91,7 @@ Dims dims_of(const kc_config* c) {
 struct Workspace {
   // staged inputs (host entry points)
   DevBuf rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow, band_allow, uniforms, mask;
+  DevBuf word_ids;
   DevBuf bank_schema, bank_band;
   // pack
   DevBuf rec_meta, frame_t, frame_q, frame_r, t_off, q_off, r_off, p_off, totals;
@@ -405,6 +406,8 @@ struct DevBatch {
   const uint32_t *token_ids = nullptr, *field_roles = nullptr, *schema_ids = nullptr, *band_ids = nullptr;
   const uint32_t *schema_allow = nullptr, *band_allow = nullptr;
   const double* uniforms = nullptr;
+  const uint32_t* word_ids = nullptr;  // the same-word bias (null or alpha 0: none)
+  float word_alpha = 0.0f;
 };
 
 const char* bad_message(uint32_t code) {
@@ -541,7 +544,8 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     {
       ProfScope ps(h, kStEncAttn);
       kc::LocalAttnArgs la{bqkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
-                           sv ? sv->enc_p + blk * T * 32 : nullptr};
+                           sv ? sv->enc_p + blk * T * 32 : nullptr, P<uint32_t>(ws.tok_recpos),
+                           b.word_alpha != 0.0f ? b.word_ids : nullptr, b.word_alpha};
       kc::k_local_attn_exact<<<unsigned((N + 3) / 4), 128, 0, h->stream>>>(la);
       h->launches++;
     }
@@ -638,7 +642,9 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     }
     {
       ProfScope ps(h, kStEncAttn);
-      kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale};
+      kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
+                               P<uint32_t>(ws.tok_recpos), b.word_alpha != 0.0f ? b.word_ids : nullptr,
+                               b.word_alpha};
       kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, 0, h->stream>>>(
           la);
       h->launches++;
@@ -746,11 +752,14 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   KC_TRY(ensure(fb.schema_allow, nq * 32 + 32), "workspace");
   KC_TRY(ensure(fb.band_allow, nq * 4 + 4), "workspace");
   KC_TRY(ensure(fb.uniforms, nq * 8 + 8), "workspace");
+  const bool words = b.word_ids && b.word_alpha != 0.0f;
+  if (words) KC_TRY(ensure(fb.word_ids, nrec * 32), "workspace");
   kc::k_fallback_gather<<<n, 256, 0, h->stream>>>(
       P<uint32_t>(fb.list), b.rec_off, P<uint64_t>(ws.q_off), P<uint64_t>(fb.rec_off), P<uint64_t>(fb.rows_off),
       b.token_ids, b.field_roles, b.schema_ids, b.band_ids, b.schema_allow, b.band_allow, b.uniforms,
-      P<uint32_t>(fb.token_ids), P<uint32_t>(fb.field_roles), P<uint32_t>(fb.schema_ids), P<uint32_t>(fb.band_ids),
-      P<uint32_t>(fb.schema_allow), P<uint32_t>(fb.band_allow), P<double>(fb.uniforms));
+      words ? b.word_ids : nullptr, P<uint32_t>(fb.token_ids), P<uint32_t>(fb.field_roles),
+      P<uint32_t>(fb.schema_ids), P<uint32_t>(fb.band_ids), P<uint32_t>(fb.schema_allow),
+      P<uint32_t>(fb.band_allow), P<double>(fb.uniforms), words ? P<uint32_t>(fb.word_ids) : nullptr);
   h->launches++;
   DevBatch sub;
   sub.frames = n; sub.records = nrec; sub.rec_off = P<uint64_t>(fb.rec_off);
@@ -759,6 +768,8 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   sub.schema_allow = b.schema_allow ? P<uint32_t>(fb.schema_allow) : nullptr;
   sub.band_allow = b.band_allow ? P<uint32_t>(fb.band_allow) : nullptr;
   sub.uniforms = b.uniforms ? P<double>(fb.uniforms) : nullptr;
+  sub.word_ids = words ? P<uint32_t>(fb.word_ids) : nullptr;
+  sub.word_alpha = b.word_alpha;
   kc::FrameTotals sub_tot;
   KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
@@ -1485,6 +1496,11 @@ static kc_status batch_host_common(kc_handle* h, const kc_batch_view* bv, DevBat
   b.frames = F; b.records = N; b.rec_off = P<uint64_t>(ws.rec_off);
   b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
   b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  if (bv->word_ids && bv->word_alpha != 0.0f) {
+    if ((s = stage(h, ws.word_ids, bv->word_ids, N * 8))) return s;
+    b.word_ids = P<uint32_t>(ws.word_ids);
+    b.word_alpha = bv->word_alpha;
+  }
   return KC_OK;
 }
 
@@ -1560,6 +1576,8 @@ kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_devi
   b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
   b.band_ids = bv->band_ids; b.schema_allow = bv->schema_allow; b.band_allow = bv->band_allow;
   b.uniforms = bv->uniforms;
+  b.word_ids = bv->word_ids;
+  b.word_alpha = bv->word_alpha;
   kc::FrameTotals tot;
   kc_status s = run_batch(h, b, false, &tot);
   if (s) return s;
@@ -1814,7 +1832,7 @@ void kc_destroy(kc_handle* h) {
                       &h->ws.rec_start, &h->ws.rec_row, &h->ws.bank_rec, &h->ws.bank_frame, &h->ws.query_rec,
                       &h->ws.query_frame, &h->ws.x, &h->ws.qkv, &h->ws.bk, &h->ws.bv, &h->ws.mk, &h->ws.mv,
                       &h->ws.qstate, &h->ws.mq, &h->ws.mh, &h->ws.sq, &h->ws.sk, &h->ws.p, &h->ws.index,
-                      &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off};
+                      &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off, &h->ws.word_ids, &h->ws_fb.word_ids};
     for (DevBuf* b : bufs)
       if (b->p) cudaFree(b->p);
     Workspace& f = h->ws_fb;

@@ -133,9 +133,13 @@ void add_inplace(float* a, const float* b, uint64_t n) {
 
 // attentionOracle (oracle.ts:64-105). `local_start/local_count` restrict each
 // query row to its record's key range (the encoder); NULL means all kRows.
+// In local mode a record mask may carry the same-word bias (compileRecordMask,
+// masks.ts:167-198): `words` holds each compact token's word id, and two
+// tokens of one record with the same valid id get the f32 `alpha` as their
+// mask entry (every other in-record entry is 0).
 void attention(const float* q, const float* k, const float* v, const float* mask, uint64_t q_rows, uint64_t k_rows,
                uint32_t h, uint32_t heads, uint32_t head_dim, const uint32_t* local_start,
-               const uint32_t* local_count, float* out) {
+               const uint32_t* local_count, float* out, const uint32_t* words = nullptr, float alpha = 0.0f) {
   std::vector<float> scores(k_rows ? k_rows : 1);
   const double scale = 1 / std::sqrt(double(head_dim));
   for (uint64_t i = 0; i < q_rows * h; i++) out[i] = 0;
@@ -147,7 +151,9 @@ void attention(const float* q, const float* k, const float* v, const float* mask
       for (uint64_t j = from; j < to; j++) {
         double s = 0;
         for (uint32_t dd = 0; dd < head_dim; dd++) s += double(q[i * h + hb + dd]) * double(k[j * h + hb + dd]);
-        scores[j] = f32(s * scale + (mask ? double(mask[i * k_rows + j]) : 0.0));
+        double m = mask ? double(mask[i * k_rows + j]) : 0.0;
+        if (words && alpha != 0.0f && words[i] != kInvalidU32 && words[i] == words[j]) m = double(alpha);
+        scores[j] = f32(s * scale + m);
       }
       bool all_blocked = true;
       for (uint64_t j = from; j < to; j++)
@@ -304,7 +310,7 @@ int forward(const ko_dims* d, const float* W, const uint32_t* token_rows, uint32
             const uint32_t* token_ids, const uint32_t* field_roles, const uint32_t* schema_ids,
             const uint32_t* band_ids, const Active& a, const float* mixer_mask, float* field_states,
             float* bank_keys, float* bank_values, float* query_keys, float* query_values_premix,
-            float* query_output) {
+            float* query_output, const uint32_t* word_ids = nullptr, float alpha = 0.0f) {
   const Layout L = layout_of(d);
   const uint32_t h = d->hidden, f = d->ffn;
   const uint64_t t = a.tokens.size();
@@ -341,6 +347,13 @@ int forward(const ko_dims* d, const float* W, const uint32_t* token_rows, uint32
     }
   }
 
+  // the same-word bias's labels per compact token (indexed like activeTokens)
+  std::vector<uint32_t> words;
+  if (word_ids && alpha != 0.0f) {
+    words.resize(t);
+    for (uint64_t ti = 0; ti < t; ti++) words[ti] = word_ids[a.tokens[ti]];
+  }
+
   // 2. Encoder blocks.
   std::vector<float> qb(t * h), kb(t * h), vb(t * h), attn(t * h), hid(t * f), ff(t * h);
   for (uint32_t b = 0; b < d->enc_blocks; b++) {
@@ -351,7 +364,7 @@ int forward(const ko_dims* d, const float* W, const uint32_t* token_rows, uint32
     matmul(x.data(), wk, t, h, h, kb.data());
     matmul(x.data(), wv, t, h, h, vb.data());
     attention(qb.data(), kb.data(), vb.data(), nullptr, t, t, h, d->heads, d->head_dim, rs.data(), rc.data(),
-              attn.data());
+              attn.data(), words.empty() ? nullptr : words.data(), alpha);
     add_inplace(x.data(), attn.data(), t * h);
     ffn(x.data(), w1, w2, t, h, f, hid.data(), ff.data());
     add_inplace(x.data(), ff.data(), t * h);
@@ -944,11 +957,12 @@ int ko_forward(const ko_dims* d, const float* weights, const uint32_t* token_row
                uint32_t slots, const uint32_t* token_ids, const uint32_t* field_roles, const uint32_t* schema_ids,
                const uint32_t* band_ids, const uint32_t* active_record_indices, const float* mixer_mask,
                float* field_states, float* bank_keys, float* bank_values, float* query_keys,
-               float* query_values_premix, float* query_output) {
+               float* query_values_premix, float* query_output, const uint32_t* word_ids, float alpha) {
   Active a;
   compile_active(slots, token_ids, band_ids, active_record_indices, a);
   return forward(d, weights, token_rows, token_rows_len, slots, token_ids, field_roles, schema_ids, band_ids, a,
-                 mixer_mask, field_states, bank_keys, bank_values, query_keys, query_values_premix, query_output);
+                 mixer_mask, field_states, bank_keys, bank_values, query_keys, query_values_premix, query_output,
+                 word_ids, alpha);
 }
 
 void ko_selector(const float* query, const float* bank_keys, const float* bank_values, const float* mask,
@@ -983,7 +997,8 @@ int ko_forward_batch(const ko_dims* d, const float* weights, const uint32_t* tok
                      uint32_t frames, const uint64_t* rec_off, const uint32_t* token_ids, const uint32_t* field_roles,
                      const uint32_t* schema_ids, const uint32_t* band_ids, const uint32_t* schema_allow,
                      const uint32_t* band_allow, const double* uniforms, int threads, uint64_t* p_off,
-                     uint64_t* q_off, float* p, uint32_t* index, float* query_output) {
+                     uint64_t* q_off, float* p, uint32_t* index, float* query_output, const uint32_t* word_ids,
+                     float alpha) {
   ko_batch_offsets(frames, rec_off, token_ids, band_ids, p_off, q_off, nullptr, nullptr);
   const Layout L = layout_of(d);
   const uint32_t h = d->hidden;
@@ -1008,7 +1023,8 @@ int ko_forward_batch(const ko_dims* d, const float* weights, const uint32_t* tok
       }
       std::vector<float> bk(uint64_t(r) * h), bv(uint64_t(r) * h), qout(uint64_t(q) * h), mask(uint64_t(q) * r);
       if (forward(d, weights, token_rows, token_rows_len, slots, tid, rid, sid, bid, a, nullptr, nullptr, bk.data(),
-                  bv.data(), nullptr, nullptr, qout.data()) != 0) {
+                  bv.data(), nullptr, nullptr, qout.data(), word_ids ? word_ids + r0 * kRecordWidth : nullptr,
+                  alpha) != 0) {
         failed = 1;
         continue;
       }

@@ -73,12 +73,16 @@ uint32_t ko_compile_active(uint32_t slots, const uint32_t* token_ids, const uint
 /* brainForwardOracle (oracle.ts:231-299) for one packed frame.
  * mixer_mask: [Q,R] or NULL for the open (all-zero) mask the session uses.
  * Outputs sized [T,H], [R,H], [R,H], [Q,H], [Q,H], [Q,H]; any may be NULL
- * except query_output/bank_keys/bank_values. Returns 0, or -1 on a bad frame. */
+ * except query_output/bank_keys/bank_values. word_ids [slots*8] (frame token
+ * order, 0xffffffff = no word) with alpha != 0 adds the same-word bias to the
+ * encoder's record mask (WordBias, masks.ts:145-198); NULL / 0 for none.
+ * Returns 0, or -1 on a bad frame. */
 int ko_forward(const ko_dims* d, const float* weights, const uint32_t* token_rows, uint32_t token_rows_len,
                uint32_t slots, const uint32_t* token_ids, const uint32_t* field_roles,
                const uint32_t* schema_ids, const uint32_t* band_ids, const uint32_t* active_record_indices,
                const float* mixer_mask, float* field_states, float* bank_keys, float* bank_values,
-               float* query_keys, float* query_values_premix, float* query_output);
+               float* query_keys, float* query_values_premix, float* query_output, const uint32_t* word_ids,
+               float alpha);
 
 /* selectorOracle (oracle.ts:332-382). uniforms: [Q] or NULL (argmax).
  * gather may be NULL. */
@@ -100,14 +104,15 @@ void ko_selection_mask_rule(uint32_t q, uint32_t r, const uint32_t* bank_records
  * (one per question, in batch question order).
  * p_off[f] / q_off[f] (size F+1) are written: frame f's p rows start at
  * p_off[f] (Q_f*R_f floats) and its indices at q_off[f].
- * Frames run in parallel over `threads` host threads (0 = all).
+ * Frames run in parallel over `threads` host threads (0 = all). word_ids
+ * [records*8] and alpha: the same-word bias as for ko_forward.
  * Returns 0, or -1 on a bad frame. */
 int ko_forward_batch(const ko_dims* d, const float* weights, const uint32_t* token_rows, uint32_t token_rows_len,
                      uint32_t frames, const uint64_t* rec_off, const uint32_t* token_ids,
                      const uint32_t* field_roles, const uint32_t* schema_ids, const uint32_t* band_ids,
                      const uint32_t* schema_allow, const uint32_t* band_allow, const double* uniforms,
                      int threads, uint64_t* p_off, uint64_t* q_off, float* p, uint32_t* index,
-                     float* query_output);
+                     float* query_output, const uint32_t* word_ids, float alpha);
 
 /* Sizes of a batch without running it: fills p_off/q_off/t_off (F+1 each). */
 void ko_batch_offsets(uint32_t frames, const uint64_t* rec_off, const uint32_t* token_ids,

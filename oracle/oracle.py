@@ -52,17 +52,22 @@ def lib():
         _lib.ko_compile_active.restype = u32
         _lib.ko_compile_active.argtypes = [u32, P, P, P, P, P, P, P, P, P, P, P, P]
         _lib.ko_forward.restype = C.c_int
-        _lib.ko_forward.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, P, P, P, P, P]
+        _lib.ko_forward.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, P, P, P, P, P, P, C.c_float]
         _lib.ko_selector.argtypes = [P, P, P, P, P, P, u32, u32, u32, P, P, P, P]
         _lib.ko_selection_mask_rule.argtypes = [u32, u32, P, P, P, P, P, P]
         _lib.ko_forward_batch.restype = C.c_int
-        _lib.ko_forward_batch.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, P, C.c_int, P, P, P, P, P]
+        _lib.ko_forward_batch.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, P, C.c_int, P, P, P, P, P, P,
+                                          C.c_float]
         _lib.ko_batch_offsets.argtypes = [u32, P, P, P, P, P, P, P]
         _lib.ko_max_threads.restype = C.c_int
         _lib.ko_backward.restype = C.c_int
         _lib.ko_backward.argtypes = [P, P, P, u32, u32, P, P, P, P, P, P, P, C.c_int, C.c_double, P, P, P, P, P, P,
                                      P, P]
     return _lib
+
+
+def _u32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.uint32)
 
 
 def _p(a):
@@ -141,8 +146,9 @@ def compile_active(token_ids, band_ids, active_record_indices=None) -> dict:
             "active_count": n.value}
 
 
-def forward(config, weights_page: np.ndarray, frame, mixer_mask=None) -> dict:
-    """brainForwardOracle on one BrainFrameGpu-like object (fields token_ids, ...)."""
+def forward(config, weights_page: np.ndarray, frame, mixer_mask=None, word_ids=None, alpha: float = 0.0) -> dict:
+    """brainForwardOracle on one BrainFrameGpu-like object (fields token_ids, ...).
+    word_ids [slots*8] / alpha: the same-word bias on the encoder's record mask."""
     d = dims_of(config)
     h = config.hidden_size
     act = compile_active(frame.token_ids, frame.band_ids, frame.active_record_indices)
@@ -156,7 +162,7 @@ def forward(config, weights_page: np.ndarray, frame, mixer_mask=None) -> dict:
                           _p(frame.token_ids), _p(frame.field_roles), _p(frame.schema_ids), _p(frame.band_ids),
                           _p(frame.active_record_indices), _p(mm), _p(out["field_states"]), _p(out["bank_keys"]),
                           _p(out["bank_values"]), _p(out["query_keys"]), _p(out["query_values"]),
-                          _p(out["query_output"]))
+                          _p(out["query_output"]), _p(_u32(word_ids)), float(alpha))
     if rc != 0:
         raise ValueError("oracle: frame references a row outside its table")
     out.update(t=t, r=r, q=q, active=act)
@@ -201,7 +207,7 @@ def batch_offsets(batch) -> dict:
 
 
 def forward_batch(config, weights_page: np.ndarray, batch, rule=None, uniforms=None, threads: int = 0,
-                  want_query_output: bool = False) -> dict:
+                  want_query_output: bool = False, word_ids=None, alpha: float = 0.0) -> dict:
     d = dims_of(config)
     offs = batch_offsets(batch)
     F = batch.frames
@@ -211,10 +217,11 @@ def forward_batch(config, weights_page: np.ndarray, batch, rule=None, uniforms=N
     rows = np.ascontiguousarray(config.token_rows, dtype=np.uint32)
     sa, ba = (None, None) if rule is None else rule
     u = None if uniforms is None else np.ascontiguousarray(uniforms, dtype=np.float64)
+    wid = _u32(word_ids)
     rc = lib().ko_forward_batch(C.byref(d), _p(weights_page), _p(rows), rows.size, F, _p(batch.rec_off),
                                 _p(batch.token_ids), _p(batch.field_roles), _p(batch.schema_ids),
                                 _p(batch.band_ids), _p(sa), _p(ba), _p(u), threads, _p(offs["p_off"]),
-                                _p(offs["q_off"]), _p(p), _p(index), _p(qout))
+                                _p(offs["q_off"]), _p(p), _p(index), _p(qout), _p(wid), float(alpha))
     if rc != 0:
         raise ValueError("oracle: a frame references a row outside its table")
     out = {"p": p, "index": index, **offs}

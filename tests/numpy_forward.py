@@ -24,7 +24,7 @@ def mm(x, w, out_dim, in_dim):
         np.float32)
 
 
-def forward(config, weights, frame):
+def forward(config, weights, frame, word_ids=None, alpha=0.0):
     h, heads, hd, f = config.hidden_size, config.head_count, config.head_dim, config.ffn_size
     g, act = frame.gpu, frame.active
     b = embedding_table_bases(config)
@@ -42,6 +42,9 @@ def forward(config, weights, frame):
          + E[b.stream + stream[:, None] * h + d] + E[b.pos + local[:, None] * h + d]).astype(np.float32)
     start, count = record_ranges(act)
     t = x.shape[0]
+    # the same-word bias (WordBias): f32 alpha between two tokens of one record with one valid word id
+    words = None if word_ids is None or alpha == 0 else np.asarray(word_ids, np.uint32)[ft]
+    a32 = float(np.float32(alpha))
     for blk in weights.enc:
         q, k, v = mm(x, blk.wq, h, h), mm(x, blk.wk, h, h), mm(x, blk.wv, h, h)
         out = np.zeros((t, h), dtype=np.float32)
@@ -49,8 +52,12 @@ def forward(config, weights, frame):
             s0, c = int(start[i]), int(count[i])
             for hh in range(heads):
                 sl = slice(hh * hd, (hh + 1) * hd)
-                sc = (k[s0:s0 + c, sl].astype(np.float64) @ q[i, sl].astype(np.float64) / np.sqrt(hd)).astype(
-                    np.float32)
+                bias = 0.0
+                if words is not None:
+                    wj = words[s0:s0 + c]
+                    bias = np.where((wj == words[i]) & (words[i] != 0xFFFFFFFF), a32, 0.0)
+                sc = (k[s0:s0 + c, sl].astype(np.float64) @ q[i, sl].astype(np.float64) / np.sqrt(hd)
+                      + bias).astype(np.float32)
                 p = softmax_rows(sc)
                 out[i, sl] = (p.astype(np.float64) @ v[s0:s0 + c, sl].astype(np.float64)).astype(np.float32)
         x = (x + out).astype(np.float32)

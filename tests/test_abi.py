@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_sizes_match_the_c_layout():
     import ctypes as C
     assert C.sizeof(abi.KcConfig) == 13 * 4 + 4 + 8 + 4 + 4  # 13 u32, pad, pointer, u32, tail pad
-    assert C.sizeof(abi.KcBatchView) == 8 + 8 + 8 * 8
+    assert C.sizeof(abi.KcBatchView) == 8 + 8 + 8 * 9 + 8
     assert C.sizeof(abi.KcBatchOut) == 8 * 11
 
 
