@@ -17,7 +17,7 @@ namespace kc {
 // ---------------------------------------------------------------------------
 // fieldEmbed (oracle.ts:151-184): x[t] = token + field + schema + band +
 // stream + pos rows, summed in that order in f64, stored f32.
-// One warp per compact token, float4 per lane (H = 128).
+// 32 compact tokens per warp, float4 per lane (H = 128).
 // ---------------------------------------------------------------------------
 struct EmbedArgs {
   const uint32_t* tok_recpos;
@@ -32,33 +32,65 @@ struct EmbedArgs {
   uint64_t t;
 };
 
-__global__ void __launch_bounds__(256) k_embed_exact(EmbedArgs a) {
-  const uint64_t t = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (t >= a.t) return;
-  const int d = (threadIdx.x & 31) * 4;
-  const uint32_t rp = a.tok_recpos[t];
-  const uint32_t g = rp >> 3, l = rp & 7u;
-  const uint32_t tok = a.token_rows[a.token_ids[uint64_t(g) * KC_RW + l]];
-  const uint32_t role = a.token_rows[a.field_roles[uint64_t(g) * KC_RW + l]];
-  const uint32_t band = a.band_ids[g];
-  const uint32_t stream = band == KC_QUERY_BAND_ID ? 1u : 0u;
-  const float4 r0 = *reinterpret_cast<const float4*>(a.table + a.tb_token + uint64_t(tok) * KC_H + d);
-  const float4 r1 = *reinterpret_cast<const float4*>(a.table + a.tb_field + uint64_t(role) * KC_H + d);
-  const float4 r2 = *reinterpret_cast<const float4*>(a.table + a.tb_schema + uint64_t(a.schema_ids[g]) * KC_H + d);
-  const float4 r3 = *reinterpret_cast<const float4*>(a.table + a.tb_band + uint64_t(band) * KC_H + d);
-  const float4 r4 = *reinterpret_cast<const float4*>(a.table + a.tb_stream + uint64_t(stream) * KC_H + d);
-  const float4 r5 = *reinterpret_cast<const float4*>(a.table + a.tb_pos + uint64_t(l) * KC_H + d);
+// 32 tokens per warp: lane i first resolves token i's rows (the dependent
+// chain record position -> token id -> tokenRows -> table row), so 32 chains
+// are in flight at once; then the warp gathers and sums the six rows of four
+// tokens at a time, lane l owning columns 4l..4l+3.
+constexpr int kEmbedWarps = 8;
+constexpr int kEmbedTokensPerWarp = 32;
+
+__global__ void __launch_bounds__(kEmbedWarps * 32, 2) k_embed_exact(EmbedArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t base = (uint64_t(blockIdx.x) * kEmbedWarps + warp) * kEmbedTokensPerWarp;
+  if (base >= a.t) return;
+  const uint64_t left = a.t - base;
+  const int n = left < kEmbedTokensPerWarp ? int(left) : kEmbedTokensPerWarp;
+  uint32_t tok = 0, role = 0, schema = 0, band = 0, pos = 0;
+  if (lane < n) {
+    const uint32_t rp = a.tok_recpos[base + lane];
+    const uint32_t g = rp >> 3;
+    pos = rp & 7u;
+    tok = a.token_rows[a.token_ids[uint64_t(g) * KC_RW + pos]];
+    role = a.token_rows[a.field_roles[uint64_t(g) * KC_RW + pos]];
+    schema = a.schema_ids[g];
+    band = a.band_ids[g];
+  }
+  const int d = lane * 4;
   auto sum6 = [](float v0, float v1, float v2, float v3, float v4, float v5) {
     double v = 0.0;
     v += double(v0); v += double(v1); v += double(v2); v += double(v3); v += double(v4); v += double(v5);
     return f32(v);
   };
-  float4 o;
-  o.x = sum6(r0.x, r1.x, r2.x, r3.x, r4.x, r5.x);
-  o.y = sum6(r0.y, r1.y, r2.y, r3.y, r4.y, r5.y);
-  o.z = sum6(r0.z, r1.z, r2.z, r3.z, r4.z, r5.z);
-  o.w = sum6(r0.w, r1.w, r2.w, r3.w, r4.w, r5.w);
-  *reinterpret_cast<float4*>(a.x + t * KC_H + d) = o;
+  for (int i0 = 0; i0 < n; i0 += 4) {
+    float4 r[4][6];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u;  // every lane shuffles; only tokens below n are read
+      const uint32_t ti = __shfl_sync(0xffffffffu, tok, i & 31), ri = __shfl_sync(0xffffffffu, role, i & 31);
+      const uint32_t si = __shfl_sync(0xffffffffu, schema, i & 31), bi = __shfl_sync(0xffffffffu, band, i & 31);
+      const uint32_t li = __shfl_sync(0xffffffffu, pos, i & 31);
+      if (i < n) {
+        const uint32_t stream = bi == KC_QUERY_BAND_ID ? 1u : 0u;
+        r[u][0] = *reinterpret_cast<const float4*>(a.table + a.tb_token + uint64_t(ti) * KC_H + d);
+        r[u][1] = *reinterpret_cast<const float4*>(a.table + a.tb_field + uint64_t(ri) * KC_H + d);
+        r[u][2] = *reinterpret_cast<const float4*>(a.table + a.tb_schema + uint64_t(si) * KC_H + d);
+        r[u][3] = *reinterpret_cast<const float4*>(a.table + a.tb_band + uint64_t(bi) * KC_H + d);
+        r[u][4] = *reinterpret_cast<const float4*>(a.table + a.tb_stream + uint64_t(stream) * KC_H + d);
+        r[u][5] = *reinterpret_cast<const float4*>(a.table + a.tb_pos + uint64_t(li) * KC_H + d);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u;
+      if (i >= n) break;
+      float4 o;
+      o.x = sum6(r[u][0].x, r[u][1].x, r[u][2].x, r[u][3].x, r[u][4].x, r[u][5].x);
+      o.y = sum6(r[u][0].y, r[u][1].y, r[u][2].y, r[u][3].y, r[u][4].y, r[u][5].y);
+      o.z = sum6(r[u][0].z, r[u][1].z, r[u][2].z, r[u][3].z, r[u][4].z, r[u][5].z);
+      o.w = sum6(r[u][0].w, r[u][1].w, r[u][2].w, r[u][3].w, r[u][4].w, r[u][5].w);
+      *reinterpret_cast<float4*>(a.x + (base + i) * KC_H + d) = o;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -48,24 +48,22 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
   const int cnt = int(a.rec_meta[g].y & 15u);
   if (cnt == 0) return;
   float4* st = stage[warp];
+  // stage q|k|v with 16-byte asynchronous copies, every one of the record's in
+  // flight at once; the residual rows load meanwhile
   const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
   const int n4 = cnt * kLaRowF4;
-  for (int b0 = 0; b0 < n4; b0 += 4 * 32) {  // four 16-byte loads in flight per lane
-    float4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int i = b0 + u * 32 + lane;
-      if (i < n4) v[u] = __ldg(src + i);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int i = b0 + u * 32 + lane;
-      if (i < n4) {
-        const int r = i / kLaRowF4, f = i - r * kLaRowF4;
-        st[la_swz(r, f)] = v[u];
-      }
-    }
+  for (int i = lane; i < n4; i += 32) {
+    const int r = i / kLaRowF4, f = i - r * kLaRowF4;
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(st + la_swz(r, f)));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i) : "memory");
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  float4* xr = reinterpret_cast<float4*>(a.x + uint64_t(start) * KC_H);
+  float4 xv[KC_RW];
+#pragma unroll
+  for (int r = 0; r < KC_RW; r++)
+    if (r < cnt) xv[r] = xr[r * 32 + lane];
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
   const int head = lane >> 3, ti = lane & 7;
   // word ids of the record's tokens: lane j (head 0) holds token j's
@@ -124,11 +122,6 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
     for (int m = 0; m < 8; m++) st[la_swz(ti, head * 8 + m)] = o[m];
   }
   __syncwarp();
-  float4* xr = reinterpret_cast<float4*>(a.x + uint64_t(start) * KC_H);
-  float4 xv[KC_RW];
-#pragma unroll
-  for (int r = 0; r < KC_RW; r++)
-    if (r < cnt) xv[r] = xr[r * 32 + lane];
 #pragma unroll
   for (int r = 0; r < KC_RW; r++)
     if (r < cnt) {
@@ -170,25 +163,33 @@ __global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
                                                   : a.bank_values + uint64_t(r) * KC_H) + lane;
   const float4 pk = __ldg(reinterpret_cast<const float4*>(a.pool) + lane);
   const float4 pv = __ldg(reinterpret_cast<const float4*>(a.pool + KC_H) + lane);
+  // every row of the record in flight before any reduction
   float4 xs[KC_RW];
+  const float4* xr = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H) + lane;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++) xs[j] = j < cnt ? __ldg(xr + j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
   float ks[KC_RW], vs[KC_RW];
-  float kmx = -INFINITY, vmx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < KC_RW; j++) {
+    ks[j] = pk.x * xs[j].x + pk.y * xs[j].y + pk.z * xs[j].z + pk.w * xs[j].w;
+    vs[j] = pv.x * xs[j].x + pv.y * xs[j].y + pv.z * xs[j].z + pv.w * xs[j].w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) {
+      ks[j] += __shfl_xor_sync(0xffffffffu, ks[j], o);
+      vs[j] += __shfl_xor_sync(0xffffffffu, vs[j], o);
+    }
+  float kmx = -INFINITY, vmx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++)
     if (j < cnt) {
-      xs[j] = __ldg(reinterpret_cast<const float4*>(a.x + (uint64_t(start) + j) * KC_H) + lane);
-      float k = pk.x * xs[j].x + pk.y * xs[j].y + pk.z * xs[j].z + pk.w * xs[j].w;
-      float v = pv.x * xs[j].x + pv.y * xs[j].y + pv.z * xs[j].z + pv.w * xs[j].w;
-      for (int o = 16; o; o >>= 1) {
-        k += __shfl_xor_sync(0xffffffffu, k, o);
-        v += __shfl_xor_sync(0xffffffffu, v, o);
-      }
-      ks[j] = k * a.scale;
-      vs[j] = v * a.scale;
+      ks[j] *= a.scale;
+      vs[j] *= a.scale;
       kmx = fmaxf(kmx, ks[j]);
       vmx = fmaxf(vmx, vs[j]);
     }
-  }
   float ksum = 0.f, vsum = 0.f;
 #pragma unroll
   for (int j = 0; j < KC_RW; j++)
@@ -212,6 +213,7 @@ __global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Mixer cross-attention + residual, f32// ---------------------------------------------------------------------------
 // Mixer cross-attention + residual, f32 (oracle.ts:292-293 with the open
 // mixer mask). One CTA of 128 threads per question; warp w = head w.
 // ---------------------------------------------------------------------------

@@ -525,7 +525,7 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
                      h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
                      x, T};
-    kc::k_embed_exact<<<unsigned((T + 7) / 8), 256, 0, h->stream>>>(ea);
+    kc::k_embed_exact<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(ea);
     h->launches++;
   }
   const double attn_scale = 1.0 / std::sqrt(double(d.hd));
@@ -630,7 +630,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
                      h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
                      x, T};
-    kc::k_embed_exact<<<unsigned((T + 7) / 8), 256, 0, h->stream>>>(ea);
+    kc::k_embed_exact<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(ea);
     h->launches++;
   }
   const float attn_scale = float(1.0 / std::sqrt(double(d.hd)));
