@@ -204,6 +204,10 @@ typedef struct kc_stage_times {
   double fallback_ms;       /* exact recomputation of uncertified frames */
   uint64_t fallback_frames; /* frames recomputed (counted whether or not profiling is on) */
   double enc_gemm_bytes;    /* algorithmic bytes of the encoder GEMMs timed (A read, C written) */
+  /* the fused feed-forward kernel (W1, ReLU, W2, residual in one launch) */
+  double enc_ffn_ms;
+  uint64_t enc_ffn_launches;
+  double enc_ffn_flops, enc_ffn_bytes;
 } kc_stage_times;
 
 uint32_t kc_abi_version(void);

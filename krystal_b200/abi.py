@@ -132,7 +132,8 @@ class KcStageTimes(C.Structure):
                                           "mixer_ms", "selector_ms", "total_ms")] + [
         ("enc_gemm_launches", C.c_uint64), ("launches", C.c_uint64), ("batches", C.c_uint64),
         ("enc_gemm_flops", C.c_double), ("fallback_ms", C.c_double), ("fallback_frames", C.c_uint64),
-        ("enc_gemm_bytes", C.c_double)]
+        ("enc_gemm_bytes", C.c_double), ("enc_ffn_ms", C.c_double), ("enc_ffn_launches", C.c_uint64),
+        ("enc_ffn_flops", C.c_double), ("enc_ffn_bytes", C.c_double)]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "exact.cuh"
 #include "fast.cuh"
+#include "ffn.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 
@@ -118,7 +119,8 @@ struct BackWs {
   const float* mask_used = nullptr;
 };
 
-enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStCount };
+enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStEncFfn,
+             kStCount };
 
 // The matrices the tensor-core path multiplies by, in a fixed order:
 // per encoder block QKV [3H,H], W1 [F,H], W2 [H,F]; per mixer block Wq, Wk,
@@ -258,7 +260,8 @@ void prof_collect(kc_handle* h) {
   if (!h->profiling || h->ev_used.empty()) return;
   cudaStreamSynchronize(h->stream);
   double* dst[kStCount] = {&h->prof.pack_ms, &h->prof.embed_ms, &h->prof.enc_gemm_ms, &h->prof.enc_attn_ms,
-                           &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms, &h->prof.fallback_ms};
+                           &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms, &h->prof.fallback_ms,
+                           &h->prof.enc_ffn_ms};
   for (size_t i = 0; i < h->ev_used.size(); i++) {
     float ms = 0;
     auto& pr = h->ev_pool[h->ev_used[i].second];
@@ -269,6 +272,10 @@ void prof_collect(kc_handle* h) {
       h->prof.enc_gemm_launches++;
       h->prof.enc_gemm_flops += h->ev_flops[i];
       h->prof.enc_gemm_bytes += h->ev_bytes[i];
+    } else if (h->ev_used[i].first == kStEncFfn) {
+      h->prof.enc_ffn_launches++;
+      h->prof.enc_ffn_flops += h->ev_flops[i];
+      h->prof.enc_ffn_bytes += h->ev_bytes[i];
     }
   }
   h->ev_used.clear();
@@ -383,6 +390,26 @@ kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, c
   const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
   kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, gmap, g);
+  h->launches++;
+  return KC_OK;
+}
+
+// x += relu(x·W1ᵀ)·W2ᵀ on the tensor cores in one kernel (ffn.cuh), for the
+// W1 / W2 matrices mat_w1 / mat_w2 of the tensor-core list. Needs H = 128 and
+// F = 384 (the kernel's fixed tiling); ffn_fusable() says whether it applies.
+bool ffn_fusable(const kc_handle* h) { return h->d.h == 128 && h->d.ffn == 384; }
+
+kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
+  if (M == 0) return KC_OK;
+  CUtensorMap amap, cmap;
+  if (!kc::tc::make_a_map(&amap, x, M, 128, 128) || !kc::tc::make_c_map(&cmap, x, M, 128, 128))
+    return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for the feed-forward operand");
+  kc::tc::FfnArgs fa{int(M), P<uint8_t>(h->images) + h->img_off[mat_w1], P<uint8_t>(h->images) + h->img_off[mat_w2],
+                     std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat_w1))),
+                     std::ldexp(1.0f, -(h->sa + mat_sw(h, mat_w2))), h->d_err};
+  const uint64_t tiles = (M + 127) / 128;
+  const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
+  kc::tc::k_tc_ffn<<<grid, kc::tc::kThreadsT, kc::tc::kFfnSmem, h->stream>>>(amap, cmap, fa);
   h->launches++;
   return KC_OK;
 }
@@ -649,13 +676,18 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
           la);
       h->launches++;
     }
-    {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
-      KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, x, T, enc_m + 3 * blk + 1, qkv));
-    }
-    {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
-      KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, qkv, T, enc_m + 3 * blk + 2, x));
+    if (ffn_fusable(h)) {  // W1, ReLU, W2 and the residual in one kernel: h1 stays on chip
+      ProfScope ps(h, kStEncFfn, 4.0 * T * H * FF, 4.0 * T * (2 * H));
+      KC_CHECK(tc_ffn(h, x, T, enc_m + 3 * blk + 1, enc_m + 3 * blk + 2));
+    } else {
+      {
+        ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (H + FF));
+        KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, x, T, enc_m + 3 * blk + 1, qkv));
+      }
+      {
+        ProfScope ps(h, kStEncGemm, 2.0 * T * H * FF, 4.0 * T * (FF + 2 * H));
+        KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, qkv, T, enc_m + 3 * blk + 2, x));
+      }
     }
   }
   {
@@ -1268,6 +1300,7 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiGate>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * 4)))
     return bail(e, "smem");
