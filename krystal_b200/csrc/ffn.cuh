@@ -11,20 +11,27 @@
 //
 // One persistent CTA per SM, 128-row tiles, 320 threads:
 //   warp 0     TMA: the x tile (two [128 x 64] f32 boxes) and, per tile,
-//              twelve 32 KB weight-image chunks in the order warp 5 consumes
-//              them, through a two-stage ring;
-//   warps 1-4  split the x tile in place to swizzled fp16 hi | lo;
-//   warp 5     MMA issuer. Per tile, for hidden chunks j = 0, 1, 2 of 128
-//              columns: P1(j) = x·W1[j]ᵀ into TMEM buffer j % 2, and
-//              P2(j) += h1[j]·W2[:, j]ᵀ into the output accumulator, issued
-//              P1(0) P1(1) P2(0) P1(2) P2(1) P2(2) so each P1 overlaps the
-//              epilogue of the one before;
-//   warps 6-9  for each j: TMEM → ×2^-(sa+sw1), ReLU, ×2^sa, split → the
-//              fp16 hi | lo operand of P2(j) in shared memory; then the
-//              output: TMEM → ×2^-(sa+sw2) + x (TMA-loaded) → TMA store.
-// Shared memory: x operand 64 KB, h1 operand 64 KB, weight ring 2 x 32 KB,
-// epilogue store buffers 32 KB. TMEM: 512 columns (two 128-column P1
-// buffers, one 128-column output accumulator). Every wait is bounded; an
+//              the twelve 32 KB weight-image chunks (W1 then W2) through a
+//              three-stage ring;
+//   warps 1-4  split the x tile in place to swizzled fp16 hi | lo, and
+//              share the epilogues below with warps 6-9;
+//   warp 5     MMA issuer. Per tile: P1(j) = x·W1[j]ᵀ for hidden chunks
+//              j = 0, 1, 2 of 128 columns into TMEM buffer j (A and B in
+//              shared memory), then P2(j) += h1[j]·W2[:, j]ᵀ into the output
+//              accumulator with A = h1[j] read from TMEM buffer j itself;
+//   epilogues  for each j: TMEM → ×2^-(sa+sw1), ReLU, ×2^sa, split → fp16
+//              hi | lo written back over the same TMEM columns (each 16-column
+//              K step: 8 columns of hi pairs, then 8 of lo pairs); then the
+//              output: TMEM → ×2^-(sa+sw2) + x → TMA store, with x prefetched
+//              into shared memory a tile ahead. Warps 6-9 take hidden columns
+//              0-63 of each chunk and output columns 0-63; warps 1-4 the
+//              other halves, and they split the next tile's x before their
+//              output half.
+// Keeping h1 in TMEM halves the shared-memory reads of the W2 products and
+// removes the h1 stores: the SS products at N = 128 alone read shared memory
+// at its full rate. Shared memory: x operand 64 KB, output staging 8 warps x
+// 2 x 4 KB, weight ring 3 x 32 KB. TMEM: 512 columns (three 128-column P1 /
+// h1 buffers, one 128-column output accumulator). Every wait is bounded; an
 // expired wait sets the error word and the CTA drains and exits.
 #pragma once
 #include "tc_gemm.cuh"
@@ -32,12 +39,12 @@
 namespace kc {
 namespace tc {
 
-constexpr int kFfnWStages = 2;
+constexpr int kFfnWStages = 3;
 constexpr int kFfnChunk = 2 * kTileBytes;                // one weight chunk: hi | lo, 32 KB
 constexpr int kFfnXBytes = 2 * kFfnChunk;                // x operand: 2 K-chunks, 64 KB
-constexpr int kFfnHBytes = 2 * kFfnChunk;                // h1 operand: 2 K-chunks, 64 KB
-constexpr int kFfnSmem = kFfnXBytes + kFfnHBytes + kFfnWStages * kFfnChunk + kEpiBytes + 1024 + 256;
-constexpr int kFfnChunksPerTile = 12;                    // 3 x (W1: 2 chunks) + 6 W2 chunks
+constexpr int kFfnEBytes = 8 * 2 * kEpiBuf;              // output staging: 8 warps x 2 blocks, 64 KB
+constexpr int kFfnSmem = kFfnXBytes + kFfnEBytes + kFfnWStages * kFfnChunk + 1024 + 512;
+constexpr int kFfnChunksPerTile = 12;                    // W1: 3 n-tiles x 2 k-chunks, then W2: 6 k-chunks
 
 struct FfnArgs {
   int M;                 // rows
@@ -49,12 +56,10 @@ struct FfnArgs {
   int* err;
 };
 
-// Weight chunk c of a tile, in consumption order: (is_w2, index into its image).
+// Weight chunk c of a tile, in consumption order: P1(0..2) take W1 chunks
+// 0..5, P2(0..2) take W2 chunks 0..5.
 __device__ __forceinline__ const uint8_t* ffn_chunk(const FfnArgs& a, int c) {
-  // P1(0): W1 n0 k0,k1 | P1(1): n1 k0,k1 | P2(0): W2 k0,k1 | P1(2): n2 k0,k1 | P2(1): k2,k3 | P2(2): k4,k5
-  constexpr int kW2[kFfnChunksPerTile] = {0, 0, 0, 0, 1, 1, 0, 0, 1, 1, 1, 1};
-  constexpr int kIdx[kFfnChunksPerTile] = {0, 1, 2, 3, 0, 1, 4, 5, 2, 3, 4, 5};
-  return (kW2[c] ? a.w2 : a.w1) + size_t(kIdx[c]) * kFfnChunk;
+  return c < 6 ? a.w1 + size_t(c) * kFfnChunk : a.w2 + size_t(c - 6) * kFfnChunk;
 }
 
 __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__ CUtensorMap amap,
@@ -63,24 +68,22 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* xs = smem;                                   // x operand (f32 staging, then hi|lo)
-  unsigned char* hs = smem + kFfnXBytes;                      // h1 operand
-  unsigned char* ws = hs + kFfnHBytes;                        // weight ring
-  float* epi_buf = reinterpret_cast<float*>(ws + kFfnWStages * kFfnChunk);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ws + kFfnWStages * kFfnChunk + kEpiBytes);
+  unsigned char* es = smem + kFfnXBytes;                      // output staging
+  unsigned char* ws = es + kFfnEBytes;                        // weight ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ws + kFfnWStages * kFfnChunk);
   uint64_t* xraw = bars;         // [2] x box landed
   uint64_t* xfull = bars + 2;    // [2] x chunk split
   uint64_t* xempty = bars + 4;   // the tile's P1s are done with x
-  uint64_t* wfull = bars + 5;    // [2]
-  uint64_t* wempty = bars + 7;   // [2]
-  uint64_t* pfull = bars + 9;    // [2] P1 accumulator ready
-  uint64_t* pempty = bars + 11;  // [2] P1 accumulator read
-  uint64_t* hfull = bars + 13;   // h1 operand written
-  uint64_t* hempty = bars + 14;  // P2 done reading the h1 operand
-  uint64_t* ofull = bars + 15;   // output accumulator ready
-  uint64_t* oempty = bars + 16;  // output accumulator read
-  uint64_t* drain = bars + 17;
-  uint64_t* cload = bars + 18;   // [4 warps][2 buffers] residual tiles landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  uint64_t* wfull = bars + 5;    // [kFfnWStages]
+  uint64_t* wempty = bars + 8;   // [kFfnWStages]
+  uint64_t* pfull = bars + 11;   // [3] P1 accumulator j ready
+  uint64_t* pempty = bars + 14;  // [3] P2(j) done reading h1 from buffer j
+  uint64_t* hfull = bars + 17;   // [3] h1 chunk j written to TMEM
+  uint64_t* ofull = bars + 20;   // output accumulator ready
+  uint64_t* oempty = bars + 21;  // output accumulator read
+  uint64_t* drain = bars + 22;
+  uint64_t* cload = bars + 23;   // [8 epilogue warps][2 blocks] residual landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 39);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (a.M + kBM - 1) / kBM;
@@ -89,18 +92,21 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
     for (int i = 0; i < 2; i++) {
       mbar_init(&xraw[i], 1);
       mbar_init(&xfull[i], 128);
+    }
+    for (int i = 0; i < 3; i++) {
+      mbar_init(&pfull[i], 1);
+      mbar_init(&pempty[i], 1);
+      mbar_init(&hfull[i], 256);
+    }
+    for (int i = 0; i < kFfnWStages; i++) {
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], 1);
-      mbar_init(&pfull[i], 1);
-      mbar_init(&pempty[i], 128);
     }
     mbar_init(xempty, 1);
-    mbar_init(hfull, 128);
-    mbar_init(hempty, 1);
     mbar_init(ofull, 1);
-    mbar_init(oempty, 128);
+    mbar_init(oempty, 256);
     mbar_init(drain, 1);
-    for (int i = 0; i < 8; i++) mbar_init(&cload[i], 1);
+    for (int i = 0; i < 16; i++) mbar_init(&cload[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 5) tmem_alloc(tmem_slot, 512);
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_out = tmem_base + 2 * kBN;
+  const uint32_t tmem_out = tmem_base + 3 * kBN;
 
   if (warp == 0) {
     // ---------------- TMA issuer ----------------
@@ -139,19 +145,93 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
         for (int kc = 0; kc < 2; kc++) mbar_wait(&xraw[kc], (tl - 1) & 1, a.err);
     }
     __syncwarp();
-  } else if (warp <= 4) {
-    // ---------------- split the x tile: f32 staging -> swizzled fp16 hi / lo ----------------
-    const int tid = threadIdx.x - 32;
-    uint32_t tl = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
       bool ok = true;
+      auto next_w = [&](uint32_t& s_out) -> bool {  // the next weight chunk has landed
+        const int s = it % kFfnWStages;
+        const uint32_t ph = (it / kFfnWStages) & 1;
+        if (!mbar_wait(&wfull[s], ph, a.err)) return false;
+        tc_fence_after();
+        s_out = smem_u32(ws + s * kFfnChunk);
+        return true;
+      };
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
+        for (int kc = 0; kc < 2 && ok; kc++) ok = mbar_wait(&xfull[kc], tl & 1, a.err);
+        if (!ok) break;
+        tc_fence_after();
+        // P1(j): three MMAs per 16-wide K step, A = x (shared), B = W1 chunk
+        for (int j = 0; j < 3 && ok; j++) {
+          const uint32_t d = tmem_base + j * kBN;
+          if (!mbar_wait(&pempty[j], (tl & 1) ^ 1, a.err)) { ok = false; break; }
+          tc_fence_after();
+          for (int kc = 0; kc < 2; kc++, it++) {
+            uint32_t sb;
+            if (!next_w(sb)) { ok = false; break; }
+            const uint32_t sa = smem_u32(xs + kc * kFfnChunk);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; kk++) {
+              const uint64_t ah = smem_desc(sa + kk * 32), al = smem_desc(sa + kTileBytes + kk * 32);
+              const uint64_t bh = smem_desc(sb + kk * 32), bl = smem_desc(sb + kTileBytes + kk * 32);
+              mma_f16(d, ah, bh, (kc == 0 && kk == 0) ? 0u : 1u);
+              mma_f16(d, ah, bl, 1u);
+              mma_f16(d, al, bh, 1u);
+            }
+            mma_commit(&wempty[it % kFfnWStages]);
+          }
+          if (!ok) break;
+          mma_commit(&pfull[j]);
+        }
+        if (!ok) break;
+        mma_commit(xempty);
+        // P2(j): A = h1 chunk j in TMEM buffer j, B = W2 chunk
+        for (int j = 0; j < 3 && ok; j++) {
+          if (j == 0 && !mbar_wait(oempty, (tl & 1) ^ 1, a.err)) { ok = false; break; }
+          if (!mbar_wait(&hfull[j], tl & 1, a.err)) { ok = false; break; }
+          tc_fence_after();
+          for (int kc = 0; kc < 2; kc++, it++) {
+            uint32_t sb;
+            if (!next_w(sb)) { ok = false; break; }
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; kk++) {
+              const uint32_t ah = tmem_base + j * kBN + kc * 64 + kk * 16, al = ah + 8;
+              const uint64_t bh = smem_desc(sb + kk * 32), bl = smem_desc(sb + kTileBytes + kk * 32);
+              mma_f16_ts(tmem_out, ah, bh, (j == 0 && kc == 0 && kk == 0) ? 0u : 1u);
+              mma_f16_ts(tmem_out, ah, bl, 1u);
+              mma_f16_ts(tmem_out, al, bh, 1u);
+            }
+            mma_commit(&wempty[it % kFfnWStages]);
+          }
+          if (!ok) break;
+          mma_commit(&pempty[j]);
+        }
+        if (!ok) break;
+        mma_commit(ofull);
+      }
+      // every MMA this thread issued completes before TMEM is released
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- split (warps 1-4) and the epilogues (warps 1-4, 6-9) ----------------
+    const bool helper = warp <= 4;
+    const int half = helper ? 1 : 0;             // which 64 columns of each 128-column block
+    const int wi = helper ? warp - 1 + 4 : warp - 6;  // epilogue buffer / barrier index 0..7
+    const int q = warp & 3;                      // TMEM lane quarter this warp may read
+    unsigned char* eb[2] = {es + wi * 2 * kEpiBuf, es + wi * 2 * kEpiBuf + kEpiBuf};
+    // the x tile of tile number tl: f32 staging -> swizzled fp16 hi / lo, in place
+    auto split = [&](uint32_t tl) -> bool {
+      const int tid = threadIdx.x - 32;
       for (int kc = 0; kc < 2; kc++) {
         const int mine = mbar_wait(&xraw[kc], tl & 1, a.err) ? 1 : 0;
         int all;
         asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %1, 0;\n\t"
                      "bar.red.and.pred p, 1, 128, p;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(all) : "r"(mine) : "memory");
-        if (!all) { ok = false; break; }
+        if (!all) return false;
         unsigned char* st = xs + kc * kFfnChunk;
         float4 v[16];
         const float4* stage = reinterpret_cast<const float4*>(st);
@@ -180,163 +260,89 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
         fence_proxy_async_smem();
         mbar_arrive(&xfull[kc]);
       }
-      if (!ok) break;
-    }
-  } else if (warp == 5) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      uint32_t it = 0, tl = 0;
-      bool ok = true;
-      // three MMAs per 16-wide K step over one 64-wide chunk pair (A, B)
-      auto chunk_mma = [&](uint32_t d, uint32_t a_saddr, uint32_t b_saddr, bool first) {
+      return true;
+    };
+    // 32 columns (two K steps) of a P1 accumulator -> ReLU, re-split, packed
+    // for the TMEM A operand: per K step, hi pairs then lo pairs
+    auto pack_h = [&](const float* v, uint32_t* w, bool& bad) {
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; kk++) {
-          const uint64_t ah = smem_desc(a_saddr + kk * 32), al = smem_desc(a_saddr + kTileBytes + kk * 32);
-          const uint64_t bh = smem_desc(b_saddr + kk * 32), bl = smem_desc(b_saddr + kTileBytes + kk * 32);
-          mma_f16(d, ah, bh, (first && kk == 0) ? 0u : 1u);
-          mma_f16(d, ah, bl, 1u);
-          mma_f16(d, al, bh, 1u);
-        }
-      };
-      auto next_w = [&](uint32_t& s_out) -> bool {  // the next weight chunk has landed
-        const int s = it % kFfnWStages;
-        const uint32_t ph = (it / kFfnWStages) & 1;
-        if (!mbar_wait(&wfull[s], ph, a.err)) return false;
-        tc_fence_after();
-        s_out = smem_u32(ws + s * kFfnChunk);
-        return true;
-      };
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
-        for (int kc = 0; kc < 2 && ok; kc++) ok = mbar_wait(&xfull[kc], tl & 1, a.err);
-        if (!ok) break;
-        tc_fence_after();
-        // the schedule P1(0) P1(1) P2(0) P1(2) P2(1) P2(2): step -> (is P2, hidden chunk j)
-        constexpr int kP2[6] = {0, 0, 1, 0, 1, 1};
-        constexpr int kJ[6] = {0, 1, 0, 2, 1, 2};
-        for (int step = 0; step < 6 && ok; step++) {
-          const bool p2 = kP2[step] != 0;
-          const int j = kJ[step];
-          const uint32_t u = 3 * tl + j;
-          if (!p2) {
-            const uint32_t buf = u & 1;
-            if (!mbar_wait(&pempty[buf], ((u >> 1) & 1) ^ 1, a.err)) { ok = false; break; }
-            tc_fence_after();
-            for (int kc = 0; kc < 2; kc++, it++) {
-              uint32_t sb;
-              if (!next_w(sb)) { ok = false; break; }
-              chunk_mma(tmem_base + buf * kBN, smem_u32(xs + kc * kFfnChunk), sb, kc == 0);
-              mma_commit(&wempty[it % kFfnWStages]);
-            }
-            if (!ok) break;
-            mma_commit(&pfull[buf]);
-            if (j == 2) mma_commit(xempty);
-          } else {
-            if (j == 0 && !mbar_wait(oempty, (tl & 1) ^ 1, a.err)) { ok = false; break; }
-            if (!mbar_wait(hfull, u & 1, a.err)) { ok = false; break; }
-            tc_fence_after();
-            for (int kc = 0; kc < 2; kc++, it++) {
-              uint32_t sb;
-              if (!next_w(sb)) { ok = false; break; }
-              chunk_mma(tmem_out, smem_u32(hs + kc * kFfnChunk), sb, j == 0 && kc == 0);
-              mma_commit(&wempty[it % kFfnWStages]);
-            }
-            if (!ok) break;
-            mma_commit(hempty);
-            if (j == 2) mma_commit(ofull);
+      for (int ks = 0; ks < 2; ks++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          float h2[2], l2[2];
+#pragma unroll
+          for (int z = 0; z < 2; z++) {
+            const float y = fmaxf(v[16 * ks + 2 * e + z] * a.unscale1, 0.f) * a.a_scale;
+            bad |= !(fabsf(y) < 32768.0f);
+            split_f32(y, h2[z], l2[z]);
           }
+          w[16 * ks + e] = h2u(__floats2half2_rn(h2[0], h2[1]));
+          w[16 * ks + 8 + e] = h2u(__floats2half2_rn(l2[0], l2[1]));
+        }
+    };
+    // this warp's 64 columns of hidden chunk j of tile number tl, in place in TMEM
+    auto e1 = [&](uint32_t tl, int j) -> bool {
+      int okw = 0;
+      if (lane == 0) okw = mbar_wait(&pfull[j], tl & 1, a.err) ? 1 : 0;
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) return false;
+      tc_fence_after();
+      const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + j * kBN + half * 64;
+      float v0[32], v1[32];
+      uint32_t w[32];
+      bool bad = false;
+      tmem_ld32(ta, v0);
+      tmem_ld32_async(ta + 32, v1);  // in flight while the first 32 columns convert
+      pack_h(v0, w, bad);
+      tmem_st32(ta, w);
+      tmem_ld_wait(v1);
+      pack_h(v1, w, bad);
+      tmem_st32(ta + 32, w);
+      tmem_st_wait();
+      if (bad) atomicOr(a.err, kErrOverflow);
+      tc_fence_before();
+      mbar_arrive(&hfull[j]);
+      return true;
+    };
+    // the residual x rows of tile t for this warp's output blocks, into staging
+    auto prefetch = [&](int t) {
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging free again
+        for (int b = 0; b < 2; b++) {
+          mbar_arrive_expect_tx(&cload[wi * 2 + b], kEpiBuf);
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+              ::"r"(smem_u32(eb[b])), "l"(reinterpret_cast<uint64_t>(&cmap)), "r"((half * 2 + b) * 32),
+              "r"(t * kBM + q * 32), "r"(smem_u32(&cload[wi * 2 + b]))
+              : "memory");
         }
       }
-      // every MMA this thread issued completes before TMEM is released
-      mma_commit(drain);
-      mbar_wait(drain, 0, a.err);
-    }
-    __syncwarp();
-  } else {
-    // ---------------- epilogue ----------------
-    const int g = warp & 3;  // TMEM lane quarter this warp may read
-    const int ew = warp - 6;
-    unsigned char* bufs = reinterpret_cast<unsigned char*>(epi_buf) + ew * 2 * kEpiBuf;
-    uint32_t cphase = 0;
-    uint32_t tl = 0;
-    bool ok = true;
-    const int row = g * 32 + lane;  // this lane's row of the tile
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
-      // h1 for hidden chunks j = 0, 1, 2: the operand of P2(j)
-      for (int j = 0; j < 3 && ok; j++) {
-        const uint32_t u = 3 * tl + j, buf = u & 1;
-        int okw = 0;
-        if (lane == 0)
-          okw = (mbar_wait(&pfull[buf], (u >> 1) & 1, a.err) && mbar_wait(hempty, (u & 1) ^ 1, a.err)) ? 1 : 0;
-        okw = __shfl_sync(0xffffffffu, okw, 0);
-        if (!okw) { ok = false; break; }
-        tc_fence_after();
-        bool bad = false;
-#pragma unroll 1
-        for (int cg = 0; cg < kBN / 32; cg++) {
-          float v[32];
-          tmem_ld32(tmem_base + (uint32_t(g * 32) << 16) + buf * kBN + cg * 32, v);
-          // columns cg*32 .. +31 of this 128-column chunk: K chunk cg / 2, K offset (cg % 2) * 32
-          unsigned char* base = hs + (cg >> 1) * kFfnChunk;
-#pragma unroll
-          for (int q = 0; q < 4; q++) {  // 8 columns per 16-byte store
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-              float h2[2], l2[2];
-#pragma unroll
-              for (int z = 0; z < 2; z++) {
-                const float y = fmaxf(v[8 * q + 2 * e + z] * a.unscale1, 0.f) * a.a_scale;
-                bad |= !(fabsf(y) < 32768.0f);
-                split_f32(y, h2[z], l2[z]);
-              }
-              hw[e] = h2u(__floats2half2_rn(h2[0], h2[1]));
-              lw[e] = h2u(__floats2half2_rn(l2[0], l2[1]));
-            }
-            const uint32_t off = swz_offset(row, (cg & 1) * 32 + 8 * q);
-            *reinterpret_cast<uint4*>(base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(base + kTileBytes + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-          }
-        }
-        if (bad) atomicOr(a.err, kErrOverflow);
-        tc_fence_before();
-        mbar_arrive(&pempty[buf]);
-        fence_proxy_async_smem();
-        mbar_arrive(hfull);
-      }
-      if (!ok) break;
-      // the output: x += acc · 2^-(sa+sw2), through 128-byte swizzled 32x32 blocks
+      __syncwarp();
+    };
+    // this warp's half of the output of tile t (number tl): x += acc · 2^-(sa+sw2)
+    auto e2 = [&](uint32_t tl, int t) -> bool {
       int okw = 0;
       if (lane == 0) okw = mbar_wait(ofull, tl & 1, a.err) ? 1 : 0;
       okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw) { ok = false; break; }
+      if (!okw) return false;
       tc_fence_after();
-      const int row0 = t * kBM + g * 32;
-#pragma unroll 1
-      for (int cc = 0; cc < kBN / 32; cc++) {
-        const int b = cc & 1;
-        unsigned char* eb = bufs + b * kEpiBuf;
-        const int x = cc * 32;
-        if (lane == 0) {
-          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          mbar_arrive_expect_tx(&cload[ew * 2 + b], kEpiBuf);
-          asm volatile(
-              "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-              ::"r"(smem_u32(eb)), "l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0),
-              "r"(smem_u32(&cload[ew * 2 + b]))
-              : "memory");
-        }
-        float v[32];
-        tmem_ld32(tmem_out + (uint32_t(g * 32) << 16) + cc * 32, v);
-        const bool mine = mbar_wait(&cload[ew * 2 + b], (cphase >> b) & 1, a.err);
-        cphase ^= 1u << b;
-        if (!__all_sync(0xffffffffu, mine)) { ok = false; break; }
-        unsigned char* rowp = eb + lane * 128;
+      float v[2][32];
+      tmem_ld32(tmem_out + (uint32_t(q * 32) << 16) + half * 64, v[0]);
+      tmem_ld32_async(tmem_out + (uint32_t(q * 32) << 16) + half * 64 + 32, v[1]);
+      tmem_ld_wait(v[1]);
+      tc_fence_before();
+      mbar_arrive(oempty);  // the accumulator is free for the next tile
+#pragma unroll
+      for (int b = 0; b < 2; b++) {
+        const bool mine = mbar_wait(&cload[wi * 2 + b], tl & 1, a.err);
+        if (!__all_sync(0xffffffffu, mine)) return false;
+        unsigned char* rowp = eb[b] + lane * 128;
 #pragma unroll
         for (int jj = 0; jj < 8; jj++) {
           float4* cp = reinterpret_cast<float4*>(rowp + ((jj ^ (lane & 7)) << 4));
           const float4 c = *cp;
-          float4 o = make_float4(v[4 * jj] * a.unscale2, v[4 * jj + 1] * a.unscale2, v[4 * jj + 2] * a.unscale2,
-                                 v[4 * jj + 3] * a.unscale2);
+          float4 o = make_float4(v[b][4 * jj] * a.unscale2, v[b][4 * jj + 1] * a.unscale2,
+                                 v[b][4 * jj + 2] * a.unscale2, v[b][4 * jj + 3] * a.unscale2);
           o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
           *cp = o;
         }
@@ -344,15 +350,36 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
         __syncwarp();
         if (lane == 0) {
           asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
-                       ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0), "r"(smem_u32(eb))
+                       ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"((half * 2 + b) * 32), "r"(t * kBM + q * 32),
+                       "r"(smem_u32(eb[b]))
                        : "memory");
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
       }
-      if (!ok) break;
-      tc_fence_before();
-      mbar_arrive(oempty);
+      return true;
+    };
+    bool ok = true;
+    uint32_t tl = 0;
+    int pending = -1;  // tile number whose residual prefetch is in flight
+    if (blockIdx.x < tiles) {
+      prefetch(blockIdx.x);
+      pending = 0;
     }
+    if (helper && blockIdx.x < tiles) ok = split(0);
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
+      for (int j = 0; j < 3 && ok; j++) ok = e1(tl, j);
+      if (ok && helper && t + int(gridDim.x) < tiles) ok = split(tl + 1);
+      if (ok) ok = e2(tl, t);
+      if (ok) pending = -1;
+      if (ok && t + int(gridDim.x) < tiles) {
+        prefetch(t + gridDim.x);
+        pending = int(tl + 1);
+      }
+    }
+    // a residual prefetch left unconsumed by an error lands before the CTA exits
+    if (pending >= 0 && lane == 0)
+      for (int b = 0; b < 2; b++) mbar_wait(&cload[wi * 2 + b], uint32_t(pending) & 1, a.err);
+    // every store has left shared memory and landed before the CTA exits
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
   }
