@@ -28,6 +28,7 @@
 #include "exact.cuh"
 #include "fast.cuh"
 #include "ffn.cuh"
+#include "attn_tc.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 
@@ -97,6 +98,8 @@ struct Workspace {
   // pack
   DevBuf rec_meta, frame_t, frame_q, frame_r, t_off, q_off, r_off, p_off, totals;
   DevBuf tok_recpos, rec_start, rec_row, bank_rec, bank_frame, query_rec, query_frame;
+  // the fused attention's record-aligned tiles (first row per tile) and row info
+  DevBuf tile_row, row_rc;
   // activations
   DevBuf x, qkv, bk, bv, mk, mv, qstate, mq, mh, sq, sk, p, index, gather;
   // weight-row scatter staging
@@ -414,6 +417,50 @@ kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
   return KC_OK;
 }
 
+// qkv = x·Wqkvᵀ, record-local attention and x += o in one kernel
+// (attn_tc.cuh) for the encoder block whose Wqkv is `mat`. Needs H = 128 and
+// a head dim of 32 (the kernel's fixed tiling); attn_fusable() says whether it
+// applies.
+bool attn_fusable(const kc_handle* h) { return h->d.h == 128 && h->d.hd == 32 && h->d.heads == 4; }
+
+uint64_t attn_tiles(uint64_t T) { return (T + kc::tc::kAtWindow - 1) / kc::tc::kAtWindow; }
+
+// The tile table and row info of a packed batch (once per batch).
+kc_status attn_prepare(kc_handle* h, Workspace& ws, uint64_t T) {
+  if (T == 0) return KC_OK;
+  const uint64_t tiles = attn_tiles(T);
+  KC_TRY(ensure(ws.tile_row, (tiles + 1) * 4), "workspace");
+  KC_TRY(ensure(ws.row_rc, T * 4), "workspace");
+  kc::tc::k_attn_tiles<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(
+      P<uint32_t>(ws.tok_recpos), P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), int(T), int(tiles),
+      P<uint32_t>(ws.row_rc), P<int>(ws.tile_row));
+  h->launches++;
+  return KC_OK;
+}
+
+kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, const uint32_t* word_ids,
+                  float word_alpha, float scale) {
+  if (T == 0) return KC_OK;
+  CUtensorMap xmap;
+  if (!kc::tc::make_x_map(&xmap, x, T))
+    return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for the attention operand");
+  kc::tc::AttnTcArgs aa{};
+  aa.T = int(T);
+  aa.tiles = int(attn_tiles(T));
+  aa.tile_row = P<int>(ws.tile_row);
+  aa.row_rc = P<uint32_t>(ws.row_rc);
+  aa.w = P<uint8_t>(h->images) + h->img_off[mat];
+  aa.a_scale = std::ldexp(1.0f, h->sa);
+  aa.unscale = std::ldexp(1.0f, -(h->sa + mat_sw(h, mat)));
+  aa.x = x; aa.tok_recpos = P<uint32_t>(ws.tok_recpos);
+  aa.word_ids = word_alpha != 0.0f ? word_ids : nullptr;
+  aa.word_alpha = word_alpha; aa.scale = scale; aa.err = h->d_err;
+  const unsigned grid = unsigned(std::min<uint64_t>(uint64_t(aa.tiles), uint64_t(h->sms)));
+  kc::tc::k_tc_attn<<<grid, kc::tc::kAtThreads, kc::tc::kAtSmem, h->stream>>>(xmap, aa);
+  h->launches++;
+  return KC_OK;
+}
+
 // One GEMM of the exact sequence: on the FP64 pipe in the oracle's order, or
 // (tc) on the tensor cores, where `mat` names the matrix in the tensor-core
 // list and B / ldb the same matrix for the FP64 kernel. The tensor-core path
@@ -662,19 +709,25 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   }
   const float attn_scale = float(1.0 / std::sqrt(double(d.hd)));
   const int enc_m = 0, mix_m = 3 * int(d.enc), sel_m = mix_m + 5 * int(d.mix);
+  if (attn_fusable(h) && d.enc > 0) KC_CHECK(attn_prepare(h, ws, T));
   for (uint32_t blk = 0; blk < d.enc && T > 0; blk++) {
-    {
-      ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
-      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, x, T, enc_m + 3 * blk, qkv));
-    }
-    {
-      ProfScope ps(h, kStEncAttn);
-      kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
-                               P<uint32_t>(ws.tok_recpos), b.word_alpha != 0.0f ? b.word_ids : nullptr,
-                               b.word_alpha};
-      kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, 0, h->stream>>>(
-          la);
-      h->launches++;
+    if (attn_fusable(h)) {  // q|k|v, attention and the residual in one kernel: q|k|v stay on chip
+      ProfScope ps(h, kStEncAttn, 2.0 * T * H * 3 * H, 4.0 * T * (2 * H));
+      KC_CHECK(tc_attn(h, ws, x, T, enc_m + 3 * blk, b.word_ids, b.word_alpha, attn_scale));
+    } else {
+      {
+        ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
+        KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, x, T, enc_m + 3 * blk, qkv));
+      }
+      {
+        ProfScope ps(h, kStEncAttn);
+        kc::LocalAttnFastArgs la{qkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
+                                 P<uint32_t>(ws.tok_recpos), b.word_alpha != 0.0f ? b.word_ids : nullptr,
+                                 b.word_alpha};
+        kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, 0,
+                                h->stream>>>(la);
+        h->launches++;
+      }
     }
     if (ffn_fusable(h)) {  // W1, ReLU, W2 and the residual in one kernel: h1 stays on chip
       ProfScope ps(h, kStEncFfn, 4.0 * T * H * FF, 4.0 * T * (2 * H));
@@ -1301,6 +1354,7 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiGate>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * 4)))
     return bail(e, "smem");
