@@ -44,9 +44,10 @@ constexpr int kAtWindow = 120;
 constexpr int kAtThreads = 384;
 constexpr int kAtChunk = 2 * kTileBytes;                 // one weight chunk / x K-chunk: 32 KB
 constexpr int kAtXBytes = 2 * kAtChunk;                  // x operand, 64 KB
-constexpr int kAtWStages = 3;
+constexpr int kAtWStages = 2;
 constexpr int kAtSlotBytes = 128 * 256;                  // one head's k | v for 128 rows
-constexpr int kAtSmem = kAtXBytes + kAtWStages * kAtChunk + 2 * kAtSlotBytes + 1024 + 512;
+constexpr int kAtResBytes = 128 * 128;                   // one head's 32 columns of x for 128 rows
+constexpr int kAtSmem = kAtXBytes + kAtWStages * kAtChunk + 2 * kAtSlotBytes + 2 * kAtResBytes + 1024 + 512;
 
 struct AttnTcArgs {
   int T;                       // rows (compact tokens)
@@ -92,9 +93,12 @@ __device__ __forceinline__ float4* at_row(unsigned char* slot, int i) {
 // float4 f of the row is at (at_key(slot, i) ^ (f << 4)).
 __device__ __forceinline__ uint32_t at_key(uint32_t slot_u32, int i) { return slot_u32 + i * 256 + ((i & 15) << 4); }
 
-__device__ __forceinline__ float4 lds4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+// A shared float4 where p holds, zeros elsewhere (no load issued).
+__device__ __forceinline__ float4 lds4_if(uint32_t addr, bool p) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n\t}"
+               : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w)
+               : "r"(addr), "r"(int(p)));
   return v;
 }
 
@@ -105,7 +109,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
   unsigned char* xs = smem;                                   // x operand (f32 boxes, then hi|lo)
   unsigned char* ws = smem + kAtXBytes;                       // weight ring
   unsigned char* kvs = ws + kAtWStages * kAtChunk;            // k|v staging, two slots
-  uint64_t* bars = reinterpret_cast<uint64_t*>(kvs + 2 * kAtSlotBytes);
+  unsigned char* res = kvs + 2 * kAtSlotBytes;                // residual x columns, one per half
+  uint64_t* bars = reinterpret_cast<uint64_t*>(res + 2 * kAtResBytes);
   uint64_t* xraw = bars;         // [2] x K-chunk landed
   uint64_t* xfull = bars + 2;    // [2] x K-chunk split
   uint64_t* xempty = bars + 4;   // the tile's MMAs are done with x
@@ -115,7 +120,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
   uint64_t* qempty = bars + 12;  // [2] q buffer read
   uint64_t* kvempty = bars + 14; // k and v read
   uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* rfull = bars + 16;   // [2] a half's residual columns landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -133,6 +139,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
     mbar_init(accfull, 1);
     mbar_init(kvempty, 256);
     mbar_init(drain, 1);
+    mbar_init(&rfull[0], 1);
+    mbar_init(&rfull[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -267,6 +275,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
     const int i = q * 32 + lane;  // this thread's row of the tile (its TMEM lane)
     const int bar_id = 2 + half;
     unsigned char* slot = kvs + half * kAtSlotBytes;
+    unsigned char* rb = res + half * kAtResBytes;  // x[:, hd*32 .. +32] of the tile, TMA 128-byte swizzle
+    const bool issuer = q == 0 && lane == 0;
     const uint32_t slot_u32 = smem_u32(slot);
     const bool words = a.word_ids != nullptr;
     const uint32_t lq = uint32_t(q * 32) << 16;
@@ -313,7 +323,11 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
 #pragma unroll
       for (int r = 0; r < 2; r++) {
         const int hd = 2 * half + r;
-        if (r == 1) named_bar(bar_id, 128);  // round 0 is done with the slot
+        if (r == 1) named_bar(bar_id, 128);  // round 0 is done with the slot and the residual buffer
+        if (issuer) {  // this round's residual columns, landing while the scores run
+          mbar_arrive_expect_tx(&rfull[half], kAtResBytes);
+          tma_load_2d(rb, &xmap, hd * 32, row0, &rfull[half]);
+        }
         float4* mine_row = at_row(slot, i);
         {
           float t[32];
@@ -346,12 +360,12 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
           for (int m = 0; m < 8; m++)
             qq[m] = make_float4(qv[4 * m] * a.unscale, qv[4 * m + 1] * a.unscale, qv[4 * m + 2] * a.unscale,
                                 qv[4 * m + 3] * a.unscale);
-          // all eight keys at once (rows past the record repeat its last row and
-          // are masked out below), so the eight 32-long fmaf chains interleave;
-          // each chain keeps the order of the one-key-at-a-time loop
+          // all eight keys at once, so the eight 32-long fmaf chains interleave
+          // (each keeps the order of the one-key-at-a-time loop); keys past the
+          // record load nothing (zeros) and are masked out below
           uint32_t kr[KC_RW];
 #pragma unroll
-          for (int j = 0; j < KC_RW; j++) kr[j] = at_key(slot_u32, s0 + (j < cnt ? j : cnt - 1));
+          for (int j = 0; j < KC_RW; j++) kr[j] = at_key(slot_u32, s0 + j);
           float p[KC_RW];
 #pragma unroll
           for (int j = 0; j < KC_RW; j++) p[j] = 0.f;
@@ -359,7 +373,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
           for (int m = 0; m < 8; m++)
 #pragma unroll
             for (int j = 0; j < KC_RW; j++) {
-              const float4 kv = lds4(kr[j] ^ (m << 4));
+              const float4 kv = lds4_if(kr[j] ^ (m << 4), j < cnt);
               p[j] = fmaf(qq[m].x, kv.x, p[j]); p[j] = fmaf(qq[m].y, kv.y, p[j]);
               p[j] = fmaf(qq[m].z, kv.z, p[j]); p[j] = fmaf(qq[m].w, kv.w, p[j]);
             }
@@ -383,38 +397,37 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
             const float pj = p[j] * inv;
 #pragma unroll
             for (int m = 0; m < 8; m++) {
-              const float4 vv = lds4(kr[j] ^ ((8 + m) << 4));
+              const float4 vv = lds4_if(kr[j] ^ ((8 + m) << 4), j < cnt);
               o[m].x = fmaf(pj, vv.x, o[m].x); o[m].y = fmaf(pj, vv.y, o[m].y);
               o[m].z = fmaf(pj, vv.z, o[m].z); o[m].w = fmaf(pj, vv.w, o[m].w);
             }
           }
         }
-        // the residual rows of this warp's quarter for head hd, in flight across the barriers
-        float4 xres[8];
+        // x += o on this thread's row, in the residual buffer
+        mbar_wait(&rfull[half], uint32_t(r), a.err);
+        if (valid) {
+          float4* xr = reinterpret_cast<float4*>(rb + i * 128);
+#pragma unroll
+          for (int m = 0; m < 8; m++) {
+            float4 xv = xr[m ^ (i & 7)];
+            xv.x += o[m].x; xv.y += o[m].y; xv.z += o[m].z; xv.w += o[m].w;
+            xr[m ^ (i & 7)] = xv;
+          }
+        }
+        named_bar(bar_id, 128);  // the updated rows are in the buffer
+        // coalesced stores: 8 lanes per row, 4 rows per instruction
         const int cl = lane & 7;
 #pragma unroll
         for (int it = 0; it < 8; it++) {
           const int rr = q * 32 + (lane >> 3) + 4 * it;
-          if (rr < n) xres[it] = *reinterpret_cast<const float4*>(a.x + size_t(row0 + rr) * KC_H + hd * 32 + cl * 4);
-        }
-        named_bar(bar_id, 128);  // every token is done reading the slot's k | v rows
-        if (valid) {
-#pragma unroll
-          for (int m = 0; m < 8; m++) mine_row[m ^ (i & 15)] = o[m];
-        }
-        named_bar(bar_id, 128);  // the outputs are in the slot
-#pragma unroll
-        for (int it = 0; it < 8; it++) {
-          const int rr = q * 32 + (lane >> 3) + 4 * it;
-          if (rr < n) {
-            const float4 ov = at_row(slot, rr)[cl ^ (rr & 15)];
-            float4 xv = xres[it];
-            xv.x += ov.x; xv.y += ov.y; xv.z += ov.z; xv.w += ov.w;
-            *reinterpret_cast<float4*>(a.x + size_t(row0 + rr) * KC_H + hd * 32 + cl * 4) = xv;
-          }
+          if (rr < n)
+            *reinterpret_cast<float4*>(a.x + size_t(row0 + rr) * KC_H + hd * 32 + cl * 4) =
+                reinterpret_cast<const float4*>(rb + rr * 128)[cl ^ (rr & 7)];
         }
       }
     }
+    // a residual load left in flight by an expired wait lands before the CTA exits
+    if (issuer && tl > 0) mbar_wait(&rfull[half], 1u, a.err);
   }
 
   tc_fence_before();
