@@ -215,71 +215,140 @@ __global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
 // ---------------------------------------------------------------------------
 // Mixer cross-attention + residual, f32// ---------------------------------------------------------------------------
 // Mixer cross-attention + residual, f32 (oracle.ts:292-293 with the open
-// mixer mask). One CTA of 128 threads per question; warp w = head w.
+// mixer mask). One CTA per frame: its questions go in chunks of up to
+// kCaChunk, and each bank row's k and v slices are loaded once per chunk.
+// Per (question, head): score j = the 32-long fmaf chain q·k_j in dimension
+// order, scaled; softmax with lane-strided max and sum (lane l takes j = l,
+// l+32, ...) reduced by an xor-shuffle tree; output = (sum over even j of
+// p_j v_j + sum over odd j of p_j v_j) / sum, added to the question row.
 // ---------------------------------------------------------------------------
-struct CrossAttnFastArgs {
+constexpr int kCaChunk = 8;
+constexpr int kCaThreads = 256;
+
+struct CrossAttnFrameArgs {
   const float* mq;
   const float* mk;
   const float* mv;
   float* query;
-  const uint32_t* query_frame;
-  const uint64_t* r_off;
+  const uint64_t* q_off;   // [frames + 1]
+  const uint64_t* r_off;   // [frames + 1]
+  int qc;                  // questions per chunk (the score buffer holds qc x 4 x max_r)
   uint32_t max_r;
   float scale;
 };
 
-__global__ void __launch_bounds__(128) k_cross_attn_fast(CrossAttnFastArgs a) {
-  extern __shared__ __align__(16) float ca_smem[];  // [4][max_r]
-  __shared__ float qs[KC_H];
-  __shared__ float inv_s[KC_HEADS];
-  const uint32_t qi = blockIdx.x;
-  const uint32_t f = a.query_frame[qi];
-  const uint64_t rb = a.r_off[f];
-  const int R = int(a.r_off[f + 1] - rb);
+__global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameArgs a) {
+  extern __shared__ __align__(16) float caf_smem[];  // scores [qc][4][max_r], then q [qc][128]
+  __shared__ float inv_s[kCaChunk][KC_HEADS];
+  const uint32_t f = blockIdx.x;
+  const uint64_t qb = a.q_off[f], rb = a.r_off[f];
+  const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
+  if (nq == 0) return;
+  float* sc = caf_smem;
+  float* qs = caf_smem + size_t(a.qc) * KC_HEADS * a.max_r;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  qs[tid] = a.mq[uint64_t(qi) * KC_H + tid];
-  __syncthreads();
-  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
-    const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
-    const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
-    float s = 0.f;
+  for (int q0 = 0; q0 < nq; q0 += a.qc) {
+    const int nc = min(a.qc, nq - q0);
+    for (int i = tid; i < nc * KC_H; i += kCaThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
+    __syncthreads();
+    // scores: one (head, key) per thread, head-major so a warp reads one q
+    // slice (a broadcast); the k slice is loaded once for the chunk, and the
+    // chunk's questions run as independent chains
+    for (int idx = tid; idx < R * KC_HEADS; idx += kCaThreads) {
+      const int head = idx / R, j = idx - head * R, hb = head * KC_HEAD_DIM;
+      const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
+      float4 k4[KC_HEAD_DIM / 4];
 #pragma unroll
-    for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
-      const float4 k = kr[d4];
-      s = fmaf(qs[hb + 4 * d4], k.x, s);
-      s = fmaf(qs[hb + 4 * d4 + 1], k.y, s);
-      s = fmaf(qs[hb + 4 * d4 + 2], k.z, s);
-      s = fmaf(qs[hb + 4 * d4 + 3], k.w, s);
+      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) k4[d4] = kr[d4];
+      float sv[kCaChunk];
+#pragma unroll
+      for (int c = 0; c < kCaChunk; c++) sv[c] = 0.f;
+#pragma unroll
+      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++)
+#pragma unroll
+        for (int c = 0; c < kCaChunk; c++)
+          if (c < nc) {
+            const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
+            sv[c] = fmaf(q4.x, k4[d4].x, sv[c]);
+            sv[c] = fmaf(q4.y, k4[d4].y, sv[c]);
+            sv[c] = fmaf(q4.z, k4[d4].z, sv[c]);
+            sv[c] = fmaf(q4.w, k4[d4].w, sv[c]);
+          }
+#pragma unroll
+      for (int c = 0; c < kCaChunk; c++)
+        if (c < nc) sc[(c * KC_HEADS + head) * a.max_r + j] = sv[c] * a.scale;
     }
-    ca_smem[head * a.max_r + j] = s * a.scale;
-  }
-  __syncthreads();
-  {
-    float* row = ca_smem + warp * a.max_r;
-    float mx = -INFINITY;
-    for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    for (int j = lane; j < R; j += 32) {
-      const float e = expf(row[j] - mx);
-      row[j] = e;
-      sum += e;
+    __syncthreads();
+    // softmax rows (question, head): one warp each
+    for (int rw = warp; rw < nc * KC_HEADS; rw += kCaThreads / 32) {
+      float* row = sc + size_t(rw) * a.max_r;
+      float mx = -INFINITY;
+      for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+      for (int j = lane; j < R; j += 32) {
+        const float e = expf(row[j] - mx);
+        row[j] = e;
+        sum += e;
+      }
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) inv_s[rw >> 2][rw & 3] = 1.f / fmaxf(sum, 1e-20f);
     }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) inv_s[warp] = 1.f / fmaxf(sum, 1e-20f);
-  }
-  __syncthreads();
-  {
-    const int head = tid >> 5, d = tid & 31, col = head * KC_HEAD_DIM + d;
-    const float* row = ca_smem + head * a.max_r;
-    float v0 = 0.f, v1 = 0.f;
-    int j = 0;
-    for (; j + 1 < R; j += 2) {
-      v0 = fmaf(row[j], a.mv[(rb + j) * KC_H + col], v0);
-      v1 = fmaf(row[j + 1], a.mv[(rb + j + 1) * KC_H + col], v1);
+    __syncthreads();
+    // p·v: one output column per thread for every other question of the chunk,
+    // each v element loaded once for them
+    {
+      const int col = tid & (KC_H - 1), head = col >> 5, c0 = tid >> 7;
+      float v0[kCaChunk / 2], v1[kCaChunk / 2];
+#pragma unroll
+      for (int u = 0; u < kCaChunk / 2; u++) v0[u] = v1[u] = 0.f;
+      const float* vcol = a.mv + rb * KC_H + col;
+      int j = 0;
+      // sixteen v elements in flight per step; the even / odd sums keep their order
+      for (; j + 15 < R; j += 16) {
+        float vv[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) vv[e] = vcol[size_t(j + e) * KC_H];
+#pragma unroll
+        for (int u = 0; u < kCaChunk / 2; u++) {
+          const int c = c0 + 2 * u;
+          if (c < nc) {
+            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              v0[u] = fmaf(row[e], vv[e], v0[u]);
+              v1[u] = fmaf(row[e + 1], vv[e + 1], v1[u]);
+            }
+          }
+        }
+      }
+      for (; j + 1 < R; j += 2) {
+        const float va = vcol[size_t(j) * KC_H], vb = vcol[size_t(j + 1) * KC_H];
+#pragma unroll
+        for (int u = 0; u < kCaChunk / 2; u++) {
+          const int c = c0 + 2 * u;
+          if (c < nc) {
+            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r;
+            v0[u] = fmaf(row[j], va, v0[u]);
+            v1[u] = fmaf(row[j + 1], vb, v1[u]);
+          }
+        }
+      }
+      if (j < R) {
+        const float va = vcol[size_t(j) * KC_H];
+#pragma unroll
+        for (int u = 0; u < kCaChunk / 2; u++) {
+          const int c = c0 + 2 * u;
+          if (c < nc) v0[u] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, v0[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCaChunk / 2; u++) {
+        const int c = c0 + 2 * u;
+        if (c < nc) a.query[(qb + q0 + c) * KC_H + col] += (v0[u] + v1[u]) * inv_s[c][head];
+      }
     }
-    if (j < R) v0 = fmaf(row[j], a.mv[(rb + j) * KC_H + col], v0);
-    a.query[uint64_t(qi) * KC_H + col] += (v0 + v1) * inv_s[head];
+    __syncthreads();
   }
 }
 

@@ -417,6 +417,17 @@ kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
   return KC_OK;
 }
 
+// The per-frame cross attention's question chunk for a batch whose largest
+// bank is max_r rows (its score buffer stays within 96 KB), and its shared memory.
+int cross_chunk(uint32_t max_r) {
+  const uint64_t fit = (96u << 10) / (uint64_t(KC_HEADS) * 4 * std::max<uint32_t>(max_r, 1));
+  return int(std::min<uint64_t>(std::max<uint64_t>(fit, 1), kc::kCaChunk));
+}
+size_t cross_smem(uint32_t max_r) {
+  const int qc = cross_chunk(max_r);
+  return size_t(qc) * KC_HEADS * std::max<uint32_t>(max_r, 1) * 4 + size_t(qc) * KC_H * 4;
+}
+
 // qkv = x·Wqkvᵀ, record-local attention and x += o in one kernel
 // (attn_tc.cuh) for the encoder block whose Wqkv is `mat`. Needs H = 128 and
 // a head dim of 32 (the kernel's fixed tiling); attn_fusable() says whether it
@@ -758,9 +769,10 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
-      kc::CrossAttnFastArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
-                               P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off), tot.max_r, attn_scale};
-      kc::k_cross_attn_fast<<<unsigned(Q), 128, size_t(tot.max_r) * 4 * 4, h->stream>>>(ca);
+      kc::CrossAttnFrameArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
+                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), cross_chunk(tot.max_r), tot.max_r,
+                                attn_scale};
+      kc::k_cross_attn_frame<<<b.frames, kc::kCaThreads, cross_smem(tot.max_r), h->stream>>>(ca);
       h->launches++;
       KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, P<float>(ws.qstate), Q, m0 + 3, P<float>(ws.mh)));
       KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, P<float>(ws.mh), Q, m0 + 4, P<float>(ws.qstate)));
@@ -1355,8 +1367,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
-      (e = cudaFuncSetAttribute(kc::k_cross_attn_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(KC_MAX_BANK) * 4 * 4)))
+      (e = cudaFuncSetAttribute(kc::k_cross_attn_frame, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (96 << 10) + kc::kCaChunk * KC_H * 4)))
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
