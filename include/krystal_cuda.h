@@ -208,6 +208,12 @@ typedef struct kc_stage_times {
   double enc_ffn_ms;
   uint64_t enc_ffn_launches;
   double enc_ffn_flops, enc_ffn_bytes;
+  /* the fused attention kernel (q|k|v projection, record-local attention,
+     residual in one launch): its time, launches and algorithmic FLOPs
+     (the projection) and bytes (x read and written) */
+  double enc_attn_tc_ms;
+  uint64_t enc_attn_tc_launches;
+  double enc_attn_tc_flops, enc_attn_tc_bytes;
 } kc_stage_times;
 
 uint32_t kc_abi_version(void);

@@ -123,7 +123,7 @@ struct BackWs {
 };
 
 enum Stage { kStPack, kStEmbed, kStEncGemm, kStEncAttn, kStPool, kStMixer, kStSelector, kStFallback, kStEncFfn,
-             kStCount };
+             kStEncAttnTc, kStCount };
 
 // The matrices the tensor-core path multiplies by, in a fixed order:
 // per encoder block QKV [3H,H], W1 [F,H], W2 [H,F]; per mixer block Wq, Wk,
@@ -264,7 +264,7 @@ void prof_collect(kc_handle* h) {
   cudaStreamSynchronize(h->stream);
   double* dst[kStCount] = {&h->prof.pack_ms, &h->prof.embed_ms, &h->prof.enc_gemm_ms, &h->prof.enc_attn_ms,
                            &h->prof.pool_ms, &h->prof.mixer_ms, &h->prof.selector_ms, &h->prof.fallback_ms,
-                           &h->prof.enc_ffn_ms};
+                           &h->prof.enc_ffn_ms, &h->prof.enc_attn_tc_ms};
   for (size_t i = 0; i < h->ev_used.size(); i++) {
     float ms = 0;
     auto& pr = h->ev_pool[h->ev_used[i].second];
@@ -279,6 +279,10 @@ void prof_collect(kc_handle* h) {
       h->prof.enc_ffn_launches++;
       h->prof.enc_ffn_flops += h->ev_flops[i];
       h->prof.enc_ffn_bytes += h->ev_bytes[i];
+    } else if (h->ev_used[i].first == kStEncAttnTc) {
+      h->prof.enc_attn_tc_launches++;
+      h->prof.enc_attn_tc_flops += h->ev_flops[i];
+      h->prof.enc_attn_tc_bytes += h->ev_bytes[i];
     }
   }
   h->ev_used.clear();
@@ -723,7 +727,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   if (attn_fusable(h) && d.enc > 0) KC_CHECK(attn_prepare(h, ws, T));
   for (uint32_t blk = 0; blk < d.enc && T > 0; blk++) {
     if (attn_fusable(h)) {  // q|k|v, attention and the residual in one kernel: q|k|v stay on chip
-      ProfScope ps(h, kStEncAttn, 2.0 * T * H * 3 * H, 4.0 * T * (2 * H));
+      ProfScope ps(h, kStEncAttnTc, 2.0 * T * H * 3 * H, 4.0 * T * (2 * H));
       KC_CHECK(tc_attn(h, ws, x, T, enc_m + 3 * blk, b.word_ids, b.word_alpha, attn_scale));
     } else {
       {
