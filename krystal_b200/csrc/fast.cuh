@@ -354,13 +354,19 @@ __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameA
 
 // ---------------------------------------------------------------------------
 // Pointer selector, f32, with certification (selectorOracle,
-// forward/oracle.ts:332-382). One CTA of 256 threads per question. Writes p
-// and the index, and raises flags[frame] when the decision is not certain.
+// forward/oracle.ts:332-382). One CTA of 256 threads per frame: the frame's
+// questions go in chunks of up to kSelChunk, whose scores are computed
+// together so each bank key row is read once per chunk (per score: the
+// 128-long fmaf chain in dimension order); then each question of the chunk in
+// turn: mask, top two, softmax, p, the argmax or the draw, and its
+// certification. Writes p and the index, and raises flags[frame] when a
+// decision is not certain.
 // ---------------------------------------------------------------------------
+constexpr int kSelChunk = 8;
+
 struct SelectFastArgs {
   const float* sq;
   const float* sk;
-  const uint32_t* query_frame;
   const uint64_t* r_off;
   const uint64_t* q_off;
   const uint64_t* p_off;
@@ -371,6 +377,7 @@ struct SelectFastArgs {
   const uint32_t* band_ids;
   const double* uniforms;
   uint32_t max_r;
+  int qc;           // questions per chunk (the score buffer holds qc x max_r)
   float scale;
   float tau;        // certified argmax: top-two score gap above tau
   float tau_c;      // certified draw: the uniform farther than tau_c from a cumulative boundary
@@ -381,152 +388,174 @@ struct SelectFastArgs {
 
 __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
   constexpr int NT = 256;
-  extern __shared__ __align__(16) float sel_smem[];  // [max_r]
-  __shared__ float qs[KC_H];
+  extern __shared__ __align__(16) float sel_smem[];  // scores [qc][max_r], then q [qc][128]
   __shared__ float red_f[NT / 32];
   __shared__ float red_g[NT / 32];
   __shared__ uint32_t red_u[NT / 32];
   __shared__ uint32_t red_i[NT / 32];
   __shared__ int red_b[NT / 32];
-  const uint32_t qi = blockIdx.x;
-  const uint32_t f = a.query_frame[qi];
-  const uint64_t rb = a.r_off[f];
-  const int R = int(a.r_off[f + 1] - rb);
-  const uint64_t il = qi - a.q_off[f];
+  const uint32_t f = blockIdx.x;
+  const uint64_t rb = a.r_off[f], qb = a.q_off[f];
+  const int R = int(a.r_off[f + 1] - rb), nq = int(a.q_off[f + 1] - qb);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (nq == 0) return;
   if (R == 0) {
-    if (tid == 0) a.index[qi] = KC_INVALID;
+    for (int c = tid; c < nq; c += NT) a.index[qb + c] = KC_INVALID;
     return;
   }
-  float* prow = a.p + a.p_off[f] + il * uint64_t(R);
-  if (tid < KC_H) qs[tid] = a.sq[uint64_t(qi) * KC_H + tid];
-
-  bool reopen = false;
-  const uint32_t* sa = nullptr;
-  uint32_t ba = 0;
-  if (a.schema_allow) {
-    sa = a.schema_allow + uint64_t(qi) * 8;
-    ba = a.band_allow[qi];
-    uint32_t admitted = 0;
-    for (int j = tid; j < R; j += NT) {
-      const uint32_t gr = a.bank_rec[rb + j];
-      const uint32_t s = a.schema_ids[gr], b = a.band_ids[gr];
-      admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
-    }
-    for (int o = 16; o; o >>= 1) admitted += __shfl_xor_sync(0xffffffffu, admitted, o);
-    if (lane == 0) red_u[warp] = admitted;
+  float* qs = sel_smem + size_t(a.qc) * a.max_r;
+  for (int q0 = 0; q0 < nq; q0 += a.qc) {
+    const int nc = min(a.qc, nq - q0);
+    for (int i = tid; i < nc * KC_H; i += NT) qs[i] = a.sq[(qb + q0) * KC_H + i];
     __syncthreads();
-    uint32_t tot = 0;
-    for (int w = 0; w < NT / 32; w++) tot += red_u[w];
-    reopen = tot == 0;
-  }
-  __syncthreads();
-
-  // scores; per-thread best / second-best (value, first index) and finiteness
-  float b1 = -INFINITY, b2 = -INFINITY;
-  uint32_t i1 = KC_INVALID;
-  int nonfinite = 0, open = 0;
-  for (int j = tid; j < R; j += NT) {
-    const float4* kr = reinterpret_cast<const float4*>(a.sk + (rb + j) * KC_H);
-    float s = 0.f;
-#pragma unroll 8
-    for (int d4 = 0; d4 < KC_H / 4; d4++) {
-      const float4 k = kr[d4];
-      s = fmaf(qs[4 * d4], k.x, s);
-      s = fmaf(qs[4 * d4 + 1], k.y, s);
-      s = fmaf(qs[4 * d4 + 2], k.z, s);
-      s = fmaf(qs[4 * d4 + 3], k.w, s);
-    }
-    float m = 0.f;
-    if (sa && !reopen) {
-      const uint32_t gr = a.bank_rec[rb + j];
-      const uint32_t sid = a.schema_ids[gr], b = a.band_ids[gr];
-      m = (sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u)) ? 0.f : -1e30f;
-    }
-    const float sc = s * a.scale + m;
-    sel_smem[j] = sc;
-    nonfinite |= !isfinite(s);
-    open |= sc >= -1e29f;
-    if (sc > b1) { b2 = b1; b1 = sc; i1 = uint32_t(j); }
-    else if (sc > b2) b2 = sc;
-  }
-  // block reduce: top two values, index of the first top, any-open, any-nonfinite
-  for (int o = 16; o; o >>= 1) {
-    const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o), ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
-    const uint32_t oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
-    if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b2 = fmaxf(b1, ob2); b1 = ob1; i1 = oi1; }
-    else b2 = fmaxf(b2, ob1);
-    nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
-    open |= __shfl_xor_sync(0xffffffffu, open, o);
-  }
-  if (lane == 0) { red_f[warp] = b1; red_g[warp] = b2; red_i[warp] = i1; red_b[warp] = (nonfinite << 1) | open; }
-  __syncthreads();
-  float B1 = red_f[0], B2 = red_g[0];
-  uint32_t I1 = red_i[0];
-  int flagsum = red_b[0];
-  for (int w = 1; w < NT / 32; w++) {
-    const float ob1 = red_f[w], ob2 = red_g[w];
-    const uint32_t oi1 = red_i[w];
-    if (ob1 > B1 || (ob1 == B1 && oi1 < I1)) { B2 = fmaxf(B1, ob2); B1 = ob1; I1 = oi1; }
-    else B2 = fmaxf(B2, ob1);
-    flagsum |= red_b[w];
-  }
-  const bool any_nonfinite = flagsum & 2, any_open = flagsum & 1;
-  __syncthreads();
-  // softmax (the all-blocked row keeps p = 0)
-  float inv = 0.f;
-  if (any_open) {
-    float sum = 0.f;
+    // raw dot products for the chunk: one key row per thread, read once
     for (int j = tid; j < R; j += NT) {
-      const float e = expf(sel_smem[j] - B1);
-      sel_smem[j] = e;
-      sum += e;
+      const float4* kr = reinterpret_cast<const float4*>(a.sk + (rb + j) * KC_H);
+      float sv[kSelChunk];
+#pragma unroll
+      for (int c = 0; c < kSelChunk; c++) sv[c] = 0.f;
+#pragma unroll 4
+      for (int d4 = 0; d4 < KC_H / 4; d4++) {
+        const float4 k = kr[d4];
+#pragma unroll
+        for (int c = 0; c < kSelChunk; c++)
+          if (c < nc) {
+            const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H)[d4];
+            sv[c] = fmaf(q4.x, k.x, sv[c]);
+            sv[c] = fmaf(q4.y, k.y, sv[c]);
+            sv[c] = fmaf(q4.z, k.z, sv[c]);
+            sv[c] = fmaf(q4.w, k.w, sv[c]);
+          }
+      }
+#pragma unroll
+      for (int c = 0; c < kSelChunk; c++)
+        if (c < nc) sel_smem[size_t(c) * a.max_r + j] = sv[c];
     }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) red_f[warp] = sum;
     __syncthreads();
-    float tot = 0.f;
-    for (int w = 0; w < NT / 32; w++) tot += red_f[w];
-    inv = 1.f / fmaxf(tot, 1e-20f);
-  }
-  for (int j = tid; j < R; j += NT) {
-    const float pv = any_open ? sel_smem[j] * inv : 0.f;
-    sel_smem[j] = pv;
-    prow[j] = pv;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    bool certain = !any_nonfinite;
-    uint32_t best;
-    if (!any_open) {
-      best = KC_INVALID;  // every score below -1e29 on any accurate computation
-    } else if (a.uniforms) {
-      // sampleRow's inverse CDF; certain when the draw is clear of both edges
-      const double u = a.uniforms[qi];
-      double cum = 0.0, prev = 0.0;
-      int last = -1, drawn = -2;
-      for (int j = 0; j < R; j++) {
-        const double w = sel_smem[j];
-        if (!(w > 0)) continue;
-        last = j;
-        prev = cum;
-        cum += w;
-        if (u < cum) { drawn = j; break; }
+    for (int c = 0; c < nc; c++) {
+      const uint64_t qi = qb + q0 + c;
+      float* row = sel_smem + size_t(c) * a.max_r;
+      float* prow = a.p + a.p_off[f] + uint64_t(q0 + c) * uint64_t(R);
+      bool reopen = false;
+      const uint32_t* sa = nullptr;
+      uint32_t ba = 0;
+      if (a.schema_allow) {
+        sa = a.schema_allow + qi * 8;
+        ba = a.band_allow[qi];
+        uint32_t admitted = 0;
+        for (int j = tid; j < R; j += NT) {
+          const uint32_t gr = a.bank_rec[rb + j];
+          const uint32_t s = a.schema_ids[gr], b = a.band_ids[gr];
+          admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
+        }
+        for (int o = 16; o; o >>= 1) admitted += __shfl_xor_sync(0xffffffffu, admitted, o);
+        if (lane == 0) red_u[warp] = admitted;
+        __syncthreads();
+        uint32_t tot = 0;
+        for (int w = 0; w < NT / 32; w++) tot += red_u[w];
+        reopen = tot == 0;
       }
-      if (drawn == -2) {
-        drawn = last;
-        certain = certain && (u - cum > a.tau_c);
-      } else {
-        certain = certain && (cum - u > a.tau_c) && (u - prev > a.tau_c || drawn == 0);
+      __syncthreads();
+      // scaled, masked scores; per-thread best / second-best (value, first index) and finiteness
+      float b1 = -INFINITY, b2 = -INFINITY;
+      uint32_t i1 = KC_INVALID;
+      int nonfinite = 0, open = 0;
+      for (int j = tid; j < R; j += NT) {
+        const float s = row[j];
+        float m = 0.f;
+        if (sa && !reopen) {
+          const uint32_t gr = a.bank_rec[rb + j];
+          const uint32_t sid = a.schema_ids[gr], b = a.band_ids[gr];
+          m = (sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u)) ? 0.f : -1e30f;
+        }
+        const float sc = s * a.scale + m;
+        row[j] = sc;
+        nonfinite |= !isfinite(s);
+        open |= sc >= -1e29f;
+        if (sc > b1) { b2 = b1; b1 = sc; i1 = uint32_t(j); }
+        else if (sc > b2) b2 = sc;
       }
-      // tiny weights near zero may flip between zero and positive
-      best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
-    } else {
-      best = I1;
-      certain = certain && (R == 1 || B1 - B2 > a.tau);
+      // block reduce: top two values, index of the first top, any-open, any-nonfinite
+      for (int o = 16; o; o >>= 1) {
+        const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o), ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const uint32_t oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
+        if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b2 = fmaxf(b1, ob2); b1 = ob1; i1 = oi1; }
+        else b2 = fmaxf(b2, ob1);
+        nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
+        open |= __shfl_xor_sync(0xffffffffu, open, o);
+      }
+      if (lane == 0) { red_f[warp] = b1; red_g[warp] = b2; red_i[warp] = i1; red_b[warp] = (nonfinite << 1) | open; }
+      __syncthreads();
+      float B1 = red_f[0], B2 = red_g[0];
+      uint32_t I1 = red_i[0];
+      int flagsum = red_b[0];
+      for (int w = 1; w < NT / 32; w++) {
+        const float ob1 = red_f[w], ob2 = red_g[w];
+        const uint32_t oi1 = red_i[w];
+        if (ob1 > B1 || (ob1 == B1 && oi1 < I1)) { B2 = fmaxf(B1, ob2); B1 = ob1; I1 = oi1; }
+        else B2 = fmaxf(B2, ob1);
+        flagsum |= red_b[w];
+      }
+      const bool any_nonfinite = flagsum & 2, any_open = flagsum & 1;
+      __syncthreads();
+      // softmax (the all-blocked row keeps p = 0)
+      float inv = 0.f;
+      if (any_open) {
+        float sum = 0.f;
+        for (int j = tid; j < R; j += NT) {
+          const float e = expf(row[j] - B1);
+          row[j] = e;
+          sum += e;
+        }
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) red_f[warp] = sum;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < NT / 32; w++) tot += red_f[w];
+        inv = 1.f / fmaxf(tot, 1e-20f);
+      }
+      for (int j = tid; j < R; j += NT) {
+        const float pv = any_open ? row[j] * inv : 0.f;
+        row[j] = pv;
+        prow[j] = pv;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        bool certain = !any_nonfinite;
+        uint32_t best;
+        if (!any_open) {
+          best = KC_INVALID;  // every score below -1e29 on any accurate computation
+        } else if (a.uniforms) {
+          // sampleRow's inverse CDF; certain when the draw is clear of both edges
+          const double u = a.uniforms[qi];
+          double cum = 0.0, prev = 0.0;
+          int last = -1, drawn = -2;
+          for (int j = 0; j < R; j++) {
+            const double w = row[j];
+            if (!(w > 0)) continue;
+            last = j;
+            prev = cum;
+            cum += w;
+            if (u < cum) { drawn = j; break; }
+          }
+          if (drawn == -2) {
+            drawn = last;
+            certain = certain && (u - cum > a.tau_c);
+          } else {
+            certain = certain && (cum - u > a.tau_c) && (u - prev > a.tau_c || drawn == 0);
+          }
+          // tiny weights near zero may flip between zero and positive
+          best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
+        } else {
+          best = I1;
+          certain = certain && (R == 1 || B1 - B2 > a.tau);
+        }
+        a.index[qi] = best;
+        if (!certain) atomicOr(&a.flags[f], 1u);
+      }
+      // red_* and this row are reused by the next question
+      __syncthreads();
     }
-    a.index[qi] = best;
-    if (!certain) atomicOr(&a.flags[f], 1u);
   }
 }
 

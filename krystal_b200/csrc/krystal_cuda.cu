@@ -432,6 +432,16 @@ size_t cross_smem(uint32_t max_r) {
   return size_t(qc) * KC_HEADS * std::max<uint32_t>(max_r, 1) * 4 + size_t(qc) * KC_H * 4;
 }
 
+// The same for the per-frame selector (scores [qc][max_r], then q [qc][128]).
+int sel_chunk(uint32_t max_r) {
+  const uint64_t fit = (96u << 10) / (4ull * std::max<uint32_t>(max_r, 1));
+  return int(std::min<uint64_t>(std::max<uint64_t>(fit, 1), kc::kSelChunk));
+}
+size_t sel_smem(uint32_t max_r) {
+  const int qc = sel_chunk(max_r);
+  return size_t(qc) * std::max<uint32_t>(max_r, 1) * 4 + size_t(qc) * KC_H * 4;
+}
+
 // qkv = x·Wqkvᵀ, record-local attention and x += o in one kernel
 // (attn_tc.cuh) for the encoder block whose Wqkv is `mat`. Needs H = 128 and
 // a head dim of 32 (the kernel's fixed tiling); attn_fusable() says whether it
@@ -788,14 +798,15 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, sel_m + 1, P<float>(ws.sk)));
     kc::SelectFastArgs sa{};
     sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk);
-    sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
+    sa.r_off = P<uint64_t>(ws.r_off);
     sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
     sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
     sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
-    sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = float(1.0 / std::sqrt(double(H)));
+    sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
+    sa.scale = float(1.0 / std::sqrt(double(H)));
     sa.tau = h->tau; sa.tau_c = h->tau_c;
     sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
-    kc::k_select_fast<<<unsigned(Q), 256, size_t(tot.max_r) * 4, h->stream>>>(sa);
+    kc::k_select_fast<<<b.frames, 256, sel_smem(tot.max_r), h->stream>>>(sa);
     h->launches++;
   }
   KC_TRY(cudaGetLastError(), "launch");
@@ -1372,7 +1383,9 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_frame, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (96 << 10) + kc::kCaChunk * KC_H * 4)))
+                                (96 << 10) + kc::kCaChunk * KC_H * 4)) ||
+      (e = cudaFuncSetAttribute(kc::k_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (96 << 10) + kc::kSelChunk * KC_H * 4)))
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
