@@ -99,62 +99,70 @@ __global__ void __launch_bounds__(kEmbedWarps * 32, 2) k_embed_exact(EmbedArgs a
 //   C = relu(f32(A·Bᵀ))                    kEpiRelu   (reluOracle of the W1 output)
 //   C = f32(C + f32(A·Bᵀ))                 kEpiResid  (addInPlace of the W2 output)
 // A [M,K] f32, B [N,K] f32 (weights, [out,in]); every output is one f64
-// accumulator over k = 0..K-1 in order. 128x128 CTA tile, 8x8 per thread,
-// operands converted to f64 once when staged in shared memory.
+// accumulator over k = 0..K-1 in order. Square CTA tiles of 128, 64 or 32
+// rows, operands converted to f64 once when staged in shared memory.
 // Requires N % 128 == 0, K % 8 == 0, 16-byte aligned rows.
 // ---------------------------------------------------------------------------
 //   C = gate > 0 ? f32(A·Bᵀ) : 0            kEpiGate   (reluBackward of a saved ReLU output,
 //                                                        backward.ts:65-70)
 enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2, kEpiGate = 3 };
 
-template <int EPI>
-__global__ void __launch_bounds__(256, 1) k_dgemm_exact(const float* __restrict__ A, const float* __restrict__ B,
-                                                       float* C, int M, int N, int K, int lda, int ldb, int ldc,
-                                                       const float* __restrict__ gate = nullptr) {
-  constexpr int BM = 128, BN = 128, BK = 8;
+// BM x BM CTA tiles (BM = 128, 64 or 32) over 16 x 16 threads, each holding
+// (BM/16)^2 accumulators at stride 16; the smaller tiles keep small-M
+// products (mixer and selector rows of a few recomputed frames) spread over
+// the SMs. The tiling never changes an output's accumulation order.
+template <int EPI, int BM = 128>
+__global__ void __launch_bounds__(256, BM == 128 ? 1 : 2) k_dgemm_exact(const float* __restrict__ A,
+                                                                        const float* __restrict__ B, float* C, int M,
+                                                                        int N, int K, int lda, int ldb, int ldc,
+                                                                        const float* __restrict__ gate = nullptr) {
+  constexpr int BN = BM, BK = 8, TM = BM / 16;
   __shared__ double As[2][BK][BM];
   __shared__ double Bs[2][BK][BN];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t m0 = int64_t(blockIdx.x) * BM;  // row tiles on x: M may exceed 65535 tiles
   const int n0 = blockIdx.y * BN;
   const int lr = tid >> 1, lc = (tid & 1) * 4;
-  const bool a_ok = m0 + lr < M;
+  const bool loader = lr < BM;  // thread lr stages row lr of the A and B tiles
+  const bool a_ok = loader && m0 + lr < M;
   const float* Ap = A + (m0 + lr) * int64_t(lda) + lc;
   const float* Bp = B + int64_t(n0 + lr) * ldb + lc;
 
-  double acc[8][8];
+  double acc[TM][TM];
 #pragma unroll
-  for (int i = 0; i < 8; i++)
+  for (int i = 0; i < TM; i++)
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+    for (int j = 0; j < TM; j++) acc[i][j] = 0.0;
 
   float4 ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 rb = __ldg(reinterpret_cast<const float4*>(Bp));
-  As[0][lc + 0][lr] = ra.x; As[0][lc + 1][lr] = ra.y; As[0][lc + 2][lr] = ra.z; As[0][lc + 3][lr] = ra.w;
-  Bs[0][lc + 0][lr] = rb.x; Bs[0][lc + 1][lr] = rb.y; Bs[0][lc + 2][lr] = rb.z; Bs[0][lc + 3][lr] = rb.w;
+  float4 rb = loader ? __ldg(reinterpret_cast<const float4*>(Bp)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  if (loader) {
+    As[0][lc + 0][lr] = ra.x; As[0][lc + 1][lr] = ra.y; As[0][lc + 2][lr] = ra.z; As[0][lc + 3][lr] = ra.w;
+    Bs[0][lc + 0][lr] = rb.x; Bs[0][lc + 1][lr] = rb.y; Bs[0][lc + 2][lr] = rb.z; Bs[0][lc + 3][lr] = rb.w;
+  }
   __syncthreads();
 
   const int steps = K / BK;
   for (int s = 0; s < steps; s++) {
     const int cur = s & 1;
     const bool more = s + 1 < steps;
-    if (more) {
+    if (more && loader) {
       ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap + (s + 1) * BK)) : make_float4(0.f, 0.f, 0.f, 0.f);
       rb = __ldg(reinterpret_cast<const float4*>(Bp + (s + 1) * BK));
     }
 #pragma unroll
     for (int kk = 0; kk < BK; kk++) {
-      double av[8], bv[8];
+      double av[TM], bv[TM];
 #pragma unroll
-      for (int i = 0; i < 8; i++) av[i] = As[cur][kk][ty + 16 * i];
+      for (int i = 0; i < TM; i++) av[i] = As[cur][kk][ty + 16 * i];
 #pragma unroll
-      for (int j = 0; j < 8; j++) bv[j] = Bs[cur][kk][tx + 16 * j];
+      for (int j = 0; j < TM; j++) bv[j] = Bs[cur][kk][tx + 16 * j];
 #pragma unroll
-      for (int i = 0; i < 8; i++)
+      for (int i = 0; i < TM; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < TM; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
     }
-    if (more) {
+    if (more && loader) {
       const int nx = cur ^ 1;
       As[nx][lc + 0][lr] = ra.x; As[nx][lc + 1][lr] = ra.y; As[nx][lc + 2][lr] = ra.z; As[nx][lc + 3][lr] = ra.w;
       Bs[nx][lc + 0][lr] = rb.x; Bs[nx][lc + 1][lr] = rb.y; Bs[nx][lc + 2][lr] = rb.z; Bs[nx][lc + 3][lr] = rb.w;
@@ -163,12 +171,12 @@ __global__ void __launch_bounds__(256, 1) k_dgemm_exact(const float* __restrict_
   }
 
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < TM; i++) {
     const int64_t row = m0 + ty + 16 * i;
     if (row >= M) continue;
     float* cp = C + row * int64_t(ldc) + n0 + tx;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
+    for (int j = 0; j < TM; j++) {
       const float v = f32(acc[i][j]);
       if (EPI == kEpiStore) cp[16 * j] = v;
       else if (EPI == kEpiRelu) cp[16 * j] = js_relu(v);

@@ -290,12 +290,29 @@ void prof_collect(kc_handle* h) {
   h->ev_bytes.clear();
 }
 
+// The exact GEMM with the largest CTA tile that still gives every SM a tile
+// (128 for the token-parallel products, 64 or 32 for the few rows of the
+// recomputed frames' mixer and selector).
+template <int EPI>
+void launch_dgemm(kc_handle* h, const float* A, uint32_t lda, const float* B, uint32_t ldb, float* C, uint64_t M,
+                  uint32_t N, uint32_t K, const float* gate) {
+  const uint64_t sms = uint64_t(h->sms);
+  if (((M + 127) / 128) * (N / 128) >= sms)
+    kc::k_dgemm_exact<EPI, 128><<<dim3(unsigned((M + 127) / 128), N / 128), 256, 0, h->stream>>>(
+        A, B, C, int(M), int(N), int(K), int(lda), int(ldb), int(N), gate);
+  else if (((M + 63) / 64) * (N / 64) >= sms)
+    kc::k_dgemm_exact<EPI, 64><<<dim3(unsigned((M + 63) / 64), N / 64), 256, 0, h->stream>>>(
+        A, B, C, int(M), int(N), int(K), int(lda), int(ldb), int(N), gate);
+  else
+    kc::k_dgemm_exact<EPI, 32><<<dim3(unsigned((M + 31) / 32), N / 32), 256, 0, h->stream>>>(
+        A, B, C, int(M), int(N), int(K), int(lda), int(ldb), int(N), gate);
+  h->launches++;
+}
+
 template <int EPI>
 kc_status dgemm(kc_handle* h, const float* A, const float* B, float* C, uint64_t M, uint32_t N, uint32_t K) {
   if (M == 0) return KC_OK;
-  dim3 grid(unsigned((M + 127) / 128), N / 128);
-  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(K), int(K), int(N));
-  h->launches++;
+  launch_dgemm<EPI>(h, A, K, B, K, C, M, N, K, nullptr);
   return KC_OK;
 }
 
@@ -304,10 +321,7 @@ template <int EPI>
 kc_status dgemm_ld(kc_handle* h, const float* A, uint32_t lda, const float* B, float* C, uint64_t M, uint32_t N,
                    uint32_t K, const float* gate = nullptr, uint32_t ldb = 0) {
   if (M == 0) return KC_OK;
-  dim3 grid(unsigned((M + 127) / 128), N / 128);
-  kc::k_dgemm_exact<EPI><<<grid, 256, 0, h->stream>>>(A, B, C, int(M), int(N), int(K), int(lda),
-                                                      int(ldb ? ldb : K), int(N), gate);
-  h->launches++;
+  launch_dgemm<EPI>(h, A, lda, B, ldb ? ldb : K, C, M, N, K, gate);
   return KC_OK;
 }
 
