@@ -213,14 +213,15 @@ __global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Mixer cross-attention + residual, f32// ---------------------------------------------------------------------------
 // Mixer cross-attention + residual, f32 (oracle.ts:292-293 with the open
-// mixer mask). One CTA per frame: its questions go in chunks of up to
-// kCaChunk, and each bank row's k and v slices are loaded once per chunk.
-// Per (question, head): score j = the 32-long fmaf chain q·k_j in dimension
-// order, scaled; softmax with lane-strided max and sum (lane l takes j = l,
-// l+32, ...) reduced by an xor-shuffle tree; output = (sum over even j of
-// p_j v_j + sum over odd j of p_j v_j) / sum, added to the question row.
+// mixer mask). One CTA per chunk of up to kCaChunk questions of a frame (as
+// many as the score buffer holds), the chunks of a frame adjacent in the grid
+// so they share the bank in L2; each bank row's k and v slices are loaded
+// once per chunk. Per (question, head): score j = the 32-long fmaf chain
+// q·k_j in dimension order, scaled; softmax with lane-strided max and sum
+// (lane l takes j = l, l+32, ...) reduced by an xor-shuffle tree; output =
+// (sum over even j of p_j v_j + sum over odd j of p_j v_j) / sum, added to
+// the question row.
 // ---------------------------------------------------------------------------
 constexpr int kCaChunk = 8;
 constexpr int kCaThreads = 256;
@@ -233,6 +234,7 @@ struct CrossAttnFrameArgs {
   const uint64_t* q_off;   // [frames + 1]
   const uint64_t* r_off;   // [frames + 1]
   int qc;                  // questions per chunk (the score buffer holds qc x 4 x max_r)
+  int chunks;              // CTAs per frame: ceil(largest question count / qc)
   uint32_t max_r;
   float scale;
 };
@@ -240,14 +242,15 @@ struct CrossAttnFrameArgs {
 __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameArgs a) {
   extern __shared__ __align__(16) float caf_smem[];  // scores [qc][4][max_r], then q [qc][128]
   __shared__ float inv_s[kCaChunk][KC_HEADS];
-  const uint32_t f = blockIdx.x;
+  const uint32_t f = blockIdx.x / a.chunks;
+  const int q0 = int(blockIdx.x % a.chunks) * a.qc;
   const uint64_t qb = a.q_off[f], rb = a.r_off[f];
   const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
-  if (nq == 0) return;
+  if (q0 >= nq) return;
   float* sc = caf_smem;
   float* qs = caf_smem + size_t(a.qc) * KC_HEADS * a.max_r;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int q0 = 0; q0 < nq; q0 += a.qc) {
+  {
     const int nc = min(a.qc, nq - q0);
     for (int i = tid; i < nc * KC_H; i += kCaThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
     __syncthreads();
@@ -354,13 +357,13 @@ __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameA
 
 // ---------------------------------------------------------------------------
 // Pointer selector, f32, with certification (selectorOracle,
-// forward/oracle.ts:332-382). One CTA of 256 threads per frame: the frame's
-// questions go in chunks of up to kSelChunk, whose scores are computed
-// together so each bank key row is read once per chunk (per score: the
-// 128-long fmaf chain in dimension order); then each question of the chunk in
-// turn: mask, top two, softmax, p, the argmax or the draw, and its
-// certification. Writes p and the index, and raises flags[frame] when a
-// decision is not certain.
+// forward/oracle.ts:332-382). One CTA of 256 threads per chunk of up to
+// kSelChunk questions of a frame (the chunks of a frame adjacent in the grid,
+// sharing the bank in L2): the chunk's scores are computed together so each
+// bank key row is read once per chunk (per score: the 128-long fmaf chain in
+// dimension order); then each question of the chunk in turn: mask, top two,
+// softmax, p, the argmax or the draw, and its certification. Writes p and
+// the index, and raises flags[frame] when a decision is not certain.
 // ---------------------------------------------------------------------------
 constexpr int kSelChunk = 8;
 
@@ -378,6 +381,7 @@ struct SelectFastArgs {
   const double* uniforms;
   uint32_t max_r;
   int qc;           // questions per chunk (the score buffer holds qc x max_r)
+  int chunks;       // CTAs per frame: ceil(largest question count / qc)
   float scale;
   float tau;        // certified argmax: top-two score gap above tau
   float tau_c;      // certified draw: the uniform farther than tau_c from a cumulative boundary
@@ -394,17 +398,18 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
   __shared__ uint32_t red_u[NT / 32];
   __shared__ uint32_t red_i[NT / 32];
   __shared__ int red_b[NT / 32];
-  const uint32_t f = blockIdx.x;
+  const uint32_t f = blockIdx.x / a.chunks;
+  const int q0 = int(blockIdx.x % a.chunks) * a.qc;
   const uint64_t rb = a.r_off[f], qb = a.q_off[f];
   const int R = int(a.r_off[f + 1] - rb), nq = int(a.q_off[f + 1] - qb);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (nq == 0) return;
+  if (q0 >= nq) return;
   if (R == 0) {
-    for (int c = tid; c < nq; c += NT) a.index[qb + c] = KC_INVALID;
+    for (int c = q0 + tid; c < min(nq, q0 + a.qc); c += NT) a.index[qb + c] = KC_INVALID;
     return;
   }
   float* qs = sel_smem + size_t(a.qc) * a.max_r;
-  for (int q0 = 0; q0 < nq; q0 += a.qc) {
+  {
     const int nc = min(a.qc, nq - q0);
     for (int i = tid; i < nc * KC_H; i += NT) qs[i] = a.sq[(qb + q0) * KC_H + i];
     __syncthreads();

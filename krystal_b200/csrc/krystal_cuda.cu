@@ -797,10 +797,10 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
+      const int qc = cross_chunk(tot.max_r), chunks = int((std::max<uint32_t>(tot.max_q, 1) + qc - 1) / qc);
       kc::CrossAttnFrameArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
-                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), cross_chunk(tot.max_r), tot.max_r,
-                                attn_scale};
-      kc::k_cross_attn_frame<<<b.frames, kc::kCaThreads, cross_smem(tot.max_r), h->stream>>>(ca);
+                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), qc, chunks, tot.max_r, attn_scale};
+      kc::k_cross_attn_frame<<<b.frames * unsigned(chunks), kc::kCaThreads, cross_smem(tot.max_r), h->stream>>>(ca);
       h->launches++;
       KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, P<float>(ws.qstate), Q, m0 + 3, P<float>(ws.mh)));
       KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, P<float>(ws.mh), Q, m0 + 4, P<float>(ws.qstate)));
@@ -817,10 +817,11 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
     sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
     sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
+    sa.chunks = int((std::max<uint32_t>(tot.max_q, 1) + sa.qc - 1) / sa.qc);
     sa.scale = float(1.0 / std::sqrt(double(H)));
     sa.tau = h->tau; sa.tau_c = h->tau_c;
     sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
-    kc::k_select_fast<<<b.frames, 256, sel_smem(tot.max_r), h->stream>>>(sa);
+    kc::k_select_fast<<<b.frames * unsigned(sa.chunks), 256, sel_smem(tot.max_r), h->stream>>>(sa);
     h->launches++;
   }
   KC_TRY(cudaGetLastError(), "launch");
