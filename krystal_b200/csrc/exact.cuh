@@ -224,21 +224,41 @@ struct LocalAttnArgs {
 };
 
 
+// Staged q|k|v row r of a record: 96 float4 (q heads 0-3, k heads 4-7, v
+// heads 8-11, 8 float4 each). Within each head's 8, float4 m sits at
+// (m + 2·(head & 3) + (r & 1)) & 7, so the 8 lanes of a quarter-warp —
+// heads 0-3 of two tokens — hit 8 different bank groups, reading q (one row
+// each) or the same k / v row (4 distinct addresses).
+__device__ __forceinline__ int la_exact_f4(int r, int f) {
+  return r * 96 + (f & ~7) + (((f & 7) + 2 * ((f >> 3) & 3) + (r & 1)) & 7);
+}
+
 __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
-  __shared__ float sm[4][KC_RW][3 * KC_H];  // 48 KB
+  __shared__ float4 sm[4][KC_RW * 96];  // 48 KB
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * 4 + warp;
   if (g >= a.records) return;
   const uint32_t start = a.rec_start[g];
   const int cnt = int(a.rec_meta[g].y & 15u);
   if (cnt == 0) return;
-  float(*rec)[3 * KC_H] = sm[warp];
-  // stage q|k|v rows: cnt * 384 floats = cnt * 96 float4
+  float4* rec = sm[warp];
+  // stage q|k|v rows: cnt * 96 float4, every load in flight before the stores
   const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
-  float4* dst = reinterpret_cast<float4*>(&rec[0][0]);
-  for (int i = lane; i < cnt * 96; i += 32) dst[i] = src[i];
+  {
+    float4 t[KC_RW * 3];
+#pragma unroll
+    for (int u = 0; u < KC_RW * 3; u++) {
+      const int i = lane + 32 * u;
+      if (i < cnt * 96) t[u] = src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < KC_RW * 3; u++) {
+      const int i = lane + 32 * u;
+      if (i < cnt * 96) rec[la_exact_f4(i / 96, i % 96)] = t[u];
+    }
+  }
   __syncwarp();
-  const int ti = lane >> 2, head = lane & 3, hb = head * KC_HEAD_DIM;
+  const int ti = lane >> 2, head = lane & 3;
   float p[KC_RW];
   // word ids of the record's tokens: lane 4j holds token j's (all lanes shuffle)
   uint32_t wmine = KC_INVALID, wj[KC_RW];
@@ -250,13 +270,29 @@ __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
 #pragma unroll
     for (int j = 0; j < KC_RW; j++) wj[j] = KC_INVALID;
   }
+  float4 o4[KC_HEAD_DIM / 4];
   if (ti < cnt) {
-    for (int j = 0; j < cnt; j++) {
-      double s = 0.0;
-#pragma unroll 8
-      for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(rec[ti][hb + d]), double(rec[j][KC_H + hb + d]), s);
-      p[j] = f32(s * a.scale + double(word_bias(wmine, wj[j], a.word_alpha)));
-    }
+    float4 q4[KC_HEAD_DIM / 4];
+#pragma unroll
+    for (int m = 0; m < 8; m++) q4[m] = rec[la_exact_f4(ti, head * 8 + m)];
+    // the eight keys' f64 chains side by side, each over d = 0..31 in order
+    // (keys past the record read row 0 and are never used)
+    double s[KC_RW];
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) s[j] = 0.0;
+#pragma unroll
+    for (int m = 0; m < 8; m++)
+#pragma unroll
+      for (int j = 0; j < KC_RW; j++) {
+        const float4 k = rec[la_exact_f4(j < cnt ? j : 0, (4 + head) * 8 + m)];
+        s[j] = fma(double(q4[m].x), double(k.x), s[j]);
+        s[j] = fma(double(q4[m].y), double(k.y), s[j]);
+        s[j] = fma(double(q4[m].z), double(k.z), s[j]);
+        s[j] = fma(double(q4[m].w), double(k.w), s[j]);
+      }
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++)
+      if (j < cnt) p[j] = f32(s[j] * a.scale + double(word_bias(wmine, wj[j], a.word_alpha)));
     bool blocked = true;
     for (int j = 0; j < cnt; j++)
       if (double(p[j]) >= -1e29) { blocked = false; break; }
@@ -267,25 +303,39 @@ __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
     }
     if (a.p_out)
       for (int j = 0; j < cnt; j++) a.p_out[((uint64_t(start) + ti) * KC_HEADS + head) * KC_RW + j] = p[j];
+    // p·v: per output dimension an f64 chain over the record's keys in order
+    double v[KC_HEAD_DIM];
+#pragma unroll
+    for (int d = 0; d < KC_HEAD_DIM; d++) v[d] = 0.0;
+    for (int j = 0; j < cnt; j++) {
+      const double pj = double(p[j]);
+#pragma unroll
+      for (int m = 0; m < 8; m++) {
+        const float4 vv = rec[la_exact_f4(j, (8 + head) * 8 + m)];
+        v[4 * m] = fma(pj, double(vv.x), v[4 * m]);
+        v[4 * m + 1] = fma(pj, double(vv.y), v[4 * m + 1]);
+        v[4 * m + 2] = fma(pj, double(vv.z), v[4 * m + 2]);
+        v[4 * m + 3] = fma(pj, double(vv.w), v[4 * m + 3]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 8; m++) o4[m] = make_float4(f32(v[4 * m]), f32(v[4 * m + 1]), f32(v[4 * m + 2]), f32(v[4 * m + 3]));
   }
   __syncwarp();
   if (ti < cnt) {
-    float out[KC_HEAD_DIM];
-#pragma unroll 4
-    for (int d = 0; d < KC_HEAD_DIM; d++) {
-      double v = 0.0;
-      for (int j = 0; j < cnt; j++) v = fma(double(p[j]), double(rec[j][2 * KC_H + hb + d]), v);
-      out[d] = f32(v);
-    }
     // every lane is done reading q (only lane ti*4+head reads this slice)
 #pragma unroll
-    for (int d = 0; d < KC_HEAD_DIM; d++) rec[ti][hb + d] = out[d];
+    for (int m = 0; m < 8; m++) rec[la_exact_f4(ti, head * 8 + m)] = o4[m];
   }
   __syncwarp();
-  float* xr = a.x + uint64_t(start) * KC_H;
-  for (int i = lane; i < cnt * KC_H; i += 32) {
-    const int r = i >> 7, d = i & 127;
-    xr[i] = f32(double(xr[i]) + double(rec[r][d]));
+  float4* xr = reinterpret_cast<float4*>(a.x + uint64_t(start) * KC_H);
+  for (int i = lane; i < cnt * (KC_H / 4); i += 32) {
+    const int r = i >> 5, f = i & 31;
+    const float4 ov = rec[la_exact_f4(r, f)];
+    float4 xv = xr[i];
+    xv.x = f32(double(xv.x) + double(ov.x)); xv.y = f32(double(xv.y) + double(ov.y));
+    xv.z = f32(double(xv.z) + double(ov.z)); xv.w = f32(double(xv.w) + double(ov.w));
+    xr[i] = xv;
   }
 }
 
