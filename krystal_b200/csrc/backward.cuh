@@ -536,6 +536,13 @@ constexpr int kLocalBackWarps = 4;
 constexpr int kLocalBackWarpFloats = KC_RW * 3 * KC_H + KC_RW * KC_H + 2 * KC_HEADS * KC_RW * KC_RW;
 constexpr size_t kLocalBackSmem = size_t(kLocalBackWarps) * kLocalBackWarpFloats * 4;
 
+// dOut row r staged as 32 float4, rotated within each head's 8 like the
+// q|k|v rows (la_exact_f4), so a quarter-warp's (token, head) lanes read
+// 8 different bank groups.
+__device__ __forceinline__ int lb_dout_f4(int r, int f) {
+  return r * 32 + (f & ~7) + (((f & 7) + 2 * ((f >> 3) & 3) + (r & 1)) & 7);
+}
+
 __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   extern __shared__ __align__(16) float lsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -545,48 +552,64 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   const int cnt = int(a.rec_meta[g].y & 15u);
   if (cnt == 0) return;
   float* base = lsm + size_t(warp) * kLocalBackWarpFloats;
-  float(*rec)[3 * KC_H] = reinterpret_cast<float(*)[3 * KC_H]>(base);                         // q|k|v
-  float(*dos)[KC_H] = reinterpret_cast<float(*)[KC_H]>(base + KC_RW * 3 * KC_H);              // dOut
+  float4* rec = reinterpret_cast<float4*>(base);                                  // q|k|v, la_exact_f4 layout
+  float4* dos = reinterpret_cast<float4*>(base + KC_RW * 3 * KC_H);               // dOut, lb_dout_f4 layout
   float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(base + KC_RW * 4 * KC_H);  // [head][i][j]
   float(*dsh)[KC_RW][KC_RW] = pp + KC_HEADS;                                                   // [head][i][j]
   {
     const float4* s1 = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
-    float4* d1 = reinterpret_cast<float4*>(&rec[0][0]);
-    for (int i = lane; i < cnt * 96; i += 32) d1[i] = s1[i];
     const float4* s2 = reinterpret_cast<const float4*>(a.dout + uint64_t(start) * KC_H);
-    float4* d2 = reinterpret_cast<float4*>(&dos[0][0]);
-    for (int i = lane; i < cnt * 32; i += 32) d2[i] = s2[i];
+    for (int i = lane; i < cnt * 96; i += 32) cp_async16(rec + la_exact_f4(i / 96, i % 96), s1 + i);
+    for (int i = lane; i < cnt * 32; i += 32) cp_async16(dos + lb_dout_f4(i >> 5, i & 31), s2 + i);
     for (int i = lane; i < cnt * KC_HEADS * KC_RW; i += 32) {
       const int ti = i >> 5, head = (i >> 3) & 3, jj = i & 7;
       pp[head][ti][jj] = a.p[(uint64_t(start) + ti) * KC_HEADS * KC_RW + head * KC_RW + jj];
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
   }
   __syncwarp();
   {
-    const int ti = lane >> 2, head = lane & 3, hb = head * KC_HEAD_DIM;
+    const int ti = lane >> 2, head = lane & 3;
     if (ti < cnt) {
+      float4 d4[KC_HEAD_DIM / 4];
+#pragma unroll
+      for (int m = 0; m < 8; m++) d4[m] = dos[lb_dout_f4(ti, head * 8 + m)];
+      // s[j] = dOut_i · v_j: eight f64 chains side by side, each over d in order
+      // (keys past the record read row 0 and are never used)
       double s[KC_RW];
+#pragma unroll
+      for (int j = 0; j < KC_RW; j++) s[j] = 0.0;
+#pragma unroll
+      for (int m = 0; m < 8; m++)
+#pragma unroll
+        for (int j = 0; j < KC_RW; j++) {
+          const float4 v = rec[la_exact_f4(j < cnt ? j : 0, (8 + head) * 8 + m)];
+          s[j] = fma(double(d4[m].x), double(v.x), s[j]);
+          s[j] = fma(double(d4[m].y), double(v.y), s[j]);
+          s[j] = fma(double(d4[m].z), double(v.z), s[j]);
+          s[j] = fma(double(d4[m].w), double(v.w), s[j]);
+        }
       double rs = 0.0;
-      for (int j = 0; j < cnt; j++) {
-        double acc = 0.0;
-#pragma unroll 8
-        for (int d = 0; d < KC_HEAD_DIM; d++) acc = fma(double(dos[ti][hb + d]), double(rec[j][2 * KC_H + hb + d]), acc);
-        s[j] = acc;
-        rs = rs + double(pp[head][ti][j]) * acc;
-      }
-      for (int j = 0; j < cnt; j++) dsh[head][ti][j] = f32(double(pp[head][ti][j]) * (double(f32(s[j])) - rs));
+#pragma unroll
+      for (int j = 0; j < KC_RW; j++)
+        if (j < cnt) rs = rs + double(pp[head][ti][j]) * s[j];
+#pragma unroll
+      for (int j = 0; j < KC_RW; j++)
+        if (j < cnt) dsh[head][ti][j] = f32(double(pp[head][ti][j]) * (double(f32(s[j])) - rs));
     }
   }
   __syncwarp();
   float* out = a.dqkv + uint64_t(start) * 3 * KC_H;
+  const float* recf = reinterpret_cast<const float*>(rec);
+  const float* dosf = reinterpret_cast<const float*>(dos);
   for (int m = 0; m < KC_HEADS; m++) {
-    const int col = m * KC_HEAD_DIM + lane;
+    const int col = m * KC_HEAD_DIM + lane, c4 = col >> 2, cw = col & 3;
     for (int i = 0; i < cnt; i++) {
       double aq = 0.0, ak = 0.0, av = 0.0;
       for (int j = 0; j < cnt; j++) {
-        aq = fma(double(dsh[m][i][j]), double(rec[j][KC_H + col]), aq);
-        ak = fma(double(dsh[m][j][i]), double(rec[j][col]), ak);
-        av = fma(double(pp[m][j][i]), double(dos[j][col]), av);
+        aq = fma(double(dsh[m][i][j]), double(recf[4 * la_exact_f4(j, 32 + c4) + cw]), aq);
+        ak = fma(double(dsh[m][j][i]), double(recf[4 * la_exact_f4(j, c4) + cw]), ak);
+        av = fma(double(pp[m][j][i]), double(dosf[4 * lb_dout_f4(j, c4) + cw]), av);
       }
       out[uint64_t(i) * 3 * KC_H + col] = f32(aq * a.scale);
       out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak * a.scale);

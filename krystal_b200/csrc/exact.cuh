@@ -224,6 +224,12 @@ struct LocalAttnArgs {
 };
 
 
+// One 16-byte asynchronous global -> shared copy (cp.async.wait_all before use).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
+}
+
 // Staged q|k|v row r of a record: 96 float4 (q heads 0-3, k heads 4-7, v
 // heads 8-11, 8 float4 each). Within each head's 8, float4 m sits at
 // (m + 2·(head & 3) + (r & 1)) & 7, so the 8 lanes of a quarter-warp —
@@ -244,19 +250,8 @@ __global__ void __launch_bounds__(128) k_local_attn_exact(LocalAttnArgs a) {
   float4* rec = sm[warp];
   // stage q|k|v rows: cnt * 96 float4, every load in flight before the stores
   const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
-  {
-    float4 t[KC_RW * 3];
-#pragma unroll
-    for (int u = 0; u < KC_RW * 3; u++) {
-      const int i = lane + 32 * u;
-      if (i < cnt * 96) t[u] = src[i];
-    }
-#pragma unroll
-    for (int u = 0; u < KC_RW * 3; u++) {
-      const int i = lane + 32 * u;
-      if (i < cnt * 96) rec[la_exact_f4(i / 96, i % 96)] = t[u];
-    }
-  }
+  for (int i = lane; i < cnt * 96; i += 32) cp_async16(rec + la_exact_f4(i / 96, i % 96), src + i);
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
   const int ti = lane >> 2, head = lane & 3;
   float p[KC_RW];
