@@ -149,7 +149,7 @@ struct PoolFastArgs {
   float* query_values;
 };
 
-__global__ void __launch_bounds__(256) k_pool_fast(PoolFastArgs a) {
+__global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
   if (g >= a.records) return;
