@@ -10,9 +10,10 @@
 // re-reading h1 (3 KB per token and block).
 //
 // One persistent CTA per SM, 128-row tiles, 320 threads:
-//   warp 0     TMA: the x tile (two [128 x 64] f32 boxes) and, per tile,
-//              the twelve 32 KB weight-image chunks (W1 then W2) through a
-//              three-stage ring;
+//   warp 0     TMA: lane 0 the twelve 32 KB weight-image chunks per tile
+//              (W1 then W2) through a three-stage ring; lane 1 the x tile
+//              (two [128 x 64] f32 boxes) as soon as the previous tile's P1
+//              products release the operand;
 //   warps 1-4  split the x tile in place to swizzled fp16 hi | lo, and
 //              share the epilogues below with warps 6-9;
 //   warp 5     MMA issuer. Per tile: P1(j) = x·W1[j]ᵀ for hidden chunks
@@ -117,17 +118,13 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
   const uint32_t tmem_out = tmem_base + 3 * kBN;
 
   if (warp == 0) {
-    // ---------------- TMA issuer ----------------
+    // ---------------- TMA issuers ----------------
+    // lane 0 streams the weight chunks; lane 1 loads each tile's x as soon as
+    // the previous tile's P1 products release it (not behind the W2 chunks)
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
-      uint32_t it = 0, tl = 0;
+      uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
-        if (!mbar_wait(xempty, (tl & 1) ^ 1, a.err)) { ok = false; break; }
-        for (int kc = 0; kc < 2; kc++) {
-          mbar_arrive_expect_tx(&xraw[kc], kFfnChunk);
-          tma_load_2d(xs + kc * kFfnChunk, &amap, kc * kBK, t * kBM, &xraw[kc]);
-        }
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         for (int c = 0; c < kFfnChunksPerTile; c++, it++) {
           const int s = it % kFfnWStages;
           const uint32_t ph = (it / kFfnWStages) & 1;
@@ -141,6 +138,17 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
       // every copy issued lands before the CTA may exit
       for (uint32_t j = it > uint32_t(kFfnWStages) ? it - kFfnWStages : 0u; j < it; j++)
         mbar_wait(&wfull[j % kFfnWStages], (j / kFfnWStages) & 1, a.err);
+    } else if (lane == 1) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+      uint32_t tl = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+        if (!mbar_wait(xempty, (tl & 1) ^ 1, a.err)) break;
+        for (int kc = 0; kc < 2; kc++) {
+          mbar_arrive_expect_tx(&xraw[kc], kFfnChunk);
+          tma_load_2d(xs + kc * kFfnChunk, &amap, kc * kBK, t * kBM, &xraw[kc]);
+        }
+      }
+      // the last x issued lands before the CTA may exit
       if (tl > 0)
         for (int kc = 0; kc < 2; kc++) mbar_wait(&xraw[kc], (tl - 1) & 1, a.err);
     }
