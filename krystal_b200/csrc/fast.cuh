@@ -307,18 +307,18 @@ __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameA
       for (int u = 0; u < kCaChunk / 2; u++) v0[u] = v1[u] = 0.f;
       const float* vcol = a.mv + rb * KC_H + col;
       int j = 0;
-      // sixteen v elements in flight per step; the even / odd sums keep their order
-      for (; j + 15 < R; j += 16) {
-        float vv[16];
+      // thirty-two v elements in flight per step; the even / odd sums keep their order
+      for (; j + 31 < R; j += 32) {
+        float vv[32];
 #pragma unroll
-        for (int e = 0; e < 16; e++) vv[e] = vcol[size_t(j + e) * KC_H];
+        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + e) * KC_H];
 #pragma unroll
         for (int u = 0; u < kCaChunk / 2; u++) {
           const int c = c0 + 2 * u;
           if (c < nc) {
             const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
 #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
+            for (int e = 0; e < 32; e += 2) {
               v0[u] = fmaf(row[e], vv[e], v0[u]);
               v1[u] = fmaf(row[e + 1], vv[e + 1], v1[u]);
             }
@@ -361,9 +361,10 @@ __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameA
 // kSelChunk questions of a frame (the chunks of a frame adjacent in the grid,
 // sharing the bank in L2): the chunk's scores are computed together so each
 // bank key row is read once per chunk (per score: the 128-long fmaf chain in
-// dimension order); then each question of the chunk in turn: mask, top two,
-// softmax, p, the argmax or the draw, and its certification. Writes p and
-// the index, and raises flags[frame] when a decision is not certain.
+// dimension order); then one warp per question: mask, top two, softmax (lane-
+// strided sums reduced by an xor-shuffle tree), p, the argmax or the draw,
+// and its certification. Writes p and the index, and raises flags[frame]
+// when a decision is not certain.
 // ---------------------------------------------------------------------------
 constexpr int kSelChunk = 8;
 
@@ -393,11 +394,6 @@ struct SelectFastArgs {
 __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
   constexpr int NT = 256;
   extern __shared__ __align__(16) float sel_smem[];  // scores [qc][max_r], then q [qc][128]
-  __shared__ float red_f[NT / 32];
-  __shared__ float red_g[NT / 32];
-  __shared__ uint32_t red_u[NT / 32];
-  __shared__ uint32_t red_i[NT / 32];
-  __shared__ int red_b[NT / 32];
   const uint32_t f = blockIdx.x / a.chunks;
   const int q0 = int(blockIdx.x % a.chunks) * a.qc;
   const uint64_t rb = a.r_off[f], qb = a.q_off[f];
@@ -437,7 +433,8 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         if (c < nc) sel_smem[size_t(c) * a.max_r + j] = sv[c];
     }
     __syncthreads();
-    for (int c = 0; c < nc; c++) {
+    // one warp per question of the chunk: mask, top two, softmax, p, decision
+    for (int c = warp; c < nc; c += NT / 32) {
       const uint64_t qi = qb + q0 + c;
       float* row = sel_smem + size_t(c) * a.max_r;
       float* prow = a.p + a.p_off[f] + uint64_t(q0 + c) * uint64_t(R);
@@ -448,24 +445,19 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         sa = a.schema_allow + qi * 8;
         ba = a.band_allow[qi];
         uint32_t admitted = 0;
-        for (int j = tid; j < R; j += NT) {
+        for (int j = lane; j < R; j += 32) {
           const uint32_t gr = a.bank_rec[rb + j];
           const uint32_t s = a.schema_ids[gr], b = a.band_ids[gr];
           admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
         }
         for (int o = 16; o; o >>= 1) admitted += __shfl_xor_sync(0xffffffffu, admitted, o);
-        if (lane == 0) red_u[warp] = admitted;
-        __syncthreads();
-        uint32_t tot = 0;
-        for (int w = 0; w < NT / 32; w++) tot += red_u[w];
-        reopen = tot == 0;
+        reopen = admitted == 0;
       }
-      __syncthreads();
-      // scaled, masked scores; per-thread best / second-best (value, first index) and finiteness
+      // scaled, masked scores; per-lane best / second-best (value, first index) and finiteness
       float b1 = -INFINITY, b2 = -INFINITY;
       uint32_t i1 = KC_INVALID;
       int nonfinite = 0, open = 0;
-      for (int j = tid; j < R; j += NT) {
+      for (int j = lane; j < R; j += 32) {
         const float s = row[j];
         float m = 0.f;
         if (sa && !reopen) {
@@ -480,7 +472,7 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         if (sc > b1) { b2 = b1; b1 = sc; i1 = uint32_t(j); }
         else if (sc > b2) b2 = sc;
       }
-      // block reduce: top two values, index of the first top, any-open, any-nonfinite
+      // warp reduce: top two values, index of the first top, any-open, any-nonfinite
       for (int o = 16; o; o >>= 1) {
         const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o), ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
         const uint32_t oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
@@ -489,46 +481,28 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
         open |= __shfl_xor_sync(0xffffffffu, open, o);
       }
-      if (lane == 0) { red_f[warp] = b1; red_g[warp] = b2; red_i[warp] = i1; red_b[warp] = (nonfinite << 1) | open; }
-      __syncthreads();
-      float B1 = red_f[0], B2 = red_g[0];
-      uint32_t I1 = red_i[0];
-      int flagsum = red_b[0];
-      for (int w = 1; w < NT / 32; w++) {
-        const float ob1 = red_f[w], ob2 = red_g[w];
-        const uint32_t oi1 = red_i[w];
-        if (ob1 > B1 || (ob1 == B1 && oi1 < I1)) { B2 = fmaxf(B1, ob2); B1 = ob1; I1 = oi1; }
-        else B2 = fmaxf(B2, ob1);
-        flagsum |= red_b[w];
-      }
-      const bool any_nonfinite = flagsum & 2, any_open = flagsum & 1;
-      __syncthreads();
       // softmax (the all-blocked row keeps p = 0)
       float inv = 0.f;
-      if (any_open) {
+      if (open) {
         float sum = 0.f;
-        for (int j = tid; j < R; j += NT) {
-          const float e = expf(row[j] - B1);
+        for (int j = lane; j < R; j += 32) {
+          const float e = expf(row[j] - b1);
           row[j] = e;
           sum += e;
         }
         for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) red_f[warp] = sum;
-        __syncthreads();
-        float tot = 0.f;
-        for (int w = 0; w < NT / 32; w++) tot += red_f[w];
-        inv = 1.f / fmaxf(tot, 1e-20f);
+        inv = 1.f / fmaxf(sum, 1e-20f);
       }
-      for (int j = tid; j < R; j += NT) {
-        const float pv = any_open ? row[j] * inv : 0.f;
+      for (int j = lane; j < R; j += 32) {
+        const float pv = open ? row[j] * inv : 0.f;
         row[j] = pv;
         prow[j] = pv;
       }
-      __syncthreads();
-      if (tid == 0) {
-        bool certain = !any_nonfinite;
+      __syncwarp();
+      if (lane == 0) {
+        bool certain = !nonfinite;
         uint32_t best;
-        if (!any_open) {
+        if (!open) {
           best = KC_INVALID;  // every score below -1e29 on any accurate computation
         } else if (a.uniforms) {
           // sampleRow's inverse CDF; certain when the draw is clear of both edges
@@ -552,14 +526,12 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
           // tiny weights near zero may flip between zero and positive
           best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
         } else {
-          best = I1;
-          certain = certain && (R == 1 || B1 - B2 > a.tau);
+          best = i1;
+          certain = certain && (R == 1 || b1 - b2 > a.tau);
         }
         a.index[qi] = best;
         if (!certain) atomicOr(&a.flags[f], 1u);
       }
-      // red_* and this row are reused by the next question
-      __syncthreads();
     }
   }
 }
