@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -186,6 +187,10 @@ struct kc_handle {
   kc::FrameTotals* h_tot = nullptr;  // pinned
   std::string err;
   uint64_t launches = 0;
+  // the fused encoder kernels (k_tc_attn, k_tc_ffn) where the dimensions fit;
+  // KC_NO_FUSION=1 in the environment at kc_create runs the unfused sequence
+  // (the same arithmetic, kept for the learn path and checked against the fused)
+  bool fuse = true;
   // precision
   int precision = KC_PRECISION_CERTIFIED;
   float tau = 2e-5f, tau_c = 2e-5f;
@@ -418,7 +423,7 @@ kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, c
 // x += relu(x·W1ᵀ)·W2ᵀ on the tensor cores in one kernel (ffn.cuh), for the
 // W1 / W2 matrices mat_w1 / mat_w2 of the tensor-core list. Needs H = 128 and
 // F = 384 (the kernel's fixed tiling); ffn_fusable() says whether it applies.
-bool ffn_fusable(const kc_handle* h) { return h->d.h == 128 && h->d.ffn == 384; }
+bool ffn_fusable(const kc_handle* h) { return h->fuse && h->d.h == 128 && h->d.ffn == 384; }
 
 kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
   if (M == 0) return KC_OK;
@@ -460,7 +465,7 @@ size_t sel_smem(uint32_t max_r) {
 // (attn_tc.cuh) for the encoder block whose Wqkv is `mat`. Needs H = 128 and
 // a head dim of 32 (the kernel's fixed tiling); attn_fusable() says whether it
 // applies.
-bool attn_fusable(const kc_handle* h) { return h->d.h == 128 && h->d.hd == 32 && h->d.heads == 4; }
+bool attn_fusable(const kc_handle* h) { return h->fuse && h->d.h == 128 && h->d.hd == 32 && h->d.heads == 4; }
 
 uint64_t attn_tiles(uint64_t T) { return (T + kc::tc::kAtWindow - 1) / kc::tc::kAtWindow; }
 
@@ -1353,6 +1358,10 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   auto* h = new kc_handle();
   h->device = device;
   h->d = dims_of(config);
+  {
+    const char* nf = std::getenv("KC_NO_FUSION");
+    h->fuse = !(nf && nf[0] && nf[0] != '0');
+  }
   if (!weights_ok(h->d, weights)) {
     delete h;
     return fail(nullptr, KC_ERR_INVALID_ARG, "weights view is incomplete");
