@@ -602,19 +602,33 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   float* out = a.dqkv + uint64_t(start) * 3 * KC_H;
   const float* recf = reinterpret_cast<const float*>(rec);
   const float* dosf = reinterpret_cast<const float*>(dos);
+  // dQ_i = Σ_j dS_ij k_j, dK_i = Σ_j dS_ji q_j, dV_i = Σ_j P_ji dOut_j per
+  // column: every row i of the record at once (24 f64 chains per lane), each
+  // chain over j in order
   for (int m = 0; m < KC_HEADS; m++) {
     const int col = m * KC_HEAD_DIM + lane, c4 = col >> 2, cw = col & 3;
-    for (int i = 0; i < cnt; i++) {
-      double aq = 0.0, ak = 0.0, av = 0.0;
-      for (int j = 0; j < cnt; j++) {
-        aq = fma(double(dsh[m][i][j]), double(recf[4 * la_exact_f4(j, 32 + c4) + cw]), aq);
-        ak = fma(double(dsh[m][j][i]), double(recf[4 * la_exact_f4(j, c4) + cw]), ak);
-        av = fma(double(pp[m][j][i]), double(dosf[4 * lb_dout_f4(j, c4) + cw]), av);
-      }
-      out[uint64_t(i) * 3 * KC_H + col] = f32(aq * a.scale);
-      out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak * a.scale);
-      out[uint64_t(i) * 3 * KC_H + 2 * KC_H + col] = f32(av);
+    double aq[KC_RW], ak[KC_RW], av[KC_RW];
+#pragma unroll
+    for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = 0.0;
+    for (int j = 0; j < cnt; j++) {
+      const double kj = double(recf[4 * la_exact_f4(j, 32 + c4) + cw]);
+      const double qj = double(recf[4 * la_exact_f4(j, c4) + cw]);
+      const double dj = double(dosf[4 * lb_dout_f4(j, c4) + cw]);
+#pragma unroll
+      for (int i = 0; i < KC_RW; i++)
+        if (i < cnt) {
+          aq[i] = fma(double(dsh[m][i][j]), kj, aq[i]);
+          ak[i] = fma(double(dsh[m][j][i]), qj, ak[i]);
+          av[i] = fma(double(pp[m][j][i]), dj, av[i]);
+        }
     }
+#pragma unroll
+    for (int i = 0; i < KC_RW; i++)
+      if (i < cnt) {
+        out[uint64_t(i) * 3 * KC_H + col] = f32(aq[i] * a.scale);
+        out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak[i] * a.scale);
+        out[uint64_t(i) * 3 * KC_H + 2 * KC_H + col] = f32(av[i]);
+      }
   }
 }
 
