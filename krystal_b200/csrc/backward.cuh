@@ -532,18 +532,15 @@ struct LocalBackArgs {
   float* dqkv;               // [T,384]
 };
 
-constexpr int kLocalBackWarps = 4;
-constexpr int kLocalBackWarpFloats = KC_RW * 3 * KC_H + KC_RW * KC_H + 2 * KC_HEADS * KC_RW * KC_RW;
+constexpr int kLocalBackWarps = 8;
+constexpr int kLocalBackWarpFloats = 2 * KC_HEADS * KC_RW * KC_RW;  // p and dS of one record
 constexpr size_t kLocalBackSmem = size_t(kLocalBackWarps) * kLocalBackWarpFloats * 4;
 
-// dOut row r staged as 32 float4, rotated within each head's 8 like the
-// q|k|v rows (la_exact_f4), so a quarter-warp's (token, head) lanes read
-// 8 different bank groups.
-__device__ __forceinline__ int lb_dout_f4(int r, int f) {
-  return r * 32 + (f & ~7) + (((f & 7) + 2 * ((f >> 3) & 3) + (r & 1)) & 7);
-}
-
-__global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
+// One warp per record. q|k|v and dOut are read straight from global memory
+// (a record's rows are a few KB, so repeated reads hit L1), leaving only the
+// record's p and dS in shared memory: 2 KB per warp, so many records are in
+// flight per SM.
+__global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(LocalBackArgs a) {
   extern __shared__ __align__(16) float lsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * kLocalBackWarps + warp;
@@ -551,29 +548,22 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   const uint32_t start = a.rec_start[g];
   const int cnt = int(a.rec_meta[g].y & 15u);
   if (cnt == 0) return;
-  float* base = lsm + size_t(warp) * kLocalBackWarpFloats;
-  float4* rec = reinterpret_cast<float4*>(base);                                  // q|k|v, la_exact_f4 layout
-  float4* dos = reinterpret_cast<float4*>(base + KC_RW * 3 * KC_H);               // dOut, lb_dout_f4 layout
-  float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(base + KC_RW * 4 * KC_H);  // [head][i][j]
-  float(*dsh)[KC_RW][KC_RW] = pp + KC_HEADS;                                                   // [head][i][j]
-  {
-    const float4* s1 = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
-    const float4* s2 = reinterpret_cast<const float4*>(a.dout + uint64_t(start) * KC_H);
-    for (int i = lane; i < cnt * 96; i += 32) cp_async16(rec + la_exact_f4(i / 96, i % 96), s1 + i);
-    for (int i = lane; i < cnt * 32; i += 32) cp_async16(dos + lb_dout_f4(i >> 5, i & 31), s2 + i);
-    for (int i = lane; i < cnt * KC_HEADS * KC_RW; i += 32) {
-      const int ti = i >> 5, head = (i >> 3) & 3, jj = i & 7;
-      pp[head][ti][jj] = a.p[(uint64_t(start) + ti) * KC_HEADS * KC_RW + head * KC_RW + jj];
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+  float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(lsm + size_t(warp) * kLocalBackWarpFloats);
+  float(*dsh)[KC_RW][KC_RW] = pp + KC_HEADS;  // [head][i][j]
+  const float* qkv = a.qkv + uint64_t(start) * 3 * KC_H;
+  const float* dout = a.dout + uint64_t(start) * KC_H;
+  for (int i = lane; i < cnt * KC_HEADS * KC_RW; i += 32) {
+    const int ti = i >> 5, head = (i >> 3) & 3, jj = i & 7;
+    pp[head][ti][jj] = a.p[(uint64_t(start) + ti) * KC_HEADS * KC_RW + head * KC_RW + jj];
   }
   __syncwarp();
   {
     const int ti = lane >> 2, head = lane & 3;
     if (ti < cnt) {
       float4 d4[KC_HEAD_DIM / 4];
+      const float4* dr = reinterpret_cast<const float4*>(dout + ti * KC_H + head * KC_HEAD_DIM);
 #pragma unroll
-      for (int m = 0; m < 8; m++) d4[m] = dos[lb_dout_f4(ti, head * 8 + m)];
+      for (int m = 0; m < 8; m++) d4[m] = dr[m];
       // s[j] = dOut_i · v_j: eight f64 chains side by side, each over d in order
       // (keys past the record read row 0 and are never used)
       double s[KC_RW];
@@ -583,7 +573,8 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
       for (int m = 0; m < 8; m++)
 #pragma unroll
         for (int j = 0; j < KC_RW; j++) {
-          const float4 v = rec[la_exact_f4(j < cnt ? j : 0, (8 + head) * 8 + m)];
+          const float4 v = reinterpret_cast<const float4*>(qkv + (j < cnt ? j : 0) * 3 * KC_H + 2 * KC_H +
+                                                           head * KC_HEAD_DIM)[m];
           s[j] = fma(double(d4[m].x), double(v.x), s[j]);
           s[j] = fma(double(d4[m].y), double(v.y), s[j]);
           s[j] = fma(double(d4[m].z), double(v.z), s[j]);
@@ -600,20 +591,18 @@ __global__ void __launch_bounds__(128) k_local_attn_back(LocalBackArgs a) {
   }
   __syncwarp();
   float* out = a.dqkv + uint64_t(start) * 3 * KC_H;
-  const float* recf = reinterpret_cast<const float*>(rec);
-  const float* dosf = reinterpret_cast<const float*>(dos);
   // dQ_i = Σ_j dS_ij k_j, dK_i = Σ_j dS_ji q_j, dV_i = Σ_j P_ji dOut_j per
   // column: every row i of the record at once (24 f64 chains per lane), each
   // chain over j in order
   for (int m = 0; m < KC_HEADS; m++) {
-    const int col = m * KC_HEAD_DIM + lane, c4 = col >> 2, cw = col & 3;
+    const int col = m * KC_HEAD_DIM + lane;
     double aq[KC_RW], ak[KC_RW], av[KC_RW];
 #pragma unroll
     for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = 0.0;
     for (int j = 0; j < cnt; j++) {
-      const double kj = double(recf[4 * la_exact_f4(j, 32 + c4) + cw]);
-      const double qj = double(recf[4 * la_exact_f4(j, c4) + cw]);
-      const double dj = double(dosf[4 * lb_dout_f4(j, c4) + cw]);
+      const double kj = double(qkv[j * 3 * KC_H + KC_H + col]);
+      const double qj = double(qkv[j * 3 * KC_H + col]);
+      const double dj = double(dout[j * KC_H + col]);
 #pragma unroll
       for (int i = 0; i < KC_RW; i++)
         if (i < cnt) {

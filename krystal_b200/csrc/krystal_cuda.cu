@@ -1307,8 +1307,8 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
       ProfScope ps(h, kStEncAttn);
       kc::LocalBackArgs lb{P<float>(bw.enc_qkv) + blk * T * 3 * H, P<float>(bw.enc_p) + blk * T * 32, dfs,
                            P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale, P<float>(bw.edqkv)};
-      kc::k_local_attn_back<<<unsigned((N + kc::kLocalBackWarps - 1) / kc::kLocalBackWarps), 128,
-                              kc::kLocalBackSmem, h->stream>>>(lb);
+      kc::k_local_attn_back<<<unsigned((N + kc::kLocalBackWarps - 1) / kc::kLocalBackWarps),
+                              kc::kLocalBackWarps * 32, kc::kLocalBackSmem, h->stream>>>(lb);
       h->launches++;
     }
     // dStates += dQ·Wq + dK·Wk + dV·Wv: three f32-rounded adds in the oracle's
