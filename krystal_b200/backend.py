@@ -286,9 +286,12 @@ class CudaBrainBackend:
     # --- packed ragged batches ------------------------------------------------
     def forward_batch(self, batch: FrameBatch, rule: MaskRule | None = None, uniforms=None,
                       want_query_output: bool = False, p_capacity: int | None = None, word_ids=None,
-                      word_alpha: float = 0.0) -> dict:
+                      word_alpha: float = 0.0, out: dict | None = None) -> dict:
         """Pack, encode and select a whole batch; host arrays in and out.
-        word_ids [records*8] / word_alpha: the same-word bias (WordBias)."""
+        word_ids [records*8] / word_alpha: the same-word bias (WordBias).
+        out: caller-owned result arrays to fill instead of fresh ones — "p"
+        (f32), "index" (u32), "p_off" and "q_off" (u64, frames + 1), e.g.
+        pinned buffers reused across calls; p and index set the capacities."""
         keep = [_u32(batch.token_ids), _u32(batch.field_roles), _u32(batch.schema_ids), _u32(batch.band_ids),
                 np.ascontiguousarray(batch.rec_off, dtype=np.uint64)]
         tok, role, sch, band, off = keep
@@ -303,24 +306,32 @@ class CudaBrainBackend:
         bv = abi.KcBatchView(batch.frames, batch.records, off.ctypes.data, tok.ctypes.data, role.ctypes.data,
                              sch.ctypes.data, band.ctypes.data, abi.ptr(sa), abi.ptr(ba), abi.ptr(u), abi.ptr(wid),
                              float(word_alpha))
-        nq = int((band == 5).sum())
-        if p_capacity is None:
+        nq = int((band == 5).sum()) if out is None or want_query_output else 0
+        if p_capacity is None and out is None:
             rec = np.diff(off.astype(np.int64))
             fid = np.repeat(np.arange(batch.frames), rec)
             isq = np.bincount(fid, weights=(band == 5), minlength=batch.frames).astype(np.int64)
             p_capacity = int((isq * (rec - isq)).sum())
-        p = np.empty(max(1, p_capacity), dtype=np.float32)
-        idx = np.empty(max(1, nq), dtype=np.uint32)
-        p_off = np.empty(batch.frames + 1, dtype=np.uint64)
-        q_off = np.empty(batch.frames + 1, dtype=np.uint64)
+        if out is not None:
+            p, idx, p_off, q_off = out["p"], out["index"], out["p_off"], out["q_off"]
+            for a, dt in ((p, np.float32), (idx, np.uint32), (p_off, np.uint64), (q_off, np.uint64)):
+                if a.dtype != dt or not a.flags.c_contiguous:
+                    raise ValueError("out arrays must be contiguous p f32, index u32, p_off / q_off u64")
+            if p_off.size < batch.frames + 1 or q_off.size < batch.frames + 1:
+                raise ValueError("out p_off / q_off need frames + 1 entries")
+        else:
+            p = np.empty(max(1, p_capacity), dtype=np.float32)
+            idx = np.empty(max(1, nq), dtype=np.uint32)
+            p_off = np.empty(batch.frames + 1, dtype=np.uint64)
+            q_off = np.empty(batch.frames + 1, dtype=np.uint64)
         qo = np.empty(max(1, nq) * self.config.hidden_size, dtype=np.float32) if want_query_output else None
-        out = abi.KcBatchOut(p.ctypes.data, p.size, idx.ctypes.data, idx.size, p_off.ctypes.data, q_off.ctypes.data,
-                             abi.ptr(qo), 0, 0, 0, 0)
-        abi.check(self._lib.kc_forward_batch(self._h, C.byref(bv), C.byref(out)), self._h)
-        res = {"p": p[:out.total_p], "index": idx[:out.total_q], "p_off": p_off, "q_off": q_off,
-               "total_t": out.total_t, "total_r": out.total_r}
+        bo = abi.KcBatchOut(p.ctypes.data, p.size, idx.ctypes.data, idx.size, p_off.ctypes.data, q_off.ctypes.data,
+                            abi.ptr(qo), 0, 0, 0, 0)
+        abi.check(self._lib.kc_forward_batch(self._h, C.byref(bv), C.byref(bo)), self._h)
+        res = {"p": p[:bo.total_p], "index": idx[:bo.total_q], "p_off": p_off, "q_off": q_off,
+               "total_t": bo.total_t, "total_r": bo.total_r}
         if qo is not None:
-            res["query_output"] = qo[:out.total_q * self.config.hidden_size]
+            res["query_output"] = qo[:bo.total_q * self.config.hidden_size]
         return res
 
     def forward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,

@@ -120,3 +120,23 @@ def test_word_bias_fused_equals_unfused(pair):
     words[rng.random(words.size) < 0.2] = 0xFFFFFFFF
     kw = dict(word_ids=words, word_alpha=1.5)
     assert_same(run(fused, batch, "fast", **kw), run(unfused, batch, "fast", **kw))
+
+
+def test_caller_output_buffers(pair):
+    """forward_batch(out=...) fills caller-owned arrays (reused across calls)
+    with exactly what fresh arrays receive; too small a p buffer is refused."""
+    fused, _ = pair
+    fused.set_precision("certified")
+    batch = synth.make_batch(WL, seed=47, frames=64)
+    want = fused.forward_batch(batch)
+    offs = batch.offsets()
+    out = {"p": np.full(int(offs["p_off"][-1]) + 7, -1.0, np.float32),
+           "index": np.zeros(int(offs["q_off"][-1]), np.uint32),
+           "p_off": np.zeros(batch.frames + 1, np.uint64), "q_off": np.zeros(batch.frames + 1, np.uint64)}
+    for _ in range(2):
+        got = fused.forward_batch(batch, out=out)
+        assert np.array_equal(got["p"], want["p"]) and np.array_equal(got["index"], want["index"])
+        assert np.array_equal(out["p_off"], want["p_off"]) and np.array_equal(out["q_off"], want["q_off"])
+    small = dict(out, p=np.empty(int(offs["p_off"][-1]) - 1, np.float32))
+    with pytest.raises(Exception):
+        fused.forward_batch(batch, out=small)
