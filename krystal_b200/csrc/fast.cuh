@@ -239,7 +239,7 @@ struct CrossAttnFrameArgs {
   float scale;
 };
 
-__global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameArgs a) {
+__global__ void __launch_bounds__(kCaThreads, 3) k_cross_attn_frame(CrossAttnFrameArgs a) {
   extern __shared__ __align__(16) float caf_smem[];  // scores [qc][4][max_r], then q [qc][128]
   __shared__ float inv_s[kCaChunk][KC_HEADS];
   const uint32_t f = blockIdx.x / a.chunks;
@@ -298,58 +298,45 @@ __global__ void __launch_bounds__(kCaThreads) k_cross_attn_frame(CrossAttnFrameA
       if (lane == 0) inv_s[rw >> 2][rw & 3] = 1.f / fmaxf(sum, 1e-20f);
     }
     __syncthreads();
-    // p·v: one output column per thread for every other question of the chunk,
-    // each v element loaded once for them
+    // p·v per output column: threads 0-127 form the sum over the even keys and
+    // threads 128-255 the sum over the odd keys (each in key order, every
+    // question of the chunk at once, each v element loaded once for them);
+    // the output adds the two, as the one-question-at-a-time form does
     {
-      const int col = tid & (KC_H - 1), head = col >> 5, c0 = tid >> 7;
-      float v0[kCaChunk / 2], v1[kCaChunk / 2];
+      const int col = tid & (KC_H - 1), head = col >> 5, par = tid >> 7;
+      float acc[kCaChunk];
 #pragma unroll
-      for (int u = 0; u < kCaChunk / 2; u++) v0[u] = v1[u] = 0.f;
+      for (int c = 0; c < kCaChunk; c++) acc[c] = 0.f;
       const float* vcol = a.mv + rb * KC_H + col;
-      int j = 0;
-      // thirty-two v elements in flight per step; the even / odd sums keep their order
-      for (; j + 31 < R; j += 32) {
+      int j = par;
+      for (; j + 62 < R; j += 64) {  // 32 keys of this parity in flight per step
         float vv[32];
 #pragma unroll
-        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + e) * KC_H];
+        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + 2 * e) * KC_H];
 #pragma unroll
-        for (int u = 0; u < kCaChunk / 2; u++) {
-          const int c = c0 + 2 * u;
+        for (int c = 0; c < kCaChunk; c++)
           if (c < nc) {
             const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              v0[u] = fmaf(row[e], vv[e], v0[u]);
-              v1[u] = fmaf(row[e + 1], vv[e + 1], v1[u]);
-            }
+            for (int e = 0; e < 32; e++) acc[c] = fmaf(row[2 * e], vv[e], acc[c]);
           }
-        }
       }
-      for (; j + 1 < R; j += 2) {
-        const float va = vcol[size_t(j) * KC_H], vb = vcol[size_t(j + 1) * KC_H];
-#pragma unroll
-        for (int u = 0; u < kCaChunk / 2; u++) {
-          const int c = c0 + 2 * u;
-          if (c < nc) {
-            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r;
-            v0[u] = fmaf(row[j], va, v0[u]);
-            v1[u] = fmaf(row[j + 1], vb, v1[u]);
-          }
-        }
-      }
-      if (j < R) {
+      for (; j < R; j += 2) {
         const float va = vcol[size_t(j) * KC_H];
 #pragma unroll
-        for (int u = 0; u < kCaChunk / 2; u++) {
-          const int c = c0 + 2 * u;
-          if (c < nc) v0[u] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, v0[u]);
-        }
+        for (int c = 0; c < kCaChunk; c++)
+          if (c < nc) acc[c] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, acc[c]);
       }
+      // the odd sums meet the even ones in the (now free) question buffer
+      if (par == 1)
 #pragma unroll
-      for (int u = 0; u < kCaChunk / 2; u++) {
-        const int c = c0 + 2 * u;
-        if (c < nc) a.query[(qb + q0 + c) * KC_H + col] += (v0[u] + v1[u]) * inv_s[c][head];
-      }
+        for (int c = 0; c < kCaChunk; c++)
+          if (c < nc) qs[c * KC_H + col] = acc[c];
+      __syncthreads();
+      if (par == 0)
+#pragma unroll
+        for (int c = 0; c < kCaChunk; c++)
+          if (c < nc) a.query[(qb + q0 + c) * KC_H + col] += (acc[c] + qs[c * KC_H + col]) * inv_s[c][head];
     }
     __syncthreads();
   }
