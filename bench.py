@@ -724,9 +724,30 @@ def e2e_leg(be, batch, stream, args, dev, world) -> dict:
     sec = float(t.item()) / 1e3
     h2d = sum(a.nbytes for a in (hb.rec_off, hb.token_ids, hb.field_roles, hb.schema_ids, hb.band_ids))
     d2h = res["p"].nbytes + res["index"].nbytes + 2 * (batch.frames + 1) * 8
+    # consider once, choose many: the resident batch decided again under
+    # alternating per-question mask rules (kc_select_batch), host results
+    from krystal_b200.backend import MaskRule
+    rules = [MaskRule(*[pinned(a) for a in synth.make_rule(batch, seed=11 + k, density=0.5)]) for k in range(2)]
+    be.forward_batch(hb, out=outb)
+    for k in range(2):
+        be.select_batch(rule=rules[k], out=outb)
+    torch.cuda.synchronize(dev)
+    r0 = torch.cuda.Event(enable_timing=True)
+    r1 = torch.cuda.Event(enable_timing=True)
+    reps = max(4, args.steps)
+    r0.record(stream)
+    for k in range(reps):
+        be.select_batch(rule=rules[k % 2], out=outb)
+    r1.record(stream)
+    torch.cuda.synchronize(dev)
+    rms = r0.elapsed_time(r1) / reps
+    nq = int(offs["q_off"][-1])
     return {"value": world * batch.frames * args.steps / sec, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "entry": "kc_forward_batch (host buffers, pinned inputs and reused pinned outputs)"}
+            "entry": "kc_forward_batch (host buffers, pinned inputs and reused pinned outputs)",
+            "reselect": {"entry": "kc_select_batch (the resident batch, a new per-question mask rule; "
+                                  "certified, results to host)", "ms": rms, "questions_per_sec": nq / (rms / 1e3),
+                         "rule_bytes": int(rules[0].schema_allow.nbytes + rules[0].band_allow.nbytes)}}
 
 
 def latency_leg(be, stream, dev, repeats: int = 200) -> dict:

@@ -261,6 +261,25 @@ kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, const float* q
  * host<->device copies are part of the call. */
 kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* batch, kc_batch_out* out);
 
+/* consider / choose reuse at batch scale (host/session.ts:128-176: consider()
+ * encodes once, each choose() selects again under its own mask): the last
+ * batch kc_forward_batch ran on this handle, selected again under a new mask
+ * rule (per question, laid out as in kc_batch_view) and/or new uniforms
+ * (NULL: argmax), without encoding it again. At the batch's precision; in
+ * the certified mode frames it cannot certify are recomputed on the exact
+ * path as in kc_forward_batch. The batch is resident until any other call on
+ * the handle that packs or selects (kc_forward_batch again, kc_encode,
+ * kc_select, the backward and learn calls, a stream's batches) or changes
+ * weights (kc_sync, kc_load_checkpoint); KC_ERR_INVALID_ARG otherwise.
+ * Results as for kc_forward_batch. */
+typedef struct kc_batch_select_view {
+  const uint32_t* schema_allow;  /* [Q * 8] or NULL (the open mask) */
+  const uint32_t* band_allow;    /* [Q], NULL with schema_allow */
+  const double* uniforms;        /* [Q] or NULL */
+} kc_batch_select_view;
+
+kc_status kc_select_batch(kc_handle* h, const kc_batch_select_view* select, kc_batch_out* out);
+
 /* As kc_forward_batch, but every array in `batch` is a DEVICE pointer on the
  * handle's device. Work is queued on the handle's stream; the call returns
  * once the result is queued (one short host wait inside, for the batch's

@@ -40,7 +40,7 @@ EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "
            "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
            "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_pending",
            "kc_stream_poll", "kc_stream_clock_ms", "kc_stream_last_error", "kc_stream_destroy",
-           "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint")
+           "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch")
 
 
 class KrystalCudaError(RuntimeError):
@@ -100,6 +100,10 @@ class KcBatchOut(C.Structure):
     _fields_ = [("p", P), ("p_capacity", C.c_uint64), ("index", P), ("q_capacity", C.c_uint64), ("p_off", P),
                 ("q_off", P), ("query_output", P), ("total_p", C.c_uint64), ("total_q", C.c_uint64),
                 ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
+
+
+class KcBatchSelectView(C.Structure):
+    _fields_ = [("schema_allow", P), ("band_allow", P), ("uniforms", P)]
 
 
 class KcDeviceResult(C.Structure):
@@ -162,6 +166,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_encode.argtypes = [P, C.POINTER(KcFrameView), P, P, P, C.c_uint32, C.c_uint32, u32p, u32p]
     lib.kc_select.argtypes = [P, C.POINTER(KcEncodedView), P, C.POINTER(KcMaskRule), P, P, P, P]
     lib.kc_forward_batch.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcBatchOut)]
+    lib.kc_select_batch.argtypes = [P, C.POINTER(KcBatchSelectView), C.POINTER(KcBatchOut)]
     lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
     lib.kc_select_noalloc.argtypes = [P, C.c_uint32, C.c_uint32, P, P, P, P, P, P, P]
     lib.kc_set_precision.argtypes = [P, C.c_int, C.c_float]
@@ -200,7 +205,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
                  "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
                  "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_poll",
-                 "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint"):
+                 "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

@@ -330,9 +330,35 @@ class CudaBrainBackend:
         abi.check(self._lib.kc_forward_batch(self._h, C.byref(bv), C.byref(bo)), self._h)
         res = {"p": p[:bo.total_p], "index": idx[:bo.total_q], "p_off": p_off, "q_off": q_off,
                "total_t": bo.total_t, "total_r": bo.total_r}
+        self._last_batch_sizes = (int(bo.total_p), int(bo.total_q), batch.frames)
         if qo is not None:
             res["query_output"] = qo[:bo.total_q * self.config.hidden_size]
         return res
+
+    def select_batch(self, rule: MaskRule | None = None, uniforms=None, out: dict | None = None) -> dict:
+        """kc_select_batch: the last forward_batch's batch selected again under
+        `rule` and/or `uniforms` (per question), without encoding it again
+        (consider once, choose many: host/session.ts:128-176). `out` as for
+        forward_batch; without it the result arrays are sized from that batch."""
+        sa = ba = u = None
+        if rule is not None:
+            sa, ba = _u32(rule.schema_allow), _u32(rule.band_allow)
+        if uniforms is not None:
+            u = np.ascontiguousarray(uniforms, dtype=np.float64)
+        sv = abi.KcBatchSelectView(abi.ptr(sa), abi.ptr(ba), abi.ptr(u))
+        if out is None:
+            last = getattr(self, "_last_batch_sizes", None)
+            if last is None:
+                raise RuntimeError("no batch has been run through forward_batch on this backend")
+            p_cap, nq, frames = last
+            out = {"p": np.empty(max(1, p_cap), np.float32), "index": np.empty(max(1, nq), np.uint32),
+                   "p_off": np.empty(frames + 1, np.uint64), "q_off": np.empty(frames + 1, np.uint64)}
+        p, idx, p_off, q_off = out["p"], out["index"], out["p_off"], out["q_off"]
+        bo = abi.KcBatchOut(p.ctypes.data, p.size, idx.ctypes.data, idx.size, p_off.ctypes.data, q_off.ctypes.data,
+                            None, 0, 0, 0, 0)
+        abi.check(self._lib.kc_select_batch(self._h, C.byref(sv), C.byref(bo)), self._h)
+        return {"p": p[:bo.total_p], "index": idx[:bo.total_q], "p_off": p_off, "q_off": q_off,
+                "total_t": bo.total_t, "total_r": bo.total_r}
 
     def forward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,
                              schema_ids: int, band_ids: int, schema_allow: int | None = None,

@@ -187,6 +187,17 @@ struct kc_handle {
   kc::FrameTotals* h_tot = nullptr;  // pinned
   std::string err;
   uint64_t launches = 0;
+  // the batch whose encodings are resident in ws for kc_select_batch: ws_epoch
+  // counts packings into ws and weight changes; the batch is resident while
+  // resident_epoch still equals it
+  uint64_t ws_epoch = 0, resident_epoch = 0;
+  int resident_precision = KC_PRECISION_CERTIFIED;
+  uint32_t resident_frames = 0;
+  uint64_t resident_records = 0;
+  float resident_alpha = 0.0f;      // the resident batch's same-word bias (its ids stay in ws.word_ids)
+  bool resident_words = false;
+  kc::FrameTotals resident_tot{};   // the resident batch's totals
+  bool last_overflow = false;       // the last certified batch split out of range
   // the fused encoder kernels (k_tc_attn, k_tc_ffn) where the dimensions fit;
   // KC_NO_FUSION=1 in the environment at kc_create runs the unfused sequence
   // (the same arithmetic, kept for the learn path and checked against the fused)
@@ -546,6 +557,7 @@ const char* bad_message(uint32_t code) {
 // wait for the batch totals (sizes the rest of the workspace).
 kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTotals* out_tot) {
   const Dims& d = h->d;
+  if (&ws == &h->ws) h->ws_epoch++;
   const uint32_t F = b.frames;
   const uint64_t N = b.records;
   if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "a batch with no frames");
@@ -628,6 +640,29 @@ struct Saves {
   const float* mask;                                // [P]
   float* gather;                                    // [Q,H]
 };
+
+// The exact selection over the resident sq / sk of a packed batch: the rule
+// and uniforms of b, or (the backward) an explicit mask, no sampling and the
+// soft gather into `gather`.
+void launch_select_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
+                         const float* mask, float* gather) {
+  kc::SelectArgs sa{};
+  sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk); sa.bank_values = nullptr;
+  sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
+  sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
+  sa.mask = nullptr; sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
+  sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
+  sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = 1.0 / std::sqrt(double(h->d.h));
+  sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = nullptr;
+  if (mask) {
+    sa.mask = mask; sa.schema_allow = nullptr; sa.band_allow = nullptr; sa.uniforms = nullptr;
+    sa.bank_values = P<float>(ws.bv); sa.gather = gather;
+  }
+  const size_t smem = size_t(tot.max_r) * (8 + 4);
+  kc::k_select_exact<<<unsigned(tot.q), 256, smem, h->stream>>>(sa);
+  h->launches++;
+}
+
 
 // The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
 // the workspace: qstate [Q,H], bk/bv [R,H], p, index.
@@ -712,24 +747,28 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
     const int sm = 3 * int(d.enc) + 5 * int(d.mix);
     KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, sm, h->w + d.off_swq, H, P<float>(ws.sq), H, H));
     KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, sm + 1, h->w + d.off_swk, H, P<float>(ws.sk), H, H));
-    kc::SelectArgs sa{};
-    sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk); sa.bank_values = nullptr;
-    sa.query_frame = P<uint32_t>(ws.query_frame); sa.r_off = P<uint64_t>(ws.r_off);
-    sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
-    sa.mask = nullptr; sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
-    sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
-    sa.uniforms = b.uniforms; sa.max_r = tot.max_r; sa.scale = h_scale;
-    sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = nullptr;
-    if (sv) {  // the backward's selection: its mask, no sampling, the soft gather
-      sa.mask = sv->mask; sa.schema_allow = nullptr; sa.band_allow = nullptr; sa.uniforms = nullptr;
-      sa.bank_values = P<float>(ws.bv); sa.gather = sv->gather;
-    }
-    const size_t smem = size_t(tot.max_r) * (8 + 4);
-    kc::k_select_exact<<<unsigned(Q), 256, smem, h->stream>>>(sa);
-    h->launches++;
+    launch_select_exact(h, ws, b, tot, sv ? sv->mask : nullptr, sv ? sv->gather : nullptr);
   }
   KC_TRY(cudaGetLastError(), "launch");
   return KC_OK;
+}
+
+// The certified selection over the resident sq / sk of a packed batch: p,
+// indices and the per-frame flags of decisions it cannot certify.
+void launch_select_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
+  kc::SelectFastArgs sa{};
+  sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk);
+  sa.r_off = P<uint64_t>(ws.r_off);
+  sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
+  sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
+  sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
+  sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
+  sa.chunks = int((std::max<uint32_t>(tot.max_q, 1) + sa.qc - 1) / sa.qc);
+  sa.scale = float(1.0 / std::sqrt(double(h->d.h)));
+  sa.tau = h->tau; sa.tau_c = h->tau_c;
+  sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
+  kc::k_select_fast<<<b.frames * unsigned(sa.chunks), 256, sel_smem(tot.max_r), h->stream>>>(sa);
+  h->launches++;
 }
 
 // The forward on the tensor cores (tc_gemm.cuh, fast.cuh): the selector
@@ -815,19 +854,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     ProfScope ps(h, kStSelector);
     KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, sel_m, P<float>(ws.sq)));
     KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, sel_m + 1, P<float>(ws.sk)));
-    kc::SelectFastArgs sa{};
-    sa.sq = P<float>(ws.sq); sa.sk = P<float>(ws.sk);
-    sa.r_off = P<uint64_t>(ws.r_off);
-    sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
-    sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
-    sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
-    sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
-    sa.chunks = int((std::max<uint32_t>(tot.max_q, 1) + sa.qc - 1) / sa.qc);
-    sa.scale = float(1.0 / std::sqrt(double(H)));
-    sa.tau = h->tau; sa.tau_c = h->tau_c;
-    sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
-    kc::k_select_fast<<<b.frames * unsigned(sa.chunks), 256, sel_smem(tot.max_r), h->stream>>>(sa);
-    h->launches++;
+    launch_select_fast(h, ws, b, tot);
   }
   KC_TRY(cudaGetLastError(), "launch");
   return KC_OK;
@@ -852,6 +879,7 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   if (e & kc::tc::kErrTimeout)
     return fail(h, KC_ERR_TIMEOUT, "a tensor-core pipeline wait expired; the batch was not completed");
   const bool all = e & kc::tc::kErrOverflow;
+  h->last_overflow = all;
   if (all && h->sa > -24) h->sa -= 6;  // later batches split at a smaller scale
   std::vector<uint32_t>& list = h->h_flags;
   list.clear();
@@ -1433,6 +1461,7 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
 kc_status kc_sync(kc_handle* h, const kc_weights_view* weights, const kc_changes* changes) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   return do_sync(h, weights, changes);
 }
@@ -1441,6 +1470,7 @@ kc_status kc_encode(kc_handle* h, const kc_frame_view* frame, float* query_outpu
                     float* bank_values, uint32_t q_cap, uint32_t r_cap, uint32_t* q_out, uint32_t* r_out) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   uint32_t q = 0, r = 0;
   DevBatch b;
@@ -1468,6 +1498,7 @@ kc_status kc_select(kc_handle* h, const kc_encoded_view* enc, const float* mask,
                     const double* uniforms, float* p, uint32_t* index, float* gather) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (!enc || !enc->query_output || (enc->r && (!enc->bank_keys || !enc->bank_values)) || !p || !index)
     return fail(h, KC_ERR_INVALID_ARG, "select arguments are incomplete");
@@ -1574,6 +1605,7 @@ extern "C" kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, con
                                        float* p, uint32_t* index, float* gather) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (q > kNoAllocMaxQ || r > kNoAllocMaxR) {
     char buf[160];
@@ -1647,6 +1679,8 @@ static kc_status batch_host_common(kc_handle* h, const kc_batch_view* bv, DevBat
 }  // extern "C"
 
 namespace {
+kc_status copy_out(kc_handle* h, uint32_t frames, const kc::FrameTotals& tot, kc_batch_out* out);
+
 // kc_forward_batch with the handle's lock held and its device current.
 kc_status forward_batch_host(kc_handle* h, const kc_batch_view* bv, kc_batch_out* out) {
   if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
@@ -1676,18 +1710,92 @@ kc_status forward_batch_host(kc_handle* h, const kc_batch_view* bv, kc_batch_out
   }
   kc::FrameTotals tot;
   if ((s = run_batch(h, b, false, &tot))) return s;
+  // the batch stays resident for kc_select_batch until ws is packed again or
+  // the weights change (the last overflowed certified batch has no usable
+  // tensor-core projections: its reselection runs the whole batch again)
+  h->resident_epoch = h->ws_epoch;
+  h->resident_precision = h->precision;
+  h->resident_frames = b.frames;
+  h->resident_records = b.records;
+  h->resident_words = b.word_ids != nullptr;
+  h->resident_alpha = b.word_alpha;
+  h->resident_tot = tot;
+  return copy_out(h, bv->frames, tot, out);
+}
+
+// The results of the batch in ws (p, indices, offsets, optionally the mixer's
+// query output) into the caller's host buffers.
+kc_status copy_out(kc_handle* h, uint32_t frames, const kc::FrameTotals& tot, kc_batch_out* out) {
+  Workspace& ws = h->ws;
   out->total_p = tot.p; out->total_q = tot.q; out->total_r = tot.r; out->total_t = tot.t;
   if (tot.p > out->p_capacity || tot.q > out->q_capacity || (tot.p && !out->p) || (tot.q && !out->index))
     return fail(h, KC_ERR_CAPACITY, "output buffers are smaller than the batch's p / index");
   if (tot.p) KC_TRY(cudaMemcpyAsync(out->p, ws.p.p, tot.p * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
   if (tot.q) KC_TRY(cudaMemcpyAsync(out->index, ws.index.p, tot.q * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
-  if (out->p_off) KC_TRY(cudaMemcpyAsync(out->p_off, ws.p_off.p, (bv->frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
-  if (out->q_off) KC_TRY(cudaMemcpyAsync(out->q_off, ws.q_off.p, (bv->frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (out->p_off) KC_TRY(cudaMemcpyAsync(out->p_off, ws.p_off.p, (frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  if (out->q_off) KC_TRY(cudaMemcpyAsync(out->q_off, ws.q_off.p, (frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
   if (out->query_output && tot.q)
     KC_TRY(cudaMemcpyAsync(out->query_output, ws.qstate.p, tot.q * h->d.h * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
   KC_TRY(cudaStreamSynchronize(h->stream), "batch");
   prof_collect(h);
   return KC_OK;
+}
+
+// kc_select_batch with the handle's lock held and its device current.
+kc_status select_batch_host(kc_handle* h, const kc_batch_select_view* sv, kc_batch_out* out) {
+  if (!out) return fail(h, KC_ERR_INVALID_ARG, "select_batch arguments are incomplete");
+  if (h->resident_epoch == 0 || h->resident_epoch != h->ws_epoch)
+    return fail(h, KC_ERR_INVALID_ARG,
+                "no batch is resident: run kc_forward_batch first (another call on this handle, or a weight "
+                "change, since then releases it)");
+  const bool rule = sv && sv->schema_allow;
+  if (sv && (sv->schema_allow == nullptr) != (sv->band_allow == nullptr))
+    return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  Workspace& ws = h->ws;
+  const kc::FrameTotals tot = h->resident_tot;
+  DevBatch b;
+  b.frames = h->resident_frames; b.records = h->resident_records; b.rec_off = P<uint64_t>(ws.rec_off);
+  b.token_ids = P<uint32_t>(ws.token_ids); b.field_roles = P<uint32_t>(ws.field_roles);
+  b.schema_ids = P<uint32_t>(ws.schema_ids); b.band_ids = P<uint32_t>(ws.band_ids);
+  if (h->resident_words) { b.word_ids = P<uint32_t>(ws.word_ids); b.word_alpha = h->resident_alpha; }
+  kc_status s;
+  if (rule) {
+    if ((s = stage(h, ws.schema_allow, sv->schema_allow, tot.q * 8)) || (s = stage(h, ws.band_allow, sv->band_allow, tot.q)))
+      return s;
+    b.schema_allow = P<uint32_t>(ws.schema_allow);
+    b.band_allow = P<uint32_t>(ws.band_allow);
+  }
+  if (sv && sv->uniforms) {
+    if ((s = stage(h, ws.uniforms, sv->uniforms, tot.q))) return s;
+    b.uniforms = P<double>(ws.uniforms);
+  }
+  if (tot.q > 0) {
+    const int precision = h->resident_precision;
+    if (precision == KC_PRECISION_EXACT) {
+      ProfScope ps(h, kStSelector);
+      launch_select_exact(h, ws, b, tot, nullptr, nullptr);
+      KC_TRY(cudaGetLastError(), "launch");
+    } else if (h->last_overflow) {
+      // the tensor-core projections overflowed the split: the batch again, whole
+      kc::FrameTotals t2;
+      const int saved = h->precision;
+      h->precision = precision;
+      s = run_batch(h, b, false, &t2);
+      h->precision = saved;
+      h->resident_epoch = h->ws_epoch;
+      if (s) return s;
+    } else {
+      KC_TRY(cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream), "memset");
+      KC_TRY(cudaMemsetAsync(ws.flags.p, 0, b.frames * 4ull, h->stream), "memset");
+      {
+        ProfScope ps(h, kStSelector);
+        launch_select_fast(h, ws, b, tot);
+        KC_TRY(cudaGetLastError(), "launch");
+      }
+      if (precision == KC_PRECISION_CERTIFIED) KC_CHECK(certify(h, ws, b, tot));
+    }
+  }
+  return copy_out(h, b.frames, tot, out);
 }
 }  // namespace
 
@@ -1700,9 +1808,17 @@ kc_status kc_forward_batch(kc_handle* h, const kc_batch_view* bv, kc_batch_out* 
   return forward_batch_host(h, bv, out);
 }
 
+kc_status kc_select_batch(kc_handle* h, const kc_batch_select_view* sv, kc_batch_out* out) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  return select_batch_host(h, sv, out);
+}
+
 kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_device_result* out) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
   if (!bv->rec_off || !bv->token_ids || !bv->field_roles || !bv->schema_ids || !bv->band_ids)
@@ -1732,6 +1848,7 @@ kc_status kc_backward(kc_handle* h, const kc_frame_view* frame, const float* sel
                       int has_valence, double valence, kc_backward_out* out) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (!out || !out->policy || !out->value_prediction || !out->d_selector_wq || !out->d_selector_wk ||
       !out->d_pool || !out->d_value_wv)
@@ -1778,6 +1895,7 @@ kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* bv, const 
                                    const uint32_t* targets, const double* valence, kc_backward_result* out) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
   if (!bv->rec_off || !bv->token_ids || !bv->field_roles || !bv->schema_ids || !bv->band_ids)
@@ -1808,6 +1926,7 @@ kc_status kc_backward_batch_device(kc_handle* h, const kc_batch_view* bv, const 
 kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* stats) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   const uint32_t F = h->bw.frames;
   if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "no batch has been differentiated on this handle");
@@ -1826,6 +1945,7 @@ kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* st
 kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   const uint32_t F = h->bw.frames;
   if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "no batch has been differentiated on this handle");
@@ -1846,6 +1966,7 @@ kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* va
 kc_status kc_load_checkpoint(kc_handle* h, const void* bytes, uint64_t len, int* refusal) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
   DeviceGuard dg(h->device);
   if (!refusal || (!bytes && len)) return fail(h, KC_ERR_INVALID_ARG, "checkpoint arguments are incomplete");
   const Dims& d = h->d;
