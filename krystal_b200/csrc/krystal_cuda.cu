@@ -306,14 +306,14 @@ void prof_collect(kc_handle* h) {
   h->ev_bytes.clear();
 }
 
-// The exact GEMM with the largest CTA tile that still gives every SM a tile
-// (128 for the token-parallel products, 64 or 32 for the few rows of the
-// recomputed frames' mixer and selector).
+// The exact GEMM with the largest CTA tile that still keeps most SMs busy
+// (128 once its grid covers half of them: the token-parallel products; 64
+// or 32 for the few rows of the recomputed frames' mixer and selector).
 template <int EPI>
 void launch_dgemm(kc_handle* h, const float* A, uint32_t lda, const float* B, uint32_t ldb, float* C, uint64_t M,
                   uint32_t N, uint32_t K, const float* gate) {
   const uint64_t sms = uint64_t(h->sms);
-  if (((M + 127) / 128) * (N / 128) >= sms)
+  if (2 * ((M + 127) / 128) * (N / 128) >= sms)
     kc::k_dgemm_exact<EPI, 128><<<dim3(unsigned((M + 127) / 128), N / 128), 256, 0, h->stream>>>(
         A, B, C, int(M), int(N), int(K), int(lda), int(ldb), int(N), gate);
   else if (((M + 63) / 64) * (N / 64) >= sms)
