@@ -174,13 +174,43 @@ __global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
     ks[j] = pk.x * xs[j].x + pk.y * xs[j].y + pk.z * xs[j].z + pk.w * xs[j].w;
     vs[j] = pv.x * xs[j].x + pv.y * xs[j].y + pv.z * xs[j].z + pv.w * xs[j].w;
   }
+  // The sixteen lane partials (8 rows x the key and value queries), each
+  // reduced over the 32 lanes by the xor butterfly 16, 8, 4, 2, 1 — transposed:
+  // at each step a lane keeps half of its partial sums and hands the other
+  // half to its partner, so the sixteen reductions take 16 shuffles instead
+  // of 80 (and 16 to broadcast the totals). Every partial is formed from the
+  // same two operands in the same order as in sixteen separate butterflies,
+  // so the totals are bit-identical to them. Lane l ends with total l >> 1.
+  {
+    float v16[2 * KC_RW];
 #pragma unroll
-  for (int o = 16; o; o >>= 1)
+    for (int j = 0; j < KC_RW; j++) { v16[j] = ks[j]; v16[KC_RW + j] = vs[j]; }
+    float a8[8], a4[4], a2[2];
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float keep = b4 ? v16[8 + i] : v16[i], send = b4 ? v16[i] : v16[8 + i];
+      a8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float keep = b3 ? a8[4 + i] : a8[i], send = b3 ? a8[i] : a8[4 + i];
+      a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const float keep = b2 ? a4[2 + i] : a4[i], send = b2 ? a4[i] : a4[2 + i];
+      a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const float keep = b1 ? a2[1] : a2[0], send = b1 ? a2[0] : a2[1];
+    float t = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
 #pragma unroll
     for (int j = 0; j < KC_RW; j++) {
-      ks[j] += __shfl_xor_sync(0xffffffffu, ks[j], o);
-      vs[j] += __shfl_xor_sync(0xffffffffu, vs[j], o);
+      ks[j] = __shfl_sync(0xffffffffu, t, 2 * j);
+      vs[j] = __shfl_sync(0xffffffffu, t, 2 * (KC_RW + j));
     }
+  }
   float kmx = -INFINITY, vmx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < KC_RW; j++)
