@@ -293,7 +293,24 @@ __global__ void __launch_bounds__(256) k_weight_grad(const float* __restrict__ d
   const int k = threadIdx.x & 127, n0 = blockIdx.y * 8 + (threadIdx.x >> 7) * 4;
   const uint64_t l0 = row_off[f], L = row_off[f + 1] - l0;
   double acc[4] = {0.0, 0.0, 0.0, 0.0};
-  for (uint64_t l = 0; l < L; l++) {
+  uint64_t l = 0;
+  for (; l + 4 <= L; l += 4) {  // four rows' loads in flight, each chain still in row order
+    float x[4];
+    float4 dy[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      x[u] = X[(l0 + l + u) * KC_H + k];
+      dy[u] = *reinterpret_cast<const float4*>(dY + (l0 + l + u) * KC_H + n0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      acc[0] = fma(double(dy[u].x), double(x[u]), acc[0]);
+      acc[1] = fma(double(dy[u].y), double(x[u]), acc[1]);
+      acc[2] = fma(double(dy[u].z), double(x[u]), acc[2]);
+      acc[3] = fma(double(dy[u].w), double(x[u]), acc[3]);
+    }
+  }
+  for (; l < L; l++) {
     const double x = X[(l0 + l) * KC_H + k];
     const float* dy = dY + (l0 + l) * KC_H + n0;
 #pragma unroll
@@ -366,8 +383,17 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   __syncthreads();
   const int head = tid >> 5;
   const float* dr = dss + head * size_t(a.max_r);
+  const float* mkc = a.mk + rb * KC_H + tid;
   double acc = 0.0;
-  for (int j = 0; j < R; j++) acc = fma(double(dr[j]), double(a.mk[(rb + j) * KC_H + tid]), acc);
+  int j = 0;
+  for (; j + 8 <= R; j += 8) {  // eight keys' loads in flight, the chain in key order
+    float kv[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) kv[u] = mkc[size_t(j + u) * KC_H];
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = fma(double(dr[j + u]), double(kv[u]), acc);
+  }
+  for (; j < R; j++) acc = fma(double(dr[j]), double(mkc[size_t(j) * KC_H]), acc);
   a.dq[uint64_t(qi) * KC_H + tid] = f32(acc * a.scale);
 }
 
