@@ -62,4 +62,10 @@ __device__ __forceinline__ T block_excl_scan(T v, T* total, T* tmp) {
   return prefix + x - v;
 }
 
+// One 16-byte asynchronous global -> shared copy (cp.async.wait_all before use).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
+}
+
 }  // namespace kc

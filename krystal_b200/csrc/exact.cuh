@@ -224,12 +224,6 @@ struct LocalAttnArgs {
 };
 
 
-// One 16-byte asynchronous global -> shared copy (cp.async.wait_all before use).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-               ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
-}
-
 // Staged q|k|v row r of a record: 96 float4 (q heads 0-3, k heads 4-7, v
 // heads 8-11, 8 float4 each). Within each head's 8, float4 m sits at
 // (m + 2·(head & 3) + (r & 1)) & 7, so the 8 lanes of a quarter-warp —
@@ -442,94 +436,249 @@ __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* red) {
 // ---------------------------------------------------------------------------
 // Mixer cross-attention (attentionOracle dense mode with the session's open
 // mixer mask, oracle.ts:292, session.ts:146) fused with the residual add
-// (:293). One CTA of 128 threads per question; the frame's bank rows are
-// R = r_off[f+1]-r_off[f] (<= max_r). Dynamic shared memory: 4 heads x R
-// f32 scores + 4 x R f64 exponentials.
+// (:293), in the oracle's arithmetic:
+//   score_j = f32(Σ_d fma(q_d, k_jd) · scale + 0)   (f64, d in order)
+//   m = max_j score_j;  e_j = exp(score_j − m) (f64)
+//   sum = Σ_j e_j in index order (f64);  p_j = f32(f32(e_j) · (1 / max(sum, 1e-20)))
+//   out_c = Σ_j fma(p_j, v_jc) in index order (f64);  x_c = f32(x_c + f32(out_c))
+// with rows whose every score is below -1e29 giving p = 0.
+//
+// One CTA per chunk of up to kXaChunk questions of a frame, the chunks of a
+// frame adjacent in the grid (they share the bank in L2). The bank's k rows
+// stream through shared memory in blocks of kXaBlock keys, each loaded once
+// for the whole chunk; three passes over the blocks compute the scores
+// again, identically, each time: (1) the row maxima and the all-blocked test
+// (neither depends on the order), (2) the exponentials, which one thread per
+// row adds in index order, the sum carried from block to block, (3) p, then
+// p·v, each output chain carried in index order from block to block.
+//
+// Score tiles: thread t takes head t>>6, questions 2((t>>3)&7) and +1, keys
+// (t&7) + 8i of the block (i < 8); the k block's float4 c of row j sits at
+// j*32 + (c ^ (j & 7)) so the 8 lanes of a quarter-warp read 8 bank groups.
+// p·v tiles: thread t takes questions 4(t>>6) .. +3 and columns 2(t&63), +1.
 // ---------------------------------------------------------------------------
+constexpr int kXaChunk = 16;
+constexpr int kXaBlock = 64;
+constexpr int kXaThreads = 256;
+constexpr int kXaRows = kXaChunk * KC_HEADS;
+// k block f32 [kXaBlock][128] | q f64 [kXaChunk][128] | exponentials f64 [kXaRows][kXaBlock] | p f32 [kXaRows][kXaBlock]
+constexpr size_t kXaSmem = size_t(kXaBlock) * KC_H * 4 + size_t(kXaChunk) * KC_H * 8 +
+                           size_t(kXaRows) * kXaBlock * 8 + size_t(kXaRows) * kXaBlock * 4;
+
 struct CrossAttnArgs {
   const float* mq;          // [Q,128]
   const float* mk;          // [R,128]
   const float* mv;          // [R,128]
   float* query;             // [Q,128], updated in place
-  const uint32_t* query_frame;
-  const uint64_t* r_off;
-  uint32_t max_r;
+  const uint64_t* q_off;    // [frames + 1]
+  const uint64_t* r_off;    // [frames + 1]
+  int chunks;               // CTAs per frame: ceil(largest question count / kXaChunk)
   double scale;             // 1/sqrt(headDim)
   float* p_out;             // optional [4][sum Q_f R_f]: head h of question i at h*P + p_off[f] + il*R + j
-  const uint64_t* q_off;
   const uint64_t* p_off;
   uint64_t total_p;
 };
 
-__global__ void __launch_bounds__(128) k_cross_attn_exact(CrossAttnArgs a) {
+__global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArgs a) {
   extern __shared__ __align__(16) unsigned char dyn[];
-  __shared__ float qs[KC_H];
-  __shared__ double sums[KC_HEADS];
-  const uint32_t qi = blockIdx.x;
-  const uint32_t f = a.query_frame[qi];
-  const uint64_t rb = a.r_off[f];
-  const int R = int(a.r_off[f + 1] - rb);
-  double* e64 = reinterpret_cast<double*>(dyn);                  // [4][max_r]
-  float* sc = reinterpret_cast<float*>(e64 + 4 * size_t(a.max_r)); // [4][max_r]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  qs[tid] = a.mq[uint64_t(qi) * KC_H + tid];
-  __syncthreads();
-  // scores: thread handles (j, head) pairs; one f64 accumulator over d
-  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
-    const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
-    const float* kr = a.mk + (rb + j) * KC_H + hb;
-    double s = 0.0;
-#pragma unroll 8
-    for (int d = 0; d < KC_HEAD_DIM; d++) s = fma(double(qs[hb + d]), double(kr[d]), s);
-    sc[head * a.max_r + j] = f32(s * a.scale + 0.0);
-  }
-  __syncthreads();
-  // per head (warp w = head w): all-blocked test, max, exponentials
-  {
-    const int head = warp;
-    float* row = sc + head * a.max_r;
-    bool any_open = false;
-    double mx = -INFINITY;
-    for (int j = lane; j < R; j += 32) {
-      any_open |= double(row[j]) >= -1e29;
-      mx = js_max(mx, double(row[j]));
+  float4* ks = reinterpret_cast<float4*>(dyn);
+  double* qd = reinterpret_cast<double*>(dyn + size_t(kXaBlock) * KC_H * 4);
+  double* e64 = qd + kXaChunk * KC_H;
+  float* pf = reinterpret_cast<float*>(e64 + kXaRows * kXaBlock);
+  __shared__ double row_mx[kXaRows], row_inv[kXaRows];
+  __shared__ int row_open[kXaRows];
+  const uint32_t f = blockIdx.x / a.chunks;
+  const int q0 = int(blockIdx.x % a.chunks) * kXaChunk;
+  const uint64_t qb = a.q_off[f], rb = a.r_off[f];
+  const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
+  if (q0 >= nq) return;
+  const int nc = min(kXaChunk, nq - q0);
+  const int tid = threadIdx.x;
+  for (int i = tid; i < kXaChunk * KC_H; i += kXaThreads)
+    qd[i] = i < nc * KC_H ? double(a.mq[(qb + q0) * KC_H + i]) : 0.0;
+  const int nblk = (R + kXaBlock - 1) / kXaBlock;
+  const float4* mk4 = reinterpret_cast<const float4*>(a.mk + rb * KC_H);
+  auto stage = [&](int j0) {  // k rows [j0, j0 + block) into the block buffer
+    const int nb = min(kXaBlock, R - j0);
+    for (int i = tid; i < nb * 32; i += kXaThreads) {
+      const int j = i >> 5, c4 = i & 31;
+      cp_async16(ks + j * 32 + (c4 ^ (j & 7)), mk4 + size_t(j0 + j) * 32 + c4);
     }
-    any_open = __any_sync(0xffffffffu, any_open);
-    for (int o = 16; o; o >>= 1) mx = js_max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (any_open) {
-      double* er = e64 + head * size_t(a.max_r);
-      for (int j = lane; j < R; j += 32) {
-        const double e = exp(double(row[j]) - mx);
-        er[j] = e;
-        row[j] = f32(e);
+  };
+  auto staged = [&]() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+  };
+
+  const int s_head = tid >> 6, s_q = ((tid >> 3) & 7) * 2, s_k = tid & 7;
+  // the tile's scores of the staged block (keys past its end are never used)
+  auto scores = [&](float (&sf)[2][8]) {
+    double acc[2][8];
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+#pragma unroll
+      for (int i = 0; i < 8; i++) acc[c][i] = 0.0;
+    const double* qp = qd + s_q * KC_H + s_head * KC_HEAD_DIM;
+#pragma unroll 2
+    for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+      float4 k4[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int j = s_k + 8 * i;
+        k4[i] = ks[j * 32 + ((s_head * 8 + d4) ^ (j & 7))];
       }
-      __syncwarp();
-      if (lane == 0) {  // softmaxRow's running sum, in index order
-        double sum = 0.0;
-        for (int j = 0; j < R; j++) sum += er[j];
-        sums[head] = 1.0 / js_max(sum, 1e-20);
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        const double2 qa = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4);
+        const double2 qc = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4 + 2);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          acc[c][i] = fma(qa.x, double(k4[i].x), acc[c][i]);
+          acc[c][i] = fma(qa.y, double(k4[i].y), acc[c][i]);
+          acc[c][i] = fma(qc.x, double(k4[i].z), acc[c][i]);
+          acc[c][i] = fma(qc.y, double(k4[i].w), acc[c][i]);
+        }
       }
-      __syncwarp();
-      const double inv = sums[head];
-      for (int j = lane; j < R; j += 32) row[j] = f32(double(row[j]) * inv);
-    } else {
-      for (int j = lane; j < R; j += 32) row[j] = 0.0f;
     }
-    if (a.p_out) {
-      float* po = a.p_out + uint64_t(head) * a.total_p + a.p_off[f] + (qi - a.q_off[f]) * uint64_t(R);
-      for (int j = lane; j < R; j += 32) po[j] = row[j];
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+#pragma unroll
+      for (int i = 0; i < 8; i++) sf[c][i] = f32(acc[c][i] * a.scale + 0.0);
+  };
+  const int row0 = s_q * KC_HEADS + s_head;  // the tile's rows: row0 and row0 + 4
+
+  // (1) row maxima and the all-blocked test
+  {
+    double m[2] = {-INFINITY, -INFINITY};
+    bool open[2] = {false, false};
+    if (nblk > 0) stage(0);
+    for (int b = 0; b < nblk; b++) {
+      const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
+      staged();
+      float sf[2][8];
+      scores(sf);
+      __syncthreads();
+      if (b + 1 < nblk) stage(j0 + kXaBlock);
+#pragma unroll
+      for (int c = 0; c < 2; c++)
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          if (s_k + 8 * i < nb) {
+            m[c] = js_max(m[c], double(sf[c][i]));
+            open[c] |= double(sf[c][i]) >= -1e29;
+          }
+    }
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      for (int o = 1; o < 8; o <<= 1) {
+        m[c] = js_max(m[c], __shfl_xor_sync(0xffffffffu, m[c], o));
+        open[c] |= __shfl_xor_sync(0xffffffffu, int(open[c]), o) != 0;
+      }
+      if (s_k == 0) {
+        row_mx[row0 + 4 * c] = m[c];
+        row_open[row0 + 4 * c] = open[c];
+      }
     }
   }
   __syncthreads();
-  // P·V: thread (head, d), one f64 accumulator over j in order
+  const double mx0 = row_mx[row0], mx1 = row_mx[row0 + 4];
+  const bool op0 = row_open[row0] != 0, op1 = row_open[row0 + 4] != 0;
+
+  // (2) exponentials; thread r < kXaRows adds row r's in index order
   {
-    const int head = tid >> 5, d = tid & 31, col = head * KC_HEAD_DIM + d;
-    const float* row = sc + head * a.max_r;
-    double v = 0.0;
-    for (int j = 0; j < R; j++) v = fma(double(row[j]), double(a.mv[(rb + j) * KC_H + col]), v);
-    float* qp = a.query + uint64_t(qi) * KC_H + col;
-    *qp = f32(double(*qp) + double(f32(v)));
+    double sum = 0.0;
+    const bool summer = tid < kXaRows && row_open[tid] != 0;
+    if (nblk > 0) stage(0);
+    for (int b = 0; b < nblk; b++) {
+      const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
+      staged();
+      float sf[2][8];
+      scores(sf);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int j = s_k + 8 * i;
+        if (j < nb) {
+          if (op0) e64[row0 * kXaBlock + j] = exp(double(sf[0][i]) - mx0);
+          if (op1) e64[(row0 + 4) * kXaBlock + j] = exp(double(sf[1][i]) - mx1);
+        }
+      }
+      __syncthreads();
+      if (b + 1 < nblk) stage(j0 + kXaBlock);
+      if (summer)
+        for (int j = 0; j < nb; j++) sum += e64[tid * kXaBlock + j];
+    }
+    if (tid < kXaRows) row_inv[tid] = 1.0 / js_max(sum, 1e-20);
   }
+  __syncthreads();
+  const double inv0 = row_inv[row0], inv1 = row_inv[row0 + 4];
+
+  // (3) p, then p·v
+  const int v_q = (tid >> 6) * 4, v_col = (tid & 63) * 2, v_head = (tid & 63) >> 4;
+  double acc[4][2];
+#pragma unroll
+  for (int c = 0; c < 4; c++) acc[c][0] = acc[c][1] = 0.0;
+  if (nblk > 0) stage(0);
+  for (int b = 0; b < nblk; b++) {
+    const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
+    staged();
+    {
+      float sf[2][8];
+      scores(sf);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int j = s_k + 8 * i;
+        if (j < nb) {
+          const float p0 = op0 ? f32(double(f32(exp(double(sf[0][i]) - mx0))) * inv0) : 0.0f;
+          const float p1 = op1 ? f32(double(f32(exp(double(sf[1][i]) - mx1))) * inv1) : 0.0f;
+          pf[row0 * kXaBlock + j] = p0;
+          pf[(row0 + 4) * kXaBlock + j] = p1;
+          if (a.p_out) {
+            const uint64_t base = uint64_t(s_head) * a.total_p + a.p_off[f] + uint64_t(j0 + j);
+            if (s_q < nc) a.p_out[base + uint64_t(q0 + s_q) * R] = p0;
+            if (s_q + 1 < nc) a.p_out[base + uint64_t(q0 + s_q + 1) * R] = p1;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (b + 1 < nblk) stage(j0 + kXaBlock);
+    if (v_q < nc) {
+      const float* pr = pf + (v_q * KC_HEADS + v_head) * kXaBlock;
+      const float* vr = a.mv + (rb + j0) * KC_H + v_col;
+      int j = 0;
+      for (; j + 4 <= nb; j += 4) {
+        float2 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = *reinterpret_cast<const float2*>(vr + size_t(j + u) * KC_H);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float4 p4 = *reinterpret_cast<const float4*>(pr + c * KC_HEADS * kXaBlock + j);
+          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            acc[c][0] = fma(double(pv[u]), double(v[u].x), acc[c][0]);
+            acc[c][1] = fma(double(pv[u]), double(v[u].y), acc[c][1]);
+          }
+        }
+      }
+      for (; j < nb; j++) {
+        const float2 v = *reinterpret_cast<const float2*>(vr + size_t(j) * KC_H);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const double pj = double(pr[c * KC_HEADS * kXaBlock + j]);
+          acc[c][0] = fma(pj, double(v.x), acc[c][0]);
+          acc[c][1] = fma(pj, double(v.y), acc[c][1]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+    if (v_q + c < nc) {
+      float* qp = a.query + (qb + q0 + v_q + c) * KC_H + v_col;
+      qp[0] = f32(double(qp[0]) + double(f32(acc[c][0])));
+      qp[1] = f32(double(qp[1]) + double(f32(acc[c][1])));
+    }
 }
 
 // ---------------------------------------------------------------------------

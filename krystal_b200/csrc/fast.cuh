@@ -244,17 +244,39 @@ __global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
 
 // ---------------------------------------------------------------------------
 // Mixer cross-attention + residual, f32 (oracle.ts:292-293 with the open
-// mixer mask). One CTA per chunk of up to kCaChunk questions of a frame (as
-// many as the score buffer holds), the chunks of a frame adjacent in the grid
-// so they share the bank in L2; each bank row's k and v slices are loaded
-// once per chunk. Per (question, head): score j = the 32-long fmaf chain
-// q·k_j in dimension order, scaled; softmax with lane-strided max and sum
-// (lane l takes j = l, l+32, ...) reduced by an xor-shuffle tree; output =
-// (sum over even j of p_j v_j + sum over odd j of p_j v_j) / sum, added to
-// the question row.
+// mixer mask). One CTA per chunk of up to kCaChunk questions of a frame, the
+// chunks of a frame adjacent in the grid so they share the bank in L2. The
+// bank is streamed through shared memory in blocks of up to kCaBlock keys, so
+// the chunk does not depend on the bank's length (a 4096-key bank is read by
+// 4 CTAs per frame, not 64).
+//
+// Per (question, head): score j = the 32-long fmaf chain q·k_j in dimension
+// order, scaled; softmax max and sum with lane l taking j = l, l+32, ... in
+// key order, reduced by an xor-shuffle tree; output = (sum over even j of
+// e_j v_j + sum over odd j of e_j v_j) / sum, each sum in key order, added to
+// the question row. With more than one block, a first pass computes the
+// scores for the row maxima only (a max does not depend on the order) and the
+// second computes them again, identically, for the exponentials, the sums and
+// p·v; every sum keeps its key order across the blocks (blocks start at
+// multiples of 32 keys), so the result depends on neither the block size nor
+// the thread tiling.
+//
+// Register tiles, so that each operand fetched from shared memory feeds
+// several chains: a score thread holds 8 questions x 4 keys of one head (the
+// warp: one head, 8 questions, 128 keys), a p·v thread 4 questions x 4
+// columns of one key parity (the warp: 4 questions, all 128 columns).
+//
+// Shared memory: the k block, row j's float4 c at j*32 + (c ^ (j & 7)) (the
+// score warp's lanes read 8 consecutive rows per quarter: 8 bank groups);
+// the scores, row (question c, head) at (c*4 + head)*stride, key jj at
+// (jj&1)*half + (jj>>1), so that a p·v chain reads four keys of its parity
+// per float4 (half = 16 mod 32 keeps the score writes and the softmax reads
+// free of bank conflicts); the chunk's question rows.
 // ---------------------------------------------------------------------------
-constexpr int kCaChunk = 8;
+constexpr int kCaChunk = 16;
+constexpr int kCaBlock = 128;
 constexpr int kCaThreads = 256;
+constexpr int kCaRowsPerWarp = kCaChunk * KC_HEADS / (kCaThreads / 32);
 
 struct CrossAttnFrameArgs {
   const float* mq;
@@ -263,113 +285,212 @@ struct CrossAttnFrameArgs {
   float* query;
   const uint64_t* q_off;   // [frames + 1]
   const uint64_t* r_off;   // [frames + 1]
-  int qc;                  // questions per chunk (the score buffer holds qc x 4 x max_r)
-  int chunks;              // CTAs per frame: ceil(largest question count / qc)
-  uint32_t max_r;
+  int chunks;              // CTAs per frame: ceil(largest question count / kCaChunk)
+  int kb;                  // keys per block: a multiple of 32, at most kCaBlock
+  int half;                // the parity half's length in a score row (16 mod 32, >= kb/2)
   float scale;
 };
 
-__global__ void __launch_bounds__(kCaThreads, 3) k_cross_attn_frame(CrossAttnFrameArgs a) {
-  extern __shared__ __align__(16) float caf_smem[];  // scores [qc][4][max_r], then q [qc][128]
+__global__ void __launch_bounds__(kCaThreads, 2) k_cross_attn_frame(CrossAttnFrameArgs a) {
+  extern __shared__ __align__(16) float4 caf_smem4[];  // k block [kCaBlock*32], scores, q [kCaChunk][32]
   __shared__ float inv_s[kCaChunk][KC_HEADS];
   const uint32_t f = blockIdx.x / a.chunks;
-  const int q0 = int(blockIdx.x % a.chunks) * a.qc;
+  const int q0 = int(blockIdx.x % a.chunks) * kCaChunk;
   const uint64_t qb = a.q_off[f], rb = a.r_off[f];
   const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
   if (q0 >= nq) return;
-  float* sc = caf_smem;
-  float* qs = caf_smem + size_t(a.qc) * KC_HEADS * a.max_r;
+  const int stride = 2 * a.half;
+  float4* ks = caf_smem4;
+  float* sc = reinterpret_cast<float*>(caf_smem4 + kCaBlock * 32);
+  float* qs = sc + kCaChunk * KC_HEADS * stride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  {
-    const int nc = min(a.qc, nq - q0);
-    for (int i = tid; i < nc * KC_H; i += kCaThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
-    __syncthreads();
-    // scores: one (head, key) per thread, head-major so a warp reads one q
-    // slice (a broadcast); the k slice is loaded once for the chunk, and the
-    // chunk's questions run as independent chains
-    for (int idx = tid; idx < R * KC_HEADS; idx += kCaThreads) {
-      const int head = idx / R, j = idx - head * R, hb = head * KC_HEAD_DIM;
-      const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
-      float4 k4[KC_HEAD_DIM / 4];
-#pragma unroll
-      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) k4[d4] = kr[d4];
-      float sv[kCaChunk];
-#pragma unroll
-      for (int c = 0; c < kCaChunk; c++) sv[c] = 0.f;
-#pragma unroll
-      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++)
-#pragma unroll
-        for (int c = 0; c < kCaChunk; c++)
-          if (c < nc) {
-            const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
-            sv[c] = fmaf(q4.x, k4[d4].x, sv[c]);
-            sv[c] = fmaf(q4.y, k4[d4].y, sv[c]);
-            sv[c] = fmaf(q4.z, k4[d4].z, sv[c]);
-            sv[c] = fmaf(q4.w, k4[d4].w, sv[c]);
-          }
-#pragma unroll
-      for (int c = 0; c < kCaChunk; c++)
-        if (c < nc) sc[(c * KC_HEADS + head) * a.max_r + j] = sv[c] * a.scale;
+  const int nc = min(kCaChunk, nq - q0);
+  const int nblk = (R + a.kb - 1) / a.kb;
+  for (int i = tid; i < kCaChunk * KC_H; i += kCaThreads) qs[i] = i < nc * KC_H ? a.mq[(qb + q0) * KC_H + i] : 0.f;
+  const float4* mk4 = reinterpret_cast<const float4*>(a.mk + rb * KC_H);
+  auto stage = [&](int j0, int nb) {  // k rows [j0, j0 + nb) into the block buffer
+    for (int i = tid; i < nb * 32; i += kCaThreads) {
+      const int j = i >> 5, c4 = i & 31;
+      cp_async16(ks + j * 32 + (c4 ^ (j & 7)), mk4 + size_t(j0 + j) * 32 + c4);
     }
+  };
+  auto staged = [&]() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    // softmax rows (question, head): one warp each
-    for (int rw = warp; rw < nc * KC_HEADS; rw += kCaThreads / 32) {
-      float* row = sc + size_t(rw) * a.max_r;
-      float mx = -INFINITY;
-      for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float sum = 0.f;
-      for (int j = lane; j < R; j += 32) {
-        const float e = expf(row[j] - mx);
-        row[j] = e;
-        sum += e;
+  };
+
+  // scores of the staged block: warp w takes head w/2 and questions
+  // 8*(w&1) .. +7 (skipped when the chunk has none of them); lane l the keys
+  // l, l+32, l+64, l+96 of the block
+  const int s_head = warp >> 1, s_c0 = (warp & 1) * 8;
+  auto scores = [&](int nb) {
+    if (s_c0 >= nc) return;
+    float acc[8][4];
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+#pragma unroll
+      for (int t = 0; t < 4; t++) acc[c][t] = 0.f;
+    const float4* q4p = reinterpret_cast<const float4*>(qs) + s_c0 * 32 + s_head * 8;
+#pragma unroll 2
+    for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+      float4 k4[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const int j = lane + 32 * t;
+        k4[t] = ks[j * 32 + ((s_head * 8 + d4) ^ (j & 7))];
       }
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) inv_s[rw >> 2][rw & 3] = 1.f / fmaxf(sum, 1e-20f);
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        const float4 q = q4p[c * 32 + d4];
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          acc[c][t] = fmaf(q.x, k4[t].x, acc[c][t]);
+          acc[c][t] = fmaf(q.y, k4[t].y, acc[c][t]);
+          acc[c][t] = fmaf(q.z, k4[t].z, acc[c][t]);
+          acc[c][t] = fmaf(q.w, k4[t].w, acc[c][t]);
+        }
+      }
     }
-    __syncthreads();
-    // p·v per output column: threads 0-127 form the sum over the even keys and
-    // threads 128-255 the sum over the odd keys (each in key order, every
-    // question of the chunk at once, each v element loaded once for them);
-    // the output adds the two, as the one-question-at-a-time form does
-    {
-      const int col = tid & (KC_H - 1), head = col >> 5, par = tid >> 7;
-      float acc[kCaChunk];
 #pragma unroll
-      for (int c = 0; c < kCaChunk; c++) acc[c] = 0.f;
-      const float* vcol = a.mv + rb * KC_H + col;
-      int j = par;
-      for (; j + 62 < R; j += 64) {  // 32 keys of this parity in flight per step
-        float vv[32];
+    for (int t = 0; t < 4; t++) {
+      const int jj = lane + 32 * t;
+      if (jj < nb) {
+        const int pos = (jj & 1) * a.half + (jj >> 1);
 #pragma unroll
-        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + 2 * e) * KC_H];
-#pragma unroll
-        for (int c = 0; c < kCaChunk; c++)
-          if (c < nc) {
-            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
-#pragma unroll
-            for (int e = 0; e < 32; e++) acc[c] = fmaf(row[2 * e], vv[e], acc[c]);
-          }
+        for (int c = 0; c < 8; c++)
+          if (s_c0 + c < nc) sc[((s_c0 + c) * KC_HEADS + s_head) * stride + pos] = acc[c][t] * a.scale;
       }
-      for (; j < R; j += 2) {
-        const float va = vcol[size_t(j) * KC_H];
-#pragma unroll
-        for (int c = 0; c < kCaChunk; c++)
-          if (c < nc) acc[c] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, acc[c]);
-      }
-      // the odd sums meet the even ones in the (now free) question buffer
-      if (par == 1)
-#pragma unroll
-        for (int c = 0; c < kCaChunk; c++)
-          if (c < nc) qs[c * KC_H + col] = acc[c];
-      __syncthreads();
-      if (par == 0)
-#pragma unroll
-        for (int c = 0; c < kCaChunk; c++)
-          if (c < nc) a.query[(qb + q0 + c) * KC_H + col] += (acc[c] + qs[c * KC_H + col]) * inv_s[c][head];
     }
-    __syncthreads();
+  };
+  auto at = [&](int rw, int jj) -> float& { return sc[rw * stride + (jj & 1) * a.half + (jj >> 1)]; };
+
+  // rows (question, head) rw = warp + 8r belong to one warp for the whole kernel
+  float mx[kCaRowsPerWarp], sum[kCaRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kCaRowsPerWarp; r++) {
+    mx[r] = -INFINITY;
+    sum[r] = 0.f;
   }
+  auto row_max = [&](int nb) {
+#pragma unroll
+    for (int r = 0; r < kCaRowsPerWarp; r++) {
+      const int rw = warp + r * (kCaThreads / 32);
+      if (rw < nc * KC_HEADS)
+        for (int jj = lane; jj < nb; jj += 32) mx[r] = fmaxf(mx[r], at(rw, jj));
+    }
+  };
+  auto reduce_max = [&]() {
+#pragma unroll
+    for (int r = 0; r < kCaRowsPerWarp; r++)
+      for (int o = 16; o; o >>= 1) mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], o));
+  };
+  if (nblk > 1) {
+    stage(0, min(a.kb, R));
+    for (int b = 0; b < nblk; b++) {
+      const int j0 = b * a.kb, nb = min(a.kb, R - j0);
+      staged();
+      scores(nb);
+      __syncthreads();
+      if (b + 1 < nblk) stage(j0 + a.kb, min(a.kb, R - j0 - a.kb));
+      row_max(nb);
+    }
+    reduce_max();
+  }
+
+  // p·v: warp w takes questions 4*(w&3) .. +3 and key parity w>>2 (skipped
+  // when the chunk has none of those questions); lane l columns 4l .. 4l+3
+  const int v_c0 = (warp & 3) * 4, par = warp >> 2, col0 = lane * 4, v_head = lane >> 3;
+  float acc[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[c][i] = 0.f;
+  if (nblk > 0) stage(0, min(a.kb, R));
+  for (int b = 0; b < nblk; b++) {
+    const int j0 = b * a.kb, nb = min(a.kb, R - j0);
+    staged();
+    scores(nb);
+    __syncthreads();
+    if (b + 1 < nblk) stage(j0 + a.kb, min(a.kb, R - j0 - a.kb));
+    if (nblk == 1) {
+      row_max(nb);
+      reduce_max();
+    }
+#pragma unroll
+    for (int r = 0; r < kCaRowsPerWarp; r++) {
+      const int rw = warp + r * (kCaThreads / 32);
+      if (rw < nc * KC_HEADS)
+        for (int jj = lane; jj < nb; jj += 32) {
+          float& s = at(rw, jj);
+          const float e = expf(s - mx[r]);
+          s = e;
+          sum[r] += e;
+        }
+    }
+    __syncthreads();
+    if (v_c0 < nc) {
+      const int npar = (nb - par + 1) >> 1;
+      const float4* vp = reinterpret_cast<const float4*>(a.mv + (rb + j0 + par) * KC_H + col0);
+      const float* srow = sc + v_head * stride + par * a.half;
+      int e = 0;
+      for (; e + 8 <= npar; e += 8) {  // 8 keys of this parity in flight per step
+        float4 vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) vv[u] = vp[size_t(e + u) * (2 * KC_H / 4)];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float4* s4 = reinterpret_cast<const float4*>(srow + (v_c0 + c) * KC_HEADS * stride + e);
+          const float4 sa = s4[0], sb = s4[1];
+          const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            acc[c][0] = fmaf(sv[u], vv[u].x, acc[c][0]);
+            acc[c][1] = fmaf(sv[u], vv[u].y, acc[c][1]);
+            acc[c][2] = fmaf(sv[u], vv[u].z, acc[c][2]);
+            acc[c][3] = fmaf(sv[u], vv[u].w, acc[c][3]);
+          }
+        }
+      }
+      for (; e < npar; e++) {
+        const float4 v = vp[size_t(e) * (2 * KC_H / 4)];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float s = srow[(v_c0 + c) * KC_HEADS * stride + e];
+          acc[c][0] = fmaf(s, v.x, acc[c][0]);
+          acc[c][1] = fmaf(s, v.y, acc[c][1]);
+          acc[c][2] = fmaf(s, v.z, acc[c][2]);
+          acc[c][3] = fmaf(s, v.w, acc[c][3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kCaRowsPerWarp; r++) {
+    const int rw = warp + r * (kCaThreads / 32);
+    for (int o = 16; o; o >>= 1) sum[r] += __shfl_xor_sync(0xffffffffu, sum[r], o);
+    if (lane == 0 && rw < nc * KC_HEADS) inv_s[rw >> 2][rw & 3] = 1.f / fmaxf(sum[r], 1e-20f);
+  }
+  __syncthreads();  // the last block's p·v has read the scores; the q rows are free
+  // the odd sums meet the even ones in the question buffer
+  if (par == 1 && v_c0 < nc)
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      reinterpret_cast<float4*>(qs)[(v_c0 + c) * 32 + lane] = make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+  __syncthreads();
+  if (par == 0)
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      if (v_c0 + c < nc) {
+        const float4 o = reinterpret_cast<const float4*>(qs)[(v_c0 + c) * 32 + lane];
+        const float is = inv_s[v_c0 + c][v_head];
+        float4* dst = reinterpret_cast<float4*>(a.query + (qb + q0 + v_c0 + c) * KC_H) + lane;
+        float4 y = *dst;
+        y.x += (acc[c][0] + o.x) * is;
+        y.y += (acc[c][1] + o.y) * is;
+        y.z += (acc[c][2] + o.z) * is;
+        y.w += (acc[c][3] + o.w) * is;
+        *dst = y;
+      }
 }
 
 // ---------------------------------------------------------------------------

@@ -451,15 +451,20 @@ kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
   return KC_OK;
 }
 
-// The per-frame cross attention's question chunk for a batch whose largest
-// bank is max_r rows (its score buffer stays within 96 KB), and its shared memory.
-int cross_chunk(uint32_t max_r) {
-  const uint64_t fit = (96u << 10) / (uint64_t(KC_HEADS) * 4 * std::max<uint32_t>(max_r, 1));
-  return int(std::min<uint64_t>(std::max<uint64_t>(fit, 1), kc::kCaChunk));
-}
-size_t cross_smem(uint32_t max_r) {
-  const int qc = cross_chunk(max_r);
-  return size_t(qc) * KC_HEADS * std::max<uint32_t>(max_r, 1) * 4 + size_t(qc) * KC_H * 4;
+// The per-frame cross attention's key block for a batch whose largest bank
+// is max_r rows (a multiple of 32, at most kCaBlock), the length of a score
+// row's parity half (16 mod 32, at least half the block), and its shared
+// memory (the k block buffer, the scores, the question rows).
+struct CrossShape {
+  int kb, half;
+  size_t smem;
+};
+CrossShape cross_shape(uint32_t max_r) {
+  const int kb = int(std::min<uint32_t>(kc::kCaBlock, (std::max<uint32_t>(max_r, 1) + 31) / 32 * 32));
+  const int half = (kb / 2 + 31) / 32 * 32 + 16;
+  return {kb, half,
+          size_t(kc::kCaBlock) * KC_H * 4 + size_t(kc::kCaChunk) * KC_HEADS * 2 * half * 4 +
+              size_t(kc::kCaChunk) * KC_H * 4};
 }
 
 // The same for the per-frame selector (scores [qc][max_r], then q [qc][128]).
@@ -732,11 +737,11 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, m0, W, H, mq, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, m0 + 1, W + uint64_t(H) * H, H, mk, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bv), H, R, m0 + 2, W + 2ull * H * H, H, mv, H, H));
-      kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint32_t>(ws.query_frame), P<uint64_t>(ws.r_off),
-                           tot.max_r, attn_scale, sv ? sv->mix_p + blk * 4 * tot.p : nullptr,
-                           P<uint64_t>(ws.q_off), P<uint64_t>(ws.p_off), tot.p};
-      const size_t smem = size_t(tot.max_r) * 4 * (8 + 4);
-      kc::k_cross_attn_exact<<<unsigned(Q), 128, smem, h->stream>>>(ca);
+      const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kXaChunk - 1) / kc::kXaChunk);
+      kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+                           chunks, attn_scale, sv ? sv->mix_p + blk * 4 * tot.p : nullptr,
+                           P<uint64_t>(ws.p_off), tot.p};
+      kc::k_cross_attn_exact<<<b.frames * unsigned(chunks), kc::kXaThreads, kc::kXaSmem, h->stream>>>(ca);
       h->launches++;
       KC_CHECK(gemm<kc::kEpiRelu>(h, tc, P<float>(ws.qstate), H, Q, m0 + 3, w1, H, mh, FF, H));
       KC_CHECK(gemm<kc::kEpiResid>(h, tc, mh, FF, Q, m0 + 4, w2, FF, P<float>(ws.qstate), H, FF));
@@ -841,10 +846,12 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
-      const int qc = cross_chunk(tot.max_r), chunks = int((std::max<uint32_t>(tot.max_q, 1) + qc - 1) / qc);
-      kc::CrossAttnFrameArgs ca{P<float>(ws.mq), P<float>(ws.mk), P<float>(ws.mv), P<float>(ws.qstate),
-                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), qc, chunks, tot.max_r, attn_scale};
-      kc::k_cross_attn_frame<<<b.frames * unsigned(chunks), kc::kCaThreads, cross_smem(tot.max_r), h->stream>>>(ca);
+      const CrossShape cs = cross_shape(tot.max_r);
+      const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCaChunk - 1) / kc::kCaChunk);
+      kc::CrossAttnFrameArgs ca{P<float>(ws.mq),     P<float>(ws.mk),         P<float>(ws.mv), P<float>(ws.qstate),
+                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), chunks,          cs.kb,
+                                cs.half,              attn_scale};
+      kc::k_cross_attn_frame<<<b.frames * unsigned(chunks), kc::kCaThreads, cs.smem, h->stream>>>(ca);
       h->launches++;
       KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, P<float>(ws.qstate), Q, m0 + 3, P<float>(ws.mh)));
       KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, P<float>(ws.mh), Q, m0 + 4, P<float>(ws.qstate)));
@@ -1435,12 +1442,12 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_frame, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (96 << 10) + kc::kCaChunk * KC_H * 4)) ||
+                                int(cross_shape(kc::kCaBlock).smem))) ||
       (e = cudaFuncSetAttribute(kc::k_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (96 << 10) + kc::kSelChunk * KC_H * 4)))
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(KC_MAX_BANK) * 4 * (8 + 4)))) return bail(e, "smem");
+                                int(kc::kXaSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * (8 + 4)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_back_q, cudaFuncAttributeMaxDynamicSharedMemorySize,
