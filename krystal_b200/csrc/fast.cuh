@@ -494,6 +494,136 @@ __global__ void __launch_bounds__(kCaThreads, 2) k_cross_attn_frame(CrossAttnFra
 }
 
 // ---------------------------------------------------------------------------
+// Mixer cross-attention for banks of at most kCsMaxBank keys: the same
+// arithmetic as k_cross_attn_frame (bit for bit) in one pass, the chunk's
+// scores for the whole bank held in shared memory, so that small frames need
+// neither the key-block staging nor the second score pass. One CTA per chunk
+// of up to kCsChunk questions (as many as the score buffer holds); each bank
+// row's k and v slices are loaded once per chunk; p·v per output column, the
+// even keys' sum on threads 0-127 and the odd keys' on 128-255, each in key
+// order, every question of the chunk at once.
+// ---------------------------------------------------------------------------
+constexpr int kCsMaxBank = 256;
+constexpr int kCsChunk = 8;
+constexpr int kCsThreads = 256;
+
+struct CrossAttnSmallArgs {
+  const float* mq;
+  const float* mk;
+  const float* mv;
+  float* query;
+  const uint64_t* q_off;   // [frames + 1]
+  const uint64_t* r_off;   // [frames + 1]
+  int qc;                  // questions per chunk (the score buffer holds qc x 4 x max_r)
+  int chunks;              // CTAs per frame: ceil(largest question count / qc)
+  uint32_t max_r;
+  float scale;
+};
+
+__global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSmallArgs a) {
+  extern __shared__ __align__(16) float cas_smem[];  // scores [qc][4][max_r], then q [qc][128]
+  __shared__ float inv_s[kCsChunk][KC_HEADS];
+  const uint32_t f = blockIdx.x / a.chunks;
+  const int q0 = int(blockIdx.x % a.chunks) * a.qc;
+  const uint64_t qb = a.q_off[f], rb = a.r_off[f];
+  const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
+  if (q0 >= nq) return;
+  float* sc = cas_smem;
+  float* qs = cas_smem + size_t(a.qc) * KC_HEADS * a.max_r;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  {
+    const int nc = min(a.qc, nq - q0);
+    for (int i = tid; i < nc * KC_H; i += kCsThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
+    __syncthreads();
+    // scores: one (head, key) per thread, head-major so a warp reads one q
+    // slice (a broadcast); the k slice is loaded once for the chunk, and the
+    // chunk's questions run as independent chains
+    for (int idx = tid; idx < R * KC_HEADS; idx += kCsThreads) {
+      const int head = idx / R, j = idx - head * R, hb = head * KC_HEAD_DIM;
+      const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
+      float4 k4[KC_HEAD_DIM / 4];
+#pragma unroll
+      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) k4[d4] = kr[d4];
+      float sv[kCsChunk];
+#pragma unroll
+      for (int c = 0; c < kCsChunk; c++) sv[c] = 0.f;
+#pragma unroll
+      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++)
+#pragma unroll
+        for (int c = 0; c < kCsChunk; c++)
+          if (c < nc) {
+            const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
+            sv[c] = fmaf(q4.x, k4[d4].x, sv[c]);
+            sv[c] = fmaf(q4.y, k4[d4].y, sv[c]);
+            sv[c] = fmaf(q4.z, k4[d4].z, sv[c]);
+            sv[c] = fmaf(q4.w, k4[d4].w, sv[c]);
+          }
+#pragma unroll
+      for (int c = 0; c < kCsChunk; c++)
+        if (c < nc) sc[(c * KC_HEADS + head) * a.max_r + j] = sv[c] * a.scale;
+    }
+    __syncthreads();
+    // softmax rows (question, head): one warp each
+    for (int rw = warp; rw < nc * KC_HEADS; rw += kCsThreads / 32) {
+      float* row = sc + size_t(rw) * a.max_r;
+      float mx = -INFINITY;
+      for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+      for (int j = lane; j < R; j += 32) {
+        const float e = expf(row[j] - mx);
+        row[j] = e;
+        sum += e;
+      }
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) inv_s[rw >> 2][rw & 3] = 1.f / fmaxf(sum, 1e-20f);
+    }
+    __syncthreads();
+    // p·v per output column: threads 0-127 form the sum over the even keys and
+    // threads 128-255 the sum over the odd keys (each in key order, every
+    // question of the chunk at once, each v element loaded once for them);
+    // the output adds the two, as the one-question-at-a-time form does
+    {
+      const int col = tid & (KC_H - 1), head = col >> 5, par = tid >> 7;
+      float acc[kCsChunk];
+#pragma unroll
+      for (int c = 0; c < kCsChunk; c++) acc[c] = 0.f;
+      const float* vcol = a.mv + rb * KC_H + col;
+      int j = par;
+      for (; j + 62 < R; j += 64) {  // 32 keys of this parity in flight per step
+        float vv[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + 2 * e) * KC_H];
+#pragma unroll
+        for (int c = 0; c < kCsChunk; c++)
+          if (c < nc) {
+            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
+#pragma unroll
+            for (int e = 0; e < 32; e++) acc[c] = fmaf(row[2 * e], vv[e], acc[c]);
+          }
+      }
+      for (; j < R; j += 2) {
+        const float va = vcol[size_t(j) * KC_H];
+#pragma unroll
+        for (int c = 0; c < kCsChunk; c++)
+          if (c < nc) acc[c] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, acc[c]);
+      }
+      // the odd sums meet the even ones in the (now free) question buffer
+      if (par == 1)
+#pragma unroll
+        for (int c = 0; c < kCsChunk; c++)
+          if (c < nc) qs[c * KC_H + col] = acc[c];
+      __syncthreads();
+      if (par == 0)
+#pragma unroll
+        for (int c = 0; c < kCsChunk; c++)
+          if (c < nc) a.query[(qb + q0 + c) * KC_H + col] += (acc[c] + qs[c * KC_H + col]) * inv_s[c][head];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Pointer selector, f32, with certification (selectorOracle,
 // forward/oracle.ts:332-382). One CTA of 256 threads per chunk of up to
 // kSelChunk questions of a frame (the chunks of a frame adjacent in the grid,

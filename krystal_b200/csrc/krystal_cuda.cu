@@ -467,6 +467,12 @@ CrossShape cross_shape(uint32_t max_r) {
               size_t(kc::kCaChunk) * KC_H * 4};
 }
 
+// The one-pass cross attention's shared memory (scores [kCsChunk][4][max_r],
+// then q [kCsChunk][128]) for banks of at most kCsMaxBank rows.
+size_t cross_small_smem(uint32_t max_r) {
+  return size_t(kc::kCsChunk) * KC_HEADS * std::max<uint32_t>(max_r, 1) * 4 + size_t(kc::kCsChunk) * KC_H * 4;
+}
+
 // The same for the per-frame selector (scores [qc][max_r], then q [qc][128]).
 int sel_chunk(uint32_t max_r) {
   const uint64_t fit = (96u << 10) / (4ull * std::max<uint32_t>(max_r, 1));
@@ -846,12 +852,23 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
-      const CrossShape cs = cross_shape(tot.max_r);
-      const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCaChunk - 1) / kc::kCaChunk);
-      kc::CrossAttnFrameArgs ca{P<float>(ws.mq),     P<float>(ws.mk),         P<float>(ws.mv), P<float>(ws.qstate),
-                                P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off), chunks,          cs.kb,
-                                cs.half,              attn_scale};
-      kc::k_cross_attn_frame<<<b.frames * unsigned(chunks), kc::kCaThreads, cs.smem, h->stream>>>(ca);
+      if (tot.max_r <= uint32_t(kc::kCsMaxBank)) {  // every bank fits the one-pass kernel's score buffer
+        const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCsChunk - 1) / kc::kCsChunk);
+        kc::CrossAttnSmallArgs ca{P<float>(ws.mq),       P<float>(ws.mk),         P<float>(ws.mv),
+                                  P<float>(ws.qstate),   P<uint64_t>(ws.q_off),   P<uint64_t>(ws.r_off),
+                                  kc::kCsChunk,          chunks,                  std::max<uint32_t>(tot.max_r, 1),
+                                  attn_scale};
+        kc::k_cross_attn_small<<<b.frames * unsigned(chunks), kc::kCsThreads, cross_small_smem(tot.max_r),
+                                 h->stream>>>(ca);
+      } else {
+        const CrossShape cs = cross_shape(tot.max_r);
+        const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCaChunk - 1) / kc::kCaChunk);
+        kc::CrossAttnFrameArgs ca{P<float>(ws.mq),       P<float>(ws.mk),       P<float>(ws.mv),
+                                  P<float>(ws.qstate),   P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+                                  chunks,                cs.kb,                 cs.half,
+                                  attn_scale};
+        kc::k_cross_attn_frame<<<b.frames * unsigned(chunks), kc::kCaThreads, cs.smem, h->stream>>>(ca);
+      }
       h->launches++;
       KC_CHECK(tc_gemm<kc::tc::kEpiRelu>(h, P<float>(ws.qstate), Q, m0 + 3, P<float>(ws.mh)));
       KC_CHECK(tc_gemm<kc::tc::kEpiResid>(h, P<float>(ws.mh), Q, m0 + 4, P<float>(ws.qstate)));
@@ -1443,6 +1460,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_frame, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(cross_shape(kc::kCaBlock).smem))) ||
+      (e = cudaFuncSetAttribute(kc::k_cross_attn_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(cross_small_smem(kc::kCsMaxBank)))) ||
       (e = cudaFuncSetAttribute(kc::k_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (96 << 10) + kc::kSelChunk * KC_H * 4)))
     return bail(e, "smem");
