@@ -711,13 +711,134 @@ struct SelectArgs {
   float* gather;            // [Q,128] or null
 };
 
+// selectorOracle's masked scores (oracle.ts:340-345) for a chunk of up to
+// kXsChunk questions of a frame per CTA, the chunks of a frame adjacent in the
+// grid: score_j = f32(Σ_d fma(q_d, k_jd) · scale + mask_j) with the f64 chain
+// in dimension order, written into the question's p row for k_select_exact
+// to finish. The bank's key rows stream through shared memory in blocks of
+// kXsBlock, each loaded once for the chunk (float4 c of row j at
+// j*32 + (c ^ (j & 7))); warp w takes questions 2w and 2w+1, lane l the keys
+// l and l+32 of the block. The rule mask's reopen-if-none-admitted
+// (host/learn.ts:229) is counted first for each question.
+constexpr int kXsChunk = 16;
+constexpr int kXsBlock = 64;
+constexpr int kXsThreads = 256;
+constexpr size_t kXsSmem = size_t(kXsBlock) * KC_H * 4 + size_t(kXsChunk) * KC_H * 8;
+
+__global__ void __launch_bounds__(kXsThreads) k_select_scores_exact(SelectArgs a, int chunks) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  float4* ks = reinterpret_cast<float4*>(dyn);
+  double* qd = reinterpret_cast<double*>(dyn + size_t(kXsBlock) * KC_H * 4);
+  __shared__ uint32_t s_allow[kXsChunk][9];  // schema words 0-7, band word 8
+  __shared__ uint32_t s_admitted[kXsChunk];
+  __shared__ uint32_t s_rec[kXsBlock];       // the block's keys: schema | band << 16, or ~0 when out of range
+  const uint32_t f = blockIdx.x / chunks;
+  const int q0 = int(blockIdx.x % chunks) * kXsChunk;
+  const uint64_t qb = a.q_off[f], rb = a.r_off[f];
+  const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
+  if (q0 >= nq || R == 0) return;
+  const int nc = min(kXsChunk, nq - q0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kXsChunk * KC_H; i += kXsThreads)
+    qd[i] = i < nc * KC_H ? double(a.sq[(qb + q0) * KC_H + i]) : 0.0;
+  const bool rule = a.mask == nullptr && a.schema_allow != nullptr;
+  auto key_ok = [&](int c, uint32_t sb) {
+    const uint32_t sid = sb & 0xffffu, b = sb >> 16;
+    return sid < 256u && b < 32u && ((s_allow[c][sid >> 5] >> (sid & 31)) & 1u) && ((s_allow[c][8] >> b) & 1u);
+  };
+  auto rec_of = [&](int j) {  // schema | band << 16 of bank row j (ids >= 65536 read as out of range)
+    const uint32_t g = a.bank_rec[rb + j];
+    const uint32_t sid = a.schema_ids[g], b = a.band_ids[g];
+    return (sid < 65536u && b < 65536u) ? (sid | (b << 16)) : 0xffffffffu;
+  };
+  if (rule) {
+    for (int i = tid; i < kXsChunk * 9; i += kXsThreads) {
+      const int c = i / 9, w = i % 9;
+      s_allow[c][w] = c < nc ? (w < 8 ? a.schema_allow[(qb + q0 + c) * 8 + w] : a.band_allow[qb + q0 + c]) : 0u;
+    }
+    if (tid < kXsChunk) s_admitted[tid] = 0;
+    __syncthreads();
+    uint32_t cnt[kXsChunk];
+#pragma unroll
+    for (int c = 0; c < kXsChunk; c++) cnt[c] = 0;
+    for (int j = tid; j < R; j += kXsThreads) {
+      const uint32_t sb = rec_of(j);
+#pragma unroll
+      for (int c = 0; c < kXsChunk; c++) cnt[c] += key_ok(c, sb) ? 1u : 0u;
+    }
+#pragma unroll
+    for (int c = 0; c < kXsChunk; c++)
+      if (c < nc && cnt[c]) atomicAdd(&s_admitted[c], cnt[c]);
+  }
+  const int nblk = (R + kXsBlock - 1) / kXsBlock;
+  const float4* sk4 = reinterpret_cast<const float4*>(a.sk + rb * KC_H);
+  auto stage = [&](int j0) {
+    const int nb = min(kXsBlock, R - j0);
+    for (int i = tid; i < nb * 32; i += kXsThreads) {
+      const int j = i >> 5, c4 = i & 31;
+      cp_async16(ks + j * 32 + (c4 ^ (j & 7)), sk4 + size_t(j0 + j) * 32 + c4);
+    }
+  };
+  const int c0 = warp * 2;
+  stage(0);
+  for (int b = 0; b < nblk; b++) {
+    const int j0 = b * kXsBlock, nb = min(kXsBlock, R - j0);
+    if (rule && tid < kXsBlock) s_rec[tid] = tid < nb ? rec_of(j0 + tid) : 0xffffffffu;
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    double acc[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+    if (c0 < nc) {
+      const double* qp = qd + c0 * KC_H;
+#pragma unroll 4
+      for (int d4 = 0; d4 < KC_H / 4; d4++) {
+        float4 k4[2];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+          const int j = lane + 32 * t;
+          k4[t] = ks[j * 32 + (d4 ^ (j & 7))];
+        }
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+          const double2 qa = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4);
+          const double2 qc = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4 + 2);
+#pragma unroll
+          for (int t = 0; t < 2; t++) {
+            acc[c][t] = fma(qa.x, double(k4[t].x), acc[c][t]);
+            acc[c][t] = fma(qa.y, double(k4[t].y), acc[c][t]);
+            acc[c][t] = fma(qc.x, double(k4[t].z), acc[c][t]);
+            acc[c][t] = fma(qc.y, double(k4[t].w), acc[c][t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        const int qi = q0 + c0 + c;
+        if (c0 + c >= nc) continue;
+        float* prow = a.p + a.p_off[f] + uint64_t(qi) * R + j0;
+        const bool reopen = rule && s_admitted[c0 + c] == 0;
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+          const int j = lane + 32 * t;
+          if (j >= nb) continue;
+          float m = 0.0f;
+          if (a.mask) m = a.mask[a.p_off[f] + uint64_t(qi) * R + j0 + j];
+          else if (rule && !reopen) m = key_ok(c0 + c, s_rec[j]) ? 0.0f : -1e30f;
+          prow[j] = f32(acc[c][t] * a.scale + double(m));
+        }
+      }
+    }
+    __syncthreads();
+    if (b + 1 < nblk) stage(j0 + kXsBlock);
+  }
+}
+
+// The rest of selectorOracle for one question per CTA, from the masked
+// scores k_select_scores_exact left in the question's p row:
 __global__ void __launch_bounds__(256) k_select_exact(SelectArgs a) {
   constexpr int NT = 256;
   extern __shared__ __align__(16) unsigned char dyn[];
-  __shared__ double qs[KC_H];
   __shared__ double red[NT / 32];
   __shared__ int redi[NT / 32];
-  __shared__ uint32_t redu[NT / 32];
   __shared__ double inv_s;
   __shared__ float bestv[NT / 32];
   __shared__ uint32_t besti[NT / 32];
@@ -734,41 +855,7 @@ __global__ void __launch_bounds__(256) k_select_exact(SelectArgs a) {
   double* e64 = reinterpret_cast<double*>(dyn);               // [max_r]
   float* sc = reinterpret_cast<float*>(e64 + size_t(a.max_r)); // [max_r]
   const int tid = threadIdx.x;
-  if (tid < KC_H) qs[tid] = a.sq[uint64_t(qi) * KC_H + tid];
-
-  // mask rule: admitted count first (a row nothing admits is reopened)
-  bool reopen = false;
-  const uint32_t* sa = nullptr;
-  uint32_t ba = 0;
-  if (a.schema_allow) {
-    sa = a.schema_allow + uint64_t(qi) * 8;
-    ba = a.band_allow[qi];
-    uint32_t admitted = 0;
-    for (int j = tid; j < R; j += NT) {
-      const uint32_t g = a.bank_rec[rb + j];
-      const uint32_t s = a.schema_ids[g], b = a.band_ids[g];
-      admitted += (s < 256u && b < 32u && ((sa[s >> 5] >> (s & 31)) & 1u) && ((ba >> b) & 1u)) ? 1u : 0u;
-    }
-    reopen = block_sum_u32<NT>(admitted, redu) == 0;
-  }
-  __syncthreads();
-
-  for (int j = tid; j < R; j += NT) {
-    const float* kr = a.sk + (rb + j) * KC_H;
-    double s = 0.0;
-#pragma unroll 8
-    for (int d = 0; d < KC_H; d++) s = fma(qs[d], double(kr[d]), s);
-    float m = 0.0f;
-    if (a.mask) {
-      m = a.mask[a.p_off[f] + il * uint64_t(R) + j];
-    } else if (sa && !reopen) {
-      const uint32_t g = a.bank_rec[rb + j];
-      const uint32_t sid = a.schema_ids[g], b = a.band_ids[g];
-      const bool ok = sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u);
-      m = ok ? 0.0f : -1e30f;
-    }
-    sc[j] = f32(s * a.scale + double(m));
-  }
+  for (int j = tid; j < R; j += NT) sc[j] = prow[j];
   __syncthreads();
 
   // scores.every(score => score < -1e29): NaN is NOT blocked here

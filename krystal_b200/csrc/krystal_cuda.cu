@@ -655,6 +655,18 @@ struct Saves {
 // The exact selection over the resident sq / sk of a packed batch: the rule
 // and uniforms of b, or (the backward) an explicit mask, no sampling and the
 // soft gather into `gather`.
+// selectorOracle in the exact arithmetic: the masked scores for chunks of a
+// frame's questions (k_select_scores_exact, into p), then softmax, the
+// decision and the gather one question per CTA (k_select_exact).
+void select_exact(kc_handle* h, const kc::SelectArgs& sa, uint32_t frames, uint32_t max_q, uint32_t q,
+                  uint32_t max_r) {
+  if (q == 0) return;
+  const int chunks = int((std::max<uint32_t>(max_q, 1) + kc::kXsChunk - 1) / kc::kXsChunk);
+  kc::k_select_scores_exact<<<frames * unsigned(chunks), kc::kXsThreads, kc::kXsSmem, h->stream>>>(sa, chunks);
+  kc::k_select_exact<<<q, 256, size_t(std::max<uint32_t>(max_r, 1)) * 12, h->stream>>>(sa);
+  h->launches += 2;
+}
+
 void launch_select_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
                          const float* mask, float* gather) {
   kc::SelectArgs sa{};
@@ -669,9 +681,7 @@ void launch_select_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const k
     sa.mask = mask; sa.schema_allow = nullptr; sa.band_allow = nullptr; sa.uniforms = nullptr;
     sa.bank_values = P<float>(ws.bv); sa.gather = gather;
   }
-  const size_t smem = size_t(tot.max_r) * (8 + 4);
-  kc::k_select_exact<<<unsigned(tot.q), 256, smem, h->stream>>>(sa);
-  h->launches++;
+  select_exact(h, sa, b.frames, tot.max_q, uint32_t(tot.q), tot.max_r);
 }
 
 
@@ -1467,6 +1477,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kXaSmem)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_select_scores_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kXsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * (8 + 4)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_back_q, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1575,8 +1587,7 @@ kc_status kc_select(kc_handle* h, const kc_encoded_view* enc, const float* mask,
     sa.uniforms = uniforms ? P<double>(ws.uniforms) : nullptr;
     sa.max_r = R; sa.scale = 1.0 / std::sqrt(double(H));
     sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.gather = P<float>(ws.gather);
-    kc::k_select_exact<<<Q, 256, size_t(R) * 12, h->stream>>>(sa);
-    h->launches++;
+    select_exact(h, sa, 1, Q, Q, R);
   }
   KC_TRY(cudaGetLastError(), "launch");
   if (R) KC_TRY(cudaMemcpyAsync(p, ws.p.p, uint64_t(Q) * R * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
@@ -1670,8 +1681,8 @@ extern "C" kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, con
   sa.mask = mask;
   sa.max_r = r; sa.scale = 1.0 / std::sqrt(double(H));
   sa.p = p; sa.index = index; sa.gather = gather;
-  kc::k_select_exact<<<q, 256, size_t(r) * 12, h->stream>>>(sa);
-  h->launches += 2;
+  h->launches++;
+  select_exact(h, sa, 1, q, q, r);
   KC_TRY(cudaGetLastError(), "kc_select_noalloc launch");
   return KC_OK;
 }
