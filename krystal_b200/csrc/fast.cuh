@@ -657,7 +657,74 @@ struct SelectFastArgs {
   float* p;
   uint32_t* index;
   uint32_t* flags;  // [frames]
+  int scores_in_p;  // the raw dot products are already in p (k_select_scores_fast)
 };
+
+// The selector's raw dot products q·k_j (the 128-long fmaf chain in dimension
+// order, as k_select_fast forms them) for long banks: one CTA per chunk of up
+// to kSsChunk questions of a frame, the chunks of a frame adjacent in the
+// grid; the bank's key rows stream through shared memory in blocks of
+// kSsBlock (float4 c of row j at j*32 + (c ^ (j & 7))), each loaded once for
+// the chunk; warp w takes questions 8(w&1) .. +7 and keys 32(w>>1) + lane.
+// The products go to the questions' p rows, where k_select_fast picks them up.
+constexpr int kSsChunk = 16;
+constexpr int kSsBlock = 128;
+constexpr int kSsThreads = 256;
+constexpr size_t kSsSmem = size_t(kSsBlock) * KC_H * 4 + size_t(kSsChunk) * KC_H * 4;
+
+__global__ void __launch_bounds__(kSsThreads, 2) k_select_scores_fast(SelectFastArgs a, int chunks) {
+  extern __shared__ __align__(16) float4 ss_smem[];
+  float4* ks = ss_smem;
+  const float4* qs4 = ss_smem + kSsBlock * 32;
+  float* qs = reinterpret_cast<float*>(ss_smem + kSsBlock * 32);
+  const uint32_t f = blockIdx.x / chunks;
+  const int q0 = int(blockIdx.x % chunks) * kSsChunk;
+  const uint64_t rb = a.r_off[f], qb = a.q_off[f];
+  const int R = int(a.r_off[f + 1] - rb), nq = int(a.q_off[f + 1] - qb);
+  if (q0 >= nq || R == 0) return;
+  const int nc = min(kSsChunk, nq - q0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kSsChunk * KC_H; i += kSsThreads) qs[i] = i < nc * KC_H ? a.sq[(qb + q0) * KC_H + i] : 0.f;
+  const float4* sk4 = reinterpret_cast<const float4*>(a.sk + rb * KC_H);
+  auto stage = [&](int j0) {
+    const int nb = min(kSsBlock, R - j0);
+    for (int i = tid; i < nb * 32; i += kSsThreads) {
+      const int j = i >> 5, c4 = i & 31;
+      cp_async16(ks + j * 32 + (c4 ^ (j & 7)), sk4 + size_t(j0 + j) * 32 + c4);
+    }
+  };
+  const int c0 = (warp & 1) * 8, j = (warp >> 1) * 32 + lane;
+  float* pbase = a.p + a.p_off[f] + uint64_t(q0) * R;
+  const int nblk = (R + kSsBlock - 1) / kSsBlock;
+  stage(0);
+  for (int b = 0; b < nblk; b++) {
+    const int j0 = b * kSsBlock, nb = min(kSsBlock, R - j0);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    if (c0 < nc && j < nb) {
+      float sv[8];
+#pragma unroll
+      for (int c = 0; c < 8; c++) sv[c] = 0.f;
+#pragma unroll 2
+      for (int d4 = 0; d4 < KC_H / 4; d4++) {
+        const float4 k = ks[j * 32 + (d4 ^ (j & 7))];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const float4 q4 = qs4[(c0 + c) * 32 + d4];
+          sv[c] = fmaf(q4.x, k.x, sv[c]);
+          sv[c] = fmaf(q4.y, k.y, sv[c]);
+          sv[c] = fmaf(q4.z, k.z, sv[c]);
+          sv[c] = fmaf(q4.w, k.w, sv[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        if (c0 + c < nc) pbase[uint64_t(c0 + c) * R + j0 + j] = sv[c];
+    }
+    __syncthreads();
+    if (b + 1 < nblk) stage(j0 + kSsBlock);
+  }
+}
 
 __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
   constexpr int NT = 256;
@@ -675,10 +742,16 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
   float* qs = sel_smem + size_t(a.qc) * a.max_r;
   {
     const int nc = min(a.qc, nq - q0);
-    for (int i = tid; i < nc * KC_H; i += NT) qs[i] = a.sq[(qb + q0) * KC_H + i];
+    if (a.scores_in_p) {  // k_select_scores_fast left the raw dot products in the p rows
+      const float* src = a.p + a.p_off[f] + uint64_t(q0) * R;
+      for (int c = 0; c < nc; c++)
+        for (int j = tid; j < R; j += NT) sel_smem[size_t(c) * a.max_r + j] = src[uint64_t(c) * R + j];
+    } else {
+      for (int i = tid; i < nc * KC_H; i += NT) qs[i] = a.sq[(qb + q0) * KC_H + i];
+    }
     __syncthreads();
     // raw dot products for the chunk: one key row per thread, read once
-    for (int j = tid; j < R; j += NT) {
+    for (int j = tid; j < R && !a.scores_in_p; j += NT) {
       const float4* kr = reinterpret_cast<const float4*>(a.sk + (rb + j) * KC_H);
       float sv[kSelChunk];
 #pragma unroll

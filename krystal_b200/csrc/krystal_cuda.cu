@@ -788,6 +788,12 @@ void launch_select_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
   sa.scale = float(1.0 / std::sqrt(double(h->d.h)));
   sa.tau = h->tau; sa.tau_c = h->tau_c;
   sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
+  sa.scores_in_p = tot.max_r > uint32_t(kc::kCsMaxBank);
+  if (sa.scores_in_p) {  // long banks: the dot products for 16-question chunks, the bank read once per chunk
+    const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kSsChunk - 1) / kc::kSsChunk);
+    kc::k_select_scores_fast<<<b.frames * unsigned(chunks), kc::kSsThreads, kc::kSsSmem, h->stream>>>(sa, chunks);
+    h->launches++;
+  }
   kc::k_select_fast<<<b.frames * unsigned(sa.chunks), 256, sel_smem(tot.max_r), h->stream>>>(sa);
   h->launches++;
 }
@@ -1477,6 +1483,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kXaSmem)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_select_scores_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kSsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_scores_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kXsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
