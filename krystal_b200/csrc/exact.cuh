@@ -443,7 +443,7 @@ __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* red) {
 //   out_c = Σ_j fma(p_j, v_jc) in index order (f64);  x_c = f32(x_c + f32(out_c))
 // with rows whose every score is below -1e29 giving p = 0.
 //
-// One CTA per chunk of up to kXaChunk questions of a frame, the chunks of a
+// One CTA per chunk of up to QC (16, 8 or 4) questions of a frame, the chunks of a
 // frame adjacent in the grid (they share the bank in L2). The bank's k rows
 // stream through shared memory in blocks of kXaBlock keys, each loaded once
 // for the whole chunk; three passes over the blocks compute the scores
@@ -452,18 +452,19 @@ __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* red) {
 // row adds in index order, the sum carried from block to block, (3) p, then
 // p·v, each output chain carried in index order from block to block.
 //
-// Score tiles: thread t takes head t>>6, questions 2((t>>3)&7) and +1, keys
-// (t&7) + 8i of the block (i < 8); the k block's float4 c of row j sits at
-// j*32 + (c ^ (j & 7)) so the 8 lanes of a quarter-warp read 8 bank groups.
-// p·v tiles: thread t takes questions 4(t>>6) .. +3 and columns 2(t&63), +1.
+// Score tiles: thread t takes head t>>6, questions 2((t&63)/G) and +1, keys
+// ((t&63)%G) + G·i of the block (G = 64/(QC/2) key groups, i < QC/2); the k
+// block's float4 c of row j sits at j*32 + (c ^ (j & 7)) so the 8 lanes of a
+// quarter-warp read 8 bank groups. p·v tiles: thread t takes questions
+// (QC/4)(t>>6) .. and columns 2(t&63), +1. A smaller chunk gives a batch of
+// few frames more CTAs; the arithmetic of a question does not depend on it.
 // ---------------------------------------------------------------------------
-constexpr int kXaChunk = 16;
 constexpr int kXaBlock = 64;
 constexpr int kXaThreads = 256;
-constexpr int kXaRows = kXaChunk * KC_HEADS;
-// k block f32 [kXaBlock][128] | q f64 [kXaChunk][128] | exponentials f64 [kXaRows][kXaBlock] | p f32 [kXaRows][kXaBlock]
-constexpr size_t kXaSmem = size_t(kXaBlock) * KC_H * 4 + size_t(kXaChunk) * KC_H * 8 +
-                           size_t(kXaRows) * kXaBlock * 8 + size_t(kXaRows) * kXaBlock * 4;
+// k block f32 [kXaBlock][128] | q f64 [QC][128] | exponentials f64 [4 QC][kXaBlock] | p f32 [4 QC][kXaBlock]
+constexpr size_t xa_smem(int qc) {
+  return size_t(kXaBlock) * KC_H * 4 + size_t(qc) * KC_H * 8 + size_t(qc) * KC_HEADS * kXaBlock * 12;
+}
 
 struct CrossAttnArgs {
   const float* mq;          // [Q,128]
@@ -472,29 +473,34 @@ struct CrossAttnArgs {
   float* query;             // [Q,128], updated in place
   const uint64_t* q_off;    // [frames + 1]
   const uint64_t* r_off;    // [frames + 1]
-  int chunks;               // CTAs per frame: ceil(largest question count / kXaChunk)
+  int chunks;               // CTAs per frame: ceil(largest question count / the chunk)
   double scale;             // 1/sqrt(headDim)
   float* p_out;             // optional [4][sum Q_f R_f]: head h of question i at h*P + p_off[f] + il*R + j
   const uint64_t* p_off;
   uint64_t total_p;
 };
 
+template <int QC>
 __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArgs a) {
+  constexpr int kRows = QC * KC_HEADS;
+  constexpr int NK = QC / 2;          // keys per score thread
+  constexpr int KG = kXaBlock / NK;   // key groups per (head, question pair)
+  constexpr int PQ = QC / 4;          // questions per p·v thread
   extern __shared__ __align__(16) unsigned char dyn[];
   float4* ks = reinterpret_cast<float4*>(dyn);
   double* qd = reinterpret_cast<double*>(dyn + size_t(kXaBlock) * KC_H * 4);
-  double* e64 = qd + kXaChunk * KC_H;
-  float* pf = reinterpret_cast<float*>(e64 + kXaRows * kXaBlock);
-  __shared__ double row_mx[kXaRows], row_inv[kXaRows];
-  __shared__ int row_open[kXaRows];
+  double* e64 = qd + QC * KC_H;
+  float* pf = reinterpret_cast<float*>(e64 + kRows * kXaBlock);
+  __shared__ double row_mx[kRows], row_inv[kRows];
+  __shared__ int row_open[kRows];
   const uint32_t f = blockIdx.x / a.chunks;
-  const int q0 = int(blockIdx.x % a.chunks) * kXaChunk;
+  const int q0 = int(blockIdx.x % a.chunks) * QC;
   const uint64_t qb = a.q_off[f], rb = a.r_off[f];
   const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
   if (q0 >= nq) return;
-  const int nc = min(kXaChunk, nq - q0);
+  const int nc = min(QC, nq - q0);
   const int tid = threadIdx.x;
-  for (int i = tid; i < kXaChunk * KC_H; i += kXaThreads)
+  for (int i = tid; i < QC * KC_H; i += kXaThreads)
     qd[i] = i < nc * KC_H ? double(a.mq[(qb + q0) * KC_H + i]) : 0.0;
   const int nblk = (R + kXaBlock - 1) / kXaBlock;
   const float4* mk4 = reinterpret_cast<const float4*>(a.mk + rb * KC_H);
@@ -510,21 +516,21 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
     __syncthreads();
   };
 
-  const int s_head = tid >> 6, s_q = ((tid >> 3) & 7) * 2, s_k = tid & 7;
+  const int s_head = tid >> 6, s_q = ((tid & 63) / KG) * 2, s_k = (tid & 63) % KG;
   // the tile's scores of the staged block (keys past its end are never used)
-  auto scores = [&](float (&sf)[2][8]) {
-    double acc[2][8];
+  auto scores = [&](float (&sf)[2][NK]) {
+    double acc[2][NK];
 #pragma unroll
     for (int c = 0; c < 2; c++)
 #pragma unroll
-      for (int i = 0; i < 8; i++) acc[c][i] = 0.0;
+      for (int i = 0; i < NK; i++) acc[c][i] = 0.0;
     const double* qp = qd + s_q * KC_H + s_head * KC_HEAD_DIM;
 #pragma unroll 2
     for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
-      float4 k4[8];
+      float4 k4[NK];
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int j = s_k + 8 * i;
+      for (int i = 0; i < NK; i++) {
+        const int j = s_k + KG * i;
         k4[i] = ks[j * 32 + ((s_head * 8 + d4) ^ (j & 7))];
       }
 #pragma unroll
@@ -532,7 +538,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
         const double2 qa = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4);
         const double2 qc = *reinterpret_cast<const double2*>(qp + c * KC_H + 4 * d4 + 2);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
+        for (int i = 0; i < NK; i++) {
           acc[c][i] = fma(qa.x, double(k4[i].x), acc[c][i]);
           acc[c][i] = fma(qa.y, double(k4[i].y), acc[c][i]);
           acc[c][i] = fma(qc.x, double(k4[i].z), acc[c][i]);
@@ -543,7 +549,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
 #pragma unroll
     for (int c = 0; c < 2; c++)
 #pragma unroll
-      for (int i = 0; i < 8; i++) sf[c][i] = f32(acc[c][i] * a.scale + 0.0);
+      for (int i = 0; i < NK; i++) sf[c][i] = f32(acc[c][i] * a.scale + 0.0);
   };
   const int row0 = s_q * KC_HEADS + s_head;  // the tile's rows: row0 and row0 + 4
 
@@ -555,22 +561,22 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
     for (int b = 0; b < nblk; b++) {
       const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
       staged();
-      float sf[2][8];
+      float sf[2][NK];
       scores(sf);
       __syncthreads();
       if (b + 1 < nblk) stage(j0 + kXaBlock);
 #pragma unroll
       for (int c = 0; c < 2; c++)
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          if (s_k + 8 * i < nb) {
+        for (int i = 0; i < NK; i++)
+          if (s_k + KG * i < nb) {
             m[c] = js_max(m[c], double(sf[c][i]));
             open[c] |= double(sf[c][i]) >= -1e29;
           }
     }
 #pragma unroll
     for (int c = 0; c < 2; c++) {
-      for (int o = 1; o < 8; o <<= 1) {
+      for (int o = 1; o < KG; o <<= 1) {
         m[c] = js_max(m[c], __shfl_xor_sync(0xffffffffu, m[c], o));
         open[c] |= __shfl_xor_sync(0xffffffffu, int(open[c]), o) != 0;
       }
@@ -584,19 +590,19 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
   const double mx0 = row_mx[row0], mx1 = row_mx[row0 + 4];
   const bool op0 = row_open[row0] != 0, op1 = row_open[row0 + 4] != 0;
 
-  // (2) exponentials; thread r < kXaRows adds row r's in index order
+  // (2) exponentials; thread r < kRows adds row r's in index order
   {
     double sum = 0.0;
-    const bool summer = tid < kXaRows && row_open[tid] != 0;
+    const bool summer = tid < kRows && row_open[tid] != 0;
     if (nblk > 0) stage(0);
     for (int b = 0; b < nblk; b++) {
       const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
       staged();
-      float sf[2][8];
+      float sf[2][NK];
       scores(sf);
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int j = s_k + 8 * i;
+      for (int i = 0; i < NK; i++) {
+        const int j = s_k + KG * i;
         if (j < nb) {
           if (op0) e64[row0 * kXaBlock + j] = exp(double(sf[0][i]) - mx0);
           if (op1) e64[(row0 + 4) * kXaBlock + j] = exp(double(sf[1][i]) - mx1);
@@ -607,26 +613,26 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
       if (summer)
         for (int j = 0; j < nb; j++) sum += e64[tid * kXaBlock + j];
     }
-    if (tid < kXaRows) row_inv[tid] = 1.0 / js_max(sum, 1e-20);
+    if (tid < kRows) row_inv[tid] = 1.0 / js_max(sum, 1e-20);
   }
   __syncthreads();
   const double inv0 = row_inv[row0], inv1 = row_inv[row0 + 4];
 
   // (3) p, then p·v
-  const int v_q = (tid >> 6) * 4, v_col = (tid & 63) * 2, v_head = (tid & 63) >> 4;
-  double acc[4][2];
+  const int v_q = (tid >> 6) * PQ, v_col = (tid & 63) * 2, v_head = (tid & 63) >> 4;
+  double acc[PQ][2];
 #pragma unroll
-  for (int c = 0; c < 4; c++) acc[c][0] = acc[c][1] = 0.0;
+  for (int c = 0; c < PQ; c++) acc[c][0] = acc[c][1] = 0.0;
   if (nblk > 0) stage(0);
   for (int b = 0; b < nblk; b++) {
     const int j0 = b * kXaBlock, nb = min(kXaBlock, R - j0);
     staged();
     {
-      float sf[2][8];
+      float sf[2][NK];
       scores(sf);
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int j = s_k + 8 * i;
+      for (int i = 0; i < NK; i++) {
+        const int j = s_k + KG * i;
         if (j < nb) {
           const float p0 = op0 ? f32(double(f32(exp(double(sf[0][i]) - mx0))) * inv0) : 0.0f;
           const float p1 = op1 ? f32(double(f32(exp(double(sf[1][i]) - mx1))) * inv1) : 0.0f;
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
 #pragma unroll
         for (int u = 0; u < 4; u++) v[u] = *reinterpret_cast<const float2*>(vr + size_t(j + u) * KC_H);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < PQ; c++) {
           const float4 p4 = *reinterpret_cast<const float4*>(pr + c * KC_HEADS * kXaBlock + j);
           const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
@@ -664,7 +670,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
       for (; j < nb; j++) {
         const float2 v = *reinterpret_cast<const float2*>(vr + size_t(j) * KC_H);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < PQ; c++) {
           const double pj = double(pr[c * KC_HEADS * kXaBlock + j]);
           acc[c][0] = fma(pj, double(v.x), acc[c][0]);
           acc[c][1] = fma(pj, double(v.y), acc[c][1]);
@@ -673,7 +679,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
     }
   }
 #pragma unroll
-  for (int c = 0; c < 4; c++)
+  for (int c = 0; c < PQ; c++)
     if (v_q + c < nc) {
       float* qp = a.query + (qb + q0 + v_q + c) * KC_H + v_col;
       qp[0] = f32(double(qp[0]) + double(f32(acc[c][0])));

@@ -753,11 +753,19 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, m0, W, H, mq, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, m0 + 1, W + uint64_t(H) * H, H, mk, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bv), H, R, m0 + 2, W + 2ull * H * H, H, mv, H, H));
-      const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kXaChunk - 1) / kc::kXaChunk);
+      // the largest question chunk whose grid still fills two CTAs per SM
+      // (few frames, e.g. the recomputed ones, get smaller chunks)
+      const uint32_t mq1 = std::max<uint32_t>(tot.max_q, 1);
+      int qc = 16;
+      while (qc > 4 && uint64_t(b.frames) * ((mq1 + qc - 1) / qc) < 2ull * uint64_t(h->sms)) qc /= 2;
+      const int chunks = int((mq1 + qc - 1) / qc);
       kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
                            chunks, attn_scale, sv ? sv->mix_p + blk * 4 * tot.p : nullptr,
                            P<uint64_t>(ws.p_off), tot.p};
-      kc::k_cross_attn_exact<<<b.frames * unsigned(chunks), kc::kXaThreads, kc::kXaSmem, h->stream>>>(ca);
+      const unsigned grid = b.frames * unsigned(chunks);
+      if (qc == 16) kc::k_cross_attn_exact<16><<<grid, kc::kXaThreads, kc::xa_smem(16), h->stream>>>(ca);
+      else if (qc == 8) kc::k_cross_attn_exact<8><<<grid, kc::kXaThreads, kc::xa_smem(8), h->stream>>>(ca);
+      else kc::k_cross_attn_exact<4><<<grid, kc::kXaThreads, kc::xa_smem(4), h->stream>>>(ca);
       h->launches++;
       KC_CHECK(gemm<kc::kEpiRelu>(h, tc, P<float>(ws.qstate), H, Q, m0 + 3, w1, H, mh, FF, H));
       KC_CHECK(gemm<kc::kEpiResid>(h, tc, mh, FF, Q, m0 + 4, w2, FF, P<float>(ws.qstate), H, FF));
@@ -1481,8 +1489,13 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::k_select_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (96 << 10) + kc::kSelChunk * KC_H * 4)))
     return bail(e, "smem");
-  if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(kc::kXaSmem)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_cross_attn_exact<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::xa_smem(16)))) ||
+      (e = cudaFuncSetAttribute(kc::k_cross_attn_exact<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::xa_smem(8)))) ||
+      (e = cudaFuncSetAttribute(kc::k_cross_attn_exact<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::xa_smem(4)))))
+    return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_scores_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kSsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_scores_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
