@@ -134,39 +134,45 @@ __global__ void __launch_bounds__(256, BM == 128 ? 1 : 2) k_dgemm_exact(const fl
 #pragma unroll
     for (int j = 0; j < TM; j++) acc[i][j] = 0.0;
 
-  float4 ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 rb = loader ? __ldg(reinterpret_cast<const float4*>(Bp)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  if (loader) {
-    As[0][lc + 0][lr] = ra.x; As[0][lc + 1][lr] = ra.y; As[0][lc + 2][lr] = ra.z; As[0][lc + 3][lr] = ra.w;
-    Bs[0][lc + 0][lr] = rb.x; Bs[0][lc + 1][lr] = rb.y; Bs[0][lc + 2][lr] = rb.z; Bs[0][lc + 3][lr] = rb.w;
-  }
-  __syncthreads();
-
-  const int steps = K / BK;
-  for (int s = 0; s < steps; s++) {
-    const int cur = s & 1;
-    const bool more = s + 1 < steps;
-    if (more && loader) {
-      ra = a_ok ? __ldg(reinterpret_cast<const float4*>(Ap + (s + 1) * BK)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      rb = __ldg(reinterpret_cast<const float4*>(Bp + (s + 1) * BK));
-    }
+  // a thread stages row lr of the A and B tiles, k-step s's four columns;
+  // the global loads run two k-steps ahead of the products (registers x for
+  // even steps, y for odd), so their latency spans two steps of DFMAs
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto load_a = [&](int s) { return a_ok ? __ldg(reinterpret_cast<const float4*>(Ap + s * BK)) : z4; };
+  auto load_b = [&](int s) { return loader ? __ldg(reinterpret_cast<const float4*>(Bp + s * BK)) : z4; };
+  auto stage = [&](int buf, float4 ra, float4 rb) {
+    if (!loader) return;
+    As[buf][lc + 0][lr] = ra.x; As[buf][lc + 1][lr] = ra.y; As[buf][lc + 2][lr] = ra.z; As[buf][lc + 3][lr] = ra.w;
+    Bs[buf][lc + 0][lr] = rb.x; Bs[buf][lc + 1][lr] = rb.y; Bs[buf][lc + 2][lr] = rb.z; Bs[buf][lc + 3][lr] = rb.w;
+  };
+  auto products = [&](int buf) {
 #pragma unroll
     for (int kk = 0; kk < BK; kk++) {
       double av[TM], bv[TM];
 #pragma unroll
-      for (int i = 0; i < TM; i++) av[i] = As[cur][kk][ty + 16 * i];
+      for (int i = 0; i < TM; i++) av[i] = As[buf][kk][ty + 16 * i];
 #pragma unroll
-      for (int j = 0; j < TM; j++) bv[j] = Bs[cur][kk][tx + 16 * j];
+      for (int j = 0; j < TM; j++) bv[j] = Bs[buf][kk][tx + 16 * j];
 #pragma unroll
       for (int i = 0; i < TM; i++)
 #pragma unroll
         for (int j = 0; j < TM; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
     }
-    if (more && loader) {
-      const int nx = cur ^ 1;
-      As[nx][lc + 0][lr] = ra.x; As[nx][lc + 1][lr] = ra.y; As[nx][lc + 2][lr] = ra.z; As[nx][lc + 3][lr] = ra.w;
-      Bs[nx][lc + 0][lr] = rb.x; Bs[nx][lc + 1][lr] = rb.y; Bs[nx][lc + 2][lr] = rb.z; Bs[nx][lc + 3][lr] = rb.w;
-    }
+  };
+  const int steps = K / BK;
+  float4 xa = load_a(0), xb = load_b(0), ya = z4, yb = z4;
+  stage(0, xa, xb);
+  if (steps > 1) { ya = load_a(1); yb = load_b(1); }
+  __syncthreads();
+  for (int s = 0; s < steps; s += 2) {
+    if (s + 2 < steps) { xa = load_a(s + 2); xb = load_b(s + 2); }
+    products(0);
+    if (s + 1 < steps) stage(1, ya, yb);
+    __syncthreads();
+    if (s + 1 >= steps) break;
+    if (s + 3 < steps) { ya = load_a(s + 3); yb = load_b(s + 3); }
+    products(1);
+    if (s + 2 < steps) stage(0, xa, xb);
     __syncthreads();
   }
 
