@@ -51,6 +51,13 @@ def load_peaks() -> tuple[dict, str]:
         return PEAKS_FALLBACK, "fallback"
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per token of one
+# launch, from ncu on the full ragged_4096 batch (2 491 910 tokens, two
+# launches each; profiles/fused_encoder_dram_traffic_ragged_4096.md). The
+# kernels move x once in and once out, so traffic scales with the tokens.
+DRAM_BYTES_PER_TOKEN = {"enc_attn_tc": 1004.8, "enc_ffn": 999.3}
+
+
 def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: str) -> dict:
     """Roofline of one fused tensor-core kernel from the profile counters
     (<key>_ms, _launches, _flops, _bytes): ALGORITHMIC FLOPs per launch (the
@@ -66,8 +73,13 @@ def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: s
     gbs = nbytes / (ms / 1e3) / 1e9 if ms > 0 else 0.0
     peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     hbm = peaks.get("hbm_gbs")
+    tokens = nbytes / (4 * 2 * 128)  # the algorithmic bytes are x read and written: 1 KB per token
+    per_token = DRAM_BYTES_PER_TOKEN.get(key)
+    traffic = per_token * tokens if per_token else None
     return {"kernel": kernel, "bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-            "frac": tflops / peak if peak else None, "traffic": None,
+            "frac": tflops / peak if peak else None, "traffic": traffic,
+            "traffic_source": ("ncu DRAM bytes per token on the full 4096-frame batch, scaled to this launch's "
+                               "tokens") if per_token else None,
             "peak_kind": f"{peaks_kind} sustained bf16 dense (cuBLAS)",
             "issued_tensor_tflops": 3 * tflops, "issued_frac": 3 * tflops / peak if peak else None,
             "hbm_gbs_algorithmic": gbs, "hbm_frac": gbs / hbm if hbm else None,
