@@ -566,7 +566,7 @@ constexpr size_t kLocalBackSmem = size_t(kLocalBackWarps) * kLocalBackWarpFloats
 // (a record's rows are a few KB, so repeated reads hit L1), leaving only the
 // record's p and dS in shared memory: 2 KB per warp, so many records are in
 // flight per SM.
-__global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(LocalBackArgs a) {
+__global__ void __launch_bounds__(kLocalBackWarps * 32, 2) k_local_attn_back(LocalBackArgs a) {
   extern __shared__ __align__(16) float lsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * kLocalBackWarps + warp;
@@ -625,10 +625,19 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(Loc
     double aq[KC_RW], ak[KC_RW], av[KC_RW];
 #pragma unroll
     for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = 0.0;
-    for (int j = 0; j < cnt; j++) {
-      const double kj = double(qkv[j * 3 * KC_H + KC_H + col]);
-      const double qj = double(qkv[j * 3 * KC_H + col]);
-      const double dj = double(dout[j * KC_H + col]);
+    // the head's column of every row of the record, loaded before the chains
+    float kc[KC_RW], qc[KC_RW], dc[KC_RW];
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++)
+      if (j < cnt) {
+        kc[j] = qkv[j * 3 * KC_H + KC_H + col];
+        qc[j] = qkv[j * 3 * KC_H + col];
+        dc[j] = dout[j * KC_H + col];
+      }
+#pragma unroll
+    for (int j = 0; j < KC_RW; j++) {
+      if (j >= cnt) break;
+      const double kj = double(kc[j]), qj = double(qc[j]), dj = double(dc[j]);
 #pragma unroll
       for (int i = 0; i < KC_RW; i++)
         if (i < cnt) {
