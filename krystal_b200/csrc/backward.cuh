@@ -447,6 +447,7 @@ __global__ void __launch_bounds__(256) k_pool_back(PoolBackArgs a) {
   __shared__ float dp[8][2][KC_RW];     // dPk, dPv
   __shared__ double dsm[8][2][KC_RW];   // dSk, dSv
   __shared__ double rsm[8][2];
+  __shared__ float gs[8][2][KC_H];      // the record's dKey (0 for a question) and dValue rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 2 * KC_H; i += 256) (&ps[0][0])[i] = a.pool[i];
   __syncthreads();
@@ -463,6 +464,10 @@ __global__ void __launch_bounds__(256) k_pool_back(PoolBackArgs a) {
   const float4* src = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H);
   float4* dst = reinterpret_cast<float4*>(&xs[warp][0][0]);
   for (int i = lane; i < cnt * 32; i += 32) dst[i] = src[i];
+  for (int d = lane; d < KC_H; d += 32) {
+    gs[warp][0][d] = dkey ? dkey[d] : 0.0f;
+    gs[warp][1][d] = dval[d];
+  }
   __syncwarp();
   const int j = lane & 7, which = lane >> 3;  // lanes 0..15 work
   if (lane < 16 && j < cnt) {
@@ -474,9 +479,9 @@ __global__ void __launch_bounds__(256) k_pool_back(PoolBackArgs a) {
   if (lane == 0 || lane == 8) softmax_small(pr[warp][lane >> 3], cnt);
   __syncwarp();
   if (lane < 16 && j < cnt) {
-    const float* gr = which ? dval : dkey;
+    const float* gr = gs[warp][which];
     double s = 0.0;
-    for (int d = 0; d < KC_H; d++) s = fma(gr ? double(gr[d]) : 0.0, double(xs[warp][j][d]), s);
+    for (int d = 0; d < KC_H; d++) s = fma(double(gr[d]), double(xs[warp][j][d]), s);
     dp[warp][which][j] = f32(s);
   }
   __syncwarp();
@@ -494,7 +499,7 @@ __global__ void __launch_bounds__(256) k_pool_back(PoolBackArgs a) {
   }
   __syncwarp();
   for (int d = lane; d < KC_H; d += 32) {
-    const double gk = dkey ? double(dkey[d]) : 0.0, gv = double(dval[d]);
+    const double gk = double(gs[warp][0][d]), gv = double(gs[warp][1][d]);
     const double pk_d = ps[0][d], pv_d = ps[1][d];
     for (int t = 0; t < cnt; t++) {
       const double ds = double(pr[warp][0][t]) * gk + double(pr[warp][1][t]) * gv +
