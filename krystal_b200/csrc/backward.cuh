@@ -563,15 +563,24 @@ struct LocalBackArgs {
   float* dqkv;               // [T,384]
 };
 
-constexpr int kLocalBackWarps = 8;
-constexpr int kLocalBackWarpFloats = 2 * KC_HEADS * KC_RW * KC_RW;  // p and dS of one record
+constexpr int kLocalBackWarps = 4;
+// per warp: p and dS of one record, then its q|k|v rows (8 x 96 float4) and
+// dOut rows (8 x 32 float4)
+constexpr int kLocalBackWarpFloats = 2 * KC_HEADS * KC_RW * KC_RW + KC_RW * (96 + 32) * 4;
 constexpr size_t kLocalBackSmem = size_t(kLocalBackWarps) * kLocalBackWarpFloats * 4;
 
-// One warp per record. q|k|v and dOut are read straight from global memory
-// (a record's rows are a few KB, so repeated reads hit L1), leaving only the
-// record's p and dS in shared memory: 2 KB per warp, so many records are in
-// flight per SM.
-__global__ void __launch_bounds__(kLocalBackWarps * 32, 2) k_local_attn_back(LocalBackArgs a) {
+// Staged dOut row r of a record: 32 float4 (heads 0-3, 8 float4 each), float4
+// m of head h at h*8 + ((m + 2h + (r & 1)) & 7) — the dOut analogue of
+// la_exact_f4, so a quarter-warp (two tokens x four heads) reads 8 bank groups.
+__device__ __forceinline__ int lb_dout_f4(int r, int f) {
+  return r * 32 + (f & ~7) + (((f & 7) + 2 * ((f >> 3) & 3) + (r & 1)) & 7);
+}
+
+// One warp per record, 4 warps per CTA. The record's q|k|v and dOut rows
+// (at most 16 KB) are staged in shared memory with one batch of asynchronous
+// 16-byte copies, so each record costs one round trip to memory; the scores,
+// dS and the dQ | dK | dV chains then read shared memory only.
+__global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(LocalBackArgs a) {
   extern __shared__ __align__(16) float lsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t g = uint64_t(blockIdx.x) * kLocalBackWarps + warp;
@@ -579,22 +588,29 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 2) k_local_attn_back(Loc
   const uint32_t start = a.rec_start[g];
   const int cnt = int(a.rec_meta[g].y & 15u);
   if (cnt == 0) return;
-  float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(lsm + size_t(warp) * kLocalBackWarpFloats);
+  float* wsm = lsm + size_t(warp) * kLocalBackWarpFloats;
+  float(*pp)[KC_RW][KC_RW] = reinterpret_cast<float(*)[KC_RW][KC_RW]>(wsm);
   float(*dsh)[KC_RW][KC_RW] = pp + KC_HEADS;  // [head][i][j]
-  const float* qkv = a.qkv + uint64_t(start) * 3 * KC_H;
-  const float* dout = a.dout + uint64_t(start) * KC_H;
+  float4* rows = reinterpret_cast<float4*>(wsm + 2 * KC_HEADS * KC_RW * KC_RW);  // q|k|v, la_exact_f4 layout
+  float4* drows = rows + KC_RW * 96;                                              // dOut, lb_dout_f4 layout
+  {
+    const float4* src = reinterpret_cast<const float4*>(a.qkv + uint64_t(start) * 3 * KC_H);
+    for (int i = lane; i < cnt * 96; i += 32) cp_async16(rows + la_exact_f4(i / 96, i % 96), src + i);
+    const float4* dsrc = reinterpret_cast<const float4*>(a.dout + uint64_t(start) * KC_H);
+    for (int i = lane; i < cnt * 32; i += 32) cp_async16(drows + lb_dout_f4(i >> 5, i & 31), dsrc + i);
+  }
   for (int i = lane; i < cnt * KC_HEADS * KC_RW; i += 32) {
     const int ti = i >> 5, head = (i >> 3) & 3, jj = i & 7;
     pp[head][ti][jj] = a.p[(uint64_t(start) + ti) * KC_HEADS * KC_RW + head * KC_RW + jj];
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
   {
     const int ti = lane >> 2, head = lane & 3;
     if (ti < cnt) {
       float4 d4[KC_HEAD_DIM / 4];
-      const float4* dr = reinterpret_cast<const float4*>(dout + ti * KC_H + head * KC_HEAD_DIM);
 #pragma unroll
-      for (int m = 0; m < 8; m++) d4[m] = dr[m];
+      for (int m = 0; m < 8; m++) d4[m] = drows[lb_dout_f4(ti, head * 8 + m)];
       // s[j] = dOut_i · v_j: eight f64 chains side by side, each over d in order
       // (keys past the record read row 0 and are never used)
       double s[KC_RW];
@@ -604,8 +620,7 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 2) k_local_attn_back(Loc
       for (int m = 0; m < 8; m++)
 #pragma unroll
         for (int j = 0; j < KC_RW; j++) {
-          const float4 v = reinterpret_cast<const float4*>(qkv + (j < cnt ? j : 0) * 3 * KC_H + 2 * KC_H +
-                                                           head * KC_HEAD_DIM)[m];
+          const float4 v = rows[la_exact_f4(j < cnt ? j : 0, 64 + head * 8 + m)];
           s[j] = fma(double(d4[m].x), double(v.x), s[j]);
           s[j] = fma(double(d4[m].y), double(v.y), s[j]);
           s[j] = fma(double(d4[m].z), double(v.z), s[j]);
@@ -622,27 +637,22 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 2) k_local_attn_back(Loc
   }
   __syncwarp();
   float* out = a.dqkv + uint64_t(start) * 3 * KC_H;
+  const float* rowsf = reinterpret_cast<const float*>(rows);
+  const float* drowsf = reinterpret_cast<const float*>(drows);
   // dQ_i = Σ_j dS_ij k_j, dK_i = Σ_j dS_ji q_j, dV_i = Σ_j P_ji dOut_j per
   // column: every row i of the record at once (24 f64 chains per lane), each
   // chain over j in order
   for (int m = 0; m < KC_HEADS; m++) {
-    const int col = m * KC_HEAD_DIM + lane;
+    const int col = m * KC_HEAD_DIM + lane, f = m * 8 + (lane >> 2), c = lane & 3;
     double aq[KC_RW], ak[KC_RW], av[KC_RW];
 #pragma unroll
     for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = 0.0;
-    // the head's column of every row of the record, loaded before the chains
-    float kc[KC_RW], qc[KC_RW], dc[KC_RW];
-#pragma unroll
-    for (int j = 0; j < KC_RW; j++)
-      if (j < cnt) {
-        kc[j] = qkv[j * 3 * KC_H + KC_H + col];
-        qc[j] = qkv[j * 3 * KC_H + col];
-        dc[j] = dout[j * KC_H + col];
-      }
 #pragma unroll
     for (int j = 0; j < KC_RW; j++) {
       if (j >= cnt) break;
-      const double kj = double(kc[j]), qj = double(qc[j]), dj = double(dc[j]);
+      const double kj = double(rowsf[la_exact_f4(j, 32 + f) * 4 + c]);
+      const double qj = double(rowsf[la_exact_f4(j, f) * 4 + c]);
+      const double dj = double(drowsf[lb_dout_f4(j, f) * 4 + c]);
 #pragma unroll
       for (int i = 0; i < KC_RW; i++)
         if (i < cnt) {
