@@ -345,7 +345,7 @@ struct CrossBackArgs {
 __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   extern __shared__ __align__(16) unsigned char dyn[];
   double* s64 = reinterpret_cast<double*>(dyn);                     // [4][max_r]
-  float* dss = reinterpret_cast<float*>(s64 + 4 * size_t(a.max_r));  // [4][max_r]
+  float* dss = reinterpret_cast<float*>(s64 + 4 * size_t(a.max_r));  // [4][max_r]: the question's p rows, then dS
   __shared__ float dos[KC_H];
   __shared__ double rsum[KC_HEADS];
   const uint32_t qi = blockIdx.x, f = a.g.query_frame[qi];
@@ -354,6 +354,10 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   const uint64_t po = a.g.p_off[f] + (qi - a.g.q_off[f]) * uint64_t(R);
   const int tid = threadIdx.x;
   dos[tid] = a.dout[uint64_t(qi) * KC_H + tid];
+  for (int idx = tid; idx < R * KC_HEADS; idx += 128) {  // p rows staged once (coalesced per head)
+    const int head = idx / R, j = idx - head * R;
+    dss[head * size_t(a.max_r) + j] = a.p[uint64_t(head) * a.total_p + po + j];
+  }
   __syncthreads();
   for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
     const int j = idx >> 2, head = idx & 3, hb = head * KC_HEAD_DIM;
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   }
   __syncthreads();
   if (tid < KC_HEADS) {
-    const float* prow = a.p + uint64_t(tid) * a.total_p + po;
+    const float* prow = dss + tid * size_t(a.max_r);
     const double* sr = s64 + tid * size_t(a.max_r);
     double rs = 0.0;
     for (int j = 0; j < R; j++) rs = rs + double(prow[j]) * sr[j];
@@ -375,9 +379,10 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   for (int idx = tid; idx < R * KC_HEADS; idx += 128) {
     const int head = idx / R, j = idx - head * R;
     const uint64_t pi = uint64_t(head) * a.total_p + po + j;
-    const double pij = a.p[pi];
+    float* slot = dss + head * size_t(a.max_r) + j;
+    const double pij = *slot;
     const float v = f32(pij * (double(f32(s64[head * size_t(a.max_r) + j])) - rsum[head]));
-    dss[head * size_t(a.max_r) + j] = v;
+    *slot = v;
     a.ds[pi] = v;
   }
   __syncthreads();
