@@ -91,56 +91,48 @@ class UpdatePlan:
     mean_confidence: float
 
 
+def _running_total(x: np.ndarray) -> float:
+    """The loop's `total += x[i]` from 0.0, in order: the last running sum
+    (np.cumsum adds sequentially; np.sum would pair terms)."""
+    return float(np.cumsum(np.concatenate(([0.0], x)))[-1])
+
+
 def plan_update(stats: np.ndarray, rewards: np.ndarray, answered: np.ndarray, options: LearnOptions) -> UpdatePlan:
     """The scalar half of learnFromExperience over a batch, in batch order.
 
     stats: [F, 8] per-frame readings (kc_learn_frame_stats); rewards: [F]
     (NaN = no reward: the experience is skipped, learn.ts:320); answered: [F]
-    whether any question had a target (:325-334)."""
+    whether any question had a target (:325-334). Vectorised, with every sum
+    taken in frame order as the reference's loop takes it."""
+    stats = np.asarray(stats, np.float64)
+    rewards = np.asarray(rewards, np.float64)
     F = rewards.size
     step = np.zeros(F, np.float64)
     value_weight = np.zeros(F, np.float64)
-    pending: list[tuple[int, float]] = []
-    seen = 0
-    adv_total = loss_total = ent_total = conf_total = 0.0
-    ent_rows = conf_rows = 0.0
-    for f in range(F):
-        reward = float(rewards[f])
-        if math.isnan(reward) or not stats[f, 0] or not stats[f, 1]:
-            continue
-        advantage = reward - float(stats[f, 2])
-        value_weight[f] = 1.0
-        if answered[f] and math.isfinite(advantage):
-            pending.append((f, advantage))
-        ent_total += stats[f, 4]
-        ent_rows += stats[f, 5]
-        conf_total += stats[f, 6]
-        conf_rows += stats[f, 7]
-        adv_total += advantage
-        loss_total += float(stats[f, 3])
-        seen += 1
+    used = np.flatnonzero(~np.isnan(rewards) & (stats[:, 0] != 0) & (stats[:, 1] != 0))
+    advantage = rewards[used] - stats[used, 2]
+    value_weight[used] = 1.0
+    seen = int(used.size)
+    adv_total, loss_total = _running_total(advantage), _running_total(stats[used, 3])
+    ent_total, ent_rows = _running_total(stats[used, 4]), _running_total(stats[used, 5])
+    conf_total, conf_rows = _running_total(stats[used, 6]), _running_total(stats[used, 7])
+    pend = np.asarray(answered, bool)[used] & np.isfinite(advantage)
+    frames, adv = used[pend], advantage[pend]
     reinforced = discouraged = 0
     actor_moved = False
-    if pending:
-        mean = 0.0
-        for _, a in pending:
-            mean += a
-        mean /= len(pending)
-        var = 0.0
-        for _, a in pending:
-            var += (a - mean) ** 2
-        var /= len(pending)
+    if adv.size:
+        n = adv.size
+        mean = _running_total(adv) / n
+        d = adv - mean
+        var = _running_total(d * d) / n  # (a - mean) ** 2: a square, as the reference's pow(x, 2) is
         deviation = math.sqrt(var)
         if deviation > 1e-6:  # a batch where everything went equally well pushes nothing (:447-451)
             actor_moved = True
             clip = options.advantage_clip
-            for f, a in pending:
-                st = max(-clip, min(clip, (a - mean) / deviation))
-                step[f] = (options.learning_rate * options.policy_scale * st) / len(pending)
-                if st > 0:
-                    reinforced += 1
-                elif st < 0:
-                    discouraged += 1
+            st = np.minimum(clip, np.maximum(-clip, (adv - mean) / deviation))
+            step[frames] = (options.learning_rate * options.policy_scale * st) / n
+            reinforced = int((st > 0).sum())
+            discouraged = int((st < 0).sum())
     return UpdatePlan(step, value_weight, seen, actor_moved, reinforced, discouraged,
                       adv_total / seen if seen else 0.0, loss_total / seen if seen else 0.0,
                       ent_total / ent_rows if ent_rows else 0.0, conf_total / conf_rows if conf_rows else 0.0)
