@@ -263,25 +263,35 @@ struct SelBackKArgs {
   double hscale;
   float* dkp;               // [R,128]
   float* dbv;               // [R,128]
+  uint32_t rows;            // R: bank rows of the batch
 };
 
+constexpr int kSelBackRows = 8;  // bank rows per CTA of k_sel_back_dk
+
 __global__ void __launch_bounds__(128) k_sel_back_dk(SelBackKArgs a) {
-  const uint32_t jg = blockIdx.x, f = a.g.bank_frame[jg];
-  const uint64_t rb = a.g.r_off[f];
-  const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
-  const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0, pb = a.g.p_off[f];
   const int c = threadIdx.x;
-  float dv1 = 0.0f;
-  double ak = 0.0, av = 0.0;
-  for (uint64_t i = 0; i < Q; i++) {
-    const uint64_t pi = pb + i * R + j;
-    const uint64_t qr = (q0 + i) * KC_H + c;
-    if (double(a.mask[pi]) > -1e29) dv1 = f32(double(dv1) + double(a.dag[qr]) / double(a.n_allowed[q0 + i]));
-    ak = fma(double(a.dscore[pi]), double(a.sq[qr]), ak);
-    av = fma(double(a.p[pi]), double(a.dig[qr]), av);
+  // kSelBackRows bank rows per CTA (two in flight at a time); each row's
+  // chains run over its frame's questions in order
+#pragma unroll 2
+  for (int r = 0; r < kSelBackRows; r++) {
+    const uint32_t jg = blockIdx.x * kSelBackRows + r;
+    if (jg >= a.rows) break;
+    const uint32_t f = a.g.bank_frame[jg];
+    const uint64_t rb = a.g.r_off[f];
+    const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
+    const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0, pb = a.g.p_off[f];
+    float dv1 = 0.0f;
+    double ak = 0.0, av = 0.0;
+    for (uint64_t i = 0; i < Q; i++) {
+      const uint64_t pi = pb + i * R + j;
+      const uint64_t qr = (q0 + i) * KC_H + c;
+      if (double(a.mask[pi]) > -1e29) dv1 = f32(double(dv1) + double(a.dag[qr]) / double(a.n_allowed[q0 + i]));
+      ak = fma(double(a.dscore[pi]), double(a.sq[qr]), ak);
+      av = fma(double(a.p[pi]), double(a.dig[qr]), av);
+    }
+    a.dkp[uint64_t(jg) * KC_H + c] = f32(ak * a.hscale);
+    a.dbv[uint64_t(jg) * KC_H + c] = f32(double(dv1) + double(f32(av)));
   }
-  a.dkp[uint64_t(jg) * KC_H + c] = f32(ak * a.hscale);
-  a.dbv[uint64_t(jg) * KC_H + c] = f32(double(dv1) + double(f32(av)));
 }
 
 // matmulBackWeight (backward.ts:560-569) per frame: dW_f[n,k] =

@@ -1312,8 +1312,8 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
     }
     if (R) {
       kc::SelBackKArgs sk{geo, P<float>(bw.dscore), p, mask, P<float>(ws.sq), P<float>(bw.dig), P<float>(bw.dag),
-                          P<uint32_t>(bw.n_allowed), h_scale, P<float>(bw.dkp), dbv};
-      kc::k_sel_back_dk<<<unsigned(R), 128, 0, h->stream>>>(sk);
+                          P<uint32_t>(bw.n_allowed), h_scale, P<float>(bw.dkp), dbv, uint32_t(R)};
+      kc::k_sel_back_dk<<<unsigned((R + kc::kSelBackRows - 1) / kc::kSelBackRows), 128, 0, h->stream>>>(sk);
       h->launches++;
     }
     // dQuery = dQueryOut + dQProj·Wq; dBankKeys = dKProj·Wk (backward.ts:900-912)
