@@ -350,7 +350,10 @@ struct CrossBackArgs {
   float* dq;          // [Q,128]
   float* dk;          // [R,128]
   float* dv;          // [R,128]
+  uint32_t rows;      // R: bank rows of the batch (k_cross_attn_back_kv)
 };
+
+constexpr int kCrossBackRows = 8;  // bank rows per CTA of k_cross_attn_back_kv
 
 __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   extern __shared__ __align__(16) unsigned char dyn[];
@@ -416,21 +419,28 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
 // dV[j,c] = f32(Σ_i p·dOut[i,c]), i over the frame's questions in order.
 // One CTA per bank row; warp w is head w.
 __global__ void __launch_bounds__(128) k_cross_attn_back_kv(CrossBackArgs a) {
-  const uint32_t jg = blockIdx.x, f = a.g.bank_frame[jg];
-  const uint64_t rb = a.g.r_off[f];
-  const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
-  const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0;
   const int col = threadIdx.x, head = col >> 5;
-  const uint64_t base = uint64_t(head) * a.total_p + a.g.p_off[f] + j;
-  double ak = 0.0, av = 0.0;
-  for (uint64_t i = 0; i < Q; i++) {
-    const uint64_t pi = base + i * R;
-    const uint64_t qr = (q0 + i) * KC_H + col;
-    ak = fma(double(a.ds[pi]), double(a.mq[qr]), ak);
-    av = fma(double(a.p[pi]), double(a.dout[qr]), av);
+  // kCrossBackRows bank rows per CTA (two in flight at a time); each row's
+  // chains run over its frame's questions in order
+#pragma unroll 2
+  for (int r = 0; r < kCrossBackRows; r++) {
+    const uint32_t jg = blockIdx.x * kCrossBackRows + r;
+    if (jg >= a.rows) break;
+    const uint32_t f = a.g.bank_frame[jg];
+    const uint64_t rb = a.g.r_off[f];
+    const uint64_t R = a.g.r_off[f + 1] - rb, j = jg - rb;
+    const uint64_t q0 = a.g.q_off[f], Q = a.g.q_off[f + 1] - q0;
+    const uint64_t base = uint64_t(head) * a.total_p + a.g.p_off[f] + j;
+    double ak = 0.0, av = 0.0;
+    for (uint64_t i = 0; i < Q; i++) {
+      const uint64_t pi = base + i * R;
+      const uint64_t qr = (q0 + i) * KC_H + col;
+      ak = fma(double(a.ds[pi]), double(a.mq[qr]), ak);
+      av = fma(double(a.p[pi]), double(a.dout[qr]), av);
+    }
+    a.dk[uint64_t(jg) * KC_H + col] = f32(ak * a.scale);
+    a.dv[uint64_t(jg) * KC_H + col] = f32(av);
   }
-  a.dk[uint64_t(jg) * KC_H + col] = f32(ak * a.scale);
-  a.dv[uint64_t(jg) * KC_H + col] = f32(av);
 }
 
 // poolBackward (backward.ts:184-262) for every record: the two pooling
@@ -541,18 +551,53 @@ struct PoolGradArgs {
   float* dpool;  // [F, 2H]
 };
 
+constexpr int kPoolGradChunk = 1024;  // records whose start and count are staged at a time
+
 __global__ void __launch_bounds__(256) k_pool_grad(PoolGradArgs a) {
+  __shared__ uint2 meta[kPoolGradChunk];  // (first token, token count) of the chunk's records
   const uint32_t f = blockIdx.x;
   const int c = threadIdx.x, which = c >> 7, d = c & 127;
+  // the running f32 sum over the list's records and their tokens, in order;
+  // the record list is staged a chunk at a time, and each record's terms are
+  // loaded together, the next record's while this one is summed
   auto walk = [&](const uint32_t* list, uint64_t b, uint64_t e) {
     float acc = 0.0f;
-    for (uint64_t r = b; r < e; r++) {
-      const uint32_t g = list[r];
-      const uint32_t start = a.rec_start[g];
-      const int cnt = int(a.rec_meta[g].y & 15u);
-      for (int t = 0; t < cnt; t++) {
-        const uint64_t tok = uint64_t(start) + t;
-        acc = f32(double(acc) + a.scale * a.tok_ds[tok * 2 + which] * double(a.x[tok * KC_H + d]));
+    for (uint64_t c0 = b; c0 < e; c0 += kPoolGradChunk) {
+      const int n = int(e - c0 < uint64_t(kPoolGradChunk) ? e - c0 : uint64_t(kPoolGradChunk));
+      __syncthreads();  // the previous chunk's walk is done with meta
+      for (int i = c; i < n; i += 256) {
+        const uint32_t g = list[c0 + i];
+        meta[i] = make_uint2(a.rec_start[g], a.rec_meta[g].y & 15u);
+      }
+      __syncthreads();
+      float xn[KC_RW];
+      double dn[KC_RW];
+      auto fetch = [&](int r) {
+        const uint2 m = meta[r];
+#pragma unroll
+        for (int t = 0; t < KC_RW; t++)
+          if (t < int(m.y)) {
+            const uint64_t tok = uint64_t(m.x) + t;
+            xn[t] = a.x[tok * KC_H + d];
+            dn[t] = a.tok_ds[tok * 2 + which];
+          }
+      };
+      fetch(0);
+      for (int r = 0; r < n; r++) {
+        float xc[KC_RW];
+        double dc[KC_RW];
+#pragma unroll
+        for (int t = 0; t < KC_RW; t++) {
+          xc[t] = xn[t];
+          dc[t] = dn[t];
+        }
+        const int cnt = int(meta[r].y);
+        if (r + 1 < n) fetch(r + 1);
+#pragma unroll
+        for (int t = 0; t < KC_RW; t++) {
+          if (t >= cnt) break;
+          acc = f32(double(acc) + a.scale * dc[t] * double(xc[t]));
+        }
       }
     }
     return acc;

@@ -1342,7 +1342,9 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
       kc::k_cross_attn_back_q<<<unsigned(Q), 128, size_t(tot.max_r) * 48, h->stream>>>(cb);
       h->launches++;
       if (R) {
-        kc::k_cross_attn_back_kv<<<unsigned(R), 128, 0, h->stream>>>(cb);
+        cb.rows = uint32_t(R);
+        kc::k_cross_attn_back_kv<<<unsigned((R + kc::kCrossBackRows - 1) / kc::kCrossBackRows), 128, 0,
+                                   h->stream>>>(cb);
         h->launches++;
       }
       KC_CHECK(gemm<kc::kEpiResid>(h, tc, P<float>(bw.mdq), H, Q, m0, wT, H, dquery, H, H));
