@@ -937,7 +937,8 @@ __global__ void k_fallback_gather(const uint32_t* __restrict__ list, const uint6
     for (uint64_t k = threadIdx.x; k < nq; k += blockDim.x) s_uni[e0 + k] = uniforms[q0 + k];
 }
 
-// One CTA per listed frame: exact p block and indices back to the batch.
+// Exact p blocks and indices back to the batch: a row of 32 CTAs per listed
+// frame (blockIdx.x the frame, blockIdx.y its slice of the copy).
 __global__ void k_fallback_scatter(const uint32_t* __restrict__ list, const uint64_t* __restrict__ p_off,
                                    const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ sub_p_off,
                                    const uint64_t* __restrict__ sub_q_off, const float* __restrict__ sub_p,
@@ -945,8 +946,9 @@ __global__ void k_fallback_scatter(const uint32_t* __restrict__ list, const uint
                                    uint32_t* __restrict__ index) {
   const uint32_t i = blockIdx.x, f = list[i];
   const uint64_t np = p_off[f + 1] - p_off[f], nq = q_off[f + 1] - q_off[f];
-  for (uint64_t k = threadIdx.x; k < np; k += blockDim.x) p[p_off[f] + k] = sub_p[sub_p_off[i] + k];
-  for (uint64_t k = threadIdx.x; k < nq; k += blockDim.x) index[q_off[f] + k] = sub_index[sub_q_off[i] + k];
+  const uint64_t first = uint64_t(blockIdx.y) * blockDim.x + threadIdx.x, stride = uint64_t(gridDim.y) * blockDim.x;
+  for (uint64_t k = first; k < np; k += stride) p[p_off[f] + k] = sub_p[sub_p_off[i] + k];
+  for (uint64_t k = first; k < nq; k += stride) index[q_off[f] + k] = sub_index[sub_q_off[i] + k];
 }
 
 }  // namespace kc

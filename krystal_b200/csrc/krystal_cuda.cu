@@ -981,7 +981,7 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   kc::FrameTotals sub_tot;
   KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
-  kc::k_fallback_scatter<<<n, 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.p_off),
+  kc::k_fallback_scatter<<<dim3(n, 32), 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.p_off),
                                                    P<uint64_t>(ws.q_off), P<uint64_t>(fb.p_off),
                                                    P<uint64_t>(fb.q_off), P<float>(fb.p), P<uint32_t>(fb.index),
                                                    P<float>(ws.p), P<uint32_t>(ws.index));
