@@ -514,23 +514,28 @@ struct CrossAttnSmallArgs {
   float* query;
   const uint64_t* q_off;   // [frames + 1]
   const uint64_t* r_off;   // [frames + 1]
-  int qc;                  // questions per chunk (the score buffer holds qc x 4 x max_r)
+  int qc;                  // questions per chunk
   int chunks;              // CTAs per frame: ceil(largest question count / qc)
-  uint32_t max_r;
+  int half;                // a score row's parity half (16 mod 32, >= ceil(max_r / 2))
   float scale;
 };
 
+// Score rows here are parity-split like k_cross_attn_frame's: key j of row
+// (c, head) at (c*4 + head)*2*half + (j&1)*half + (j>>1), so each p·v chain
+// (one key parity) reads four keys per float4.
 __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSmallArgs a) {
-  extern __shared__ __align__(16) float cas_smem[];  // scores [qc][4][max_r], then q [qc][128]
+  extern __shared__ __align__(16) float cas_smem[];  // scores [qc][4][2*half], then q [qc][128]
   __shared__ float inv_s[kCsChunk][KC_HEADS];
   const uint32_t f = blockIdx.x / a.chunks;
   const int q0 = int(blockIdx.x % a.chunks) * a.qc;
   const uint64_t qb = a.q_off[f], rb = a.r_off[f];
   const int nq = int(a.q_off[f + 1] - qb), R = int(a.r_off[f + 1] - rb);
   if (q0 >= nq) return;
+  const int stride = 2 * a.half;
   float* sc = cas_smem;
-  float* qs = cas_smem + size_t(a.qc) * KC_HEADS * a.max_r;
+  float* qs = cas_smem + size_t(a.qc) * KC_HEADS * stride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto at = [&](float* row, int j) -> float& { return row[(j & 1) * a.half + (j >> 1)]; };
   {
     const int nc = min(a.qc, nq - q0);
     for (int i = tid; i < nc * KC_H; i += kCsThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
@@ -560,19 +565,20 @@ __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSma
           }
 #pragma unroll
       for (int c = 0; c < kCsChunk; c++)
-        if (c < nc) sc[(c * KC_HEADS + head) * a.max_r + j] = sv[c] * a.scale;
+        if (c < nc) at(sc + (c * KC_HEADS + head) * stride, j) = sv[c] * a.scale;
     }
     __syncthreads();
     // softmax rows (question, head): one warp each
     for (int rw = warp; rw < nc * KC_HEADS; rw += kCsThreads / 32) {
-      float* row = sc + size_t(rw) * a.max_r;
+      float* row = sc + size_t(rw) * stride;
       float mx = -INFINITY;
-      for (int j = lane; j < R; j += 32) mx = fmaxf(mx, row[j]);
+      for (int j = lane; j < R; j += 32) mx = fmaxf(mx, at(row, j));
       for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       float sum = 0.f;
       for (int j = lane; j < R; j += 32) {
-        const float e = expf(row[j] - mx);
-        row[j] = e;
+        float& s = at(row, j);
+        const float e = expf(s - mx);
+        s = e;
         sum += e;
       }
       for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -588,25 +594,33 @@ __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSma
       float acc[kCsChunk];
 #pragma unroll
       for (int c = 0; c < kCsChunk; c++) acc[c] = 0.f;
-      const float* vcol = a.mv + rb * KC_H + col;
-      int j = par;
-      for (; j + 62 < R; j += 64) {  // 32 keys of this parity in flight per step
-        float vv[32];
+      const float* vcol = a.mv + (rb + par) * KC_H + col;
+      const float* srow = sc + head * stride + par * a.half;
+      const int npar = (R - par + 1) >> 1;  // keys of this parity
+      int e = 0;
+      for (; e + 16 <= npar; e += 16) {  // 16 keys of this parity in flight per step
+        float vv[16];
 #pragma unroll
-        for (int e = 0; e < 32; e++) vv[e] = vcol[size_t(j + 2 * e) * KC_H];
+        for (int u = 0; u < 16; u++) vv[u] = vcol[size_t(e + u) * (2 * KC_H)];
 #pragma unroll
         for (int c = 0; c < kCsChunk; c++)
           if (c < nc) {
-            const float* row = sc + size_t(c * KC_HEADS + head) * a.max_r + j;
+            const float4* s4 = reinterpret_cast<const float4*>(srow + c * KC_HEADS * stride + e);
 #pragma unroll
-            for (int e = 0; e < 32; e++) acc[c] = fmaf(row[2 * e], vv[e], acc[c]);
+            for (int u4 = 0; u4 < 4; u4++) {
+              const float4 s = s4[u4];
+              acc[c] = fmaf(s.x, vv[4 * u4 + 0], acc[c]);
+              acc[c] = fmaf(s.y, vv[4 * u4 + 1], acc[c]);
+              acc[c] = fmaf(s.z, vv[4 * u4 + 2], acc[c]);
+              acc[c] = fmaf(s.w, vv[4 * u4 + 3], acc[c]);
+            }
           }
       }
-      for (; j < R; j += 2) {
-        const float va = vcol[size_t(j) * KC_H];
+      for (; e < npar; e++) {
+        const float va = vcol[size_t(e) * (2 * KC_H)];
 #pragma unroll
         for (int c = 0; c < kCsChunk; c++)
-          if (c < nc) acc[c] = fmaf(sc[size_t(c * KC_HEADS + head) * a.max_r + j], va, acc[c]);
+          if (c < nc) acc[c] = fmaf(srow[c * KC_HEADS * stride + e], va, acc[c]);
       }
       // the odd sums meet the even ones in the (now free) question buffer
       if (par == 1)

@@ -467,10 +467,14 @@ CrossShape cross_shape(uint32_t max_r) {
               size_t(kc::kCaChunk) * KC_H * 4};
 }
 
-// The one-pass cross attention's shared memory (scores [kCsChunk][4][max_r],
-// then q [kCsChunk][128]) for banks of at most kCsMaxBank rows.
+// The one-pass cross attention's score-row parity half for banks of at most
+// max_r rows (16 mod 32, at least half the longest bank) and its shared memory
+// (scores [kCsChunk][4][2*half], then q [kCsChunk][128]).
+int cross_small_half(uint32_t max_r) {
+  return int((std::max<uint32_t>(max_r, 1) + 1) / 2 + 31) / 32 * 32 + 16;
+}
 size_t cross_small_smem(uint32_t max_r) {
-  return size_t(kc::kCsChunk) * KC_HEADS * std::max<uint32_t>(max_r, 1) * 4 + size_t(kc::kCsChunk) * KC_H * 4;
+  return size_t(kc::kCsChunk) * KC_HEADS * 2 * cross_small_half(max_r) * 4 + size_t(kc::kCsChunk) * KC_H * 4;
 }
 
 // The same for the per-frame selector (scores [qc][max_r], then q [qc][128]).
@@ -880,7 +884,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
         const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCsChunk - 1) / kc::kCsChunk);
         kc::CrossAttnSmallArgs ca{P<float>(ws.mq),       P<float>(ws.mk),         P<float>(ws.mv),
                                   P<float>(ws.qstate),   P<uint64_t>(ws.q_off),   P<uint64_t>(ws.r_off),
-                                  kc::kCsChunk,          chunks,                  std::max<uint32_t>(tot.max_r, 1),
+                                  kc::kCsChunk,          chunks,                  cross_small_half(tot.max_r),
                                   attn_scale};
         kc::k_cross_attn_small<<<b.frames * unsigned(chunks), kc::kCsThreads, cross_small_smem(tot.max_r),
                                  h->stream>>>(ca);
