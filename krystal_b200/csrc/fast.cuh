@@ -540,32 +540,43 @@ __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSma
     const int nc = min(a.qc, nq - q0);
     for (int i = tid; i < nc * KC_H; i += kCsThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
     __syncthreads();
-    // scores: one (head, key) per thread, head-major so a warp reads one q
-    // slice (a broadcast); the k slice is loaded once for the chunk, and the
+    // scores: two keys of one head per thread (j and j + ceil(R/2)), head-
+    // major so a warp reads one q slice (a broadcast) and each q value feeds
+    // both keys' chains; each k slice is loaded once for the chunk, and the
     // chunk's questions run as independent chains
-    for (int idx = tid; idx < R * KC_HEADS; idx += kCsThreads) {
-      const int head = idx / R, j = idx - head * R, hb = head * KC_HEAD_DIM;
-      const float4* kr = reinterpret_cast<const float4*>(a.mk + (rb + j) * KC_H + hb);
-      float4 k4[KC_HEAD_DIM / 4];
+    const int R2 = (R + 1) >> 1;
+    for (int idx = tid; idx < R2 * KC_HEADS; idx += kCsThreads) {
+      const int head = idx / R2, ja = idx - head * R2, jb = ja + R2, hb = head * KC_HEAD_DIM;
+      const bool two = jb < R;
+      const float4* kra = reinterpret_cast<const float4*>(a.mk + (rb + ja) * KC_H + hb);
+      const float4* krb = reinterpret_cast<const float4*>(a.mk + (rb + (two ? jb : ja)) * KC_H + hb);
+      float sa[kCsChunk], sb[kCsChunk];
 #pragma unroll
-      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) k4[d4] = kr[d4];
-      float sv[kCsChunk];
-#pragma unroll
-      for (int c = 0; c < kCsChunk; c++) sv[c] = 0.f;
-#pragma unroll
-      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++)
+      for (int c = 0; c < kCsChunk; c++) sa[c] = sb[c] = 0.f;
+#pragma unroll 2
+      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+        const float4 x = kra[d4], y = krb[d4];
 #pragma unroll
         for (int c = 0; c < kCsChunk; c++)
           if (c < nc) {
             const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
-            sv[c] = fmaf(q4.x, k4[d4].x, sv[c]);
-            sv[c] = fmaf(q4.y, k4[d4].y, sv[c]);
-            sv[c] = fmaf(q4.z, k4[d4].z, sv[c]);
-            sv[c] = fmaf(q4.w, k4[d4].w, sv[c]);
+            sa[c] = fmaf(q4.x, x.x, sa[c]);
+            sa[c] = fmaf(q4.y, x.y, sa[c]);
+            sa[c] = fmaf(q4.z, x.z, sa[c]);
+            sa[c] = fmaf(q4.w, x.w, sa[c]);
+            sb[c] = fmaf(q4.x, y.x, sb[c]);
+            sb[c] = fmaf(q4.y, y.y, sb[c]);
+            sb[c] = fmaf(q4.z, y.z, sb[c]);
+            sb[c] = fmaf(q4.w, y.w, sb[c]);
           }
+      }
 #pragma unroll
       for (int c = 0; c < kCsChunk; c++)
-        if (c < nc) at(sc + (c * KC_HEADS + head) * stride, j) = sv[c] * a.scale;
+        if (c < nc) {
+          float* row = sc + (c * KC_HEADS + head) * stride;
+          at(row, ja) = sa[c] * a.scale;
+          if (two) at(row, jb) = sb[c] * a.scale;
+        }
     }
     __syncthreads();
     // softmax rows (question, head): one warp each
