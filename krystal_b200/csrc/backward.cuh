@@ -304,16 +304,16 @@ __global__ void __launch_bounds__(256) k_weight_grad(const float* __restrict__ d
   const uint64_t l0 = row_off[f], L = row_off[f + 1] - l0;
   double acc[4] = {0.0, 0.0, 0.0, 0.0};
   uint64_t l = 0;
-  for (; l + 4 <= L; l += 4) {  // four rows' loads in flight, each chain still in row order
-    float x[4];
-    float4 dy[4];
+  for (; l + 8 <= L; l += 8) {  // eight rows' loads in flight, each chain still in row order
+    float x[8];
+    float4 dy[8];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
+    for (int u = 0; u < 8; u++) {
       x[u] = X[(l0 + l + u) * KC_H + k];
       dy[u] = *reinterpret_cast<const float4*>(dY + (l0 + l + u) * KC_H + n0);
     }
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
+    for (int u = 0; u < 8; u++) {
       acc[0] = fma(double(dy[u].x), double(x[u]), acc[0]);
       acc[1] = fma(double(dy[u].y), double(x[u]), acc[1]);
       acc[2] = fma(double(dy[u].z), double(x[u]), acc[2]);
