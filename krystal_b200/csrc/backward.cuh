@@ -404,12 +404,12 @@ __global__ void __launch_bounds__(128) k_cross_attn_back_q(CrossBackArgs a) {
   const float* mkc = a.mk + rb * KC_H + tid;
   double acc = 0.0;
   int j = 0;
-  for (; j + 8 <= R; j += 8) {  // eight keys' loads in flight, the chain in key order
-    float kv[8];
+  for (; j + 16 <= R; j += 16) {  // sixteen keys' loads in flight, the chain in key order
+    float kv[16];
 #pragma unroll
-    for (int u = 0; u < 8; u++) kv[u] = mkc[size_t(j + u) * KC_H];
+    for (int u = 0; u < 16; u++) kv[u] = mkc[size_t(j + u) * KC_H];
 #pragma unroll
-    for (int u = 0; u < 8; u++) acc = fma(double(dr[j + u]), double(kv[u]), acc);
+    for (int u = 0; u < 16; u++) acc = fma(double(dr[j + u]), double(kv[u]), acc);
   }
   for (; j < R; j++) acc = fma(double(dr[j]), double(mkc[size_t(j) * KC_H]), acc);
   a.dq[uint64_t(qi) * KC_H + tid] = f32(acc * a.scale);
