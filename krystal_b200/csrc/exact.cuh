@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(kXaThreads, 2) k_cross_attn_exact(CrossAttnArg
       for (int i = 0; i < NK; i++) acc[c][i] = 0.0;
     const double* qp = qd + s_q * KC_H + s_head * KC_HEAD_DIM;
 #pragma unroll 2
-    for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+    for (int d4 = 0; d4 < (s_q < nc ? KC_HEAD_DIM / 4 : 0); d4++) {  // pairs past the chunk's questions: zeros
       float4 k4[NK];
 #pragma unroll
       for (int i = 0; i < NK; i++) {

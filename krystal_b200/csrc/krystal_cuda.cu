@@ -757,10 +757,12 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.qstate), H, Q, m0, W, H, mq, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bk), H, R, m0 + 1, W + uint64_t(H) * H, H, mk, H, H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, P<float>(ws.bv), H, R, m0 + 2, W + 2ull * H * H, H, mv, H, H));
-      // the largest question chunk whose grid still fills two CTAs per SM
-      // (few frames, e.g. the recomputed ones, get smaller chunks)
+      // the smallest question chunk that holds the largest frame's questions,
+      // smaller still while the grid would not fill two CTAs per SM (few
+      // frames, e.g. the recomputed ones)
       const uint32_t mq1 = std::max<uint32_t>(tot.max_q, 1);
       int qc = 16;
+      while (qc > 4 && uint32_t(qc / 2) >= mq1) qc /= 2;
       while (qc > 4 && uint64_t(b.frames) * ((mq1 + qc - 1) / qc) < 2ull * uint64_t(h->sms)) qc /= 2;
       const int chunks = int((mq1 + qc - 1) / qc);
       kc::CrossAttnArgs ca{mq, mk, mv, P<float>(ws.qstate), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
