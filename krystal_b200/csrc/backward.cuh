@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(384) k_value_wv(const float* qout, const float
 // Σ p·(unrounded dot); dScore = f32(p·(dP − rowSum) + policy term), where the
 // policy term is p − onehot for a target, sc·(onehot − p) with
 // sc = pAway / max(1 − pAway, 1e-6) for an AWAY target (bit 31), 0 without.
-// One CTA per question; dynamic shared memory 8 B × max_r.
+// One CTA per question; dynamic shared memory 12 B × max_r (the dot products, then the p row).
 struct SelBackArgs {
   BatchGeo g;
   const float* p;            // [P] policy
@@ -202,6 +202,8 @@ __global__ void __launch_bounds__(256) k_sel_back_scores(SelBackArgs a) {
     a.dag[o] = f32(dl * double(a.wv[2 * KC_H + tid]));
     digs[tid] = vig;
   }
+  float* ps = reinterpret_cast<float*>(s64 + R);  // the question's p row, staged once
+  for (int j = tid; j < R; j += 256) ps[j] = prow[j];
   __syncthreads();
   for (int j = tid; j < R; j += 256) {
     const float* vr = a.bank_values + (rb + j) * KC_H;
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(256) k_sel_back_scores(SelBackArgs a) {
   __syncthreads();
   if (tid == 0) {
     double rs = 0.0;
-    for (int j = 0; j < R; j++) rs = rs + double(prow[j]) * s64[j];
+    for (int j = 0; j < R; j++) rs = rs + double(ps[j]) * s64[j];
     row_sum_s = rs;
   }
   __syncthreads();
@@ -222,10 +224,10 @@ __global__ void __launch_bounds__(256) k_sel_back_scores(SelBackArgs a) {
   const bool valid = raw != KC_INVALID;
   const bool away = valid && raw >= 0x80000000u;
   const uint32_t target = away ? raw - 0x80000000u : raw;
-  const double p_away = away && target < uint32_t(R) ? double(prow[target]) : 0.0;
+  const double p_away = away && target < uint32_t(R) ? double(ps[target]) : 0.0;
   const double sc = away ? p_away / js_max(1.0 - p_away, 1e-6) : 0.0;
   for (int j = tid; j < R; j += 256) {
-    const double pij = prow[j];
+    const double pij = ps[j];
     const double one = uint32_t(j) == target ? 1.0 : 0.0;
     const double pg = !valid ? 0.0 : away ? sc * (one - pij) : pij - one;
     a.dscore[po + j] = f32(pij * (double(f32(s64[j])) - row_sum) + pg);
@@ -242,7 +244,18 @@ __global__ void __launch_bounds__(128) k_sel_back_dq(BatchGeo g, const float* ds
   const float* drow = dscore + g.p_off[f] + (qi - g.q_off[f]) * uint64_t(R);
   const int c = threadIdx.x;
   double acc = 0.0;
-  for (int j = 0; j < R; j++) acc = fma(double(drow[j]), double(sk[(rb + j) * KC_H + c]), acc);
+  int j = 0;
+  for (; j + 8 <= R; j += 8) {  // eight keys' loads in flight, the chain in key order
+    float dv[8], kv[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      dv[u] = drow[j + u];
+      kv[u] = sk[(rb + j + u) * KC_H + c];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = fma(double(dv[u]), double(kv[u]), acc);
+  }
+  for (; j < R; j++) acc = fma(double(drow[j]), double(sk[(rb + j) * KC_H + c]), acc);
   dqp[uint64_t(qi) * KC_H + c] = f32(acc * hscale);
 }
 

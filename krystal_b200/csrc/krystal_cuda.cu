@@ -1311,7 +1311,7 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
     if (Q) {
       kc::SelBackArgs sb{geo, p, bv, h->w + d.off_val, P<float>(bw.dpred), targets, dquery, P<float>(bw.dig),
                          P<float>(bw.dag), P<float>(bw.dscore)};
-      kc::k_sel_back_scores<<<unsigned(Q), 256, size_t(tot.max_r) * 8, h->stream>>>(sb);
+      kc::k_sel_back_scores<<<unsigned(Q), 256, size_t(tot.max_r) * 12, h->stream>>>(sb);
       kc::k_sel_back_dq<<<unsigned(Q), 128, 0, h->stream>>>(geo, P<float>(bw.dscore), P<float>(ws.sk), h_scale,
                                                            P<float>(bw.dqp));
       h->launches += 2;
@@ -1510,6 +1510,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 int(kc::kXsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * (8 + 4)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_sel_back_scores, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(KC_MAX_BANK) * 12))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_back_q, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 48)) ||
       (e = cudaFuncSetAttribute(kc::k_local_attn_back, cudaFuncAttributeMaxDynamicSharedMemorySize,
