@@ -105,7 +105,22 @@ __global__ void __launch_bounds__(128) k_offered_pred(OfferedArgs a) {
   const int d = threadIdx.x;
   float o = 0.0f;
   uint32_t n = 0;
-  for (int j = 0; j < R; j++) {
+  int j = 0;
+  for (; j + 8 <= R; j += 8) {  // eight keys' loads in flight, the running sum in key order
+    float mv[8], bv[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      mv[u] = mrow[j + u];
+      bv[u] = a.bank_values[(rb + j + u) * KC_H + d];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (double(mv[u]) > -1e29) {
+        o = f32(double(o) + double(bv[u]));
+        n++;
+      }
+  }
+  for (; j < R; j++) {
     if (double(mrow[j]) > -1e29) {
       o = f32(double(o) + double(a.bank_values[(rb + j) * KC_H + d]));
       n++;
