@@ -790,7 +790,23 @@ __global__ void __launch_bounds__(256) k_learn_frame_stats(BatchGeo g, const flo
       const float* mrow = mask + pb + i * R;
       uint32_t allowed = 0;
       double e = 0.0;
-      for (uint64_t j = 0; j < R; j++) {
+      uint64_t j = 0;
+      for (; j + 8 <= R; j += 8) {  // eight keys' loads in flight, the sum in key order
+        float mv[8], pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          mv[u] = mrow[j + u];
+          pv[u] = prow[j + u];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          if (double(mv[u]) <= -1e30 / 2) continue;
+          allowed++;
+          const double pj = pv[u];
+          if (pj > 0) e -= pj * log(pj);
+        }
+      }
+      for (; j < R; j++) {
         if (double(mrow[j]) <= -1e30 / 2) continue;
         allowed++;
         const double pj = prow[j];
