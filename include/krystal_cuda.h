@@ -5,7 +5,7 @@
  * through the `BrainBackend` seam (packages/krystal/src/host/backend.ts:
  * 146-180); `@krystal/webgpu` implements it in packages/webgpu/src/
  * backend.ts:91-181. A `@krystal/cuda` adapter binds the functions below
- * through bun:ffi (see INTEGRATION.md) and implements the same seam:
+ * through bun:ffi and implements the same seam:
  *
  *   BrainBackendFactory (backend.ts:177-180)  -> kc_create
  *   BrainBackend.encode (backend.ts:149)      -> kc_encode
@@ -53,11 +53,14 @@ extern "C" {
 
 /* Precision of the batch entry points (kc_forward_batch[_device]).
  * EXACT: the oracle's arithmetic (f64 accumulation in its order, f32 stores).
- * CERTIFIED (default): tensor cores at fp32-class accuracy; every question
- *   whose selection could differ from the exact computation's (top-two score
- *   gap <= tau, a sampled draw within tau of a cumulative edge, non-finite
- *   values) has its frame recomputed on the exact path, so selections match
- *   the exact path and distributions agree to ~1e-6.
+ * CERTIFIED (default): tensor cores at fp32-class accuracy; every score
+ *   carries a margin B_qj = kappa_q * |sq_q| * |sk_j| / sqrt(H) + 4u|s_qj|
+ *   (kappa_q = kappa0 * (1 + sqrt(max_j |s_qj| / 2)), kappa0 = 2e-5, u = 2^-24)
+ *   and every question whose selection those margins cannot settle (the top
+ *   score's interval touching another's, a sampled draw within the cumulative
+ *   p's error of an edge, non-finite values) has its frame recomputed on the
+ *   exact path, so selections match the exact path and distributions agree
+ *   to ~1e-6. The recomputed frames audit the margin (kc_stage_times).
  * FAST: the tensor-core path without the recomputation (diagnostics).
  * kc_backward_batch_device runs its products on the tensor cores at CERTIFIED
  * and FAST (gradients to fp32-class accuracy; the backward makes no discrete
@@ -214,6 +217,15 @@ typedef struct kc_stage_times {
   double enc_attn_tc_ms;
   uint64_t enc_attn_tc_launches;
   double enc_attn_tc_flops, enc_attn_tc_bytes;
+  /* the certificate's audit: every frame recomputed exactly has each fast
+     score compared with its exact score; the largest |s^ - s| / B seen
+     (B the margin the selector allowed), the batches where it exceeded 1
+     (each raises the margin fourfold for later batches), the frames audited,
+     and the base margin kappa0 in force (counted whether or not profiling is on) */
+  double cert_audit_max;
+  uint64_t cert_audit_violations;
+  uint64_t cert_audit_frames;
+  double cert_kappa0;
 } kc_stage_times;
 
 uint32_t kc_abi_version(void);
@@ -442,7 +454,7 @@ const char* kc_stream_last_error(kc_stream* s);
 void kc_stream_destroy(kc_stream* s);
 
 /* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
- * certification margin (default 2e-5, in score units; 0 keeps it). */
+ * certificate's base relative margin kappa0 (default 2e-5; 0 keeps it). */
 kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 
 /* Stream control: run on `stream` (a cudaStream_t; NULL = the handle's own). */

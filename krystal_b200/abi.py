@@ -138,7 +138,9 @@ class KcStageTimes(C.Structure):
         ("enc_gemm_flops", C.c_double), ("fallback_ms", C.c_double), ("fallback_frames", C.c_uint64),
         ("enc_gemm_bytes", C.c_double), ("enc_ffn_ms", C.c_double), ("enc_ffn_launches", C.c_uint64),
         ("enc_ffn_flops", C.c_double), ("enc_ffn_bytes", C.c_double), ("enc_attn_tc_ms", C.c_double),
-        ("enc_attn_tc_launches", C.c_uint64), ("enc_attn_tc_flops", C.c_double), ("enc_attn_tc_bytes", C.c_double)]
+        ("enc_attn_tc_launches", C.c_uint64), ("enc_attn_tc_flops", C.c_double), ("enc_attn_tc_bytes", C.c_double),
+        ("cert_audit_max", C.c_double), ("cert_audit_violations", C.c_uint64), ("cert_audit_frames", C.c_uint64),
+        ("cert_kappa0", C.c_double)]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}

@@ -3,10 +3,14 @@
 // The tensor-core path computes the forward to fp32-class accuracy (split
 // fp16 GEMMs, f32 everywhere else) instead of the oracle's exact f64 order.
 // Its distributions agree with the oracle to ~1e-6; its selections are
-// CERTIFIED: k_select_fast marks a question whose decision could differ from
-// the exact computation's (top-two score gap within tau, a sampled draw within
-// tau_c of a cumulative boundary, anything non-finite), and the frames holding
-// such questions are recomputed on the exact path.
+// CERTIFIED: k_select_fast bounds every score's distance from the exact
+// computation's score by B_qj = kappa_q * scale * |sq_q| * |sk_j| + 4u|s_qj|
+// and marks a question whose decision those bounds cannot settle (the top
+// score's interval touching another's, a sampled draw within the cumulative
+// error of a boundary, anything non-finite); the frames holding such
+// questions are recomputed on the exact path. kappa_q = kappa0 * (1 +
+// sqrt(Lambda_q / lam0)) grows with the question's largest |score| Lambda_q
+// (sharper softmaxes upstream amplify relative errors).
 #pragma once
 #include "common.cuh"
 
@@ -677,13 +681,52 @@ struct SelectFastArgs {
   int qc;           // questions per chunk (the score buffer holds qc x max_r)
   int chunks;       // CTAs per frame: ceil(largest question count / qc)
   float scale;
-  float tau;        // certified argmax: top-two score gap above tau
-  float tau_c;      // certified draw: the uniform farther than tau_c from a cumulative boundary
+  const float* nq;  // [Q] |sq| of each question's projection (k_row_norms)
+  const float* nk;  // [R] |sk| of each bank row's projection
+  float kappa0;     // base relative error of the projections' dot product (see kCertKappa0)
+  float lam0;       // score scale at which the amplification term reaches 1 (see kCertLam0)
+  float* kappa;     // [Q] out: kappa_q, for the audit of recomputed frames
   float* p;
   uint32_t* index;
   uint32_t* flags;  // [frames]
   int scores_in_p;  // the raw dot products are already in p (k_select_scores_fast)
 };
+
+// The certification margin. Fast scores s^ differ from the exact path's s by
+// first-order propagated rounding: the split-fp16 products (each within
+// 3 * 2^-22 of the product, the dropped lo*lo term and the two splits) and the
+// fp32 accumulations of the ~14 projection stages and the f32 attention /
+// pooling / softmax stages on a question's path. Treating the rounding errors
+// as independent and zero-mean (Higham & Mary, SIAM J. Sci. Comput. 41(5),
+// 2019), a stage of inner dimension K contributes a relative row error of
+// about (12 + sqrt(K/2)) u, u = 2^-24; fourteen such stages in quadrature
+// give about 75 u = 4.5e-6 per row; at lambda = 5 standard deviations (a
+// one-sided tail below 3e-7 per score) the rows sq, sk carry relative errors
+// below 2.2e-5. |s^ - s| <= scale (|dsq||sk| + |sq||dsk|) (Cauchy-Schwarz,
+// no credit for the random direction) then gives kappa0 = 2e-5 per score
+// norm product, before the softmax term. Softmaxes with large logits L turn a
+// relative logit error rho into an output change of order rho * L times the
+// distribution's spread; the envelope 1 + sqrt(Lambda_q / lam0) (Lambda_q the
+// question's largest |score|, which grows as the squared activation norm like
+// every logit upstream) covers the measured growth of the error per norm
+// product from 1x to 256x token rows with a margin of 3 or more. The margin
+// is checked at run time: every recomputed frame is audited (k_cert_audit).
+constexpr float kCertKappa0 = 2e-5f;
+constexpr float kCertLam0 = 2.0f;
+constexpr float kCertTie = 9.5367431640625e-07f;  // 2^-20: exact scores this far apart give distinct stored p
+
+// |row| of each [rows, 128] f32 row, one warp per row, rounded up.
+__global__ void __launch_bounds__(256) k_row_norms(const float* __restrict__ x, uint64_t rows,
+                                                   float* __restrict__ out) {
+  const uint64_t r = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const float4 v = reinterpret_cast<const float4*>(x + r * KC_H)[lane];
+  float s = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  // an f32 sum of 128 squares is within 9 * 2^-24 of the true sum; 1 + 2^-19 covers it after the root
+  if (lane == 0) out[r] = sqrtf(s) * 1.0000019073486328f;
+}
 
 // The selector's raw dot products q·k_j (the 128-long fmaf chain in dimension
 // order, as k_select_fast forms them) for long banks: one CTA per chunk of up
@@ -819,8 +862,9 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         for (int o = 16; o; o >>= 1) admitted += __shfl_xor_sync(0xffffffffu, admitted, o);
         reopen = admitted == 0;
       }
-      // scaled, masked scores; per-lane best / second-best (value, first index) and finiteness
-      float b1 = -INFINITY, b2 = -INFINITY;
+      // scaled, masked scores; per-lane best (value, first index), the largest
+      // |score| among admitted keys, and finiteness
+      float b1 = -INFINITY, lam = 0.f;
       uint32_t i1 = KC_INVALID;
       int nonfinite = 0, open = 0;
       for (int j = lane; j < R; j += 32) {
@@ -835,17 +879,35 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
         row[j] = sc;
         nonfinite |= !isfinite(s);
         open |= sc >= -1e29f;
-        if (sc > b1) { b2 = b1; b1 = sc; i1 = uint32_t(j); }
-        else if (sc > b2) b2 = sc;
+        if (m == 0.f) lam = fmaxf(lam, fabsf(sc));
+        if (sc > b1) { b1 = sc; i1 = uint32_t(j); }
       }
-      // warp reduce: top two values, index of the first top, any-open, any-nonfinite
+      // warp reduce: top value, index of the first top, Lambda_q, any-open, any-nonfinite
       for (int o = 16; o; o >>= 1) {
-        const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o), ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o);
         const uint32_t oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
-        if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b2 = fmaxf(b1, ob2); b1 = ob1; i1 = oi1; }
-        else b2 = fmaxf(b2, ob1);
+        if (ob1 > b1 || (ob1 == b1 && oi1 < i1)) { b1 = ob1; i1 = oi1; }
+        lam = fmaxf(lam, __shfl_xor_sync(0xffffffffu, lam, o));
         nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, o);
         open |= __shfl_xor_sync(0xffffffffu, open, o);
+      }
+      // the score bounds B_j: the top's own (bt), the largest s_j + B_j over the
+      // other keys (hi), and the largest B_j (bmax, for draws)
+      const float kap = a.kappa0 * (1.f + sqrtf(lam / a.lam0));
+      const float qn = a.scale * a.nq[qi] * kap;
+      float bt = 0.f, hi = -INFINITY, bmax = 0.f;
+      for (int j = lane; j < R; j += 32) {
+        const float sc = row[j];
+        // + 4u|s|: the f32 roundings of the fast and the exact score, and of the comparison below
+        const float bj = qn * a.nk[rb + j] + 2.384185791015625e-07f * fabsf(sc);
+        if (sc >= -1e29f) bmax = fmaxf(bmax, bj);
+        if (uint32_t(j) == i1) bt = bj;
+        else hi = fmaxf(hi, sc + bj);
+      }
+      for (int o = 16; o; o >>= 1) {
+        bt = fmaxf(bt, __shfl_xor_sync(0xffffffffu, bt, o));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
       }
       // softmax (the all-blocked row keeps p = 0)
       float inv = 0.f;
@@ -868,10 +930,19 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
       if (lane == 0) {
         bool certain = !nonfinite;
         uint32_t best;
+        a.kappa[qi] = kap;
         if (!open) {
           best = KC_INVALID;  // every score below -1e29 on any accurate computation
         } else if (a.uniforms) {
           // sampleRow's inverse CDF; certain when the draw is clear of both edges
+          // by more than the cumulative p can move: each p_j by at most
+          // expm1(2 bmax) relative (its score and the normaliser's log); 8u for
+          // the f32 roundings of e and p in both paths and expf's 2 ulp; the f32
+          // rounding of expf's argument, sum_j p_j |s_j - s_max| u <= u log R
+          // (at most 12u here, 16u allowed); the f32 normalising sum's
+          // (R/32 + 5) u
+          const float tau_c = expm1f(2.f * bmax) +
+                              float((R + 31) / 32 + 5 + 24) * 5.9604644775390625e-08f;
           const double u = a.uniforms[qi];
           double cum = 0.0, prev = 0.0;
           int last = -1, drawn = -2;
@@ -885,20 +956,76 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
           }
           if (drawn == -2) {
             drawn = last;
-            certain = certain && (u - cum > a.tau_c);
+            certain = certain && (u - cum > tau_c);
           } else {
-            certain = certain && (cum - u > a.tau_c) && (u - prev > a.tau_c || drawn == 0);
+            certain = certain && (cum - u > tau_c) && (u - prev > tau_c || drawn == 0);
           }
           // tiny weights near zero may flip between zero and positive
           best = drawn < 0 ? KC_INVALID : uint32_t(drawn);
         } else {
+          // certain when the top score's interval clears every other's by the
+          // tie margin: then the exact scores keep the order and the stored p too
           best = i1;
-          certain = certain && (R == 1 || b1 - b2 > a.tau);
+          certain = certain && (R == 1 || b1 - bt > hi + kCertTie);
         }
         a.index[qi] = best;
         if (!certain) atomicOr(&a.flags[f], 1u);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Audit of the certification margin on the frames recomputed exactly: for
+// every (question, bank row) pair of listed frame list[i] (one CTA each), the
+// fast score (the selector's fmaf chain over the fast projections, scaled in
+// f32) against the exact score (the f64 chain over the exact projections,
+// rounded to f32), as a ratio to the margin B the selector allowed that pair
+// (kappa_q * scale * |sq| * |sk| + 4u|s^|). The largest ratio goes to *out
+// (non-negative float bits, so an unsigned max orders them). Unmasked: the
+// audit measures score error, which the mask does not change.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_cert_audit(
+    const uint32_t* __restrict__ list, const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ r_off,
+    const uint64_t* __restrict__ sub_q_off, const uint64_t* __restrict__ sub_r_off, const float* __restrict__ fsq,
+    const float* __restrict__ fsk, const float* __restrict__ esq, const float* __restrict__ esk,
+    const float* __restrict__ nq, const float* __restrict__ nk, const float* __restrict__ kappa, float scale,
+    double scale_d, unsigned* __restrict__ out) {
+  __shared__ float red[8];
+  const uint32_t f = list[blockIdx.x];
+  const uint64_t qb = q_off[f], rb = r_off[f];
+  const uint64_t Q = q_off[f + 1] - qb, R = r_off[f + 1] - rb;
+  const uint64_t eq = sub_q_off[blockIdx.x], er = sub_r_off[blockIdx.x];
+  float worst = 0.f;
+  for (uint64_t idx = threadIdx.x; idx < Q * R; idx += blockDim.x) {
+    const uint64_t c = idx / R, j = idx % R;
+    const float4* q4 = reinterpret_cast<const float4*>(fsq + (qb + c) * KC_H);
+    const float4* k4 = reinterpret_cast<const float4*>(fsk + (rb + j) * KC_H);
+    float sv = 0.f;
+    for (int d4 = 0; d4 < KC_H / 4; d4++) {
+      const float4 a = q4[d4], b = k4[d4];
+      sv = fmaf(a.x, b.x, sv);
+      sv = fmaf(a.y, b.y, sv);
+      sv = fmaf(a.z, b.z, sv);
+      sv = fmaf(a.w, b.w, sv);
+    }
+    const float fs = sv * scale;
+    const float* eqr = esq + (eq + c) * KC_H;
+    const float* ekr = esk + (er + j) * KC_H;
+    double dv = 0.0;
+    for (int d = 0; d < KC_H; d++) dv = fma(double(eqr[d]), double(ekr[d]), dv);
+    const float es = __double2float_rn(dv * scale_d);
+    const float bound = kappa[qb + c] * scale * nq[qb + c] * nk[rb + j] + 2.384185791015625e-07f * fabsf(fs);
+    const float r = fabsf(fs - es) / bound;
+    if (r == r) worst = fmaxf(worst, r);  // a non-finite score was never certified
+  }
+  for (int o = 16; o; o >>= 1) worst = fmaxf(worst, __shfl_xor_sync(0xffffffffu, worst, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = worst;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+    atomicMax(out, __float_as_uint(m));
   }
 }
 

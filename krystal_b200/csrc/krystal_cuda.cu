@@ -107,6 +107,8 @@ struct Workspace {
   DevBuf rows_val, rows_off;
   // certification flags per frame, and the list of frames to recompute
   DevBuf flags, list;
+  // the certificate's inputs: |sq|, |sk| per row and kappa_q per question
+  DevBuf nq, nk, kappa;
 };
 
 // The backward's buffers: what the forward saves for it (per block), the
@@ -204,7 +206,12 @@ struct kc_handle {
   bool fuse = true;
   // precision
   int precision = KC_PRECISION_CERTIFIED;
-  float tau = 2e-5f, tau_c = 2e-5f;
+  // the certification margin: kappa0 (kc_set_precision may set it) times
+  // kappa_mul, which the audit of recomputed frames raises after a violation
+  float kappa0 = kc::kCertKappa0, kappa_mul = 1.0f;
+  float* d_audit = nullptr;         // [1] largest |s^ - s| / B over the last batch's recomputed pairs (float bits)
+  float* h_audit = nullptr;         // pinned copy
+  bool audit_pending = false;       // h_audit holds an unread audit
   int sa = 10;                      // activations are split at x * 2^sa
   std::vector<Mat> mats;
   std::vector<float> mat_max;       // max |W| per matrix (host side, from the last sync)
@@ -633,6 +640,9 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
   KC_TRY(ensure(ws.p, PP * 4), "workspace");
   KC_TRY(ensure(ws.index, Q * 4), "workspace");
   KC_TRY(ensure(ws.flags, F * 4ull), "workspace");
+  KC_TRY(ensure(ws.nq, Q * 4), "workspace");
+  KC_TRY(ensure(ws.nk, R * 4), "workspace");
+  KC_TRY(ensure(ws.kappa, Q * 4), "workspace");
   {
     ProfScope ps(h, kStPack);
     kc::k_record_rows<256><<<F, 256, 0, h->stream>>>(
@@ -800,8 +810,17 @@ void launch_select_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
   sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
   sa.chunks = int((std::max<uint32_t>(tot.max_q, 1) + sa.qc - 1) / sa.qc);
   sa.scale = float(1.0 / std::sqrt(double(h->d.h)));
-  sa.tau = h->tau; sa.tau_c = h->tau_c;
+  sa.nq = P<float>(ws.nq); sa.nk = P<float>(ws.nk); sa.kappa = P<float>(ws.kappa);
+  sa.kappa0 = h->kappa0 * h->kappa_mul; sa.lam0 = kc::kCertLam0;
   sa.p = P<float>(ws.p); sa.index = P<uint32_t>(ws.index); sa.flags = P<uint32_t>(ws.flags);
+  if (tot.q) {
+    kc::k_row_norms<<<unsigned((tot.q + 7) / 8), 256, 0, h->stream>>>(sa.sq, tot.q, P<float>(ws.nq));
+    h->launches++;
+  }
+  if (tot.r) {
+    kc::k_row_norms<<<unsigned((tot.r + 7) / 8), 256, 0, h->stream>>>(sa.sk, tot.r, P<float>(ws.nk));
+    h->launches++;
+  }
   sa.scores_in_p = tot.max_r > uint32_t(kc::kCsMaxBank);
   if (sa.scores_in_p) {  // long banks: the dot products for 16-question chunks, the bank read once per chunk
     const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kSsChunk - 1) / kc::kSsChunk);
@@ -914,11 +933,28 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   return KC_OK;
 }
 
+// Takes up the audit of the last recomputation: the largest ratio of a
+// fast score's distance from its exact score to the margin B that the
+// selector allowed it. Above 1 the margin was too small for this data: the
+// violation is counted and later batches run with four times the margin.
+void audit_collect(kc_handle* h) {
+  if (!h->audit_pending) return;
+  cudaStreamSynchronize(h->stream);
+  h->audit_pending = false;
+  const float r = *h->h_audit;
+  h->prof.cert_audit_max = std::max(h->prof.cert_audit_max, double(r));
+  if (r > 1.0f) {
+    h->prof.cert_audit_violations++;
+    h->kappa_mul = std::min(h->kappa_mul * 4.0f, 65536.0f);
+  }
+}
+
 // Recompute on the exact path every frame the fast selector could not
 // certify (or all of them after a split overflow), then scatter the exact
 // p blocks and indices into the batch's outputs.
 kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
   const uint32_t F = b.frames;
+  audit_collect(h);
   if (h->h_flags_cap < F) {
     if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
     h->h_flags_pinned = nullptr;
@@ -987,6 +1023,19 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   kc::FrameTotals sub_tot;
   KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
+  // audit the margin on the recomputed frames: the fast scores against the exact ones
+  KC_TRY(cudaMemsetAsync(h->d_audit, 0, sizeof(float), h->stream), "memset");
+  kc::k_cert_audit<<<n, 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+                                             P<uint64_t>(fb.q_off), P<uint64_t>(fb.r_off), P<float>(ws.sq),
+                                             P<float>(ws.sk), P<float>(fb.sq), P<float>(fb.sk), P<float>(ws.nq),
+                                             P<float>(ws.nk), P<float>(ws.kappa),
+                                             float(1.0 / std::sqrt(double(h->d.h))),
+                                             1.0 / std::sqrt(double(h->d.h)),
+                                             reinterpret_cast<unsigned*>(h->d_audit));
+  h->launches++;
+  KC_TRY(cudaMemcpyAsync(h->h_audit, h->d_audit, sizeof(float), cudaMemcpyDeviceToHost, h->stream), "readback");
+  h->audit_pending = true;
+  h->prof.cert_audit_frames += n;
   kc::k_fallback_scatter<<<dim3(n, 32), 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.p_off),
                                                    P<uint64_t>(ws.q_off), P<uint64_t>(fb.p_off),
                                                    P<uint64_t>(fb.q_off), P<float>(fb.p), P<uint32_t>(fb.index),
@@ -1471,6 +1520,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   if ((e = cudaMallocHost(&h->h_tot, sizeof(kc::FrameTotals)))) return bail(e, "pinned");
   if ((e = cudaMallocHost(&h->h_err, sizeof(int)))) return bail(e, "pinned");
   if ((e = cudaMalloc(&h->d_err, sizeof(int)))) return bail(e, "error word");
+  if ((e = cudaMallocHost(&h->h_audit, sizeof(float)))) return bail(e, "pinned");
+  if ((e = cudaMalloc(&h->d_audit, sizeof(float)))) return bail(e, "audit word");
   if ((e = cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device))) return bail(e, "attributes");
   h->mats = mat_list(h->d);
   h->mat_max.assign(h->mats.size(), 0.f);
@@ -1673,7 +1724,8 @@ extern "C" kc_status kc_select_noalloc(kc_handle* h, uint32_t q, uint32_t r, con
                                        float* p, uint32_t* index, float* gather) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
-  h->ws_epoch++;  // the resident batch (kc_select_batch) is gone
+  // no ws_epoch bump: this entry point never touches the handle's workspace,
+  // so a batch resident for kc_select_batch stays usable
   DeviceGuard dg(h->device);
   if (q > kNoAllocMaxQ || r > kNoAllocMaxR) {
     char buf[160];
@@ -2107,13 +2159,15 @@ kc_status kc_set_precision(kc_handle* h, int mode, float tau) {
     return fail(h, KC_ERR_INVALID_ARG, "unknown precision mode");
   if (tau < 0.f || !(tau == tau)) return fail(h, KC_ERR_INVALID_ARG, "tau must be a non-negative number");
   h->precision = mode;
-  if (tau > 0.f) h->tau = h->tau_c = tau;
+  if (tau > 0.f) h->kappa0 = tau;
   return KC_OK;
 }
 
 kc_status kc_set_stream(kc_handle* h, void* stream) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  audit_collect(h);  // its readback is queued on the old stream
   h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own;
   return KC_OK;
 }
@@ -2140,8 +2194,10 @@ kc_status kc_profile_read(kc_handle* h, kc_stage_times* out, int reset) {
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard dg(h->device);
   prof_collect(h);
+  audit_collect(h);
   *out = h->prof;
   out->launches = h->launches;
+  out->cert_kappa0 = double(h->kappa0) * h->kappa_mul;
   if (reset) h->prof = kc_stage_times{};
   return KC_OK;
 }
@@ -2184,6 +2240,8 @@ void kc_destroy(kc_handle* h) {
       if (b->p) cudaFree(b->p);
     if (h->d_err) cudaFree(h->d_err);
     if (h->h_err) cudaFreeHost(h->h_err);
+    if (h->d_audit) cudaFree(h->d_audit);
+    if (h->h_audit) cudaFreeHost(h->h_audit);
     if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
     for (auto& pr : h->ev_pool) {
       cudaEventDestroy(pr.first);
