@@ -98,6 +98,8 @@ def parse_args():
     ap.add_argument("--device-only", action="store_true",
                     help="time only the device-resident leg (for profiler captures of the same kernels)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the other configurations' figures after the headline (one GPU only)")
     ap.add_argument("--precision", choices=["certified", "exact", "fast"], default="certified",
                     help="certified: tensor cores + exact recomputation of uncertain frames (the product default)")
     return ap.parse_args()
@@ -244,7 +246,7 @@ def learn_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def learn_main(args) -> None:
+def learn_main(args) -> dict | None:
     """The learn step (forward + backward + update) over one global batch split
     into contiguous frame shards, one per rank; the gradient sums cross NVLink
     in one NCCL all-reduce per step (strong scaling: the batch is fixed)."""
@@ -340,6 +342,7 @@ def learn_main(args) -> None:
 
     ms_e2e = None if args.device_only else timed(e2e_step)
     rep = step(d_in)
+    line = None
     if rank == 0:
         peaks, peaks_kind = load_peaks()
         value = F * args.steps / (ms / 1e3)
@@ -383,10 +386,10 @@ def learn_main(args) -> None:
                            "entry": "learn step from pinned host inputs"}
         if clk:
             line["clocks"] = clk
-        print(json.dumps(line), flush=True)
     be.destroy()
     if world > 1:
         dist.destroy_process_group()
+    return line
 
 
 def stream_run(st, batch, arrivals_ms, max_batch_frames: int) -> tuple[np.ndarray, float, int]:
@@ -451,7 +454,7 @@ def batch_stats(batches) -> dict:
                 0.0, sealed[1:] - done[:-1]).sum()) if len(batches) > 1 else 0.0}
 
 
-def stream_main(args) -> None:
+def stream_main(args) -> dict | None:
     """The interactive stream: 100k frames (records 8-512, questions 1-32) of
     Poisson-arriving sizes, dispatched round-robin to the ranks, each packing
     its arrivals into rolling batches on its GPU through the streaming packer."""
@@ -515,6 +518,7 @@ def stream_main(args) -> None:
     else:
         every = mine_t.cpu().numpy()
     every = every[~np.isnan(every)]
+    line = None
     if rank == 0:
         offs = batch.offsets()
         line = {
@@ -545,27 +549,73 @@ def stream_main(args) -> None:
         }
         if clk:
             line["clocks"] = clk
-        print(json.dumps(line), flush=True)
     st.close()
     be.destroy()
     if world > 1:
         dist.destroy_process_group()
+    return line
 
 
 def main():
     args = parse_args()
-    if args.workload.startswith("stream"):
-        if args.impl == "reference":
-            reference_arm(args)
-        else:
-            stream_main(args)
-        return
-    if args.workload.startswith("learn"):
-        (learn_reference_arm if args.impl == "reference" else learn_main)(args)
-        return
     if args.impl == "reference":
-        reference_arm(args)
+        (learn_reference_arm if args.workload.startswith("learn") else reference_arm)(args)
         return
+    if args.workload.startswith("stream"):
+        line = stream_main(args)
+    elif args.workload.startswith("learn"):
+        line = learn_main(args)
+    else:
+        line = forward_main(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if line is not None and world == 1 and args.workload == "ragged_4096" and not args.device_only \
+            and not args.no_side:
+        line["side"] = side_legs(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def side_legs(args) -> dict:
+    """The other configurations on this GPU, after the headline: the
+    long-bank batch (1024 frames x 4096 bank + 64 questions), the headline
+    batch at exact precision (the oracle's f64 arithmetic), the learn step
+    (1024 frames) and the interactive stream (100k frames). Each leg times
+    its own warm-up and steps with CUDA events (the stream: host steady
+    clock) and samples its own clocks."""
+    import copy
+
+    def leg(workload, precision="certified", device_only=False):
+        a = copy.copy(args)
+        a.workload, a.precision, a.frames, a.device_only = workload, precision, None, device_only
+        a.steps, a.warmup = min(args.steps, 5), max(3, min(args.warmup, 3))
+        return a
+
+    def summary(line, keys=("metric", "value", "unit", "ms_per_step", "steps", "warmup", "questions_per_sec",
+                            "fallback_frames_per_step", "dtype", "scaling")):
+        if line is None:
+            return None
+        out = {k: line[k] for k in keys if k in line}
+        out["config"] = {k: v for k, v in line.get("config", {}).items() if k != "l2"}
+        for k in ("e2e", "clocks", "latency", "saturation"):
+            if k in line:
+                out[k] = line[k]
+        if "roofline" in line:
+            out["roofline"] = {k: line["roofline"].get(k) for k in ("kernel", "achieved", "unit", "frac", "launch_ms")}
+        if "stage_ms_per_step" in line:
+            out["stage_ms_per_step"] = line["stage_ms_per_step"]
+        return out
+
+    side = {}
+    side["long_bank_1024"] = summary(forward_main(leg("long_bank_1024"), side=True))
+    side["exact_ragged_4096"] = summary(forward_main(leg("ragged_4096", "exact", device_only=True), side=True))
+    side["learn_1024"] = summary(learn_main(leg("learn_1024")))
+    side["stream_100k"] = summary(stream_main(leg("stream_100k")))
+    return side
+
+
+def forward_main(args, side: bool = False) -> dict | None:
+    """The packed ragged batch forward (pack, encode, select) of args.workload;
+    side=True skips the single-frame latency and the CPU baseline."""
     import torch
     import torch.distributed as dist
 
@@ -688,20 +738,22 @@ def main():
         if clk:
             line["clocks"] = clk
     if not args.device_only:
-        e2e = e2e_leg(be, batch, stream, args, dev, world)
+        e2e = e2e_leg(be, batch, stream, args, dev, world, reselect=not side)
         if rank == 0:
             line["e2e"] = e2e
-            line["latency"] = latency_leg(be, stream, dev)
-            from oracle import oracle as O  # noqa: F401  (cpu baseline below)
-            line["cpu_baseline"] = cpu_baseline(cfg, w, wl, frames, seed=7, budget_s=args.cpu_seconds)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+            if not side:
+                line["latency"] = latency_leg(be, stream, dev)
+                from oracle import oracle as O  # noqa: F401  (cpu baseline below)
+                line["cpu_baseline"] = cpu_baseline(cfg, w, wl, frames, seed=7, budget_s=args.cpu_seconds)
     be.destroy()
+    del d_in, d_off, flush
+    torch.cuda.empty_cache()
     if world > 1:
         dist.destroy_process_group()
+    return line
 
 
-def e2e_leg(be, batch, stream, args, dev, world) -> dict:
+def e2e_leg(be, batch, stream, args, dev, world, reselect: bool = True) -> dict:
     """kc_forward_batch with pinned host buffers: H2D, compute, D2H per step."""
     import torch
     import torch.distributed as dist
@@ -736,6 +788,11 @@ def e2e_leg(be, batch, stream, args, dev, world) -> dict:
     sec = float(t.item()) / 1e3
     h2d = sum(a.nbytes for a in (hb.rec_off, hb.token_ids, hb.field_roles, hb.schema_ids, hb.band_ids))
     d2h = res["p"].nbytes + res["index"].nbytes + 2 * (batch.frames + 1) * 8
+    out = {"value": world * batch.frames * args.steps / sec, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h),
+           "entry": "kc_forward_batch (host buffers, pinned inputs and reused pinned outputs)"}
+    if not reselect:
+        return out
     # consider once, choose many: the resident batch decided again under
     # alternating per-question mask rules (kc_select_batch), host results
     from krystal_b200.backend import MaskRule
@@ -754,9 +811,7 @@ def e2e_leg(be, batch, stream, args, dev, world) -> dict:
     torch.cuda.synchronize(dev)
     rms = r0.elapsed_time(r1) / reps
     nq = int(offs["q_off"][-1])
-    return {"value": world * batch.frames * args.steps / sec, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h),
-            "entry": "kc_forward_batch (host buffers, pinned inputs and reused pinned outputs)",
+    return {**out,
             "reselect": {"entry": "kc_select_batch (the resident batch, a new per-question mask rule; "
                                   "certified, results to host)", "ms": rms, "questions_per_sec": nq / (rms / 1e3),
                          "rule_bytes": int(rules[0].schema_allow.nbytes + rules[0].band_allow.nbytes)}}

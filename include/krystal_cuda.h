@@ -373,6 +373,54 @@ kc_status kc_learn_frame_stats(kc_handle* h, const uint32_t* targets, double* st
  * several GPUs, these per-rank sums are what an all-reduce adds. */
 kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* value_weight, double* sums);
 
+/* The update half of learnFromExperience (host/learn.ts:318-512) on the
+ * device, in stream order, so that a learn step needs no host round trip
+ * between the backward and the next forward. All pointers are DEVICE
+ * pointers unless named host. The options are LearnOptions (learn.ts:61-139)
+ * with the reference's defaults (:292-299): learning_rate 0.05, policy_scale
+ * 1, advantage_clip 3, max_parameter_abs +inf, token_rate 0.1 (unfreeze.
+ * tokenRate), unfreeze_pool / unfreeze_tokens 0. */
+typedef struct kc_learn_options {
+  double learning_rate, policy_scale, advantage_clip, max_parameter_abs, token_rate;
+  int32_t unfreeze_pool, unfreeze_tokens;
+} kc_learn_options;
+#define KC_LEARN_ROW 10    /* the KC_LEARN_STATS readings, the reward (NaN = none), answered (0 / 1) */
+#define KC_LEARN_REPORT 9  /* seen, actor moved, reinforced, discouraged, mean advantage, mean value loss,
+                              mean entropy, mean confidence, frames pending */
+#define KC_LEARN_RESULT 19 /* applied, rejected (0 none, 1 "non-finite", 2 "parameter-limit"), finite, health
+                              maxima (table rows, selector, value head, pool, selector Wq, selector Wk),
+                              table rows touched, then the plan's KC_LEARN_REPORT values */
+/* The plan (learn.ts:318-470) over every frame of a batch in frame order —
+ * with several GPUs, the all-gathered rows of every rank, so that every rank
+ * plans the same update: rows [frames, KC_LEARN_ROW] f64 -> step,
+ * value_weight (kc_learn_accumulate's weights) and pending (the frames whose
+ * gradients the actor takes) [frames] f64, report [KC_LEARN_REPORT] f64.
+ * Every sum is a running sum in frame order, as the reference's loop. */
+kc_status kc_learn_plan(kc_handle* h, const double* rows, uint32_t frames, const kc_learn_options* options,
+                        double* step, double* value_weight, double* pending, double* report);
+/* Unfrozen tables (scatterEmbeddings, learn.ts:242-263, as one sum per
+ * row): over the last batch differentiated (whose token_ids / field_roles
+ * are passed again), row_sums [token_space + field_space, H] f64 gain
+ * step[f] * dFieldStates of every token of a pending frame at its token row
+ * and at token_space + its field row; touched [token_space + field_space]
+ * is set to 1 for those rows. Both must start at zero; several GPUs add
+ * them with one all-reduce. step / pending: this rank's frames. */
+kc_status kc_learn_accumulate_rows(kc_handle* h, const uint32_t* token_ids, const uint32_t* field_roles,
+                                   const double* step, const double* pending, double* row_sums, double* touched);
+/* The update itself on the device's weight page (learn.ts:427-470) from the
+ * (all-reduced) sums of kc_learn_accumulate, and of kc_learn_accumulate_rows
+ * when unfreeze_tokens (else NULL), and kc_learn_plan's report; then
+ * parameterHealth (:187-205), the rejection rule and the rollback
+ * (:477-495). Waits for the device; result (HOST, [KC_LEARN_RESULT] f64)
+ * reports it, its health that of the arrays as left, followed by a copy of
+ * the report. The weights the caller
+ * holds on the host are not touched: read them back with kc_copy_weights. */
+kc_status kc_learn_apply(kc_handle* h, const double* sums, const double* row_sums, const double* touched,
+                         const double* report, const kc_learn_options* options, double* result);
+/* count floats of the device weight page from offset (createBrainForwardWeights
+ * order) into host memory; waits for the device. */
+kc_status kc_copy_weights(kc_handle* h, uint64_t offset, uint64_t count, float* host);
+
 /* KRY1 checkpoints (host/checkpoint.ts:17-116): 11 little-endian u32 header
  * words (magic "KRY1" = 0x4b525931, version 1, hiddenSize, ffnSize,
  * encoderBlocks, mixerBlocks, headCount, headDim, routeKindCount, tokenRows
@@ -456,6 +504,19 @@ void kc_stream_destroy(kc_stream* s);
 /* Precision of the batch entry points (KC_PRECISION_*); tau > 0 also sets the
  * certificate's base relative margin kappa0 (default 2e-5; 0 keeps it). */
 kc_status kc_set_precision(kc_handle* h, int mode, float tau);
+
+/* Test hook for the failure path, no counterpart in the reference: the next
+ * launch of one tensor-core kernel (KC_INJECT_ATTN: the fused encoder
+ * attention; KC_INJECT_FFN: the fused feed-forward; KC_INJECT_GEMM: the
+ * projection GEMM) behaves as if its producer's first bounded wait had
+ * expired, before it issues any copy: the kernel raises the error word,
+ * every warp role leaves, TMEM is freed, and the batch call returns
+ * KC_ERR_TIMEOUT with kc_last_error naming the expired wait. One shot; the
+ * handle stays usable. Nothing faults or hangs: no wait actually runs out. */
+#define KC_INJECT_ATTN 0
+#define KC_INJECT_FFN 1
+#define KC_INJECT_GEMM 2
+kc_status kc_inject_wait_expiry(kc_handle* h, int kernel);
 
 /* Stream control: run on `stream` (a cudaStream_t; NULL = the handle's own). */
 kc_status kc_set_stream(kc_handle* h, void* stream);

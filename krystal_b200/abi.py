@@ -25,6 +25,7 @@ KC_NO_SELECTION = 0xFFFFFFFF
 KC_PRECISION_EXACT = 0
 KC_PRECISION_CERTIFIED = 1
 KC_PRECISION_FAST = 2
+KC_INJECT_ATTN, KC_INJECT_FFN, KC_INJECT_GEMM = 0, 1, 2  # kc_inject_wait_expiry (test hook)
 KC_MAX_BANK = 4096
 KC_NO_TARGET = 0xFFFFFFFF
 KC_AWAY_TARGET = 0x80000000
@@ -40,7 +41,9 @@ EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "
            "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
            "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_pending",
            "kc_stream_poll", "kc_stream_clock_ms", "kc_stream_last_error", "kc_stream_destroy",
-           "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch")
+           "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch",
+           "kc_inject_wait_expiry", "kc_learn_plan", "kc_learn_accumulate_rows", "kc_learn_apply",
+           "kc_copy_weights")
 
 
 class KrystalCudaError(RuntimeError):
@@ -125,6 +128,15 @@ class KcBackwardResult(C.Structure):
                 ("total_r", C.c_uint64), ("total_t", C.c_uint64)]
 
 
+class KcLearnOptions(C.Structure):
+    _fields_ = [("learning_rate", C.c_double), ("policy_scale", C.c_double), ("advantage_clip", C.c_double),
+                ("max_parameter_abs", C.c_double), ("token_rate", C.c_double), ("unfreeze_pool", C.c_int32),
+                ("unfreeze_tokens", C.c_int32)]
+
+
+KC_LEARN_ROW, KC_LEARN_REPORT, KC_LEARN_RESULT = 10, 9, 19
+
+
 class KcStreamResult(C.Structure):
     _fields_ = [("first_ticket", C.c_uint64), ("frames", C.c_uint32), ("questions", C.c_uint64),
                 ("total_p", C.c_uint64), ("p_off", P), ("q_off", P), ("p", P), ("index", P), ("status", C.c_int),
@@ -172,10 +184,15 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_forward_batch_device.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(KcDeviceResult)]
     lib.kc_select_noalloc.argtypes = [P, C.c_uint32, C.c_uint32, P, P, P, P, P, P, P]
     lib.kc_set_precision.argtypes = [P, C.c_int, C.c_float]
+    lib.kc_inject_wait_expiry.argtypes = [P, C.c_int]
     lib.kc_backward.argtypes = [P, C.POINTER(KcFrameView), P, P, i, C.c_double, C.POINTER(KcBackwardOut)]
     lib.kc_backward_batch_device.argtypes = [P, C.POINTER(KcBatchView), P, P, P, C.POINTER(KcBackwardResult)]
     lib.kc_learn_frame_stats.argtypes = [P, P, P]
     lib.kc_learn_accumulate.argtypes = [P, P, P, P]
+    lib.kc_learn_plan.argtypes = [P, P, C.c_uint32, C.POINTER(KcLearnOptions), P, P, P, P]
+    lib.kc_learn_accumulate_rows.argtypes = [P, P, P, P, P, P, P]
+    lib.kc_learn_apply.argtypes = [P, P, P, P, P, C.POINTER(KcLearnOptions), P]
+    lib.kc_copy_weights.argtypes = [P, C.c_uint64, C.c_uint64, P]
     lib.kc_stream_create.argtypes = [P, C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint32, C.POINTER(P)]
     lib.kc_stream_push.argtypes = [P, C.POINTER(KcFrameView), P, P, C.POINTER(C.c_uint64)]
     lib.kc_stream_push_many.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]
@@ -207,7 +224,9 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
                  "kc_set_stream", "kc_synchronize", "kc_profile", "kc_profile_read", "kc_select_noalloc",
                  "kc_set_precision", "kc_backward", "kc_backward_batch_device", "kc_learn_frame_stats",
                  "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_poll",
-                 "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch"):
+                 "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch",
+                 "kc_inject_wait_expiry", "kc_learn_plan", "kc_learn_accumulate_rows", "kc_learn_apply",
+                 "kc_copy_weights"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

@@ -234,6 +234,33 @@ class CudaBrainBackend:
         """kc_learn_accumulate over the last batch differentiated (device pointers)."""
         abi.check(self._lib.kc_learn_accumulate(self._h, step, value_weight, sums), self._h)
 
+    def learn_plan(self, rows: int, frames: int, options: abi.KcLearnOptions, step: int, value_weight: int,
+                   pending: int, report: int) -> None:
+        """kc_learn_plan (device pointers)."""
+        abi.check(self._lib.kc_learn_plan(self._h, rows, frames, C.byref(options), step, value_weight, pending,
+                                          report), self._h)
+
+    def learn_accumulate_rows(self, token_ids: int, field_roles: int, step: int, pending: int, row_sums: int,
+                              touched: int) -> None:
+        """kc_learn_accumulate_rows over the last batch differentiated (device pointers)."""
+        abi.check(self._lib.kc_learn_accumulate_rows(self._h, token_ids, field_roles, step, pending, row_sums,
+                                                     touched), self._h)
+
+    def learn_apply(self, sums: int, row_sums: int | None, touched: int | None, report: int,
+                    options: abi.KcLearnOptions) -> np.ndarray:
+        """kc_learn_apply: the update on the device's weight page; returns the
+        KC_LEARN_RESULT values (host)."""
+        out = np.zeros(abi.KC_LEARN_RESULT, np.float64)
+        abi.check(self._lib.kc_learn_apply(self._h, sums, row_sums, touched, report, C.byref(options),
+                                           out.ctypes.data), self._h)
+        return out
+
+    def copy_weights(self, offset: int, out: np.ndarray) -> None:
+        """The device weight page from `offset` into the float32 array `out`."""
+        if out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous float32 array")
+        abi.check(self._lib.kc_copy_weights(self._h, offset, out.size, out.ctypes.data), self._h)
+
     def load_checkpoint(self, data) -> str | None:
         """A KRY1 checkpoint straight into the device weight page
         (kc_load_checkpoint); None when taken up, else the refusal."""
@@ -375,6 +402,10 @@ class CudaBrainBackend:
     def set_stream(self, stream_ptr: int | None) -> None:
         abi.check(self._lib.kc_set_stream(self._h, stream_ptr), self._h)
 
+    def stream_ptr(self) -> int:
+        """The cudaStream_t the handle launches on (kc_get_stream)."""
+        return int(self._lib.kc_get_stream(self._h) or 0)
+
     def synchronize(self) -> None:
         abi.check(self._lib.kc_synchronize(self._h), self._h)
 
@@ -384,6 +415,14 @@ class CudaBrainBackend:
                  "fast": abi.KC_PRECISION_FAST}
         m = modes[mode] if isinstance(mode, str) else int(mode)
         abi.check(self._lib.kc_set_precision(self._h, m, float(tau)), self._h)
+
+    def inject_wait_expiry(self, kernel: str) -> None:
+        """Test hook (kc_inject_wait_expiry): the next launch of the named
+        tensor-core kernel ("attn", "ffn" or "gemm") reports an expired
+        bounded wait before it issues any copy; the batch call then fails
+        with KC_ERR_TIMEOUT and the handle stays usable."""
+        k = {"attn": abi.KC_INJECT_ATTN, "ffn": abi.KC_INJECT_FFN, "gemm": abi.KC_INJECT_GEMM}[kernel]
+        abi.check(self._lib.kc_inject_wait_expiry(self._h, k), self._h)
 
     def profile(self, enable: bool) -> None:
         abi.check(self._lib.kc_profile(self._h, int(enable)), self._h)

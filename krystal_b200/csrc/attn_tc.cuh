@@ -63,6 +63,7 @@ struct AttnTcArgs {
   float word_alpha;
   float scale;                 // 1/sqrt(head dim)
   int* err;
+  int inject_expiry;           // test hook: the producer reports an expired wait before it issues any copy
 };
 
 // Per batch, shared by every encoder block: per row its position in its
@@ -155,6 +156,10 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       uint32_t it = 0, tl = 0;
       bool ok = true;
+      if (a.inject_expiry) {  // as if the first wait had expired: nothing is issued
+        atomicOr(a.err, kErrTimeout);
+        ok = false;
+      }
       for (int k = blockIdx.x; k < a.tiles && ok; k += gridDim.x, tl++) {
         const int row0 = a.tile_row[k];
         if (!mbar_wait(xempty, (tl & 1) ^ 1, a.err)) { ok = false; break; }
@@ -175,9 +180,9 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
       }
       // every copy issued lands before the CTA may exit
       for (uint32_t j = it > uint32_t(kAtWStages) ? it - kAtWStages : 0u; j < it; j++)
-        mbar_wait(&wfull[j % kAtWStages], (j / kAtWStages) & 1, a.err);
+        mbar_wait_drain(&wfull[j % kAtWStages], (j / kAtWStages) & 1);
       if (tl > 0)
-        for (int kc = 0; kc < 2; kc++) mbar_wait(&xraw[kc], (tl - 1) & 1, a.err);
+        for (int kc = 0; kc < 2; kc++) mbar_wait_drain(&xraw[kc], (tl - 1) & 1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -219,7 +224,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
       }
       // every MMA this thread issued completes before TMEM is released
       mma_commit(drain);
-      mbar_wait(drain, 0, a.err);
+      mbar_wait_drain(drain, 0);
     }
     __syncwarp();
   } else if (warp <= 3) {
@@ -427,7 +432,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
       }
     }
     // a residual load left in flight by an expired wait lands before the CTA exits
-    if (issuer && tl > 0) mbar_wait(&rfull[half], 1u, a.err);
+    if (issuer && tl > 0) mbar_wait_drain(&rfull[half], 1u);
   }
 
   tc_fence_before();

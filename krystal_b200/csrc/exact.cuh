@@ -16,8 +16,7 @@ namespace kc {
 
 // ---------------------------------------------------------------------------
 // fieldEmbed (oracle.ts:151-184): x[t] = token + field + schema + band +
-// stream + pos rows, summed in that order in f64, stored f32.
-// 32 compact tokens per warp, float4 per lane (H = 128).
+// stream + pos rows, summed in that order in f64, stored f32 (H = 128).
 // ---------------------------------------------------------------------------
 struct EmbedArgs {
   const uint32_t* tok_recpos;
@@ -30,65 +29,108 @@ struct EmbedArgs {
   uint64_t tb_token, tb_field, tb_schema, tb_band, tb_stream, tb_pos;
   float* x;  // [T,128]
   uint64_t t;
+  uint64_t small_floats;  // floats of the schema..pos tables staged in shared memory (0: read them from global)
 };
 
-// 32 tokens per warp: lane i first resolves token i's rows (the dependent
-// chain record position -> token id -> tokenRows -> table row), so 32 chains
-// are in flight at once; then the warp gathers and sums the six rows of four
-// tokens at a time, lane l owning columns 4l..4l+3.
-constexpr int kEmbedWarps = 8;
+// fieldEmbed (oracle.ts:151-184): x[t] = f32(token + field + schema + band +
+// stream + pos rows, summed in that order in f64). A persistent grid of one
+// CTA per SM. The CTA first stages the small tables in shared memory: the
+// schema rows as f32, the band, stream and position rows already converted
+// to f64 (the f32 -> f64 conversions, not the loads, bound this kernel), so
+// that only the token and field rows are gathered from global memory (L2).
+// Each warp takes 32 tokens at a time: lane i resolves token i's rows (the
+// dependent chain record position -> token id -> tokenRows -> table row), so
+// 32 chains are in flight at once; then the warp gathers the token and field
+// rows of eight tokens at once and sums them with the staged rows, lane l
+// owning columns 4l..4l+3.
+constexpr int kEmbedWarps = 12;
 constexpr int kEmbedTokensPerWarp = 32;
+constexpr uint64_t kEmbedSmemMax = 200u << 10;
 
-__global__ void __launch_bounds__(kEmbedWarps * 32, 2) k_embed_exact(EmbedArgs a) {
+// Shared memory of k_embed_exact for the small tables (0: not staged).
+__host__ __device__ inline uint64_t embed_smem_bytes(uint64_t schema_rows, uint64_t other_rows) {
+  return schema_rows * KC_H * 4 + other_rows * KC_H * 8;
+}
+
+__global__ void __launch_bounds__(kEmbedWarps * 32, 1) k_embed_exact(EmbedArgs a) {
+  extern __shared__ __align__(16) float emb_small[];
+  // staged: schema rows (f32) | band, stream, pos rows (f64), contiguous in the page from tb_band
+  const uint64_t n_schema = a.small_floats ? (a.tb_band - a.tb_schema) : 0;
+  const uint64_t n_other = a.small_floats ? a.small_floats - n_schema : 0;
+  double* emb_d = reinterpret_cast<double*>(emb_small + n_schema);
+  for (uint64_t i = threadIdx.x; i < n_schema / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(emb_small)[i] = reinterpret_cast<const float4*>(a.table + a.tb_schema)[i];
+  for (uint64_t i = threadIdx.x; i < n_other; i += blockDim.x) emb_d[i] = double(a.table[a.tb_band + i]);
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t base = (uint64_t(blockIdx.x) * kEmbedWarps + warp) * kEmbedTokensPerWarp;
-  if (base >= a.t) return;
-  const uint64_t left = a.t - base;
-  const int n = left < kEmbedTokensPerWarp ? int(left) : kEmbedTokensPerWarp;
-  uint32_t tok = 0, role = 0, schema = 0, band = 0, pos = 0;
-  if (lane < n) {
-    const uint32_t rp = a.tok_recpos[base + lane];
-    const uint32_t g = rp >> 3;
-    pos = rp & 7u;
-    tok = a.token_rows[a.token_ids[uint64_t(g) * KC_RW + pos]];
-    role = a.token_rows[a.field_roles[uint64_t(g) * KC_RW + pos]];
-    schema = a.schema_ids[g];
-    band = a.band_ids[g];
-  }
   const int d = lane * 4;
-  auto sum6 = [](float v0, float v1, float v2, float v3, float v4, float v5) {
-    double v = 0.0;
-    v += double(v0); v += double(v1); v += double(v2); v += double(v3); v += double(v4); v += double(v5);
-    return f32(v);
-  };
-  for (int i0 = 0; i0 < n; i0 += 4) {
-    float4 r[4][6];
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int i = i0 + u;  // every lane shuffles; only tokens below n are read
-      const uint32_t ti = __shfl_sync(0xffffffffu, tok, i & 31), ri = __shfl_sync(0xffffffffu, role, i & 31);
-      const uint32_t si = __shfl_sync(0xffffffffu, schema, i & 31), bi = __shfl_sync(0xffffffffu, band, i & 31);
-      const uint32_t li = __shfl_sync(0xffffffffu, pos, i & 31);
-      if (i < n) {
-        const uint32_t stream = bi == KC_QUERY_BAND_ID ? 1u : 0u;
-        r[u][0] = *reinterpret_cast<const float4*>(a.table + a.tb_token + uint64_t(ti) * KC_H + d);
-        r[u][1] = *reinterpret_cast<const float4*>(a.table + a.tb_field + uint64_t(ri) * KC_H + d);
-        r[u][2] = *reinterpret_cast<const float4*>(a.table + a.tb_schema + uint64_t(si) * KC_H + d);
-        r[u][3] = *reinterpret_cast<const float4*>(a.table + a.tb_band + uint64_t(bi) * KC_H + d);
-        r[u][4] = *reinterpret_cast<const float4*>(a.table + a.tb_stream + uint64_t(stream) * KC_H + d);
-        r[u][5] = *reinterpret_cast<const float4*>(a.table + a.tb_pos + uint64_t(li) * KC_H + d);
-      }
+  const uint64_t stride = uint64_t(gridDim.x) * kEmbedWarps * kEmbedTokensPerWarp;
+  for (uint64_t base = (uint64_t(blockIdx.x) * kEmbedWarps + warp) * kEmbedTokensPerWarp; base < a.t;
+       base += stride) {
+    const uint64_t left = a.t - base;
+    const int n = left < kEmbedTokensPerWarp ? int(left) : kEmbedTokensPerWarp;
+    uint32_t tok = 0, role = 0, schema = 0, band = 0, pos = 0;
+    if (lane < n) {
+      const uint32_t rp = a.tok_recpos[base + lane];
+      const uint32_t g = rp >> 3;
+      pos = rp & 7u;
+      tok = a.token_rows[a.token_ids[uint64_t(g) * KC_RW + pos]];
+      role = a.token_rows[a.field_roles[uint64_t(g) * KC_RW + pos]];
+      schema = a.schema_ids[g];
+      band = a.band_ids[g];
     }
+    for (int i0 = 0; i0 < n; i0 += 8) {
+      float4 r[8][2];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int i = i0 + u;
-      if (i >= n) break;
-      float4 o;
-      o.x = sum6(r[u][0].x, r[u][1].x, r[u][2].x, r[u][3].x, r[u][4].x, r[u][5].x);
-      o.y = sum6(r[u][0].y, r[u][1].y, r[u][2].y, r[u][3].y, r[u][4].y, r[u][5].y);
-      o.z = sum6(r[u][0].z, r[u][1].z, r[u][2].z, r[u][3].z, r[u][4].z, r[u][5].z);
-      o.w = sum6(r[u][0].w, r[u][1].w, r[u][2].w, r[u][3].w, r[u][4].w, r[u][5].w);
-      *reinterpret_cast<float4*>(a.x + (base + i) * KC_H + d) = o;
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + u;  // every lane shuffles; only tokens below n are read
+        const uint32_t ti = __shfl_sync(0xffffffffu, tok, i & 31), ri = __shfl_sync(0xffffffffu, role, i & 31);
+        if (i < n) {
+          r[u][0] = *reinterpret_cast<const float4*>(a.table + a.tb_token + uint64_t(ti) * KC_H + d);
+          r[u][1] = *reinterpret_cast<const float4*>(a.table + a.tb_field + uint64_t(ri) * KC_H + d);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + u;
+        const uint32_t si = __shfl_sync(0xffffffffu, schema, i & 31), bi = __shfl_sync(0xffffffffu, band, i & 31);
+        const uint32_t li = __shfl_sync(0xffffffffu, pos, i & 31);
+        if (i >= n) continue;
+        const uint32_t stream = bi == KC_QUERY_BAND_ID ? 1u : 0u;
+        const uint64_t ob = a.tb_band + uint64_t(bi) * KC_H + d, ost = a.tb_stream + uint64_t(stream) * KC_H + d;
+        const uint64_t op = a.tb_pos + uint64_t(li) * KC_H + d, os = a.tb_schema + uint64_t(si) * KC_H + d;
+        float4 s4;
+        double b[4], st[4], p[4];
+        if (n_other) {
+          s4 = *reinterpret_cast<const float4*>(emb_small + (os - a.tb_schema));
+          const double2* b2 = reinterpret_cast<const double2*>(emb_d + (ob - a.tb_band));
+          const double2* st2 = reinterpret_cast<const double2*>(emb_d + (ost - a.tb_band));
+          const double2* p2 = reinterpret_cast<const double2*>(emb_d + (op - a.tb_band));
+          const double2 b01 = b2[0], b23 = b2[1], st01 = st2[0], st23 = st2[1], p01 = p2[0], p23 = p2[1];
+          b[0] = b01.x; b[1] = b01.y; b[2] = b23.x; b[3] = b23.y;
+          st[0] = st01.x; st[1] = st01.y; st[2] = st23.x; st[3] = st23.y;
+          p[0] = p01.x; p[1] = p01.y; p[2] = p23.x; p[3] = p23.y;
+        } else {
+          s4 = *reinterpret_cast<const float4*>(a.table + os);
+          const float4 b4 = *reinterpret_cast<const float4*>(a.table + ob);
+          const float4 st4 = *reinterpret_cast<const float4*>(a.table + ost);
+          const float4 p4 = *reinterpret_cast<const float4*>(a.table + op);
+          b[0] = b4.x; b[1] = b4.y; b[2] = b4.z; b[3] = b4.w;
+          st[0] = st4.x; st[1] = st4.y; st[2] = st4.z; st[3] = st4.w;
+          p[0] = p4.x; p[1] = p4.y; p[2] = p4.z; p[3] = p4.w;
+        }
+        const float tv[4] = {r[u][0].x, r[u][0].y, r[u][0].z, r[u][0].w};
+        const float fv[4] = {r[u][1].x, r[u][1].y, r[u][1].z, r[u][1].w};
+        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          double v = 0.0;
+          v += double(tv[e]); v += double(fv[e]); v += double(sv[e]); v += b[e]; v += st[e]; v += p[e];
+          o[e] = f32(v);
+        }
+        *reinterpret_cast<float4*>(a.x + (base + i) * KC_H + d) = make_float4(o[0], o[1], o[2], o[3]);
+      }
     }
   }
 }

@@ -55,6 +55,7 @@ struct FfnArgs {
   float unscale1;        // 2^-(sa + sw1)
   float unscale2;        // 2^-(sa + sw2)
   int* err;
+  int inject_expiry;  // test hook: the producers report an expired wait before they issue any copy
 };
 
 // Weight chunk c of a tile, in consumption order: P1(0..2) take W1 chunks
@@ -124,6 +125,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      if (a.inject_expiry) {  // as if the first wait had expired: nothing is issued
+        atomicOr(a.err, kErrTimeout);
+        ok = false;
+      }
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         for (int c = 0; c < kFfnChunksPerTile; c++, it++) {
           const int s = it % kFfnWStages;
@@ -137,11 +142,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
       }
       // every copy issued lands before the CTA may exit
       for (uint32_t j = it > uint32_t(kFfnWStages) ? it - kFfnWStages : 0u; j < it; j++)
-        mbar_wait(&wfull[j % kFfnWStages], (j / kFfnWStages) & 1, a.err);
+        mbar_wait_drain(&wfull[j % kFfnWStages], (j / kFfnWStages) & 1);
     } else if (lane == 1) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
       uint32_t tl = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+      for (int t = blockIdx.x; t < tiles && !a.inject_expiry; t += gridDim.x, tl++) {
         if (!mbar_wait(xempty, (tl & 1) ^ 1, a.err)) break;
         for (int kc = 0; kc < 2; kc++) {
           mbar_arrive_expect_tx(&xraw[kc], kFfnChunk);
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
       }
       // the last x issued lands before the CTA may exit
       if (tl > 0)
-        for (int kc = 0; kc < 2; kc++) mbar_wait(&xraw[kc], (tl - 1) & 1, a.err);
+        for (int kc = 0; kc < 2; kc++) mbar_wait_drain(&xraw[kc], (tl - 1) & 1);
     }
     __syncwarp();
   } else if (warp == 5) {
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
       }
       // every MMA this thread issued completes before TMEM is released
       mma_commit(drain);
-      mbar_wait(drain, 0, a.err);
+      mbar_wait_drain(drain, 0);
     }
     __syncwarp();
   } else {
@@ -386,7 +391,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_ffn(const __grid_constant__
     }
     // a residual prefetch left unconsumed by an error lands before the CTA exits
     if (pending >= 0 && lane == 0)
-      for (int b = 0; b < 2; b++) mbar_wait(&cload[wi * 2 + b], uint32_t(pending) & 1, a.err);
+      for (int b = 0; b < 2; b++) mbar_wait_drain(&cload[wi * 2 + b], uint32_t(pending) & 1);
     // every store has left shared memory and landed before the CTA exits
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();

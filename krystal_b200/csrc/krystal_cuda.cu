@@ -30,6 +30,7 @@
 #include "fast.cuh"
 #include "ffn.cuh"
 #include "attn_tc.cuh"
+#include "learn.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 
@@ -37,9 +38,16 @@ namespace {
 
 thread_local std::string g_create_error;
 
+// A grow-only device buffer; it frees its memory when its owner is destroyed.
 struct DevBuf {
   void* p = nullptr;
   size_t cap = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
 };
 
 cudaError_t ensure(DevBuf& b, size_t bytes) {
@@ -120,6 +128,8 @@ struct BackWs {
   DevBuf dquery, dig, dag, dscore, dqp, dkp, dbk, dbv, dswq, dswk;
   DevBuf dh1, ads, mdq, mdk, mdv, tok_ds, dfs, dpool, edqkv;
   DevBuf learn_partial;
+  // the device learn step's rollback copy, health words and readback
+  DevBuf learn_backup, learn_health, learn_out;
   // the last batch differentiated: its frame count and the selection it ran under
   uint32_t frames = 0;
   const float* mask_used = nullptr;
@@ -213,6 +223,9 @@ struct kc_handle {
   float* h_audit = nullptr;         // pinned copy
   bool audit_pending = false;       // h_audit holds an unread audit
   int sa = 10;                      // activations are split at x * 2^sa
+  // test hook (kc_inject_wait_expiry): the next launch of this tensor-core
+  // kernel (KC_INJECT_*) reports an expired wait before it issues any copy
+  int inject = -1;
   std::vector<Mat> mats;
   std::vector<float> mat_max;       // max |W| per matrix (host side, from the last sync)
   std::vector<uint64_t> img_off;    // byte offset of each matrix's image
@@ -420,6 +433,13 @@ int mat_sw(kc_handle* h, int i) {
   return std::min(std::max(sw, -40), 40);
 }
 
+// 1 when the test hook is armed for this kernel (and disarms it).
+int take_injection(kc_handle* h, int kernel) {
+  if (h->inject != kernel) return 0;
+  h->inject = -1;
+  return 1;
+}
+
 // y = A·Wᵀ on the tensor cores for matrix `mat` of mat_list.
 template <int EPI>
 kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, const float* gate = nullptr) {
@@ -430,7 +450,8 @@ kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, c
       !kc::tc::make_c_map(&gmap, gate ? gate : C, M, mt.n, mt.n))
     return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a GEMM operand");
   kc::tc::GemmArgs g{int(M), int(mt.k), int(mt.n / 128), P<uint8_t>(h->images) + h->img_off[mat], C,
-                     int(mt.n), std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat))), h->d_err};
+                     int(mt.n), std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat))), h->d_err,
+                     take_injection(h, KC_INJECT_GEMM)};
   const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
   kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, gmap, g);
@@ -450,7 +471,8 @@ kc_status tc_ffn(kc_handle* h, float* x, uint64_t M, int mat_w1, int mat_w2) {
     return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for the feed-forward operand");
   kc::tc::FfnArgs fa{int(M), P<uint8_t>(h->images) + h->img_off[mat_w1], P<uint8_t>(h->images) + h->img_off[mat_w2],
                      std::ldexp(1.0f, h->sa), std::ldexp(1.0f, -(h->sa + mat_sw(h, mat_w1))),
-                     std::ldexp(1.0f, -(h->sa + mat_sw(h, mat_w2))), h->d_err};
+                     std::ldexp(1.0f, -(h->sa + mat_sw(h, mat_w2))), h->d_err,
+                     take_injection(h, KC_INJECT_FFN)};
   const uint64_t tiles = (M + 127) / 128;
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
   kc::tc::k_tc_ffn<<<grid, kc::tc::kThreadsT, kc::tc::kFfnSmem, h->stream>>>(amap, cmap, fa);
@@ -532,6 +554,7 @@ kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, co
   aa.x = x; aa.tok_recpos = P<uint32_t>(ws.tok_recpos);
   aa.word_ids = word_alpha != 0.0f ? word_ids : nullptr;
   aa.word_alpha = word_alpha; aa.scale = scale; aa.err = h->d_err;
+  aa.inject_expiry = take_injection(h, KC_INJECT_ATTN);
   const unsigned grid = unsigned(std::min<uint64_t>(uint64_t(aa.tiles), uint64_t(h->sms)));
   kc::tc::k_tc_attn<<<grid, kc::tc::kAtThreads, kc::tc::kAtSmem, h->stream>>>(xmap, aa);
   h->launches++;
@@ -699,6 +722,23 @@ void launch_select_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const k
 }
 
 
+// fieldEmbed for the batch's T tokens (k_embed_exact): one CTA per SM, the
+// small tables staged in shared memory when they fit.
+void launch_embed(kc_handle* h, Workspace& ws, const DevBatch& b, float* x, uint64_t T) {
+  const Dims& d = h->d;
+  const uint64_t small = d.tb_pos + uint64_t(d.pos_space) * d.h - d.tb_schema;  // floats, schema..pos
+  const size_t bytes = kc::embed_smem_bytes(d.schema_space, uint64_t(d.band_space) + d.stream_space + d.pos_space);
+  const bool staged = bytes <= kc::kEmbedSmemMax && (d.tb_schema & 3) == 0 && d.h == KC_H;
+  const size_t smem = staged ? bytes : 0;
+  kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
+                   h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
+                   x, T, staged ? small : 0};
+  const uint64_t groups = (T + kc::kEmbedTokensPerWarp - 1) / kc::kEmbedTokensPerWarp;
+  const unsigned blocks = unsigned(std::min<uint64_t>(uint64_t(h->sms), (groups + kc::kEmbedWarps - 1) / kc::kEmbedWarps));
+  kc::k_embed_exact<<<blocks, kc::kEmbedWarps * 32, smem, h->stream>>>(ea);
+  h->launches++;
+}
+
 // The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
 // the workspace: qstate [Q,H], bk/bv [R,H], p, index.
 kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
@@ -710,11 +750,7 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
   float* qkv = P<float>(ws.qkv);
   if (T > 0) {
     ProfScope ps(h, kStEmbed);
-    kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
-                     h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
-                     x, T};
-    kc::k_embed_exact<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(ea);
-    h->launches++;
+    launch_embed(h, ws, b, x, T);
   }
   const double attn_scale = 1.0 / std::sqrt(double(d.hd));
   const double h_scale = 1.0 / std::sqrt(double(H));
@@ -844,11 +880,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   float* qkv = P<float>(ws.qkv);
   if (T > 0) {
     ProfScope ps(h, kStEmbed);
-    kc::EmbedArgs ea{P<uint32_t>(ws.tok_recpos), b.token_ids, b.field_roles, b.schema_ids, b.band_ids,
-                     h->token_rows, h->w, d.tb_token, d.tb_field, d.tb_schema, d.tb_band, d.tb_stream, d.tb_pos,
-                     x, T};
-    kc::k_embed_exact<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(ea);
-    h->launches++;
+    launch_embed(h, ws, b, x, T);
   }
   const float attn_scale = float(1.0 / std::sqrt(double(d.hd)));
   const int enc_m = 0, mix_m = 3 * int(d.enc), sel_m = mix_m + 5 * int(d.mix);
@@ -1541,6 +1573,10 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
+      (e = cudaFuncSetAttribute(kc::k_embed_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kEmbedSmemMax))) ||
+      (e = cudaFuncSetAttribute(kc::k_learn_plan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kPlanSmem))) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_frame, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(cross_shape(kc::kCaBlock).smem))) ||
       (e = cudaFuncSetAttribute(kc::k_cross_attn_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2083,6 +2119,126 @@ kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* va
   return KC_OK;
 }
 
+namespace {
+
+bool learn_opts_ok(const kc_learn_options* o) {
+  return o && o->learning_rate == o->learning_rate && o->policy_scale == o->policy_scale &&
+         o->advantage_clip == o->advantage_clip && o->token_rate == o->token_rate &&
+         !(o->max_parameter_abs != o->max_parameter_abs);
+}
+
+kc::LearnOpts learn_opts(const kc_learn_options* o) {
+  return kc::LearnOpts{o->learning_rate, o->policy_scale, o->advantage_clip, o->max_parameter_abs, o->token_rate,
+                       o->unfreeze_pool ? 1 : 0, o->unfreeze_tokens ? 1 : 0};
+}
+
+}  // namespace
+
+kc_status kc_learn_plan(kc_handle* h, const double* rows, uint32_t frames, const kc_learn_options* o, double* step,
+                        double* value_weight, double* pending, double* report) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if ((frames && (!rows || !step || !value_weight || !pending)) || !report || !learn_opts_ok(o))
+    return fail(h, KC_ERR_INVALID_ARG, "learn plan arguments are incomplete");
+  kc::k_learn_plan<<<1, kc::kPlanThreads, kc::kPlanSmem, h->stream>>>(rows, frames, learn_opts(o), step,
+                                                                       value_weight, pending, report);
+  h->launches++;
+  KC_TRY(cudaGetLastError(), "learn plan");
+  return KC_OK;
+}
+
+kc_status kc_learn_accumulate_rows(kc_handle* h, const uint32_t* token_ids, const uint32_t* field_roles,
+                                   const double* step, const double* pending, double* row_sums, double* touched) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  const uint32_t F = h->bw.frames;
+  if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "no batch has been differentiated on this handle");
+  if (!token_ids || !field_roles || !step || !pending || !row_sums || !touched)
+    return fail(h, KC_ERR_INVALID_ARG, "learn row arguments are incomplete");
+  Workspace& ws = h->ws;
+  uint64_t T = 0;
+  KC_TRY(cudaMemcpyAsync(&T, P<uint64_t>(ws.t_off) + F, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "learn rows");
+  if (T) {
+    const uint64_t warps = (T + 31) / 32;
+    kc::k_learn_rows<<<unsigned((warps + 7) / 8), 256, 0, h->stream>>>(
+        P<uint64_t>(ws.t_off), F, P<uint32_t>(ws.tok_recpos), token_ids, field_roles, h->token_rows, step, pending,
+        P<float>(h->bw.dfs), T, h->d.token_space, row_sums, touched);
+    h->launches++;
+  }
+  KC_TRY(cudaGetLastError(), "learn rows");
+  return KC_OK;
+}
+
+kc_status kc_learn_apply(kc_handle* h, const double* sums, const double* row_sums, const double* touched,
+                         const double* report, const kc_learn_options* o, double* result) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  h->ws_epoch++;  // the weights may change: the resident batch (kc_select_batch) is gone
+  DeviceGuard dg(h->device);
+  if (!sums || !report || !result || !learn_opts_ok(o) || (o->unfreeze_tokens && (!row_sums || !touched)))
+    return fail(h, KC_ERR_INVALID_ARG, "learn apply arguments are incomplete");
+  const Dims& d = h->d;
+  if (d.h != KC_H) return fail(h, KC_ERR_INVALID_ARG, "the device update needs the default hidden size");
+  kc::LearnApplyArgs a{};
+  a.page = h->w;
+  a.off_swq = d.off_swq; a.off_swk = d.off_swk; a.off_val = d.off_val; a.off_pool = d.off_pool;
+  a.tb_token = d.tb_token;
+  a.rows = d.token_space + d.field_space;
+  a.sums = sums;
+  a.row_sums = o->unfreeze_tokens ? row_sums : nullptr;
+  a.touched = o->unfreeze_tokens ? touched : nullptr;
+  a.report = report;
+  a.o = learn_opts(o);
+  BackWs& bw = h->bw;
+  const uint64_t elems = 2ull * d.h * d.h + 5ull * d.h + (a.row_sums ? uint64_t(a.rows) * d.h : 0);
+  KC_TRY(ensure(bw.learn_backup, elems * 4), "workspace");
+  KC_TRY(ensure(bw.learn_health, 4 * kc::kHealthGroups * 4), "workspace");
+  KC_TRY(ensure(bw.learn_out, (kc::kLearnResult + kc::kLearnReport) * 8), "workspace");
+  a.backup = P<float>(bw.learn_backup);
+  a.health = P<unsigned>(bw.learn_health);
+  a.result = P<double>(bw.learn_out);
+  const unsigned grid = unsigned(std::min<uint64_t>((elems + 255) / 256, uint64_t(h->sms) * 4));
+  KC_TRY(cudaMemsetAsync(a.health, 0, 4 * kc::kHealthGroups * 4, h->stream), "memset");
+  kc::k_learn_health<<<grid, 256, 0, h->stream>>>(a, 0);
+  kc::k_learn_backup<<<grid, 256, 0, h->stream>>>(a);
+  kc::k_learn_update<<<grid, 256, 0, h->stream>>>(a);
+  kc::k_learn_health<<<grid, 256, 0, h->stream>>>(a, 1);
+  kc::k_learn_settle<<<grid, 256, 0, h->stream>>>(a);
+  h->launches += 5;
+  double out[kc::kLearnResult + kc::kLearnReport];
+  KC_TRY(cudaMemcpyAsync(P<double>(bw.learn_out) + kc::kLearnResult, report, kc::kLearnReport * 8,
+                         cudaMemcpyDeviceToDevice, h->stream), "copy");
+  KC_TRY(cudaMemcpyAsync(out, bw.learn_out.p, sizeof out, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "learn apply");
+  KC_TRY(cudaGetLastError(), "learn apply");
+  for (int i = 0; i < kc::kLearnResult + kc::kLearnReport; i++) result[i] = out[i];
+  const bool applied = out[0] != 0.0, moved = out[kc::kLearnResult + 1] != 0.0;
+  if (applied && moved) {  // the selector moved: its tensor-core images and transposed copies are stale
+    const size_t nf = h->mats.size() / 2, i = nf - 2;
+    h->mat_max[i] = h->mat_max[nf + i] = float(out[7]);
+    h->mat_max[i + 1] = h->mat_max[nf + i + 1] = float(out[8]);
+    h->mat_dirty[i] = h->mat_dirty[i + 1] = h->mat_dirty[nf + i] = h->mat_dirty[nf + i + 1] = 1;
+    h->wt_sel_dirty = true;
+  }
+  return KC_OK;
+}
+
+kc_status kc_copy_weights(kc_handle* h, uint64_t offset, uint64_t count, float* host) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  DeviceGuard dg(h->device);
+  if (!host && count) return fail(h, KC_ERR_INVALID_ARG, "copy destination is null");
+  if (offset > h->d.total || count > h->d.total - offset)
+    return fail(h, KC_ERR_INVALID_ARG, "the range lies outside the weight page");
+  if (count)
+    KC_TRY(cudaMemcpyAsync(host, h->w + offset, count * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaStreamSynchronize(h->stream), "copy weights");
+  return KC_OK;
+}
+
 kc_status kc_load_checkpoint(kc_handle* h, const void* bytes, uint64_t len, int* refusal) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
@@ -2163,6 +2319,15 @@ kc_status kc_set_precision(kc_handle* h, int mode, float tau) {
   return KC_OK;
 }
 
+kc_status kc_inject_wait_expiry(kc_handle* h, int kernel) {
+  if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (kernel != KC_INJECT_ATTN && kernel != KC_INJECT_FFN && kernel != KC_INJECT_GEMM)
+    return fail(h, KC_ERR_INVALID_ARG, "unknown tensor-core kernel for the injected expiry");
+  h->inject = kernel;
+  return KC_OK;
+}
+
 kc_status kc_set_stream(kc_handle* h, void* stream) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
@@ -2219,7 +2384,7 @@ void kc_destroy(kc_handle* h) {
                       &h->ws.qstate, &h->ws.mq, &h->ws.mh, &h->ws.sq, &h->ws.sk, &h->ws.p, &h->ws.index,
                       &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off, &h->ws.word_ids, &h->ws_fb.word_ids};
     for (DevBuf* b : bufs)
-      if (b->p) cudaFree(b->p);
+      if (b->p) cudaFree(b->p), b->p = nullptr;
     Workspace& f = h->ws_fb;
     DevBuf* fbufs[] = {&f.rec_off, &f.token_ids, &f.field_roles, &f.schema_ids, &f.band_ids, &f.schema_allow,
                        &f.band_allow, &f.uniforms, &f.mask, &f.bank_schema, &f.bank_band, &f.rec_meta, &f.frame_t,
@@ -2229,7 +2394,7 @@ void kc_destroy(kc_handle* h) {
                        &f.gather, &f.rows_val, &f.rows_off, &f.flags, &f.list, &h->ws.flags, &h->ws.list,
                        &h->images};
     for (DevBuf* b : fbufs)
-      if (b->p) cudaFree(b->p);
+      if (b->p) cudaFree(b->p), b->p = nullptr;
     BackWs& k = h->bw;
     DevBuf* bbufs[] = {&k.mask, &k.targets, &k.valence, &k.enc_qkv, &k.enc_p, &k.enc_h1, &k.mix_q, &k.mix_k,
                        &k.mix_v, &k.mix_p, &k.mix_h1, &k.gather, &k.offered, &k.n_allowed, &k.pred, &k.dpred,
@@ -2237,7 +2402,7 @@ void kc_destroy(kc_handle* h) {
                        &k.dswq, &k.dswk, &k.dh1, &k.ads, &k.mdq, &k.mdk, &k.mdv, &k.tok_ds, &k.dfs, &k.dpool,
                        &k.edqkv, &k.learn_partial, &h->wt};
     for (DevBuf* b : bbufs)
-      if (b->p) cudaFree(b->p);
+      if (b->p) cudaFree(b->p), b->p = nullptr;
     if (h->d_err) cudaFree(h->d_err);
     if (h->h_err) cudaFreeHost(h->h_err);
     if (h->d_audit) cudaFree(h->d_audit);
@@ -2252,6 +2417,8 @@ void kc_destroy(kc_handle* h) {
     if (h->h_tot) cudaFreeHost(h->h_tot);
     if (h->own) cudaStreamDestroy(h->own);
   }
+  const int dev = h->device;
+  DeviceGuard dg(dev);  // buffers not listed above free themselves here, with their device current
   delete h;
 }
 

@@ -88,6 +88,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// Wait for copies or MMAs already issued before the CTA leaves: bounded by
+// the clock alone. It does not give up when the error word is raised, since
+// a copy still landing in shared memory, or an MMA still using TMEM, must
+// finish before the CTA exits or frees TMEM. An issued copy or MMA always
+// completes, so the bound is only a backstop.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitCycles) return;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -245,6 +256,7 @@ struct GemmArgs {
   float a_scale;         // 2^sa
   float unscale;         // 2^-(sa+sw)
   int* err;              // error word
+  int inject_expiry;     // test hook: the producer reports an expired wait before it issues any copy
 };
 
 // 2-D TMA load of a [128 rows x 64 f32] box of A (no swizzle) at (x = k, y = row).
@@ -314,6 +326,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
       uint32_t it = 0;
       bool ok = true;
+      if (a.inject_expiry) {  // as if the first wait had expired: nothing is issued
+        atomicOr(a.err, kErrTimeout);
+        ok = false;
+      }
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         const int m = t / a.n_sub, n = t % a.n_sub;
         for (int kc = 0; kc < kchunks; kc++, it++) {
@@ -331,7 +347,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       // every copy issued must have landed before the CTA may exit (on the
       // normal path the split warps already waited for them: these pass at once)
       for (uint32_t j = it > uint32_t(kStagesT) ? it - kStagesT : 0u; j < it; j++)
-        mbar_wait(&raw[j % kStagesT], (j / kStagesT) & 1, a.err);
+        mbar_wait_drain(&raw[j % kStagesT], (j / kStagesT) & 1);
     }
     __syncwarp();
   } else if (warp <= 4) {
@@ -415,7 +431,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       }
       // every MMA this thread issued completes before TMEM is released
       mma_commit(drain);
-      mbar_wait(drain, 0, a.err);
+      mbar_wait_drain(drain, 0);
     }
     __syncwarp();
   } else {
@@ -461,8 +477,13 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
         tmem_ld32(tmem_base + (uint32_t(g * 32) << 16) + acc * kBN + cc * 32, v);
         if (kLoadTile) {  // every lane observes the landing of the tile it reads
           const bool mine = mbar_wait(&cload[ew * 2 + b], (cphase >> b) & 1, a.err);
+          if (!__all_sync(0xffffffffu, mine)) {
+            // the residual load issued above lands before the CTA may exit
+            if (lane == 0) mbar_wait_drain(&cload[ew * 2 + b], (cphase >> b) & 1);
+            ok = false;
+            break;
+          }
           cphase ^= 1u << b;
-          if (!__all_sync(0xffffffffu, mine)) { ok = false; break; }
         }
         // row = lane; 16-byte chunk j of the row sits at chunk j ^ (row & 7)
         unsigned char* rowp = buf + lane * 128;

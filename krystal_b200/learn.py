@@ -20,7 +20,14 @@ Several GPUs (one process each, frames split into contiguous shards in rank
 order): the per-frame readings are gathered so that every rank computes the
 same steps in the same frame order, and the per-rank gradient sums are added
 by one all-reduce (NCCL over NVLink on GPUs) before every rank applies the
-same update. Token-table unfreezing (learn.ts:298-299) is not on this path.
+same update.
+
+On a CUDA backend (``BatchLearner``) the scalar half and the update run on
+the device too (``kc_learn_plan``, ``kc_learn_apply``), with token-table
+unfreezing (learn.ts:298-299, scatterEmbeddings :242-263). ``plan_update``
+and ``apply_update`` below are the same arithmetic on the host: the
+reference form the device plan is checked against, and the host half for
+gradient sources without a device.
 """
 from __future__ import annotations
 
@@ -50,6 +57,7 @@ class LearnOptions:
     max_parameter_abs: float = math.inf
     unfreeze_pool: bool = False
     unfreeze_tokens: bool = False
+    token_rate: float = 0.1
 
 
 @dataclass
@@ -223,11 +231,34 @@ def all_reduce_sums(sums, group) -> np.ndarray:
     return sums.cpu().numpy()
 
 
+def gather_frame_rows_device(local, global_frames: int, group):
+    """All ranks' per-frame rows [F_r, C] (a CUDA tensor) in global frame
+    order, on the device: one NCCL all-gather, no host copy."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    fmax = -(-global_frames // world)
+    pad = torch.zeros((fmax, local.shape[1]), dtype=local.dtype, device=local.device)
+    pad[:local.shape[0]] = local
+    out = torch.empty((world * fmax, local.shape[1]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, pad, group=group)
+    keep = torch.cat([torch.arange(r * fmax, r * fmax + (b - a), device=local.device)
+                      for r, (a, b) in ((r, shard_bounds(global_frames, world, r)) for r in range(world))])
+    return out.index_select(0, keep)
+
+
 class BatchLearner:
     """The learn step over device-resident batches for one backend (one GPU).
 
-    ``group``: a torch.distributed process group for several GPUs, every rank
-    holding the contiguous shard ``shard_bounds(global_frames, world, rank)``.
+    The backward, the per-frame readings, the update plan, the gradient sums,
+    the update of the device's weight page with its health check and rollback
+    all run on the device in stream order (``kc_learn_plan``,
+    ``kc_learn_accumulate[_rows]``, ``kc_learn_apply``); the host's arrays are
+    then read back from the page. ``group``: a torch.distributed process
+    group for several GPUs, every rank holding the contiguous shard
+    ``shard_bounds(global_frames, world, rank)``; the per-frame rows are
+    all-gathered and the gradient sums all-reduced on the device, so that
+    every rank plans and applies the same update.
     """
 
     def __init__(self, backend: CudaBrainBackend, weights: BrainForwardWeights, group=None):
@@ -236,10 +267,30 @@ class BatchLearner:
         self.be = backend
         self.weights = weights
         self.group = group
-        h = backend.config.hidden_size
+        cfg = backend.config
+        h = cfg.hidden_size
         self.dev = torch.device("cuda", backend.device)
         self.sums = torch.zeros(2 * h * h + 5 * h, dtype=torch.float64, device=self.dev)
         self.stats = torch.zeros(0, dtype=torch.float64, device=self.dev)
+        self.report = torch.zeros(abi.KC_LEARN_REPORT, dtype=torch.float64, device=self.dev)
+        self.table_rows = cfg.token_space + cfg.field_space
+        self.stream = torch.cuda.Stream(device=self.dev)
+        self.rows_buf = None  # [table rows * H + table rows] f64: row sums, then touched flags
+        self._pinned = {}
+
+    def _to_device(self, name: str, a: np.ndarray):
+        """a host array through a reused pinned buffer, copied without waiting."""
+        torch = self.torch
+        t = self._pinned.get(name)
+        if t is None or t.numel() < a.size:
+            t = torch.empty(max(a.size, 1), dtype=torch.float64).pin_memory()
+            self._pinned[name] = t
+        t[:a.size] = torch.from_numpy(a)
+        return t[:a.size].to(self.dev, non_blocking=True)
+
+    def _options(self, o: LearnOptions) -> abi.KcLearnOptions:
+        return abi.KcLearnOptions(o.learning_rate, o.policy_scale, o.advantage_clip, o.max_parameter_abs,
+                                  o.token_rate, int(o.unfreeze_pool), int(o.unfreeze_tokens))
 
     def step(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int, schema_ids: int,
              band_ids: int, rewards: np.ndarray, answered: np.ndarray, targets: int | None = None,
@@ -247,39 +298,84 @@ class BatchLearner:
              options: LearnOptions = LearnOptions(), global_frames: int | None = None) -> LearnReport:
         """One update from a device-resident batch (raw device pointers as for
         kc_backward_batch_device). rewards [frames] f64 (NaN = none), answered
-        [frames] bool, host arrays for this rank's frames."""
-        if options.unfreeze_tokens:
-            raise NotImplementedError("unfreezing the token tables is not on the device learn path")
+        [frames] bool, host arrays for this rank's frames. The library runs
+        the step on a torch stream, and every torch operation of the step
+        (copies, the row table, the collectives) is queued on it, in order
+        with the library's kernels; the library's stream is restored after."""
+        torch = self.torch
+        # a stream torch owns (never destroyed under its tensors): the caller's
+        # current one, or the learner's own when that is the default stream
+        cur = torch.cuda.current_stream(self.dev)
+        run = cur if cur.cuda_stream else self.stream
+        prev = self.be.stream_ptr()
+        self.be.set_stream(run.cuda_stream)
+        try:
+            with torch.cuda.stream(run):
+                return self._step(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, rewards,
+                                  answered, targets, selection, schema_allow, band_allow, options, global_frames)
+        finally:
+            self.be.set_stream(prev)
+
+    def _step(self, frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, rewards, answered,
+              targets, selection, schema_allow, band_allow, options, global_frames) -> LearnReport:
         torch = self.torch
         rewards = np.ascontiguousarray(rewards, np.float64)
-        valence = torch.from_numpy(rewards).to(self.dev)
+        valence = self._to_device("rewards", rewards)
+        flags = self._to_device("answered", np.asarray(answered, np.float64))
         self.be.backward_batch_device(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids,
                                       selection, targets, valence.data_ptr(), schema_allow, band_allow)
         if self.stats.numel() < frames * STATS:
             self.stats = torch.empty(frames * STATS, dtype=torch.float64, device=self.dev)
         self.be.learn_frame_stats(targets, self.stats.data_ptr())
-        self.be.synchronize()
-        stats = self.stats[:frames * STATS].cpu().numpy().reshape(frames, STATS)
-        local = np.concatenate([stats, rewards[:, None], np.asarray(answered, np.float64)[:, None]], 1)
+        local = torch.cat([self.stats[:frames * STATS].view(frames, STATS), valence.view(frames, 1),
+                           flags.view(frames, 1)], 1).contiguous()
         lo = 0
         rows = local
         if self.group is not None:
             import torch.distributed as dist
             g = global_frames if global_frames is not None else frames
-            rows = gather_frame_rows(local, g, self.group)
+            rows = gather_frame_rows_device(local, g, self.group)
             lo, _ = shard_bounds(g, dist.get_world_size(self.group), dist.get_rank(self.group))
-        plan = plan_update(rows[:, :STATS], rows[:, STATS], rows[:, STATS + 1] > 0, options)
-        step = torch.from_numpy(np.ascontiguousarray(plan.step[lo:lo + frames])).to(self.dev)
-        vw = torch.from_numpy(np.ascontiguousarray(plan.value_weight[lo:lo + frames])).to(self.dev)
-        self.be.learn_accumulate(step.data_ptr(), vw.data_ptr(), self.sums.data_ptr())
-        self.be.synchronize()
-        sums = all_reduce_sums(self.sums, self.group) if self.group is not None else self.sums.cpu().numpy()
-        changes, rejected, health = apply_update(self.weights, sums, plan, options)
-        if changes is not None:
-            self.be.sync(self.weights, changes)
-        return LearnReport(plan.seen, plan.mean_advantage, plan.mean_value_loss, plan.reinforced, plan.discouraged,
-                           plan.mean_entropy, plan.mean_confidence, plan.seen > 0 and rejected is None, rejected,
-                           health)
+        n = rows.shape[0]
+        plan = torch.empty((3, max(n, 1)), dtype=torch.float64, device=self.dev)  # step, value weight, pending
+        step, vw, pend = plan[0], plan[1], plan[2]
+        opts = self._options(options)
+        self.be.learn_plan(rows.data_ptr(), n, opts, step.data_ptr(), vw.data_ptr(), pend.data_ptr(),
+                           self.report.data_ptr())
+        self.be.learn_accumulate(step[lo:].data_ptr(), vw[lo:].data_ptr(), self.sums.data_ptr())
+        row_sums = touched = None
+        h = self.be.config.hidden_size
+        if options.unfreeze_tokens:
+            if self.rows_buf is None:
+                self.rows_buf = torch.zeros(self.table_rows * (h + 1), dtype=torch.float64, device=self.dev)
+            self.rows_buf.zero_()
+            row_sums, touched = self.rows_buf[:self.table_rows * h], self.rows_buf[self.table_rows * h:]
+            self.be.learn_accumulate_rows(token_ids, field_roles, step[lo:].data_ptr(), pend[lo:].data_ptr(),
+                                          row_sums.data_ptr(), touched.data_ptr())
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(self.sums, group=self.group)
+            if row_sums is not None:
+                dist.all_reduce(self.rows_buf, group=self.group)
+        result = self.be.learn_apply(self.sums.data_ptr(), row_sums.data_ptr() if row_sums is not None else None,
+                                     touched.data_ptr() if touched is not None else None,
+                                     self.report.data_ptr(), opts)
+        report = result[10:]
+        self._read_back(options, moved=report[1] != 0.0 and result[0] != 0.0)
+        rejected = {0: None, 1: "non-finite", 2: "parameter-limit"}[int(result[1])]
+        health = dict(semantic_embedding_max_abs=float(result[3]), selector_max_abs=float(result[4]),
+                      value_max_abs=float(result[5]), pool_max_abs=float(result[6]), finite=bool(result[2]))
+        return LearnReport(int(report[0]), float(report[4]), float(report[5]), int(report[2]), int(report[3]),
+                           float(report[6]), float(report[7]), bool(result[0]), rejected, health)
+
+    def _read_back(self, options: LearnOptions, moved: bool) -> None:
+        """The host's arrays as the device page left them."""
+        w, lay = self.weights, self.weights.layout
+        self.be.copy_weights(lay.selector_wq, w.page[lay.selector_wq:lay.total])  # selector, decision and value heads
+        self.be.copy_weights(lay.pool, w.pool)
+        if options.unfreeze_tokens and moved:
+            h = self.be.config.hidden_size
+            self.be.copy_weights(lay.embeddings, w.embeddings[:self.table_rows * h])
 
 
 def experience_batch(experiences: Sequence[HostExperience]) -> tuple[FrameBatch, np.ndarray, np.ndarray,

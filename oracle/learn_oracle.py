@@ -30,6 +30,8 @@ class Options:
     advantage_clip: float = 3.0   # :294
     max_parameter_abs: float = math.inf  # :295
     unfreeze_pool: bool = False   # :297
+    unfreeze_tokens: bool = False  # :298
+    token_rate: float = 0.1       # :299
 
 
 def _f32_update(dst: np.ndarray, delta: np.ndarray) -> None:
@@ -47,8 +49,11 @@ def _max_abs(a: np.ndarray) -> float:
 def learn_from_experience(config, page: np.ndarray, experiences, options: Options = Options(),
                           threads: int = 0) -> tuple[np.ndarray, dict]:
     """Returns the updated weight page (a copy) and the LearnReport fields.
-    threads > 1 runs the per-frame backwards on that many threads. Token-table
-    unfreezing (learn.ts:298-299) is not restated here."""
+    threads > 1 runs the per-frame backwards on that many threads. With
+    unfreeze_tokens the token and field rows of the answered frames move too
+    (scatterEmbeddings, learn.ts:242-263, frame after frame, token after
+    token, each write rounded to f32), and join the health check and the
+    rollback (:401-425, :477-495)."""
     h = config.hidden_size
     page = page.copy()
     off = {k: O.weight_offset(config, k) for k in O.WEIGHT_PARTS}
@@ -107,7 +112,8 @@ def learn_from_experience(config, page: np.ndarray, experiences, options: Option
         advantage = float(ex["reward"]) - baseline
         d_value[:] = (d_value.astype(np.float64) + res["d_value_wv"]).astype(np.float32)
         if answered and math.isfinite(advantage):
-            pending.append((advantage, res["d_selector_wq"], res["d_selector_wk"], res["d_pool"]))
+            pending.append((advantage, res["d_selector_wq"], res["d_selector_wk"], res["d_pool"],
+                            (ex["frame"], res["d_field_states"]) if options.unfreeze_tokens else None))
         pol = res["policy"]
         for i in range(q):
             allowed, ent = 0, 0.0
@@ -127,6 +133,19 @@ def learn_from_experience(config, page: np.ndarray, experiences, options: Option
         adv_total += advantage
         loss_total += res["value_loss"]
         seen += 1
+    # the rows this batch can move (:401-414): token and field rows of the answered frames
+    base_tok = O.weight_offset(config, "embeddings")
+    base_field = base_tok + config.token_space * h
+    rows_hit = set()
+    if options.unfreeze_tokens:
+        tr = np.asarray(config.token_rows, np.int64)
+        for *_, emb in pending:
+            frame, _ = emb
+            act = O.compile_active(frame.token_ids, frame.band_ids, frame.active_record_indices)
+            for ft in act["active_tokens"]:
+                rows_hit.add(base_tok + int(tr[frame.token_ids[ft]]) * h)
+                rows_hit.add(base_field + int(tr[frame.field_roles[ft]]) * h)
+    touched = sorted(rows_hit)
     before = page.copy()
     if seen:
         wv[:] = (wv.astype(np.float64) - (lr * d_value.astype(np.float64)) / seen).astype(np.float32)
@@ -144,27 +163,46 @@ def learn_from_experience(config, page: np.ndarray, experiences, options: Option
         dev = math.sqrt(var)
         if dev > 1e-6:
             actor_moved = True
-            for a, gq, gk, gp in pending:
+            for a, gq, gk, gp, emb in pending:
                 st = max(-clip, min(clip, (a - mean) / dev))
                 step = (lr * options.policy_scale * st) / len(pending)
                 _f32_update(wq, step * gq.astype(np.float64))
                 _f32_update(wk, step * gk.astype(np.float64))
                 if options.unfreeze_pool:
                     _f32_update(pool, step * gp.astype(np.float64))
+                if emb is not None:  # scatterEmbeddings(..., step * tokenRate)
+                    frame, ds = emb
+                    act = O.compile_active(frame.token_ids, frame.band_ids, frame.active_record_indices)
+                    tr = np.asarray(config.token_rows, np.int64)
+                    s_tok = step * options.token_rate
+                    for t, ft in enumerate(act["active_tokens"]):
+                        g = s_tok * ds[t * h:(t + 1) * h].astype(np.float64)
+                        for row in (base_tok + int(tr[frame.token_ids[ft]]) * h,
+                                    base_field + int(tr[frame.field_roles[ft]]) * h):
+                            _f32_update(page[row:row + h], g)
                 if st > 0:
                     reinforced += 1
                 elif st < 0:
                     discouraged += 1
     sel_max = max(_max_abs(wq), _max_abs(wk))
-    health = dict(selector_max_abs=sel_max, value_max_abs=_max_abs(wv), pool_max_abs=_max_abs(pool))
+    sem = max((_max_abs(page[r:r + h]) for r in touched), default=0.0)
+    health = dict(semantic_embedding_max_abs=sem, selector_max_abs=sel_max, value_max_abs=_max_abs(wv),
+                  pool_max_abs=_max_abs(pool))
     finite = all(math.isfinite(v) for v in health.values())
     over = any(v > options.max_parameter_abs for v in health.values())
     rejected = "non-finite" if not finite else "parameter-limit" if over else None
     if rejected:
         page = before
+        wq, wk = (page[off[k]:off[k] + h * h] for k in ("selector_wq", "selector_wk"))
+        wv = page[off["value_head"]:off["value_head"] + 3 * h]
+        pool = page[off["pool"]:off["pool"] + 2 * h]
+        health = dict(semantic_embedding_max_abs=max((_max_abs(page[r:r + h]) for r in touched), default=0.0),
+                      selector_max_abs=max(_max_abs(wq), _max_abs(wk)), value_max_abs=_max_abs(wv),
+                      pool_max_abs=_max_abs(pool))
     report = dict(frames_seen=seen, mean_advantage=adv_total / seen if seen else 0.0,
                   mean_value_loss=loss_total / seen if seen else 0.0, reinforced=reinforced,
                   discouraged=discouraged, mean_entropy=ent_total / ent_rows if ent_rows else 0.0,
                   mean_confidence=conf_total / conf_rows if conf_rows else 0.0,
-                  update_applied=seen > 0 and not rejected, rejected=rejected, actor_moved=actor_moved)
+                  update_applied=seen > 0 and not rejected, rejected=rejected, actor_moved=actor_moved,
+                  health=health)
     return page, report

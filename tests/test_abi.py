@@ -38,7 +38,8 @@ STRUCTS = {"kc_config": "KcConfig", "kc_block_view": "KcBlockView", "kc_weights_
            "kc_mask_rule": "KcMaskRule", "kc_batch_view": "KcBatchView", "kc_batch_out": "KcBatchOut",
            "kc_device_result": "KcDeviceResult", "kc_stage_times": "KcStageTimes",
            "kc_backward_out": "KcBackwardOut", "kc_backward_result": "KcBackwardResult",
-           "kc_stream_result": "KcStreamResult", "kc_batch_select_view": "KcBatchSelectView"}
+           "kc_stream_result": "KcStreamResult", "kc_batch_select_view": "KcBatchSelectView",
+           "kc_learn_options": "KcLearnOptions"}
 
 
 def test_struct_layouts_match_the_header(tmp_path):
