@@ -62,16 +62,18 @@ def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: s
     """Roofline of one fused tensor-core kernel from the profile counters
     (<key>_ms, _launches, _flops, _bytes): ALGORITHMIC FLOPs per launch (the
     f32 products, not the three split-fp16 MMAs issued for each) over the
-    launch's CUDA-event time, against the sustained bf16 peak (the kernel is
-    timed inside a long step); the HBM figure beside it uses the algorithmic
-    bytes (x read once and written once)."""
+    launch's CUDA-event time, against the burst bf16 peak (the timed region
+    lasts about a tenth of a second, not the seconds-long regime of the
+    sustained figure, which is reported beside it); the HBM figure uses the
+    algorithmic bytes (x read once and written once)."""
     n = max(prof.get(f"{key}_launches", 0), 1)
     ms = prof.get(f"{key}_ms", 0.0) / n
     flops = prof.get(f"{key}_flops", 0.0) / n
     nbytes = prof.get(f"{key}_bytes", 0.0) / n
     tflops = flops / (ms / 1e3) / 1e12 if ms > 0 else 0.0
     gbs = nbytes / (ms / 1e3) / 1e9 if ms > 0 else 0.0
-    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    peak = peaks.get("bf16_tflops")
+    sustained = peaks.get("bf16_tflops_sustained")
     hbm = peaks.get("hbm_gbs")
     tokens = nbytes / (4 * 2 * 128)  # the algorithmic bytes are x read and written: 1 KB per token
     per_token = DRAM_BYTES_PER_TOKEN.get(key)
@@ -80,7 +82,8 @@ def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: s
             "frac": tflops / peak if peak else None, "traffic": traffic,
             "traffic_source": ("ncu DRAM bytes per token on the full 4096-frame batch, scaled to this launch's "
                                "tokens") if per_token else None,
-            "peak_kind": f"{peaks_kind} sustained bf16 dense (cuBLAS)",
+            "peak_kind": f"{peaks_kind} burst bf16 dense (cuBLAS)",
+            "frac_of_sustained": tflops / sustained if sustained else None,
             "issued_tensor_tflops": 3 * tflops, "issued_frac": 3 * tflops / peak if peak else None,
             "hbm_gbs_algorithmic": gbs, "hbm_frac": gbs / hbm if hbm else None,
             "launch_ms": ms, "launches": prof.get(f"{key}_launches", 0), "flops_per_launch": flops,
@@ -100,6 +103,13 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the other configurations' figures after the headline (one GPU only)")
+    ap.add_argument("--all-legs", action="store_true",
+                    help="on N GPUs, one line per configuration in one launch: the ragged batch (weak), the learn "
+                         "step (strong), 1024 long-bank frames split over the ranks, the 100k-frame stream")
+    ap.add_argument("--stream-threads", type=int, default=0,
+                    help="stream_100k: threads that stage a push_many (0: automatic)")
+    ap.add_argument("--stream-bind", type=int, default=1,
+                    help="stream_100k: 1 binds the worker to the GPU's CPUs and NUMA node, 0 leaves it to the OS")
     ap.add_argument("--precision", choices=["certified", "exact", "fast"], default="certified",
                     help="certified: tensor cores + exact recomputation of uncertain frames (the product default)")
     return ap.parse_args()
@@ -430,7 +440,7 @@ def stream_run(st, batch, arrivals_ms, max_batch_frames: int) -> tuple[np.ndarra
                 raise RuntimeError(f"stream batch failed: {b.error}")
             done[b.first_ticket - base:b.first_ticket - base + b.frames] = b.done_ms - t0
             finished += b.frames
-            batches.append((b.frames, b.sealed_ms - t0, b.done_ms - t0))
+            batches.append((b.frames, b.sealed_ms - t0, b.done_ms - t0, b.started_ms - t0, b.sync_wait_ms))
             progressed = True
             b = st.poll(wait=False)
         if not progressed and pushed == avail and st.pending():
@@ -448,10 +458,28 @@ def batch_stats(batches) -> dict:
     done = np.array([b[2] for b in batches])
     start = np.maximum(sealed, np.concatenate([[-np.inf], done[:-1]]))
     svc = done - start
+    began = np.array([b[3] for b in batches])
+    wait = np.array([b[4] for b in batches])
+    host = (done - began) - wait  # the worker on the CPU inside the batch: launches, staging, host loops
     return {"batch_frames_mean": float(fr.mean()), "batch_frames_max": int(fr.max()),
+            "worker_host_ms_mean": float(host.mean()), "worker_host_ms_p99": float(np.percentile(host, 99)),
+            "worker_sync_wait_ms_mean": float(wait.mean()),
             "service_ms_mean": float(svc.mean()), "service_ms_p99": float(np.percentile(svc, 99)),
             "service_ms_max": float(svc.max()), "idle_ms_total": float(np.maximum(
                 0.0, sealed[1:] - done[:-1]).sum()) if len(batches) > 1 else 0.0}
+
+
+def host_stats(x: dict) -> dict:
+    """The stream's host counters (kc_stream_read_stats) in the JSON line:
+    where the push and worker time went, faults, context switches and NUMA
+    placement (GPU, staging pages, worker and caller threads)."""
+    keep = ("batches", "frames_pushed", "push_ms", "run_ms", "sync_wait_ms", "idle_ms", "workspace_grows",
+            "workspace_grow_ms", "worker_minor_faults", "worker_major_faults", "worker_involuntary_switches",
+            "worker_cpu_moves", "caller_minor_faults", "caller_involuntary_switches", "gpu_numa_node",
+            "staging_numa_node", "worker_numa_node", "caller_numa_node", "push_threads", "bound_cpus")
+    out = {k: (round(x[k], 3) if isinstance(x[k], float) else int(x[k])) for k in keep}
+    out["push_gb_per_s"] = round(x["bytes_staged"] / max(1e-9, x["push_ms"] * 1e6), 2)
+    return out
 
 
 def stream_main(args) -> dict | None:
@@ -482,7 +510,7 @@ def stream_main(args) -> dict | None:
     batch = synth.make_batch(wl, seed=100 + rank, frames=mine)
     max_batch = 2048
     st = FrameStream(be, max_frames=max_batch, max_records=max_batch * wl.records[1], max_p=1 << 24, depth=3,
-                     copy_results=False)
+                     copy_results=False, push_threads=args.stream_threads, bind_cpus=bool(args.stream_bind))
     warm = synth.make_batch(wl, seed=99, frames=256)
     stream_run(st, warm, np.zeros(warm.frames), max_batch)  # warm-up: sizes the workspace
 
@@ -493,9 +521,11 @@ def stream_main(args) -> dict | None:
     barrier()
     be.profile(True)
     be.profile_read(reset=True)
+    st.stats(reset=True)
     sat_lat, sat_ms, sat_batches = stream_run(st, batch, np.zeros(mine), max_batch)
     prof = be.profile_read(reset=True)
     be.profile(False)
+    sat_host = host_stats(st.stats(reset=True))
     t = torch.tensor([sat_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -508,6 +538,7 @@ def stream_main(args) -> dict | None:
         clocks.start()
     lat, lat_ms, lat_batches = stream_run(st, batch, arrivals, max_batch)
     clk = clocks.stop() if clocks else None
+    lat_host = host_stats(st.stats(reset=True))
     pad = -(-total // world)
     mine_t = torch.full((pad,), float("nan"), dtype=torch.float64, device=dev)
     mine_t[:mine] = torch.from_numpy(lat)
@@ -537,11 +568,13 @@ def stream_main(args) -> dict | None:
                            **batch_stats(sat_batches),
                            "device_stage_ms_per_batch": {k[:-3]: round(prof[k] / max(1, len(sat_batches)), 3)
                                                          for k in prof if k.endswith("_ms")},
-                           "fallback_frames_per_batch": prof["fallback_frames"] / max(1, len(sat_batches))},
+                           "fallback_frames_per_batch": prof["fallback_frames"] / max(1, len(sat_batches)),
+                           "host": sat_host},
             "latency": {"offered_rate_frames_per_s": rate, "p50_ms": float(np.percentile(every, 50)),
                         "p90_ms": float(np.percentile(every, 90)), "p99_ms": float(np.percentile(every, 99)),
                         "p999_ms": float(np.percentile(every, 99.9)), "max_ms": float(every.max()),
-                        "frames": int(every.size), "batches_rank0": len(lat_batches), **batch_stats(lat_batches)},
+                        "frames": int(every.size), "batches_rank0": len(lat_batches), **batch_stats(lat_batches),
+                        "host": lat_host},
             "e2e": {"value": sustained, "unit": UNIT,
                     "h2d_bytes_per_step": int(world * (batch.records * 72 + 8 * (mine + 1))),
                     "d2h_bytes_per_step": int(world * (4 * offs["p_off"][-1] + 4 * offs["q_off"][-1])),
@@ -561,13 +594,26 @@ def main():
     if args.impl == "reference":
         (learn_reference_arm if args.workload.startswith("learn") else reference_arm)(args)
         return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.all_legs:
+        import copy
+        legs = [("ragged_4096", None, forward_main), ("learn_1024", None, learn_main),
+                ("long_bank_1024", max(1, 1024 // world), forward_main), ("stream_100k", None, stream_main)]
+        for wl_name, frames, fn in legs:
+            a = copy.copy(args)
+            a.workload, a.frames, a.no_side = wl_name, frames, True
+            line = fn(a) if fn is not forward_main else fn(a, side=True)
+            if line is not None:
+                if frames is not None:
+                    line["config"]["split"] = f"{frames * world} frames over {world} ranks"
+                print(json.dumps(line), flush=True)
+        return
     if args.workload.startswith("stream"):
         line = stream_main(args)
     elif args.workload.startswith("learn"):
         line = learn_main(args)
     else:
         line = forward_main(args)
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     if line is not None and world == 1 and args.workload == "ragged_4096" and not args.device_only \
             and not args.no_side:
         line["side"] = side_legs(args)

@@ -172,6 +172,14 @@ typedef struct kc_batch_view {
    * and so does the streaming packer. */
   const uint32_t* word_ids;
   float word_alpha;
+  /* Optional explicit selection mask laid out like p ([sum_f Q_f R_f], frame
+   * f's [Q_f, R_f] block at p_off[f]): added to every score, as selectorOracle
+   * adds selectionMask's rows (forward/oracle.ts:340-345; NEG_INF -1e30 =
+   * blocked, 0 = open; host/learn.ts:215-232 builds it from any allows(q, r)
+   * closure, a row nothing admits reopened). For grammars that are not a
+   * schema x band product. Exclusive with schema_allow / band_allow. Not taken
+   * by the streaming packer. */
+  const float* mask;
 } kc_batch_view;
 
 /* Outputs of a batch. p of frame f is a [Q_f, R_f] block at p_off[f]; the
@@ -226,6 +234,15 @@ typedef struct kc_stage_times {
   uint64_t cert_audit_violations;
   uint64_t cert_audit_frames;
   double cert_kappa0;
+  /* the exact path's products on the int8 tensor cores (counted whether or
+     not profiling is on): products run, their outputs, the outputs whose
+     error interval straddled an f32 rounding boundary (recomputed by the
+     sequential chain), and forwards sent again through the FP64 kernel
+     because a product listed more outputs than its list holds */
+  uint64_t oz_products;
+  double oz_outputs;
+  uint64_t oz_listed;
+  uint64_t oz_reruns;
 } kc_stage_times;
 
 uint32_t kc_abi_version(void);
@@ -288,6 +305,7 @@ typedef struct kc_batch_select_view {
   const uint32_t* schema_allow;  /* [Q * 8] or NULL (the open mask) */
   const uint32_t* band_allow;    /* [Q], NULL with schema_allow */
   const double* uniforms;        /* [Q] or NULL */
+  const float* mask;             /* [total_p] explicit mask laid out like p, or NULL; exclusive with the rule */
 } kc_batch_select_view;
 
 kc_status kc_select_batch(kc_handle* h, const kc_batch_select_view* select, kc_batch_out* out);
@@ -470,12 +488,54 @@ typedef struct kc_stream_result {
   kc_status status;        /* the batch's own status; error: its message or NULL */
   const char* error;
   double sealed_ms, done_ms; /* kc_stream_clock_ms() at flush and when the results landed */
+  double started_ms;       /* kc_stream_clock_ms() when the worker took the batch up */
+  double sync_wait_ms;     /* of done_ms - started_ms, the worker's time blocked until the device finished */
 } kc_stream_result;
+
+/* Placement and helpers of a stream (kc_stream_create uses {0, 1}).
+ * push_threads: the threads a large kc_stream_push_many call validates and
+ * stages with, the caller's included; 0 picks one per 8 CPUs local to the GPU,
+ * at most 4; 1 is the caller alone. bind_cpus != 0: the worker and the helpers
+ * run on the CPUs sysfs lists as local to the GPU (local_cpulist, as far as
+ * this process may use them), and the worker allocates the pinned staging, so
+ * that its pages lie on the GPU's NUMA node. */
+typedef struct kc_stream_options {
+  uint32_t push_threads;
+  int32_t bind_cpus;
+} kc_stream_options;
+
+/* Where a stream's host time went (kc_stream_read_stats; the counters since
+ * the last reset). Fault and switch counts are getrusage(RUSAGE_THREAD)
+ * differences over the worker's batches and the callers' push_many calls. */
+typedef struct kc_stream_stats {
+  uint64_t batches;                    /* batches the worker finished */
+  uint64_t push_calls, frames_pushed;  /* kc_stream_push / _push_many calls and the frames they queued */
+  uint64_t bytes_staged;               /* record and rule bytes copied into the staging */
+  double push_ms;                      /* time inside push calls (checks and staging copies) */
+  double run_ms;                       /* worker: time inside batches */
+  double sync_wait_ms;                 /* worker: of run_ms, blocked until the device finished */
+  double idle_ms;                      /* worker: waiting for a sealed buffer */
+  uint64_t workspace_grows;            /* device workspace reallocations inside batches */
+  double workspace_grow_ms;
+  uint64_t worker_minor_faults, worker_major_faults;
+  uint64_t worker_voluntary_switches, worker_involuntary_switches;
+  uint64_t worker_cpu_moves;           /* batches that ended on another CPU than they began on */
+  uint64_t caller_minor_faults, caller_involuntary_switches;
+  int32_t gpu_numa_node;               /* sysfs numa_node of the GPU; -1 unknown */
+  int32_t staging_numa_node;           /* node of the first staging page; -1 unknown */
+  int32_t worker_numa_node;            /* node of the worker's CPU at its last batch */
+  int32_t caller_numa_node;            /* node of the CPU of the last push_many call */
+  uint32_t push_threads;               /* threads a large push_many uses */
+  uint32_t bound_cpus;                 /* CPUs the worker and helpers are bound to (0: unbound) */
+} kc_stream_stats;
 
 /* depth >= 2 staging buffers, each for up to max_frames frames, max_records
  * records and max_p p entries (0: 64 per record). Pinned host memory only. */
 kc_status kc_stream_create(kc_handle* h, uint32_t max_frames, uint64_t max_records, uint64_t max_p, uint32_t depth,
                            kc_stream** out);
+/* kc_stream_create with the placement and helpers of *opts (NULL: {0, 1}). */
+kc_status kc_stream_create_ex(kc_handle* h, uint32_t max_frames, uint64_t max_records, uint64_t max_p,
+                              uint32_t depth, const kc_stream_options* opts, kc_stream** out);
 /* Queue one packed frame (kc_frame_view as for kc_encode). schema_allow /
  * band_allow: the frame's questions' rule ([Q*8], [Q]) or both NULL (open).
  * *ticket numbers the frame (consecutive from 0). KC_ERR_CAPACITY when the
@@ -495,6 +555,9 @@ uint32_t kc_stream_pending(kc_stream* s);
 /* The oldest finished batch (wait != 0: block until one finishes, unless none
  * is queued). Its arrays stay valid until the next poll. */
 kc_status kc_stream_poll(kc_stream* s, int wait, kc_stream_result* out);
+/* The stream's host-side counters (reset != 0: zeroed after reading; the
+ * placement fields stay). */
+kc_status kc_stream_read_stats(kc_stream* s, int reset, kc_stream_stats* out);
 /* The steady clock the stream's timestamps use, in milliseconds. */
 double kc_stream_clock_ms(void);
 const char* kc_stream_last_error(kc_stream* s);
@@ -508,7 +571,8 @@ kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 /* Test hook for the failure path, no counterpart in the reference: the next
  * launch of one tensor-core kernel (KC_INJECT_ATTN: the fused encoder
  * attention; KC_INJECT_FFN: the fused feed-forward; KC_INJECT_GEMM: the
- * projection GEMM) behaves as if its producer's first bounded wait had
+ * projection GEMM; KC_INJECT_EXACT_GEMM: the exact path's int8 product)
+ * behaves as if its producer's first bounded wait had
  * expired, before it issues any copy: the kernel raises the error word,
  * every warp role leaves, TMEM is freed, and the batch call returns
  * KC_ERR_TIMEOUT with kc_last_error naming the expired wait. One shot; the
@@ -516,6 +580,7 @@ kc_status kc_set_precision(kc_handle* h, int mode, float tau);
 #define KC_INJECT_ATTN 0
 #define KC_INJECT_FFN 1
 #define KC_INJECT_GEMM 2
+#define KC_INJECT_EXACT_GEMM 3  /* the exact path's int8 tensor-core product */
 kc_status kc_inject_wait_expiry(kc_handle* h, int kernel);
 
 /* Stream control: run on `stream` (a cudaStream_t; NULL = the handle's own). */

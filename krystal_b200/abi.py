@@ -25,7 +25,7 @@ KC_NO_SELECTION = 0xFFFFFFFF
 KC_PRECISION_EXACT = 0
 KC_PRECISION_CERTIFIED = 1
 KC_PRECISION_FAST = 2
-KC_INJECT_ATTN, KC_INJECT_FFN, KC_INJECT_GEMM = 0, 1, 2  # kc_inject_wait_expiry (test hook)
+KC_INJECT_ATTN, KC_INJECT_FFN, KC_INJECT_GEMM, KC_INJECT_EXACT_GEMM = 0, 1, 2, 3  # kc_inject_wait_expiry (test hook)
 KC_MAX_BANK = 4096
 KC_NO_TARGET = 0xFFFFFFFF
 KC_AWAY_TARGET = 0x80000000
@@ -43,7 +43,7 @@ EXPORTS = ("kc_abi_version", "kc_create", "kc_sync", "kc_encode", "kc_select", "
            "kc_stream_poll", "kc_stream_clock_ms", "kc_stream_last_error", "kc_stream_destroy",
            "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch",
            "kc_inject_wait_expiry", "kc_learn_plan", "kc_learn_accumulate_rows", "kc_learn_apply",
-           "kc_copy_weights")
+           "kc_copy_weights", "kc_stream_create_ex", "kc_stream_read_stats")
 
 
 class KrystalCudaError(RuntimeError):
@@ -96,7 +96,7 @@ class KcMaskRule(C.Structure):
 class KcBatchView(C.Structure):
     _fields_ = [("frames", C.c_uint32), ("records", C.c_uint64), ("rec_off", P), ("token_ids", P),
                 ("field_roles", P), ("schema_ids", P), ("band_ids", P), ("schema_allow", P), ("band_allow", P),
-                ("uniforms", P), ("word_ids", P), ("word_alpha", C.c_float)]
+                ("uniforms", P), ("word_ids", P), ("word_alpha", C.c_float), ("mask", P)]
 
 
 class KcBatchOut(C.Structure):
@@ -106,7 +106,7 @@ class KcBatchOut(C.Structure):
 
 
 class KcBatchSelectView(C.Structure):
-    _fields_ = [("schema_allow", P), ("band_allow", P), ("uniforms", P)]
+    _fields_ = [("schema_allow", P), ("band_allow", P), ("uniforms", P), ("mask", P)]
 
 
 class KcDeviceResult(C.Structure):
@@ -140,7 +140,24 @@ KC_LEARN_ROW, KC_LEARN_REPORT, KC_LEARN_RESULT = 10, 9, 19
 class KcStreamResult(C.Structure):
     _fields_ = [("first_ticket", C.c_uint64), ("frames", C.c_uint32), ("questions", C.c_uint64),
                 ("total_p", C.c_uint64), ("p_off", P), ("q_off", P), ("p", P), ("index", P), ("status", C.c_int),
-                ("error", C.c_char_p), ("sealed_ms", C.c_double), ("done_ms", C.c_double)]
+                ("error", C.c_char_p), ("sealed_ms", C.c_double), ("done_ms", C.c_double),
+                ("started_ms", C.c_double), ("sync_wait_ms", C.c_double)]
+
+
+class KcStreamOptions(C.Structure):
+    _fields_ = [("push_threads", C.c_uint32), ("bind_cpus", C.c_int32)]
+
+
+class KcStreamStats(C.Structure):
+    _fields_ = [("batches", C.c_uint64), ("push_calls", C.c_uint64), ("frames_pushed", C.c_uint64),
+                ("bytes_staged", C.c_uint64), ("push_ms", C.c_double), ("run_ms", C.c_double),
+                ("sync_wait_ms", C.c_double), ("idle_ms", C.c_double), ("workspace_grows", C.c_uint64),
+                ("workspace_grow_ms", C.c_double)] + [
+        (n, C.c_uint64) for n in ("worker_minor_faults", "worker_major_faults", "worker_voluntary_switches",
+                                  "worker_involuntary_switches", "worker_cpu_moves", "caller_minor_faults",
+                                  "caller_involuntary_switches")] + [
+        (n, C.c_int32) for n in ("gpu_numa_node", "staging_numa_node", "worker_numa_node", "caller_numa_node")] + [
+        ("push_threads", C.c_uint32), ("bound_cpus", C.c_uint32)]
 
 
 class KcStageTimes(C.Structure):
@@ -152,7 +169,8 @@ class KcStageTimes(C.Structure):
         ("enc_ffn_flops", C.c_double), ("enc_ffn_bytes", C.c_double), ("enc_attn_tc_ms", C.c_double),
         ("enc_attn_tc_launches", C.c_uint64), ("enc_attn_tc_flops", C.c_double), ("enc_attn_tc_bytes", C.c_double),
         ("cert_audit_max", C.c_double), ("cert_audit_violations", C.c_uint64), ("cert_audit_frames", C.c_uint64),
-        ("cert_kappa0", C.c_double)]
+        ("cert_kappa0", C.c_double), ("oz_products", C.c_uint64), ("oz_outputs", C.c_double),
+        ("oz_listed", C.c_uint64), ("oz_reruns", C.c_uint64)]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -195,6 +213,9 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     lib.kc_copy_weights.argtypes = [P, C.c_uint64, C.c_uint64, P]
     lib.kc_stream_create.argtypes = [P, C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint32, C.POINTER(P)]
     lib.kc_stream_push.argtypes = [P, C.POINTER(KcFrameView), P, P, C.POINTER(C.c_uint64)]
+    lib.kc_stream_create_ex.argtypes = [P, C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint32,
+                                        C.POINTER(KcStreamOptions), C.POINTER(P)]
+    lib.kc_stream_read_stats.argtypes = [P, i, C.POINTER(KcStreamStats)]
     lib.kc_stream_push_many.argtypes = [P, C.POINTER(KcBatchView), C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]
     lib.kc_stream_flush.argtypes = [P]
     lib.kc_load_checkpoint.argtypes = [P, P, C.c_uint64, C.POINTER(C.c_int)]
@@ -226,7 +247,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
                  "kc_learn_accumulate", "kc_stream_create", "kc_stream_push", "kc_stream_flush", "kc_stream_poll",
                  "kc_stream_push_many", "kc_load_checkpoint", "kc_save_checkpoint", "kc_select_batch",
                  "kc_inject_wait_expiry", "kc_learn_plan", "kc_learn_accumulate_rows", "kc_learn_apply",
-                 "kc_copy_weights"):
+                 "kc_copy_weights", "kc_stream_create_ex", "kc_stream_read_stats"):
         getattr(lib, name).restype = C.c_int
     _lib = lib
     return lib

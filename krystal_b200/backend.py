@@ -313,9 +313,12 @@ class CudaBrainBackend:
     # --- packed ragged batches ------------------------------------------------
     def forward_batch(self, batch: FrameBatch, rule: MaskRule | None = None, uniforms=None,
                       want_query_output: bool = False, p_capacity: int | None = None, word_ids=None,
-                      word_alpha: float = 0.0, out: dict | None = None) -> dict:
+                      word_alpha: float = 0.0, out: dict | None = None, mask=None) -> dict:
         """Pack, encode and select a whole batch; host arrays in and out.
         word_ids [records*8] / word_alpha: the same-word bias (WordBias).
+        mask: an explicit selection mask laid out like p (frame f's [Q_f, R_f]
+        block at p_off[f]; NEG_INF blocked, 0 open), for a grammar that is not
+        a schema x band rule; exclusive with `rule`.
         out: caller-owned result arrays to fill instead of fresh ones — "p"
         (f32), "index" (u32), "p_off" and "q_off" (u64, frames + 1), e.g.
         pinned buffers reused across calls; p and index set the capacities."""
@@ -330,9 +333,10 @@ class CudaBrainBackend:
         wid = _u32(word_ids) if word_ids is not None else None
         if wid is not None and wid.size != batch.records * 8:
             raise ValueError("word_ids must hold one label per token slot (records * 8)")
+        m = _f32(mask) if mask is not None else None
         bv = abi.KcBatchView(batch.frames, batch.records, off.ctypes.data, tok.ctypes.data, role.ctypes.data,
                              sch.ctypes.data, band.ctypes.data, abi.ptr(sa), abi.ptr(ba), abi.ptr(u), abi.ptr(wid),
-                             float(word_alpha))
+                             float(word_alpha), abi.ptr(m))
         nq = int((band == 5).sum()) if out is None or want_query_output else 0
         if p_capacity is None and out is None:
             rec = np.diff(off.astype(np.int64))
@@ -362,7 +366,8 @@ class CudaBrainBackend:
             res["query_output"] = qo[:bo.total_q * self.config.hidden_size]
         return res
 
-    def select_batch(self, rule: MaskRule | None = None, uniforms=None, out: dict | None = None) -> dict:
+    def select_batch(self, rule: MaskRule | None = None, uniforms=None, out: dict | None = None,
+                     mask=None) -> dict:
         """kc_select_batch: the last forward_batch's batch selected again under
         `rule` and/or `uniforms` (per question), without encoding it again
         (consider once, choose many: host/session.ts:128-176). `out` as for
@@ -372,7 +377,8 @@ class CudaBrainBackend:
             sa, ba = _u32(rule.schema_allow), _u32(rule.band_allow)
         if uniforms is not None:
             u = np.ascontiguousarray(uniforms, dtype=np.float64)
-        sv = abi.KcBatchSelectView(abi.ptr(sa), abi.ptr(ba), abi.ptr(u))
+        m = _f32(mask) if mask is not None else None
+        sv = abi.KcBatchSelectView(abi.ptr(sa), abi.ptr(ba), abi.ptr(u), abi.ptr(m))
         if out is None:
             last = getattr(self, "_last_batch_sizes", None)
             if last is None:
@@ -390,10 +396,11 @@ class CudaBrainBackend:
     def forward_batch_device(self, frames: int, records: int, rec_off: int, token_ids: int, field_roles: int,
                              schema_ids: int, band_ids: int, schema_allow: int | None = None,
                              band_allow: int | None = None, uniforms: int | None = None,
-                             word_ids: int | None = None, word_alpha: float = 0.0) -> abi.KcDeviceResult:
+                             word_ids: int | None = None, word_alpha: float = 0.0,
+                             mask: int | None = None) -> abi.KcDeviceResult:
         """Device-resident batch (raw device pointers); results stay on the device."""
         bv = abi.KcBatchView(frames, records, rec_off, token_ids, field_roles, schema_ids, band_ids, schema_allow,
-                             band_allow, uniforms, word_ids, float(word_alpha))
+                             band_allow, uniforms, word_ids, float(word_alpha), mask)
         res = abi.KcDeviceResult()
         abi.check(self._lib.kc_forward_batch_device(self._h, C.byref(bv), C.byref(res)), self._h)
         return res
@@ -421,7 +428,8 @@ class CudaBrainBackend:
         tensor-core kernel ("attn", "ffn" or "gemm") reports an expired
         bounded wait before it issues any copy; the batch call then fails
         with KC_ERR_TIMEOUT and the handle stays usable."""
-        k = {"attn": abi.KC_INJECT_ATTN, "ffn": abi.KC_INJECT_FFN, "gemm": abi.KC_INJECT_GEMM}[kernel]
+        k = {"attn": abi.KC_INJECT_ATTN, "ffn": abi.KC_INJECT_FFN, "gemm": abi.KC_INJECT_GEMM,
+             "exact_gemm": abi.KC_INJECT_EXACT_GEMM}[kernel]
         abi.check(self._lib.kc_inject_wait_expiry(self._h, k), self._h)
 
     def profile(self, enable: bool) -> None:

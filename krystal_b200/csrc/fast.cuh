@@ -676,6 +676,7 @@ struct SelectFastArgs {
   const uint32_t* bank_rec;
   const uint32_t* schema_ids;
   const uint32_t* band_ids;
+  const float* mask;  // explicit mask laid out like p (exclusive with the rule), or null
   const double* uniforms;
   uint32_t max_r;
   int qc;           // questions per chunk (the score buffer holds qc x max_r)
@@ -867,19 +868,23 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
       float b1 = -INFINITY, lam = 0.f;
       uint32_t i1 = KC_INVALID;
       int nonfinite = 0, open = 0;
+      const float* mrow = a.mask ? a.mask + a.p_off[f] + uint64_t(q0 + c) * uint64_t(R) : nullptr;
       for (int j = lane; j < R; j += 32) {
         const float s = row[j];
         float m = 0.f;
-        if (sa && !reopen) {
+        if (mrow) {
+          m = mrow[j];
+        } else if (sa && !reopen) {
           const uint32_t gr = a.bank_rec[rb + j];
           const uint32_t sid = a.schema_ids[gr], b = a.band_ids[gr];
           m = (sid < 256u && b < 32u && ((sa[sid >> 5] >> (sid & 31)) & 1u) && ((ba >> b) & 1u)) ? 0.f : -1e30f;
         }
-        const float sc = s * a.scale + m;
+        const float ss = s * a.scale;
+        const float sc = ss + m;
         row[j] = sc;
-        nonfinite |= !isfinite(s);
+        nonfinite |= !isfinite(s) || !isfinite(m);
         open |= sc >= -1e29f;
-        if (m == 0.f) lam = fmaxf(lam, fabsf(sc));
+        if (m > -1e29f) lam = fmaxf(lam, fabsf(ss));
         if (sc > b1) { b1 = sc; i1 = uint32_t(j); }
       }
       // warp reduce: top value, index of the first top, Lambda_q, any-open, any-nonfinite
@@ -898,8 +903,11 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
       float bt = 0.f, hi = -INFINITY, bmax = 0.f;
       for (int j = lane; j < R; j += 32) {
         const float sc = row[j];
-        // + 4u|s|: the f32 roundings of the fast and the exact score, and of the comparison below
-        const float bj = qn * a.nk[rb + j] + 2.384185791015625e-07f * fabsf(sc);
+        // + 4u|s|: the f32 roundings of the fast and the exact score, and of the
+        // comparison below; an explicit mask adds the rounding of s*scale + m
+        // (|s*scale| <= |s| + |m|)
+        const float mag = mrow ? fabsf(sc) + fabsf(mrow[j]) : fabsf(sc);
+        const float bj = qn * a.nk[rb + j] + 2.384185791015625e-07f * mag;
         if (sc >= -1e29f) bmax = fmaxf(bmax, bj);
         if (uint32_t(j) == i1) bt = bj;
         else hi = fmaxf(hi, sc + bj);
@@ -977,7 +985,8 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
 
 // ---------------------------------------------------------------------------
 // Audit of the certification margin on the frames recomputed exactly: for
-// every (question, bank row) pair of listed frame list[i] (one CTA each), the
+// every (question, bank row) pair of listed frame list[blockIdx.x] (its pairs
+// spread over gridDim.y CTAs), the
 // fast score (the selector's fmaf chain over the fast projections, scaled in
 // f32) against the exact score (the f64 chain over the exact projections,
 // rounded to f32), as a ratio to the margin B the selector allowed that pair
@@ -997,7 +1006,9 @@ __global__ void __launch_bounds__(256) k_cert_audit(
   const uint64_t Q = q_off[f + 1] - qb, R = r_off[f + 1] - rb;
   const uint64_t eq = sub_q_off[blockIdx.x], er = sub_r_off[blockIdx.x];
   float worst = 0.f;
-  for (uint64_t idx = threadIdx.x; idx < Q * R; idx += blockDim.x) {
+  // the frame's pairs are spread over gridDim.y CTAs
+  for (uint64_t idx = uint64_t(blockIdx.y) * blockDim.x + threadIdx.x; idx < Q * R;
+       idx += uint64_t(gridDim.y) * blockDim.x) {
     const uint64_t c = idx / R, j = idx % R;
     const float4* q4 = reinterpret_cast<const float4*>(fsq + (qb + c) * KC_H);
     const float4* k4 = reinterpret_cast<const float4*>(fsk + (rb + j) * KC_H);
@@ -1010,10 +1021,16 @@ __global__ void __launch_bounds__(256) k_cert_audit(
       sv = fmaf(a.w, b.w, sv);
     }
     const float fs = sv * scale;
-    const float* eqr = esq + (eq + c) * KC_H;
-    const float* ekr = esk + (er + j) * KC_H;
+    const float4* eq4 = reinterpret_cast<const float4*>(esq + (eq + c) * KC_H);
+    const float4* ek4 = reinterpret_cast<const float4*>(esk + (er + j) * KC_H);
     double dv = 0.0;
-    for (int d = 0; d < KC_H; d++) dv = fma(double(eqr[d]), double(ekr[d]), dv);
+    for (int d4 = 0; d4 < KC_H / 4; d4++) {
+      const float4 a = eq4[d4], b = ek4[d4];
+      dv = fma(double(a.x), double(b.x), dv);
+      dv = fma(double(a.y), double(b.y), dv);
+      dv = fma(double(a.z), double(b.z), dv);
+      dv = fma(double(a.w), double(b.w), dv);
+    }
     const float es = __double2float_rn(dv * scale_d);
     const float bound = kappa[qb + c] * scale * nq[qb + c] * nk[rb + j] + 2.384185791015625e-07f * fabsf(fs);
     const float r = fabsf(fs - es) / bound;
@@ -1033,27 +1050,39 @@ __global__ void __launch_bounds__(256) k_cert_audit(
 // Fallback plumbing: gather the records of the frames to recompute into a
 // compact batch, and scatter their exact results back.
 // ---------------------------------------------------------------------------
-// One CTA: sub_rec_off / sub_q_off over the listed frames.
+// One CTA: sub_rec_off / sub_q_off / sub_p_off over the listed frames.
 __global__ void k_fallback_offsets(const uint32_t* __restrict__ list, uint32_t n, const uint64_t* __restrict__ rec_off,
-                                   const uint64_t* __restrict__ q_off, uint64_t* __restrict__ sub_rec_off,
-                                   uint64_t* __restrict__ sub_q_off) {
+                                   const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ p_off,
+                                   uint64_t* __restrict__ sub_rec_off, uint64_t* __restrict__ sub_q_off,
+                                   uint64_t* __restrict__ sub_p_off) {
   __shared__ unsigned long long tmp[32];
-  unsigned long long br = 0, bq = 0;
+  unsigned long long br = 0, bq = 0, bp = 0;
   for (uint32_t c = 0; c < n; c += 1024) {
     const uint32_t i = c + threadIdx.x;
-    unsigned long long r = 0, q = 0;
+    unsigned long long r = 0, q = 0, pp = 0;
     if (i < n) {
       const uint32_t f = list[i];
       r = rec_off[f + 1] - rec_off[f];
       q = q_off[f + 1] - q_off[f];
+      pp = p_off[f + 1] - p_off[f];
     }
-    unsigned long long tr, tq;
+    unsigned long long tr, tq, tp;
     const unsigned long long er = block_excl_scan<1024, unsigned long long>(r, &tr, tmp);
     const unsigned long long eq = block_excl_scan<1024, unsigned long long>(q, &tq, tmp);
-    if (i < n) { sub_rec_off[i] = br + er; sub_q_off[i] = bq + eq; }
-    br += tr; bq += tq;
+    const unsigned long long ep = block_excl_scan<1024, unsigned long long>(pp, &tp, tmp);
+    if (i < n) { sub_rec_off[i] = br + er; sub_q_off[i] = bq + eq; sub_p_off[i] = bp + ep; }
+    br += tr; bq += tq; bp += tp;
   }
-  if (threadIdx.x == 0) { sub_rec_off[n] = br; sub_q_off[n] = bq; }
+  if (threadIdx.x == 0) { sub_rec_off[n] = br; sub_q_off[n] = bq; sub_p_off[n] = bp; }
+}
+
+// One CTA per listed frame: its block of the explicit mask into the compact batch.
+__global__ void k_fallback_mask(const uint32_t* __restrict__ list, const uint64_t* __restrict__ p_off,
+                                const uint64_t* __restrict__ sub_p_off, const float* __restrict__ mask,
+                                float* __restrict__ s_mask) {
+  const uint32_t i = blockIdx.x, f = list[i];
+  const uint64_t p0 = p_off[f], np = p_off[f + 1] - p0, d0 = sub_p_off[i];
+  for (uint64_t k = threadIdx.x; k < np; k += blockDim.x) s_mask[d0 + k] = mask[p0 + k];
 }
 
 // One CTA per listed frame: copy its records (and its questions' rule rows

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <cmath>
 #include <cstdio>
@@ -31,6 +32,7 @@
 #include "ffn.cuh"
 #include "attn_tc.cuh"
 #include "learn.cuh"
+#include "ozaki.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 
@@ -50,17 +52,14 @@ struct DevBuf {
   }
 };
 
-cudaError_t ensure(DevBuf& b, size_t bytes) {
-  if (bytes <= b.cap && b.p) return cudaSuccess;
-  if (b.p) cudaFree(b.p);
-  b.p = nullptr;
-  b.cap = 0;
-  size_t want = bytes < 256 ? 256 : bytes;
-  want = (want + 255) & ~size_t(255);
-  cudaError_t e = cudaMalloc(&b.p, want);
-  if (e == cudaSuccess) b.cap = want;
-  return e;
+double now_ms() {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
+
+// Workspace reallocations made by this thread, and the time they took (a
+// cudaFree waits for the device): the stream's worker reports them per batch.
+thread_local uint64_t t_grows = 0;
+thread_local double t_grow_ms = 0;
 
 template <typename T>
 T* P(DevBuf& b) { return static_cast<T*>(b.p); }
@@ -214,6 +213,19 @@ struct kc_handle {
   // KC_NO_FUSION=1 in the environment at kc_create runs the unfused sequence
   // (the same arithmetic, kept for the learn path and checked against the fused)
   bool fuse = true;
+  // the exact path's GEMMs on the int8 tensor cores (ozaki.cuh), with the
+  // FP64 kernel's results; KC_NO_OZAKI=1 at kc_create keeps them on the FP64
+  // kernel. oz_suspend runs a forward again on the FP64 kernel after a list
+  // overflow.
+  bool oz = true, oz_suspend = false, oz_ran = false;
+  long long oz_cap = -1;            // KC_OZAKI_LIST_CAP at kc_create: the list's length (tests); -1 sized by M·N
+  DevBuf oz_w;                      // weight slices and row data per forward matrix
+  std::vector<uint64_t> oz_w_off;   // per matrix (forward ones only): offset into oz_w
+  std::vector<char> oz_dirty;       // per matrix: its slices are stale
+  DevBuf oz_a, oz_meta, oz_list;    // A slices, A row data, the listed outputs
+  unsigned* d_oz_word = nullptr;    // [0] listed outputs of the current product, [1] error bits,
+                                    // [2..3] outputs listed since the last profile read (u64)
+  int* h_oz_err = nullptr;          // pinned
   // precision
   int precision = KC_PRECISION_CERTIFIED;
   // the certification margin: kappa0 (kc_set_precision may set it) times
@@ -222,6 +234,8 @@ struct kc_handle {
   float* d_audit = nullptr;         // [1] largest |s^ - s| / B over the last batch's recomputed pairs (float bits)
   float* h_audit = nullptr;         // pinned copy
   bool audit_pending = false;       // h_audit holds an unread audit
+  double host_wait_ms = 0;          // time the host spent blocked in wait_stream (the stream's worker reports it)
+  std::vector<void*> retired;       // workspace buffers replaced since the last stream wait (ensure)
   int sa = 10;                      // activations are split at x * 2^sa
   // test hook (kc_inject_wait_expiry): the next launch of this tensor-core
   // kernel (KC_INJECT_*) reports an expired wait before it issues any copy
@@ -247,6 +261,36 @@ struct kc_handle {
 
 namespace {
 
+// A workspace buffer of at least `bytes`. A buffer that must grow again gets
+// an eighth more than asked, so that batches of slowly rising size (rolling
+// stream batches, the varying number of recomputed frames) do not reallocate
+// at every new high. The buffer it replaces may still be read by work queued
+// on the stream, and cudaFree would wait for the whole device in the middle
+// of a batch: it is retired instead and freed after the next stream wait.
+cudaError_t ensure(kc_handle* h, DevBuf& b, size_t bytes) {
+  if (bytes <= b.cap && b.p) return cudaSuccess;
+  const double t0 = now_ms();
+  const bool regrow = b.p != nullptr;
+  if (b.p) h->retired.push_back(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  size_t want = bytes < 256 ? 256 : bytes;
+  if (regrow) want += want / 8;
+  want = (want + 255) & ~size_t(255);
+  cudaError_t e = cudaMalloc(&b.p, want);
+  if (e == cudaSuccess) b.cap = want;
+  t_grows++;
+  t_grow_ms += now_ms() - t0;
+  return e;
+}
+
+// Frees the buffers ensure retired; only after a wait for the stream, when
+// nothing queued can still read them.
+void release_retired(kc_handle* h) {
+  for (void* p : h->retired) cudaFree(p);
+  h->retired.clear();
+}
+
 kc_status fail(kc_handle* h, kc_status s, const std::string& msg) {
   if (h) h->err = msg;
   else g_create_error = msg;
@@ -256,6 +300,15 @@ kc_status fail(kc_handle* h, kc_status s, const std::string& msg) {
 kc_status cuda_fail(kc_handle* h, cudaError_t e, const char* what) {
   return fail(h, e == cudaErrorMemoryAllocation ? KC_ERR_CAPACITY : KC_ERR_CUDA,
               std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// The batch path's host waits for its stream, timed.
+cudaError_t wait_stream(kc_handle* h) {
+  const double t0 = now_ms();
+  const cudaError_t e = cudaStreamSynchronize(h->stream);
+  h->host_wait_ms += now_ms() - t0;
+  if (e == cudaSuccess && !h->retired.empty()) release_retired(h);
+  return e;
 }
 
 #define KC_TRY(expr, what)                                     \
@@ -366,7 +419,7 @@ kc_status dgemm_ld(kc_handle* h, const float* A, uint32_t lda, const float* B, f
 kc_status build_transposes(kc_handle* h) {
   if (!h->wt_blocks_dirty && !h->wt_sel_dirty) return KC_OK;
   const Dims& d = h->d;
-  KC_TRY(ensure(h->wt, d.total * 4), "transposed weights");
+  KC_TRY(ensure(h, h->wt, d.total * 4), "transposed weights");
   float* wt = P<float>(h->wt);
   auto tr = [&](uint64_t off, uint32_t n, uint32_t k) {
     dim3 grid((k + 31) / 32, (n + 31) / 32);
@@ -412,7 +465,7 @@ kc_status build_images(kc_handle* h) {
       h->img_off[i] = off;
       off += uint64_t(m[i].n) * m[i].k * 4;  // hi + lo fp16
     }
-    KC_TRY(ensure(h->images, off), "weight images");
+    KC_TRY(ensure(h, h->images, off), "weight images");
   }
   for (size_t i = 0; i < m.size(); i++) {
     if (!h->mat_dirty[i]) continue;
@@ -528,8 +581,8 @@ uint64_t attn_tiles(uint64_t T) { return (T + kc::tc::kAtWindow - 1) / kc::tc::k
 kc_status attn_prepare(kc_handle* h, Workspace& ws, uint64_t T) {
   if (T == 0) return KC_OK;
   const uint64_t tiles = attn_tiles(T);
-  KC_TRY(ensure(ws.tile_row, (tiles + 1) * 4), "workspace");
-  KC_TRY(ensure(ws.row_rc, T * 4), "workspace");
+  KC_TRY(ensure(h, ws.tile_row, (tiles + 1) * 4), "workspace");
+  KC_TRY(ensure(h, ws.row_rc, T * 4), "workspace");
   kc::tc::k_attn_tiles<<<unsigned((T + 255) / 256), 256, 0, h->stream>>>(
       P<uint32_t>(ws.tok_recpos), P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), int(T), int(tiles),
       P<uint32_t>(ws.row_rc), P<int>(ws.tile_row));
@@ -561,14 +614,106 @@ kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, co
   return KC_OK;
 }
 
-// One GEMM of the exact sequence: on the FP64 pipe in the oracle's order, or
-// (tc) on the tensor cores, where `mat` names the matrix in the tensor-core
+// Whether an exact-path product can run on the int8 tensor cores: a forward
+// matrix of the list read from the weight page, K a multiple of 128 up to
+// 512, N a multiple of 64, A rows 16-byte aligned.
+bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, int mat, const float* B, uint32_t ldb, uint32_t N,
+             uint32_t K) {
+  if (!h->oz || h->oz_suspend || mat < 0 || size_t(mat) >= h->mats.size()) return false;
+  const Mat& mt = h->mats[mat];
+  return !mt.transposed && mt.page_off % 4 == 0 && mt.n == N && mt.k == K && B == h->w + mt.page_off && ldb == K &&
+         K % 128 == 0 &&
+         K <= uint32_t(kc::oz::kMaxK) && N % 64 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+}
+
+// The slices and row data of forward matrix `mat` (rebuilt after a sync
+// changed it): [6][N][K] int8, then l1 [N], l2 [N] (f64), e [N] (int).
+kc_status oz_weights(kc_handle* h, int mat) {
+  const auto& m = h->mats;
+  if (h->oz_w_off.size() != m.size()) {
+    h->oz_w_off.assign(m.size(), 0);
+    uint64_t off = 0;
+    for (size_t i = 0; i < m.size(); i++) {
+      if (m[i].transposed) continue;
+      h->oz_w_off[i] = off;
+      off += (uint64_t(m[i].n) * m[i].k * kc::oz::kSlices + uint64_t(m[i].n) * 20 + 255) & ~uint64_t(255);
+    }
+    KC_TRY(ensure(h, h->oz_w, off), "weight slices");
+  }
+  if (!h->oz_dirty[mat]) return KC_OK;
+  h->oz_dirty[mat] = 0;
+  const Mat& mt = m[mat];
+  uint8_t* base = P<uint8_t>(h->oz_w) + h->oz_w_off[mat];
+  const uint64_t plane = uint64_t(mt.n) * mt.k;
+  double* l1 = reinterpret_cast<double*>(base + plane * kc::oz::kSlices);
+  kc::oz::SliceArgs sa{h->w + mt.page_off, mt.n, int(mt.k), mt.k, base, plane, reinterpret_cast<int*>(l1 + 2 * mt.n),
+                       l1, l1 + mt.n, nullptr};
+  kc::oz::k_oz_slice<<<(mt.n + 7) / 8, 256, 0, h->stream>>>(sa);
+  h->launches++;
+  KC_TRY(cudaGetLastError(), "weight slices");
+  return KC_OK;
+}
+
+// C (= epilogue) A·Wᵀ for forward matrix `mat` on the int8 tensor cores:
+// slice A, the product (outputs it cannot settle are listed), the listed
+// outputs by the sequential chain. The same f32 results as dgemm.
+template <int EPI>
+kc_status oz_gemm(kc_handle* h, const float* A, uint32_t lda, uint64_t M, int mat, float* C, uint32_t N, uint32_t K,
+                  const float* gate) {
+  if (M == 0) return KC_OK;
+  KC_CHECK(oz_weights(h, mat));
+  const Mat& mt = h->mats[mat];
+  const uint64_t plane = M * K;
+  KC_TRY(ensure(h, h->oz_a, plane * kc::oz::kSlices), "workspace");
+  KC_TRY(ensure(h, h->oz_meta, M * 20), "workspace");
+  const uint64_t cap = h->oz_cap >= 0 ? uint64_t(h->oz_cap) : std::max<uint64_t>(65536, M * N / 128);
+  KC_TRY(ensure(h, h->oz_list, cap * 8), "workspace");
+  double* l1a = P<double>(h->oz_meta);
+  int* ea = reinterpret_cast<int*>(l1a + 2 * M);
+  unsigned* count = h->d_oz_word;
+  kc::oz::SliceArgs sa{A, M, int(K), lda, P<uint8_t>(h->oz_a), plane, ea, l1a, l1a + M, count};
+  kc::oz::k_oz_slice<<<unsigned((M + 7) / 8), 256, 0, h->stream>>>(sa);
+  const uint8_t* wb = P<uint8_t>(h->oz_w) + h->oz_w_off[mat];
+  const uint64_t wplane = uint64_t(mt.n) * mt.k;
+  const double* l1b = reinterpret_cast<const double*>(wb + wplane * kc::oz::kSlices);
+  CUtensorMap amap, bmap;
+  if (!kc::oz::make_slice_map(&amap, P<uint8_t>(h->oz_a), M, K, kc::oz::kBM) ||
+      !kc::oz::make_slice_map(&bmap, wb, N, K, kc::oz::kBN))
+    return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a sliced operand");
+  kc::oz::GemmArgs g{};
+  g.M = int(M); g.N = int(N); g.K = int(K);
+  g.ea = ea; g.l1a = l1a; g.l2a = l1a + M;
+  g.eb = reinterpret_cast<const int*>(l1b + 2 * mt.n); g.l1b = l1b; g.l2b = l1b + mt.n;
+  g.C = C; g.ldc = int(N); g.gate = gate;
+  g.list = P<unsigned long long>(h->oz_list); g.count = count; g.cap = unsigned(cap);
+  g.err = reinterpret_cast<int*>(count + 1);
+  g.c2 = kc::oz::dropped_levels_bound(int(K));
+  g.gamma = kc::oz::chain_gamma(int(K));
+  g.inject_expiry = take_injection(h, KC_INJECT_EXACT_GEMM);
+  const uint64_t tiles = ((M + kc::oz::kBM - 1) / kc::oz::kBM) * (N / kc::oz::kBN);
+  const unsigned grid = unsigned(std::min<uint64_t>(tiles, uint64_t(h->sms)));
+  kc::oz::k_oz_gemm<EPI><<<grid, kc::oz::kThreads, kc::oz::kSmem, h->stream>>>(amap, bmap, g);
+  kc::oz::FixupArgs fx{A, lda, h->w + mt.page_off, K, int(K), C, int(N), gate, g.list, count, unsigned(cap),
+                       reinterpret_cast<unsigned long long*>(count + 2)};
+  kc::oz::k_oz_fixup<EPI><<<unsigned(h->sms) * 2, 256, 0, h->stream>>>(fx);
+  h->launches += 3;
+  h->oz_ran = true;
+  h->prof.oz_products++;
+  h->prof.oz_outputs += double(M) * N;
+  KC_TRY(cudaGetLastError(), "sliced product");
+  return KC_OK;
+}
+
+// One GEMM of the exact sequence: on the FP64 pipe in the oracle's order (or
+// with the same results on the int8 tensor cores, oz_gemm), or (tc) on the
+// split-fp16 tensor cores, where `mat` names the matrix in the tensor-core
 // list and B / ldb the same matrix for the FP64 kernel. The tensor-core path
 // reads A with row stride K.
 template <int EPI>
 kc_status gemm(kc_handle* h, bool tc, const float* A, uint32_t lda, uint64_t M, int mat, const float* B,
                uint32_t ldb, float* C, uint32_t N, uint32_t K, const float* gate = nullptr) {
   if (tc) return tc_gemm<EPI>(h, A, M, mat, C, gate);
+  if (oz_fits(h, A, lda, mat, B, ldb, N, K)) return oz_gemm<EPI>(h, A, lda, M, mat, C, N, K, gate);
   return dgemm_ld<EPI>(h, A, lda, B, C, M, N, K, gate, ldb);
 }
 
@@ -582,6 +727,8 @@ struct DevBatch {
   const double* uniforms = nullptr;
   const uint32_t* word_ids = nullptr;  // the same-word bias (null or alpha 0: none)
   float word_alpha = 0.0f;
+  const float* mask = nullptr;         // explicit selection mask laid out like p (null: the rule, or open)
+  uint64_t mask_len = UINT64_MAX;      // its entries when staged here (checked against the packed size)
 };
 
 const char* bad_message(uint32_t code) {
@@ -606,17 +753,17 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
   const uint32_t F = b.frames;
   const uint64_t N = b.records;
   if (F == 0) return fail(h, KC_ERR_INVALID_ARG, "a batch with no frames");
-  KC_TRY(ensure(ws.rec_meta, N * sizeof(uint2)), "workspace");
-  KC_TRY(ensure(ws.frame_t, F * 4ull), "workspace");
-  KC_TRY(ensure(ws.frame_q, F * 4ull), "workspace");
-  KC_TRY(ensure(ws.frame_r, F * 4ull), "workspace");
-  KC_TRY(ensure(ws.t_off, (F + 1) * 8ull), "workspace");
-  KC_TRY(ensure(ws.q_off, (F + 1) * 8ull), "workspace");
-  KC_TRY(ensure(ws.r_off, (F + 1) * 8ull), "workspace");
-  KC_TRY(ensure(ws.p_off, (F + 1) * 8ull), "workspace");
-  KC_TRY(ensure(ws.totals, sizeof(kc::FrameTotals)), "workspace");
-  KC_TRY(ensure(ws.rec_start, N * 4), "workspace");
-  KC_TRY(ensure(ws.rec_row, N * 4), "workspace");
+  KC_TRY(ensure(h, ws.rec_meta, N * sizeof(uint2)), "workspace");
+  KC_TRY(ensure(h, ws.frame_t, F * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.frame_q, F * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.frame_r, F * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.t_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, ws.q_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, ws.r_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, ws.p_off, (F + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, ws.totals, sizeof(kc::FrameTotals)), "workspace");
+  KC_TRY(ensure(h, ws.rec_start, N * 4), "workspace");
+  KC_TRY(ensure(h, ws.rec_row, N * 4), "workspace");
   kc::FrameTotals* dtot = P<kc::FrameTotals>(ws.totals);
   {
     ProfScope ps(h, kStPack);
@@ -632,7 +779,7 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
     h->launches += 2;
     KC_TRY(cudaMemcpyAsync(h->h_tot, dtot, sizeof(kc::FrameTotals), cudaMemcpyDeviceToHost, h->stream), "readback");
   }
-  KC_TRY(cudaStreamSynchronize(h->stream), "pack");
+  KC_TRY(wait_stream(h), "pack");
   const kc::FrameTotals tot = *h->h_tot;
   if (tot.bad) {
     char buf[160];
@@ -644,28 +791,28 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
   }
   const uint64_t T = tot.t, Q = tot.q, R = tot.r, PP = tot.p;
   const uint32_t H = d.h, FF = d.ffn;
-  KC_TRY(ensure(ws.tok_recpos, T * 4), "workspace");
-  KC_TRY(ensure(ws.bank_rec, R * 4), "workspace");
-  KC_TRY(ensure(ws.bank_frame, R * 4), "workspace");
-  KC_TRY(ensure(ws.query_rec, Q * 4), "workspace");
-  KC_TRY(ensure(ws.query_frame, Q * 4), "workspace");
-  KC_TRY(ensure(ws.x, T * H * 4), "workspace");
-  KC_TRY(ensure(ws.qkv, T * (3 * H > FF ? 3 * H : FF) * 4ull), "workspace");
-  KC_TRY(ensure(ws.bk, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.bv, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.mk, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.mv, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.sk, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.qstate, Q * H * 4), "workspace");
-  KC_TRY(ensure(ws.mq, Q * H * 4), "workspace");
-  KC_TRY(ensure(ws.sq, Q * H * 4), "workspace");
-  KC_TRY(ensure(ws.mh, Q * FF * 4ull), "workspace");
-  KC_TRY(ensure(ws.p, PP * 4), "workspace");
-  KC_TRY(ensure(ws.index, Q * 4), "workspace");
-  KC_TRY(ensure(ws.flags, F * 4ull), "workspace");
-  KC_TRY(ensure(ws.nq, Q * 4), "workspace");
-  KC_TRY(ensure(ws.nk, R * 4), "workspace");
-  KC_TRY(ensure(ws.kappa, Q * 4), "workspace");
+  KC_TRY(ensure(h, ws.tok_recpos, T * 4), "workspace");
+  KC_TRY(ensure(h, ws.bank_rec, R * 4), "workspace");
+  KC_TRY(ensure(h, ws.bank_frame, R * 4), "workspace");
+  KC_TRY(ensure(h, ws.query_rec, Q * 4), "workspace");
+  KC_TRY(ensure(h, ws.query_frame, Q * 4), "workspace");
+  KC_TRY(ensure(h, ws.x, T * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.qkv, T * (3 * H > FF ? 3 * H : FF) * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.bk, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.bv, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.mk, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.mv, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.sk, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.qstate, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.mq, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.sq, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.mh, Q * FF * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.p, PP * 4), "workspace");
+  KC_TRY(ensure(h, ws.index, Q * 4), "workspace");
+  KC_TRY(ensure(h, ws.flags, F * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.nq, Q * 4), "workspace");
+  KC_TRY(ensure(h, ws.nk, R * 4), "workspace");
+  KC_TRY(ensure(h, ws.kappa, Q * 4), "workspace");
   {
     ProfScope ps(h, kStPack);
     kc::k_record_rows<256><<<F, 256, 0, h->stream>>>(
@@ -717,6 +864,8 @@ void launch_select_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const k
   if (mask) {
     sa.mask = mask; sa.schema_allow = nullptr; sa.band_allow = nullptr; sa.uniforms = nullptr;
     sa.bank_values = P<float>(ws.bv); sa.gather = gather;
+  } else if (b.mask) {  // a batch's explicit mask, in place of the rule
+    sa.mask = b.mask; sa.schema_allow = nullptr; sa.band_allow = nullptr;
   }
   select_exact(h, sa, b.frames, tot.max_q, uint32_t(tot.q), tot.max_r);
 }
@@ -741,8 +890,8 @@ void launch_embed(kc_handle* h, Workspace& ws, const DevBatch& b, float* x, uint
 
 // The forward in the oracle's exact arithmetic (exact.cuh). Results stay in
 // the workspace: qstate [Q,H], bk/bv [R,H], p, index.
-kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
-                        bool encode_only, const Saves* sv = nullptr, bool tc = false) {
+kc_status forward_exact_pass(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
+                             bool encode_only, const Saves* sv, bool tc) {
   const Dims& d = h->d;
   const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r;
   const uint32_t H = d.h, FF = d.ffn;
@@ -834,6 +983,34 @@ kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
   return KC_OK;
 }
 
+// forward_exact_pass, whose products run on the int8 tensor cores where they
+// fit (oz_gemm). Their error word is read once at the end: an expired wait
+// fails the call; a product that listed more outputs than its list holds
+// sends the whole forward again through the FP64 kernel.
+kc_status forward_exact(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot,
+                        bool encode_only, const Saves* sv = nullptr, bool tc = false) {
+  const bool armed = !tc && h->oz && !h->oz_suspend;
+  if (armed) {
+    h->oz_ran = false;
+    KC_TRY(cudaMemsetAsync(h->d_oz_word + 1, 0, sizeof(unsigned), h->stream), "memset");
+  }
+  kc_status s = forward_exact_pass(h, ws, b, tot, encode_only, sv, tc);
+  if (s || !armed || !h->oz_ran) return s;
+  KC_TRY(cudaMemcpyAsync(h->h_oz_err, h->d_oz_word + 1, sizeof(int), cudaMemcpyDeviceToHost, h->stream),
+         "readback");
+  KC_TRY(wait_stream(h), "exact");
+  const int e = *h->h_oz_err;
+  if (e & kc::tc::kErrTimeout)
+    return fail(h, KC_ERR_TIMEOUT, "a tensor-core pipeline wait expired; the batch was not completed");
+  if (e & kc::oz::kOzListFull) {
+    h->prof.oz_reruns++;
+    h->oz_suspend = true;
+    s = forward_exact_pass(h, ws, b, tot, encode_only, sv, tc);
+    h->oz_suspend = false;
+  }
+  return s;
+}
+
 // The certified selection over the resident sq / sk of a packed batch: p,
 // indices and the per-frame flags of decisions it cannot certify.
 void launch_select_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
@@ -843,6 +1020,8 @@ void launch_select_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc
   sa.q_off = P<uint64_t>(ws.q_off); sa.p_off = P<uint64_t>(ws.p_off);
   sa.schema_allow = b.schema_allow; sa.band_allow = b.band_allow;
   sa.bank_rec = P<uint32_t>(ws.bank_rec); sa.schema_ids = b.schema_ids; sa.band_ids = b.band_ids;
+  sa.mask = b.mask;
+  if (b.mask) sa.schema_allow = sa.band_allow = nullptr;
   sa.uniforms = b.uniforms; sa.max_r = std::max<uint32_t>(tot.max_r, 1); sa.qc = sel_chunk(tot.max_r);
   sa.chunks = int((std::max<uint32_t>(tot.max_q, 1) + sa.qc - 1) / sa.qc);
   sa.scale = float(1.0 / std::sqrt(double(h->d.h)));
@@ -971,7 +1150,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
 // violation is counted and later batches run with four times the margin.
 void audit_collect(kc_handle* h) {
   if (!h->audit_pending) return;
-  cudaStreamSynchronize(h->stream);
+  wait_stream(h);
   h->audit_pending = false;
   const float r = *h->h_audit;
   h->prof.cert_audit_max = std::max(h->prof.cert_audit_max, double(r));
@@ -996,7 +1175,7 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   }
   KC_TRY(cudaMemcpyAsync(h->h_flags_pinned, ws.flags.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
   KC_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(cudaStreamSynchronize(h->stream), "certify");
+  KC_TRY(wait_stream(h), "certify");
   const int e = *h->h_err;
   if (e & kc::tc::kErrTimeout)
     return fail(h, KC_ERR_TIMEOUT, "a tensor-core pipeline wait expired; the batch was not completed");
@@ -1012,30 +1191,39 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   h->prof.fallback_frames += list.size();
   const uint32_t n = uint32_t(list.size());
   Workspace& fb = h->ws_fb;
-  KC_TRY(ensure(fb.list, n * 4ull), "workspace");
-  KC_TRY(ensure(fb.rec_off, (n + 1) * 8ull), "workspace");
-  KC_TRY(ensure(fb.uniforms, (n + 1) * 8ull), "workspace");  // sub question offsets
+  KC_TRY(ensure(h, fb.list, n * 4ull), "workspace");
+  KC_TRY(ensure(h, fb.rec_off, (n + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, fb.uniforms, (n + 1) * 8ull), "workspace");  // sub question offsets
   KC_TRY(cudaMemcpyAsync(fb.list.p, list.data(), n * 4ull, cudaMemcpyHostToDevice, h->stream), "upload");
+  KC_TRY(ensure(h, fb.rows_val, (n + 1) * 8ull), "workspace");  // sub p offsets, for an explicit mask
   kc::k_fallback_offsets<<<1, 1024, 0, h->stream>>>(P<uint32_t>(fb.list), n, b.rec_off, P<uint64_t>(ws.q_off),
-                                                    P<uint64_t>(fb.rec_off), P<uint64_t>(fb.uniforms));
+                                                    P<uint64_t>(ws.p_off), P<uint64_t>(fb.rec_off),
+                                                    P<uint64_t>(fb.uniforms), P<uint64_t>(fb.rows_val));
   h->launches++;
-  uint64_t sizes[2];
+  uint64_t sizes[3];
   KC_TRY(cudaMemcpyAsync(&sizes[0], P<uint64_t>(fb.rec_off) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
   KC_TRY(cudaMemcpyAsync(&sizes[1], P<uint64_t>(fb.uniforms) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(cudaStreamSynchronize(h->stream), "certify");
-  const uint64_t nrec = sizes[0], nq = sizes[1];
+  KC_TRY(cudaMemcpyAsync(&sizes[2], P<uint64_t>(fb.rows_val) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(wait_stream(h), "certify");
+  const uint64_t nrec = sizes[0], nq = sizes[1], np = sizes[2];
   // the sub question offsets live in fb.uniforms until the gather; move them
-  KC_TRY(ensure(fb.rows_off, (n + 1) * 8ull), "workspace");
+  KC_TRY(ensure(h, fb.rows_off, (n + 1) * 8ull), "workspace");
   KC_TRY(cudaMemcpyAsync(fb.rows_off.p, fb.uniforms.p, (n + 1) * 8ull, cudaMemcpyDeviceToDevice, h->stream), "copy");
-  KC_TRY(ensure(fb.token_ids, nrec * 32), "workspace");
-  KC_TRY(ensure(fb.field_roles, nrec * 32), "workspace");
-  KC_TRY(ensure(fb.schema_ids, nrec * 4), "workspace");
-  KC_TRY(ensure(fb.band_ids, nrec * 4), "workspace");
-  KC_TRY(ensure(fb.schema_allow, nq * 32 + 32), "workspace");
-  KC_TRY(ensure(fb.band_allow, nq * 4 + 4), "workspace");
-  KC_TRY(ensure(fb.uniforms, nq * 8 + 8), "workspace");
+  KC_TRY(ensure(h, fb.token_ids, nrec * 32), "workspace");
+  KC_TRY(ensure(h, fb.field_roles, nrec * 32), "workspace");
+  KC_TRY(ensure(h, fb.schema_ids, nrec * 4), "workspace");
+  KC_TRY(ensure(h, fb.band_ids, nrec * 4), "workspace");
+  KC_TRY(ensure(h, fb.schema_allow, nq * 32 + 32), "workspace");
+  KC_TRY(ensure(h, fb.band_allow, nq * 4 + 4), "workspace");
+  KC_TRY(ensure(h, fb.uniforms, nq * 8 + 8), "workspace");
   const bool words = b.word_ids && b.word_alpha != 0.0f;
-  if (words) KC_TRY(ensure(fb.word_ids, nrec * 32), "workspace");
+  if (words) KC_TRY(ensure(h, fb.word_ids, nrec * 32), "workspace");
+  if (b.mask) {
+    KC_TRY(ensure(h, fb.mask, np * 4 + 4), "workspace");
+    kc::k_fallback_mask<<<n, 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.p_off),
+                                                  P<uint64_t>(fb.rows_val), b.mask, P<float>(fb.mask));
+    h->launches++;
+  }
   kc::k_fallback_gather<<<n, 256, 0, h->stream>>>(
       P<uint32_t>(fb.list), b.rec_off, P<uint64_t>(ws.q_off), P<uint64_t>(fb.rec_off), P<uint64_t>(fb.rows_off),
       b.token_ids, b.field_roles, b.schema_ids, b.band_ids, b.schema_allow, b.band_allow, b.uniforms,
@@ -1052,12 +1240,13 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   sub.uniforms = b.uniforms ? P<double>(fb.uniforms) : nullptr;
   sub.word_ids = words ? P<uint32_t>(fb.word_ids) : nullptr;
   sub.word_alpha = b.word_alpha;
+  if (b.mask) { sub.mask = P<float>(fb.mask); sub.mask_len = np; }
   kc::FrameTotals sub_tot;
   KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
   // audit the margin on the recomputed frames: the fast scores against the exact ones
   KC_TRY(cudaMemsetAsync(h->d_audit, 0, sizeof(float), h->stream), "memset");
-  kc::k_cert_audit<<<n, 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+  kc::k_cert_audit<<<dim3(n, 32), 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
                                              P<uint64_t>(fb.q_off), P<uint64_t>(fb.r_off), P<float>(ws.sq),
                                              P<float>(ws.sk), P<float>(fb.sq), P<float>(fb.sk), P<float>(ws.nq),
                                              P<float>(ws.nk), P<float>(ws.kappa),
@@ -1082,6 +1271,8 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
 kc_status run_batch(kc_handle* h, const DevBatch& b, bool encode_only, kc::FrameTotals* tot_out) {
   kc::FrameTotals tot;
   KC_CHECK(pack_batch(h, h->ws, b, &tot));
+  if (b.mask && tot.p > b.mask_len)
+    return fail(h, KC_ERR_INVALID_ARG, "the selection mask is smaller than the batch's sum of Q_f * R_f");
   if (encode_only || h->precision == KC_PRECISION_EXACT) {
     KC_CHECK(forward_exact(h, h->ws, b, tot, encode_only));
   } else {
@@ -1157,8 +1348,8 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
       if (uint64_t(off) + d.h > d.emb_elems) return fail(h, KC_ERR_INVALID_ARG, "embedding row outside the page");
       memcpy(&vals[uint64_t(i) * d.h], w->embeddings + off, d.h * 4);
     }
-    KC_TRY(ensure(h->ws.rows_val, vals.size() * 4), "workspace");
-    KC_TRY(ensure(h->ws.rows_off, n * 4ull), "workspace");
+    KC_TRY(ensure(h, h->ws.rows_val, vals.size() * 4), "workspace");
+    KC_TRY(ensure(h, h->ws.rows_off, n * 4ull), "workspace");
     KC_TRY(cudaMemcpyAsync(h->ws.rows_val.p, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice, h->stream), "sync");
     KC_TRY(cudaMemcpyAsync(h->ws.rows_off.p, ch->embedding_rows, n * 4ull, cudaMemcpyHostToDevice, h->stream), "sync");
     k_scatter_rows<<<n, 128, 0, h->stream>>>(h->w, P<float>(h->ws.rows_val), P<uint32_t>(h->ws.rows_off), n, d.h);
@@ -1211,7 +1402,7 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
     const size_t nsel = nf - 2;            // the selector's two matrices end each half
     for (size_t j = 0; j < nf; j++) {
       h->mat_max[nf + j] = h->mat_max[j];
-      if (j < nsel ? blocks : sel) h->mat_dirty[j] = h->mat_dirty[nf + j] = 1;
+      if (j < nsel ? blocks : sel) h->mat_dirty[j] = h->mat_dirty[nf + j] = h->oz_dirty[j] = h->oz_dirty[nf + j] = 1;
     }
     h->wt_blocks_dirty |= blocks;
     h->wt_sel_dirty |= sel;
@@ -1222,7 +1413,7 @@ kc_status do_sync(kc_handle* h, const kc_weights_view* w, const kc_changes* ch) 
 
 template <typename T>
 kc_status stage(kc_handle* h, DevBuf& buf, const T* src, uint64_t n) {
-  KC_TRY(ensure(buf, n * sizeof(T)), "workspace");
+  KC_TRY(ensure(h, buf, n * sizeof(T)), "workspace");
   if (n) KC_TRY(cudaMemcpyAsync(buf.p, src, n * sizeof(T), cudaMemcpyHostToDevice, h->stream), "upload");
   return KC_OK;
 }
@@ -1300,7 +1491,7 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
   const uint32_t F = b.frames;
   const uint64_t N = b.records, T = tot.t, Q = tot.q, R = tot.r, PP = tot.p;
   const uint64_t H = d.h, FF = d.ffn;
-  auto need = [&](DevBuf& buf, uint64_t bytes) { return ensure(buf, bytes); };
+  auto need = [&](DevBuf& buf, uint64_t bytes) { return ensure(h, buf, bytes); };
   KC_TRY(need(bw.mask, PP * 4), "workspace");
   KC_TRY(need(bw.enc_qkv, uint64_t(d.enc) * T * 3 * H * 4), "workspace");
   KC_TRY(need(bw.enc_p, uint64_t(d.enc) * T * 32 * 4), "workspace");
@@ -1336,7 +1527,7 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
   KC_TRY(need(bw.dfs, T * H * 4), "workspace");
   KC_TRY(need(bw.dpool, F * 2 * H * 4), "workspace");
   KC_TRY(need(bw.edqkv, T * 3 * H * 4), "workspace");
-  KC_TRY(ensure(ws.gather, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.gather, Q * H * 4), "workspace");
   KC_CHECK(build_transposes(h));
   const float* wt = P<float>(h->wt);
   kc::BatchGeo geo{P<uint32_t>(ws.query_frame), P<uint32_t>(ws.bank_frame), P<uint64_t>(ws.q_off),
@@ -1526,6 +1717,10 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   {
     const char* nf = std::getenv("KC_NO_FUSION");
     h->fuse = !(nf && nf[0] && nf[0] != '0');
+    const char* no = std::getenv("KC_NO_OZAKI");
+    h->oz = !(no && no[0] && no[0] != '0');
+    const char* cap = std::getenv("KC_OZAKI_LIST_CAP");
+    if (cap && cap[0]) h->oz_cap = std::max(0ll, std::atoll(cap));
   }
   if (!weights_ok(h->d, weights)) {
     delete h;
@@ -1552,12 +1747,16 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   if ((e = cudaMallocHost(&h->h_tot, sizeof(kc::FrameTotals)))) return bail(e, "pinned");
   if ((e = cudaMallocHost(&h->h_err, sizeof(int)))) return bail(e, "pinned");
   if ((e = cudaMalloc(&h->d_err, sizeof(int)))) return bail(e, "error word");
+  if ((e = cudaMallocHost(&h->h_oz_err, sizeof(int)))) return bail(e, "pinned");
+  if ((e = cudaMalloc(&h->d_oz_word, 4 * sizeof(unsigned)))) return bail(e, "error word");
+  if ((e = cudaMemset(h->d_oz_word, 0, 4 * sizeof(unsigned)))) return bail(e, "error word");
   if ((e = cudaMallocHost(&h->h_audit, sizeof(float)))) return bail(e, "pinned");
   if ((e = cudaMalloc(&h->d_audit, sizeof(float)))) return bail(e, "audit word");
   if ((e = cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device))) return bail(e, "attributes");
   h->mats = mat_list(h->d);
   h->mat_max.assign(h->mats.size(), 0.f);
   h->mat_dirty.assign(h->mats.size(), 1);
+  h->oz_dirty.assign(h->mats.size(), 1);
   for (const Mat& m : h->mats)
     if (m.n % 128 || m.k % 64) {
       kc_destroy(h);
@@ -1603,6 +1802,15 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 int(KC_MAX_BANK) * 48)) ||
       (e = cudaFuncSetAttribute(kc::k_local_attn_back, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kLocalBackSmem))))
+    return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::oz::k_oz_gemm<kc::kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::oz::kSmem)) ||
+      (e = cudaFuncSetAttribute(kc::oz::k_oz_gemm<kc::kEpiRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::oz::kSmem)) ||
+      (e = cudaFuncSetAttribute(kc::oz::k_oz_gemm<kc::kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::oz::kSmem)) ||
+      (e = cudaFuncSetAttribute(kc::oz::k_oz_gemm<kc::kEpiGate>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::oz::kSmem)))
     return bail(e, "smem");
   s = do_sync(h, weights, nullptr);
   if (s) {
@@ -1683,11 +1891,11 @@ kc_status kc_select(kc_handle* h, const kc_encoded_view* enc, const float* mask,
       return s;
   }
   if (uniforms && (s = stage(h, ws.uniforms, uniforms, Q))) return s;
-  KC_TRY(ensure(ws.sq, Q * H * 4), "workspace");
-  KC_TRY(ensure(ws.sk, R * H * 4), "workspace");
-  KC_TRY(ensure(ws.p, uint64_t(Q) * R * 4), "workspace");
-  KC_TRY(ensure(ws.index, Q * 4ull), "workspace");
-  KC_TRY(ensure(ws.gather, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.sq, Q * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.sk, R * H * 4), "workspace");
+  KC_TRY(ensure(h, ws.p, uint64_t(Q) * R * 4), "workspace");
+  KC_TRY(ensure(h, ws.index, Q * 4ull), "workspace");
+  KC_TRY(ensure(h, ws.gather, Q * H * 4), "workspace");
   {
     ProfScope ps(h, kStSelector);
     dgemm<kc::kEpiStore>(h, P<float>(ws.qstate), h->w + h->d.off_swq, P<float>(ws.sq), Q, uint32_t(H), uint32_t(H));
@@ -1842,6 +2050,8 @@ kc_status forward_batch_host(kc_handle* h, const kc_batch_view* bv, kc_batch_out
   if (!bv || !out || bv->frames == 0) return fail(h, KC_ERR_INVALID_ARG, "batch arguments are incomplete");
   if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
     return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  if (bv->mask && bv->schema_allow)
+    return fail(h, KC_ERR_INVALID_ARG, "a batch takes a mask rule or an explicit mask, not both");
   DevBatch b;
   kc_status s = batch_host_common(h, bv, b);
   if (s) return s;
@@ -1863,6 +2073,17 @@ kc_status forward_batch_host(kc_handle* h, const kc_batch_view* bv, kc_batch_out
       if ((s = stage(h, ws.uniforms, bv->uniforms, nq))) return s;
       b.uniforms = P<double>(ws.uniforms);
     }
+  }
+  if (bv->mask) {  // sum_f Q_f * R_f, as the packer will lay p out
+    uint64_t np = 0;
+    for (uint32_t f = 0; f < bv->frames; f++) {
+      uint64_t q = 0;
+      for (uint64_t i = bv->rec_off[f]; i < bv->rec_off[f + 1]; i++) q += bv->band_ids[i] == KC_QUERY_BAND;
+      np += q * (bv->rec_off[f + 1] - bv->rec_off[f] - q);
+    }
+    if ((s = stage(h, ws.mask, bv->mask, np))) return s;
+    b.mask = P<float>(ws.mask);
+    b.mask_len = np;
   }
   kc::FrameTotals tot;
   if ((s = run_batch(h, b, false, &tot))) return s;
@@ -1892,7 +2113,7 @@ kc_status copy_out(kc_handle* h, uint32_t frames, const kc::FrameTotals& tot, kc
   if (out->q_off) KC_TRY(cudaMemcpyAsync(out->q_off, ws.q_off.p, (frames + 1ull) * 8, cudaMemcpyDeviceToHost, h->stream), "readback");
   if (out->query_output && tot.q)
     KC_TRY(cudaMemcpyAsync(out->query_output, ws.qstate.p, tot.q * h->d.h * 4, cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(cudaStreamSynchronize(h->stream), "batch");
+  KC_TRY(wait_stream(h), "batch");
   prof_collect(h);
   return KC_OK;
 }
@@ -1907,6 +2128,7 @@ kc_status select_batch_host(kc_handle* h, const kc_batch_select_view* sv, kc_bat
   const bool rule = sv && sv->schema_allow;
   if (sv && (sv->schema_allow == nullptr) != (sv->band_allow == nullptr))
     return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  if (rule && sv->mask) return fail(h, KC_ERR_INVALID_ARG, "a mask rule or an explicit mask, not both");
   Workspace& ws = h->ws;
   const kc::FrameTotals tot = h->resident_tot;
   DevBatch b;
@@ -1924,6 +2146,11 @@ kc_status select_batch_host(kc_handle* h, const kc_batch_select_view* sv, kc_bat
   if (sv && sv->uniforms) {
     if ((s = stage(h, ws.uniforms, sv->uniforms, tot.q))) return s;
     b.uniforms = P<double>(ws.uniforms);
+  }
+  if (sv && sv->mask) {
+    if ((s = stage(h, ws.mask, sv->mask, tot.p))) return s;
+    b.mask = P<float>(ws.mask);
+    b.mask_len = tot.p;
   }
   if (tot.q > 0) {
     const int precision = h->resident_precision;
@@ -1983,6 +2210,8 @@ kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_devi
     return fail(h, KC_ERR_INVALID_ARG, "token_ids must be 16-byte aligned and rec_off 8-byte aligned");
   if ((bv->schema_allow == nullptr) != (bv->band_allow == nullptr))
     return fail(h, KC_ERR_INVALID_ARG, "a mask rule needs both schema_allow and band_allow");
+  if (bv->mask && bv->schema_allow)
+    return fail(h, KC_ERR_INVALID_ARG, "a batch takes a mask rule or an explicit mask, not both");
   DevBatch b;
   b.frames = bv->frames; b.records = bv->records; b.rec_off = bv->rec_off;
   b.token_ids = bv->token_ids; b.field_roles = bv->field_roles; b.schema_ids = bv->schema_ids;
@@ -1990,6 +2219,7 @@ kc_status kc_forward_batch_device(kc_handle* h, const kc_batch_view* bv, kc_devi
   b.uniforms = bv->uniforms;
   b.word_ids = bv->word_ids;
   b.word_alpha = bv->word_alpha;
+  b.mask = bv->mask;
   kc::FrameTotals tot;
   kc_status s = run_batch(h, b, false, &tot);
   if (s) return s;
@@ -2108,7 +2338,7 @@ kc_status kc_learn_accumulate(kc_handle* h, const double* step, const double* va
   if (!step || !value_weight || !sums) return fail(h, KC_ERR_INVALID_ARG, "learn arguments are incomplete");
   const uint64_t H = h->d.h, E = 2 * H * H + 2 * H + 3 * H;
   const uint32_t chunks = (F + kc::kLearnChunk - 1) / kc::kLearnChunk;
-  KC_TRY(ensure(h->bw.learn_partial, uint64_t(chunks) * E * 8), "workspace");
+  KC_TRY(ensure(h, h->bw.learn_partial, uint64_t(chunks) * E * 8), "workspace");
   BackWs& bw = h->bw;
   kc::k_learn_partial<<<dim3(unsigned((E + 255) / 256), chunks), 256, 0, h->stream>>>(
       step, value_weight, P<float>(bw.dswq), P<float>(bw.dswk), P<float>(bw.dpool), P<float>(bw.dwv), F,
@@ -2194,9 +2424,9 @@ kc_status kc_learn_apply(kc_handle* h, const double* sums, const double* row_sum
   a.o = learn_opts(o);
   BackWs& bw = h->bw;
   const uint64_t elems = 2ull * d.h * d.h + 5ull * d.h + (a.row_sums ? uint64_t(a.rows) * d.h : 0);
-  KC_TRY(ensure(bw.learn_backup, elems * 4), "workspace");
-  KC_TRY(ensure(bw.learn_health, 4 * kc::kHealthGroups * 4), "workspace");
-  KC_TRY(ensure(bw.learn_out, (kc::kLearnResult + kc::kLearnReport) * 8), "workspace");
+  KC_TRY(ensure(h, bw.learn_backup, elems * 4), "workspace");
+  KC_TRY(ensure(h, bw.learn_health, 4 * kc::kHealthGroups * 4), "workspace");
+  KC_TRY(ensure(h, bw.learn_out, (kc::kLearnResult + kc::kLearnReport) * 8), "workspace");
   a.backup = P<float>(bw.learn_backup);
   a.health = P<unsigned>(bw.learn_health);
   a.result = P<double>(bw.learn_out);
@@ -2221,6 +2451,7 @@ kc_status kc_learn_apply(kc_handle* h, const double* sums, const double* row_sum
     h->mat_max[i] = h->mat_max[nf + i] = float(out[7]);
     h->mat_max[i + 1] = h->mat_max[nf + i + 1] = float(out[8]);
     h->mat_dirty[i] = h->mat_dirty[i + 1] = h->mat_dirty[nf + i] = h->mat_dirty[nf + i + 1] = 1;
+    h->oz_dirty[i] = h->oz_dirty[i + 1] = h->oz_dirty[nf + i] = h->oz_dirty[nf + i + 1] = 1;
     h->wt_sel_dirty = true;
   }
   return KC_OK;
@@ -2284,6 +2515,7 @@ kc_status kc_load_checkpoint(kc_handle* h, const void* bytes, uint64_t len, int*
     h->mat_max[i] = h->mat_max[nf + i] = amax(m.page_off, uint64_t(m.n) * m.k);
   }
   std::fill(h->mat_dirty.begin(), h->mat_dirty.end(), 1);
+  std::fill(h->oz_dirty.begin(), h->oz_dirty.end(), 1);
   h->wt_blocks_dirty = h->wt_sel_dirty = true;
   KC_TRY(cudaStreamSynchronize(h->stream), "checkpoint");
   return KC_OK;
@@ -2322,7 +2554,8 @@ kc_status kc_set_precision(kc_handle* h, int mode, float tau) {
 kc_status kc_inject_wait_expiry(kc_handle* h, int kernel) {
   if (!h) return fail(nullptr, KC_ERR_INVALID_ARG, "handle is null");
   std::lock_guard<std::mutex> lk(h->mu);
-  if (kernel != KC_INJECT_ATTN && kernel != KC_INJECT_FFN && kernel != KC_INJECT_GEMM)
+  if (kernel != KC_INJECT_ATTN && kernel != KC_INJECT_FFN && kernel != KC_INJECT_GEMM &&
+      kernel != KC_INJECT_EXACT_GEMM)
     return fail(h, KC_ERR_INVALID_ARG, "unknown tensor-core kernel for the injected expiry");
   h->inject = kernel;
   return KC_OK;
@@ -2333,7 +2566,18 @@ kc_status kc_set_stream(kc_handle* h, void* stream) {
   std::lock_guard<std::mutex> lk(h->mu);
   DeviceGuard dg(h->device);
   audit_collect(h);  // its readback is queued on the old stream
-  h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own;
+  const cudaStream_t next = stream ? static_cast<cudaStream_t>(stream) : h->own;
+  if (next != h->stream) {
+    // work on the new stream starts after everything queued on the old one
+    // (the workspace, and buffers retired but not yet freed, are shared)
+    cudaEvent_t ev;
+    KC_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
+    cudaError_t e = cudaEventRecord(ev, h->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(next, ev, 0);
+    cudaEventDestroy(ev);
+    KC_TRY(e, "stream order");
+  }
+  h->stream = next;
   return KC_OK;
 }
 
@@ -2360,9 +2604,16 @@ kc_status kc_profile_read(kc_handle* h, kc_stage_times* out, int reset) {
   DeviceGuard dg(h->device);
   prof_collect(h);
   audit_collect(h);
+  unsigned long long listed = 0;
+  if (h->d_oz_word) {
+    cudaMemcpyAsync(&listed, h->d_oz_word + 2, sizeof listed, cudaMemcpyDeviceToHost, h->stream);
+    cudaStreamSynchronize(h->stream);
+    if (reset) cudaMemsetAsync(h->d_oz_word + 2, 0, sizeof listed, h->stream);
+  }
   *out = h->prof;
   out->launches = h->launches;
   out->cert_kappa0 = double(h->kappa0) * h->kappa_mul;
+  out->oz_listed = listed;
   if (reset) h->prof = kc_stage_times{};
   return KC_OK;
 }
@@ -2375,6 +2626,8 @@ void kc_destroy(kc_handle* h) {
     std::lock_guard<std::mutex> lk(h->mu);
     DeviceGuard dg(h->device);
     if (h->own) cudaStreamSynchronize(h->own);
+    cudaStreamSynchronize(h->stream);
+    release_retired(h);
     DevBuf* bufs[] = {&h->ws.rec_off, &h->ws.token_ids, &h->ws.field_roles, &h->ws.schema_ids, &h->ws.band_ids,
                       &h->ws.schema_allow, &h->ws.band_allow, &h->ws.uniforms, &h->ws.mask, &h->ws.bank_schema,
                       &h->ws.bank_band, &h->ws.rec_meta, &h->ws.frame_t, &h->ws.frame_q, &h->ws.frame_r,
@@ -2404,6 +2657,8 @@ void kc_destroy(kc_handle* h) {
     for (DevBuf* b : bbufs)
       if (b->p) cudaFree(b->p), b->p = nullptr;
     if (h->d_err) cudaFree(h->d_err);
+    if (h->d_oz_word) cudaFree(h->d_oz_word);
+    if (h->h_oz_err) cudaFreeHost(h->h_oz_err);
     if (h->h_err) cudaFreeHost(h->h_err);
     if (h->d_audit) cudaFree(h->d_audit);
     if (h->h_audit) cudaFreeHost(h->h_audit);

@@ -1,0 +1,498 @@
+// ozaki.cuh — the exact path's GEMMs on the int8 tensor cores, with the
+// same f32 results as the FP64 kernel (k_dgemm_exact).
+//
+// matmulOracle (forward/oracle.ts:114-125) stores f32(c) where c is one f64
+// chain over k in order: c_k = fl(c_(k-1) + a_k·b_k), the products exact (two
+// f32 factors). That chain differs from the exact dot product y = Σ a_k b_k by
+// at most γ_(K-1)·Σ|a_k b_k| (γ_n = n·u / (1 − n·u), u = 2^-53). So whenever
+// y is known to lie in an interval [ŷ − E, ŷ + E] that also holds the chain
+// and whose two ends round to the same f32, that f32 IS the oracle's stored
+// value (rounding is monotone). The few outputs whose interval straddles a
+// rounding boundary are listed and recomputed by the sequential chain
+// (k_oz_fixup), so every output equals the FP64 kernel's bit for bit.
+//
+// ŷ comes from the integer tensor cores (the slicing idea of Ozaki, Ogita &
+// Oishi, "Error-free transformations of matrix multiplication by using fast
+// routines of matrix multiplication and its applications", Numer. Algorithms
+// 59, 2012, in the integer form of Ootomo, Ozaki & Yokota, IJHPCA 2024):
+//
+//   each row x of A (and of B, the weights [N, K]) gets an exponent e with
+//   max|x| < 2^e and six slices of x' = x·2^-e ∈ (−1, 1):
+//     s0 = floor(x'·2^7) ∈ [−128, 127] (signed int8), r0 = x'·2^7 − s0 ∈ [0, 1),
+//     s_i = floor(r_(i−1)·2^8) ∈ [0, 255] (unsigned int8), r_i = r_(i−1)·2^8 − s_i,
+//   so x' = s0·2^-7 + Σ_(i=1..5) s_i·2^(−7−8i) + r5·2^-47: 47 bits, every
+//   element within 2^23 of its row's largest is represented exactly, and the
+//   truncation is below 2^(e−47) (slicing rounds down);
+//
+//   the product of slices i of A and j of B is an exact integer (int8 MMA,
+//   s32 accumulation); pairs of one level L = i + j (weight 2^(−14−8L)) share
+//   one s32 accumulator in TMEM; levels 0..6 (26 pairs) are kept;
+//
+//   ŷ = 2^(ea+eb−62)·(2^32·((Q0·256 + Q1)·256 + Q2) + ((Q3·256 + Q4)·256 + Q5)·256 + Q6):
+//   both parts are exact 64-bit integers below 2^53 (K ≤ 512), so forming ŷ
+//   rounds once.
+//
+// The bound E per output (all terms rounded up, then doubled, which covers
+// the f64 rounding of the bound itself and of ŷ ± E):
+//   E1 slicing    2^(ea−47)·‖b‖₁ + 2^(eb−47)·(‖a‖₁ + K·2^(ea−47))
+//   E2 levels 7-10 (pairs i, j ∈ [2, 5]): K·255²·Σ_L n_L·2^(−14−8L)·2^(ea+eb)
+//   E3 forming ŷ  2^-53·|ŷ|
+//   E4 the chain  γ_(K−1)·‖a‖₂·‖b‖₂   (Σ|a_k b_k| ≤ ‖a‖₂‖b‖₂)
+// A row with a non-finite entry cannot be sliced: every output it touches
+// goes to the fixup. A list that overflows raises an error bit; the caller
+// then recomputes the whole forward on the FP64 kernel.
+//
+// One persistent CTA per SM, 192 threads:
+//   warp 0     TMA: per (128-row, 64-column) tile and 128-wide K chunk the
+//              six B slices (8 KB each) into a two-deep ring, then the six A
+//              slices (16 KB each) into a four-deep ring (3-D tensor maps over
+//              [slice][row][k] int8, 128-byte swizzle, zero fill past M);
+//   warp 1     MMA issuer: for A slice i, B slices j ≤ 6 − i into level i + j
+//              (four K steps of 32 each), s32 accumulators in TMEM;
+//   warps 2-5  epilogue: one output row per thread, 16 columns at a time.
+#pragma once
+#include "common.cuh"
+#include "tc_gemm.cuh"
+
+namespace kc {
+namespace oz {
+
+using tc::smem_u32;
+
+constexpr int kSlices = 6;
+constexpr int kLevels = 7;                       // L = 0..6 kept
+constexpr int kBM = 128, kBN = 64, kBK = 128;    // tile rows, tile columns, K bytes per chunk
+constexpr int kASlot = kBM * kBK;                // 16 KB: one A slice of one chunk
+constexpr int kBSlice = kBN * kBK;               // 8 KB: one B slice of one chunk
+constexpr int kBSlot = kSlices * kBSlice;        // 48 KB
+constexpr int kAStages = 4, kBStages = 2;
+constexpr int kThreads = 192;
+constexpr int kSmem = kAStages * kASlot + kBStages * kBSlot + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;              // 7 levels x 64 columns used
+constexpr int kSpecial = 0x7fffffff;             // a row with a non-finite entry
+constexpr int kMaxK = 512;
+// Error bits of the product's own word: an expired pipeline wait raises
+// tc::kErrTimeout (1), a full list kOzListFull.
+enum : int { kOzListFull = 4 };
+
+// ---------------------------------------------------------------------------
+// Slicing: one warp per row of X [rows, K] (row stride ldx, 16-byte aligned
+// rows, K % 128 == 0). Slice i of row r lands at slices + i·plane + r·K.
+// ---------------------------------------------------------------------------
+struct SliceArgs {
+  const float* X;
+  uint64_t rows;
+  int K;
+  uint64_t ldx;
+  uint8_t* slices;
+  uint64_t plane;          // rows·K (the slice stride)
+  int* e;                  // [rows]
+  double* l1;              // [rows] Σ|x|, rounded up
+  double* l2;              // [rows] sqrt(Σ x²), rounded up
+  unsigned* reset;         // optional: zeroed by the first thread (the next GEMM's list count)
+};
+
+__global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
+  if (a.reset && blockIdx.x == 0 && threadIdx.x == 0) *a.reset = 0u;
+  const int lane = threadIdx.x & 31;
+  const uint64_t r = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= a.rows) return;
+  const float* x = a.X + r * a.ldx;
+  const int chunks = a.K / 128;  // each lane holds 4 consecutive elements per 128-wide chunk
+  float4 v[kMaxK / 128];
+  float mx = 0.0f;
+  bool bad = false;
+  double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+  for (int c = 0; c < kMaxK / 128; c++) {
+    if (c >= chunks) break;
+    v[c] = *reinterpret_cast<const float4*>(x + c * 128 + lane * 4);
+    const float t[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float m = fabsf(t[q]);
+      bad |= !(m <= 3.4028234663852886e38f);  // inf or NaN
+      mx = fmaxf(mx, m);
+      s1 += double(m);
+      s2 = fma(double(t[q]), double(t[q]), s2);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    bad |= __shfl_xor_sync(0xffffffffu, int(bad), o) != 0;
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  int e = 0;
+  if (bad) e = kSpecial;
+  else if (mx > 0.0f) e = ilogbf(mx) + 1;  // 2^(e-1) <= max < 2^e
+  if (lane == 0) {
+    a.e[r] = e;
+    // the sums' own rounding (at most K·u relative) is covered by the factor
+    a.l1[r] = bad ? 0.0 : s1 * (1.0 + 0x1p-40);
+    a.l2[r] = bad ? 0.0 : sqrt(s2) * (1.0 + 0x1p-40);
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxK / 128; c++) {
+    if (c >= chunks) break;
+    const float t[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    uint32_t w[kSlices] = {0, 0, 0, 0, 0, 0};
+    if (!bad && mx > 0.0f) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        double y = ldexp(double(t[q]), 7 - e);  // x'·2^7, exact
+        const double s0 = floor(y);
+        w[0] |= (uint32_t(int(s0)) & 0xffu) << (8 * q);
+        y -= s0;
+#pragma unroll
+        for (int i = 1; i < kSlices; i++) {
+          y *= 256.0;
+          const double si = floor(y);
+          w[i] |= (uint32_t(si) & 0xffu) << (8 * q);
+          y -= si;
+        }
+      }
+    }
+    uint8_t* dst = a.slices + r * uint64_t(a.K) + c * 128 + lane * 4;
+#pragma unroll
+    for (int i = 0; i < kSlices; i++) *reinterpret_cast<uint32_t*>(dst + i * a.plane) = w[i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The product.
+// ---------------------------------------------------------------------------
+struct GemmArgs {
+  int M, N, K;
+  const int* ea;
+  const double *l1a, *l2a;
+  const int* eb;
+  const double *l1b, *l2b;
+  float* C;
+  int ldc;
+  const float* gate;            // kEpiGate: [M, ldc]
+  unsigned long long* list;     // flagged outputs: row << 32 | column
+  unsigned* count;
+  unsigned cap;
+  int* err;                     // tc::kErrTimeout / kOzListFull
+  double c2;                    // E2 / 2^(ea+eb)
+  double gamma;                 // γ_(K−1)
+  int inject_expiry;            // test hook: the producer reports an expired wait before it issues any copy
+};
+
+// Instruction descriptor: D s32, A / B int8 (signed for slice 0), K-major,
+// M = 128, N = 64.
+__host__ __device__ constexpr uint32_t idesc_i8(bool a_signed, bool b_signed) {
+  return (2u << 4) | (uint32_t(a_signed) << 7) | (uint32_t(b_signed) << 10) | (uint32_t(kBN >> 3) << 17) |
+         (uint32_t(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+
+// 3-D TMA load of one slice's [rows x 128 bytes] box at (k, row, slice).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit words from TMEM, without the wait.
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, int* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// One output's decision: the stored f32 (true) or a listing (false).
+__device__ __forceinline__ bool oz_decide(const int* q, int ea, double l1a, double l2a, int eb, double l1b,
+                                          double l2b, const GemmArgs& a, float* out) {
+  if (ea == kSpecial || eb == kSpecial) return false;
+  const long long hi = (static_cast<long long>(q[0]) * 256 + q[1]) * 256 + q[2];
+  const long long lo = ((static_cast<long long>(q[3]) * 256 + q[4]) * 256 + q[5]) * 256 + q[6];
+  const double y = ldexp(fma(double(hi), 0x1p32, double(lo)), ea + eb - 62);
+  const double e1 = ldexp(l1b, ea - 47) + ldexp(l1a, eb - 47) + ldexp(double(a.K), ea + eb - 94);
+  const double e2 = ldexp(a.c2, ea + eb);
+  const double e3 = fabs(y) * 0x1p-53;
+  const double e4 = a.gamma * (l2a * l2b);
+  const double err = 2.0 * (e1 + e2 + e3 + e4) + 0x1p-1060;  // (the last term: an ldexp that went subnormal)
+  const float lo_f = __double2float_rn(y - err), hi_f = __double2float_rn(y + err);
+  if (__float_as_uint(lo_f) != __float_as_uint(hi_f)) return false;
+  *out = lo_f;
+  return true;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__ CUtensorMap amap,
+                                                         const __grid_constant__ CUtensorMap bmap, GemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* aring = smem;
+  unsigned char* bring = smem + kAStages * kASlot;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + kBStages * kBSlot);
+  uint64_t* afull = bars;
+  uint64_t* aempty = afull + kAStages;
+  uint64_t* bfull = aempty + kAStages;
+  uint64_t* bempty = bfull + kBStages;
+  uint64_t* tfull = bempty + kBStages;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* drain = tempty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (a.M + kBM - 1) / kBM, n_tiles = a.N / kBN;
+  const int tiles = m_tiles * n_tiles;
+  const int chunks = a.K / kBK;
+  int* perr = a.err;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAStages; s++) {
+      tc::mbar_init(&afull[s], 1);
+      tc::mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < kBStages; s++) {
+      tc::mbar_init(&bfull[s], 1);
+      tc::mbar_init(&bempty[s], 1);
+    }
+    tc::mbar_init(tfull, 1);
+    tc::mbar_init(tempty, 128);
+    tc::mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA issuer ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bmap)) : "memory");
+      uint32_t ai = 0, bi = 0;
+      bool ok = true;
+      if (a.inject_expiry) {  // as if the first wait had expired: nothing is issued
+        atomicOr(perr, tc::kErrTimeout);
+        ok = false;
+      }
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m = t / n_tiles, n = t % n_tiles;
+        for (int c = 0; c < chunks && ok; c++) {
+          {
+            const int s = bi % kBStages;
+            const uint32_t ph = (bi / kBStages) & 1;
+            if (!tc::mbar_wait(&bempty[s], ph ^ 1, perr)) { ok = false; break; }
+            tc::mbar_arrive_expect_tx(&bfull[s], kBSlot);
+            for (int j = 0; j < kSlices; j++)
+              tma_load_3d(bring + s * kBSlot + j * kBSlice, &bmap, c * kBK, n * kBN, j, &bfull[s]);
+            bi++;
+          }
+          for (int i = 0; i < kSlices; i++, ai++) {
+            const int s = ai % kAStages;
+            const uint32_t ph = (ai / kAStages) & 1;
+            if (!tc::mbar_wait(&aempty[s], ph ^ 1, perr)) { ok = false; break; }
+            tc::mbar_arrive_expect_tx(&afull[s], kASlot);
+            tma_load_3d(aring + s * kASlot, &amap, c * kBK, m * kBM, i, &afull[s]);
+          }
+        }
+      }
+      // every copy issued lands before the CTA may exit
+      for (uint32_t j = ai > uint32_t(kAStages) ? ai - kAStages : 0u; j < ai; j++)
+        tc::mbar_wait_drain(&afull[j % kAStages], (j / kAStages) & 1);
+      for (uint32_t j = bi > uint32_t(kBStages) ? bi - kBStages : 0u; j < bi; j++)
+        tc::mbar_wait_drain(&bfull[j % kBStages], (j / kBStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t ai = 0, bi = 0, tl = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tl++) {
+        if (!tc::mbar_wait(tempty, (tl & 1) ^ 1, perr)) { ok = false; break; }
+        tc::tc_fence_after();
+        uint32_t started = 0;  // levels written in this tile
+        for (int c = 0; c < chunks && ok; c++) {
+          const int bs = bi % kBStages;
+          if (!tc::mbar_wait(&bfull[bs], (bi / kBStages) & 1, perr)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t bb = smem_u32(bring + bs * kBSlot);
+          for (int i = 0; i < kSlices; i++, ai++) {
+            const int as = ai % kAStages;
+            if (!tc::mbar_wait(&afull[as], (ai / kAStages) & 1, perr)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t ab = smem_u32(aring + as * kASlot);
+            for (int j = 0; j < kSlices && i + j < kLevels; j++) {
+              const int L = i + j;
+              const uint32_t id = idesc_i8(i == 0, j == 0);
+              const uint32_t d = tmem_base + uint32_t(L * kBN);
+#pragma unroll
+              for (int kk = 0; kk < kBK / 32; kk++)
+                mma_i8(d, tc::smem_desc(ab + kk * 32), tc::smem_desc(bb + j * kBSlice + kk * 32), id,
+                       ((started >> L) & 1u) | uint32_t(kk > 0));
+              started |= 1u << L;
+            }
+            tc::mma_commit(&aempty[as]);
+          }
+          if (!ok) break;
+          tc::mma_commit(&bempty[bs]);
+          bi++;
+        }
+        if (!ok) break;
+        tc::mma_commit(tfull);
+      }
+      tc::mma_commit(drain);
+      tc::mbar_wait_drain(drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: one row per thread ----------------
+    const int g = warp & 3;  // this warp's TMEM lane quarter
+    uint32_t tl = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+      const int m = t / n_tiles, n = t % n_tiles;
+      int okw = 0;
+      if (lane == 0) okw = tc::mbar_wait(tfull, tl & 1, perr) ? 1 : 0;
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) break;
+      tc::tc_fence_after();
+      const int row = m * kBM + g * 32 + lane;
+      const bool live = row < a.M;
+      int ea = 0;
+      double l1a = 0.0, l2a = 0.0;
+      if (live) {
+        ea = a.ea[row];
+        l1a = a.l1a[row];
+        l2a = a.l2a[row];
+      }
+#pragma unroll 1
+      for (int cc = 0; cc < kBN / 16; cc++) {
+        int q[kLevels][16];
+        const uint32_t base = tmem_base + (uint32_t(g * 32) << 16) + uint32_t(cc * 16);
+#pragma unroll
+        for (int L = 0; L < kLevels; L++) tmem_ld16_async(base + uint32_t(L * kBN), q[L]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (cc == kBN / 16 - 1) {  // the accumulators are read: the next tile may start
+          tc::tc_fence_before();
+          tc::mbar_arrive(tempty);
+        }
+        if (!live) continue;
+        const int col0 = n * kBN + cc * 16;
+        float* crow = a.C + uint64_t(row) * a.ldc + col0;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const int col = col0 + e;
+          const int qe[kLevels] = {q[0][e], q[1][e], q[2][e], q[3][e], q[4][e], q[5][e], q[6][e]};
+          float v;
+          if (!oz_decide(qe, ea, l1a, l2a, __ldg(a.eb + col), __ldg(a.l1b + col), __ldg(a.l2b + col), a, &v)) {
+            const unsigned slot = atomicAdd(a.count, 1u);
+            if (slot < a.cap) a.list[slot] = (static_cast<unsigned long long>(row) << 32) | unsigned(col);
+            else atomicOr(a.err, kOzListFull);
+            continue;
+          }
+          if (EPI == kEpiStore) crow[e] = v;
+          else if (EPI == kEpiRelu) crow[e] = js_relu(v);
+          else if (EPI == kEpiGate) crow[e] = a.gate[uint64_t(row) * a.ldc + col] > 0.0f ? v : 0.0f;
+          else crow[e] = f32(double(crow[e]) + double(v));
+        }
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// The listed outputs by the sequential f64 chain, as k_dgemm_exact computes
+// them, with the same epilogue. Grid-stride over the list.
+struct FixupArgs {
+  const float* A;
+  uint64_t lda;
+  const float* B;
+  uint64_t ldb;
+  int K;
+  float* C;
+  int ldc;
+  const float* gate;
+  const unsigned long long* list;
+  const unsigned* count;
+  unsigned cap;
+  unsigned long long* listed;   // running total of listed outputs (profile counter)
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(256) k_oz_fixup(FixupArgs a) {
+  const unsigned n = min(*a.count, a.cap);
+  if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(a.listed, static_cast<unsigned long long>(n));
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long ent = a.list[i];
+    const uint64_t row = ent >> 32;
+    const int col = int(ent & 0xffffffffu);
+    const float* ar = a.A + row * a.lda;
+    const float* br = a.B + uint64_t(col) * a.ldb;
+    double acc = 0.0;
+    for (int k = 0; k < a.K; k += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(ar + k);
+      const float4 w = *reinterpret_cast<const float4*>(br + k);
+      acc = fma(double(x.x), double(w.x), acc);
+      acc = fma(double(x.y), double(w.y), acc);
+      acc = fma(double(x.z), double(w.z), acc);
+      acc = fma(double(x.w), double(w.w), acc);
+    }
+    const float v = f32(acc);
+    float* cp = a.C + row * uint64_t(a.ldc) + col;
+    if (EPI == kEpiStore) *cp = v;
+    else if (EPI == kEpiRelu) *cp = js_relu(v);
+    else if (EPI == kEpiGate) *cp = a.gate[row * uint64_t(a.ldc) + col] > 0.0f ? v : 0.0f;
+    else *cp = f32(double(*cp) + double(v));
+  }
+}
+
+// E2's factor: K·255²·Σ_(L=7..10) n_L·2^(−14−8L), n_L = 11 − L pairs of slices
+// i, j ∈ [2, 5] with i + j = L.
+inline double dropped_levels_bound(int K) {
+  double s = 0.0;
+  for (int L = 7; L <= 10; L++) s += double(11 - L) * std::ldexp(1.0, -14 - 8 * L);
+  return double(K) * 65025.0 * s;
+}
+
+inline double chain_gamma(int K) {
+  const double nu = double(K - 1) * std::ldexp(1.0, -53);
+  return nu / (1.0 - nu);
+}
+
+// The tensor map of slices [6][rows][K] int8: boxes of [box_rows x 128 bytes]
+// of one slice, 128-byte swizzle, zero fill past the last row.
+inline bool make_slice_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t K, uint32_t box_rows) {
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || K % 128 || rows == 0) return false;
+  const cuuint64_t dims[3] = {K, rows, uint64_t(kSlices)};
+  const cuuint64_t strides[2] = {K, rows * K};
+  const cuuint32_t box[3] = {uint32_t(kBK), box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace oz
+}  // namespace kc

@@ -105,6 +105,17 @@ class BrainSession:
     def think(self, records: Sequence, allows=None, sample=None) -> ThinkResult:
         return self.consider(records).choose(allows, sample)
 
+    def learn(self, experiences: Sequence, options=None):
+        """session.ts:195-197: one pass over remembered turns (learnFromExperience),
+        the backend differentiating and told what moved."""
+        from .learn import LearnOptions, learn_from_experience
+        return learn_from_experience(experiences, self.weights, self.backend, options or LearnOptions())
+
+    def teach(self, demonstrations: Sequence, options=None):
+        """session.ts:205-207: be shown what can be said here (teachFromDemonstration)."""
+        from .teach import TeachOptions, teach_from_demonstration
+        return teach_from_demonstration(demonstrations, self.weights, self.backend, options or TeachOptions())
+
     def sync(self, changes=None) -> None:
         self.backend.sync(self.weights, changes)
 

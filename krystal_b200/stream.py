@@ -33,6 +33,8 @@ class StreamBatch:
     error: str | None
     sealed_ms: float
     done_ms: float
+    started_ms: float = 0.0     # when the worker took the batch up
+    sync_wait_ms: float = 0.0   # of done_ms - started_ms, blocked until the device finished
 
 
 def clock_ms() -> float:
@@ -42,13 +44,19 @@ def clock_ms() -> float:
 
 class FrameStream:
     def __init__(self, backend: CudaBrainBackend, max_frames: int = 4096, max_records: int = 1 << 20,
-                 max_p: int = 0, depth: int = 3, copy_results: bool = True):
+                 max_p: int = 0, depth: int = 3, copy_results: bool = True, push_threads: int = 0,
+                 bind_cpus: bool = True):
+        """push_threads: threads that check and stage a large push_many (0:
+        one per 8 CPUs local to the GPU, at most 4); bind_cpus: the worker and
+        helpers run on the GPU's local CPUs and the staging lies on its NUMA
+        node."""
         self._lib = abi.load()
         self.backend = backend
         self.copy_results = copy_results
         s = C.c_void_p()
-        abi.check(self._lib.kc_stream_create(backend._h, max_frames, max_records, max_p, depth, C.byref(s)),
-                  backend._h)
+        opts = abi.KcStreamOptions(push_threads, 1 if bind_cpus else 0)
+        abi.check(self._lib.kc_stream_create_ex(backend._h, max_frames, max_records, max_p, depth, C.byref(opts),
+                                                C.byref(s)), backend._h)
         self._s = s
 
     def _check(self, status: int) -> None:
@@ -116,7 +124,16 @@ class FrameStream:
         if self.copy_results:
             p_off, q_off, p, idx = p_off.copy(), q_off.copy(), p.copy(), idx.copy()
         return StreamBatch(int(r.first_ticket), int(r.frames), p_off, q_off, p, idx, int(r.status),
-                           r.error.decode() if r.error else None, float(r.sealed_ms), float(r.done_ms))
+                           r.error.decode() if r.error else None, float(r.sealed_ms), float(r.done_ms),
+                           float(r.started_ms), float(r.sync_wait_ms))
+
+    def stats(self, reset: bool = False) -> dict:
+        """Where the stream's host time went since the last reset
+        (kc_stream_read_stats): push and worker times, faults, context
+        switches, and the NUMA nodes of the GPU, the staging and the threads."""
+        st = abi.KcStreamStats()
+        self._check(self._lib.kc_stream_read_stats(self._s, int(reset), C.byref(st)))
+        return {name: getattr(st, name) for name, _ in abi.KcStreamStats._fields_}
 
     def close(self) -> None:
         if getattr(self, "_s", None):

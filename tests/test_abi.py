@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_sizes_match_the_c_layout():
     import ctypes as C
     assert C.sizeof(abi.KcConfig) == 13 * 4 + 4 + 8 + 4 + 4  # 13 u32, pad, pointer, u32, tail pad
-    assert C.sizeof(abi.KcBatchView) == 8 + 8 + 8 * 9 + 8
+    assert C.sizeof(abi.KcBatchView) == 8 + 8 + 8 * 9 + 8 + 8
     assert C.sizeof(abi.KcBatchOut) == 8 * 11
 
 
@@ -39,7 +39,8 @@ STRUCTS = {"kc_config": "KcConfig", "kc_block_view": "KcBlockView", "kc_weights_
            "kc_device_result": "KcDeviceResult", "kc_stage_times": "KcStageTimes",
            "kc_backward_out": "KcBackwardOut", "kc_backward_result": "KcBackwardResult",
            "kc_stream_result": "KcStreamResult", "kc_batch_select_view": "KcBatchSelectView",
-           "kc_learn_options": "KcLearnOptions"}
+           "kc_learn_options": "KcLearnOptions", "kc_stream_options": "KcStreamOptions",
+           "kc_stream_stats": "KcStreamStats"}
 
 
 def test_struct_layouts_match_the_header(tmp_path):

@@ -181,3 +181,40 @@ def test_stream_flow_control(ragged):
             assert np.array_equal(got[f], want[f][1])
     finally:
         st.close()
+
+
+@pytest.mark.parametrize("threads", [1, 4])
+def test_parallel_push_many_equals_the_batch_and_refuses_a_bad_frame_alone(ragged, threads):
+    """A run large enough for the helper threads (some 50k records) is staged
+    in parts; the results equal the batch path's, and a malformed frame in
+    the middle is refused alone with every frame before it queued."""
+    import copy
+    wl, cfg, w, be = ragged
+    batch = synth.make_batch(wl, seed=35, frames=400)
+    want = per_frame(be.forward_batch(batch), batch.frames)
+    bad = copy.deepcopy(batch)
+    at = 250
+    bad.token_ids[int(bad.rec_off[at]) * 8 + 3] = 10 ** 9  # no entry in tokenRows
+    st = FrameStream(be, max_frames=512, max_records=512 * 256, depth=2, push_threads=threads)
+    try:
+        assert st.stats()["push_threads"] == threads
+        with pytest.raises(abi.KrystalCudaError) as e:
+            st.push_many(bad, 0, batch.frames)
+        assert e.value.status == abi.KC_ERR_INVALID_ARG and "tokenRows" in e.value.message
+        assert f"(frame {at})" in e.value.message
+        first, n = st.push_many(bad, at + 1, batch.frames)
+        assert (first, n) == (at, batch.frames - at - 1)  # tickets run on past the refused frame
+        st.flush()
+        got = {}
+        drain(st, got, batch.frames - 1)
+        kept = [f for f in range(batch.frames) if f != at]
+        for t, f in enumerate(kept):
+            assert np.array_equal(got[t][1], want[f][1]), f
+            assert np.array_equal(got[t][0], want[f][0]), f
+        s = st.stats(reset=True)
+        assert s["frames_pushed"] == batch.frames - 1 and s["batches"] == 1
+        assert s["bytes_staged"] == 72 * (batch.records - (int(batch.rec_off[at + 1]) - int(batch.rec_off[at])))
+        assert 0 <= s["sync_wait_ms"] <= s["run_ms"]
+        assert st.stats()["frames_pushed"] == 0
+    finally:
+        st.close()
