@@ -51,11 +51,13 @@ def load_peaks() -> tuple[dict, str]:
         return PEAKS_FALLBACK, "fallback"
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per token of one
-# launch, from ncu on the full ragged_4096 batch (2 491 910 tokens, two
-# launches each; profiles/fused_encoder_dram_traffic_ragged_4096.md). The
-# kernels move x once in and once out, so traffic scales with the tokens.
-DRAM_BYTES_PER_TOKEN = {"enc_attn_tc": 1004.8, "enc_ffn": 999.3}
+# DRAM bytes read per token of one launch (dram__bytes_read.sum), from ncu on
+# the 512-frame case of ragged_4096 (311 315 tokens, one kernel per capture).
+# At that size the last tiles' writes are still in L2 when the kernel ends, so
+# the write side is the 512 bytes per token each kernel stores. The kernels
+# move x once in and once out, so traffic scales with the tokens.
+DRAM_READ_PER_TOKEN = {"enc_attn_tc": 517.4, "enc_ffn": 513.8}
+STORED_PER_TOKEN = 512.0
 
 
 def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: str) -> dict:
@@ -76,12 +78,14 @@ def fused_roofline(prof: dict, key: str, kernel: str, peaks: dict, peaks_kind: s
     sustained = peaks.get("bf16_tflops_sustained")
     hbm = peaks.get("hbm_gbs")
     tokens = nbytes / (4 * 2 * 128)  # the algorithmic bytes are x read and written: 1 KB per token
-    per_token = DRAM_BYTES_PER_TOKEN.get(key)
-    traffic = per_token * tokens if per_token else None
+    per_token = DRAM_READ_PER_TOKEN.get(key)
+    traffic = (per_token + STORED_PER_TOKEN) * tokens if per_token else None
     return {"kernel": kernel, "bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
             "frac": tflops / peak if peak else None, "traffic": traffic,
-            "traffic_source": ("ncu DRAM bytes per token on the full 4096-frame batch, scaled to this launch's "
-                               "tokens") if per_token else None,
+            "traffic_read": per_token * tokens if per_token else None,
+            "traffic_source": ("ncu dram__bytes_read.sum per token on the 512-frame case (one kernel per "
+                               "capture) plus the 512 bytes per token stored, scaled to this launch's tokens"
+                               ) if per_token else None,
             "peak_kind": f"{peaks_kind} burst bf16 dense (cuBLAS)",
             "frac_of_sustained": tflops / sustained if sustained else None,
             "issued_tensor_tflops": 3 * tflops, "issued_frac": 3 * tflops / peak if peak else None,
@@ -106,6 +110,8 @@ def parse_args():
     ap.add_argument("--all-legs", action="store_true",
                     help="on N GPUs, one line per configuration in one launch: the ragged batch (weak), the learn "
                          "step (strong), 1024 long-bank frames split over the ranks, the 100k-frame stream")
+    ap.add_argument("--legs", default="ragged_4096,learn_1024,long_bank_1024,stream_100k",
+                    help="with --all-legs: the configurations to run, comma-separated")
     ap.add_argument("--stream-threads", type=int, default=0,
                     help="stream_100k: threads that stage a push_many (0: automatic)")
     ap.add_argument("--stream-bind", type=int, default=1,
@@ -511,8 +517,8 @@ def stream_main(args) -> dict | None:
     max_batch = 2048
     st = FrameStream(be, max_frames=max_batch, max_records=max_batch * wl.records[1], max_p=1 << 24, depth=3,
                      copy_results=False, push_threads=args.stream_threads, bind_cpus=bool(args.stream_bind))
-    warm = synth.make_batch(wl, seed=99, frames=256)
-    stream_run(st, warm, np.zeros(warm.frames), max_batch)  # warm-up: sizes the workspace
+    warm = synth.make_batch(wl, seed=99, frames=2 * max_batch)
+    stream_run(st, warm, np.zeros(warm.frames), max_batch)  # warm-up: full batches size the workspace
 
     def barrier():
         if world > 1:
@@ -599,7 +605,10 @@ def main():
         import copy
         legs = [("ragged_4096", None, forward_main), ("learn_1024", None, learn_main),
                 ("long_bank_1024", max(1, 1024 // world), forward_main), ("stream_100k", None, stream_main)]
+        wanted = set(args.legs.split(","))
         for wl_name, frames, fn in legs:
+            if wl_name not in wanted:
+                continue
             a = copy.copy(args)
             a.workload, a.frames, a.no_side = wl_name, frames, True
             line = fn(a) if fn is not forward_main else fn(a, side=True)

@@ -494,8 +494,8 @@ typedef struct kc_stream_result {
 
 /* Placement and helpers of a stream (kc_stream_create uses {0, 1}).
  * push_threads: the threads a large kc_stream_push_many call validates and
- * stages with, the caller's included; 0 picks one per 8 CPUs local to the GPU,
- * at most 4; 1 is the caller alone. bind_cpus != 0: the worker and the helpers
+ * stages with, the caller's included; 0 picks one per 4 CPUs local to the GPU,
+ * at most 8; 1 is the caller alone. bind_cpus != 0: the worker and the helpers
  * run on the CPUs sysfs lists as local to the GPU (local_cpulist, as far as
  * this process may use them), and the worker allocates the pinned staging, so
  * that its pages lie on the GPU's NUMA node. */

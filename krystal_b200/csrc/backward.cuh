@@ -667,7 +667,10 @@ __device__ __forceinline__ int lb_dout_f4(int r, int f) {
 // One warp per record, 4 warps per CTA. The record's q|k|v and dOut rows
 // (at most 16 KB) are staged in shared memory with one batch of asynchronous
 // 16-byte copies, so each record costs one round trip to memory; the scores,
-// dS and the dQ | dK | dV chains then read shared memory only.
+// dS and the dQ | dK | dV chains then read shared memory only. A = double is
+// the oracle's arithmetic (the exact backward); A = float the same chains in
+// f32, for the tensor-core backward, whose products are fp32-class already.
+template <typename A>
 __global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(LocalBackArgs a) {
   extern __shared__ __align__(16) float lsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -701,26 +704,26 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(Loc
       for (int m = 0; m < 8; m++) d4[m] = drows[lb_dout_f4(ti, head * 8 + m)];
       // s[j] = dOut_i · v_j: eight f64 chains side by side, each over d in order
       // (keys past the record read row 0 and are never used)
-      double s[KC_RW];
+      A s[KC_RW];
 #pragma unroll
-      for (int j = 0; j < KC_RW; j++) s[j] = 0.0;
+      for (int j = 0; j < KC_RW; j++) s[j] = A(0);
 #pragma unroll
       for (int m = 0; m < 8; m++)
 #pragma unroll
         for (int j = 0; j < KC_RW; j++) {
           const float4 v = rows[la_exact_f4(j < cnt ? j : 0, 64 + head * 8 + m)];
-          s[j] = fma(double(d4[m].x), double(v.x), s[j]);
-          s[j] = fma(double(d4[m].y), double(v.y), s[j]);
-          s[j] = fma(double(d4[m].z), double(v.z), s[j]);
-          s[j] = fma(double(d4[m].w), double(v.w), s[j]);
+          s[j] = fma(A(d4[m].x), A(v.x), s[j]);
+          s[j] = fma(A(d4[m].y), A(v.y), s[j]);
+          s[j] = fma(A(d4[m].z), A(v.z), s[j]);
+          s[j] = fma(A(d4[m].w), A(v.w), s[j]);
         }
-      double rs = 0.0;
+      A rs = A(0);
 #pragma unroll
       for (int j = 0; j < KC_RW; j++)
-        if (j < cnt) rs = rs + double(pp[head][ti][j]) * s[j];
+        if (j < cnt) rs = rs + A(pp[head][ti][j]) * s[j];
 #pragma unroll
       for (int j = 0; j < KC_RW; j++)
-        if (j < cnt) dsh[head][ti][j] = f32(double(pp[head][ti][j]) * (double(f32(s[j])) - rs));
+        if (j < cnt) dsh[head][ti][j] = f32(A(pp[head][ti][j]) * (A(f32(s[j])) - rs));
     }
   }
   __syncwarp();
@@ -732,28 +735,28 @@ __global__ void __launch_bounds__(kLocalBackWarps * 32, 3) k_local_attn_back(Loc
   // chain over j in order
   for (int m = 0; m < KC_HEADS; m++) {
     const int col = m * KC_HEAD_DIM + lane, f = m * 8 + (lane >> 2), c = lane & 3;
-    double aq[KC_RW], ak[KC_RW], av[KC_RW];
+    A aq[KC_RW], ak[KC_RW], av[KC_RW];
 #pragma unroll
-    for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = 0.0;
+    for (int i = 0; i < KC_RW; i++) aq[i] = ak[i] = av[i] = A(0);
 #pragma unroll
     for (int j = 0; j < KC_RW; j++) {
       if (j >= cnt) break;
-      const double kj = double(rowsf[la_exact_f4(j, 32 + f) * 4 + c]);
-      const double qj = double(rowsf[la_exact_f4(j, f) * 4 + c]);
-      const double dj = double(drowsf[lb_dout_f4(j, f) * 4 + c]);
+      const A kj = A(rowsf[la_exact_f4(j, 32 + f) * 4 + c]);
+      const A qj = A(rowsf[la_exact_f4(j, f) * 4 + c]);
+      const A dj = A(drowsf[lb_dout_f4(j, f) * 4 + c]);
 #pragma unroll
       for (int i = 0; i < KC_RW; i++)
         if (i < cnt) {
-          aq[i] = fma(double(dsh[m][i][j]), kj, aq[i]);
-          ak[i] = fma(double(dsh[m][j][i]), qj, ak[i]);
-          av[i] = fma(double(pp[m][j][i]), dj, av[i]);
+          aq[i] = fma(A(dsh[m][i][j]), kj, aq[i]);
+          ak[i] = fma(A(dsh[m][j][i]), qj, ak[i]);
+          av[i] = fma(A(pp[m][j][i]), dj, av[i]);
         }
     }
 #pragma unroll
     for (int i = 0; i < KC_RW; i++)
       if (i < cnt) {
-        out[uint64_t(i) * 3 * KC_H + col] = f32(aq[i] * a.scale);
-        out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak[i] * a.scale);
+        out[uint64_t(i) * 3 * KC_H + col] = f32(aq[i] * A(a.scale));
+        out[uint64_t(i) * 3 * KC_H + KC_H + col] = f32(ak[i] * A(a.scale));
         out[uint64_t(i) * 3 * KC_H + 2 * KC_H + col] = f32(av[i]);
       }
   }

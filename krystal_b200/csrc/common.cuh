@@ -26,6 +26,7 @@ __device__ __forceinline__ float js_relu(float v) {
 }
 
 __device__ __forceinline__ float f32(double v) { return __double2float_rn(v); }
+__device__ __forceinline__ float f32(float v) { return v; }
 
 // The record mask's entry for two tokens of one record (compileRecordMask,
 // masks.ts:167-198): alpha when both carry the same valid word id, else 0.

@@ -39,6 +39,7 @@ struct LocalAttnFastArgs {
   const uint32_t* tok_recpos; // [T] record*8 | position, for the word ids
   const uint32_t* word_ids;   // optional [records*8]: the same-word bias's labels
   float word_alpha;
+  float* p_out = nullptr;     // optional [T][4][8]: the softmax rows (saved for the backward)
 };
 
 __device__ __forceinline__ int la_swz(int row, int f4) { return row * kLaRowF4 + (f4 ^ row); }
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(kLaWarps * 32) k_local_attn_fast(LocalAttnFast
     for (int j = 0; j < KC_RW; j++) {
       if (j < cnt) {
         const float pj = p[j] * inv;
+        if (a.p_out) a.p_out[((uint64_t(start) + ti) * KC_HEADS + head) * KC_RW + j] = pj;
 #pragma unroll
         for (int m = 0; m < 8; m++) {
           const float4 vv = st[la_swz(j, 64 + head * 8 + m)];

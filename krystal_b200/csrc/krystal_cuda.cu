@@ -247,8 +247,7 @@ struct kc_handle {
   std::vector<char> mat_dirty;      // per matrix: its image is stale
   int* d_err = nullptr;             // tensor-core pipeline error word
   int* h_err = nullptr;             // pinned
-  std::vector<uint32_t> h_flags;
-  uint32_t* h_flags_pinned = nullptr;
+  uint32_t* h_flags_pinned = nullptr;  // certify's readback (flags, per-frame t, q, r) and its frame list
   size_t h_flags_cap = 0;
   // profiling
   bool profiling = false;
@@ -616,9 +615,11 @@ kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, co
 
 // Whether an exact-path product can run on the int8 tensor cores: a forward
 // matrix of the list read from the weight page, K a multiple of 128 up to
-// 512, N a multiple of 64, A rows 16-byte aligned.
-bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, int mat, const float* B, uint32_t ldb, uint32_t N,
-             uint32_t K) {
+// 384, N a multiple of 64, A, C and the gate 16-byte aligned.
+bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, int mat, const float* B, uint32_t ldb, float* C,
+             const float* gate, uint32_t N, uint32_t K) {
+  const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!aligned(C) || (gate && !aligned(gate))) return false;
   if (!h->oz || h->oz_suspend || mat < 0 || size_t(mat) >= h->mats.size()) return false;
   const Mat& mt = h->mats[mat];
   return !mt.transposed && mt.page_off % 4 == 0 && mt.n == N && mt.k == K && B == h->w + mt.page_off && ldb == K &&
@@ -627,7 +628,8 @@ bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, int mat, const fl
 }
 
 // The slices and row data of forward matrix `mat` (rebuilt after a sync
-// changed it): [6][N][K] int8, then l1 [N], l2 [N] (f64), e [N] (int).
+// changed it): [6][N][K] int8, then l1, l2, the column scale 2^e and the
+// bound's column term [N] (f64), e [N] (int).
 kc_status oz_weights(kc_handle* h, int mat) {
   const auto& m = h->mats;
   if (h->oz_w_off.size() != m.size()) {
@@ -636,7 +638,7 @@ kc_status oz_weights(kc_handle* h, int mat) {
     for (size_t i = 0; i < m.size(); i++) {
       if (m[i].transposed) continue;
       h->oz_w_off[i] = off;
-      off += (uint64_t(m[i].n) * m[i].k * kc::oz::kSlices + uint64_t(m[i].n) * 20 + 255) & ~uint64_t(255);
+      off += (uint64_t(m[i].n) * m[i].k * kc::oz::kSlices + uint64_t(m[i].n) * 36 + 255) & ~uint64_t(255);
     }
     KC_TRY(ensure(h, h->oz_w, off), "weight slices");
   }
@@ -646,8 +648,11 @@ kc_status oz_weights(kc_handle* h, int mat) {
   uint8_t* base = P<uint8_t>(h->oz_w) + h->oz_w_off[mat];
   const uint64_t plane = uint64_t(mt.n) * mt.k;
   double* l1 = reinterpret_cast<double*>(base + plane * kc::oz::kSlices);
-  kc::oz::SliceArgs sa{h->w + mt.page_off, mt.n, int(mt.k), mt.k, base, plane, reinterpret_cast<int*>(l1 + 2 * mt.n),
+  kc::oz::SliceArgs sa{h->w + mt.page_off, mt.n, int(mt.k), mt.k, base, plane, reinterpret_cast<int*>(l1 + 4 * mt.n),
                        l1, l1 + mt.n, nullptr};
+  sa.col_s = l1 + 2 * mt.n;
+  sa.col_p = l1 + 3 * mt.n;
+  sa.c2k = std::ldexp(double(mt.k), -94) + kc::oz::dropped_levels_bound(int(mt.k));
   kc::oz::k_oz_slice<<<(mt.n + 7) / 8, 256, 0, h->stream>>>(sa);
   h->launches++;
   KC_TRY(cudaGetLastError(), "weight slices");
@@ -683,11 +688,10 @@ kc_status oz_gemm(kc_handle* h, const float* A, uint32_t lda, uint64_t M, int ma
   kc::oz::GemmArgs g{};
   g.M = int(M); g.N = int(N); g.K = int(K);
   g.ea = ea; g.l1a = l1a; g.l2a = l1a + M;
-  g.eb = reinterpret_cast<const int*>(l1b + 2 * mt.n); g.l1b = l1b; g.l2b = l1b + mt.n;
+  g.sb = l1b + 2 * mt.n; g.pb = l1b + 3 * mt.n; g.l2b = l1b + mt.n;
   g.C = C; g.ldc = int(N); g.gate = gate;
   g.list = P<unsigned long long>(h->oz_list); g.count = count; g.cap = unsigned(cap);
   g.err = reinterpret_cast<int*>(count + 1);
-  g.c2 = kc::oz::dropped_levels_bound(int(K));
   g.gamma = kc::oz::chain_gamma(int(K));
   g.inject_expiry = take_injection(h, KC_INJECT_EXACT_GEMM);
   const uint64_t tiles = ((M + kc::oz::kBM - 1) / kc::oz::kBM) * (N / kc::oz::kBN);
@@ -713,7 +717,7 @@ template <int EPI>
 kc_status gemm(kc_handle* h, bool tc, const float* A, uint32_t lda, uint64_t M, int mat, const float* B,
                uint32_t ldb, float* C, uint32_t N, uint32_t K, const float* gate = nullptr) {
   if (tc) return tc_gemm<EPI>(h, A, M, mat, C, gate);
-  if (oz_fits(h, A, lda, mat, B, ldb, N, K)) return oz_gemm<EPI>(h, A, lda, M, mat, C, N, K, gate);
+  if (oz_fits(h, A, lda, mat, B, ldb, C, gate, N, K)) return oz_gemm<EPI>(h, A, lda, M, mat, C, N, K, gate);
   return dgemm_ld<EPI>(h, A, lda, B, C, M, N, K, gate, ldb);
 }
 
@@ -746,8 +750,10 @@ const char* bad_message(uint32_t code) {
 }
 
 // Pack on the GPU: offset tables, compact token list, row lists. One host
-// wait for the batch totals (sizes the rest of the workspace).
-kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTotals* out_tot) {
+// wait for the batch totals (sizes the rest of the workspace), unless the
+// caller knows them (`known`: a sub-batch of frames an earlier pack checked).
+kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTotals* out_tot,
+                     const kc::FrameTotals* known = nullptr) {
   const Dims& d = h->d;
   if (&ws == &h->ws) h->ws_epoch++;
   const uint32_t F = b.frames;
@@ -777,10 +783,12 @@ kc_status pack_batch(kc_handle* h, Workspace& ws, const DevBatch& b, kc::FrameTo
                                                           P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
                                                           P<uint64_t>(ws.p_off), dtot);
     h->launches += 2;
-    KC_TRY(cudaMemcpyAsync(h->h_tot, dtot, sizeof(kc::FrameTotals), cudaMemcpyDeviceToHost, h->stream), "readback");
+    if (!known)
+      KC_TRY(cudaMemcpyAsync(h->h_tot, dtot, sizeof(kc::FrameTotals), cudaMemcpyDeviceToHost, h->stream),
+             "readback");
   }
-  KC_TRY(wait_stream(h), "pack");
-  const kc::FrameTotals tot = *h->h_tot;
+  if (!known) KC_TRY(wait_stream(h), "pack");
+  const kc::FrameTotals tot = known ? *known : *h->h_tot;
   if (tot.bad) {
     char buf[160];
     snprintf(buf, sizeof buf, "%s (%s %u)", bad_message(tot.bad),
@@ -914,7 +922,15 @@ kc_status forward_exact_pass(kc_handle* h, Workspace& ws, const DevBatch& b, con
       ProfScope ps(h, kStEncGemm, 2.0 * T * H * 3 * H, 4.0 * T * (H + 3 * H));
       KC_CHECK(gemm<kc::kEpiStore>(h, tc, x, H, T, em, W, H, bqkv, 3 * H, H));
     }
-    {
+    if (tc) {  // the tensor-core forward (the batch backward's): f32 attention, its softmax rows saved
+      ProfScope ps(h, kStEncAttn);
+      kc::LocalAttnFastArgs la{bqkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, float(attn_scale),
+                               P<uint32_t>(ws.tok_recpos), b.word_alpha != 0.0f ? b.word_ids : nullptr,
+                               b.word_alpha, sv ? sv->enc_p + blk * T * 32 : nullptr};
+      kc::k_local_attn_fast<<<unsigned((N + kc::kLaWarps - 1) / kc::kLaWarps), kc::kLaWarps * 32, 0,
+                              h->stream>>>(la);
+      h->launches++;
+    } else {
       ProfScope ps(h, kStEncAttn);
       kc::LocalAttnArgs la{bqkv, x, P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale,
                            sv ? sv->enc_p + blk * T * 32 : nullptr, P<uint32_t>(ws.tok_recpos),
@@ -1166,14 +1182,20 @@ void audit_collect(kc_handle* h) {
 kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::FrameTotals& tot) {
   const uint32_t F = b.frames;
   audit_collect(h);
+  // one readback: the flags and, per frame, its tokens, questions and bank
+  // rows, from which the host sizes the sub-batch and knows its totals
   if (h->h_flags_cap < F) {
     if (h->h_flags_pinned) cudaFreeHost(h->h_flags_pinned);
     h->h_flags_pinned = nullptr;
     h->h_flags_cap = 0;
-    KC_TRY(cudaMallocHost(&h->h_flags_pinned, F * 4ull), "pinned");
+    KC_TRY(cudaMallocHost(&h->h_flags_pinned, F * 20ull), "pinned");  // flags, t, q, r, then the list
     h->h_flags_cap = F;
   }
-  KC_TRY(cudaMemcpyAsync(h->h_flags_pinned, ws.flags.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  uint32_t* hf = h->h_flags_pinned;
+  KC_TRY(cudaMemcpyAsync(hf, ws.flags.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(hf + F, ws.frame_t.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(hf + 2 * F, ws.frame_q.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
+  KC_TRY(cudaMemcpyAsync(hf + 3 * F, ws.frame_r.p, F * 4ull, cudaMemcpyDeviceToHost, h->stream), "readback");
   KC_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream), "readback");
   KC_TRY(wait_stream(h), "certify");
   const int e = *h->h_err;
@@ -1182,30 +1204,33 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   const bool all = e & kc::tc::kErrOverflow;
   h->last_overflow = all;
   if (all && h->sa > -24) h->sa -= 6;  // later batches split at a smaller scale
-  std::vector<uint32_t>& list = h->h_flags;
-  list.clear();
-  for (uint32_t f = 0; f < F; f++)
-    if (all || h->h_flags_pinned[f]) list.push_back(f);
-  if (list.empty() || tot.q == 0) return KC_OK;
+  uint32_t* list = hf + 4 * F;  // pinned, so its upload is asynchronous
+  uint32_t n = 0;
+  kc::FrameTotals sub_tot{};
+  uint64_t nrec = 0;
+  for (uint32_t f = 0; f < F; f++) {
+    if (!all && !hf[f]) continue;
+    list[n++] = f;
+    const uint64_t t = hf[F + f], q = hf[2 * F + f], r = hf[3 * F + f];
+    sub_tot.t += t; sub_tot.q += q; sub_tot.r += r; sub_tot.p += q * r;
+    sub_tot.max_q = std::max(sub_tot.max_q, uint32_t(q));
+    sub_tot.max_r = std::max(sub_tot.max_r, uint32_t(r));
+    nrec += q + r;  // every record of a frame is a question or a bank row
+  }
+  if (n == 0 || tot.q == 0) return KC_OK;
   ProfScope ps(h, kStFallback);
-  h->prof.fallback_frames += list.size();
-  const uint32_t n = uint32_t(list.size());
+  h->prof.fallback_frames += n;
+  const uint64_t nq = sub_tot.q, np = sub_tot.p;
   Workspace& fb = h->ws_fb;
   KC_TRY(ensure(h, fb.list, n * 4ull), "workspace");
   KC_TRY(ensure(h, fb.rec_off, (n + 1) * 8ull), "workspace");
   KC_TRY(ensure(h, fb.uniforms, (n + 1) * 8ull), "workspace");  // sub question offsets
-  KC_TRY(cudaMemcpyAsync(fb.list.p, list.data(), n * 4ull, cudaMemcpyHostToDevice, h->stream), "upload");
+  KC_TRY(cudaMemcpyAsync(fb.list.p, list, n * 4ull, cudaMemcpyHostToDevice, h->stream), "upload");
   KC_TRY(ensure(h, fb.rows_val, (n + 1) * 8ull), "workspace");  // sub p offsets, for an explicit mask
   kc::k_fallback_offsets<<<1, 1024, 0, h->stream>>>(P<uint32_t>(fb.list), n, b.rec_off, P<uint64_t>(ws.q_off),
                                                     P<uint64_t>(ws.p_off), P<uint64_t>(fb.rec_off),
                                                     P<uint64_t>(fb.uniforms), P<uint64_t>(fb.rows_val));
   h->launches++;
-  uint64_t sizes[3];
-  KC_TRY(cudaMemcpyAsync(&sizes[0], P<uint64_t>(fb.rec_off) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(cudaMemcpyAsync(&sizes[1], P<uint64_t>(fb.uniforms) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(cudaMemcpyAsync(&sizes[2], P<uint64_t>(fb.rows_val) + n, 8, cudaMemcpyDeviceToHost, h->stream), "readback");
-  KC_TRY(wait_stream(h), "certify");
-  const uint64_t nrec = sizes[0], nq = sizes[1], np = sizes[2];
   // the sub question offsets live in fb.uniforms until the gather; move them
   KC_TRY(ensure(h, fb.rows_off, (n + 1) * 8ull), "workspace");
   KC_TRY(cudaMemcpyAsync(fb.rows_off.p, fb.uniforms.p, (n + 1) * 8ull, cudaMemcpyDeviceToDevice, h->stream), "copy");
@@ -1241,8 +1266,7 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   sub.word_ids = words ? P<uint32_t>(fb.word_ids) : nullptr;
   sub.word_alpha = b.word_alpha;
   if (b.mask) { sub.mask = P<float>(fb.mask); sub.mask_len = np; }
-  kc::FrameTotals sub_tot;
-  KC_CHECK(pack_batch(h, fb, sub, &sub_tot));
+  KC_CHECK(pack_batch(h, fb, sub, &sub_tot, &sub_tot));  // the totals are known: no readback
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
   // audit the margin on the recomputed frames: the fast scores against the exact ones
   KC_TRY(cudaMemsetAsync(h->d_audit, 0, sizeof(float), h->stream), "memset");
@@ -1663,8 +1687,11 @@ kc_status backward_batch(kc_handle* h, const DevBatch& b, const float* sel, cons
       ProfScope ps(h, kStEncAttn);
       kc::LocalBackArgs lb{P<float>(bw.enc_qkv) + blk * T * 3 * H, P<float>(bw.enc_p) + blk * T * 32, dfs,
                            P<uint32_t>(ws.rec_start), P<uint2>(ws.rec_meta), N, attn_scale, P<float>(bw.edqkv)};
-      kc::k_local_attn_back<<<unsigned((N + kc::kLocalBackWarps - 1) / kc::kLocalBackWarps),
-                              kc::kLocalBackWarps * 32, kc::kLocalBackSmem, h->stream>>>(lb);
+      const unsigned grid = unsigned((N + kc::kLocalBackWarps - 1) / kc::kLocalBackWarps);
+      if (tc)  // the tensor-core backward: the same chains in f32
+        kc::k_local_attn_back<float><<<grid, kc::kLocalBackWarps * 32, kc::kLocalBackSmem, h->stream>>>(lb);
+      else
+        kc::k_local_attn_back<double><<<grid, kc::kLocalBackWarps * 32, kc::kLocalBackSmem, h->stream>>>(lb);
       h->launches++;
     }
     // dStates += dQ·Wq + dK·Wk + dV·Wv: three f32-rounded adds in the oracle's
@@ -1800,7 +1827,9 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
                                 int(KC_MAX_BANK) * 12))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_cross_attn_back_q, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(KC_MAX_BANK) * 48)) ||
-      (e = cudaFuncSetAttribute(kc::k_local_attn_back, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      (e = cudaFuncSetAttribute(kc::k_local_attn_back<double>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kLocalBackSmem))) ||
+      (e = cudaFuncSetAttribute(kc::k_local_attn_back<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kLocalBackSmem))))
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::oz::k_oz_gemm<kc::kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize,

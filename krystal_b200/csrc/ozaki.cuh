@@ -29,8 +29,9 @@
 //   one s32 accumulator in TMEM; levels 0..6 (26 pairs) are kept;
 //
 //   ŷ = 2^(ea+eb−62)·(2^32·((Q0·256 + Q1)·256 + Q2) + ((Q3·256 + Q4)·256 + Q5)·256 + Q6):
-//   both parts are exact 64-bit integers below 2^53 (K ≤ 512), so forming ŷ
-//   rounds once.
+//   both parts are exact 64-bit integers below 2^51 (K ≤ 384), converted to
+//   f64 exactly (a bit-pattern add and one subtraction), so forming ŷ rounds
+//   once.
 //
 // The bound E per output (all terms rounded up, then doubled, which covers
 // the f64 rounding of the bound itself and of ŷ ± E):
@@ -42,14 +43,21 @@
 // goes to the fixup. A list that overflows raises an error bit; the caller
 // then recomputes the whole forward on the FP64 kernel.
 //
-// One persistent CTA per SM, 192 threads:
+// One persistent CTA per SM, 320 threads:
 //   warp 0     TMA: per (128-row, 64-column) tile and 128-wide K chunk the
 //              six B slices (8 KB each) into a two-deep ring, then the six A
-//              slices (16 KB each) into a four-deep ring (3-D tensor maps over
+//              slices (16 KB each) into a six-deep ring (3-D tensor maps over
 //              [slice][row][k] int8, 128-byte swizzle, zero fill past M);
 //   warp 1     MMA issuer: for A slice i, B slices j ≤ 6 − i into level i + j
 //              (four K steps of 32 each), s32 accumulators in TMEM;
-//   warps 2-5  epilogue: one output row per thread, 16 columns at a time.
+//   warps 2-9  epilogue: one output row per thread, two warps per TMEM lane
+//              quarter (32 columns each), 16 columns at a time. The bound's
+//              row terms are formed once per tile, the column terms once per
+//              sync (k_oz_slice on the weights), so an output costs three
+//              FMAs of bound and two f64 -> f32 conversions. The tile passes
+//              through shared memory (float4 group c of row r at
+//              c ^ (r & 7)), so the residual or gate input comes in and the
+//              results leave with coalesced 16-byte accesses.
 #pragma once
 #include "common.cuh"
 #include "tc_gemm.cuh"
@@ -65,12 +73,13 @@ constexpr int kBM = 128, kBN = 64, kBK = 128;    // tile rows, tile columns, K b
 constexpr int kASlot = kBM * kBK;                // 16 KB: one A slice of one chunk
 constexpr int kBSlice = kBN * kBK;               // 8 KB: one B slice of one chunk
 constexpr int kBSlot = kSlices * kBSlice;        // 48 KB
-constexpr int kAStages = 4, kBStages = 2;
-constexpr int kThreads = 192;
-constexpr int kSmem = kAStages * kASlot + kBStages * kBSlot + 1024 + 256;
+constexpr int kAStages = 6, kBStages = 2;        // a whole chunk's A slices in flight
+constexpr int kThreads = 320;                    // TMA warp, MMA warp, 8 epilogue warps
+constexpr int kStage = kBM * kBN * 4;             // 32 KB: the output tile, f32
+constexpr int kSmem = kAStages * kASlot + kBStages * kBSlot + kStage + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;              // 7 levels x 64 columns used
 constexpr int kSpecial = 0x7fffffff;             // a row with a non-finite entry
-constexpr int kMaxK = 512;
+constexpr int kMaxK = 384;                       // keeps both 64-bit parts of ŷ below 2^51
 // Error bits of the product's own word: an expired pipeline wait raises
 // tc::kErrTimeout (1), a full list kOzListFull.
 enum : int { kOzListFull = 4 };
@@ -90,7 +99,48 @@ struct SliceArgs {
   double* l1;              // [rows] Σ|x|, rounded up
   double* l2;              // [rows] sqrt(Σ x²), rounded up
   unsigned* reset;         // optional: zeroed by the first thread (the next GEMM's list count)
+  // weights only (the product's columns): 2^e, and the column's part of the
+  // bound 2^-47·‖b‖₁ + c2k·2^e (c2k = K·2^-94 + E2's factor); a column with a
+  // non-finite entry gets 0 and +inf, which lists every output it touches
+  double* col_s = nullptr;
+  double* col_p = nullptr;
+  double c2k = 0.0;
 };
+
+// 2^x as an f64, exactly, for −1022 ≤ x ≤ 1023.
+__device__ __forceinline__ double pow2(int x) { return __longlong_as_double(static_cast<long long>(x + 1023) << 52); }
+
+// floor(x·2^(47−e)) for an f32 x with |x| < 2^e, from its bits (|result| <
+// 2^47). Its bytes are the six slices: s0 = result >> 40 (arithmetic: the
+// floor), s_i = (result >> (40 − 8i)) & 255, the same digits as slicing
+// x·2^-e by repeated floors, since the dropped fraction is below one.
+__device__ __forceinline__ long long fixed47(float x, int e) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t ex = (b >> 23) & 0xffu, fr = b & 0x7fffffu;
+  if (ex == 0 && fr == 0) return 0;
+  const unsigned long long m = ex ? (fr | 0x800000u) : fr;  // |x| = m·2^p
+  const int sh = (ex ? int(ex) : 1) - 150 + 47 - e;         // |x|·2^(47−e) = m·2^sh, sh ≤ 23
+  unsigned long long mag;
+  bool inexact = false;
+  if (sh >= 0) {
+    mag = m << sh;
+  } else if (sh > -64) {
+    mag = m >> (-sh);
+    inexact = (m & ((1ull << (-sh)) - 1ull)) != 0ull;
+  } else {
+    mag = 0;
+    inexact = true;
+  }
+  const long long v = static_cast<long long>(mag);
+  return (b >> 31) ? -(v + (inexact ? 1 : 0)) : v;  // floor of a negative value
+}
+
+// A 64-bit integer below 2^51 in magnitude as an f64, exactly, without the
+// conversion pipe: added into the significand of 1.5·2^52, then 1.5·2^52
+// subtracted (both steps exact).
+__device__ __forceinline__ double i64_to_f64(long long v) {
+  return __longlong_as_double(0x4338000000000000LL + v) - 6755399441055744.0;
+}
 
 __global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
   if (a.reset && blockIdx.x == 0 && threadIdx.x == 0) *a.reset = 0u;
@@ -113,8 +163,9 @@ __global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
       const float m = fabsf(t[q]);
       bad |= !(m <= 3.4028234663852886e38f);  // inf or NaN
       mx = fmaxf(mx, m);
-      s1 += double(m);
-      s2 = fma(double(t[q]), double(t[q]), s2);
+      const double d = double(m);
+      s1 += d;
+      s2 = fma(d, d, s2);
     }
   }
 #pragma unroll
@@ -130,8 +181,13 @@ __global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
   if (lane == 0) {
     a.e[r] = e;
     // the sums' own rounding (at most K·u relative) is covered by the factor
-    a.l1[r] = bad ? 0.0 : s1 * (1.0 + 0x1p-40);
+    const double l1 = bad ? 0.0 : s1 * (1.0 + 0x1p-40);
+    a.l1[r] = l1;
     a.l2[r] = bad ? 0.0 : sqrt(s2) * (1.0 + 0x1p-40);
+    if (a.col_s) {
+      a.col_s[r] = bad ? 0.0 : pow2(e);
+      a.col_p[r] = bad ? __longlong_as_double(0x7ff0000000000000LL) : fma(a.c2k, pow2(e), l1 * 0x1p-47);
+    }
   }
 #pragma unroll
   for (int c = 0; c < kMaxK / 128; c++) {
@@ -141,17 +197,10 @@ __global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
     if (!bad && mx > 0.0f) {
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        double y = ldexp(double(t[q]), 7 - e);  // x'·2^7, exact
-        const double s0 = floor(y);
-        w[0] |= (uint32_t(int(s0)) & 0xffu) << (8 * q);
-        y -= s0;
+        const long long X = fixed47(t[q], e);
+        w[0] |= (uint32_t(X >> 40) & 0xffu) << (8 * q);
 #pragma unroll
-        for (int i = 1; i < kSlices; i++) {
-          y *= 256.0;
-          const double si = floor(y);
-          w[i] |= (uint32_t(si) & 0xffu) << (8 * q);
-          y -= si;
-        }
+        for (int i = 1; i < kSlices; i++) w[i] |= (uint32_t(X >> (40 - 8 * i)) & 0xffu) << (8 * q);
       }
     }
     uint8_t* dst = a.slices + r * uint64_t(a.K) + c * 128 + lane * 4;
@@ -165,10 +214,9 @@ __global__ void __launch_bounds__(256) k_oz_slice(SliceArgs a) {
 // ---------------------------------------------------------------------------
 struct GemmArgs {
   int M, N, K;
-  const int* ea;
+  const int* ea;                // A rows: exponent, ‖a‖₁, ‖a‖₂
   const double *l1a, *l2a;
-  const int* eb;
-  const double *l1b, *l2b;
+  const double *sb, *pb, *l2b;  // B rows (the output columns): 2^eb, the bound's column term, ‖b‖₂
   float* C;
   int ldc;
   const float* gate;            // kEpiGate: [M, ldc]
@@ -176,17 +224,21 @@ struct GemmArgs {
   unsigned* count;
   unsigned cap;
   int* err;                     // tc::kErrTimeout / kOzListFull
-  double c2;                    // E2 / 2^(ea+eb)
   double gamma;                 // γ_(K−1)
   int inject_expiry;            // test hook: the producer reports an expired wait before it issues any copy
 };
 
 // Instruction descriptor: D s32, A / B int8 (signed for slice 0), K-major,
-// M = 128, N = 64.
-__host__ __device__ constexpr uint32_t idesc_i8(bool a_signed, bool b_signed) {
-  return (2u << 4) | (uint32_t(a_signed) << 7) | (uint32_t(b_signed) << 10) | (uint32_t(kBN >> 3) << 17) |
+// M = 128, N = 64 or 128.
+__host__ __device__ constexpr uint32_t idesc_i8(bool a_signed, bool b_signed, int n) {
+  return (2u << 4) | (uint32_t(a_signed) << 7) | (uint32_t(b_signed) << 10) | (uint32_t(n >> 3) << 17) |
          (uint32_t(kBM >> 4) << 24);
 }
+
+// The order the A slices are loaded and multiplied in: slice 1 first, so that
+// its products write levels 1-6 fresh, then slice 0 (level 0 fresh, the rest
+// accumulating), then 2..5.
+__device__ __forceinline__ int slice_at(int idx) { return idx == 0 ? 1 : idx == 1 ? 0 : idx; }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -217,18 +269,20 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, int* v) {
       : "r"(taddr));
 }
 
-// One output's decision: the stored f32 (true) or a listing (false).
-__device__ __forceinline__ bool oz_decide(const int* q, int ea, double l1a, double l2a, int eb, double l1b,
-                                          double l2b, const GemmArgs& a, float* out) {
-  if (ea == kSpecial || eb == kSpecial) return false;
+// One output's decision: the stored f32 (true) or a listing (false). Row
+// terms: sr = 2^(ea−62), ar = 2^ea, br = 2^-47·‖a‖₁, cr = γ·‖a‖₂ (a row with a
+// non-finite entry: sr = 0, ar = +inf, so it is always listed). With the
+// column terms the bound is
+//   E = 2·(ar·pb + br·sb + cr·‖b‖₂ + 2^-53·|ŷ|) = 2·(E1 + E2 + E4 + E3).
+__device__ __forceinline__ bool oz_decide(const int* q, double sr, double ar, double br, double cr, double sb,
+                                          double pb, double l2b, float* out) {
   const long long hi = (static_cast<long long>(q[0]) * 256 + q[1]) * 256 + q[2];
   const long long lo = ((static_cast<long long>(q[3]) * 256 + q[4]) * 256 + q[5]) * 256 + q[6];
-  const double y = ldexp(fma(double(hi), 0x1p32, double(lo)), ea + eb - 62);
-  const double e1 = ldexp(l1b, ea - 47) + ldexp(l1a, eb - 47) + ldexp(double(a.K), ea + eb - 94);
-  const double e2 = ldexp(a.c2, ea + eb);
-  const double e3 = fabs(y) * 0x1p-53;
-  const double e4 = a.gamma * (l2a * l2b);
-  const double err = 2.0 * (e1 + e2 + e3 + e4) + 0x1p-1060;  // (the last term: an ldexp that went subnormal)
+  const double y = fma(i64_to_f64(hi), 0x1p32, i64_to_f64(lo)) * (sr * sb);
+  double t = fma(cr, l2b, fabs(y) * 0x1p-53);
+  t = fma(br, sb, t);
+  t = fma(ar, pb, t);
+  const double err = 2.0 * t + 0x1p-1060;  // (the last term: a scale that went subnormal)
   const float lo_f = __double2float_rn(y - err), hi_f = __double2float_rn(y + err);
   if (__float_as_uint(lo_f) != __float_as_uint(hi_f)) return false;
   *out = lo_f;
@@ -243,7 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* aring = smem;
   unsigned char* bring = smem + kAStages * kASlot;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + kBStages * kBSlot);
+  float4* stage = reinterpret_cast<float4*>(bring + kBStages * kBSlot);  // [128 rows][16 float4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + kBStages * kBSlot + kStage);
   uint64_t* afull = bars;
   uint64_t* aempty = afull + kAStages;
   uint64_t* bfull = aempty + kAStages;
@@ -269,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
       tc::mbar_init(&bempty[s], 1);
     }
     tc::mbar_init(tfull, 1);
-    tc::mbar_init(tempty, 128);
+    tc::mbar_init(tempty, 256);
     tc::mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -302,12 +357,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
               tma_load_3d(bring + s * kBSlot + j * kBSlice, &bmap, c * kBK, n * kBN, j, &bfull[s]);
             bi++;
           }
-          for (int i = 0; i < kSlices; i++, ai++) {
+          for (int idx = 0; idx < kSlices; idx++, ai++) {
             const int s = ai % kAStages;
             const uint32_t ph = (ai / kAStages) & 1;
             if (!tc::mbar_wait(&aempty[s], ph ^ 1, perr)) { ok = false; break; }
             tc::mbar_arrive_expect_tx(&afull[s], kASlot);
-            tma_load_3d(aring + s * kASlot, &amap, c * kBK, m * kBM, i, &afull[s]);
+            tma_load_3d(aring + s * kASlot, &amap, c * kBK, m * kBM, slice_at(idx), &afull[s]);
           }
         }
       }
@@ -332,20 +387,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
           if (!tc::mbar_wait(&bfull[bs], (bi / kBStages) & 1, perr)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t bb = smem_u32(bring + bs * kBSlot);
-          for (int i = 0; i < kSlices; i++, ai++) {
+          for (int idx = 0; idx < kSlices; idx++, ai++) {
+            const int i = slice_at(idx);
             const int as = ai % kAStages;
             if (!tc::mbar_wait(&afull[as], (ai / kAStages) & 1, perr)) { ok = false; break; }
             tc::tc_fence_after();
             const uint32_t ab = smem_u32(aring + as * kASlot);
-            for (int j = 0; j < kSlices && i + j < kLevels; j++) {
+            // B slice 0 (signed) alone; the unsigned slices j, j+1 two at a
+            // time as one N = 128 product: B slices j and j+1 are adjacent in
+            // shared memory, levels i+j and i+j+1 adjacent in TMEM, and both
+            // levels are fresh or both accumulating (the order above)
+            const int jmax = kLevels - 1 - i < kSlices - 1 ? kLevels - 1 - i : kSlices - 1;
+            for (int j = 0; j <= jmax;) {
+              const int wide = (j > 0 && j + 1 <= jmax) ? 2 : 1;
               const int L = i + j;
-              const uint32_t id = idesc_i8(i == 0, j == 0);
+              const uint32_t id = idesc_i8(i == 0, j == 0, kBN * wide);
               const uint32_t d = tmem_base + uint32_t(L * kBN);
+              const uint32_t acc = (started >> L) & 1u;
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; kk++)
                 mma_i8(d, tc::smem_desc(ab + kk * 32), tc::smem_desc(bb + j * kBSlice + kk * 32), id,
-                       ((started >> L) & 1u) | uint32_t(kk > 0));
-              started |= 1u << L;
+                       acc | uint32_t(kk > 0));
+              started |= (wide == 2 ? 3u : 1u) << L;
+              j += wide;
             }
             tc::mma_commit(&aempty[as]);
           }
@@ -362,55 +426,93 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
     __syncwarp();
   } else {
     // ---------------- epilogue: one row per thread ----------------
-    const int g = warp & 3;  // this warp's TMEM lane quarter
+    const int g = warp & 3;             // this warp's TMEM lane quarter
+    const int half = (warp - 2) >> 2;   // its 32 columns of the tile
+    const int et = threadIdx.x - 64;    // 0..255 among the epilogue threads
+    const int rl = g * 32 + lane;       // this thread's row in the tile
     uint32_t tl = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
       const int m = t / n_tiles, n = t % n_tiles;
       int okw = 0;
       if (lane == 0) okw = tc::mbar_wait(tfull, tl & 1, perr) ? 1 : 0;
       okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw) break;
+      // the eight warps agree before any of them reaches a named barrier
+      int all;
+      asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %1, 0;\n\t"
+                   "bar.red.and.pred p, 1, 256, p;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                   : "=r"(all) : "r"(okw) : "memory");
+      if (!all) break;
       tc::tc_fence_after();
-      const int row = m * kBM + g * 32 + lane;
+      const int row = m * kBM + rl;
       const bool live = row < a.M;
-      int ea = 0;
-      double l1a = 0.0, l2a = 0.0;
+      double sr = 0.0, ar = 0.0, br = 0.0, cr = 0.0;
       if (live) {
-        ea = a.ea[row];
-        l1a = a.l1a[row];
-        l2a = a.l2a[row];
+        const int ea = a.ea[row];
+        if (ea == kSpecial) {
+          ar = __longlong_as_double(0x7ff0000000000000LL);
+        } else {
+          sr = pow2(ea - 62);
+          ar = pow2(ea);
+          br = a.l1a[row] * 0x1p-47;
+          cr = a.gamma * a.l2a[row];
+        }
+      }
+      if (EPI == kEpiResid || EPI == kEpiGate) {  // the residual / gate tile, coalesced
+        const float* src = EPI == kEpiGate ? a.gate : a.C;
+        for (int i = et; i < kBM * 16; i += 256) {
+          const int r = i >> 4, c4 = i & 15;
+          const int64_t gr = int64_t(m) * kBM + r;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (gr < a.M) v = *reinterpret_cast<const float4*>(src + gr * a.ldc + n * kBN + c4 * 4);
+          stage[r * 16 + (c4 ^ (r & 7))] = v;
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
       }
 #pragma unroll 1
-      for (int cc = 0; cc < kBN / 16; cc++) {
+      for (int cc = 0; cc < 2; cc++) {
         int q[kLevels][16];
-        const uint32_t base = tmem_base + (uint32_t(g * 32) << 16) + uint32_t(cc * 16);
+        const int c0 = half * 32 + cc * 16;  // the chunk's first column in the tile
+        const uint32_t base = tmem_base + (uint32_t(g * 32) << 16) + uint32_t(c0);
 #pragma unroll
         for (int L = 0; L < kLevels; L++) tmem_ld16_async(base + uint32_t(L * kBN), q[L]);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (cc == kBN / 16 - 1) {  // the accumulators are read: the next tile may start
+        if (cc == 1) {  // this warp's accumulators are read: once all eight are, the next tile may start
           tc::tc_fence_before();
           tc::mbar_arrive(tempty);
         }
         if (!live) continue;
-        const int col0 = n * kBN + cc * 16;
-        float* crow = a.C + uint64_t(row) * a.ldc + col0;
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-          const int col = col0 + e;
-          const int qe[kLevels] = {q[0][e], q[1][e], q[2][e], q[3][e], q[4][e], q[5][e], q[6][e]};
-          float v;
-          if (!oz_decide(qe, ea, l1a, l2a, __ldg(a.eb + col), __ldg(a.l1b + col), __ldg(a.l2b + col), a, &v)) {
-            const unsigned slot = atomicAdd(a.count, 1u);
-            if (slot < a.cap) a.list[slot] = (static_cast<unsigned long long>(row) << 32) | unsigned(col);
-            else atomicOr(a.err, kOzListFull);
-            continue;
+        for (int gq = 0; gq < 4; gq++) {
+          float4* sp = stage + rl * 16 + (((c0 >> 2) + gq) ^ (rl & 7));
+          const float4 cur = *sp;  // the residual or gate input (a listed output keeps it)
+          float o[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int e = gq * 4 + u;
+            const int col = n * kBN + c0 + e;
+            const int qe[kLevels] = {q[0][e], q[1][e], q[2][e], q[3][e], q[4][e], q[5][e], q[6][e]};
+            float v;
+            if (!oz_decide(qe, sr, ar, br, cr, __ldg(a.sb + col), __ldg(a.pb + col), __ldg(a.l2b + col), &v)) {
+              const unsigned slot = atomicAdd(a.count, 1u);
+              if (slot < a.cap) a.list[slot] = (static_cast<unsigned long long>(row) << 32) | unsigned(col);
+              else atomicOr(a.err, kOzListFull);
+              continue;  // k_oz_fixup writes it
+            }
+            if (EPI == kEpiStore) o[u] = v;
+            else if (EPI == kEpiRelu) o[u] = js_relu(v);
+            else if (EPI == kEpiGate) o[u] = o[u] > 0.0f ? v : 0.0f;
+            else o[u] = f32(double(o[u]) + double(v));
           }
-          if (EPI == kEpiStore) crow[e] = v;
-          else if (EPI == kEpiRelu) crow[e] = js_relu(v);
-          else if (EPI == kEpiGate) crow[e] = a.gate[uint64_t(row) * a.ldc + col] > 0.0f ? v : 0.0f;
-          else crow[e] = f32(double(crow[e]) + double(v));
+          *sp = make_float4(o[0], o[1], o[2], o[3]);
         }
       }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      for (int i = et; i < kBM * 16; i += 256) {  // the tile leaves coalesced
+        const int r = i >> 4, c4 = i & 15;
+        const int64_t gr = int64_t(m) * kBM + r;
+        if (gr < a.M) *reinterpret_cast<float4*>(a.C + gr * a.ldc + n * kBN + c4 * 4) = stage[r * 16 + (c4 ^ (r & 7))];
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the stage is free for the next tile
     }
   }
 
@@ -468,7 +570,7 @@ __global__ void __launch_bounds__(256) k_oz_fixup(FixupArgs a) {
 }
 
 // E2's factor: K·255²·Σ_(L=7..10) n_L·2^(−14−8L), n_L = 11 − L pairs of slices
-// i, j ∈ [2, 5] with i + j = L.
+// i, j ∈ [2, 5] with i + j = L. The weights' column term adds E1's K·2^-94.
 inline double dropped_levels_bound(int K) {
   double s = 0.0;
   for (int L = 7; L <= 10; L++) s += double(11 - L) * std::ldexp(1.0, -14 - 8 * L);

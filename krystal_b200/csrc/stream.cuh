@@ -545,7 +545,7 @@ kc_status kc_stream_create_ex(kc_handle* h, uint32_t max_frames, uint64_t max_re
   s->stats.gpu_numa_node = s->place.node;
   s->stats.staging_numa_node = s->stats.worker_numa_node = s->stats.caller_numa_node = -1;
   int threads = int(o.push_threads);
-  if (threads == 0) threads = std::max(1, std::min(4, int(s->place.cpus.size()) / 8));
+  if (threads == 0) threads = std::max(1, std::min(8, int(s->place.cpus.size()) / 4));
   threads = std::max(1, std::min(threads, 64));
   s->stats.push_threads = uint32_t(threads);
   s->worker = std::thread(stream_worker, s);

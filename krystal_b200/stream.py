@@ -47,7 +47,7 @@ class FrameStream:
                  max_p: int = 0, depth: int = 3, copy_results: bool = True, push_threads: int = 0,
                  bind_cpus: bool = True):
         """push_threads: threads that check and stage a large push_many (0:
-        one per 8 CPUs local to the GPU, at most 4); bind_cpus: the worker and
+        one per 4 CPUs local to the GPU, at most 8); bind_cpus: the worker and
         helpers run on the GPU's local CPUs and the staging lies on its NUMA
         node."""
         self._lib = abi.load()
