@@ -386,11 +386,17 @@ def learn_main(args) -> dict | None:
                        "l2": "a step's working set is several GB (saved activations and gradients)",
                        "precision": "exact: f64 accumulation in the reference's order, f32 stores"
                        if args.precision == "exact" else
-                       "tensor cores: tcgen05 split-fp16 GEMMs (fp32-class), f64 attention/pool/selector",
+                       "tensor cores: tcgen05 split-fp16 GEMMs (fp32-class), f32 record-local attention, "
+                       "f64 pool/mixer attention/selector",
                        "step": "pack + forward with saves + backward + per-frame readings + gradient sums + "
-                               "all-reduce + host update + sync of what moved"},
+                               "all-reduce + update plan, update and health check on the device + readback of "
+                               "what moved"},
             "gpu_launches": launches,
             "stage_ms_per_step": {k[:-3]: round(prof[k] / args.steps, 3) for k in prof if k.endswith("_ms")},
+            # the step outside the profiled (frame-sharded) stages on rank 0: the per-frame readings,
+            # the all-gather and all-reduce, the update plan, update and health check, the weight
+            # images rebuilt for what moved, and the readback; this part does not shrink with ranks
+            "unsharded_ms_per_step": round(ms / args.steps - prof.get("total_ms", 0.0) / args.steps, 3),
             "roofline": roof,
             "report": {"frames_seen": rep.frames_seen, "mean_value_loss": rep.mean_value_loss,
                        "mean_entropy": rep.mean_entropy, "update_applied": rep.update_applied},

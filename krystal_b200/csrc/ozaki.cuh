@@ -46,7 +46,7 @@
 // One persistent CTA per SM, 320 threads:
 //   warp 0     TMA: per (128-row, 64-column) tile and 128-wide K chunk the
 //              six B slices (8 KB each) into a two-deep ring, then the six A
-//              slices (16 KB each) into a six-deep ring (3-D tensor maps over
+//              slices (16 KB each) into a five-deep ring (3-D tensor maps over
 //              [slice][row][k] int8, 128-byte swizzle, zero fill past M);
 //   warp 1     MMA issuer: for A slice i, B slices j ≤ 6 − i into level i + j
 //              (four K steps of 32 each), s32 accumulators in TMEM;
@@ -73,10 +73,11 @@ constexpr int kBM = 128, kBN = 64, kBK = 128;    // tile rows, tile columns, K b
 constexpr int kASlot = kBM * kBK;                // 16 KB: one A slice of one chunk
 constexpr int kBSlice = kBN * kBK;               // 8 KB: one B slice of one chunk
 constexpr int kBSlot = kSlices * kBSlice;        // 48 KB
-constexpr int kAStages = 6, kBStages = 2;        // a whole chunk's A slices in flight
+constexpr int kAStages = 5, kBStages = 2;
 constexpr int kThreads = 320;                    // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kStage = kBM * kBN * 4;             // 32 KB: the output tile, f32
-constexpr int kSmem = kAStages * kASlot + kBStages * kBSlot + kStage + 1024 + 256;
+constexpr int kColBytes = 3 * kBN * 8;           // the tile's column terms: 2^eb, the bound's term, ‖b‖₂
+constexpr int kSmem = kAStages * kASlot + kBStages * kBSlot + kStage + kColBytes + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;              // 7 levels x 64 columns used
 constexpr int kSpecial = 0x7fffffff;             // a row with a non-finite entry
 constexpr int kMaxK = 384;                       // keeps both 64-bit parts of ŷ below 2^51
@@ -276,6 +277,7 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, int* v) {
 //   E = 2·(ar·pb + br·sb + cr·‖b‖₂ + 2^-53·|ŷ|) = 2·(E1 + E2 + E4 + E3).
 __device__ __forceinline__ bool oz_decide(const int* q, double sr, double ar, double br, double cr, double sb,
                                           double pb, double l2b, float* out) {
+  // (no early exit: the caller keeps its loop free of branches)
   const long long hi = (static_cast<long long>(q[0]) * 256 + q[1]) * 256 + q[2];
   const long long lo = ((static_cast<long long>(q[3]) * 256 + q[4]) * 256 + q[5]) * 256 + q[6];
   const double y = fma(i64_to_f64(hi), 0x1p32, i64_to_f64(lo)) * (sr * sb);
@@ -284,9 +286,8 @@ __device__ __forceinline__ bool oz_decide(const int* q, double sr, double ar, do
   t = fma(ar, pb, t);
   const double err = 2.0 * t + 0x1p-1060;  // (the last term: a scale that went subnormal)
   const float lo_f = __double2float_rn(y - err), hi_f = __double2float_rn(y + err);
-  if (__float_as_uint(lo_f) != __float_as_uint(hi_f)) return false;
   *out = lo_f;
-  return true;
+  return __float_as_uint(lo_f) == __float_as_uint(hi_f);
 }
 
 template <int EPI>
@@ -298,7 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
   unsigned char* aring = smem;
   unsigned char* bring = smem + kAStages * kASlot;
   float4* stage = reinterpret_cast<float4*>(bring + kBStages * kBSlot);  // [128 rows][16 float4]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + kBStages * kBSlot + kStage);
+  double* colsm = reinterpret_cast<double*>(bring + kBStages * kBSlot + kStage);  // [3][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + kBStages * kBSlot + kStage + kColBytes);
   uint64_t* afull = bars;
   uint64_t* aempty = afull + kAStages;
   uint64_t* bfull = aempty + kAStages;
@@ -457,6 +459,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
           cr = a.gamma * a.l2a[row];
         }
       }
+      if (et < kBN) {  // the tile's column terms, read by every row
+        colsm[et] = a.sb[n * kBN + et];
+        colsm[kBN + et] = a.pb[n * kBN + et];
+        colsm[2 * kBN + et] = a.l2b[n * kBN + et];
+      }
       if (EPI == kEpiResid || EPI == kEpiGate) {  // the residual / gate tile, coalesced
         const float* src = EPI == kEpiGate ? a.gate : a.C;
         for (int i = et; i < kBM * 16; i += 256) {
@@ -466,8 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
           if (gr < a.M) v = *reinterpret_cast<const float4*>(src + gr * a.ldc + n * kBN + c4 * 4);
           stage[r * 16 + (c4 ^ (r & 7))] = v;
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
       }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
 #pragma unroll 1
       for (int cc = 0; cc < 2; cc++) {
         int q[kLevels][16];
@@ -480,30 +487,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_oz_gemm(const __grid_constant__
           tc::tc_fence_before();
           tc::mbar_arrive(tempty);
         }
-        if (!live) continue;
+        uint32_t listed = 0;  // bit e: output e of this chunk goes to the fixup
 #pragma unroll
-        for (int gq = 0; gq < 4; gq++) {
+        for (int gq = 0; gq < 4 && live; gq++) {
           float4* sp = stage + rl * 16 + (((c0 >> 2) + gq) ^ (rl & 7));
           const float4 cur = *sp;  // the residual or gate input (a listed output keeps it)
           float o[4] = {cur.x, cur.y, cur.z, cur.w};
 #pragma unroll
           for (int u = 0; u < 4; u++) {
             const int e = gq * 4 + u;
-            const int col = n * kBN + c0 + e;
+            const int cl = c0 + e;  // column in the tile
             const int qe[kLevels] = {q[0][e], q[1][e], q[2][e], q[3][e], q[4][e], q[5][e], q[6][e]};
             float v;
-            if (!oz_decide(qe, sr, ar, br, cr, __ldg(a.sb + col), __ldg(a.pb + col), __ldg(a.l2b + col), &v)) {
-              const unsigned slot = atomicAdd(a.count, 1u);
-              if (slot < a.cap) a.list[slot] = (static_cast<unsigned long long>(row) << 32) | unsigned(col);
-              else atomicOr(a.err, kOzListFull);
-              continue;  // k_oz_fixup writes it
-            }
-            if (EPI == kEpiStore) o[u] = v;
-            else if (EPI == kEpiRelu) o[u] = js_relu(v);
-            else if (EPI == kEpiGate) o[u] = o[u] > 0.0f ? v : 0.0f;
-            else o[u] = f32(double(o[u]) + double(v));
+            const bool ok = oz_decide(qe, sr, ar, br, cr, colsm[cl], colsm[kBN + cl], colsm[2 * kBN + cl], &v);
+            float r;
+            if (EPI == kEpiStore) r = v;
+            else if (EPI == kEpiRelu) r = js_relu(v);
+            else if (EPI == kEpiGate) r = o[u] > 0.0f ? v : 0.0f;
+            // f32(double(c) + double(v)), the oracle's addInPlace: rounding the
+            // exact sum to f64 and then to f32 equals rounding it to f32 once
+            // (double rounding is innocuous for a sum when 53 >= 2·24 + 2)
+            else r = __fadd_rn(o[u], v);
+            o[u] = ok ? r : o[u];
+            listed |= ok ? 0u : 1u << e;
           }
           *sp = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        if (__any_sync(0xffffffffu, listed != 0)) {  // every lane votes (a row past M lists nothing)
+          while (listed) {
+            const int e = __ffs(listed) - 1;
+            listed &= listed - 1;
+            const int col = n * kBN + c0 + e;
+            const unsigned slot = atomicAdd(a.count, 1u);
+            if (slot < a.cap) a.list[slot] = (static_cast<unsigned long long>(row) << 32) | unsigned(col);
+            else atomicOr(a.err, kOzListFull);
+          }
         }
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");
