@@ -613,11 +613,15 @@ kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, co
   return KC_OK;
 }
 
-// Whether an exact-path product can run on the int8 tensor cores: a forward
+// Whether an exact-path product runs on the int8 tensor cores: a forward
 // matrix of the list read from the weight page, K a multiple of 128 up to
-// 384, N a multiple of 64, A, C and the gate 16-byte aligned.
-bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, int mat, const float* B, uint32_t ldb, float* C,
-             const float* gate, uint32_t N, uint32_t K) {
+// 384, N a multiple of 64, A, C and the gate 16-byte aligned, and enough rows
+// to fill the GPU (a few dozen recomputed frames' question or bank rows take
+// one FP64 launch instead of the slicing, product and fixup launches).
+constexpr uint64_t kOzMinRows = 16384;
+bool oz_fits(const kc_handle* h, const float* A, uint32_t lda, uint64_t M, int mat, const float* B, uint32_t ldb,
+             float* C, const float* gate, uint32_t N, uint32_t K) {
+  if (M < kOzMinRows) return false;
   const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!aligned(C) || (gate && !aligned(gate))) return false;
   if (!h->oz || h->oz_suspend || mat < 0 || size_t(mat) >= h->mats.size()) return false;
@@ -717,7 +721,7 @@ template <int EPI>
 kc_status gemm(kc_handle* h, bool tc, const float* A, uint32_t lda, uint64_t M, int mat, const float* B,
                uint32_t ldb, float* C, uint32_t N, uint32_t K, const float* gate = nullptr) {
   if (tc) return tc_gemm<EPI>(h, A, M, mat, C, gate);
-  if (oz_fits(h, A, lda, mat, B, ldb, C, gate, N, K)) return oz_gemm<EPI>(h, A, lda, M, mat, C, N, K, gate);
+  if (oz_fits(h, A, lda, M, mat, B, ldb, C, gate, N, K)) return oz_gemm<EPI>(h, A, lda, M, mat, C, N, K, gate);
   return dgemm_ld<EPI>(h, A, lda, B, C, M, N, K, gate, ldb);
 }
 

@@ -101,7 +101,7 @@ def test_a_full_list_reruns_on_the_fp64_kernel(ragged):
 
 def test_expired_wait_in_the_int8_product(ragged):
     wl, cfg, w = ragged
-    batch = synth.make_batch(wl, seed=43, frames=16)
+    batch = synth.make_batch(wl, seed=43, frames=48)  # enough tokens for the encoder's products to take the int8 path
     be = make_backend(cfg, w, {})
     try:
         be.set_precision("exact")
