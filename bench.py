@@ -42,6 +42,25 @@ UNIT = "frames/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+# One NCCL process group per process: a run of several configurations
+# (--all-legs) shares it, since tearing a group down and making another in the
+# same process is not reliable with this NCCL.
+_KEEP_PG = False
+
+
+def init_pg(dev) -> None:
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+
+def release_pg() -> None:
+    import torch.distributed as dist
+    if dist.is_initialized() and not _KEEP_PG:
+        dist.destroy_process_group()
+
+
 def load_peaks() -> tuple[dict, str]:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -279,8 +298,7 @@ def learn_main(args) -> dict | None:
     dev = torch.device("cuda", local)
     group = None
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        init_pg(dev)
         group = dist.group.WORLD
     wl = synth.WORKLOADS[args.workload]
     F = args.frames or wl.frames
@@ -410,7 +428,7 @@ def learn_main(args) -> dict | None:
             line["clocks"] = clk
     be.destroy()
     if world > 1:
-        dist.destroy_process_group()
+        release_pg()
     return line
 
 
@@ -510,8 +528,7 @@ def stream_main(args) -> dict | None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        init_pg(dev)
     wl = synth.WORKLOADS[args.workload]
     total = args.frames or wl.frames
     mine = (total - rank + world - 1) // world  # round-robin share of the global stream
@@ -597,7 +614,7 @@ def stream_main(args) -> dict | None:
     st.close()
     be.destroy()
     if world > 1:
-        dist.destroy_process_group()
+        release_pg()
     return line
 
 
@@ -609,6 +626,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.all_legs:
         import copy
+        global _KEEP_PG
+        _KEEP_PG = True
         legs = [("ragged_4096", None, forward_main), ("learn_1024", None, learn_main),
                 ("long_bank_1024", max(1, 1024 // world), forward_main), ("stream_100k", None, stream_main)]
         wanted = set(args.legs.split(","))
@@ -622,6 +641,9 @@ def main():
                 if frames is not None:
                     line["config"]["split"] = f"{frames * world} frames over {world} ranks"
                 print(json.dumps(line), flush=True)
+        _KEEP_PG = False
+        if world > 1:
+            release_pg()
         return
     if args.workload.startswith("stream"):
         line = stream_main(args)
@@ -688,8 +710,7 @@ def forward_main(args, side: bool = False) -> dict | None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        init_pg(dev)
 
     def barrier():
         if world > 1:
@@ -810,7 +831,7 @@ def forward_main(args, side: bool = False) -> dict | None:
     del d_in, d_off, flush
     torch.cuda.empty_cache()
     if world > 1:
-        dist.destroy_process_group()
+        release_pg()
     return line
 
 
