@@ -155,25 +155,13 @@ struct PoolFastArgs {
   float* query_values;
 };
 
-__global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
-  if (g >= a.records) return;
-  const uint32_t start = a.rec_start[g];
-  const int cnt = int(a.rec_meta[g].y & 15u);
-  const uint32_t row = a.rec_row[g];
-  const bool isq = row & 0x80000000u;
-  const uint32_t r = row & 0x7fffffffu;
-  float4* key_out = isq ? nullptr : reinterpret_cast<float4*>(a.bank_keys + uint64_t(r) * KC_H) + lane;
-  float4* val_out = reinterpret_cast<float4*>(isq ? a.query_values + uint64_t(r) * KC_H
-                                                  : a.bank_values + uint64_t(r) * KC_H) + lane;
-  const float4 pk = __ldg(reinterpret_cast<const float4*>(a.pool) + lane);
-  const float4 pv = __ldg(reinterpret_cast<const float4*>(a.pool + KC_H) + lane);
-  // every row of the record in flight before any reduction
-  float4 xs[KC_RW];
-  const float4* xr = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H) + lane;
-#pragma unroll
-  for (int j = 0; j < KC_RW; j++) xs[j] = j < cnt ? __ldg(xr + j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+// The pooled key and value of one record from its rows xs[0..cnt) (lane l
+// holding dims 4l..4l+3 of each row, zeros past cnt) and the two learned
+// queries pk, pv (the lane's dims). Shared by k_pool_fast and the pooling
+// epilogue of the last encoder block's feed-forward kernel, so that both
+// give the same bits.
+__device__ __forceinline__ void pool_record(const float4 (&xs)[KC_RW], int cnt, float4 pk, float4 pv, float scale,
+                                            int lane, float4& ko_out, float4& vo_out) {
   float ks[KC_RW], vs[KC_RW];
 #pragma unroll
   for (int j = 0; j < KC_RW; j++) {
@@ -221,8 +209,8 @@ __global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
 #pragma unroll
   for (int j = 0; j < KC_RW; j++)
     if (j < cnt) {
-      ks[j] *= a.scale;
-      vs[j] *= a.scale;
+      ks[j] *= scale;
+      vs[j] *= scale;
       kmx = fmaxf(kmx, ks[j]);
       vmx = fmaxf(vmx, vs[j]);
     }
@@ -244,6 +232,31 @@ __global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
       vo.x = fmaf(vw, xs[j].x, vo.x); vo.y = fmaf(vw, xs[j].y, vo.y);
       vo.z = fmaf(vw, xs[j].z, vo.z); vo.w = fmaf(vw, xs[j].w, vo.w);
     }
+  ko_out = ko;
+  vo_out = vo;
+}
+
+__global__ void __launch_bounds__(256, 4) k_pool_fast(PoolFastArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = uint64_t(blockIdx.x) * 8 + warp;
+  if (g >= a.records) return;
+  const uint32_t start = a.rec_start[g];
+  const int cnt = int(a.rec_meta[g].y & 15u);
+  const uint32_t row = a.rec_row[g];
+  const bool isq = row & 0x80000000u;
+  const uint32_t r = row & 0x7fffffffu;
+  float4* key_out = isq ? nullptr : reinterpret_cast<float4*>(a.bank_keys + uint64_t(r) * KC_H) + lane;
+  float4* val_out = reinterpret_cast<float4*>(isq ? a.query_values + uint64_t(r) * KC_H
+                                                  : a.bank_values + uint64_t(r) * KC_H) + lane;
+  const float4 pk = __ldg(reinterpret_cast<const float4*>(a.pool) + lane);
+  const float4 pv = __ldg(reinterpret_cast<const float4*>(a.pool + KC_H) + lane);
+  // every row of the record in flight before any reduction
+  float4 xs[KC_RW];
+  const float4* xr = reinterpret_cast<const float4*>(a.x + uint64_t(start) * KC_H) + lane;
+#pragma unroll
+  for (int j = 0; j < KC_RW; j++) xs[j] = j < cnt ? __ldg(xr + j * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 ko, vo;
+  pool_record(xs, cnt, pk, pv, a.scale, lane, ko, vo);
   if (key_out) *key_out = ko;
   *val_out = vo;
 }

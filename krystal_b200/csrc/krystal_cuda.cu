@@ -2668,7 +2668,8 @@ void kc_destroy(kc_handle* h) {
                       &h->ws.rec_start, &h->ws.rec_row, &h->ws.bank_rec, &h->ws.bank_frame, &h->ws.query_rec,
                       &h->ws.query_frame, &h->ws.x, &h->ws.qkv, &h->ws.bk, &h->ws.bv, &h->ws.mk, &h->ws.mv,
                       &h->ws.qstate, &h->ws.mq, &h->ws.mh, &h->ws.sq, &h->ws.sk, &h->ws.p, &h->ws.index,
-                      &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off, &h->ws.word_ids, &h->ws_fb.word_ids};
+                      &h->ws.gather, &h->ws.rows_val, &h->ws.rows_off, &h->ws.word_ids, &h->ws_fb.word_ids,
+                      &h->ws.tile_row, &h->ws.row_rc};
     for (DevBuf* b : bufs)
       if (b->p) cudaFree(b->p), b->p = nullptr;
     Workspace& f = h->ws_fb;

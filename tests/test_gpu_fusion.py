@@ -140,3 +140,18 @@ def test_caller_output_buffers(pair):
     small = dict(out, p=np.empty(int(offs["p_off"][-1]) - 1, np.float32))
     with pytest.raises(Exception):
         fused.forward_batch(batch, out=small)
+
+
+def test_empty_records_at_tile_edges_fused_equals_unfused(pair):
+    """Records without tokens (all PAD) at a batch's first row, where a tile
+    starts (row 120) and at frame ends: the record-aligned tiles of the fused
+    attention must step over them as the unfused sequence does (their pooled
+    key and value are zero)."""
+    fused, unfused = pair
+    frames = [[(0, False)] + frame_of_rows(120) + [(0, True), (0, False)],
+              frame_of_rows(7) + [(0, False)],
+              [(0, True)] + frame_of_rows(129),
+              frame_of_rows(240) + [(0, False)] * 3]
+    batch = layout_batch(frames, seed=77)
+    for precision in ("fast", "certified"):
+        assert_same(run(fused, batch, precision), run(unfused, batch, precision))
