@@ -157,9 +157,7 @@ struct PoolFastArgs {
 
 // The pooled key and value of one record from its rows xs[0..cnt) (lane l
 // holding dims 4l..4l+3 of each row, zeros past cnt) and the two learned
-// queries pk, pv (the lane's dims). Shared by k_pool_fast and the pooling
-// epilogue of the last encoder block's feed-forward kernel, so that both
-// give the same bits.
+// queries pk, pv (the lane's dims).
 __device__ __forceinline__ void pool_record(const float4 (&xs)[KC_RW], int cnt, float4 pk, float4 pv, float scale,
                                             int lane, float4& ko_out, float4& vo_out) {
   float ks[KC_RW], vs[KC_RW];
@@ -1000,63 +998,98 @@ __global__ void __launch_bounds__(256) k_select_fast(SelectFastArgs a) {
 
 // ---------------------------------------------------------------------------
 // Audit of the certification margin on the frames recomputed exactly: for
-// every (question, bank row) pair of listed frame list[blockIdx.x] (its pairs
-// spread over gridDim.y CTAs), the
-// fast score (the selector's fmaf chain over the fast projections, scaled in
-// f32) against the exact score (the f64 chain over the exact projections,
-// rounded to f32), as a ratio to the margin B the selector allowed that pair
+// every (question, bank row) pair of listed frame list[blockIdx.x], the fast
+// score (the selector's fmaf chain over the fast projections, scaled in f32)
+// against the exact score (the f64 chain over the exact projections, rounded
+// to f32), as a ratio to the margin B the selector allowed that pair
 // (kappa_q * scale * |sq| * |sk| + 4u|s^|). The largest ratio goes to *out
 // (non-negative float bits, so an unsigned max orders them). Unmasked: the
 // audit measures score error, which the mask does not change.
+//
+// Tiled like a product: a CTA takes kAuChunk questions (blockIdx.z) x kAuKeys
+// bank rows (blockIdx.y) of the frame, stages their fast and exact rows in
+// shared memory with coalesced asynchronous copies (a key row's float4 c at
+// c ^ (row & 7), so a warp reading one float4 of 32 rows meets 8 bank
+// groups), and each thread forms 4 questions x 1 bank row, reading the key
+// row once for the four.
 // ---------------------------------------------------------------------------
+constexpr int kAuChunk = 16;
+constexpr int kAuKeys = 64;
+constexpr int kAuSmem = 2 * (kAuChunk + kAuKeys) * KC_H * 4;  // fast and exact rows: 80 KB
+
 __global__ void __launch_bounds__(256) k_cert_audit(
     const uint32_t* __restrict__ list, const uint64_t* __restrict__ q_off, const uint64_t* __restrict__ r_off,
     const uint64_t* __restrict__ sub_q_off, const uint64_t* __restrict__ sub_r_off, const float* __restrict__ fsq,
     const float* __restrict__ fsk, const float* __restrict__ esq, const float* __restrict__ esk,
     const float* __restrict__ nq, const float* __restrict__ nk, const float* __restrict__ kappa, float scale,
     double scale_d, unsigned* __restrict__ out) {
+  extern __shared__ __align__(16) float au_smem[];
   __shared__ float red[8];
   const uint32_t f = list[blockIdx.x];
   const uint64_t qb = q_off[f], rb = r_off[f];
-  const uint64_t Q = q_off[f + 1] - qb, R = r_off[f + 1] - rb;
+  const int Q = int(q_off[f + 1] - qb), R = int(r_off[f + 1] - rb);
+  const int c0 = int(blockIdx.z) * kAuChunk, j0 = int(blockIdx.y) * kAuKeys;
+  if (c0 >= Q || j0 >= R) return;
   const uint64_t eq = sub_q_off[blockIdx.x], er = sub_r_off[blockIdx.x];
+  const int nc = min(kAuChunk, Q - c0), nj = min(kAuKeys, R - j0);
+  float4* fq = reinterpret_cast<float4*>(au_smem);  // [kAuChunk][32]
+  float4* xq = fq + kAuChunk * 32;                   // exact
+  float4* fk = xq + kAuChunk * 32;                   // [kAuKeys][32], swizzled
+  float4* xk = fk + kAuKeys * 32;                    // exact, swizzled
+  const int tid = threadIdx.x;
+  for (int i = tid; i < nc * 32; i += 256) {
+    const int c = i >> 5, d4 = i & 31;
+    cp_async16(fq + i, fsq + (qb + c0 + c) * KC_H + d4 * 4);
+    cp_async16(xq + i, esq + (eq + c0 + c) * KC_H + d4 * 4);
+  }
+  for (int i = tid; i < nj * 32; i += 256) {
+    const int j = i >> 5, d4 = i & 31, at = j * 32 + (d4 ^ (j & 7));
+    cp_async16(fk + at, fsk + (rb + j0 + j) * KC_H + d4 * 4);
+    cp_async16(xk + at, esk + (er + j0 + j) * KC_H + d4 * 4);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int j = tid & (kAuKeys - 1), g = tid >> 6;  // bank row j; questions 4g .. 4g+3
   float worst = 0.f;
-  // the frame's pairs are spread over gridDim.y CTAs
-  for (uint64_t idx = uint64_t(blockIdx.y) * blockDim.x + threadIdx.x; idx < Q * R;
-       idx += uint64_t(gridDim.y) * blockDim.x) {
-    const uint64_t c = idx / R, j = idx % R;
-    const float4* q4 = reinterpret_cast<const float4*>(fsq + (qb + c) * KC_H);
-    const float4* k4 = reinterpret_cast<const float4*>(fsk + (rb + j) * KC_H);
-    float sv = 0.f;
+  if (j < nj && 4 * g < nc) {
+    float sv[4] = {0.f, 0.f, 0.f, 0.f};
+    double dv[4] = {0.0, 0.0, 0.0, 0.0};
+    const float4* fkr = fk + j * 32;
+    const float4* xkr = xk + j * 32;
     for (int d4 = 0; d4 < KC_H / 4; d4++) {
-      const float4 a = q4[d4], b = k4[d4];
-      sv = fmaf(a.x, b.x, sv);
-      sv = fmaf(a.y, b.y, sv);
-      sv = fmaf(a.z, b.z, sv);
-      sv = fmaf(a.w, b.w, sv);
+      const float4 b = fkr[d4 ^ (j & 7)], e = xkr[d4 ^ (j & 7)];
+      const double ex = double(e.x), ey = double(e.y), ez = double(e.z), ew = double(e.w);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float4 a = fq[(4 * g + u) * 32 + d4], x = xq[(4 * g + u) * 32 + d4];
+        sv[u] = fmaf(a.x, b.x, sv[u]);
+        sv[u] = fmaf(a.y, b.y, sv[u]);
+        sv[u] = fmaf(a.z, b.z, sv[u]);
+        sv[u] = fmaf(a.w, b.w, sv[u]);
+        dv[u] = fma(double(x.x), ex, dv[u]);
+        dv[u] = fma(double(x.y), ey, dv[u]);
+        dv[u] = fma(double(x.z), ez, dv[u]);
+        dv[u] = fma(double(x.w), ew, dv[u]);
+      }
     }
-    const float fs = sv * scale;
-    const float4* eq4 = reinterpret_cast<const float4*>(esq + (eq + c) * KC_H);
-    const float4* ek4 = reinterpret_cast<const float4*>(esk + (er + j) * KC_H);
-    double dv = 0.0;
-    for (int d4 = 0; d4 < KC_H / 4; d4++) {
-      const float4 a = eq4[d4], b = ek4[d4];
-      dv = fma(double(a.x), double(b.x), dv);
-      dv = fma(double(a.y), double(b.y), dv);
-      dv = fma(double(a.z), double(b.z), dv);
-      dv = fma(double(a.w), double(b.w), dv);
+    const float nkj = nk[rb + j0 + j];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int c = c0 + 4 * g + u;
+      if (c >= Q) break;
+      const float fs = sv[u] * scale;
+      const float es = __double2float_rn(dv[u] * scale_d);
+      const float bound = kappa[qb + c] * scale * nq[qb + c] * nkj + 2.384185791015625e-07f * fabsf(fs);
+      const float r = fabsf(fs - es) / bound;
+      if (r == r) worst = fmaxf(worst, r);  // a non-finite score was never certified
     }
-    const float es = __double2float_rn(dv * scale_d);
-    const float bound = kappa[qb + c] * scale * nq[qb + c] * nk[rb + j] + 2.384185791015625e-07f * fabsf(fs);
-    const float r = fabsf(fs - es) / bound;
-    if (r == r) worst = fmaxf(worst, r);  // a non-finite score was never certified
   }
   for (int o = 16; o; o >>= 1) worst = fmaxf(worst, __shfl_xor_sync(0xffffffffu, worst, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = worst;
+  if ((tid & 31) == 0) red[tid >> 5] = worst;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     float m = 0.f;
-    for (int w = 0; w < int(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+    for (int w = 0; w < 8; w++) m = fmaxf(m, red[w]);
     atomicMax(out, __float_as_uint(m));
   }
 }

@@ -1274,7 +1274,9 @@ kc_status certify(kc_handle* h, Workspace& ws, const DevBatch& b, const kc::Fram
   KC_CHECK(forward_exact(h, fb, sub, sub_tot, false));
   // audit the margin on the recomputed frames: the fast scores against the exact ones
   KC_TRY(cudaMemsetAsync(h->d_audit, 0, sizeof(float), h->stream), "memset");
-  kc::k_cert_audit<<<dim3(n, 32), 256, 0, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
+  const dim3 agrid(n, (std::max<uint32_t>(sub_tot.max_r, 1) + kc::kAuKeys - 1) / kc::kAuKeys,
+                   (std::max<uint32_t>(sub_tot.max_q, 1) + kc::kAuChunk - 1) / kc::kAuChunk);
+  kc::k_cert_audit<<<agrid, 256, kc::kAuSmem, h->stream>>>(P<uint32_t>(fb.list), P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
                                              P<uint64_t>(fb.q_off), P<uint64_t>(fb.r_off), P<float>(ws.sq),
                                              P<float>(ws.sk), P<float>(fb.sq), P<float>(fb.sk), P<float>(ws.nq),
                                              P<float>(ws.nk), P<float>(ws.kappa),
@@ -1823,6 +1825,8 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
     return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_scores_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kSsSmem)))) return bail(e, "smem");
+  if ((e = cudaFuncSetAttribute(kc::k_cert_audit, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kc::kAuSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_scores_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kXsSmem)))) return bail(e, "smem");
   if ((e = cudaFuncSetAttribute(kc::k_select_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
