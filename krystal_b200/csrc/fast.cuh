@@ -514,15 +514,20 @@ __global__ void __launch_bounds__(kCaThreads, 2) k_cross_attn_frame(CrossAttnFra
 // Mixer cross-attention for banks of at most kCsMaxBank keys: the same
 // arithmetic as k_cross_attn_frame (bit for bit) in one pass, the chunk's
 // scores for the whole bank held in shared memory, so that small frames need
-// neither the key-block staging nor the second score pass. One CTA per chunk
-// of up to kCsChunk questions (as many as the score buffer holds); each bank
-// row's k and v slices are loaded once per chunk; p·v per output column, the
-// even keys' sum on threads 0-127 and the odd keys' on 128-255, each in key
-// order, every question of the chunk at once.
+// no second score pass. One CTA per chunk of up to kCsChunk questions (as
+// many as the score buffer holds). The bank's k rows pass through shared
+// memory in blocks of kCsKeys rows, copied asynchronously with coalesced
+// 16-byte copies (row j's float4 c at c ^ (j & 7), so a warp reading one
+// float4 of 32 rows meets 8 bank groups); a score thread takes one (key,
+// head) of the block for every question of the chunk. p·v per output column,
+// the even keys' sum on threads 0-127 and the odd keys' on 128-255, each in
+// key order, every question of the chunk at once, v read straight from
+// global memory (a warp reads 128 contiguous bytes of a row).
 // ---------------------------------------------------------------------------
 constexpr int kCsMaxBank = 256;
 constexpr int kCsChunk = 8;
 constexpr int kCsThreads = 256;
+constexpr int kCsKeys = kCsThreads / KC_HEADS;  // keys per staged k block: one (key, head) per thread
 
 struct CrossAttnSmallArgs {
   const float* mq;
@@ -541,7 +546,7 @@ struct CrossAttnSmallArgs {
 // (c, head) at (c*4 + head)*2*half + (j&1)*half + (j>>1), so each p·v chain
 // (one key parity) reads four keys per float4.
 __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSmallArgs a) {
-  extern __shared__ __align__(16) float cas_smem[];  // scores [qc][4][2*half], then q [qc][128]
+  extern __shared__ __align__(16) float cas_smem[];  // scores [qc][4][2*half], q [qc][128], k [kCsKeys][128]
   __shared__ float inv_s[kCsChunk][KC_HEADS];
   const uint32_t f = blockIdx.x / a.chunks;
   const int q0 = int(blockIdx.x % a.chunks) * a.qc;
@@ -557,45 +562,44 @@ __global__ void __launch_bounds__(kCsThreads, 3) k_cross_attn_small(CrossAttnSma
     const int nc = min(a.qc, nq - q0);
     for (int i = tid; i < nc * KC_H; i += kCsThreads) qs[i] = a.mq[(qb + q0) * KC_H + i];
     __syncthreads();
-    // scores: two keys of one head per thread (j and j + ceil(R/2)), head-
-    // major so a warp reads one q slice (a broadcast) and each q value feeds
-    // both keys' chains; each k slice is loaded once for the chunk, and the
-    // chunk's questions run as independent chains
-    const int R2 = (R + 1) >> 1;
-    for (int idx = tid; idx < R2 * KC_HEADS; idx += kCsThreads) {
-      const int head = idx / R2, ja = idx - head * R2, jb = ja + R2, hb = head * KC_HEAD_DIM;
-      const bool two = jb < R;
-      const float4* kra = reinterpret_cast<const float4*>(a.mk + (rb + ja) * KC_H + hb);
-      const float4* krb = reinterpret_cast<const float4*>(a.mk + (rb + (two ? jb : ja)) * KC_H + hb);
-      float sa[kCsChunk], sb[kCsChunk];
+    // scores, a block of kCsKeys keys at a time: thread (head, key) of the
+    // block, the 32-long fmaf chain in dimension order for every question of
+    // the chunk (q from shared memory, a broadcast within the warp's head)
+    {
+    float4* kbuf = reinterpret_cast<float4*>(qs + size_t(a.qc) * KC_H);
+    const int kh = tid / kCsKeys, jj = tid % kCsKeys, hb = kh * KC_HEAD_DIM;
+    for (int kb0 = 0; kb0 < R; kb0 += kCsKeys) {
+      const int nb = min(kCsKeys, R - kb0);
+      for (int i = tid; i < nb * (KC_H / 4); i += kCsThreads) {
+        const int j = i >> 5, c4 = i & 31;
+        cp_async16(kbuf + j * 32 + (c4 ^ (j & 7)), a.mk + (rb + kb0 + j) * KC_H + c4 * 4);
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      if (jj < nb) {
+        float sa[kCsChunk];
 #pragma unroll
-      for (int c = 0; c < kCsChunk; c++) sa[c] = sb[c] = 0.f;
+        for (int c = 0; c < kCsChunk; c++) sa[c] = 0.f;
 #pragma unroll 2
-      for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
-        const float4 x = kra[d4], y = krb[d4];
+        for (int d4 = 0; d4 < KC_HEAD_DIM / 4; d4++) {
+          const float4 x = kbuf[jj * 32 + ((kh * 8 + d4) ^ (jj & 7))];
+#pragma unroll
+          for (int c = 0; c < kCsChunk; c++)
+            if (c < nc) {
+              const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
+              sa[c] = fmaf(q4.x, x.x, sa[c]);
+              sa[c] = fmaf(q4.y, x.y, sa[c]);
+              sa[c] = fmaf(q4.z, x.z, sa[c]);
+              sa[c] = fmaf(q4.w, x.w, sa[c]);
+            }
+        }
 #pragma unroll
         for (int c = 0; c < kCsChunk; c++)
-          if (c < nc) {
-            const float4 q4 = reinterpret_cast<const float4*>(qs + c * KC_H + hb)[d4];
-            sa[c] = fmaf(q4.x, x.x, sa[c]);
-            sa[c] = fmaf(q4.y, x.y, sa[c]);
-            sa[c] = fmaf(q4.z, x.z, sa[c]);
-            sa[c] = fmaf(q4.w, x.w, sa[c]);
-            sb[c] = fmaf(q4.x, y.x, sb[c]);
-            sb[c] = fmaf(q4.y, y.y, sb[c]);
-            sb[c] = fmaf(q4.z, y.z, sb[c]);
-            sb[c] = fmaf(q4.w, y.w, sb[c]);
-          }
+          if (c < nc) at(sc + (c * KC_HEADS + kh) * stride, kb0 + jj) = sa[c] * a.scale;
       }
-#pragma unroll
-      for (int c = 0; c < kCsChunk; c++)
-        if (c < nc) {
-          float* row = sc + (c * KC_HEADS + head) * stride;
-          at(row, ja) = sa[c] * a.scale;
-          if (two) at(row, jb) = sb[c] * a.scale;
-        }
+      __syncthreads();  // the block is read before the next one lands
     }
-    __syncthreads();
+    }
     // softmax rows (question, head): one warp each
     for (int rw = warp; rw < nc * KC_HEADS; rw += kCsThreads / 32) {
       float* row = sc + size_t(rw) * stride;

@@ -550,12 +550,14 @@ CrossShape cross_shape(uint32_t max_r) {
 
 // The one-pass cross attention's score-row parity half for banks of at most
 // max_r rows (16 mod 32, at least half the longest bank) and its shared memory
-// (scores [kCsChunk][4][2*half], then q [kCsChunk][128]).
+// (scores [kCsChunk][4][2*half], q [kCsChunk][128], then a block of kCsKeys
+// k rows).
 int cross_small_half(uint32_t max_r) {
   return int((std::max<uint32_t>(max_r, 1) + 1) / 2 + 31) / 32 * 32 + 16;
 }
 size_t cross_small_smem(uint32_t max_r) {
-  return size_t(kc::kCsChunk) * KC_HEADS * 2 * cross_small_half(max_r) * 4 + size_t(kc::kCsChunk) * KC_H * 4;
+  return size_t(kc::kCsChunk) * KC_HEADS * 2 * cross_small_half(max_r) * 4 + size_t(kc::kCsChunk) * KC_H * 4 +
+         size_t(kc::kCsKeys) * KC_H * 4;
 }
 
 // The same for the per-frame selector (scores [qc][max_r], then q [qc][128]).
