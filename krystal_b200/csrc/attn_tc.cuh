@@ -103,6 +103,9 @@ __device__ __forceinline__ float4 lds4_if(uint32_t addr, bool p) {
   return v;
 }
 
+// WORDS: the same-word bias is on (a.word_ids set); the kernel without it
+// keeps no per-key word registers.
+template <bool WORDS>
 __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant__ CUtensorMap xmap, AttnTcArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
@@ -283,7 +286,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
     unsigned char* rb = res + half * kAtResBytes;  // x[:, hd*32 .. +32] of the tile, TMA 128-byte swizzle
     const bool issuer = q == 0 && lane == 0;
     const uint32_t slot_u32 = smem_u32(slot);
-    const bool words = a.word_ids != nullptr;
+    constexpr bool words = WORDS;
     const uint32_t lq = uint32_t(q * 32) << 16;
     uint32_t tl = 0;
     bool ok = true;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_tc_attn(const __grid_constant
       tc_fence_after();
       if (k + int(gridDim.x) < a.tiles && i < nrow1 - nrow0) nrc = a.row_rc[nrow0 + i];
       const uint32_t qcol = (tl & 1) ? 384u : 0u;
-#pragma unroll
+#pragma unroll 1  // the two rounds as a loop: unrolled, the kernel spilled registers
       for (int r = 0; r < 2; r++) {
         const int hd = 2 * half + r;
         if (r == 1) named_bar(bar_id, 128);  // round 0 is done with the slot and the residual buffer

@@ -610,7 +610,10 @@ kc_status tc_attn(kc_handle* h, Workspace& ws, float* x, uint64_t T, int mat, co
   aa.word_alpha = word_alpha; aa.scale = scale; aa.err = h->d_err;
   aa.inject_expiry = take_injection(h, KC_INJECT_ATTN);
   const unsigned grid = unsigned(std::min<uint64_t>(uint64_t(aa.tiles), uint64_t(h->sms)));
-  kc::tc::k_tc_attn<<<grid, kc::tc::kAtThreads, kc::tc::kAtSmem, h->stream>>>(xmap, aa);
+  if (aa.word_ids)
+    kc::tc::k_tc_attn<true><<<grid, kc::tc::kAtThreads, kc::tc::kAtSmem, h->stream>>>(xmap, aa);
+  else
+    kc::tc::k_tc_attn<false><<<grid, kc::tc::kAtThreads, kc::tc::kAtSmem, h->stream>>>(xmap, aa);
   h->launches++;
   return KC_OK;
 }
@@ -1806,7 +1809,10 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
       (e = cudaFuncSetAttribute(kc::tc::k_tc_gemm<kc::tc::kEpiGate>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kc::tc::kSmemBytesT)) ||
       (e = cudaFuncSetAttribute(kc::tc::k_tc_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kFfnSmem)) ||
-      (e = cudaFuncSetAttribute(kc::tc::k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kc::tc::kAtSmem)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_attn<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kAtSmem)) ||
+      (e = cudaFuncSetAttribute(kc::tc::k_tc_attn<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kc::tc::kAtSmem)) ||
       (e = cudaFuncSetAttribute(kc::k_embed_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kc::kEmbedSmemMax))) ||
       (e = cudaFuncSetAttribute(kc::k_learn_plan, cudaFuncAttributeMaxDynamicSharedMemorySize,
