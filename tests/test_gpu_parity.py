@@ -239,6 +239,23 @@ def test_edge_frames_match_oracle(oracle, small_backend, mode):
 
 
 @pytest.mark.parametrize("mode", MODES)
+def test_batch_without_token_rows_matches_oracle(oracle, small_backend, mode):
+    """Every record rowless (all PAD): no encoder rows at all, every pooled key
+    and value zero."""
+    cfg, w, be = small_backend
+    be.set_precision(mode)
+    frames = [[dict(tokens=[]), dict(tokens=[0, 0]), dict(query=True, tokens=[])],
+              [dict(query=True, tokens=[0]), dict(tokens=[])]]
+    batch = _records_batch(frames)
+    res = be.forward_batch(batch, want_query_output=True)
+    want = oracle.forward_batch(cfg, w.page, batch, want_query_output=True)
+    be.set_precision("certified")
+    assert res["total_t"] == 0
+    check_batch(res, want, mode, 1.0)
+    assert np.abs(res["query_output"] - want["query_output"]).max() <= (0.0 if mode == "exact" else 1e-4)
+
+
+@pytest.mark.parametrize("mode", MODES)
 def test_rule_that_admits_nothing_reopens_the_row(oracle, small_backend, mode):
     cfg, w, be = small_backend
     be.set_precision(mode)
