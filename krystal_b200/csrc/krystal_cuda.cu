@@ -243,6 +243,10 @@ struct kc_handle {
   std::vector<Mat> mats;
   std::vector<float> mat_max;       // max |W| per matrix (host side, from the last sync)
   std::vector<uint64_t> img_off;    // byte offset of each matrix's image
+  // the bank-side projections that share an input, as the matrices of one
+  // planes product (their images contiguous, in this order): bk through the
+  // selector's Wk then each mixer block's Wk, bv through each block's Wv
+  std::vector<int> kplanes, vplanes;
   DevBuf images;
   std::vector<char> mat_dirty;      // per matrix: its image is stale
   int* d_err = nullptr;             // tensor-core pipeline error word
@@ -458,12 +462,16 @@ kc_status build_images(kc_handle* h) {
   KC_CHECK(build_transposes(h));
   const auto& m = h->mats;
   if (h->img_off.size() != m.size()) {
-    h->img_off.resize(m.size());
+    h->img_off.assign(m.size(), ~uint64_t(0));
     uint64_t off = 0;
-    for (size_t i = 0; i < m.size(); i++) {
+    auto place = [&](int i) {
+      if (h->img_off[i] != ~uint64_t(0)) return;
       h->img_off[i] = off;
       off += uint64_t(m[i].n) * m[i].k * 4;  // hi + lo fp16
-    }
+    };
+    for (int i : h->kplanes) place(i);  // each planes group contiguous, in plane order
+    for (int i : h->vplanes) place(i);
+    for (size_t i = 0; i < m.size(); i++) place(int(i));
     KC_TRY(ensure(h, h->images, off), "weight images");
   }
   for (size_t i = 0; i < m.size(); i++) {
@@ -492,6 +500,20 @@ int take_injection(kc_handle* h, int kernel) {
   return 1;
 }
 
+// The planes groups of a geometry: the selector's Wk and each mixer block's
+// Wk (all read bk), each block's Wv (all read bv); empty when a group does
+// not fit one planes product (square H = 128 matrices, at most kMaxPlanes).
+void plan_planes(kc_handle* h) {
+  const Dims& d = h->d;
+  h->kplanes.clear();
+  h->vplanes.clear();
+  const int mix_m = 3 * int(d.enc), sel_m = mix_m + 5 * int(d.mix);
+  if (d.h != 128 || d.mix == 0 || int(d.mix) + 1 > kc::tc::kMaxPlanes) return;
+  h->kplanes.push_back(sel_m + 1);
+  for (uint32_t b = 0; b < d.mix; b++) h->kplanes.push_back(mix_m + 5 * int(b) + 1);
+  for (uint32_t b = 0; b < d.mix; b++) h->vplanes.push_back(mix_m + 5 * int(b) + 2);
+}
+
 // y = A·Wᵀ on the tensor cores for matrix `mat` of mat_list.
 template <int EPI>
 kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, const float* gate = nullptr) {
@@ -507,6 +529,25 @@ kc_status tc_gemm(kc_handle* h, const float* A, uint64_t M, int mat, float* C, c
   const uint64_t tiles = ((M + 127) / 128) * (mt.n / 128);
   const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
   kc::tc::k_tc_gemm<EPI><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, gmap, g);
+  h->launches++;
+  return KC_OK;
+}
+
+// C[p] = A·W_pᵀ for the matrices of a planes group (contiguous images, H x
+// H each) in one product: A is read once for all of them, and plane p of C
+// ([planes, M, 128]) holds what tc_gemm<kEpiStore> of matrix p would store.
+kc_status tc_gemm_planes(kc_handle* h, const float* A, uint64_t M, const std::vector<int>& mats, float* C) {
+  if (M == 0) return KC_OK;
+  CUtensorMap map, cmap;
+  if (!kc::tc::make_a_map(&map, A, M, 128, 128) || !kc::tc::make_c_map3(&cmap, C, M, mats.size()))
+    return fail(h, KC_ERR_CUDA, "the driver refused a tensor map for a GEMM operand");
+  kc::tc::GemmArgs g{int(M), 128, int(mats.size()), P<uint8_t>(h->images) + h->img_off[mats[0]], C, 128,
+                     std::ldexp(1.0f, h->sa), 1.0f, h->d_err, take_injection(h, KC_INJECT_GEMM)};
+  g.planes = int(mats.size());
+  for (size_t p = 0; p < mats.size(); p++) g.unscale_n[p] = std::ldexp(1.0f, -(h->sa + mat_sw(h, mats[p])));
+  const uint64_t tiles = ((M + 127) / 128) * mats.size();
+  const unsigned grid = unsigned(tiles < uint64_t(h->sms) ? tiles : uint64_t(h->sms));
+  kc::tc::k_tc_gemm<kc::tc::kEpiStore><<<grid, kc::tc::kThreadsT, kc::tc::kSmemBytesT, h->stream>>>(map, cmap, cmap, g);
   h->launches++;
   return KC_OK;
 }
@@ -1130,16 +1171,31 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
     kc::k_pool_fast<<<unsigned((N + 7) / 8), 256, 0, h->stream>>>(pa);
     h->launches++;
   }
+  // the bank-side projections as planes products: bk once through the
+  // selector's Wk (plane 0 of ws.sk, where the selector reads it) and every
+  // block's Wk (planes 1..), bv once through every block's Wv (planes of ws.mv)
+  const bool planes = !h->kplanes.empty() && Q > 0;
+  if (planes) {
+    ProfScope ps(h, kStMixer);
+    KC_TRY(ensure(h, ws.sk, h->kplanes.size() * R * H * 4), "workspace");
+    KC_TRY(ensure(h, ws.mv, h->vplanes.size() * R * H * 4), "workspace");
+    KC_CHECK(tc_gemm_planes(h, P<float>(ws.bk), R, h->kplanes, P<float>(ws.sk)));
+    KC_CHECK(tc_gemm_planes(h, P<float>(ws.bv), R, h->vplanes, P<float>(ws.mv)));
+  }
   if (Q > 0) {
     ProfScope ps(h, kStMixer);
     for (uint32_t blk = 0; blk < d.mix; blk++) {
       const int m0 = mix_m + 5 * int(blk);
       KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, m0, P<float>(ws.mq)));
-      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, P<float>(ws.mk)));
-      KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, P<float>(ws.mv)));
+      float* mk = planes ? P<float>(ws.sk) + (1 + blk) * R * H : P<float>(ws.mk);
+      float* mv = planes ? P<float>(ws.mv) + blk * R * H : P<float>(ws.mv);
+      if (!planes) {
+        KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, m0 + 1, mk));
+        KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bv), R, m0 + 2, mv));
+      }
       if (tot.max_r <= uint32_t(kc::kCsMaxBank)) {  // every bank fits the one-pass kernel's score buffer
         const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCsChunk - 1) / kc::kCsChunk);
-        kc::CrossAttnSmallArgs ca{P<float>(ws.mq),       P<float>(ws.mk),         P<float>(ws.mv),
+        kc::CrossAttnSmallArgs ca{P<float>(ws.mq),       mk,                      mv,
                                   P<float>(ws.qstate),   P<uint64_t>(ws.q_off),   P<uint64_t>(ws.r_off),
                                   kc::kCsChunk,          chunks,                  cross_small_half(tot.max_r),
                                   attn_scale};
@@ -1148,7 +1204,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
       } else {
         const CrossShape cs = cross_shape(tot.max_r);
         const int chunks = int((std::max<uint32_t>(tot.max_q, 1) + kc::kCaChunk - 1) / kc::kCaChunk);
-        kc::CrossAttnFrameArgs ca{P<float>(ws.mq),       P<float>(ws.mk),       P<float>(ws.mv),
+        kc::CrossAttnFrameArgs ca{P<float>(ws.mq),       mk,                    mv,
                                   P<float>(ws.qstate),   P<uint64_t>(ws.q_off), P<uint64_t>(ws.r_off),
                                   chunks,                cs.kb,                 cs.half,
                                   attn_scale};
@@ -1162,7 +1218,7 @@ kc_status forward_fast(kc_handle* h, Workspace& ws, const DevBatch& b, const kc:
   if (Q > 0) {
     ProfScope ps(h, kStSelector);
     KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.qstate), Q, sel_m, P<float>(ws.sq)));
-    KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, sel_m + 1, P<float>(ws.sk)));
+    if (!planes) KC_CHECK(tc_gemm<kc::tc::kEpiStore>(h, P<float>(ws.bk), R, sel_m + 1, P<float>(ws.sk)));
     launch_select_fast(h, ws, b, tot);
   }
   KC_TRY(cudaGetLastError(), "launch");
@@ -1792,6 +1848,12 @@ kc_status kc_create(const kc_config* config, const kc_weights_view* weights, int
   if ((e = cudaMalloc(&h->d_audit, sizeof(float)))) return bail(e, "audit word");
   if ((e = cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device))) return bail(e, "attributes");
   h->mats = mat_list(h->d);
+  {
+    // KC_NO_PLANES=1 at kc_create: one product per bank-side projection (the
+    // same bits; kept to check the planes products against)
+    const char* np = std::getenv("KC_NO_PLANES");
+    if (!(np && np[0] && np[0] != '0')) plan_planes(h);
+  }
   h->mat_max.assign(h->mats.size(), 0.f);
   h->mat_dirty.assign(h->mats.size(), 1);
   h->oz_dirty.assign(h->mats.size(), 1);

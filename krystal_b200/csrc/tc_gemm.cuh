@@ -247,6 +247,8 @@ __device__ __forceinline__ uint32_t swz_offset(uint32_t row, uint32_t k) {
 // ReLU backward gate (C = gate > 0 ? acc : 0, the gate [M, N] loaded by TMA).
 enum { kEpiStore = 0, kEpiRelu = 1, kEpiResid = 2, kEpiGate = 3 };
 
+constexpr int kMaxPlanes = 8;
+
 struct GemmArgs {
   int M, K;
   int n_sub;             // N / 128
@@ -257,6 +259,11 @@ struct GemmArgs {
   float unscale;         // 2^-(sa+sw)
   int* err;              // error word
   int inject_expiry;     // test hook: the producer reports an expired wait before it issues any copy
+  // kEpiStore over several matrices of one input (planes > 1): n-tile p is
+  // matrix p, scaled by unscale_n[p] and stored to plane p of a [planes, M,
+  // 128] output through a 3-D map, as separate products would store them
+  int planes;
+  float unscale_n[kMaxPlanes];
 };
 
 // 2-D TMA load of a [128 rows x 64 f32] box of A (no swizzle) at (x = k, y = row).
@@ -455,6 +462,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       if (!okw) { ok = false; break; }
       tc_fence_after();
       const int row0 = m * kBM + g * 32;
+      float us = a.unscale;
+      if (a.planes > 1)
+#pragma unroll
+        for (int p = 0; p < kMaxPlanes; p++) us = p == n ? a.unscale_n[p] : us;
 #pragma unroll 1
       for (int cc = 0; cc < kBN / 32; cc++) {
         const int b = cc & 1;
@@ -489,8 +500,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
         unsigned char* rowp = buf + lane * 128;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-          float4 o = make_float4(v[4 * j] * a.unscale, v[4 * j + 1] * a.unscale, v[4 * j + 2] * a.unscale,
-                                 v[4 * j + 3] * a.unscale);
+          float4 o = make_float4(v[4 * j] * us, v[4 * j + 1] * us, v[4 * j + 2] * us, v[4 * j + 3] * us);
           float4* cp = reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4));
           if (EPI == kEpiRelu) {
             o.x = fmaxf(o.x, 0.f); o.y = fmaxf(o.y, 0.f); o.z = fmaxf(o.z, 0.f); o.w = fmaxf(o.w, 0.f);
@@ -507,9 +517,15 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
-                       ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0), "r"(smem_u32(buf))
-                       : "memory");
+          if (a.planes > 1)
+            asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                         ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(cc * 32), "r"(row0), "r"(n),
+                         "r"(smem_u32(buf))
+                         : "memory");
+          else
+            asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                         ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(x), "r"(row0), "r"(smem_u32(buf))
+                         : "memory");
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
       }
@@ -583,6 +599,20 @@ inline bool make_c_map(CUtensorMap* map, const float* C, uint64_t rows, uint64_t
   const cuuint32_t box[2] = {32, 32};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(C), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The output map of a planes product: [planes, rows, 128] f32, the planes
+// contiguous, [1 x 32 x 32] boxes, 128-byte swizzle (as make_c_map per plane).
+inline bool make_c_map3(CUtensorMap* map, const float* C, uint64_t rows, uint64_t planes) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(C) & 15) || rows == 0 || planes == 0) return false;
+  const cuuint64_t dims[3] = {128, rows, planes};
+  const cuuint64_t strides[2] = {128 * 4, rows * 128 * 4};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(C), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

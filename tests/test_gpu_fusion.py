@@ -155,3 +155,26 @@ def test_empty_records_at_tile_edges_fused_equals_unfused(pair):
     batch = layout_batch(frames, seed=77)
     for precision in ("fast", "certified"):
         assert_same(run(fused, batch, precision), run(unfused, batch, precision))
+
+
+def test_planes_products_equal_separate_products():
+    """The bank-side projections as one planes product per input (bk through
+    the selector's and every mixer block's Wk, bv through every block's Wv)
+    give the bits of one product per matrix (a handle created with
+    KC_NO_PLANES=1)."""
+    old = os.environ.pop("KC_NO_PLANES", None)
+    try:
+        with_planes = CudaBrainBackend(CFG, W, 0)
+        os.environ["KC_NO_PLANES"] = "1"
+        without = CudaBrainBackend(CFG, W, 0)
+    finally:
+        os.environ.pop("KC_NO_PLANES", None)
+        if old is not None:
+            os.environ["KC_NO_PLANES"] = old
+    try:
+        batch = synth.make_batch(WL, seed=53, frames=256)
+        for precision in ("fast", "certified"):
+            assert_same(run(with_planes, batch, precision), run(without, batch, precision))
+    finally:
+        with_planes.destroy()
+        without.destroy()
