@@ -559,31 +559,74 @@ struct FixupArgs {
   unsigned long long* listed;   // running total of listed outputs (profile counter)
 };
 
+// The sequential f64 chain of one listed output in k order, as k_dgemm_exact
+// forms it, and its store through the product's epilogue.
+template <int EPI>
+__device__ __forceinline__ void oz_fix_store(const FixupArgs& a, uint64_t row, int col, double acc) {
+  const float v = f32(acc);
+  float* cp = a.C + row * uint64_t(a.ldc) + col;
+  if (EPI == kEpiStore) *cp = v;
+  else if (EPI == kEpiRelu) *cp = js_relu(v);
+  else if (EPI == kEpiGate) *cp = a.gate[row * uint64_t(a.ldc) + col] > 0.0f ? v : 0.0f;
+  else *cp = f32(double(*cp) + double(v));
+}
+
+// Many listed outputs (more than 8 per warp of the grid): a thread per
+// output, its row loads inside the chain, latency hidden by the other
+// threads. Few (the frames a certified batch recomputes): a warp per output,
+// the lanes bringing its A row and B row into shared memory with coalesced
+// loads (one round trip), lane 0 running the chain over them. Either way the
+// same chain, so the same bits.
 template <int EPI>
 __global__ void __launch_bounds__(256) k_oz_fixup(FixupArgs a) {
+  __shared__ float4 rows[8][2][kMaxK / 4];  // per warp: the A row, the B row
   const unsigned n = min(*a.count, a.cap);
   if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(a.listed, static_cast<unsigned long long>(n));
-  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+  if (n > gridDim.x * 64u) {
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+      const unsigned long long ent = a.list[i];
+      const uint64_t row = ent >> 32;
+      const int col = int(ent & 0xffffffffu);
+      const float* ar = a.A + row * a.lda;
+      const float* br = a.B + uint64_t(col) * a.ldb;
+      double acc = 0.0;
+      for (int k = 0; k < a.K; k += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(ar + k);
+        const float4 w = *reinterpret_cast<const float4*>(br + k);
+        acc = fma(double(x.x), double(w.x), acc);
+        acc = fma(double(x.y), double(w.y), acc);
+        acc = fma(double(x.z), double(w.z), acc);
+        acc = fma(double(x.w), double(w.w), acc);
+      }
+      oz_fix_store<EPI>(a, row, col, acc);
+    }
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k4 = a.K / 4;
+  for (unsigned i = blockIdx.x * 8 + warp; i < n; i += gridDim.x * 8) {
     const unsigned long long ent = a.list[i];
     const uint64_t row = ent >> 32;
     const int col = int(ent & 0xffffffffu);
-    const float* ar = a.A + row * a.lda;
-    const float* br = a.B + uint64_t(col) * a.ldb;
-    double acc = 0.0;
-    for (int k = 0; k < a.K; k += 4) {
-      const float4 x = *reinterpret_cast<const float4*>(ar + k);
-      const float4 w = *reinterpret_cast<const float4*>(br + k);
-      acc = fma(double(x.x), double(w.x), acc);
-      acc = fma(double(x.y), double(w.y), acc);
-      acc = fma(double(x.z), double(w.z), acc);
-      acc = fma(double(x.w), double(w.w), acc);
+    const float4* ar = reinterpret_cast<const float4*>(a.A + row * a.lda);
+    const float4* br = reinterpret_cast<const float4*>(a.B + uint64_t(col) * a.ldb);
+    for (int k = lane; k < k4; k += 32) {
+      rows[warp][0][k] = ar[k];
+      rows[warp][1][k] = br[k];
     }
-    const float v = f32(acc);
-    float* cp = a.C + row * uint64_t(a.ldc) + col;
-    if (EPI == kEpiStore) *cp = v;
-    else if (EPI == kEpiRelu) *cp = js_relu(v);
-    else if (EPI == kEpiGate) *cp = a.gate[row * uint64_t(a.ldc) + col] > 0.0f ? v : 0.0f;
-    else *cp = f32(double(*cp) + double(v));
+    __syncwarp();
+    if (lane == 0) {
+      double acc = 0.0;
+      for (int k = 0; k < k4; k++) {
+        const float4 x = rows[warp][0][k], w = rows[warp][1][k];
+        acc = fma(double(x.x), double(w.x), acc);
+        acc = fma(double(x.y), double(w.y), acc);
+        acc = fma(double(x.z), double(w.z), acc);
+        acc = fma(double(x.w), double(w.w), acc);
+      }
+      oz_fix_store<EPI>(a, row, col, acc);
+    }
+    __syncwarp();  // the rows are read before the next output's land
   }
 }
 

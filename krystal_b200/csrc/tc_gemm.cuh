@@ -259,9 +259,10 @@ struct GemmArgs {
   float unscale;         // 2^-(sa+sw)
   int* err;              // error word
   int inject_expiry;     // test hook: the producer reports an expired wait before it issues any copy
-  // kEpiStore over several matrices of one input (planes > 1): n-tile p is
-  // matrix p, scaled by unscale_n[p] and stored to plane p of a [planes, M,
-  // 128] output through a 3-D map, as separate products would store them
+  // kEpiStore over the matrices of one input (planes > 0, the matrices'
+  // count, one or more): n-tile p is matrix p, scaled by unscale_n[p] and
+  // stored to plane p of a [planes, M, 128] output through a 3-D map, as
+  // separate products would store them; 0: an ordinary product
   int planes;
   float unscale_n[kMaxPlanes];
 };
@@ -463,7 +464,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
       tc_fence_after();
       const int row0 = m * kBM + g * 32;
       float us = a.unscale;
-      if (a.planes > 1)
+      if (a.planes > 0)
 #pragma unroll
         for (int p = 0; p < kMaxPlanes; p++) us = p == n ? a.unscale_n[p] : us;
 #pragma unroll 1
@@ -517,7 +518,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) k_tc_gemm(const __grid_constant_
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (a.planes > 1)
+          if (a.planes > 0)  // the map is 3-D
             asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
                          ::"l"(reinterpret_cast<uint64_t>(&cmap)), "r"(cc * 32), "r"(row0), "r"(n),
                          "r"(smem_u32(buf))
