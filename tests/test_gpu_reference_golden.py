@@ -1,0 +1,85 @@
+"""The CUDA path, through the C ABI, against outputs of the reference's own
+TypeScript code (tests/golden/reference_*.npz, made by executing the
+reference's source files on these inputs; tests/test_reference_golden.py
+pins the oracle to the same fixtures).
+
+The bar is the one the reference's composed test sets
+(packages/webgpu/test/krystal-composed.test.ts:67-69): selected indices
+exact, distributions within 1e-4; on the exact path the distributions are
+also bit-identical for all but a vanishing share of entries."""
+import numpy as np
+import pytest
+
+from krystal_b200.backend import CudaBrainBackend, MaskRule
+from krystal_b200.frame import HostFrame, compile_active_frame
+from tests import golden_io as G
+from tests.test_reference_golden import REFERENCE_BATCHES
+
+pytestmark = pytest.mark.gpu
+
+P_TOL = 1e-4
+MODES = ["exact", "certified"]
+
+
+def ref(name: str) -> dict:
+    return G.load(f"reference_{name}")
+
+
+def check(got_p, got_index, want_p, want_index, mode):
+    assert np.array_equal(got_index, want_index)
+    assert got_p.shape == want_p.shape
+    if got_p.size:
+        assert np.abs(got_p - want_p).max() <= P_TOL
+        if mode == "exact":
+            assert np.mean(got_p == want_p) >= 0.9999
+
+
+def test_composed_frame_matches_reference():
+    """The composed test's frame: encode and select (under its grammar, and open) against the reference's run."""
+    r = ref("test_records")
+    g, cfg, w, frame = G.test_records()
+    be = CudaBrainBackend(cfg, w, 0)
+    try:
+        enc = be.encode(HostFrame(frame, compile_active_frame(frame), frame.schema_ids.size))
+        assert np.array_equal(enc.query_output, r["query_output"])
+        assert np.array_equal(enc.bank_keys, r["bank_keys"])
+        assert np.array_equal(enc.bank_values, r["bank_values"])
+        for tag, mask in (("", r["grammar"]), ("_open", None)):
+            sel = be.select(enc, mask=mask)
+            check(sel.p, sel.index, r["p" + tag], r["index" + tag], "exact")
+            assert np.abs(sel.gather - r["gather" + tag]).max() <= 1e-6
+    finally:
+        be.destroy()
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("name", REFERENCE_BATCHES)
+def test_batch_matches_reference(name, mode):
+    """Every frame of a batch fixture, with its schema x band rule and sampler where it has them."""
+    r = ref(name)
+    g, cfg, w, b, rule, u = G.batch(name)
+    be = CudaBrainBackend(cfg, w, 0)
+    try:
+        be.set_precision(mode)
+        res = be.forward_batch(b, rule=MaskRule(*rule) if rule else None, uniforms=u, want_query_output=True)
+    finally:
+        be.destroy()
+    check(res["p"], res["index"], r["p"], r["index"], mode)
+    assert np.abs(res["query_output"] - r["query_output"]).max() <= (1e-5 if mode == "exact" else 1e-4)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_word_bias_matches_reference(mode):
+    """compileRecordMask's same-word bias on the 64-record frame, alpha 1.5 and -3.0."""
+    r = ref("word_bias_64")
+    g, cfg, w, b, _, _ = G.batch("single_frame_64")
+    be = CudaBrainBackend(cfg, w, 0)
+    try:
+        be.set_precision(mode)
+        for tag in ("pos", "neg"):
+            res = be.forward_batch(b, word_ids=r["word_ids"], word_alpha=float(r[f"{tag}_alpha"]),
+                                   want_query_output=True)
+            check(res["p"], res["index"], r[f"{tag}_p"], r[f"{tag}_index"], mode)
+            assert np.abs(res["query_output"] - r[f"{tag}_query_output"]).max() <= 1e-4
+    finally:
+        be.destroy()
