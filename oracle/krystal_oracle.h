@@ -17,12 +17,15 @@
  * used here and may differ from V8's by at most 1 ulp in f64, which the f32
  * store hides except with probability ~1e-8 per value.
  *
- * Parity pin: no JavaScript runtime exists in this environment, so the
- * restatement cannot be diffed against the TypeScript oracle itself. It is
- * pinned against every known-answer test the reference's own test files hold
- * (matmulOracle layout KAT, sampleRow KATs, packing / active-frame facts, the
- * parameter count 1 773 952, the masked-p and reopened-row facts) and against
- * an independent numpy re-implementation of the forward.
+ * Parity pin: the reference's own TypeScript (weights, packing, forward,
+ * selection with masks and sampling, the same-word bias, the session
+ * backward, learn and teach) was executed on the inputs of the golden
+ * fixtures by a runner that keeps JavaScript's number semantics
+ * (tests/golden/tsrun.py, tests/golden/make_reference_golden.py); this
+ * restatement reproduces those outputs bit for bit
+ * (tests/test_reference_golden.py). It is also checked against every
+ * known-answer test the reference's test files hold and against an
+ * independent numpy re-implementation of the forward.
  */
 #ifndef KRYSTAL_ORACLE_H
 #define KRYSTAL_ORACLE_H

@@ -3,9 +3,11 @@
     python tests/golden/make_golden.py
 
 The reference has no stored golden outputs (its parity tests compute the CPU
-oracle live) and no JavaScript runtime exists here, so these fixtures are the
-oracle's outputs on seeded inputs: they pin the oracle against regression and
-give the GPU tests a fixed target. Weights are rebuilt from their seeds at
+oracle live), so these fixtures are the oracle's outputs on seeded inputs:
+they pin the oracle against regression and give the GPU tests a fixed
+target. make_reference_golden.py runs the reference's own TypeScript on the
+same inputs, and tests/test_reference_golden.py requires the two to agree
+bit for bit. Weights are rebuilt from their seeds at
 test time; each fixture stores a checksum of the weight page it was made with.
 """
 from __future__ import annotations
