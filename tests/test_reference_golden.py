@@ -91,7 +91,7 @@ def test_backward_matches_reference(oracle, name, targets, valence, open_selecti
     assert out["value_loss"] == float(r[f"{name}_value_loss"])
 
 
-REFERENCE_BATCHES = ["single_frame_64"]
+REFERENCE_BATCHES = G.BATCHES
 
 
 @pytest.mark.parametrize("name", REFERENCE_BATCHES)
