@@ -18,6 +18,8 @@ the reference's code, unmodified, read from the reference tree:
   packages/krystal/src/host/teach.ts        teachFromDemonstration
   packages/webgpu/test/frame.ts             TEST_RECORDS, TEST_CONFIG, testFrame (the composed test's frame)
 
+and one long-bank frame (4096 bank records, 64 questions) is made here.
+
 The inputs are the ones the other fixtures here and the learn/teach tests
 are made from (the frames and rules they store, the weights rebuilt from
 their seeds); only data crosses over: records as HostRecord objects, the
@@ -316,8 +318,35 @@ def batch(ref: Reference, name: str):
                         index=np.concatenate(idx), query_output=np.concatenate(qo))
 
 
+# One long-bank frame inside the reference's geometry: a 4096-record bank and 64 questions, as in the
+# long-bank workload, with token ids over 4096 rows (the reference's token table holds 4352).
+LONG_BANK_REF = synth.Workload("long_bank_ref", 1, (4160, 4160), (64, 64), 4096, 64, bank=4096)
+
+
+def long_bank(ref: Reference):
+    """The pointer softmax over a 4096-record bank: one frame, selected open and under a schema x band rule."""
+    wl = LONG_BANK_REF
+    b = synth.make_batch(wl, seed=51, frames=1)
+    schema_allow, band_allow = synth.make_rule(b, seed=52)
+    cfg = ref.config(np.arange(wl.vocab, dtype=np.uint32))
+    w = ref.workload_weights(cfg, wl.vocab)
+    packed = ref.pack(b.token_ids, b.schema_ids, b.band_ids)
+    active = packed.active
+    q, r = len(active.queryRecords), len(active.bankRecords)
+    out = ref.oracle["brainForwardOracle"](packed.gpu, active, w, cfg, None, Float32Array(q * r))
+    res = {}
+    for tag, allows in (("open", None), ("rule", rule_allows(packed, schema_allow, band_allow, 0))):
+        mask = ref.learn["selectionMask"](active, allows)
+        sel = ref.oracle["selectorOracle"](out.queryOutput, out.bankKeys, out.bankValues, mask, w.selector, H)
+        res.update({f"p_{tag}": f32(sel.p), f"index_{tag}": u32(sel.index)})
+    np.savez_compressed(HERE / "reference_long_bank_frame.npz", weights_sha=digest(ref.page(w)), vocab=wl.vocab,
+                        rec_off=b.rec_off, token_ids=b.token_ids, field_roles=b.field_roles, schema_ids=b.schema_ids,
+                        band_ids=b.band_ids, schema_allow=schema_allow, band_allow=band_allow,
+                        query_output=f32(out.queryOutput), **res)
+
+
 STEPS = ("weights", "test_records", "word_bias", "learn", "teach", "single_frame_64", "ragged_16_open",
-         "ragged_16_rule", "ragged_12_sample")
+         "ragged_16_rule", "ragged_12_sample", "long_bank")
 
 
 def main():

@@ -1757,6 +1757,8 @@ def _array_from(src, fn=None, *_):
         items = [src[i] for i in range(n)]
     elif isinstance(src, _JSMap):
         items = [_JSArr(e) for e in src._d.items()]
+    elif isinstance(src, _TypedView):
+        items = src._mv.tolist()
     else:
         items = list(src)
     if fn is not None:
@@ -1832,6 +1834,9 @@ class _TypedBase(array.array):
 
 def _make_typed(name, code, conv):
     def __new__(cls, arg=0, *rest):
+        if isinstance(arg, ArrayBuffer):
+            return _TypedView(cls, arg, int(rest[0]) if rest and rest[0] is not None else 0,
+                              int(rest[1]) if len(rest) > 1 and rest[1] is not None else None)
         if isinstance(arg, (int, float)) and not isinstance(arg, bool):
             n = int(arg)
             if n != arg or n < 0:
@@ -1856,7 +1861,103 @@ def _make_typed(name, code, conv):
     cls = type(name, (_TypedBase,), ns)
     setattr(cls, "from", classmethod(lambda c, src, fn=None, *_: c(_array_from(src, fn))))
     cls.BYTES_PER_ELEMENT = array.array(code).itemsize
+    cls._code = code
+    cls._conv = staticmethod(conv) if conv is not None else None
     return cls
+
+
+class ArrayBuffer:
+    """Raw bytes that typed-array views alias (a memoryview of a bytearray or of a typed array's storage)."""
+
+    def __init__(self, n=0, *_):
+        self._mv = memoryview(bytearray(int(n))) if not isinstance(n, memoryview) else n
+
+    @property
+    def byteLength(self):
+        return self._mv.nbytes
+
+    def slice(self, a=None, b=None):
+        n = self._mv.nbytes
+        return ArrayBuffer(memoryview(bytearray(self._mv[_rel(a, n, 0):_rel(b, n, n)])))
+
+    def __bool__(self):
+        return True
+
+
+def _buffer_of(self):
+    return ArrayBuffer(memoryview(self).cast("B"))
+
+
+_TypedBase.buffer = property(_buffer_of)
+_TypedBase.byteOffset = property(lambda self: 0)
+_TypedBase.byteLength = property(lambda self: len(self) * self.itemsize)
+
+
+class _TypedView:
+    """A typed array over part of an ArrayBuffer: reads and writes reach the buffer, as in JavaScript."""
+
+    def __init__(self, cls, buf, off, n):
+        size = cls.BYTES_PER_ELEMENT
+        if off % size:
+            raise RangeError(f"start offset of {cls.__name__} should be a multiple of {size}")
+        if n is None:
+            if (buf.byteLength - off) % size:
+                raise RangeError(f"byte length of {cls.__name__} should be a multiple of {size}")
+            n = (buf.byteLength - off) // size
+        if off + n * size > buf.byteLength:
+            raise RangeError("invalid typed array length")
+        self._cls, self._buf, self._off, self._n = cls, buf, off, n
+        self._mv = buf._mv[off:off + n * size].cast(cls._code)
+        self._conv = cls._conv
+
+    def __len__(self):
+        return self._n
+
+    def __iter__(self):
+        return iter(self._mv.tolist())
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return self._mv.tolist()[i]
+        return self._mv[i]
+
+    def __setitem__(self, i, v):
+        conv = self._conv
+        if isinstance(i, slice):
+            vals = list(v)
+            self._mv[i] = memoryview(array.array(self._cls._code, [conv(x) for x in vals] if conv else vals)).cast(
+                "B").cast(self._cls._code)
+        else:
+            self._mv[i] = conv(v) if conv else v
+
+    def __bool__(self):
+        return True
+
+    length = property(lambda self: self._n)
+    buffer = property(lambda self: self._buf)
+    byteOffset = property(lambda self: self._off)
+    byteLength = property(lambda self: self._n * self._cls.BYTES_PER_ELEMENT)
+
+    def set(self, src, off=0):
+        off = int(off or 0)
+        src = list(src)
+        if off + len(src) > self._n:
+            raise RangeError("offset is out of bounds")
+        for k, x in enumerate(src):
+            self[off + k] = x
+
+    def subarray(self, a=None, b=None):
+        a, b = _rel(a, self._n, 0), _rel(b, self._n, self._n)
+        size = self._cls.BYTES_PER_ELEMENT
+        return _TypedView(self._cls, self._buf, self._off + a * size, max(0, b - a))
+
+    def slice(self, a=None, b=None):
+        return self._cls(self[_rel(a, self._n, 0):_rel(b, self._n, self._n)])
+
+    def fill(self, v, a=None, b=None):
+        for k in range(_rel(a, self._n, 0), _rel(b, self._n, self._n)):
+            self[k] = v
+        return self
 
 
 @functools.lru_cache(maxsize=None)
@@ -2104,7 +2205,7 @@ def _runtime():
     g.update(Math=Math, Number=Number, Object=Object, JSON=JSON, Array=Array, Error=Error, RangeError=RangeError,
              TypeError=TypeError_, Map=_JSMap, Set=_JSSet, Float32Array=Float32Array, Float64Array=Float64Array,
              Uint32Array=Uint32Array, Int32Array=Int32Array, Uint16Array=Uint16Array, Int16Array=Int16Array,
-             Uint8Array=Uint8Array, Int8Array=Int8Array, Infinity=_INF, NaN=_NAN, undefined=None,
+             Uint8Array=Uint8Array, Int8Array=Int8Array, ArrayBuffer=ArrayBuffer, Infinity=_INF, NaN=_NAN, undefined=None,
              _R_range=range, _R_getattr=getattr, _R_setattr=setattr, _R_isinstance=isinstance, _R_list=list,
              String=lambda v="", *_: _js_str(v), Boolean=lambda v=None, *_: bool(v),
              isNaN=lambda v, *_: _js_num(v) != _js_num(v),
@@ -2865,7 +2966,32 @@ class Gen:
 
     # -- expressions
     def expr(self, e):
+        if e[0] in ("mem", "idx", "call"):
+            low = self.lower_optional(e)
+            if low is not None:
+                return low
         return getattr(self, "e_" + e[0])(e)
+
+    def lower_optional(self, e):
+        """`a?.b.c(x)`: the first `?.` below this node short-circuits the whole rest of the chain."""
+        path, node = [], e
+        while node[0] in ("mem", "idx", "call"):
+            if node[-1]:  # an optional link: node = (kind, obj, ..., True)
+                break
+            path.append(node)
+            node = node[1]
+        else:
+            return None
+        if not path:
+            return None  # this node is the optional link itself (handled by e_mem / e_idx / e_call)
+        t = self.t()
+        head = (node[0], ("pyraw", t)) + node[2:-1] + (False,)
+        for outer in reversed(path):
+            head = (outer[0], head) + outer[2:]
+        return f"(None if ({t} := {self.expr(node[1])}) is None else {self.expr(head)})"
+
+    def e_pyraw(self, e):
+        return e[1]
 
     def e_paren(self, e):
         return self.expr(e[1])
@@ -3039,6 +3165,8 @@ class Gen:
         _, callee, args, opt = e
         if callee == ("super",):
             return f"{self.super_base}.__init__(self, {self.args(args)})"
+        if callee == ("id", "import"):  # a dynamic import: the module's namespace (synchronously)
+            return f"_js_namespace(_js_import({str(self.module_path)!r}, {self.args(args)}))"
         if callee[0] == "mem" and callee[1] == ("super",):
             return f"super().{callee[2]}({self.args(args)})"
         if opt:
@@ -3088,11 +3216,13 @@ class _StubModule(dict):
 
 class Runner:
     """Loads TypeScript modules from a source tree and runs them. Imports of
-    packages outside the tree (third-party, not vendored) bind stubs."""
+    packages outside the tree (third-party, not vendored) bind stubs, except
+    those given in `packages` (specifier -> dict of exports)."""
 
-    def __init__(self):
+    def __init__(self, packages=None):
         self.modules = {}
         self.sources = {}
+        self.packages = dict(packages or {})
 
     @staticmethod
     def resolve(from_file, spec):
@@ -3105,6 +3235,8 @@ class Runner:
         raise FileNotFoundError(f"cannot resolve {spec!r} from {from_file}")
 
     def import_(self, from_file, spec):
+        if spec in self.packages:
+            return self.packages[spec]
         path = self.resolve(from_file, spec)
         return _StubModule(spec) if path is None else self.load(path)
 
@@ -3127,3 +3259,154 @@ class Runner:
         self.sources[path] = code
         exec(compile(code, f"<ts {path}>", "exec"), ns)
         return ns
+
+
+# ---------------------------------------------------------------------------
+# bun:test, enough of it to run the reference's CPU unit tests
+# ---------------------------------------------------------------------------
+
+class _Expectation(Exception):
+    pass
+
+
+def _deep_equal(a, b):
+    if isinstance(a, (list, array.array)) and isinstance(b, (list, array.array)):
+        return len(a) == len(b) and all(_deep_equal(x, y) for x, y in zip(a, b))
+    if isinstance(a, _JSObject) and isinstance(b, _JSObject):
+        ka = {k for k, v in a.__dict__.items() if v is not None}
+        kb = {k for k, v in b.__dict__.items() if v is not None}
+        return ka == kb and all(_deep_equal(a.__dict__[k], b.__dict__[k]) for k in ka)
+    if isinstance(a, float) and isinstance(b, float) and a != a and b != b:
+        return True
+    return _js_seq(a, b) or (isinstance(a, (int, float)) and isinstance(b, (int, float))
+                             and not isinstance(a, bool) and not isinstance(b, bool) and a == b)
+
+
+class _Expect:
+    def __init__(self, value, negate=False):
+        self.v = value
+        self.negate = negate
+
+    def _check(self, ok, what):
+        if bool(ok) == self.negate:
+            raise _Expectation(f"expected {_js_str(self.v) if not isinstance(self.v, _JSObject) else self.v!r} "
+                               f"{'not ' if self.negate else ''}{what}")
+
+    def toBe(self, x, *_):
+        self._check(_js_seq(self.v, x) or (self.v != self.v and x != x), f"to be {x!r}")
+
+    def toEqual(self, x, *_):
+        self._check(_deep_equal(self.v, x), f"to equal {x!r}")
+
+    toStrictEqual = toEqual
+
+    def toBeCloseTo(self, x, digits=2, *_):
+        self._check(abs(self.v - x) < 10 ** (-digits) / 2, f"to be close to {x!r} ({digits} digits)")
+
+    def toBeGreaterThan(self, x, *_):
+        self._check(self.v > x, f"to be > {x!r}")
+
+    def toBeGreaterThanOrEqual(self, x, *_):
+        self._check(self.v >= x, f"to be >= {x!r}")
+
+    def toBeLessThan(self, x, *_):
+        self._check(self.v < x, f"to be < {x!r}")
+
+    def toBeLessThanOrEqual(self, x, *_):
+        self._check(self.v <= x, f"to be <= {x!r}")
+
+    def toHaveLength(self, n, *_):
+        self._check(_js_length(self.v) == n, f"to have length {n}")
+
+    def toContain(self, x, *_):
+        self._check(any(_js_seq(y, x) for y in self.v) if not isinstance(self.v, str) else x in self.v,
+                    f"to contain {x!r}")
+
+    def toBeNull(self, *_):
+        self._check(self.v is None, "to be null")
+
+    toBeUndefined = toBeNull
+
+    def toBeDefined(self, *_):
+        self._check(self.v is not None, "to be defined")
+
+    def toBeTruthy(self, *_):
+        self._check(bool(self.v) and self.v == self.v, "to be truthy")
+
+    def toBeFalsy(self, *_):
+        self._check(not (bool(self.v) and self.v == self.v), "to be falsy")
+
+    def toBeNaN(self, *_):
+        self._check(isinstance(self.v, float) and self.v != self.v, "to be NaN")
+
+    def toThrow(self, what=None, *_):
+        try:
+            self.v()
+            thrown = None
+        except _Expectation:
+            raise
+        except Exception as e:  # noqa: BLE001 - any thrown value counts
+            thrown = e
+        ok = thrown is not None
+        if ok and what is not None:
+            msg = getattr(thrown, "message", str(thrown))
+            if isinstance(what, str):
+                ok = what in msg
+            elif isinstance(what, type):
+                ok = isinstance(thrown, what)
+        self._check(ok, f"to throw {what!r}")
+
+
+setattr(_Expect, "not", property(lambda self: _Expect(self.v, not self.negate)))
+
+
+class _OutOfTime(BaseException):
+    pass
+
+
+def bun_test_module(results, select=None, budget_s=None):
+    """describe/test/expect: each test runs when it is declared and appends (name, error or None) to
+    `results`. `select`: the ordinals of the tests to run (the others are listed as "not selected");
+    `budget_s`: a test still running after that many seconds is stopped and listed as out of time."""
+    import signal
+    prefix = []
+    count = [0]
+
+    def _alarm(*_):
+        raise _OutOfTime()
+
+    def describe(name, fn=None, *_):
+        prefix.append(str(name))
+        try:
+            fn()
+        finally:
+            prefix.pop()
+
+    def test(name, fn=None, *_):
+        full = " > ".join(prefix + [str(name)])
+        k = count[0]
+        count[0] += 1
+        if select is not None and k not in select:
+            results.append((full, "not selected"))
+            return
+        if budget_s:
+            signal.signal(signal.SIGALRM, _alarm)
+            signal.alarm(int(budget_s))
+        try:
+            fn()
+            results.append((full, None))
+        except _OutOfTime:
+            results.append((full, f"out of time: still running after {budget_s} s"))
+        except Exception as e:  # noqa: BLE001 - record the failure and go on
+            results.append((full, f"{type(e).__name__}: {e}"))
+        finally:
+            if budget_s:
+                signal.alarm(0)
+
+    def skip(name, fn=None, *_):
+        results.append((" > ".join(prefix + [str(name)]), "skipped"))
+
+    setattr(test, "skip", skip)
+    setattr(test, "todo", skip)
+    expect_obj = lambda v=None, *_: _Expect(v)  # noqa: E731
+    return {"describe": describe, "test": test, "it": test, "expect": expect_obj}
