@@ -2122,20 +2122,51 @@ def _no_random(*_):
     raise NotImplementedError("Math.random")
 
 
+def _fn1(f):
+    """A one-argument Math function that, as in JavaScript, ignores extra arguments (e.g. `xs.map(Math.abs)`)."""
+    return lambda x=None, *_: f(x)
+
+
+def _fn2(f):
+    return lambda x=None, y=None, *_: f(x, y)
+
+
+def _floor(x):
+    return _int_if(math.floor(x)) if _finite(x) else x
+
+
+def _ceil(x):
+    return _int_if(math.ceil(x)) if _finite(x) else x
+
+
+def _trunc(x):
+    return _int_if(math.trunc(x)) if _finite(x) else x
+
+
+def _sign(x):
+    return x if x != x or x == 0 else (1 if x > 0 else -1)
+
+
+def _log2(x):
+    return math.log2(x) if x > 0 else _js_log(x)
+
+
+def _log10(x):
+    return math.log10(x) if x > 0 else _js_log(x)
+
+
+def _log1p(x):
+    return math.log1p(x) if x > -1 else (-_INF if x == -1 else _NAN)
+
+
 Math = _JSObject((
-    ("exp", _js_exp), ("log", _js_log), ("sqrt", _js_sqrt), ("max", _js_max), ("min", _js_min),
-    ("abs", lambda x: abs(x)),
-    ("floor", lambda x: _int_if(math.floor(x)) if _finite(x) else x),
-    ("ceil", lambda x: _int_if(math.ceil(x)) if _finite(x) else x),
-    ("round", _js_round), ("trunc", lambda x: _int_if(math.trunc(x)) if _finite(x) else x),
-    ("sign", lambda x: x if x != x or x == 0 else (1 if x > 0 else -1)),
-    ("cos", math.cos), ("sin", math.sin), ("tan", math.tan), ("tanh", math.tanh), ("atan", math.atan),
-    ("atan2", math.atan2), ("pow", _js_pow), ("hypot", math.hypot),
-    ("log2", lambda x: math.log2(x) if x > 0 else _js_log(x)),
-    ("log10", lambda x: math.log10(x) if x > 0 else _js_log(x)),
-    ("log1p", lambda x: math.log1p(x) if x > -1 else (-_INF if x == -1 else _NAN)), ("expm1", math.expm1),
-    ("imul", _imul), ("fround", _to_f32), ("random", _no_random),
-    ("PI", math.pi), ("E", math.e), ("LN2", math.log(2)), ("SQRT2", math.sqrt(2)),
+    ("exp", _fn1(_js_exp)), ("log", _fn1(_js_log)), ("sqrt", _fn1(_js_sqrt)), ("max", _js_max), ("min", _js_min),
+    ("abs", _fn1(abs)), ("floor", _fn1(_floor)), ("ceil", _fn1(_ceil)), ("round", _fn1(_js_round)),
+    ("trunc", _fn1(_trunc)), ("sign", _fn1(_sign)), ("cos", _fn1(math.cos)), ("sin", _fn1(math.sin)),
+    ("tan", _fn1(math.tan)), ("tanh", _fn1(math.tanh)), ("atan", _fn1(math.atan)), ("atan2", _fn2(math.atan2)),
+    ("pow", _fn2(_js_pow)), ("hypot", lambda *xs: math.hypot(*xs)), ("log2", _fn1(_log2)), ("log10", _fn1(_log10)),
+    ("log1p", _fn1(_log1p)), ("expm1", _fn1(math.expm1)), ("imul", _fn2(_imul)), ("fround", _fn1(_to_f32)),
+    ("random", _no_random), ("PI", math.pi), ("E", math.e), ("LN2", math.log(2)), ("SQRT2", math.sqrt(2)),
 ))
 
 Number = _JSObject((

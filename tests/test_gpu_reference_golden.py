@@ -83,3 +83,19 @@ def test_word_bias_matches_reference(mode):
             assert np.abs(res["query_output"] - r[f"{tag}_query_output"]).max() <= 1e-4
     finally:
         be.destroy()
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_long_bank_frame_matches_reference(mode):
+    """A 4096-record bank with 64 questions: selected open and under a schema x band rule."""
+    from tests.test_reference_golden import long_bank_frame
+    r, cfg, w, b = long_bank_frame()
+    be = CudaBrainBackend(cfg, w, 0)
+    try:
+        be.set_precision(mode)
+        for tag, rule in (("open", None), ("rule", MaskRule(r["schema_allow"], r["band_allow"]))):
+            res = be.forward_batch(b, rule=rule, want_query_output=True)
+            check(res["p"], res["index"], r[f"p_{tag}"], r[f"index_{tag}"], mode)
+            assert np.abs(res["query_output"] - r["query_output"]).max() <= (1e-5 if mode == "exact" else 1e-4)
+    finally:
+        be.destroy()

@@ -179,3 +179,43 @@ def test_teach_matches_reference(name, kw, opts):
     for k, js in (("frames_seen", "framesSeen"), ("shown", "shown"), ("mean_agreement", "meanAgreement"),
                   ("max_parameter_abs", "maxParameterAbs"), ("rejected", "rejected"), ("clipped", "clipped")):
         assert float(rep[k]) == float(r[f"{name}_{js}"]), k
+
+
+def test_reference_unit_tests_pass_under_the_runner():
+    """The runner that made these fixtures, checked on the reference's own CPU unit tests
+    (sampling, session, checkpoint, learn and teach test files; tests/golden/run_reference_tests.py):
+    none of their assertions failed under it. A test the record lists as not run trained for longer
+    than its time budget at the runner's Python speed; every file has tests that ran to completion."""
+    import json
+    record = json.loads((G.GOLDEN / "reference_unit_tests.json").read_text())
+    assert set(record) == {"forward/sampling.test.ts", "host/session.test.ts", "host/checkpoint.test.ts",
+                           "host/learn.test.ts", "host/teach.test.ts"}
+    for f, tests in record.items():
+        assert tests and all(t is not None for t in tests), f
+        assert not [t["test"] for t in tests if t["status"] == "failed"], f
+        assert sum(t["status"] == "passed" for t in tests) >= max(1, len(tests) // 2), f
+
+
+def long_bank_frame():
+    """The reference-run long-bank frame (4096 bank records + 64 questions, token ids over 4096 rows)."""
+    from krystal_b200 import synth
+    from krystal_b200.frame import FrameBatch
+    r = ref("long_bank_frame")
+    wl = synth.WORKLOADS["ragged_4096"]  # the same 4096-row token table and weights
+    assert int(r["vocab"]) == wl.vocab
+    cfg = synth.workload_config(wl)
+    w = synth.workload_weights(cfg, wl.vocab)
+    b = FrameBatch(r["rec_off"], r["token_ids"], r["field_roles"], r["schema_ids"], r["band_ids"])
+    return r, cfg, w, b
+
+
+@pytest.mark.parametrize("tag", ["open", "rule"])
+def test_long_bank_frame_matches_reference(oracle, tag):
+    """The pointer softmax over a 4096-record bank (oracle.ts:332-382), open and under a schema x band rule."""
+    r, cfg, w, b = long_bank_frame()
+    assert G.sha(w.page) == str(r["weights_sha"])
+    rule = (r["schema_allow"], r["band_allow"]) if tag == "rule" else None
+    res = oracle.forward_batch(cfg, w.page, b, rule=rule, want_query_output=True)
+    assert np.array_equal(res["index"], r[f"index_{tag}"])
+    assert bits_equal(res["p"], r[f"p_{tag}"])
+    assert bits_equal(res["query_output"], r["query_output"])
