@@ -22,8 +22,9 @@ What it preserves, because parity depends on it:
 
 Known limits (none met by the files it is used on, and each one fails
 loudly rather than silently where it can): NaN counts as true in a
-condition; a negative array index wraps instead of reading undefined;
-`subarray` is a copy that refuses writes instead of an alias; closures
+condition; a negative array index wraps instead of reading undefined; a
+`subarray` of an owned typed array is a copy that refuses writes (views
+made over an ArrayBuffer do alias it); closures
 capture loop variables by reference; labels, generators and
 regular-expression literals are not translated. `Math.exp/log/sin/cos` are
 the C library's (as the C++ oracle's), which may differ from V8's in the
