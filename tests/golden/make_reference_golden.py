@@ -345,8 +345,39 @@ def long_bank(ref: Reference):
                         query_output=f32(out.queryOutput), **res)
 
 
+def edges(ref: Reference):
+    """tests/edge_cases.py: frames without a bank or a question, empty records and holes, 1-token and full
+    records; the rule that admits nothing (reopened row); a blocked question with sampling."""
+    from tests import edge_cases as E
+    cfg = ref.config(E.token_rows())
+    w = ref.weights(cfg, E.WEIGHT_SEED)
+    out = {"weights_sha": digest(ref.page(w))}
+    ps, idx, qo = [], [], []
+    for recs in E.edge_frames():
+        packed = ref.frame["packHostFrame"](js_records(recs))
+        fwd, sel = ref.think(packed, w, cfg)
+        ps.append(f32(sel.p))
+        idx.append(u32(sel.index))
+        qo.append(f32(fwd.queryOutput))
+    out.update(p=np.concatenate(ps), index=np.concatenate(idx), query_output=np.concatenate(qo))
+    recs, schema_allow, band_allow = E.reopen_frame()
+    packed = ref.frame["packHostFrame"](js_records(recs))
+    _, sel = ref.think(packed, w, cfg, allows=rule_allows(packed, schema_allow, band_allow, 0))
+    out.update(reopen_p=f32(sel.p), reopen_index=u32(sel.index))
+    recs, mask, uniforms = E.blocked_frame()
+    packed = ref.frame["packHostFrame"](js_records(recs))
+    active = packed.active
+    fwd = ref.oracle["brainForwardOracle"](packed.gpu, active, w, cfg, None,
+                                           Float32Array(len(active.queryRecords) * len(active.bankRecords)))
+    sel = ref.oracle["selectorOracle"](fwd.queryOutput, fwd.bankKeys, fwd.bankValues, Float32Array(mask.tolist()),
+                                       w.selector, H, lambda row, *_: float(uniforms[row]))
+    out.update(blocked_p=f32(sel.p), blocked_index=u32(sel.index), blocked_gather=f32(sel.gather),
+               blocked_query_output=f32(fwd.queryOutput))
+    np.savez_compressed(HERE / "reference_edges.npz", **out)
+
+
 STEPS = ("weights", "test_records", "word_bias", "learn", "teach", "single_frame_64", "ragged_16_open",
-         "ragged_16_rule", "ragged_12_sample", "long_bank")
+         "ragged_16_rule", "ragged_12_sample", "long_bank", "edges")
 
 
 def main():

@@ -99,3 +99,34 @@ def test_long_bank_frame_matches_reference(mode):
             assert np.abs(res["query_output"] - r["query_output"]).max() <= (1e-5 if mode == "exact" else 1e-4)
     finally:
         be.destroy()
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_edge_frames_match_reference(mode):
+    """Frames without a bank or a question, empty records, holes, 1-token and full records; the rule that
+    admits nothing (reopened row); a question whose every record is blocked, with sampling."""
+    from krystal_b200 import abi
+    from krystal_b200.frame import pack_frame_batch, pack_host_frame
+    from tests.test_reference_golden import edge_world
+    r = ref("edges")
+    E, cfg, w = edge_world()
+    be = CudaBrainBackend(cfg, w, 0)
+    try:
+        be.set_precision(mode)
+        batch = pack_frame_batch(E.edge_frames())
+        res = be.forward_batch(batch, want_query_output=True)
+        check(res["p"], res["index"], r["p"], r["index"], mode)
+        offs = batch.offsets()  # frames without bank records define no query output (session.ts:133)
+        rows = np.repeat(np.repeat(offs["r"] > 0, offs["q"].astype(np.int64)), 128)
+        assert np.abs(res["query_output"][rows] - r["query_output"][rows]).max() <= (0.0 if mode == "exact" else 1e-4)
+        recs, schema_allow, band_allow = E.reopen_frame()
+        res = be.forward_batch(pack_frame_batch([recs]), rule=MaskRule(schema_allow, band_allow))
+        check(res["p"], res["index"], r["reopen_p"], r["reopen_index"], mode)
+        recs, mask, uniforms = E.blocked_frame()
+        enc = be.encode(pack_host_frame(recs))
+        sel = be.select(enc, mask=mask, uniforms=uniforms)
+        check(sel.p, sel.index, r["blocked_p"], r["blocked_index"], "exact")
+        assert sel.index[0] == abi.KC_NO_SELECTION
+        assert np.abs(sel.gather - r["blocked_gather"]).max() <= 1e-6
+    finally:
+        be.destroy()

@@ -219,3 +219,46 @@ def test_long_bank_frame_matches_reference(oracle, tag):
     assert np.array_equal(res["index"], r[f"index_{tag}"])
     assert bits_equal(res["p"], r[f"p_{tag}"])
     assert bits_equal(res["query_output"], r["query_output"])
+
+
+def edge_world():
+    from tests import edge_cases as E
+    cfg = BRAIN_FORWARD_CONFIG.with_token_rows(E.token_rows())
+    return E, cfg, create_brain_forward_weights(cfg, E.WEIGHT_SEED)
+
+
+def test_edge_frames_match_reference(oracle):
+    """Frames without a bank or a question, empty records, holes, 1-token and full records (tests/edge_cases.py)."""
+    from krystal_b200.frame import pack_frame_batch
+    r = ref("edges")
+    E, cfg, w = edge_world()
+    assert G.sha(w.page) == str(r["weights_sha"])
+    batch = pack_frame_batch(E.edge_frames())
+    res = oracle.forward_batch(cfg, w.page, batch, want_query_output=True)
+    assert np.array_equal(res["index"], r["index"])
+    assert bits_equal(res["p"], r["p"])
+    # A frame without bank records has no query output to compare: the session never encodes one
+    # (consider returns no selections first, session.ts:133), and the batch path defines none for it.
+    offs = batch.offsets()
+    has_bank = np.repeat(offs["r"] > 0, offs["q"].astype(np.int64))
+    rows = np.repeat(has_bank, 128)
+    assert bits_equal(res["query_output"][rows], r["query_output"][rows])
+
+
+def test_reopened_and_blocked_rows_match_reference(oracle):
+    """selectionMask's reopened row (learn.ts:229) and selectorOracle's all-blocked row with sampling
+    (oracle.ts:356-370, sampling.ts:41-57)."""
+    from krystal_b200.frame import pack_frame_batch
+    r = ref("edges")
+    E, cfg, w = edge_world()
+    recs, schema_allow, band_allow = E.reopen_frame()
+    res = oracle.forward_batch(cfg, w.page, pack_frame_batch([recs]), rule=(schema_allow, band_allow))
+    assert np.array_equal(res["index"], r["reopen_index"]) and bits_equal(res["p"], r["reopen_p"])
+    recs, mask, uniforms = E.blocked_frame()
+    frame = pack_host_frame(recs)
+    out = oracle.forward(cfg, w.page, frame.gpu)
+    assert bits_equal(out["query_output"], r["blocked_query_output"])
+    sel = oracle.selector(out["query_output"], out["bank_keys"], out["bank_values"], mask, w.selector.wq,
+                          w.selector.wk, 128, uniforms=uniforms)
+    assert np.array_equal(sel["index"], r["blocked_index"]) and bits_equal(sel["p"], r["blocked_p"])
+    assert bits_equal(sel["gather"], r["blocked_gather"])
