@@ -376,8 +376,46 @@ def edges(ref: Reference):
     np.savez_compressed(HERE / "reference_edges.npz", **out)
 
 
+LEARN_BATCH_FRAMES = 8
+
+
+def learn_batch(ref: Reference):
+    """learnFromExperience on frames shaped like the learn workload (16-256 records, four questions, a target
+    bank row per question, a reward per frame; make_batch seed 1, make_learn_inputs seed 3), open grammar."""
+    wl = synth.WORKLOADS["learn_1024"]
+    b = synth.make_batch(wl, seed=1, frames=LEARN_BATCH_FRAMES)
+    targets, rewards = synth.make_learn_inputs(b, seed=3)
+    offs = b.offsets()
+    cfg = ref.config(np.arange(wl.vocab, dtype=np.uint32))
+    w = ref.workload_weights(cfg, wl.vocab)
+    exps = []
+    for f in range(b.frames):
+        g = b.frame(f)
+        q0, q1 = int(offs["q_off"][f]), int(offs["q_off"][f + 1])
+        bank = np.flatnonzero(g.band_ids != QUERY_BAND)
+        recs = _JSArr(js_records_of(g))
+        exps.append(_js_obj([("records", recs), ("chosen", _JSArr([int(bank[t]) for t in targets[q0:q1]])),
+                             ("reward", float(rewards[f]))]))
+    rep = ref.learn["learnFromExperience"](_JSArr(exps), w, cfg, _js_obj([]))
+    page = ref.page(w)
+    out = {"sha": digest(page), **page_parts(page)}
+    for k in ("framesSeen", "meanAdvantage", "meanValueLoss", "reinforced", "discouraged", "meanEntropy",
+              "meanConfidence", "updateApplied"):
+        out[k] = np.float64(getattr(rep, k))
+    np.savez_compressed(HERE / "reference_learn_batch.npz", **out)
+
+
+def js_records_of(g):
+    """A packed frame's records back as HostRecord objects (every record active, in order)."""
+    tok = g.token_ids.reshape(-1, 8)
+    for s in range(g.schema_ids.size):
+        props = [("schemaId", int(g.schema_ids[s])), ("tokens", _JSArr([int(x) for x in tok[s] if x != 0]))]
+        props.append(("query", True) if g.band_ids[s] == QUERY_BAND else ("band", int(g.band_ids[s])))
+        yield _js_obj(props)
+
+
 STEPS = ("weights", "test_records", "word_bias", "learn", "teach", "single_frame_64", "ragged_16_open",
-         "ragged_16_rule", "ragged_12_sample", "long_bank", "edges")
+         "ragged_16_rule", "ragged_12_sample", "long_bank", "edges", "learn_batch")
 
 
 def main():

@@ -262,3 +262,33 @@ def test_reopened_and_blocked_rows_match_reference(oracle):
                           w.selector.wk, 128, uniforms=uniforms)
     assert np.array_equal(sel["index"], r["blocked_index"]) and bits_equal(sel["p"], r["blocked_p"])
     assert bits_equal(sel["gather"], r["blocked_gather"])
+
+
+def test_learn_batch_matches_reference():
+    """learnFromExperience on eight frames shaped like the learn workload (16-256 records, four questions,
+    a target bank row per question, a reward per frame): the oracle's learn leaves the same page."""
+    from krystal_b200 import synth
+    from oracle import learn_oracle as LO
+    r = ref("learn_batch")
+    wl = synth.WORKLOADS["learn_1024"]
+    cfg = synth.workload_config(wl)
+    w0 = synth.workload_weights(cfg, wl.vocab)
+    b = synth.make_batch(wl, seed=1, frames=8)
+    targets, rewards = synth.make_learn_inputs(b, seed=3)
+    offs = b.offsets()
+    exps = []
+    for f in range(b.frames):
+        g = b.frame(f)
+        q0, q1 = int(offs["q_off"][f]), int(offs["q_off"][f + 1])
+        bank = np.flatnonzero(g.band_ids != 5)
+        exps.append(dict(frame=g, chosen=[int(bank[t]) for t in targets[q0:q1]], reward=float(rewards[f]),
+                         mask=np.zeros((q1 - q0) * bank.size, np.float32)))
+    page, rep = LO.learn_from_experience(cfg, w0.page, exps)
+    for k, v in _page_parts(page).items():
+        assert v == str(r[f"sha_{k}"]), k
+    assert G.sha(page) == str(r["sha"])
+    for k, js in (("frames_seen", "framesSeen"), ("mean_advantage", "meanAdvantage"),
+                  ("mean_value_loss", "meanValueLoss"), ("reinforced", "reinforced"), ("discouraged", "discouraged"),
+                  ("mean_entropy", "meanEntropy"), ("mean_confidence", "meanConfidence"),
+                  ("update_applied", "updateApplied")):
+        assert float(rep[k]) == float(r[js]), k
